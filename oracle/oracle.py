@@ -1,0 +1,329 @@
+"""ctypes front end for the CPU oracle (oracle/vox_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and the
+CPU-baseline leg of bench.py, never by the product package.  Each wrapper
+names the reference function (crates/voxtral/src/...) it restates.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "libvoxoracle.so")
+_lib = None
+
+F32P = C.POINTER(C.c_float)
+U16P = C.POINTER(C.c_uint16)
+I32P = C.POINTER(C.c_int32)
+SZ = C.c_size_t
+
+
+class VoConfig(C.Structure):
+    """DecoderConfig (crates/voxtral/src/decoder.rs:10-19)."""
+
+    _fields_ = [
+        ("dim", SZ), ("hidden_dim", SZ), ("n_heads", SZ), ("n_kv_heads", SZ),
+        ("head_dim", SZ), ("sliding_window", SZ), ("norm_eps", C.c_float),
+        ("rope_theta", C.c_float),
+    ]
+
+
+class VoLayerWeights(C.Structure):
+    _fields_ = [
+        ("bf16", C.c_int), ("attention_norm", F32P), ("ffn_norm", F32P),
+        ("wq", F32P), ("wk", F32P), ("wv", F32P), ("wo", F32P),
+        ("w1", F32P), ("w2", F32P), ("w3", F32P),
+        ("wq_h", U16P), ("wk_h", U16P), ("wv_h", U16P), ("wo_h", U16P),
+        ("w1_h", U16P), ("w2_h", U16P), ("w3_h", U16P),
+    ]
+
+
+class VoModel(C.Structure):
+    _fields_ = [
+        ("cfg", VoConfig), ("n_layers", SZ), ("vocab", SZ),
+        ("layers", C.POINTER(VoLayerWeights)), ("embed", U16P),
+        ("final_norm", F32P), ("lm_head", U16P),
+    ]
+
+
+def build():
+    """Compile the oracle with its Makefile (gcc, -ffp-contract=off)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = C.CDLL(_LIB_PATH)
+        L.vo_config_validate.argtypes = [C.POINTER(VoConfig)]
+        L.vo_silu_inplace.argtypes = [F32P, SZ]
+        L.vo_rms_norm_rows.argtypes = [F32P, F32P, F32P, SZ, SZ, C.c_float]
+        L.vo_rope_interleaved_inplace.argtypes = [F32P, SZ, SZ, SZ, SZ, C.c_float]
+        L.vo_softmax_inplace.argtypes = [F32P, SZ]
+        L.vo_linear.argtypes = [F32P, SZ, SZ, F32P, SZ, F32P, F32P]
+        L.vo_linear_bf16.argtypes = [F32P, SZ, SZ, U16P, SZ, F32P, F32P]
+        L.vo_add_inplace.argtypes = [F32P, F32P, SZ]
+        L.vo_attention_gqa_step.argtypes = [F32P, F32P, F32P, SZ, SZ, SZ, SZ, SZ, F32P]
+        L.vo_kv_new.argtypes = [SZ, SZ, SZ, SZ]
+        L.vo_kv_new.restype = C.c_void_p
+        L.vo_kv_free.argtypes = [C.c_void_p]
+        L.vo_kv_clone.argtypes = [C.c_void_p]
+        L.vo_kv_clone.restype = C.c_void_p
+        L.vo_kv_append_layer.argtypes = [C.c_void_p, SZ, F32P, F32P, SZ]
+        L.vo_kv_layer_len_tokens.argtypes = [C.c_void_p, SZ]
+        L.vo_kv_layer_len_tokens.restype = SZ
+        L.vo_kv_layer_pos_offset.argtypes = [C.c_void_p, SZ]
+        L.vo_kv_layer_pos_offset.restype = SZ
+        L.vo_kv_layer_keys.argtypes = [C.c_void_p, SZ]
+        L.vo_kv_layer_keys.restype = F32P
+        L.vo_kv_layer_values.argtypes = [C.c_void_p, SZ]
+        L.vo_kv_layer_values.restype = F32P
+        L.vo_kv_layer_set.argtypes = [C.c_void_p, SZ, F32P, F32P, SZ, SZ]
+        L.vo_decoder_layer_forward_step.argtypes = [
+            C.POINTER(VoConfig), SZ, C.POINTER(VoLayerWeights), C.c_void_p, F32P, SZ, SZ, F32P]
+        L.vo_model_step.argtypes = [C.POINTER(VoModel), C.c_void_p, C.c_int32, SZ, F32P, I32P]
+        L.vo_gen_normal_f32.argtypes = [C.c_uint64, C.c_uint64, C.c_float, C.c_uint64, SZ, F32P]
+        L.vo_gen_normal_bf16.argtypes = [C.c_uint64, C.c_uint64, C.c_float, C.c_uint64, SZ, U16P]
+        L.vo_gen_uniform_ids.argtypes = [C.c_uint64, C.c_uint64, C.c_uint32, C.c_uint64, SZ, I32P]
+        L.vo_f32_to_bf16_rne.argtypes = [C.c_float]
+        L.vo_f32_to_bf16_rne.restype = C.c_uint16
+        L.vo_set_threads.argtypes = [C.c_int]
+        _lib = L
+    return _lib
+
+
+def set_threads(n: int) -> None:
+    lib().vo_set_threads(int(n))
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _p(a, t=F32P):
+    return a.ctypes.data_as(t)
+
+
+def config(**kw) -> VoConfig:
+    return VoConfig(**kw)
+
+
+# ---- math.rs ---------------------------------------------------------------
+
+def silu(x):
+    """math.rs:4-9"""
+    y = _f32(x).copy()
+    lib().vo_silu_inplace(_p(y), y.size)
+    return y
+
+
+def rms_norm_rows(x, w, dim, eps):
+    """math.rs:11-27"""
+    x = _f32(x)
+    w = _f32(w)
+    out = np.zeros_like(x)
+    lib().vo_rms_norm_rows(_p(out), _p(x), _p(w), x.size, dim, eps)
+    return out
+
+
+def rope_interleaved(x, seq_len, n_heads, head_dim, pos_offset, theta):
+    """math.rs:30-65"""
+    y = _f32(x).copy()
+    lib().vo_rope_interleaved_inplace(_p(y), seq_len, n_heads, head_dim, pos_offset, theta)
+    return y
+
+
+def softmax(x):
+    """math.rs:67-88"""
+    y = _f32(x).copy()
+    lib().vo_softmax_inplace(_p(y), y.size)
+    return y
+
+
+# ---- ops.rs ----------------------------------------------------------------
+
+def linear(x, n_rows, in_dim, w, out_dim, bias=None):
+    """ops.rs:11-39 (f32 weights)"""
+    x = _f32(x)
+    w = _f32(w)
+    out = np.zeros(n_rows * out_dim, np.float32)
+    b = _f32(bias) if bias is not None else None
+    lib().vo_linear(_p(x), n_rows, in_dim, _p(w), out_dim, _p(b) if b is not None else None, _p(out))
+    return out
+
+
+def linear_bf16(x, n_rows, in_dim, w_bits, out_dim, bias=None):
+    """ops.rs:11-39 with bf16 weights widened exactly (weights.rs:77-81)."""
+    x = _f32(x)
+    w = np.ascontiguousarray(w_bits, dtype=np.uint16)
+    out = np.zeros(n_rows * out_dim, np.float32)
+    b = _f32(bias) if bias is not None else None
+    lib().vo_linear_bf16(_p(x), n_rows, in_dim, _p(w, U16P), out_dim,
+                         _p(b) if b is not None else None, _p(out))
+    return out
+
+
+def add_inplace(dst, src):
+    """ops.rs:41-46 (returns the updated copy)"""
+    d = _f32(dst).copy()
+    s = _f32(src)
+    lib().vo_add_inplace(_p(d), _p(s), d.size)
+    return d
+
+
+def attention_gqa_step(q, k, v, n_heads, head_dim, seq_len, n_kv_heads, sliding_window):
+    """ops.rs:66-132"""
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    out = np.zeros(n_heads * head_dim, np.float32)
+    lib().vo_attention_gqa_step(_p(q), _p(k), _p(v), n_heads, head_dim, seq_len,
+                                n_kv_heads, sliding_window, _p(out))
+    return out
+
+
+# ---- kv.rs -----------------------------------------------------------------
+
+class RollingKvCache:
+    """kv.rs:22-101"""
+
+    def __init__(self, n_layers, n_kv_heads, head_dim, sliding_window, _handle=None):
+        self.n_layers, self.n_kv_heads, self.head_dim = n_layers, n_kv_heads, head_dim
+        self.sliding_window = sliding_window
+        self.h = _handle or lib().vo_kv_new(n_layers, n_kv_heads, head_dim, sliding_window)
+
+    def __del__(self):
+        if getattr(self, "h", None) and _lib is not None:
+            _lib.vo_kv_free(self.h)
+            self.h = None
+
+    def clone(self):
+        return RollingKvCache(self.n_layers, self.n_kv_heads, self.head_dim,
+                              self.sliding_window, lib().vo_kv_clone(self.h))
+
+    def append_layer(self, layer, k_new, v_new, n_new):
+        k, v = _f32(k_new), _f32(v_new)
+        lib().vo_kv_append_layer(self.h, layer, _p(k), _p(v), n_new)
+
+    def layer_len_tokens(self, layer):
+        return lib().vo_kv_layer_len_tokens(self.h, layer)
+
+    def layer_pos_offset(self, layer):
+        return lib().vo_kv_layer_pos_offset(self.h, layer)
+
+    def layer_tensors(self, layer):
+        n = self.layer_len_tokens(layer) * self.n_kv_heads * self.head_dim
+        if n == 0:
+            return np.zeros(0, np.float32), np.zeros(0, np.float32)
+        k = np.ctypeslib.as_array(lib().vo_kv_layer_keys(self.h, layer), shape=(n,)).copy()
+        v = np.ctypeslib.as_array(lib().vo_kv_layer_values(self.h, layer), shape=(n,)).copy()
+        return k, v
+
+    def layer_set(self, layer, keys, values, len_tokens, pos_offset):
+        k, v = _f32(keys), _f32(values)
+        lib().vo_kv_layer_set(self.h, layer, _p(k), _p(v), len_tokens, pos_offset)
+
+
+# ---- decoder.rs ------------------------------------------------------------
+
+class LayerWeights:
+    """DecoderLayerWeights (decoder.rs:45-55).  Matrices are f32 arrays, or
+    bf16 bit patterns (uint16) that the oracle widens exactly."""
+
+    NAMES = ("wq", "wk", "wv", "wo", "w1", "w2", "w3")
+
+    def __init__(self, attention_norm, ffn_norm, **mats):
+        self.attention_norm = _f32(attention_norm)
+        self.ffn_norm = _f32(ffn_norm)
+        first = mats["wq"]
+        self.bf16 = first.dtype == np.uint16
+        self.mats = {}
+        for n in self.NAMES:
+            a = mats[n]
+            self.mats[n] = (np.ascontiguousarray(a, dtype=np.uint16) if self.bf16 else _f32(a))
+        self.c = VoLayerWeights()
+        self.c.bf16 = 1 if self.bf16 else 0
+        self.c.attention_norm = _p(self.attention_norm)
+        self.c.ffn_norm = _p(self.ffn_norm)
+        for n in self.NAMES:
+            if self.bf16:
+                setattr(self.c, n + "_h", _p(self.mats[n], U16P))
+            else:
+                setattr(self.c, n, _p(self.mats[n]))
+
+
+def config_validate(cfg: VoConfig) -> int:
+    """decoder.rs:22-41; returns 0 or the VO_ERR_* code of the first failed check."""
+    return lib().vo_config_validate(C.byref(cfg))
+
+
+def decoder_layer_forward_step(cfg, layer_idx, weights: LayerWeights, cache: RollingKvCache,
+                               hidden, pos):
+    """decoder.rs:88-155.  Raises ValueError on the reference's Err cases."""
+    h = _f32(hidden)
+    out = np.zeros(cfg.dim, np.float32)
+    rc = lib().vo_decoder_layer_forward_step(C.byref(cfg), layer_idx, C.byref(weights.c),
+                                             cache.h, _p(h), h.size, pos, _p(out))
+    if rc:
+        raise ValueError(f"oracle decoder step failed with code {rc}")
+    return out
+
+
+class Model:
+    """Composed token loop: embed -> layers -> final norm -> LM head -> argmax."""
+
+    def __init__(self, cfg, layers, embed_bits, final_norm, lm_head_bits, vocab):
+        self.cfg, self.layers = cfg, layers
+        self.embed = np.ascontiguousarray(embed_bits, dtype=np.uint16)
+        self.final_norm = _f32(final_norm)
+        self.lm_head = np.ascontiguousarray(lm_head_bits, dtype=np.uint16)
+        self._arr = (VoLayerWeights * len(layers))(*[l.c for l in layers])
+        self.c = VoModel(cfg, len(layers), vocab, self._arr, _p(self.embed, U16P),
+                         _p(self.final_norm), _p(self.lm_head, U16P))
+        self.vocab = vocab
+
+    def step(self, cache, token, pos, want_logits=True):
+        logits = np.zeros(self.vocab, np.float32) if want_logits else None
+        am = C.c_int32(-1)
+        rc = lib().vo_model_step(C.byref(self.c), cache.h, int(token), int(pos),
+                                 _p(logits) if want_logits else None, C.byref(am))
+        if rc:
+            raise ValueError(f"oracle model step failed with code {rc}")
+        return logits, am.value
+
+
+# ---- seeded synthetic data ---------------------------------------------------
+
+def gen_normal_f32(seed, tensor_id, std, n, first=0):
+    out = np.empty(n, np.float32)
+    lib().vo_gen_normal_f32(seed, tensor_id, std, first, n, _p(out))
+    return out
+
+
+def gen_normal_bf16(seed, tensor_id, std, n, first=0):
+    out = np.empty(n, np.uint16)
+    lib().vo_gen_normal_bf16(seed, tensor_id, std, first, n, _p(out, U16P))
+    return out
+
+
+def gen_uniform_ids(seed, tensor_id, bound, n, first=0):
+    out = np.empty(n, np.int32)
+    lib().vo_gen_uniform_ids(seed, tensor_id, bound, first, n, _p(out, I32P))
+    return out
+
+
+def bf16_to_f32(bits):
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16(x):
+    x = _f32(x)
+    u = x.view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    nan = np.isnan(x)
+    r[nan] = 0x7FC0
+    return r

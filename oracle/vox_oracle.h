@@ -1,0 +1,142 @@
+/*
+ * vox_oracle.h -- CPU oracle for the voxtral-rust decoder token loop.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This is a plain-C restatement of the reference
+ * crate's CPU kernels (crates/voxtral/src/{math,ops,kv,decoder}.rs).  It is
+ * the checker the CUDA library is compared against; nothing in the product
+ * path links, loads or calls it.  Only tests/, __graft_entry__.smoke() and
+ * bench.py's CPU-baseline leg use it.
+ *
+ * Exactness rules followed throughout (they mirror what rustc emits for the
+ * reference): f32 arithmetic, the same loop order for every reduction, no
+ * FMA contraction and no fast-math (the Makefile passes -ffp-contract=off),
+ * and libm expf/powf/sinf/cosf for Rust's f32::exp/powf/sin_cos.
+ *
+ * Parity pin: the reference is Rust and no Rust toolchain exists in this
+ * build environment, so the crate cannot be run to produce outputs.  The
+ * oracle is pinned to the reference's own unit tests (their inputs and
+ * expected values are committed as fixtures under tests/golden/).
+ */
+#ifndef VOX_ORACLE_H
+#define VOX_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* DecoderConfig, decoder.rs:10-19 (usize fields as size_t). */
+typedef struct vo_config {
+    size_t dim;
+    size_t hidden_dim;
+    size_t n_heads;
+    size_t n_kv_heads;
+    size_t head_dim;
+    size_t sliding_window;
+    float norm_eps;
+    float rope_theta;
+} vo_config;
+
+/* Error codes returned by the oracle's fallible functions (0 = Ok). */
+enum {
+    VO_OK = 0,
+    VO_ERR_DIM = 1,          /* "dim must be > 0" */
+    VO_ERR_HIDDEN_DIM = 2,   /* "hidden_dim must be > 0" */
+    VO_ERR_N_HEADS = 3,      /* "n_heads must be > 0" */
+    VO_ERR_N_KV_HEADS = 4,   /* "n_kv_heads must be > 0" */
+    VO_ERR_HEAD_DIM = 5,     /* "head_dim must be > 0" */
+    VO_ERR_GQA_DIVISIBLE = 6,/* "n_heads must be divisible by n_kv_heads" */
+    VO_ERR_COVER_DIM = 7,    /* "n_heads * head_dim must cover dim" */
+    VO_ERR_WINDOW = 8,       /* "sliding_window must be > 0 ..." */
+    VO_ERR_HIDDEN_LEN = 9,   /* "hidden size mismatch" */
+    VO_ERR_WEIGHT_SHAPE = 10,/* "<tensor> shape mismatch" */
+    VO_ERR_ARG = 11          /* bad argument to a composed (non-reference) helper */
+};
+
+void vo_set_threads(int n);
+int vo_get_threads(void);
+
+/* ---- math.rs ---------------------------------------------------------- */
+void vo_silu_inplace(float* x, size_t n);
+void vo_rms_norm_rows(float* out, const float* in, const float* weight,
+                      size_t n_elems, size_t dim, float eps);
+void vo_rope_interleaved_inplace(float* data, size_t seq_len, size_t n_heads,
+                                 size_t head_dim, size_t pos_offset, float theta);
+void vo_softmax_inplace(float* x, size_t n);
+
+/* ---- ops.rs ----------------------------------------------------------- */
+void vo_linear(const float* input, size_t n_rows, size_t in_dim,
+               const float* weight, size_t out_dim, const float* bias,
+               float* out);
+/* Same as vo_linear with weight[o*in+i] = f32(bf16 bits << 16) (weights.rs:77-81). */
+void vo_linear_bf16(const float* input, size_t n_rows, size_t in_dim,
+                    const uint16_t* weight, size_t out_dim, const float* bias,
+                    float* out);
+void vo_add_inplace(float* dst, const float* src, size_t n);
+void vo_attention_gqa_step(const float* query, const float* keys,
+                           const float* values, size_t n_heads,
+                           size_t head_dim, size_t seq_len, size_t n_kv_heads,
+                           size_t sliding_window, float* out);
+
+/* ---- kv.rs ------------------------------------------------------------ */
+typedef struct vo_kv vo_kv;
+vo_kv* vo_kv_new(size_t n_layers, size_t n_kv_heads, size_t head_dim,
+                 size_t sliding_window);
+void vo_kv_free(vo_kv* kv);
+vo_kv* vo_kv_clone(const vo_kv* kv);
+void vo_kv_append_layer(vo_kv* kv, size_t layer, const float* k_new,
+                        const float* v_new, size_t n_new_tokens);
+size_t vo_kv_layer_len_tokens(const vo_kv* kv, size_t layer);
+size_t vo_kv_layer_pos_offset(const vo_kv* kv, size_t layer);
+const float* vo_kv_layer_keys(const vo_kv* kv, size_t layer);
+const float* vo_kv_layer_values(const vo_kv* kv, size_t layer);
+/* Overwrite a layer's logical contents (used to pre-fill a context). */
+int vo_kv_layer_set(vo_kv* kv, size_t layer, const float* keys,
+                    const float* values, size_t len_tokens, size_t pos_offset);
+
+/* ---- decoder.rs ------------------------------------------------------- */
+typedef struct vo_layer_weights {
+    /* Exactly one of the f32 / bf16 pointers of each matrix is used: the
+     * bf16 ones when `bf16` is non-zero.  Norm gains are always f32. */
+    int bf16;
+    const float* attention_norm;
+    const float* ffn_norm;
+    const float *wq, *wk, *wv, *wo, *w1, *w2, *w3;
+    const uint16_t *wq_h, *wk_h, *wv_h, *wo_h, *w1_h, *w2_h, *w3_h;
+} vo_layer_weights;
+
+int vo_config_validate(const vo_config* cfg);
+int vo_decoder_layer_forward_step(const vo_config* cfg, size_t layer_idx,
+                                  const vo_layer_weights* w, vo_kv* cache,
+                                  const float* hidden, size_t hidden_len,
+                                  size_t pos, float* out);
+
+/* ---- composed token loop (not in the reference) -------- */
+typedef struct vo_model {
+    vo_config cfg;
+    size_t n_layers;
+    size_t vocab;
+    const vo_layer_weights* layers; /* n_layers entries */
+    const uint16_t* embed;          /* [vocab, dim] bf16 */
+    const float* final_norm;        /* [dim] */
+    const uint16_t* lm_head;        /* [vocab, dim] bf16 */
+} vo_model;
+
+int vo_model_step(const vo_model* m, vo_kv* cache, int32_t token, size_t pos,
+                  float* logits_out, int32_t* argmax_out);
+
+/* ---- seeded synthetic data (counter-based, bit-exact on any IEEE target) */
+void vo_gen_normal_f32(uint64_t seed, uint64_t tensor_id, float std_scale,
+                       uint64_t first, size_t n, float* out);
+void vo_gen_normal_bf16(uint64_t seed, uint64_t tensor_id, float std_scale,
+                        uint64_t first, size_t n, uint16_t* out);
+void vo_gen_uniform_ids(uint64_t seed, uint64_t tensor_id, uint32_t bound,
+                        uint64_t first, size_t n, int32_t* out);
+uint16_t vo_f32_to_bf16_rne(float f);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
