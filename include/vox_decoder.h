@@ -1,0 +1,224 @@
+/*
+ * vox_decoder.h -- C ABI of the B200 (sm_100a) decoder-token-loop library.
+ *
+ * This is the drop-in boundary for the decoder path of voxtral-rust
+ * (crates/voxtral/src/{decoder,kv,ops,math}.rs).  Every entry point names the
+ * reference item it replaces.  Conventions:
+ *   - every function returns an int status (VOX_OK == 0); on failure
+ *     vox_last_error() returns a thread-local message for the last failure
+ *     on the calling thread (the reference returns anyhow::Error);
+ *   - host buffers are borrowed for the duration of the call only; the
+ *     library copies what it keeps (weights are copied to device memory);
+ *   - a vox_ctx owns one CUDA device and one CUDA stream.  A context and the
+ *     caches made from it are single-thread-affine, the same discipline as
+ *     the reference's `&mut RollingKvCache`.
+ *
+ * Numerics: activations, KV cache and accumulation are f32.  Weight
+ * matrices are held as bf16 by default (VOX_WEIGHTS_BF16); bf16 weights
+ * widened to f32 are exactly the f32 weights the reference would use
+ * (weights.rs:77-81).  VOX_WEIGHTS_F32 keeps f32 weights for callers whose
+ * weights are not bf16-representable.
+ */
+#ifndef VOX_DECODER_H
+#define VOX_DECODER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VOX_ABI_VERSION 1
+
+typedef enum vox_status {
+    VOX_OK = 0,
+    VOX_ERR_INVALID_ARG = 1,    /* null pointer, index out of range */
+    VOX_ERR_CONFIG = 2,         /* DecoderConfig::validate failed (decoder.rs:22-41) */
+    VOX_ERR_SHAPE = 3,          /* length mismatch (decoder.rs:58-84, :98) */
+    VOX_ERR_UNSUPPORTED = 4,    /* shape the kernels do not handle (message says which) */
+    VOX_ERR_CUDA = 5,           /* CUDA runtime error (message has the CUDA string) */
+    VOX_ERR_OOM = 6,            /* device or pinned allocation failed */
+    VOX_ERR_NOT_READY = 7,      /* weights needed by the call were never uploaded */
+    VOX_ERR_DEVICE_TIMEOUT = 8, /* a bounded wait inside a kernel expired */
+    VOX_ERR_RANGE = 9           /* position beyond the RoPE table, token outside the vocab */
+} vox_status;
+
+typedef enum vox_weight_dtype { VOX_WEIGHTS_BF16 = 0, VOX_WEIGHTS_F32 = 1 } vox_weight_dtype;
+
+/* DecoderConfig (decoder.rs:10-19), field for field. */
+typedef struct vox_decoder_config {
+    size_t dim;
+    size_t hidden_dim;
+    size_t n_heads;
+    size_t n_kv_heads;
+    size_t head_dim;
+    size_t sliding_window;
+    float norm_eps;
+    float rope_theta;
+} vox_decoder_config;
+
+/* Options of a context.  Zero-initialise and set what you need; zero means
+ * "default" for every field. */
+typedef struct vox_ctx_options {
+    int device;               /* CUDA device ordinal */
+    size_t n_layers;          /* layers whose weights the context holds (default 1) */
+    size_t vocab;             /* vocabulary for the token loop; 0 = no embedding / LM head */
+    size_t max_positions;     /* RoPE table length; positions must stay below it (default 32768) */
+    int weight_dtype;         /* vox_weight_dtype */
+} vox_ctx_options;
+
+typedef struct vox_f32_slice { const float* ptr; size_t len; } vox_f32_slice;
+typedef struct vox_bf16_slice { const uint16_t* ptr; size_t len; } vox_bf16_slice;
+
+/* DecoderLayerWeights (decoder.rs:45-55), f32 flavour: the reference's own
+ * struct.  Matrices are row-major [out, in] as in the reference. */
+typedef struct vox_layer_weights_f32 {
+    vox_f32_slice attention_norm, wq, wk, wv, wo, ffn_norm, w1, w2, w3;
+} vox_layer_weights_f32;
+
+/* Same tensors with matrices given as bf16 bit patterns. */
+typedef struct vox_layer_weights_bf16 {
+    vox_f32_slice attention_norm;
+    vox_bf16_slice wq, wk, wv, wo;
+    vox_f32_slice ffn_norm;
+    vox_bf16_slice w1, w2, w3;
+} vox_layer_weights_bf16;
+
+/* AttentionShape (ops.rs:49-56). sliding_window 0 = no window. */
+typedef struct vox_attention_shape {
+    size_t n_heads;
+    size_t head_dim;
+    size_t seq_len;
+    size_t n_kv_heads;
+    size_t sliding_window;
+} vox_attention_shape;
+
+typedef struct vox_ctx vox_ctx;
+typedef struct vox_kv vox_kv;
+
+/* ---- errors and config --------------------------------------------------- */
+const char* vox_last_error(void);
+int vox_abi_version(void);
+/* DecoderConfig::validate (decoder.rs:22-41); same checks, same order. */
+int vox_config_validate(const vox_decoder_config* cfg);
+/* DecoderLayerWeights::validate (decoder.rs:58-84). */
+int vox_layer_weights_validate_f32(const vox_decoder_config* cfg, const vox_layer_weights_f32* w);
+int vox_layer_weights_validate_bf16(const vox_decoder_config* cfg, const vox_layer_weights_bf16* w);
+
+/* ---- context and weights ------------------------------------------------- */
+int vox_ctx_create(const vox_decoder_config* cfg, const vox_ctx_options* opt, vox_ctx** out);
+void vox_ctx_destroy(vox_ctx* ctx);
+/* Copy one layer's weights to the device (caller keeps ownership).  With
+ * VOX_WEIGHTS_BF16 the f32 upload rounds matrices to bf16, nearest-even. */
+int vox_ctx_upload_layer_f32(vox_ctx* ctx, size_t layer, const vox_layer_weights_f32* w);
+int vox_ctx_upload_layer_bf16(vox_ctx* ctx, size_t layer, const vox_layer_weights_bf16* w);
+/* Token loop tensors (no reference counterpart: the reference stops at one
+ * layer step).  embed and lm_head are [vocab, dim] bf16; final_norm [dim]. */
+int vox_ctx_upload_embed_bf16(vox_ctx* ctx, const uint16_t* embed, size_t len);
+int vox_ctx_upload_lm_head_bf16(vox_ctx* ctx, const uint16_t* lm_head, size_t len);
+int vox_ctx_upload_final_norm(vox_ctx* ctx, const float* gain, size_t len);
+/* Fill every weight on the device from the library's counter-based
+ * generator (bit-identical to the oracle's): matrices ~N(0, std^2) rounded
+ * to the weight dtype, norm gains 1.0. */
+int vox_ctx_init_random(vox_ctx* ctx, uint64_t seed, float std);
+/* Copy a stored matrix back in reference layout (for checks).
+ * which: 0 wq 1 wk 2 wv 3 wo 4 w1 5 w2 6 w3 7 embed 8 lm_head.  Output is
+ * bf16 bits (uint16) or f32 according to the context's weight dtype. */
+int vox_ctx_download_matrix(vox_ctx* ctx, size_t layer, int which, void* out, size_t out_bytes);
+/* The context's CUDA stream (cudaStream_t) and a synchronise helper. */
+void* vox_ctx_stream(vox_ctx* ctx);
+int vox_ctx_synchronize(vox_ctx* ctx);
+/* CUDA-event timing on the context's stream (slots 0..15). */
+int vox_ctx_record_event(vox_ctx* ctx, int slot);
+int vox_ctx_event_elapsed_ms(vox_ctx* ctx, int slot_a, int slot_b, float* ms);
+/* Kernel launches issued by the library since the context was created. */
+uint64_t vox_ctx_kernel_launches(vox_ctx* ctx);
+
+/* ---- rolling KV cache (kv.rs) --------------------------------------------- */
+/* RollingKvCache::new (kv.rs:33-46).  Device ring of `sliding_window` tokens
+ * per layer; eviction is index arithmetic, not a copy. */
+int vox_kv_create(vox_ctx* ctx, size_t n_layers, size_t n_kv_heads, size_t head_dim,
+                  size_t sliding_window, vox_kv** out);
+/* Same with a ring larger than the window, for callers that append more
+ * than `sliding_window` tokens in one call (kv.rs:64-74 keeps them all). */
+int vox_kv_create_ex(vox_ctx* ctx, size_t n_layers, size_t n_kv_heads, size_t head_dim,
+                     size_t sliding_window, size_t capacity_tokens, vox_kv** out);
+void vox_kv_destroy(vox_kv* kv);
+/* RollingKvCache::append_layer (kv.rs:48-88); k_new/v_new are host
+ * [n_new, n_kv_heads, head_dim] f32. */
+int vox_kv_append_layer(vox_kv* kv, size_t layer, const float* k_new, const float* v_new,
+                        size_t n_new_tokens);
+/* layer_len_tokens (kv.rs:90), layer_pos_offset (kv.rs:94). */
+int vox_kv_layer_len_tokens(const vox_kv* kv, size_t layer, size_t* out);
+int vox_kv_layer_pos_offset(const vox_kv* kv, size_t layer, size_t* out);
+/* layer_tensors (kv.rs:98-101): copies the layer's K and V to host in the
+ * reference's logical order [len_tokens, n_kv_heads, head_dim].  Each
+ * buffer must hold at least len_tokens*n_kv_heads*head_dim floats
+ * (capacity given in elements). */
+int vox_kv_layer_tensors(const vox_kv* kv, size_t layer, float* keys, float* values,
+                         size_t capacity_elems);
+/* Device-side ring bookkeeping of a layer, for index checks:
+ * out[0] = len_tokens, out[1] = physical start slot, out[2] = pos_offset. */
+int vox_kv_layer_device_state(const vox_kv* kv, size_t layer, int64_t out[3]);
+/* Forget every token (all layers back to len 0, pos_offset 0). */
+int vox_kv_reset(vox_kv* kv);
+
+/* ---- decoder step (decoder.rs:88-155) -------------------------------------- */
+/* decoder_layer_forward_step: hidden [dim] f32 in, out [dim] f32 (the
+ * reference returns a new Vec; here the caller owns `out`).  Appends one
+ * token to `layer_idx` of the cache. */
+int vox_decoder_layer_forward_step(vox_ctx* ctx, size_t layer_idx, vox_kv* kv,
+                                   const float* hidden, size_t hidden_len, size_t pos,
+                                   float* out, size_t out_len);
+
+/* ---- composed token loop (no reference counterpart, see header text) ----- */
+/* One token through embed -> all layers -> final RMSNorm -> LM head ->
+ * argmax (lowest index wins ties).  Runs as one CUDA graph.  logits_out
+ * (nullable) receives [vocab] f32. */
+int vox_model_step(vox_ctx* ctx, vox_kv* kv, int32_t token, size_t pos, int32_t* next_token,
+                   float* logits_out);
+/* Greedy decode of n_steps tokens starting from `token` at `pos`, entirely
+ * on the device (each step's argmax feeds the next).  tokens_out [n_steps]. */
+int vox_model_generate(vox_ctx* ctx, vox_kv* kv, int32_t token, size_t pos, size_t n_steps,
+                       int32_t* tokens_out);
+/* Sequential prefill of n tokens at positions pos0.. (logits discarded). */
+int vox_model_prefill(vox_ctx* ctx, vox_kv* kv, const int32_t* tokens, size_t n, size_t pos0);
+
+/* ---- profiling hook (no reference counterpart) --------------------------------- */
+/* Times one of the step's weight-streaming GEMVs on its own: n_launches
+ * back-to-back launches (cycling over the layers, so every launch streams a
+ * different matrix from HBM) with programmatic dependent launch, bracketed by
+ * CUDA events on the context's stream.  which: 1 o-proj, 2 w1|w3 (SwiGLU),
+ * 3 w2, 4 LM head.  Writes activations only (no cache state changes).
+ * avg_ms = mean duration per launch; bytes_per_launch = weight bytes each
+ * launch streams. */
+int vox_profile_gemv(vox_ctx* ctx, int which, size_t n_launches, float* avg_ms,
+                     uint64_t* bytes_per_launch);
+
+/* ---- op-level entry points (host buffers) ------------------------------------ */
+/* linear (ops.rs:11-39): out[n_rows, out_dim] = input[n_rows, in_dim] * W^T + bias. */
+int vox_linear_f32(vox_ctx* ctx, const float* input, size_t n_rows, size_t in_dim,
+                   const float* weight, size_t out_dim, const float* bias, float* out);
+int vox_linear_bf16(vox_ctx* ctx, const float* input, size_t n_rows, size_t in_dim,
+                    const uint16_t* weight, size_t out_dim, const float* bias, float* out);
+/* add_inplace (ops.rs:41-46). */
+int vox_add_inplace(vox_ctx* ctx, float* dst, const float* src, size_t n);
+/* attention_gqa_step (ops.rs:66-132): q [n_heads, head_dim]; keys/values
+ * [seq_len, n_kv_heads, head_dim]; out [n_heads, head_dim]. */
+int vox_attention_gqa_step(vox_ctx* ctx, const float* query, const float* keys,
+                           const float* values, const vox_attention_shape* shape, float* out);
+/* rms_norm_rows (math.rs:11-27). */
+int vox_rms_norm_rows(vox_ctx* ctx, float* out, const float* input, const float* weight,
+                      size_t n_elems, size_t dim, float eps);
+/* rope_interleaved_inplace (math.rs:30-65): data [seq_len, n_heads, head_dim]. */
+int vox_rope_interleaved_inplace(vox_ctx* ctx, float* data, size_t seq_len, size_t n_heads,
+                                 size_t head_dim, size_t pos_offset, float theta);
+/* silu_inplace (math.rs:4-9), softmax_inplace (math.rs:67-88). */
+int vox_silu_inplace(vox_ctx* ctx, float* x, size_t n);
+int vox_softmax_inplace(vox_ctx* ctx, float* x, size_t n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VOX_DECODER_H */

@@ -1,0 +1,433 @@
+"""voxtral-rust_b200 -- B200 (sm_100a) decoder token loop of voxtral-rust.
+
+Python front end over the C ABI in include/vox_decoder.h (libvoxb200.so).
+Names and argument meanings follow the reference crate
+(crates/voxtral/src/{decoder,kv,ops,math}.rs) so that code written against
+it reads the same.  Every compute call runs CUDA kernels; there is no CPU
+fallback: if the shared library is missing the import fails.
+
+The directory name is not a Python identifier; import it with
+``importlib.import_module("voxtral-rust_b200")``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libvoxb200.so")
+HEADER_PATH = os.path.join(os.path.dirname(_HERE), "include", "vox_decoder.h")
+
+F32P = C.POINTER(C.c_float)
+U16P = C.POINTER(C.c_uint16)
+I32P = C.POINTER(C.c_int32)
+SZ = C.c_size_t
+VP = C.c_void_p
+
+OK, ERR_INVALID_ARG, ERR_CONFIG, ERR_SHAPE, ERR_UNSUPPORTED, ERR_CUDA, ERR_OOM, ERR_NOT_READY, \
+    ERR_DEVICE_TIMEOUT, ERR_RANGE = range(10)
+WEIGHTS_BF16, WEIGHTS_F32 = 0, 1
+
+
+class VoxError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"[{code}] {message}")
+        self.code = code
+        self.message = message
+
+
+class DecoderConfig(C.Structure):
+    """DecoderConfig (decoder.rs:10-19)."""
+
+    _fields_ = [("dim", SZ), ("hidden_dim", SZ), ("n_heads", SZ), ("n_kv_heads", SZ),
+                ("head_dim", SZ), ("sliding_window", SZ), ("norm_eps", C.c_float),
+                ("rope_theta", C.c_float)]
+
+    def validate(self):
+        """DecoderConfig::validate (decoder.rs:22-41)."""
+        _check(lib().vox_config_validate(C.byref(self)))
+
+
+class CtxOptions(C.Structure):
+    _fields_ = [("device", C.c_int), ("n_layers", SZ), ("vocab", SZ), ("max_positions", SZ),
+                ("weight_dtype", C.c_int)]
+
+
+class F32Slice(C.Structure):
+    _fields_ = [("ptr", F32P), ("len", SZ)]
+
+
+class BF16Slice(C.Structure):
+    _fields_ = [("ptr", U16P), ("len", SZ)]
+
+
+_NAMES = ("attention_norm", "wq", "wk", "wv", "wo", "ffn_norm", "w1", "w2", "w3")
+
+
+class LayerWeightsF32(C.Structure):
+    _fields_ = [(n, F32Slice) for n in _NAMES]
+
+
+class LayerWeightsBF16(C.Structure):
+    _fields_ = [("attention_norm", F32Slice), ("wq", BF16Slice), ("wk", BF16Slice),
+                ("wv", BF16Slice), ("wo", BF16Slice), ("ffn_norm", F32Slice),
+                ("w1", BF16Slice), ("w2", BF16Slice), ("w3", BF16Slice)]
+
+
+class AttentionShape(C.Structure):
+    """AttentionShape (ops.rs:49-56)."""
+
+    _fields_ = [("n_heads", SZ), ("head_dim", SZ), ("seq_len", SZ), ("n_kv_heads", SZ),
+                ("sliding_window", SZ)]
+
+
+_lib = None
+
+_SIGS = {
+    "vox_last_error": ([], C.c_char_p),
+    "vox_abi_version": ([], C.c_int),
+    "vox_config_validate": ([C.POINTER(DecoderConfig)], C.c_int),
+    "vox_layer_weights_validate_f32": ([C.POINTER(DecoderConfig), C.POINTER(LayerWeightsF32)], C.c_int),
+    "vox_layer_weights_validate_bf16": ([C.POINTER(DecoderConfig), C.POINTER(LayerWeightsBF16)], C.c_int),
+    "vox_ctx_create": ([C.POINTER(DecoderConfig), C.POINTER(CtxOptions), C.POINTER(VP)], C.c_int),
+    "vox_ctx_destroy": ([VP], None),
+    "vox_ctx_upload_layer_f32": ([VP, SZ, C.POINTER(LayerWeightsF32)], C.c_int),
+    "vox_ctx_upload_layer_bf16": ([VP, SZ, C.POINTER(LayerWeightsBF16)], C.c_int),
+    "vox_ctx_upload_embed_bf16": ([VP, U16P, SZ], C.c_int),
+    "vox_ctx_upload_lm_head_bf16": ([VP, U16P, SZ], C.c_int),
+    "vox_ctx_upload_final_norm": ([VP, F32P, SZ], C.c_int),
+    "vox_ctx_init_random": ([VP, C.c_uint64, C.c_float], C.c_int),
+    "vox_ctx_download_matrix": ([VP, SZ, C.c_int, VP, SZ], C.c_int),
+    "vox_ctx_stream": ([VP], VP),
+    "vox_ctx_synchronize": ([VP], C.c_int),
+    "vox_ctx_record_event": ([VP, C.c_int], C.c_int),
+    "vox_ctx_event_elapsed_ms": ([VP, C.c_int, C.c_int, F32P], C.c_int),
+    "vox_ctx_kernel_launches": ([VP], C.c_uint64),
+    "vox_kv_create": ([VP, SZ, SZ, SZ, SZ, C.POINTER(VP)], C.c_int),
+    "vox_kv_create_ex": ([VP, SZ, SZ, SZ, SZ, SZ, C.POINTER(VP)], C.c_int),
+    "vox_kv_destroy": ([VP], None),
+    "vox_kv_append_layer": ([VP, SZ, F32P, F32P, SZ], C.c_int),
+    "vox_kv_layer_len_tokens": ([VP, SZ, C.POINTER(SZ)], C.c_int),
+    "vox_kv_layer_pos_offset": ([VP, SZ, C.POINTER(SZ)], C.c_int),
+    "vox_kv_layer_tensors": ([VP, SZ, F32P, F32P, SZ], C.c_int),
+    "vox_kv_layer_device_state": ([VP, SZ, C.POINTER(C.c_int64)], C.c_int),
+    "vox_kv_reset": ([VP], C.c_int),
+    "vox_decoder_layer_forward_step": ([VP, SZ, VP, F32P, SZ, SZ, F32P, SZ], C.c_int),
+    "vox_model_step": ([VP, VP, C.c_int32, SZ, I32P, F32P], C.c_int),
+    "vox_model_generate": ([VP, VP, C.c_int32, SZ, SZ, I32P], C.c_int),
+    "vox_model_prefill": ([VP, VP, I32P, SZ, SZ], C.c_int),
+    "vox_profile_gemv": ([VP, C.c_int, SZ, F32P, C.POINTER(C.c_uint64)], C.c_int),
+    "vox_linear_f32": ([VP, F32P, SZ, SZ, F32P, SZ, F32P, F32P], C.c_int),
+    "vox_linear_bf16": ([VP, F32P, SZ, SZ, U16P, SZ, F32P, F32P], C.c_int),
+    "vox_add_inplace": ([VP, F32P, F32P, SZ], C.c_int),
+    "vox_attention_gqa_step": ([VP, F32P, F32P, F32P, C.POINTER(AttentionShape), F32P], C.c_int),
+    "vox_rms_norm_rows": ([VP, F32P, F32P, F32P, SZ, SZ, C.c_float], C.c_int),
+    "vox_rope_interleaved_inplace": ([VP, F32P, SZ, SZ, SZ, SZ, C.c_float], C.c_int),
+    "vox_silu_inplace": ([VP, F32P, SZ], C.c_int),
+    "vox_softmax_inplace": ([VP, F32P, SZ], C.c_int),
+}
+
+
+def lib():
+    """Load libvoxb200.so (build it with voxtral-rust_b200/build.py)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"libvoxb200.so not built: run python {os.path.join(_HERE, 'build.py')}")
+        L = C.CDLL(LIB_PATH)
+        for name, (args, res) in _SIGS.items():
+            f = getattr(L, name)
+            f.argtypes = args
+            f.restype = res
+        _lib = L
+    return _lib
+
+
+def header_symbols():
+    """Entry points declared in include/vox_decoder.h."""
+    import re
+    text = open(HEADER_PATH).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[\w\*]+\s+\**(vox_\w+)\s*\(", text, re.M)))
+
+
+def last_error() -> str:
+    return lib().vox_last_error().decode(errors="replace")
+
+
+def _check(rc: int):
+    if rc != OK:
+        raise VoxError(rc, last_error())
+
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _p(a, t=F32P):
+    return a.ctypes.data_as(t) if a is not None else None
+
+
+# ---------------------------------------------------------------------------
+# Context (device, stream, weights)
+# ---------------------------------------------------------------------------
+
+class Context:
+    """A CUDA device plus the decoder weights it holds."""
+
+    def __init__(self, cfg: DecoderConfig, n_layers=1, vocab=0, device=0, max_positions=0,
+                 weight_dtype=WEIGHTS_BF16):
+        self.cfg = cfg
+        self.n_layers, self.vocab = n_layers, vocab
+        self.weight_dtype = weight_dtype
+        opt = CtxOptions(device, n_layers, vocab, max_positions, weight_dtype)
+        h = VP()
+        _check(lib().vox_ctx_create(C.byref(cfg), C.byref(opt), C.byref(h)))
+        self.h = h.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().vox_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def upload_layer(self, layer, weights: dict):
+        """weights: the nine DecoderLayerWeights tensors (decoder.rs:45-55) as
+        numpy arrays; matrices f32 or uint16 bf16 bit patterns."""
+        keep = {}
+        mats_bf16 = weights["wq"].dtype == np.uint16
+        if mats_bf16:
+            s = LayerWeightsBF16()
+            for n in _NAMES:
+                a = weights[n]
+                if n in ("attention_norm", "ffn_norm"):
+                    a = _f32(a)
+                    setattr(s, n, F32Slice(_p(a), a.size))
+                else:
+                    a = np.ascontiguousarray(a, dtype=np.uint16)
+                    setattr(s, n, BF16Slice(_p(a, U16P), a.size))
+                keep[n] = a
+            _check(lib().vox_ctx_upload_layer_bf16(self.h, layer, C.byref(s)))
+        else:
+            s = LayerWeightsF32()
+            for n in _NAMES:
+                a = _f32(weights[n])
+                setattr(s, n, F32Slice(_p(a), a.size))
+                keep[n] = a
+            _check(lib().vox_ctx_upload_layer_f32(self.h, layer, C.byref(s)))
+
+    def upload_embed(self, bits):
+        a = np.ascontiguousarray(bits, dtype=np.uint16)
+        _check(lib().vox_ctx_upload_embed_bf16(self.h, _p(a, U16P), a.size))
+
+    def upload_lm_head(self, bits):
+        a = np.ascontiguousarray(bits, dtype=np.uint16)
+        _check(lib().vox_ctx_upload_lm_head_bf16(self.h, _p(a, U16P), a.size))
+
+    def upload_final_norm(self, gain):
+        a = _f32(gain)
+        _check(lib().vox_ctx_upload_final_norm(self.h, _p(a), a.size))
+
+    def init_random(self, seed=0, std=0.02):
+        _check(lib().vox_ctx_init_random(self.h, seed, std))
+
+    MATRIX_IDS = {"wq": 0, "wk": 1, "wv": 2, "wo": 3, "w1": 4, "w2": 5, "w3": 6, "embed": 7, "lm_head": 8}
+
+    def download_matrix(self, layer, name):
+        c = self.cfg
+        q_dim, kv_dim = c.n_heads * c.head_dim, c.n_kv_heads * c.head_dim
+        n = {"wq": q_dim * c.dim, "wk": kv_dim * c.dim, "wv": kv_dim * c.dim, "wo": c.dim * q_dim,
+             "w1": c.hidden_dim * c.dim, "w2": c.dim * c.hidden_dim, "w3": c.hidden_dim * c.dim,
+             "embed": self.vocab * c.dim, "lm_head": self.vocab * c.dim}[name]
+        bf16 = name == "embed" or self.weight_dtype == WEIGHTS_BF16
+        out = np.empty(n, np.uint16 if bf16 else np.float32)
+        _check(lib().vox_ctx_download_matrix(self.h, layer, self.MATRIX_IDS[name],
+                                             out.ctypes.data_as(VP), out.nbytes))
+        return out
+
+    def synchronize(self):
+        _check(lib().vox_ctx_synchronize(self.h))
+
+    def record_event(self, slot):
+        _check(lib().vox_ctx_record_event(self.h, slot))
+
+    def elapsed_ms(self, a, b):
+        ms = C.c_float()
+        _check(lib().vox_ctx_event_elapsed_ms(self.h, a, b, C.byref(ms)))
+        return ms.value
+
+    def profile_gemv(self, which, n_launches):
+        """Mean ms per launch and weight bytes per launch of one step GEMV
+        (1 o-proj, 2 w1|w3, 3 w2, 4 LM head) timed on its own."""
+        ms = C.c_float()
+        nb = C.c_uint64()
+        _check(lib().vox_profile_gemv(self.h, which, n_launches, C.byref(ms), C.byref(nb)))
+        return ms.value, nb.value
+
+    def kernel_launches(self):
+        return int(lib().vox_ctx_kernel_launches(self.h))
+
+    # ---- composed token loop ----
+    def model_step(self, cache, token, pos, want_logits=False):
+        nxt = C.c_int32()
+        logits = np.empty(self.vocab, np.float32) if want_logits else None
+        _check(lib().vox_model_step(self.h, cache.h, int(token), int(pos), C.byref(nxt), _p(logits)))
+        return nxt.value, logits
+
+    def model_prefill(self, cache, tokens, pos0=0):
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        _check(lib().vox_model_prefill(self.h, cache.h, _p(t, I32P), t.size, int(pos0)))
+
+    def model_generate(self, cache, token, pos, n_steps):
+        out = np.empty(n_steps, np.int32)
+        _check(lib().vox_model_generate(self.h, cache.h, int(token), int(pos), int(n_steps), _p(out, I32P)))
+        return out
+
+
+# ---------------------------------------------------------------------------
+# RollingKvCache (kv.rs)
+# ---------------------------------------------------------------------------
+
+class RollingKvCache:
+    """RollingKvCache (kv.rs:22-101) as a device ring buffer."""
+
+    def __init__(self, ctx: Context, n_layers, n_kv_heads, head_dim, sliding_window, capacity=None):
+        self.ctx = ctx
+        self.n_layers, self.n_kv_heads, self.head_dim = n_layers, n_kv_heads, head_dim
+        self.sliding_window = sliding_window
+        h = VP()
+        if capacity is None:
+            _check(lib().vox_kv_create(ctx.h, n_layers, n_kv_heads, head_dim, sliding_window, C.byref(h)))
+        else:
+            _check(lib().vox_kv_create_ex(ctx.h, n_layers, n_kv_heads, head_dim, sliding_window,
+                                          capacity, C.byref(h)))
+        self.h = h.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().vox_kv_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def append_layer(self, layer, k_new, v_new, n_new_tokens):
+        k, v = _f32(k_new), _f32(v_new)
+        stride = self.n_kv_heads * self.head_dim
+        if k.size != n_new_tokens * stride or v.size != n_new_tokens * stride:
+            raise ValueError("k_new/v_new must hold n_new_tokens * n_kv_heads * head_dim floats")
+        _check(lib().vox_kv_append_layer(self.h, layer, _p(k), _p(v), n_new_tokens))
+
+    def layer_len_tokens(self, layer):
+        out = SZ()
+        _check(lib().vox_kv_layer_len_tokens(self.h, layer, C.byref(out)))
+        return out.value
+
+    def layer_pos_offset(self, layer):
+        out = SZ()
+        _check(lib().vox_kv_layer_pos_offset(self.h, layer, C.byref(out)))
+        return out.value
+
+    def layer_tensors(self, layer):
+        n = self.layer_len_tokens(layer) * self.n_kv_heads * self.head_dim
+        k = np.empty(n, np.float32)
+        v = np.empty(n, np.float32)
+        _check(lib().vox_kv_layer_tensors(self.h, layer, _p(k), _p(v), n))
+        return k, v
+
+    def device_state(self, layer):
+        out = (C.c_int64 * 3)()
+        _check(lib().vox_kv_layer_device_state(self.h, layer, out))
+        return tuple(out)
+
+    def reset(self):
+        _check(lib().vox_kv_reset(self.h))
+
+
+# ---------------------------------------------------------------------------
+# decoder.rs / ops.rs / math.rs entry points
+# ---------------------------------------------------------------------------
+
+def decoder_layer_forward_step(ctx: Context, layer_idx, cache: RollingKvCache, hidden, pos):
+    """decoder_layer_forward_step (decoder.rs:88-155)."""
+    h = _f32(hidden)
+    out = np.empty(ctx.cfg.dim, np.float32)
+    _check(lib().vox_decoder_layer_forward_step(ctx.h, layer_idx, cache.h, _p(h), h.size, int(pos),
+                                                _p(out), out.size))
+    return out
+
+
+def linear(ctx: Context, x, n_rows, in_dim, weight, out_dim, bias=None):
+    """linear (ops.rs:11-39); weight f32 or uint16 bf16 bits, [out_dim, in_dim]."""
+    x = _f32(x)
+    out = np.empty(n_rows * out_dim, np.float32)
+    b = _f32(bias) if bias is not None else None
+    if weight.dtype == np.uint16:
+        w = np.ascontiguousarray(weight)
+        _check(lib().vox_linear_bf16(ctx.h, _p(x), n_rows, in_dim, _p(w, U16P), out_dim, _p(b), _p(out)))
+    else:
+        w = _f32(weight)
+        _check(lib().vox_linear_f32(ctx.h, _p(x), n_rows, in_dim, _p(w), out_dim, _p(b), _p(out)))
+    return out
+
+
+def add_inplace(ctx: Context, dst, src):
+    """add_inplace (ops.rs:41-46); returns the updated array."""
+    d = _f32(dst).copy()
+    s = _f32(src)
+    if d.size != s.size:
+        raise ValueError("length mismatch")
+    _check(lib().vox_add_inplace(ctx.h, _p(d), _p(s), d.size))
+    return d
+
+
+def attention_gqa_step(ctx: Context, query, keys, values, shape: AttentionShape):
+    """attention_gqa_step (ops.rs:66-132)."""
+    q, k, v = _f32(query), _f32(keys), _f32(values)
+    out = np.empty(shape.n_heads * shape.head_dim, np.float32)
+    _check(lib().vox_attention_gqa_step(ctx.h, _p(q), _p(k), _p(v), C.byref(shape), _p(out)))
+    return out
+
+
+def rms_norm_rows(ctx: Context, x, weight, dim, eps):
+    """rms_norm_rows (math.rs:11-27)."""
+    x, w = _f32(x), _f32(weight)
+    out = np.zeros_like(x)
+    _check(lib().vox_rms_norm_rows(ctx.h, _p(out), _p(x), _p(w), x.size, dim, eps))
+    return out
+
+
+def rope_interleaved_inplace(ctx: Context, data, seq_len, n_heads, head_dim, pos_offset, theta):
+    """rope_interleaved_inplace (math.rs:30-65); returns the rotated array."""
+    d = _f32(data).copy()
+    _check(lib().vox_rope_interleaved_inplace(ctx.h, _p(d), seq_len, n_heads, head_dim, pos_offset, theta))
+    return d
+
+
+def silu_inplace(ctx: Context, x):
+    """silu_inplace (math.rs:4-9)."""
+    d = _f32(x).copy()
+    _check(lib().vox_silu_inplace(ctx.h, _p(d), d.size))
+    return d
+
+
+def softmax_inplace(ctx: Context, x):
+    """softmax_inplace (math.rs:67-88)."""
+    d = _f32(x).copy()
+    _check(lib().vox_softmax_inplace(ctx.h, _p(d), d.size))
+    return d

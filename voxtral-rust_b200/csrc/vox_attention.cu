@@ -1,0 +1,290 @@
+// vox_attention.cu -- grouped-query decode attention over the KV ring.
+//
+// Restates attention_gqa_step (crates/voxtral/src/ops.rs:66-132) for one
+// query token: for every q head h (kv head h / G), scores over the live
+// tokens of the cache, softmax (math.rs:67-88), then the probability-weighted
+// sum of V.  Tokens older than seq_len - sliding_window are masked (ops.rs:
+// 91-95, 102-105).
+//
+// B200 layout: one CTA per (kv head, split of the token range).  The CTA
+// serves all G query heads of its kv head, so each K/V row is read from HBM
+// once per group (the reference reads it G times).  Tiles of 32 tokens are
+// staged in shared memory; the CTA keeps an online-softmax state (running
+// max m, running sum l, unnormalised accumulator) per head.  Split results
+// go to a scratch buffer and the last CTA of each kv head (atomic ticket)
+// merges them with log-sum-exp weights in a fixed split order, so results
+// are run-to-run deterministic.
+//
+// The ring is head-major [n_kv, cap, hd]: logical token t of a layer lives
+// in slot (start + t) % cap, so sliding-window eviction never moves data.
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include "vox_device.cuh"
+
+namespace vox {
+
+namespace {
+
+constexpr int kAttnThreads = 128;
+constexpr int kTile = 32;
+constexpr int kMaxAcc = 4;   // accumulator vectors per thread (G*hd/VEC <= 512)
+
+template <int VEC>
+struct VecT;
+template <>
+struct VecT<1> {
+    using T = float;
+    __device__ static __forceinline__ float dot(const float& a, const float& b) { return a * b; }
+};
+template <>
+struct VecT<4> {
+    using T = float4;
+};
+
+__device__ __forceinline__ float fdot(float acc, const float4& a, const float4& b) {
+    acc = fmaf(a.x, b.x, acc);
+    acc = fmaf(a.y, b.y, acc);
+    acc = fmaf(a.z, b.z, acc);
+    acc = fmaf(a.w, b.w, acc);
+    return acc;
+}
+__device__ __forceinline__ float fdot(float acc, const float& a, const float& b) {
+    return fmaf(a, b, acc);
+}
+__device__ __forceinline__ void faxpy(float4& acc, float p, const float4& v) {
+    acc.x = fmaf(p, v.x, acc.x);
+    acc.y = fmaf(p, v.y, acc.y);
+    acc.z = fmaf(p, v.z, acc.z);
+    acc.w = fmaf(p, v.w, acc.w);
+}
+__device__ __forceinline__ void faxpy(float& acc, float p, const float& v) { acc = fmaf(p, v, acc); }
+__device__ __forceinline__ void fscale(float4& a, float s) {
+    a.x *= s;
+    a.y *= s;
+    a.z *= s;
+    a.w *= s;
+}
+__device__ __forceinline__ void fscale(float& a, float s) { a *= s; }
+__device__ __forceinline__ void fzero(float4& a) { a = make_float4(0.f, 0.f, 0.f, 0.f); }
+__device__ __forceinline__ void fzero(float& a) { a = 0.f; }
+__device__ __forceinline__ float fget(const float4& a, int i) {
+    return i == 0 ? a.x : i == 1 ? a.y : i == 2 ? a.z : a.w;
+}
+__device__ __forceinline__ float fget(const float& a, int) { return a; }
+
+template <int VEC>
+__global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs A) {
+    using T = typename VecT<VEC>::T;
+    extern __shared__ __align__(16) float sm[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int h = blockIdx.x;          // kv head
+    const int split = blockIdx.y;
+    const int hd = A.hd;
+    const int G = A.n_heads / A.n_kv;
+    const int hdv = hd / VEC;          // vectors per row
+    const int pad = VEC == 4 ? 4 : 1;  // row padding (floats) against bank conflicts
+    const int ldk = hd + pad;
+
+    float* q_s = sm;                          // [G, hd]
+    float* k_s = q_s + G * hd;                // [kTile, ldk]
+    float* v_s = k_s + kTile * ldk;           // [kTile, ldk]
+    float* p_s = v_s + kTile * ldk;           // [G, kTile]
+    float* m_s = p_s + G * kTile;             // [G] running max
+    float* l_s = m_s + G;                     // [G] running sum
+    float* a_s = l_s + G;                     // [G] rescale factor of this tile
+    int* flag_s = reinterpret_cast<int*>(a_s + G);
+
+    pdl_allow_dependents();
+    pdl_wait_prior_grids();
+
+    KvState st = *A.st;
+    if (A.pre_append) st = kv_after_single_append(st, A.kv_window, A.cap);
+    const int len = st.len;
+    const int mask_start = (A.cfg_window > 0 && len > A.cfg_window) ? len - A.cfg_window : 0;
+    const int n_live = len - mask_start;
+    int per = (n_live + A.nsplit - 1) / A.nsplit;
+    per = ((per + kTile - 1) / kTile) * kTile;
+    const int t_begin = mask_start + split * per;
+    const int t_end = min(len, t_begin + per);
+
+    for (int i = tid; i < G * hd; i += kAttnThreads) q_s[i] = A.q[(size_t)h * G * hd + i];
+    if (tid < G) {
+        m_s[tid] = -INFINITY;
+        l_s[tid] = 0.f;
+    }
+    T acc[kMaxAcc];
+#pragma unroll
+    for (int j = 0; j < kMaxAcc; ++j) fzero(acc[j]);
+    const int n_out = G * hdv;
+
+    const float* kr = A.k_ring + (size_t)h * A.cap * hd;
+    const float* vr = A.v_ring + (size_t)h * A.cap * hd;
+
+    for (int t0 = t_begin; t0 < t_end; t0 += kTile) {
+        __syncthreads();
+        // Stage K and V rows of this tile (zero beyond t_end).
+        for (int u = tid; u < kTile * hdv; u += kAttnThreads) {
+            const int tt = u / hdv, dv = u - tt * hdv;
+            const int t = t0 + tt;
+            T kv_k, kv_v;
+            if (t < t_end) {
+                int slot = st.start + t;
+                if (slot >= A.cap) slot -= A.cap;
+                kv_k = *reinterpret_cast<const T*>(kr + (size_t)slot * hd + dv * VEC);
+                kv_v = *reinterpret_cast<const T*>(vr + (size_t)slot * hd + dv * VEC);
+            } else {
+                fzero(kv_k);
+                fzero(kv_v);
+            }
+            *reinterpret_cast<T*>(k_s + tt * ldk + dv * VEC) = kv_k;
+            *reinterpret_cast<T*>(v_s + tt * ldk + dv * VEC) = kv_v;
+        }
+        __syncthreads();
+        // Scores: (g, t) pairs; ops.rs:108-113 dot * scale.
+        for (int idx = tid; idx < G * kTile; idx += kAttnThreads) {
+            const int g = idx / kTile, tt = idx - g * kTile;
+            float s = -INFINITY;
+            if (t0 + tt < t_end) {
+                float d = 0.f;
+                const T* qv = reinterpret_cast<const T*>(q_s + g * hd);
+                const T* kv = reinterpret_cast<const T*>(k_s + tt * ldk);
+                for (int dv = 0; dv < hdv; ++dv) d = fdot(d, qv[dv], kv[dv]);
+                s = d * A.scale;
+            }
+            p_s[idx] = s;
+        }
+        __syncthreads();
+        // Online softmax update, one warp per head.
+        for (int g = warp; g < G; g += kAttnThreads / 32) {
+            const float s = p_s[g * kTile + lane];
+            float mt = s;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xFFFFFFFFu, mt, o));
+            const float m_old = m_s[g];
+            const float m_new = fmaxf(m_old, mt);
+            const float p = (s == -INFINITY) ? 0.f : expf(s - m_new);
+            float ps = p;
+#pragma unroll
+            for (int o = 16; o; o >>= 1) ps += __shfl_xor_sync(0xFFFFFFFFu, ps, o);
+            p_s[g * kTile + lane] = p;
+            if (lane == 0) {
+                const float alpha = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
+                a_s[g] = alpha;
+                l_s[g] = l_s[g] * alpha + ps;
+                m_s[g] = m_new;
+            }
+        }
+        __syncthreads();
+        // PV (ops.rs:117-128): acc = acc*alpha + sum_t p_t v_t.
+#pragma unroll
+        for (int j = 0; j < kMaxAcc; ++j) {
+            const int o = tid + j * kAttnThreads;
+            if (o < n_out) {
+                const int g = o / hdv, dv = o - g * hdv;
+                fscale(acc[j], a_s[g]);
+                const float* pg = p_s + g * kTile;
+                for (int tt = 0; tt < kTile; ++tt) {
+                    const float p = pg[tt];
+                    faxpy(acc[j], p, *reinterpret_cast<const T*>(v_s + tt * ldk + dv * VEC));
+                }
+            }
+        }
+    }
+    __syncthreads();
+
+    // Split partial: [G][hd] accumulator, then m, l per head.
+    const int G2 = hd + 2;
+    float* part = A.part + ((size_t)h * A.nsplit + split) * G * G2;
+#pragma unroll
+    for (int j = 0; j < kMaxAcc; ++j) {
+        const int o = tid + j * kAttnThreads;
+        if (o < n_out) {
+            const int g = o / hdv, dv = o - g * hdv;
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) part[g * G2 + dv * VEC + e] = fget(acc[j], e);
+        }
+    }
+    if (tid < G) {
+        part[tid * G2 + hd] = m_s[tid];
+        part[tid * G2 + hd + 1] = l_s[tid];
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned ticket = atomicAdd(&A.tickets[h], 1u);
+        flag_s[0] = (ticket == (unsigned)(A.nsplit - 1)) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!flag_s[0]) return;
+    __threadfence();
+
+    // Last CTA of this kv head: merge the splits in index order.
+    const float* base = A.part + (size_t)h * A.nsplit * G * G2;
+    for (int o = tid; o < G * hd; o += kAttnThreads) {
+        const int g = o / hd, d = o - g * hd;
+        float M = -INFINITY;
+        for (int s = 0; s < A.nsplit; ++s) M = fmaxf(M, __ldcg(base + ((size_t)s * G + g) * G2 + hd));
+        float L = 0.f, O = 0.f;
+        for (int s = 0; s < A.nsplit; ++s) {
+            const float* ps = base + ((size_t)s * G + g) * G2;
+            const float ms = __ldcg(ps + hd);
+            if (ms == -INFINITY) continue;
+            const float w = expf(ms - M);
+            L = fmaf(__ldcg(ps + hd + 1), w, L);
+            O = fmaf(__ldcg(ps + d), w, O);
+        }
+        A.out[((size_t)h * G + g) * hd + d] = (L > 0.f) ? O / L : 0.f;
+    }
+    if (tid == 0) A.tickets[h] = 0u;
+}
+
+}  // namespace
+
+bool attn_supported(int n_heads, int n_kv, int hd) {
+    if (n_kv <= 0 || n_heads % n_kv) return false;
+    const int G = n_heads / n_kv;
+    if (G > kTile * 4) return false;
+    const int vec = (hd % 4 == 0) ? 4 : 1;
+    return (G * hd / vec) <= kMaxAcc * kAttnThreads;
+}
+
+size_t attn_smem_bytes(int n_heads, int n_kv, int hd) {
+    const int G = n_heads / n_kv;
+    const int pad = (hd % 4 == 0) ? 4 : 1;
+    const size_t floats = (size_t)G * hd + 2 * kTile * (hd + pad) + (size_t)G * kTile + 3 * G + 4;
+    return floats * 4;
+}
+
+int attn_splits_for(int n_kv, int num_sms) {
+    int s = (2 * num_sms + n_kv - 1) / n_kv;
+    if (s < 1) s = 1;
+    if (s > 64) s = 64;
+    return s;
+}
+
+cudaError_t attn_prepare(int /*dev*/) {
+    cudaError_t e = cudaFuncSetAttribute(attn_split_kernel<4>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(attn_split_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                200 * 1024);
+}
+
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.n_kv, a.nsplit, 1);
+    cfg.blockDim = dim3(kAttnThreads, 1, 1);
+    cfg.dynamicSmemBytes = attn_smem_bytes(a.n_heads, a.n_kv, a.hd);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    void* args[] = {(void*)&a};
+    void* k = (a.hd % 4 == 0) ? (void*)attn_split_kernel<4> : (void*)attn_split_kernel<1>;
+    return cudaLaunchKernelExC(&cfg, k, args);
+}
+
+}  // namespace vox

@@ -1,0 +1,1274 @@
+// vox_capi.cpp -- host side of the C ABI declared in include/vox_decoder.h.
+//
+// Owns device memory, the CUDA stream, the rolling-cache bookkeeping (the
+// exact integer arithmetic of crates/voxtral/src/kv.rs:48-88, mirrored on the
+// device), kernel launch plans and the captured CUDA graph of a token step.
+// Every compute step runs on the GPU; this file only validates, copies and
+// launches.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/vox_decoder.h"
+#include "vox_kernels.h"
+
+using namespace vox;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define CUDA_TRY(expr)                                                                   \
+    do {                                                                                 \
+        cudaError_t e_ = (expr);                                                         \
+        if (e_ != cudaSuccess)                                                           \
+            return fail(e_ == cudaErrorMemoryAllocation ? VOX_ERR_OOM : VOX_ERR_CUDA,     \
+                        "%s failed: %s", #expr, cudaGetErrorString(e_));                  \
+    } while (0)
+
+#define TRY(expr)                  \
+    do {                           \
+        int rc_ = (expr);          \
+        if (rc_ != VOX_OK) return rc_; \
+    } while (0)
+
+template <class T>
+cudaError_t dalloc(T** p, size_t n) {
+    *p = nullptr;
+    if (n == 0) n = 1;
+    return cudaMalloc(reinterpret_cast<void**>(p), n * sizeof(T));
+}
+
+uint16_t f32_to_bf16(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu)) return 0x7FC0;
+    return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+float bf16_to_f32(uint16_t h) {
+    uint32_t u = (uint32_t)h << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+
+// Host mirror of one cache layer: the reference's (len_tokens, pos_offset)
+// plus the physical ring start.
+struct HostKv {
+    size_t len = 0, start = 0, pos_offset = 0;
+};
+
+// kv.rs:48-88 append bookkeeping for n tokens.  Returns the ring slot of the
+// first new token, or -1 if the result would not fit in `cap` slots.
+long long host_append(HostKv& s, size_t n, size_t window, size_t cap) {
+    if (n == 0) return (long long)((s.start + s.len) % cap);
+    HostKv t = s;
+    size_t requested = t.len + n;
+    size_t drop = requested > window ? requested - window : 0;
+    if (drop > 0) {
+        size_t keep = t.len > drop ? t.len - drop : 0;
+        size_t phys = t.len < drop ? t.len : drop;
+        t.start = (t.start + phys) % cap;
+        t.len = keep;
+        t.pos_offset += drop;
+    }
+    if (t.len + n > cap) return -1;
+    long long slot0 = (long long)((t.start + t.len) % cap);
+    t.len += n;
+    s = t;
+    return slot0;
+}
+
+struct LayerDev {
+    void* wqkv = nullptr;   // [q_dim + 2 kv_dim, dim]: wq rows, wk rows, wv rows
+    void* wo = nullptr;     // [dim, q_dim]
+    void* w13 = nullptr;    // [2 hidden, dim]: row 2j = w1[j], row 2j+1 = w3[j]
+    void* w2 = nullptr;     // [dim, hidden]
+    float* attn_norm = nullptr;
+    float* ffn_norm = nullptr;
+    bool ready = false;
+};
+
+}  // namespace
+
+struct vox_ctx {
+    vox_decoder_config cfg{};
+    vox_ctx_options opt{};
+    int dev = 0, num_sms = 148, wsize = 2;
+    size_t q_dim = 0, kv_dim = 0, qkv_rows = 0;
+    cudaStream_t stream = nullptr;
+    std::vector<LayerDev> layers;
+    uint16_t* embed = nullptr;
+    void* lm_head = nullptr;
+    float* final_norm = nullptr;
+    bool embed_ready = false, head_ready = false;
+    float* rope_cos = nullptr;
+    float* rope_sin = nullptr;
+    int max_pos = 0;
+    float *hid = nullptr, *hmid = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr,
+          *logits = nullptr;
+    ArgmaxPart* am_part = nullptr;
+    float* attn_part = nullptr;
+    unsigned* tickets = nullptr;
+    int nsplit = 1;
+    StepState* step = nullptr;
+    int32_t* tok_out = nullptr;
+    unsigned* err = nullptr;
+    StepState* h_steps = nullptr;  // pinned, one slot per queued step
+    size_t h_steps_cap = 0;
+    int32_t* h_tok = nullptr;      // pinned
+    unsigned* h_err = nullptr;     // pinned
+    cudaEvent_t ev[16] = {};
+    uint64_t launches = 0;
+    GemvPlan p_qkv{}, p_o{}, p_w13{}, p_w2{}, p_head{};
+    void* scratch = nullptr;
+    size_t scratch_bytes = 0;
+};
+
+struct vox_kv {
+    vox_ctx* ctx = nullptr;
+    size_t n_layers = 0, n_kv = 0, hd = 0, window = 0, cap = 0;
+    float* k = nullptr;          // [n_layers, n_kv, cap, hd]
+    float* v = nullptr;
+    KvState* dstate = nullptr;   // [n_layers]
+    std::vector<HostKv> hs;
+    cudaGraphExec_t step_graph = nullptr;
+    uint64_t graph_kernels = 0;
+    size_t layer_elems() const { return n_kv * cap * hd; }
+};
+
+namespace {
+
+int check_device_errors(vox_ctx* c) {
+    CUDA_TRY(cudaMemcpyAsync(c->h_err, c->err, sizeof(unsigned), cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    unsigned bits = *c->h_err;
+    if (bits) {
+        CUDA_TRY(cudaMemsetAsync(c->err, 0, sizeof(unsigned), c->stream));
+        CUDA_TRY(cudaStreamSynchronize(c->stream));
+        if (bits & (ERR_FULL_WAIT | ERR_EMPTY_WAIT | ERR_DRAIN_WAIT))
+            return fail(VOX_ERR_DEVICE_TIMEOUT, "a bounded wait inside a kernel expired (bits 0x%x)", bits);
+        if (bits & ERR_POS_RANGE) return fail(VOX_ERR_RANGE, "position beyond the RoPE table");
+        if (bits & ERR_TOKEN_RANGE) return fail(VOX_ERR_RANGE, "token id outside the vocabulary");
+        return fail(VOX_ERR_CUDA, "device error bits 0x%x", bits);
+    }
+    return VOX_OK;
+}
+
+int ensure_scratch(vox_ctx* c, size_t bytes) {
+    if (bytes <= c->scratch_bytes) return VOX_OK;
+    if (c->scratch) {
+        CUDA_TRY(cudaStreamSynchronize(c->stream));
+        cudaFree(c->scratch);
+        c->scratch = nullptr;
+        c->scratch_bytes = 0;
+    }
+    size_t b = 1 << 20;
+    while (b < bytes) b <<= 1;
+    CUDA_TRY(cudaMalloc(&c->scratch, b));
+    c->scratch_bytes = b;
+    return VOX_OK;
+}
+
+int validate_cfg(const vox_decoder_config* c) {
+    if (!c) return fail(VOX_ERR_INVALID_ARG, "config is null");
+    // decoder.rs:22-41, same order and messages.
+    if (c->dim == 0) return fail(VOX_ERR_CONFIG, "dim must be > 0");
+    if (c->hidden_dim == 0) return fail(VOX_ERR_CONFIG, "hidden_dim must be > 0");
+    if (c->n_heads == 0) return fail(VOX_ERR_CONFIG, "n_heads must be > 0");
+    if (c->n_kv_heads == 0) return fail(VOX_ERR_CONFIG, "n_kv_heads must be > 0");
+    if (c->head_dim == 0) return fail(VOX_ERR_CONFIG, "head_dim must be > 0");
+    if (c->n_heads % c->n_kv_heads != 0)
+        return fail(VOX_ERR_CONFIG, "n_heads must be divisible by n_kv_heads");
+    if (c->n_heads * c->head_dim < c->dim) return fail(VOX_ERR_CONFIG, "n_heads * head_dim must cover dim");
+    if (c->sliding_window == 0)
+        return fail(VOX_ERR_CONFIG, "sliding_window must be > 0 for rolling attention cache");
+    return VOX_OK;
+}
+
+// Shapes the kernels need beyond the reference's own checks.
+int check_kernel_shapes(const vox_decoder_config* c, int wsize) {
+    const size_t q_dim = c->n_heads * c->head_dim;
+    if (c->head_dim % 2) return fail(VOX_ERR_UNSUPPORTED, "head_dim must be even (interleaved RoPE pairs)");
+    if (c->dim > (1u << 30) || c->hidden_dim > (1u << 30))
+        return fail(VOX_ERR_UNSUPPORTED, "dimensions too large");
+    if (!gemv_supported((int)c->dim, wsize) || !gemv_supported((int)q_dim, wsize) ||
+        !gemv_supported((int)c->hidden_dim, wsize))
+        return fail(VOX_ERR_UNSUPPORTED,
+                    "dim, n_heads*head_dim and hidden_dim must be multiples of %d elements and at most %d",
+                    16 / wsize, wsize == 2 ? 16384 : 8192);
+    if (!attn_supported((int)c->n_heads, (int)c->n_kv_heads, (int)c->head_dim))
+        return fail(VOX_ERR_UNSUPPORTED, "attention shape (group %zu x head_dim %zu) too large",
+                    c->n_heads / c->n_kv_heads, c->head_dim);
+    return VOX_OK;
+}
+
+int check_matrix_len(size_t got, size_t want, const char* name) {
+    if (got != want) return fail(VOX_ERR_SHAPE, "%s shape mismatch", name);
+    return VOX_OK;
+}
+
+// decoder.rs:58-84, generic over slice flavours.
+template <class WS>
+int validate_weights(const vox_decoder_config* cfg, const WS* w) {
+    if (!w) return fail(VOX_ERR_INVALID_ARG, "weights are null");
+    const size_t q_dim = cfg->n_heads * cfg->head_dim, kv_dim = cfg->n_kv_heads * cfg->head_dim;
+    TRY(check_matrix_len(w->attention_norm.len, cfg->dim, "attention_norm"));
+    TRY(check_matrix_len(w->wq.len, q_dim * cfg->dim, "wq"));
+    TRY(check_matrix_len(w->wk.len, kv_dim * cfg->dim, "wk"));
+    TRY(check_matrix_len(w->wv.len, kv_dim * cfg->dim, "wv"));
+    TRY(check_matrix_len(w->wo.len, cfg->dim * q_dim, "wo"));
+    TRY(check_matrix_len(w->ffn_norm.len, cfg->dim, "ffn_norm"));
+    TRY(check_matrix_len(w->w1.len, cfg->hidden_dim * cfg->dim, "w1"));
+    TRY(check_matrix_len(w->w2.len, cfg->dim * cfg->hidden_dim, "w2"));
+    TRY(check_matrix_len(w->w3.len, cfg->hidden_dim * cfg->dim, "w3"));
+    const void* ptrs[] = {w->attention_norm.ptr, w->wq.ptr, w->wk.ptr, w->wv.ptr, w->wo.ptr,
+                          w->ffn_norm.ptr, w->w1.ptr, w->w2.ptr, w->w3.ptr};
+    for (const void* p : ptrs)
+        if (!p) return fail(VOX_ERR_INVALID_ARG, "a weight pointer is null");
+    return VOX_OK;
+}
+
+// Convert a host matrix into the context's weight dtype.
+std::vector<unsigned char> to_wdtype(const float* src, size_t n, int wsize) {
+    std::vector<unsigned char> out(n * wsize);
+    if (wsize == 4) {
+        std::memcpy(out.data(), src, n * 4);
+    } else {
+        uint16_t* o = reinterpret_cast<uint16_t*>(out.data());
+        for (size_t i = 0; i < n; ++i) o[i] = f32_to_bf16(src[i]);
+    }
+    return out;
+}
+std::vector<unsigned char> to_wdtype(const uint16_t* src, size_t n, int wsize) {
+    std::vector<unsigned char> out(n * wsize);
+    if (wsize == 2) {
+        std::memcpy(out.data(), src, n * 2);
+    } else {
+        float* o = reinterpret_cast<float*>(out.data());
+        for (size_t i = 0; i < n; ++i) o[i] = bf16_to_f32(src[i]);
+    }
+    return out;
+}
+
+int alloc_layer(vox_ctx* c, LayerDev& L) {
+    if (L.wqkv) return VOX_OK;
+    const size_t dim = c->cfg.dim, hid = c->cfg.hidden_dim;
+    CUDA_TRY(cudaMalloc(&L.wqkv, c->qkv_rows * dim * c->wsize));
+    CUDA_TRY(cudaMalloc(&L.wo, dim * c->q_dim * c->wsize));
+    CUDA_TRY(cudaMalloc(&L.w13, 2 * hid * dim * c->wsize));
+    CUDA_TRY(cudaMalloc(&L.w2, dim * hid * c->wsize));
+    CUDA_TRY(dalloc(&L.attn_norm, dim));
+    CUDA_TRY(dalloc(&L.ffn_norm, dim));
+    return VOX_OK;
+}
+
+template <class WS>
+int upload_layer(vox_ctx* c, size_t layer, const WS* w) {
+    if (!c) return fail(VOX_ERR_INVALID_ARG, "context is null");
+    if (layer >= c->layers.size()) return fail(VOX_ERR_INVALID_ARG, "layer %zu out of range", layer);
+    TRY(validate_weights(&c->cfg, w));
+    CUDA_TRY(cudaSetDevice(c->dev));
+    LayerDev& L = c->layers[layer];
+    TRY(alloc_layer(c, L));
+    const size_t dim = c->cfg.dim, hid = c->cfg.hidden_dim, ws = c->wsize;
+    auto put = [&](void* dst, const auto& slice) -> int {
+        auto bytes = to_wdtype(slice.ptr, slice.len, (int)ws);
+        CUDA_TRY(cudaMemcpy(dst, bytes.data(), bytes.size(), cudaMemcpyHostToDevice));
+        return VOX_OK;
+    };
+    unsigned char* qkv = static_cast<unsigned char*>(L.wqkv);
+    TRY(put(qkv, w->wq));
+    TRY(put(qkv + c->q_dim * dim * ws, w->wk));
+    TRY(put(qkv + (c->q_dim + c->kv_dim) * dim * ws, w->wv));
+    TRY(put(L.wo, w->wo));
+    TRY(put(L.w2, w->w2));
+    // w1 -> even rows, w3 -> odd rows of w13.
+    const size_t row = dim * ws;
+    {
+        auto b1 = to_wdtype(w->w1.ptr, w->w1.len, (int)ws);
+        auto b3 = to_wdtype(w->w3.ptr, w->w3.len, (int)ws);
+        CUDA_TRY(cudaMemcpy2D(L.w13, 2 * row, b1.data(), row, row, hid, cudaMemcpyHostToDevice));
+        CUDA_TRY(cudaMemcpy2D(static_cast<unsigned char*>(L.w13) + row, 2 * row, b3.data(), row, row,
+                              hid, cudaMemcpyHostToDevice));
+    }
+    CUDA_TRY(cudaMemcpy(L.attn_norm, w->attention_norm.ptr, dim * 4, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(L.ffn_norm, w->ffn_norm.ptr, dim * 4, cudaMemcpyHostToDevice));
+    L.ready = true;
+    return VOX_OK;
+}
+
+cudaError_t record_launch(vox_ctx* c, cudaError_t e) {
+    if (e == cudaSuccess) ++c->launches;
+    return e;
+}
+
+GemvArgs base_args(vox_ctx* c) {
+    GemvArgs a{};
+    a.step = c->step;
+    a.eps = c->cfg.norm_eps;
+    a.err = c->err;
+    return a;
+}
+
+// Enqueue one decoder layer (decoder.rs:88-155) as five kernels.
+int enqueue_layer(vox_ctx* c, vox_kv* kv, size_t l, bool from_embed, bool pdl) {
+    const LayerDev& L = c->layers[l];
+    float* kr = kv->k + l * kv->layer_elems();
+    float* vr = kv->v + l * kv->layer_elems();
+    KvState* st = kv->dstate + l;
+    const int cap = (int)kv->cap, win = (int)kv->window;
+
+    // 1) RMSNorm -> q|k|v -> RoPE -> k, v into the ring slot.
+    GemvArgs a = base_args(c);
+    a.W = L.wqkv;
+    if (from_embed) {
+        a.x_embed = c->embed;
+        a.vocab = (int)c->opt.vocab;
+        a.x_copy_out = c->hid;
+    } else {
+        a.x = c->hid;
+    }
+    a.norm_w = L.attn_norm;
+    a.y = c->q;
+    a.q_dim = (int)c->q_dim;
+    a.kv_dim = (int)c->kv_dim;
+    a.head_dim = (int)c->cfg.head_dim;
+    a.rope_cos = c->rope_cos;
+    a.rope_sin = c->rope_sin;
+    a.max_pos = c->max_pos;
+    a.k_ring = kr;
+    a.v_ring = vr;
+    a.ring_cap = cap;
+    a.kv_window = win;
+    a.kv_state = st;
+    CUDA_TRY(record_launch(c, launch_gemv(c->p_qkv, a, EPI_QKV, c->stream, pdl)));
+
+    // 2) attention over the ring (ops.rs:66-132).
+    AttnArgs at{};
+    at.q = c->q;
+    at.k_ring = kr;
+    at.v_ring = vr;
+    at.n_heads = (int)c->cfg.n_heads;
+    at.n_kv = (int)c->cfg.n_kv_heads;
+    at.hd = (int)c->cfg.head_dim;
+    at.cap = cap;
+    at.cfg_window = (int)c->cfg.sliding_window;
+    at.st = st;
+    at.pre_append = 1;
+    at.kv_window = win;
+    at.nsplit = c->nsplit;
+    at.part = c->attn_part;
+    at.tickets = c->tickets;
+    at.out = c->attn;
+    at.scale = 1.0f / sqrtf((float)c->cfg.head_dim);
+    at.err = c->err;
+    CUDA_TRY(record_launch(c, launch_attention(at, c->stream, pdl)));
+
+    // 3) o-proj + residual (decoder.rs:136-139); commits the append.
+    a = base_args(c);
+    a.W = L.wo;
+    a.x = c->attn;
+    a.y = c->hmid;
+    a.resid = c->hid;
+    a.kv_commit = st;
+    a.kv_window = win;
+    a.ring_cap = cap;
+    CUDA_TRY(record_launch(c, launch_gemv(c->p_o, a, EPI_RESID, c->stream, pdl)));
+
+    // 4) RMSNorm -> w1|w3 -> SiLU(gate)*up (decoder.rs:143-150).
+    a = base_args(c);
+    a.W = L.w13;
+    a.x = c->hmid;
+    a.norm_w = L.ffn_norm;
+    a.y = c->act;
+    CUDA_TRY(record_launch(c, launch_gemv(c->p_w13, a, EPI_SWIGLU, c->stream, pdl)));
+
+    // 5) w2 + residual (decoder.rs:151-152).
+    a = base_args(c);
+    a.W = L.w2;
+    a.x = c->act;
+    a.y = c->hid;
+    a.resid = c->hmid;
+    CUDA_TRY(record_launch(c, launch_gemv(c->p_w2, a, EPI_RESID, c->stream, pdl)));
+    return VOX_OK;
+}
+
+// Final RMSNorm -> LM head -> argmax.
+int enqueue_head(vox_ctx* c, bool pdl) {
+    GemvArgs a = base_args(c);
+    a.W = c->lm_head;
+    a.x = c->hid;
+    a.norm_w = c->final_norm;
+    a.y = c->logits;
+    a.am_part = c->am_part;
+    CUDA_TRY(record_launch(c, launch_gemv(c->p_head, a, EPI_ARGMAX, c->stream, pdl)));
+    CUDA_TRY(record_launch(c, launch_argmax_final(c->am_part, c->p_head.grid, c->step, c->tok_out,
+                                                  c->stream, pdl)));
+    return VOX_OK;
+}
+
+int model_ready(vox_ctx* c, vox_kv* kv) {
+    if (!c || !kv) return fail(VOX_ERR_INVALID_ARG, "null context or cache");
+    if (kv->ctx != c) return fail(VOX_ERR_INVALID_ARG, "cache belongs to another context");
+    if (c->opt.vocab == 0) return fail(VOX_ERR_NOT_READY, "context was created without a vocabulary");
+    if (!c->embed_ready || !c->head_ready) return fail(VOX_ERR_NOT_READY, "embedding or LM head not uploaded");
+    for (size_t l = 0; l < c->layers.size(); ++l)
+        if (!c->layers[l].ready) return fail(VOX_ERR_NOT_READY, "layer %zu weights not uploaded", l);
+    if (kv->n_layers != c->layers.size())
+        return fail(VOX_ERR_SHAPE, "cache has %zu layers, model has %zu", kv->n_layers, c->layers.size());
+    if (kv->n_kv != c->cfg.n_kv_heads || kv->hd != c->cfg.head_dim)
+        return fail(VOX_ERR_SHAPE, "cache head shape does not match the decoder config");
+    return VOX_OK;
+}
+
+int build_step_graph(vox_ctx* c, vox_kv* kv) {
+    if (kv->step_graph) return VOX_OK;
+    const uint64_t before = c->launches;
+    CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = VOX_OK;
+    for (size_t l = 0; l < c->layers.size() && rc == VOX_OK; ++l) rc = enqueue_layer(c, kv, l, l == 0, true);
+    if (rc == VOX_OK) rc = enqueue_head(c, true);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+    if (rc != VOX_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    CUDA_TRY(e);
+    e = cudaGraphInstantiate(&kv->step_graph, g, 0);
+    cudaGraphDestroy(g);
+    CUDA_TRY(e);
+    kv->graph_kernels = c->launches - before;
+    c->launches = before;
+    return VOX_OK;
+}
+
+int ensure_host_steps(vox_ctx* c, size_t n) {
+    if (n <= c->h_steps_cap) return VOX_OK;
+    if (c->h_steps) {
+        CUDA_TRY(cudaStreamSynchronize(c->stream));
+        cudaFreeHost(c->h_steps);
+        c->h_steps = nullptr;
+    }
+    size_t cap = 1024;
+    while (cap < n) cap <<= 1;
+    CUDA_TRY(cudaMallocHost(&c->h_steps, cap * sizeof(StepState)));
+    c->h_steps_cap = cap;
+    return VOX_OK;
+}
+
+int launch_graph(vox_ctx* c, vox_kv* kv) {
+    CUDA_TRY(cudaGraphLaunch(kv->step_graph, c->stream));
+    c->launches += kv->graph_kernels;
+    return VOX_OK;
+}
+
+void mirror_single_append_all(vox_kv* kv) {
+    for (auto& s : kv->hs) host_append(s, 1, kv->window, kv->cap);
+}
+
+int upload_state(vox_kv* kv, size_t layer) {
+    KvState d{};
+    d.len = (int32_t)kv->hs[layer].len;
+    d.start = (int32_t)kv->hs[layer].start;
+    d.pos_offset = (int64_t)kv->hs[layer].pos_offset;
+    CUDA_TRY(cudaMemcpyAsync(kv->dstate + layer, &d, sizeof d, cudaMemcpyHostToDevice, kv->ctx->stream));
+    CUDA_TRY(cudaStreamSynchronize(kv->ctx->stream));
+    return VOX_OK;
+}
+
+}  // namespace
+
+namespace {
+
+// Upload n floats, run `fn` on the device copy, download back into `io`.
+template <class F>
+int inplace_op(vox_ctx* c, float* io, size_t n, F fn) {
+    if (!c || (!io && n)) return fail(VOX_ERR_INVALID_ARG, "null argument");
+    if (n == 0) return VOX_OK;
+    CUDA_TRY(cudaSetDevice(c->dev));
+    TRY(ensure_scratch(c, n * 4));
+    float* d = static_cast<float*>(c->scratch);
+    CUDA_TRY(cudaMemcpyAsync(d, io, n * 4, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(record_launch(c, fn(d)));
+    CUDA_TRY(cudaMemcpyAsync(io, d, n * 4, cudaMemcpyDeviceToHost, c->stream));
+    return check_device_errors(c);
+}
+
+}  // namespace
+
+// ============================================================================
+// C ABI
+// ============================================================================
+extern "C" {
+
+const char* vox_last_error(void) { return g_err.c_str(); }
+int vox_abi_version(void) { return VOX_ABI_VERSION; }
+
+int vox_config_validate(const vox_decoder_config* cfg) { return validate_cfg(cfg); }
+
+int vox_layer_weights_validate_f32(const vox_decoder_config* cfg, const vox_layer_weights_f32* w) {
+    TRY(validate_cfg(cfg));
+    return validate_weights(cfg, w);
+}
+int vox_layer_weights_validate_bf16(const vox_decoder_config* cfg, const vox_layer_weights_bf16* w) {
+    TRY(validate_cfg(cfg));
+    return validate_weights(cfg, w);
+}
+
+void vox_ctx_destroy(vox_ctx* c) {
+    if (!c) return;
+    cudaSetDevice(c->dev);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    for (auto& L : c->layers) {
+        cudaFree(L.wqkv);
+        cudaFree(L.wo);
+        cudaFree(L.w13);
+        cudaFree(L.w2);
+        cudaFree(L.attn_norm);
+        cudaFree(L.ffn_norm);
+    }
+    void* ptrs[] = {c->embed, c->lm_head, c->final_norm, c->rope_cos, c->rope_sin, c->hid, c->hmid,
+                    c->q, c->attn, c->act, c->logits, c->am_part, c->attn_part, c->tickets, c->step,
+                    c->tok_out, c->err, c->scratch};
+    for (void* p : ptrs)
+        if (p) cudaFree(p);
+    if (c->h_steps) cudaFreeHost(c->h_steps);
+    if (c->h_tok) cudaFreeHost(c->h_tok);
+    if (c->h_err) cudaFreeHost(c->h_err);
+    for (auto& e : c->ev)
+        if (e) cudaEventDestroy(e);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+int vox_ctx_create(const vox_decoder_config* cfg, const vox_ctx_options* opt, vox_ctx** out) {
+    if (!out) return fail(VOX_ERR_INVALID_ARG, "out is null");
+    *out = nullptr;
+    TRY(validate_cfg(cfg));
+    vox_ctx_options o{};
+    if (opt) o = *opt;
+    if (o.n_layers == 0) o.n_layers = 1;
+    if (o.max_positions == 0) o.max_positions = 32768;
+    if (o.weight_dtype != VOX_WEIGHTS_BF16 && o.weight_dtype != VOX_WEIGHTS_F32)
+        return fail(VOX_ERR_INVALID_ARG, "unknown weight dtype %d", o.weight_dtype);
+    const int wsize = o.weight_dtype == VOX_WEIGHTS_F32 ? 4 : 2;
+    TRY(check_kernel_shapes(cfg, wsize));
+    if (o.vocab > (size_t)INT32_MAX) return fail(VOX_ERR_UNSUPPORTED, "vocab too large");
+    if (o.max_positions > (size_t)(1 << 24))
+        return fail(VOX_ERR_UNSUPPORTED, "max_positions above 2^24 (positions are exact f32)");
+
+    int ndev = 0;
+    CUDA_TRY(cudaGetDeviceCount(&ndev));
+    if (o.device < 0 || o.device >= ndev) return fail(VOX_ERR_INVALID_ARG, "device %d not present", o.device);
+    CUDA_TRY(cudaSetDevice(o.device));
+    cudaDeviceProp prop;
+    CUDA_TRY(cudaGetDeviceProperties(&prop, o.device));
+    if (prop.major != 10)
+        return fail(VOX_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a", o.device,
+                    prop.major, prop.minor);
+
+    vox_ctx* c = new vox_ctx();
+    c->cfg = *cfg;
+    c->opt = o;
+    c->dev = o.device;
+    c->num_sms = prop.multiProcessorCount;
+    c->wsize = wsize;
+    c->q_dim = cfg->n_heads * cfg->head_dim;
+    c->kv_dim = cfg->n_kv_heads * cfg->head_dim;
+    c->qkv_rows = c->q_dim + 2 * c->kv_dim;
+    c->layers.resize(o.n_layers);
+    c->max_pos = (int)o.max_positions;
+
+    auto bail = [&](int rc) {
+        vox_ctx_destroy(c);
+        return rc;
+    };
+#define CTX_TRY(expr)                                                                        \
+    do {                                                                                     \
+        cudaError_t e_ = (expr);                                                             \
+        if (e_ != cudaSuccess)                                                               \
+            return bail(fail(e_ == cudaErrorMemoryAllocation ? VOX_ERR_OOM : VOX_ERR_CUDA,    \
+                             "%s failed: %s", #expr, cudaGetErrorString(e_)));                \
+    } while (0)
+
+    CTX_TRY(gemv_prepare(c->dev));
+    CTX_TRY(attn_prepare(c->dev));
+    CTX_TRY(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    for (auto& e : c->ev) CTX_TRY(cudaEventCreate(&e));
+
+    const size_t dim = cfg->dim, hid = cfg->hidden_dim, hd = cfg->head_dim;
+    // Launch plans.
+    const int dimi = (int)dim, hidi = (int)hid;
+    c->p_qkv = plan_gemv((int)c->qkv_rows, dimi, 2, wsize, c->num_sms, 1);
+    c->p_o = plan_gemv(dimi, (int)c->q_dim, 1, wsize, c->num_sms, 1);
+    c->p_w13 = plan_gemv(2 * hidi, dimi, 2, wsize, c->num_sms, 1);
+    c->p_w2 = plan_gemv(dimi, hidi, 1, wsize, c->num_sms, 1);
+    if (o.vocab) c->p_head = plan_gemv((int)o.vocab, dimi, 1, wsize, c->num_sms, 1);
+    for (const GemvPlan* p : {&c->p_qkv, &c->p_o, &c->p_w13, &c->p_w2})
+        if (p->grid < 1 || p->smem > gemv_max_smem())
+            return bail(fail(VOX_ERR_UNSUPPORTED, "no GEMV plan for rows %d x K %d", p->rows, p->K));
+    if (o.vocab && (c->p_head.grid < 1 || c->p_head.smem > gemv_max_smem()))
+        return bail(fail(VOX_ERR_UNSUPPORTED, "no LM-head plan for vocab %zu", (size_t)o.vocab));
+    c->nsplit = attn_splits_for((int)cfg->n_kv_heads, c->num_sms);
+
+    // Activations and scratch.
+    CTX_TRY(dalloc(&c->hid, dim));
+    CTX_TRY(dalloc(&c->hmid, dim));
+    CTX_TRY(dalloc(&c->q, c->q_dim));
+    CTX_TRY(dalloc(&c->attn, c->q_dim));
+    CTX_TRY(dalloc(&c->act, hid));
+    CTX_TRY(dalloc(&c->logits, o.vocab));
+    CTX_TRY(dalloc(&c->am_part, (size_t)c->num_sms));
+    const size_t G = cfg->n_heads / cfg->n_kv_heads;
+    CTX_TRY(dalloc(&c->attn_part, cfg->n_kv_heads * c->nsplit * G * (hd + 2)));
+    CTX_TRY(dalloc(&c->tickets, cfg->n_kv_heads));
+    CTX_TRY(cudaMemset(c->tickets, 0, cfg->n_kv_heads * sizeof(unsigned)));
+    CTX_TRY(dalloc(&c->step, 1));
+    CTX_TRY(cudaMemset(c->step, 0, sizeof(StepState)));
+    CTX_TRY(dalloc(&c->tok_out, 1));
+    CTX_TRY(dalloc(&c->err, 1));
+    CTX_TRY(cudaMemset(c->err, 0, sizeof(unsigned)));
+    CTX_TRY(cudaMallocHost(&c->h_tok, sizeof(int32_t)));
+    CTX_TRY(cudaMallocHost(&c->h_err, sizeof(unsigned)));
+    if (ensure_host_steps(c, 1024) != VOX_OK) return bail(VOX_ERR_OOM);
+
+    // RoPE table: inv_freq = theta^(-(2p)/hd), angle = pos * inv_freq,
+    // (sin, cos) of angle, all in f32 with libm as math.rs:52-56 does.
+    {
+        const size_t half = hd / 2, n = (size_t)c->max_pos * half;
+        std::vector<float> ct(n), st(n), inv(half);
+        for (size_t p = 0; p < half; ++p)
+            inv[p] = powf(cfg->rope_theta, -((float)(2 * p)) / (float)hd);
+        for (size_t pos = 0; pos < (size_t)c->max_pos; ++pos)
+            for (size_t p = 0; p < half; ++p) {
+                const float angle = (float)pos * inv[p];
+                st[pos * half + p] = sinf(angle);
+                ct[pos * half + p] = cosf(angle);
+            }
+        CTX_TRY(dalloc(&c->rope_cos, n));
+        CTX_TRY(dalloc(&c->rope_sin, n));
+        CTX_TRY(cudaMemcpy(c->rope_cos, ct.data(), n * 4, cudaMemcpyHostToDevice));
+        CTX_TRY(cudaMemcpy(c->rope_sin, st.data(), n * 4, cudaMemcpyHostToDevice));
+    }
+#undef CTX_TRY
+    *out = c;
+    return VOX_OK;
+}
+
+int vox_ctx_upload_layer_f32(vox_ctx* c, size_t layer, const vox_layer_weights_f32* w) {
+    return upload_layer(c, layer, w);
+}
+int vox_ctx_upload_layer_bf16(vox_ctx* c, size_t layer, const vox_layer_weights_bf16* w) {
+    return upload_layer(c, layer, w);
+}
+
+int vox_ctx_upload_embed_bf16(vox_ctx* c, const uint16_t* embed, size_t len) {
+    if (!c || !embed) return fail(VOX_ERR_INVALID_ARG, "null argument");
+    if (c->opt.vocab == 0) return fail(VOX_ERR_NOT_READY, "context was created without a vocabulary");
+    if (len != c->opt.vocab * c->cfg.dim) return fail(VOX_ERR_SHAPE, "embed shape mismatch");
+    CUDA_TRY(cudaSetDevice(c->dev));
+    if (!c->embed) CUDA_TRY(dalloc(&c->embed, len));
+    CUDA_TRY(cudaMemcpy(c->embed, embed, len * 2, cudaMemcpyHostToDevice));
+    c->embed_ready = true;
+    return VOX_OK;
+}
+
+int vox_ctx_upload_lm_head_bf16(vox_ctx* c, const uint16_t* head, size_t len) {
+    if (!c || !head) return fail(VOX_ERR_INVALID_ARG, "null argument");
+    if (c->opt.vocab == 0) return fail(VOX_ERR_NOT_READY, "context was created without a vocabulary");
+    if (len != c->opt.vocab * c->cfg.dim) return fail(VOX_ERR_SHAPE, "lm_head shape mismatch");
+    CUDA_TRY(cudaSetDevice(c->dev));
+    if (!c->lm_head) CUDA_TRY(cudaMalloc(&c->lm_head, len * c->wsize));
+    auto bytes = to_wdtype(head, len, c->wsize);
+    CUDA_TRY(cudaMemcpy(c->lm_head, bytes.data(), bytes.size(), cudaMemcpyHostToDevice));
+    if (!c->final_norm) {
+        CUDA_TRY(dalloc(&c->final_norm, c->cfg.dim));
+        CUDA_TRY(launch_fill_f32(c->final_norm, 1.0f, (long long)c->cfg.dim, c->stream));
+        CUDA_TRY(cudaStreamSynchronize(c->stream));
+    }
+    c->head_ready = true;
+    return VOX_OK;
+}
+
+int vox_ctx_upload_final_norm(vox_ctx* c, const float* gain, size_t len) {
+    if (!c || !gain) return fail(VOX_ERR_INVALID_ARG, "null argument");
+    if (len != c->cfg.dim) return fail(VOX_ERR_SHAPE, "final_norm shape mismatch");
+    CUDA_TRY(cudaSetDevice(c->dev));
+    if (!c->final_norm) CUDA_TRY(dalloc(&c->final_norm, c->cfg.dim));
+    CUDA_TRY(cudaMemcpy(c->final_norm, gain, len * 4, cudaMemcpyHostToDevice));
+    return VOX_OK;
+}
+
+int vox_ctx_init_random(vox_ctx* c, uint64_t seed, float stdv) {
+    if (!c) return fail(VOX_ERR_INVALID_ARG, "context is null");
+    CUDA_TRY(cudaSetDevice(c->dev));
+    const long long dim = (long long)c->cfg.dim, hid = (long long)c->cfg.hidden_dim;
+    const long long qd = (long long)c->q_dim, kvd = (long long)c->kv_dim;
+    const int ws = c->wsize;
+    cudaStream_t s = c->stream;
+    for (size_t l = 0; l < c->layers.size(); ++l) {
+        LayerDev& L = c->layers[l];
+        TRY(alloc_layer(c, L));
+        const uint64_t b = 16 * (uint64_t)l;
+        CUDA_TRY(launch_gen_matrix(L.wqkv, ws, seed, b + 1, stdv, qd, dim, 1, 0, s));
+        CUDA_TRY(launch_gen_matrix(L.wqkv, ws, seed, b + 2, stdv, kvd, dim, 1, (int)qd, s));
+        CUDA_TRY(launch_gen_matrix(L.wqkv, ws, seed, b + 3, stdv, kvd, dim, 1, (int)(qd + kvd), s));
+        CUDA_TRY(launch_gen_matrix(L.wo, ws, seed, b + 4, stdv, dim, qd, 1, 0, s));
+        CUDA_TRY(launch_gen_matrix(L.w13, ws, seed, b + 5, stdv, hid, dim, 2, 0, s));
+        CUDA_TRY(launch_gen_matrix(L.w2, ws, seed, b + 6, stdv, dim, hid, 1, 0, s));
+        CUDA_TRY(launch_gen_matrix(L.w13, ws, seed, b + 7, stdv, hid, dim, 2, 1, s));
+        CUDA_TRY(launch_fill_f32(L.attn_norm, 1.0f, dim, s));
+        CUDA_TRY(launch_fill_f32(L.ffn_norm, 1.0f, dim, s));
+        L.ready = true;
+    }
+    if (c->opt.vocab) {
+        const long long V = (long long)c->opt.vocab;
+        if (!c->embed) CUDA_TRY(dalloc(&c->embed, (size_t)(V * dim)));
+        if (!c->lm_head) CUDA_TRY(cudaMalloc(&c->lm_head, (size_t)(V * dim) * ws));
+        if (!c->final_norm) CUDA_TRY(dalloc(&c->final_norm, (size_t)dim));
+        CUDA_TRY(launch_gen_matrix(c->embed, 2, seed, 1000000, stdv, V, dim, 1, 0, s));
+        CUDA_TRY(launch_gen_matrix(c->lm_head, ws, seed, 1000001, stdv, V, dim, 1, 0, s));
+        CUDA_TRY(launch_fill_f32(c->final_norm, 1.0f, dim, s));
+        c->embed_ready = c->head_ready = true;
+    }
+    CUDA_TRY(cudaStreamSynchronize(s));
+    return VOX_OK;
+}
+
+int vox_ctx_download_matrix(vox_ctx* c, size_t layer, int which, void* out, size_t out_bytes) {
+    if (!c || !out) return fail(VOX_ERR_INVALID_ARG, "null argument");
+    CUDA_TRY(cudaSetDevice(c->dev));
+    const size_t dim = c->cfg.dim, hid = c->cfg.hidden_dim, ws = c->wsize;
+    if (which >= 7) {
+        if (!c->embed_ready || !c->head_ready) return fail(VOX_ERR_NOT_READY, "no embedding / LM head");
+        const size_t n = c->opt.vocab * dim;
+        const size_t es = which == 7 ? 2 : ws;
+        if (out_bytes < n * es) return fail(VOX_ERR_SHAPE, "output buffer too small");
+        CUDA_TRY(cudaMemcpy(out, which == 7 ? (void*)c->embed : c->lm_head, n * es, cudaMemcpyDeviceToHost));
+        return VOX_OK;
+    }
+    if (layer >= c->layers.size() || !c->layers[layer].ready)
+        return fail(VOX_ERR_NOT_READY, "layer %zu not uploaded", layer);
+    const LayerDev& L = c->layers[layer];
+    const unsigned char* qkv = static_cast<const unsigned char*>(L.wqkv);
+    const void* src = nullptr;
+    size_t n = 0;
+    switch (which) {
+        case 0: src = qkv; n = c->q_dim * dim; break;
+        case 1: src = qkv + c->q_dim * dim * ws; n = c->kv_dim * dim; break;
+        case 2: src = qkv + (c->q_dim + c->kv_dim) * dim * ws; n = c->kv_dim * dim; break;
+        case 3: src = L.wo; n = dim * c->q_dim; break;
+        case 5: src = L.w2; n = dim * hid; break;
+        case 4:
+        case 6: {
+            n = hid * dim;
+            if (out_bytes < n * ws) return fail(VOX_ERR_SHAPE, "output buffer too small");
+            const size_t row = dim * ws;
+            CUDA_TRY(cudaMemcpy2D(out, row, static_cast<const unsigned char*>(L.w13) + (which == 6 ? row : 0),
+                                  2 * row, row, hid, cudaMemcpyDeviceToHost));
+            return VOX_OK;
+        }
+        default: return fail(VOX_ERR_INVALID_ARG, "unknown matrix %d", which);
+    }
+    if (out_bytes < n * ws) return fail(VOX_ERR_SHAPE, "output buffer too small");
+    CUDA_TRY(cudaMemcpy(out, src, n * ws, cudaMemcpyDeviceToHost));
+    return VOX_OK;
+}
+
+void* vox_ctx_stream(vox_ctx* c) { return c ? (void*)c->stream : nullptr; }
+
+int vox_ctx_synchronize(vox_ctx* c) {
+    if (!c) return fail(VOX_ERR_INVALID_ARG, "context is null");
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    return check_device_errors(c);
+}
+
+int vox_ctx_record_event(vox_ctx* c, int slot) {
+    if (!c || slot < 0 || slot >= 16) return fail(VOX_ERR_INVALID_ARG, "bad event slot");
+    CUDA_TRY(cudaEventRecord(c->ev[slot], c->stream));
+    return VOX_OK;
+}
+
+int vox_ctx_event_elapsed_ms(vox_ctx* c, int a, int b, float* ms) {
+    if (!c || !ms || a < 0 || a >= 16 || b < 0 || b >= 16) return fail(VOX_ERR_INVALID_ARG, "bad event slot");
+    CUDA_TRY(cudaEventSynchronize(c->ev[b]));
+    CUDA_TRY(cudaEventElapsedTime(ms, c->ev[a], c->ev[b]));
+    return VOX_OK;
+}
+
+uint64_t vox_ctx_kernel_launches(vox_ctx* c) { return c ? c->launches : 0; }
+
+// ---- KV cache ----------------------------------------------------------------
+int vox_kv_create_ex(vox_ctx* c, size_t n_layers, size_t n_kv, size_t hd, size_t window, size_t cap,
+                     vox_kv** out) {
+    if (!c || !out) return fail(VOX_ERR_INVALID_ARG, "null argument");
+    *out = nullptr;
+    if (n_layers == 0 || n_kv == 0 || hd == 0 || window == 0)
+        return fail(VOX_ERR_INVALID_ARG, "n_layers, n_kv_heads, head_dim and sliding_window must be > 0");
+    if (cap < window) return fail(VOX_ERR_INVALID_ARG, "capacity below the window");
+    if (cap > (size_t)INT32_MAX / 2) return fail(VOX_ERR_UNSUPPORTED, "capacity too large");
+    CUDA_TRY(cudaSetDevice(c->dev));
+    vox_kv* kv = new vox_kv();
+    kv->ctx = c;
+    kv->n_layers = n_layers;
+    kv->n_kv = n_kv;
+    kv->hd = hd;
+    kv->window = window;
+    kv->cap = cap;
+    kv->hs.assign(n_layers, HostKv{});
+    cudaError_t e = dalloc(&kv->k, n_layers * kv->layer_elems());
+    if (e == cudaSuccess) e = dalloc(&kv->v, n_layers * kv->layer_elems());
+    if (e == cudaSuccess) e = dalloc(&kv->dstate, n_layers);
+    if (e == cudaSuccess) e = cudaMemset(kv->dstate, 0, n_layers * sizeof(KvState));
+    if (e != cudaSuccess) {
+        vox_kv_destroy(kv);
+        return fail(e == cudaErrorMemoryAllocation ? VOX_ERR_OOM : VOX_ERR_CUDA, "cache allocation: %s",
+                    cudaGetErrorString(e));
+    }
+    *out = kv;
+    return VOX_OK;
+}
+
+int vox_kv_create(vox_ctx* c, size_t n_layers, size_t n_kv, size_t hd, size_t window, vox_kv** out) {
+    return vox_kv_create_ex(c, n_layers, n_kv, hd, window, window, out);
+}
+
+void vox_kv_destroy(vox_kv* kv) {
+    if (!kv) return;
+    cudaSetDevice(kv->ctx->dev);
+    cudaStreamSynchronize(kv->ctx->stream);
+    if (kv->step_graph) cudaGraphExecDestroy(kv->step_graph);
+    cudaFree(kv->k);
+    cudaFree(kv->v);
+    cudaFree(kv->dstate);
+    delete kv;
+}
+
+int vox_kv_reset(vox_kv* kv) {
+    if (!kv) return fail(VOX_ERR_INVALID_ARG, "cache is null");
+    CUDA_TRY(cudaSetDevice(kv->ctx->dev));
+    CUDA_TRY(cudaStreamSynchronize(kv->ctx->stream));
+    kv->hs.assign(kv->n_layers, HostKv{});
+    CUDA_TRY(cudaMemset(kv->dstate, 0, kv->n_layers * sizeof(KvState)));
+    return VOX_OK;
+}
+
+int vox_kv_append_layer(vox_kv* kv, size_t layer, const float* k_new, const float* v_new, size_t n) {
+    if (!kv) return fail(VOX_ERR_INVALID_ARG, "cache is null");
+    if (layer >= kv->n_layers) return fail(VOX_ERR_INVALID_ARG, "layer %zu out of range", layer);
+    if (n == 0) return VOX_OK;  // kv.rs:55-57
+    if (!k_new || !v_new) return fail(VOX_ERR_INVALID_ARG, "null k/v");
+    vox_ctx* c = kv->ctx;
+    CUDA_TRY(cudaSetDevice(c->dev));
+    HostKv s = kv->hs[layer];
+    const long long slot0 = host_append(s, n, kv->window, kv->cap);
+    if (slot0 < 0)
+        return fail(VOX_ERR_UNSUPPORTED, "append of %zu tokens exceeds the ring capacity %zu", n, kv->cap);
+    const size_t elems = n * kv->n_kv * kv->hd;
+    TRY(ensure_scratch(c, 2 * elems * 4));
+    float* sk = static_cast<float*>(c->scratch);
+    float* sv = sk + elems;
+    CUDA_TRY(cudaMemcpyAsync(sk, k_new, elems * 4, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(sv, v_new, elems * 4, cudaMemcpyHostToDevice, c->stream));
+    // Only the last `cap` tokens can survive; skip the rest.
+    size_t skip = n > kv->cap ? n - kv->cap : 0;
+    CUDA_TRY(record_launch(c, launch_kv_scatter(sk + skip * kv->n_kv * kv->hd, sv + skip * kv->n_kv * kv->hd,
+                                                kv->k + layer * kv->layer_elems(),
+                                                kv->v + layer * kv->layer_elems(), (int)kv->n_kv,
+                                                (int)kv->hd, (int)kv->cap, (int)((slot0 + skip) % kv->cap),
+                                                (int)(n - skip), c->stream)));
+    kv->hs[layer] = s;
+    return upload_state(kv, layer);
+}
+
+int vox_kv_layer_len_tokens(const vox_kv* kv, size_t layer, size_t* out) {
+    if (!kv || !out || layer >= kv->n_layers) return fail(VOX_ERR_INVALID_ARG, "bad argument");
+    *out = kv->hs[layer].len;
+    return VOX_OK;
+}
+
+int vox_kv_layer_pos_offset(const vox_kv* kv, size_t layer, size_t* out) {
+    if (!kv || !out || layer >= kv->n_layers) return fail(VOX_ERR_INVALID_ARG, "bad argument");
+    *out = kv->hs[layer].pos_offset;
+    return VOX_OK;
+}
+
+int vox_kv_layer_device_state(const vox_kv* kv, size_t layer, int64_t out[3]) {
+    if (!kv || !out || layer >= kv->n_layers) return fail(VOX_ERR_INVALID_ARG, "bad argument");
+    vox_ctx* c = kv->ctx;
+    CUDA_TRY(cudaSetDevice(c->dev));
+    KvState d{};
+    CUDA_TRY(cudaMemcpyAsync(&d, kv->dstate + layer, sizeof d, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    out[0] = d.len;
+    out[1] = d.start;
+    out[2] = d.pos_offset;
+    return VOX_OK;
+}
+
+int vox_kv_layer_tensors(const vox_kv* kv, size_t layer, float* keys, float* values, size_t cap_elems) {
+    if (!kv || layer >= kv->n_layers) return fail(VOX_ERR_INVALID_ARG, "bad argument");
+    vox_ctx* c = kv->ctx;
+    const HostKv& s = kv->hs[layer];
+    const size_t elems = s.len * kv->n_kv * kv->hd;
+    if (elems == 0) return VOX_OK;
+    if (!keys || !values || cap_elems < elems)
+        return fail(VOX_ERR_SHAPE, "buffers hold %zu elements, need %zu", cap_elems, elems);
+    CUDA_TRY(cudaSetDevice(c->dev));
+    TRY(ensure_scratch(c, 2 * elems * 4));
+    float* dk = static_cast<float*>(c->scratch);
+    float* dv = dk + elems;
+    CUDA_TRY(record_launch(c, launch_kv_gather(kv->k + layer * kv->layer_elems(), kv->v + layer * kv->layer_elems(),
+                                               dk, dv, (int)kv->n_kv, (int)kv->hd, (int)kv->cap, (int)s.start,
+                                               (int)s.len, c->stream)));
+    CUDA_TRY(cudaMemcpyAsync(keys, dk, elems * 4, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(values, dv, elems * 4, cudaMemcpyDeviceToHost, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    return VOX_OK;
+}
+
+// ---- decoder layer step --------------------------------------------------------
+int vox_decoder_layer_forward_step(vox_ctx* c, size_t layer, vox_kv* kv, const float* hidden,
+                                   size_t hidden_len, size_t pos, float* out, size_t out_len) {
+    if (!c || !kv) return fail(VOX_ERR_INVALID_ARG, "null context or cache");
+    TRY(validate_cfg(&c->cfg));                                    // decoder.rs:96
+    if (layer >= c->layers.size() || !c->layers[layer].ready)      // decoder.rs:97
+        return fail(VOX_ERR_NOT_READY, "layer %zu weights not uploaded", layer);
+    if (hidden_len != c->cfg.dim || !hidden) return fail(VOX_ERR_SHAPE, "hidden size mismatch");  // :98
+    if (out_len != c->cfg.dim || !out) return fail(VOX_ERR_SHAPE, "output size mismatch");
+    if (kv->ctx != c) return fail(VOX_ERR_INVALID_ARG, "cache belongs to another context");
+    if (layer >= kv->n_layers) return fail(VOX_ERR_INVALID_ARG, "layer %zu beyond the cache", layer);
+    if (kv->n_kv != c->cfg.n_kv_heads || kv->hd != c->cfg.head_dim)
+        return fail(VOX_ERR_SHAPE, "cache head shape does not match the decoder config");
+    if (pos >= (size_t)c->max_pos) return fail(VOX_ERR_RANGE, "position %zu beyond max_positions %d", pos, c->max_pos);
+    CUDA_TRY(cudaSetDevice(c->dev));
+    StepState* hs = c->h_steps;
+    CUDA_TRY(cudaStreamSynchronize(c->stream));  // the pinned slot is reused below
+    std::memset(hs, 0, sizeof(StepState));
+    hs->pos = (int64_t)pos;
+    CUDA_TRY(cudaMemcpyAsync(c->step, hs, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(c->hid, hidden, c->cfg.dim * 4, cudaMemcpyHostToDevice, c->stream));
+    TRY(enqueue_layer(c, kv, layer, false, true));
+    CUDA_TRY(cudaMemcpyAsync(out, c->hid, c->cfg.dim * 4, cudaMemcpyDeviceToHost, c->stream));
+    TRY(check_device_errors(c));
+    host_append(kv->hs[layer], 1, kv->window, kv->cap);
+    return VOX_OK;
+}
+
+// ---- token loop --------------------------------------------------------------------
+int vox_model_step(vox_ctx* c, vox_kv* kv, int32_t token, size_t pos, int32_t* next_token, float* logits) {
+    TRY(model_ready(c, kv));
+    if (token < 0 || (size_t)token >= c->opt.vocab) return fail(VOX_ERR_RANGE, "token %d outside the vocabulary", token);
+    if (pos >= (size_t)c->max_pos) return fail(VOX_ERR_RANGE, "position %zu beyond max_positions %d", pos, c->max_pos);
+    CUDA_TRY(cudaSetDevice(c->dev));
+    TRY(build_step_graph(c, kv));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    StepState* hs = c->h_steps;
+    std::memset(hs, 0, sizeof(StepState));
+    hs->pos = (int64_t)pos;
+    hs->tok = token;
+    CUDA_TRY(cudaMemcpyAsync(c->step, hs, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
+    TRY(launch_graph(c, kv));
+    CUDA_TRY(cudaMemcpyAsync(c->h_tok, c->tok_out, 4, cudaMemcpyDeviceToHost, c->stream));
+    if (logits)
+        CUDA_TRY(cudaMemcpyAsync(logits, c->logits, c->opt.vocab * 4, cudaMemcpyDeviceToHost, c->stream));
+    TRY(check_device_errors(c));
+    mirror_single_append_all(kv);
+    if (next_token) *next_token = *c->h_tok;
+    return VOX_OK;
+}
+
+int vox_model_prefill(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, size_t pos0) {
+    TRY(model_ready(c, kv));
+    if (n == 0) return VOX_OK;
+    if (!tokens) return fail(VOX_ERR_INVALID_ARG, "tokens is null");
+    if (pos0 + n > (size_t)c->max_pos) return fail(VOX_ERR_RANGE, "positions beyond max_positions %d", c->max_pos);
+    for (size_t i = 0; i < n; ++i)
+        if (tokens[i] < 0 || (size_t)tokens[i] >= c->opt.vocab)
+            return fail(VOX_ERR_RANGE, "token %d outside the vocabulary", tokens[i]);
+    CUDA_TRY(cudaSetDevice(c->dev));
+    TRY(build_step_graph(c, kv));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    TRY(ensure_host_steps(c, n));
+    for (size_t i = 0; i < n; ++i) {
+        StepState* hs = c->h_steps + i;
+        std::memset(hs, 0, sizeof(StepState));
+        hs->pos = (int64_t)(pos0 + i);
+        hs->tok = tokens[i];
+        CUDA_TRY(cudaMemcpyAsync(c->step, hs, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
+        TRY(launch_graph(c, kv));
+    }
+    TRY(check_device_errors(c));
+    for (size_t i = 0; i < n; ++i) mirror_single_append_all(kv);
+    return VOX_OK;
+}
+
+int vox_model_generate(vox_ctx* c, vox_kv* kv, int32_t token, size_t pos, size_t n_steps, int32_t* tokens_out) {
+    TRY(model_ready(c, kv));
+    if (n_steps == 0) return VOX_OK;
+    if (token < 0 || (size_t)token >= c->opt.vocab) return fail(VOX_ERR_RANGE, "token %d outside the vocabulary", token);
+    if (pos + n_steps > (size_t)c->max_pos) return fail(VOX_ERR_RANGE, "positions beyond max_positions %d", c->max_pos);
+    CUDA_TRY(cudaSetDevice(c->dev));
+    TRY(build_step_graph(c, kv));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    TRY(ensure_host_steps(c, n_steps + 1));
+    StepState* hs = c->h_steps;
+    std::memset(hs, 0, sizeof(StepState));
+    hs->pos = (int64_t)pos;
+    hs->tok = token;
+    hs->greedy = 1;
+    hs->advance = 1;
+    CUDA_TRY(cudaMemcpyAsync(c->step, hs, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
+    int32_t* tok_hist = reinterpret_cast<int32_t*>(c->h_steps + 1);  // pinned staging for the ids
+    for (size_t i = 0; i < n_steps; ++i) {
+        TRY(launch_graph(c, kv));
+        if (tokens_out)
+            CUDA_TRY(cudaMemcpyAsync(tok_hist + i, c->tok_out, 4, cudaMemcpyDeviceToHost, c->stream));
+    }
+    TRY(check_device_errors(c));
+    for (size_t i = 0; i < n_steps; ++i) mirror_single_append_all(kv);
+    if (tokens_out) std::memcpy(tokens_out, tok_hist, n_steps * 4);
+    return VOX_OK;
+}
+
+// ---- profiling hook ----------------------------------------------------------------
+int vox_profile_gemv(vox_ctx* c, int which, size_t n, float* avg_ms, uint64_t* bytes_per_launch) {
+    if (!c || !avg_ms || n == 0) return fail(VOX_ERR_INVALID_ARG, "bad argument");
+    if (which < 1 || which > 4) return fail(VOX_ERR_INVALID_ARG, "which must be 1..4");
+    for (size_t l = 0; l < c->layers.size(); ++l)
+        if (!c->layers[l].ready) return fail(VOX_ERR_NOT_READY, "layer %zu weights not uploaded", l);
+    if (which == 4 && (!c->head_ready || !c->opt.vocab)) return fail(VOX_ERR_NOT_READY, "no LM head");
+    CUDA_TRY(cudaSetDevice(c->dev));
+    const GemvPlan* plan = which == 1 ? &c->p_o : which == 2 ? &c->p_w13 : which == 3 ? &c->p_w2 : &c->p_head;
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    CUDA_TRY(cudaEventRecord(c->ev[14], c->stream));
+    for (size_t i = 0; i < n; ++i) {
+        const LayerDev& L = c->layers[i % c->layers.size()];
+        GemvArgs a = base_args(c);
+        int epi = EPI_RESID;
+        if (which == 1) {
+            a.W = L.wo; a.x = c->attn; a.y = c->hmid; a.resid = c->hid;
+        } else if (which == 2) {
+            a.W = L.w13; a.x = c->hmid; a.norm_w = L.ffn_norm; a.y = c->act; epi = EPI_SWIGLU;
+        } else if (which == 3) {
+            a.W = L.w2; a.x = c->act; a.y = c->hmid; a.resid = c->hmid;
+        } else {
+            a.W = c->lm_head; a.x = c->hid; a.norm_w = c->final_norm; a.y = c->logits;
+            a.am_part = c->am_part; epi = EPI_ARGMAX;
+        }
+        CUDA_TRY(record_launch(c, launch_gemv(*plan, a, epi, c->stream, true)));
+    }
+    CUDA_TRY(cudaEventRecord(c->ev[15], c->stream));
+    CUDA_TRY(cudaEventSynchronize(c->ev[15]));
+    float ms = 0.f;
+    CUDA_TRY(cudaEventElapsedTime(&ms, c->ev[14], c->ev[15]));
+    *avg_ms = ms / (float)n;
+    if (bytes_per_launch) *bytes_per_launch = (uint64_t)plan->rows * (uint64_t)plan->K * (uint64_t)c->wsize;
+    return check_device_errors(c);
+}
+
+// ---- op-level entry points ----------------------------------------------------------
+static int linear_impl(vox_ctx* c, const float* input, size_t n_rows, size_t in_dim, const void* weight,
+                       int wsize, size_t out_dim, const float* bias, float* out) {
+    if (!c || !input || !weight || !out) return fail(VOX_ERR_INVALID_ARG, "null argument");
+    if (n_rows == 0 || out_dim == 0) return VOX_OK;
+    if (!gemv_supported((int)in_dim, wsize) || in_dim > (1u << 30) || out_dim > (1u << 30) || n_rows > 65535)
+        return fail(VOX_ERR_UNSUPPORTED, "linear: in_dim %zu must be a multiple of %d and at most %d", in_dim,
+                    16 / wsize, wsize == 2 ? 16384 : 8192);
+    CUDA_TRY(cudaSetDevice(c->dev));
+    GemvPlan p = plan_gemv((int)out_dim, (int)in_dim, 1, wsize, c->num_sms, (int)n_rows);
+    if (p.grid < 1 || p.smem > gemv_max_smem()) return fail(VOX_ERR_UNSUPPORTED, "no plan for this linear");
+    const size_t wb = (out_dim * in_dim * wsize + 255) & ~size_t(255);
+    const size_t xb = (n_rows * in_dim * 4 + 255) & ~size_t(255);
+    const size_t yb = (n_rows * out_dim * 4 + 255) & ~size_t(255);
+    const size_t bb = (out_dim * 4 + 255) & ~size_t(255);
+    TRY(ensure_scratch(c, wb + xb + yb + bb));
+    unsigned char* base = static_cast<unsigned char*>(c->scratch);
+    void* dW = base;
+    float* dx = reinterpret_cast<float*>(base + wb);
+    float* dy = reinterpret_cast<float*>(base + wb + xb);
+    float* db = reinterpret_cast<float*>(base + wb + xb + yb);
+    CUDA_TRY(cudaMemcpyAsync(dW, weight, out_dim * in_dim * wsize, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(dx, input, n_rows * in_dim * 4, cudaMemcpyHostToDevice, c->stream));
+    if (bias) CUDA_TRY(cudaMemcpyAsync(db, bias, out_dim * 4, cudaMemcpyHostToDevice, c->stream));
+    GemvArgs a = base_args(c);
+    a.W = dW;
+    a.x = dx;
+    a.x_stride = (long long)in_dim;
+    a.y = dy;
+    a.y_stride = (long long)out_dim;
+    a.bias = bias ? db : nullptr;
+    CUDA_TRY(record_launch(c, launch_gemv(p, a, EPI_STORE, c->stream, false)));
+    CUDA_TRY(cudaMemcpyAsync(out, dy, n_rows * out_dim * 4, cudaMemcpyDeviceToHost, c->stream));
+    return check_device_errors(c);
+}
+
+int vox_linear_f32(vox_ctx* c, const float* input, size_t n_rows, size_t in_dim, const float* weight,
+                   size_t out_dim, const float* bias, float* out) {
+    return linear_impl(c, input, n_rows, in_dim, weight, 4, out_dim, bias, out);
+}
+
+int vox_linear_bf16(vox_ctx* c, const float* input, size_t n_rows, size_t in_dim, const uint16_t* weight,
+                    size_t out_dim, const float* bias, float* out) {
+    return linear_impl(c, input, n_rows, in_dim, weight, 2, out_dim, bias, out);
+}
+
+int vox_silu_inplace(vox_ctx* c, float* x, size_t n) {
+    return inplace_op(c, x, n, [&](float* d) { return launch_silu(d, (long long)n, c->stream); });
+}
+
+int vox_softmax_inplace(vox_ctx* c, float* x, size_t n) {
+    return inplace_op(c, x, n, [&](float* d) { return launch_softmax(d, (long long)n, c->stream); });
+}
+
+int vox_add_inplace(vox_ctx* c, float* dst, const float* src, size_t n) {
+    if (!c || ((!dst || !src) && n)) return fail(VOX_ERR_INVALID_ARG, "null argument");
+    if (n == 0) return VOX_OK;
+    CUDA_TRY(cudaSetDevice(c->dev));
+    TRY(ensure_scratch(c, 2 * n * 4 + 256));
+    float* dd = static_cast<float*>(c->scratch);
+    float* ds = dd + ((n + 63) & ~size_t(63));
+    CUDA_TRY(cudaMemcpyAsync(dd, dst, n * 4, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(ds, src, n * 4, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(record_launch(c, launch_add(dd, ds, (long long)n, c->stream)));
+    CUDA_TRY(cudaMemcpyAsync(dst, dd, n * 4, cudaMemcpyDeviceToHost, c->stream));
+    return check_device_errors(c);
+}
+
+int vox_rms_norm_rows(vox_ctx* c, float* out, const float* input, const float* weight, size_t n_elems,
+                      size_t dim, float eps) {
+    if (!c || ((!out || !input || !weight) && n_elems)) return fail(VOX_ERR_INVALID_ARG, "null argument");
+    if (dim == 0) return fail(VOX_ERR_INVALID_ARG, "dim must be > 0");
+    const size_t rows = n_elems / dim;  // math.rs:17 chunks_exact: a ragged tail is left untouched
+    if (rows == 0) return VOX_OK;
+    if (rows > 0x7FFFFFFF) return fail(VOX_ERR_UNSUPPORTED, "too many rows");
+    CUDA_TRY(cudaSetDevice(c->dev));
+    const size_t n = rows * dim, nb = (n * 4 + 255) & ~size_t(255), wb = (dim * 4 + 255) & ~size_t(255);
+    TRY(ensure_scratch(c, 2 * nb + wb));
+    unsigned char* base = static_cast<unsigned char*>(c->scratch);
+    float* din = reinterpret_cast<float*>(base);
+    float* dout = reinterpret_cast<float*>(base + nb);
+    float* dw = reinterpret_cast<float*>(base + 2 * nb);
+    CUDA_TRY(cudaMemcpyAsync(din, input, n * 4, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(dw, weight, dim * 4, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(record_launch(c, launch_rmsnorm_rows(dout, din, dw, (long long)rows, (int)dim, eps, c->stream)));
+    CUDA_TRY(cudaMemcpyAsync(out, dout, n * 4, cudaMemcpyDeviceToHost, c->stream));
+    return check_device_errors(c);
+}
+
+int vox_rope_interleaved_inplace(vox_ctx* c, float* data, size_t seq_len, size_t n_heads, size_t hd,
+                                 size_t pos_offset, float theta) {
+    if (!c) return fail(VOX_ERR_INVALID_ARG, "context is null");
+    if (hd % 2) return fail(VOX_ERR_INVALID_ARG, "head_dim must be even");  // math.rs:39
+    const size_t n = seq_len * n_heads * hd;
+    if (n == 0) return VOX_OK;
+    if (!data) return fail(VOX_ERR_INVALID_ARG, "data is null");
+    CUDA_TRY(cudaSetDevice(c->dev));
+    // Angle table in f32 with libm (math.rs:52-56); the rotation runs on the GPU.
+    const size_t half = hd / 2;
+    std::vector<float> ct(seq_len * half), st(seq_len * half), inv(half);
+    for (size_t p = 0; p < half; ++p) inv[p] = powf(theta, -((float)(2 * p)) / (float)hd);
+    for (size_t t = 0; t < seq_len; ++t) {
+        const float posf = (float)(pos_offset + t);
+        for (size_t p = 0; p < half; ++p) {
+            const float angle = posf * inv[p];
+            st[t * half + p] = sinf(angle);
+            ct[t * half + p] = cosf(angle);
+        }
+    }
+    const size_t db = (n * 4 + 255) & ~size_t(255), tb = (seq_len * half * 4 + 255) & ~size_t(255);
+    TRY(ensure_scratch(c, db + 2 * tb));
+    unsigned char* base = static_cast<unsigned char*>(c->scratch);
+    float* dd = reinterpret_cast<float*>(base);
+    float* dc = reinterpret_cast<float*>(base + db);
+    float* ds = reinterpret_cast<float*>(base + db + tb);
+    CUDA_TRY(cudaMemcpyAsync(dd, data, n * 4, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(dc, ct.data(), seq_len * half * 4, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(ds, st.data(), seq_len * half * 4, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(record_launch(c, launch_rope_table(dd, dc, ds, (long long)seq_len, (int)n_heads, (int)hd, c->stream)));
+    CUDA_TRY(cudaMemcpyAsync(data, dd, n * 4, cudaMemcpyDeviceToHost, c->stream));
+    return check_device_errors(c);
+}
+
+int vox_attention_gqa_step(vox_ctx* c, const float* q, const float* keys, const float* values,
+                           const vox_attention_shape* sh, float* out) {
+    if (!c || !sh || !q || !out) return fail(VOX_ERR_INVALID_ARG, "null argument");
+    if (sh->n_heads == 0 || sh->n_kv_heads == 0 || sh->head_dim == 0)
+        return fail(VOX_ERR_INVALID_ARG, "n_heads, n_kv_heads and head_dim must be > 0");
+    if (sh->n_heads % sh->n_kv_heads) return fail(VOX_ERR_INVALID_ARG, "n_heads must be divisible by n_kv_heads");
+    if (!attn_supported((int)sh->n_heads, (int)sh->n_kv_heads, (int)sh->head_dim))
+        return fail(VOX_ERR_UNSUPPORTED, "attention shape not supported");
+    if (sh->seq_len > (size_t)INT32_MAX / 2) return fail(VOX_ERR_UNSUPPORTED, "seq_len too large");
+    if (sh->seq_len && (!keys || !values)) return fail(VOX_ERR_INVALID_ARG, "null keys/values");
+    CUDA_TRY(cudaSetDevice(c->dev));
+    const size_t nh = sh->n_heads, nkv = sh->n_kv_heads, hd = sh->head_dim, L = sh->seq_len;
+    const size_t G = nh / nkv;
+    const int nsplit = attn_splits_for((int)nkv, c->num_sms);
+    auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
+    const size_t kvb = al(L * nkv * hd * 4), qb = al(nh * hd * 4), pb = al(nkv * nsplit * G * (hd + 2) * 4),
+                 tb = al(nkv * 4), sb = al(sizeof(KvState));
+    TRY(ensure_scratch(c, 4 * kvb + 2 * qb + pb + tb + sb));
+    unsigned char* base = static_cast<unsigned char*>(c->scratch);
+    float* stage_k = reinterpret_cast<float*>(base);
+    float* stage_v = reinterpret_cast<float*>(base + kvb);
+    float* ring_k = reinterpret_cast<float*>(base + 2 * kvb);
+    float* ring_v = reinterpret_cast<float*>(base + 3 * kvb);
+    float* dq = reinterpret_cast<float*>(base + 4 * kvb);
+    float* dout = reinterpret_cast<float*>(base + 4 * kvb + qb);
+    float* dpart = reinterpret_cast<float*>(base + 4 * kvb + 2 * qb);
+    unsigned* dtick = reinterpret_cast<unsigned*>(base + 4 * kvb + 2 * qb + pb);
+    KvState* dst = reinterpret_cast<KvState*>(base + 4 * kvb + 2 * qb + pb + tb);
+    if (L) {
+        CUDA_TRY(cudaMemcpyAsync(stage_k, keys, L * nkv * hd * 4, cudaMemcpyHostToDevice, c->stream));
+        CUDA_TRY(cudaMemcpyAsync(stage_v, values, L * nkv * hd * 4, cudaMemcpyHostToDevice, c->stream));
+        CUDA_TRY(record_launch(c, launch_kv_scatter(stage_k, stage_v, ring_k, ring_v, (int)nkv, (int)hd, (int)L, 0,
+                                                    (int)L, c->stream)));
+    }
+    CUDA_TRY(cudaMemcpyAsync(dq, q, nh * hd * 4, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(cudaMemsetAsync(dtick, 0, nkv * 4, c->stream));
+    KvState* hst = reinterpret_cast<KvState*>(c->h_steps);
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    hst->len = (int32_t)L;
+    hst->start = 0;
+    hst->pos_offset = 0;
+    CUDA_TRY(cudaMemcpyAsync(dst, hst, sizeof(KvState), cudaMemcpyHostToDevice, c->stream));
+    AttnArgs at{};
+    at.q = dq;
+    at.k_ring = ring_k;
+    at.v_ring = ring_v;
+    at.n_heads = (int)nh;
+    at.n_kv = (int)nkv;
+    at.hd = (int)hd;
+    at.cap = L ? (int)L : 1;
+    at.cfg_window = (int)sh->sliding_window;
+    at.st = dst;
+    at.pre_append = 0;
+    at.nsplit = nsplit;
+    at.part = dpart;
+    at.tickets = dtick;
+    at.out = dout;
+    at.scale = 1.0f / sqrtf((float)hd);  // ops.rs:89
+    at.err = c->err;
+    CUDA_TRY(record_launch(c, launch_attention(at, c->stream, false)));
+    CUDA_TRY(cudaMemcpyAsync(out, dout, nh * hd * 4, cudaMemcpyDeviceToHost, c->stream));
+    return check_device_errors(c);
+}
+
+}  // extern "C"

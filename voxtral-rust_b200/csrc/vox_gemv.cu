@@ -1,0 +1,493 @@
+// vox_gemv.cu -- batch-1 weight-streaming GEMV for sm_100a.
+//
+// y[r] = sum_k W[r, k] * x[k] for a row-major weight matrix W [rows, K]
+// (bf16 or f32), the reference's `linear` (crates/voxtral/src/ops.rs:11-39)
+// for n_rows = 1, fused with what surrounds each linear in
+// decoder_layer_forward_step (crates/voxtral/src/decoder.rs:88-155):
+//   prologue  RMSNorm of x (math.rs:11-27) or the bf16 embedding row of the
+//             step's token;
+//   epilogue  store (+bias) | residual add (ops.rs:41-46) | RoPE on q/k
+//             (math.rs:30-65) with k/v written into the KV ring slot |
+//             SiLU(gate)*up (math.rs:4-9, decoder.rs:147-150) | argmax.
+//
+// Work split: CTA b owns a contiguous band of rows, hence one contiguous
+// byte range of W.  Warp 8 is a producer: one lane streams the band into a
+// ring of shared-memory stages with cp.async.bulk (TMA, no multicast) and
+// mbarrier completion.  Warps 0..7 consume: warp w always handles K segment
+// (w % nseg) of row pair (w / nseg) of each stage, so its slice of x lives
+// in registers for the whole kernel and shared memory carries weights only.
+// Each (row, segment) partial sum goes to shared memory and is summed in a
+// fixed order, so results are run-to-run deterministic.
+//
+// Programmatic dependent launch: the producer starts streaming weights (which
+// no earlier kernel writes) before griddepcontrol.wait; consumers wait before
+// reading x.  Consecutive GEMVs therefore overlap one kernel's tail with the
+// next kernel's weight fetch.
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include "vox_device.cuh"
+
+namespace vox {
+
+namespace {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr size_t kStageBudget = 108 * 1024;   // weight ring bytes per CTA
+constexpr size_t kSmemLimit = 113 * 1024;     // two CTAs per SM
+
+template <typename WT>
+struct Elem;
+template <>
+struct Elem<uint16_t> {
+    static constexpr int kPerChunk = 8;
+    __device__ static __forceinline__ void fma_chunk(float& acc0, float& acc1, const uint4& w,
+                                                     const float* x) {
+        acc0 = fmaf(bf16_lo(w.x), x[0], acc0);
+        acc1 = fmaf(bf16_hi(w.x), x[1], acc1);
+        acc0 = fmaf(bf16_lo(w.y), x[2], acc0);
+        acc1 = fmaf(bf16_hi(w.y), x[3], acc1);
+        acc0 = fmaf(bf16_lo(w.z), x[4], acc0);
+        acc1 = fmaf(bf16_hi(w.z), x[5], acc1);
+        acc0 = fmaf(bf16_lo(w.w), x[6], acc0);
+        acc1 = fmaf(bf16_hi(w.w), x[7], acc1);
+    }
+};
+template <>
+struct Elem<float> {
+    static constexpr int kPerChunk = 4;
+    __device__ static __forceinline__ void fma_chunk(float& acc0, float& acc1, const uint4& w,
+                                                     const float* x) {
+        acc0 = fmaf(__uint_as_float(w.x), x[0], acc0);
+        acc1 = fmaf(__uint_as_float(w.y), x[1], acc1);
+        acc0 = fmaf(__uint_as_float(w.z), x[2], acc0);
+        acc1 = fmaf(__uint_as_float(w.w), x[3], acc1);
+    }
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
+// silu(g) * u exactly as the reference orders it: g / (1 + exp(-g)), then * u.
+__device__ __forceinline__ float swiglu(float g, float u) {
+    float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+    return __fmul_rn(s, u);
+}
+
+template <typename WT, int CPT, int EPI>
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvPlan P, const GemvArgs A) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int EPC = Elem<WT>::kPerChunk;
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int K = P.K;
+    const int C = K / EPC;                    // 16-byte chunks per row
+    const size_t row_bytes = (size_t)K * sizeof(WT);
+    const uint32_t stage_bytes = (uint32_t)(P.stage_rows * row_bytes);
+
+    // Row band of this CTA (whole units; paired epilogues never straddle CTAs).
+    const int units = P.rows / P.unit;
+    const int u0 = (int)((long long)units * blockIdx.x / gridDim.x);
+    const int u1 = (int)((long long)units * (blockIdx.x + 1) / gridDim.x);
+    const int r0 = u0 * P.unit;
+    const int nrows = (u1 - u0) * P.unit;
+    const int n_stages_total = (nrows + P.stage_rows - 1) / P.stage_rows;
+    const int NS = P.nstages;
+
+    unsigned char* stage_base = smem;
+    float* red = reinterpret_cast<float*>(smem + (size_t)NS * stage_bytes);
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(
+        smem + (((size_t)NS * stage_bytes + (size_t)P.max_rows_cta * P.nseg * 4 + 15) & ~size_t(15)));
+    uint64_t* empty_bar = full_bar + NS;
+    float* scratch = reinterpret_cast<float*>(empty_bar + NS);  // 16 floats + 16 ints
+
+    if (tid == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], kConsumerWarps);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+    pdl_allow_dependents();
+
+    const unsigned char* Wband =
+        reinterpret_cast<const unsigned char*>(A.W) + (size_t)r0 * row_bytes;
+
+    if (warp == kConsumerWarps) {
+        // ---------------- producer ----------------
+        if (lane == 0 && n_stages_total > 0) {
+            const uint64_t pol = l2_evict_first_policy();
+            bool ok = true;
+            int issued = 0;
+            for (int s = 0; s < n_stages_total; ++s) {
+                const int buf = s % NS;
+                if (s >= NS) {
+                    if (!mbar_wait(&empty_bar[buf], ((s / NS) - 1) & 1)) {
+                        raise_error(A.err, ERR_EMPTY_WAIT);
+                        ok = false;
+                        break;
+                    }
+                }
+                const int rows_here = min(P.stage_rows, nrows - s * P.stage_rows);
+                const uint32_t bytes = (uint32_t)(rows_here * row_bytes);
+                mbar_arrive_expect_tx(&full_bar[buf], bytes);
+                bulk_copy_g2s(stage_base + (size_t)buf * stage_bytes,
+                              Wband + (size_t)s * stage_bytes, bytes, &full_bar[buf], pol);
+                ++issued;
+            }
+            if (!ok) {
+                // Leave no copy in flight: wait (bounded) for the last issued stages.
+                for (int s = max(0, issued - NS); s < issued; ++s)
+                    if (!mbar_wait(&full_bar[s % NS], (s / NS) & 1)) raise_error(A.err, ERR_DRAIN_WAIT);
+            }
+        }
+        pdl_wait_prior_grids();
+        return;
+    }
+
+    // ---------------- consumers ----------------
+    pdl_wait_prior_grids();
+
+    const int nseg = P.nseg;
+    const int seg = warp % nseg;
+    const int tp = warp / nseg;               // row pair inside a stage
+    const int segc = C / nseg;
+    const int c0 = seg * segc;
+    const int vec = blockIdx.y;
+
+    // Input vector: x, or the embedding row of the step's token.
+    const float* x = A.x ? A.x + (long long)vec * A.x_stride : nullptr;
+    const uint16_t* xe = nullptr;
+    if (A.x_embed) {
+        int tok = A.step->tok;
+        if (tok < 0 || tok >= A.vocab) {
+            if (tid == 0 && blockIdx.x == 0) raise_error(A.err, ERR_TOKEN_RANGE);
+            tok = 0;
+        }
+        xe = A.x_embed + (size_t)tok * K;
+    }
+
+    float inv_rms = 1.0f;
+    if (A.norm_w || (A.x_copy_out && blockIdx.x == 0)) {
+        float ss = 0.0f;
+        for (int k = tid; k < K; k += kConsumerWarps * 32) {
+            float v = xe ? bf16_bits_to_f32(xe[k]) : x[k];
+            if (A.x_copy_out && blockIdx.x == 0) A.x_copy_out[k] = v;
+            ss = fmaf(v, v, ss);
+        }
+        if (A.norm_w) {
+            ss = warp_sum(ss);
+            if (lane == 0) scratch[warp] = ss;
+            named_barrier_sync(1, kConsumerWarps * 32);
+            float tot = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) tot += scratch[w];
+            // math.rs:22: inv_rms = 1 / sqrt(sq_sum / dim + eps)
+            inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), A.eps)));
+        }
+    }
+
+    // This warp's slice of x in registers (normalised when asked).
+    float xr[CPT][EPC];
+#pragma unroll
+    for (int i = 0; i < CPT; ++i) {
+        const int cc = lane + 32 * i;
+#pragma unroll
+        for (int e = 0; e < EPC; ++e) xr[i][e] = 0.0f;
+        if (cc < segc) {
+            const int k0 = (c0 + cc) * EPC;
+#pragma unroll
+            for (int e = 0; e < EPC; ++e) {
+                float v = xe ? bf16_bits_to_f32(xe[k0 + e]) : x[k0 + e];
+                if (A.norm_w) v = __fmul_rn(__fmul_rn(v, inv_rms), A.norm_w[k0 + e]);
+                xr[i][e] = v;
+            }
+        }
+    }
+
+    bool ok = true;
+    for (int s = 0; s < n_stages_total; ++s) {
+        const int buf = s % NS;
+        if (!mbar_wait(&full_bar[buf], (s / NS) & 1)) {
+            if (lane == 0) raise_error(A.err, ERR_FULL_WAIT);
+            ok = false;
+            break;
+        }
+        const int ra = s * P.stage_rows + 2 * tp;   // local row index
+        if (ra < nrows) {
+            const bool has_b = ra + 1 < nrows;
+            const unsigned char* rowa = stage_base + (size_t)buf * stage_bytes + (size_t)(2 * tp) * row_bytes;
+            const unsigned char* rowb = rowa + row_bytes;
+            float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+#pragma unroll
+            for (int i = 0; i < CPT; ++i) {
+                const int cc = lane + 32 * i;
+                if (cc < segc) {
+                    const uint4 wa = ld_shared_v4(rowa + (size_t)(c0 + cc) * 16);
+                    Elem<WT>::fma_chunk(a0, a1, wa, xr[i]);
+                    if (has_b) {
+                        const uint4 wb = ld_shared_v4(rowb + (size_t)(c0 + cc) * 16);
+                        Elem<WT>::fma_chunk(b0, b1, wb, xr[i]);
+                    }
+                }
+            }
+            const float sa = warp_sum(a0 + a1);
+            const float sb = warp_sum(b0 + b1);
+            if (lane == 0) {
+                red[ra * nseg + seg] = sa;
+                if (has_b) red[(ra + 1) * nseg + seg] = sb;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty_bar[buf]);
+    }
+    named_barrier_sync(1, kConsumerWarps * 32);
+    if (!ok) return;
+
+    // ---------------- epilogue ----------------
+    const int nthr = kConsumerWarps * 32;
+    auto row_sum = [&](int lr) {
+        float v = 0.0f;
+        for (int q = 0; q < nseg; ++q) v += red[lr * nseg + q];
+        return v;
+    };
+
+    if constexpr (EPI == EPI_STORE) {
+        float* y = A.y + (long long)vec * A.y_stride;
+        for (int lr = tid; lr < nrows; lr += nthr) {
+            const int r = r0 + lr;
+            float v = row_sum(lr);
+            if (A.bias) v = __fadd_rn(A.bias[r], v);
+            y[r] = v;
+        }
+    } else if constexpr (EPI == EPI_RESID) {
+        float* y = A.y + (long long)vec * A.y_stride;
+        for (int lr = tid; lr < nrows; lr += nthr) {
+            const int r = r0 + lr;
+            y[r] = __fadd_rn(A.resid[r], row_sum(lr));
+        }
+        if (A.kv_commit && blockIdx.x == 0 && tid == 0)
+            *A.kv_commit = kv_after_single_append(*A.kv_commit, A.kv_window, A.ring_cap);
+    } else if constexpr (EPI == EPI_QKV) {
+        const long long pos = A.step->pos;
+        const bool pos_ok = pos >= 0 && pos < A.max_pos;
+        if (!pos_ok && tid == 0 && blockIdx.x == 0) raise_error(A.err, ERR_POS_RANGE);
+        const int half = A.head_dim / 2;
+        const float* ct = A.rope_cos + (pos_ok ? pos : 0) * half;
+        const float* st = A.rope_sin + (pos_ok ? pos : 0) * half;
+        const KvState post = kv_after_single_append(*A.kv_state, A.kv_window, A.ring_cap);
+        const int slot = (post.start + post.len - 1) % A.ring_cap;
+        for (int pp = tid; pp < nrows / 2; pp += nthr) {
+            const int r = r0 + 2 * pp;
+            const float ya = row_sum(2 * pp), yb = row_sum(2 * pp + 1);
+            if (r < A.q_dim + A.kv_dim) {
+                // math.rs:58-61: (x0*c - x1*s, x0*s + x1*c), unfused
+                const int rr = r < A.q_dim ? r : r - A.q_dim;
+                const int d = rr % A.head_dim;
+                const float c = ct[d / 2], sn = st[d / 2];
+                const float o0 = __fsub_rn(__fmul_rn(ya, c), __fmul_rn(yb, sn));
+                const float o1 = __fadd_rn(__fmul_rn(ya, sn), __fmul_rn(yb, c));
+                if (r < A.q_dim) {
+                    A.y[r] = o0;
+                    A.y[r + 1] = o1;
+                } else {
+                    const int h = rr / A.head_dim;
+                    float* dst = A.k_ring + ((size_t)h * A.ring_cap + slot) * A.head_dim + d;
+                    dst[0] = o0;
+                    dst[1] = o1;
+                }
+            } else {
+                const int rr = r - A.q_dim - A.kv_dim;
+                const int h = rr / A.head_dim, d = rr % A.head_dim;
+                float* dst = A.v_ring + ((size_t)h * A.ring_cap + slot) * A.head_dim + d;
+                dst[0] = ya;
+                dst[1] = yb;
+            }
+        }
+    } else if constexpr (EPI == EPI_SWIGLU) {
+        float* y = A.y + (long long)vec * A.y_stride;
+        for (int pp = tid; pp < nrows / 2; pp += nthr) {
+            const int j = (r0 >> 1) + pp;
+            y[j] = swiglu(row_sum(2 * pp), row_sum(2 * pp + 1));
+        }
+    } else if constexpr (EPI == EPI_ARGMAX) {
+        float best = -INFINITY;
+        int bi = 0x7FFFFFFF;
+        for (int lr = tid; lr < nrows; lr += nthr) {
+            const int r = r0 + lr;
+            const float v = row_sum(lr);
+            if (A.y) A.y[r] = v;
+            if (v > best || (v == best && r < bi)) {
+                best = v;
+                bi = r;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+            const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+            if (ov > best || (ov == best && oi < bi)) {
+                best = ov;
+                bi = oi;
+            }
+        }
+        int* si = reinterpret_cast<int*>(scratch + 16);
+        if (lane == 0) {
+            scratch[warp] = best;
+            si[warp] = bi;
+        }
+        named_barrier_sync(1, nthr);
+        if (tid == 0) {
+            for (int w = 1; w < kConsumerWarps; ++w) {
+                if (scratch[w] > best || (scratch[w] == best && si[w] < bi)) {
+                    best = scratch[w];
+                    bi = si[w];
+                }
+            }
+            A.am_part[blockIdx.x].v = best;
+            A.am_part[blockIdx.x].i = bi;
+        }
+    }
+}
+
+template <typename WT, int EPI>
+void* pick_kernel(int cpt) {
+    switch (cpt) {
+        case 1: return (void*)gemv_kernel<WT, 1, EPI>;
+        case 2: return (void*)gemv_kernel<WT, 2, EPI>;
+        case 3: return (void*)gemv_kernel<WT, 3, EPI>;
+        case 4: return (void*)gemv_kernel<WT, 4, EPI>;
+        case 5: return (void*)gemv_kernel<WT, 5, EPI>;
+        case 6: return (void*)gemv_kernel<WT, 6, EPI>;
+        case 8: return (void*)gemv_kernel<WT, 8, EPI>;
+        default: return nullptr;
+    }
+}
+
+void* pick(int wsize, int epi, int cpt) {
+    if (wsize == 2) {
+        switch (epi) {
+            case EPI_STORE: return pick_kernel<uint16_t, EPI_STORE>(cpt);
+            case EPI_RESID: return pick_kernel<uint16_t, EPI_RESID>(cpt);
+            case EPI_QKV: return pick_kernel<uint16_t, EPI_QKV>(cpt);
+            case EPI_SWIGLU: return pick_kernel<uint16_t, EPI_SWIGLU>(cpt);
+            case EPI_ARGMAX: return pick_kernel<uint16_t, EPI_ARGMAX>(cpt);
+        }
+    } else {
+        switch (epi) {
+            case EPI_STORE: return pick_kernel<float, EPI_STORE>(cpt);
+            case EPI_RESID: return pick_kernel<float, EPI_RESID>(cpt);
+            case EPI_QKV: return pick_kernel<float, EPI_QKV>(cpt);
+            case EPI_SWIGLU: return pick_kernel<float, EPI_SWIGLU>(cpt);
+            case EPI_ARGMAX: return pick_kernel<float, EPI_ARGMAX>(cpt);
+        }
+    }
+    return nullptr;
+}
+
+int cpt_round(int c) {
+    if (c <= 6) return c < 1 ? 1 : c;
+    return c <= 8 ? 8 : -1;
+}
+
+}  // namespace
+
+bool gemv_supported(int K, int wsize) {
+    const int epc = 16 / wsize;
+    if (K <= 0 || K % epc) return false;
+    const int C = K / epc;
+    for (int nseg = 1; nseg <= 8; nseg *= 2)
+        if (C % nseg == 0 && cpt_round((C / nseg + 31) / 32) > 0) return true;
+    return false;
+}
+
+size_t gemv_max_smem() { return kSmemLimit; }
+
+GemvPlan plan_gemv(int rows, int K, int unit, int wsize, int num_sms, int n_vec) {
+    GemvPlan p{};
+    p.rows = rows;
+    p.K = K;
+    p.unit = unit;
+    p.wsize = wsize;
+    p.n_vec = n_vec < 1 ? 1 : n_vec;
+    const int epc = 16 / wsize;
+    const int C = K / epc;
+    // Fewest segments whose per-lane chunk count stays <= 4 (x slice in
+    // registers); otherwise the widest split that fits.
+    p.nseg = -1;
+    for (int nseg = 1; nseg <= 8; nseg *= 2) {
+        if (C % nseg) continue;
+        if ((C / nseg + 31) / 32 <= 4) {
+            p.nseg = nseg;
+            break;
+        }
+    }
+    if (p.nseg < 0) {
+        for (int nseg = 8; nseg >= 1; nseg /= 2)
+            if (C % nseg == 0 && cpt_round((C / nseg + 31) / 32) > 0) {
+                p.nseg = nseg;
+                break;
+            }
+    }
+    if (p.nseg < 0) {
+        p.grid = 0;
+        return p;
+    }
+    p.cpt = cpt_round((C / p.nseg + 31) / 32);
+    p.stage_rows = 2 * (kConsumerWarps / p.nseg);
+    const size_t row_bytes = (size_t)K * wsize;
+    size_t stage_bytes = p.stage_rows * row_bytes;
+    const int units = rows / unit;
+    p.grid = units < num_sms ? units : num_sms;
+    if (p.grid < 1) p.grid = 1;
+    p.max_rows_cta = ((units + p.grid - 1) / p.grid) * unit;
+    // Do not reserve stages a CTA can never fill.
+    int max_stages_needed = (p.max_rows_cta + p.stage_rows - 1) / p.stage_rows;
+    int ns = (int)(kStageBudget / stage_bytes);
+    if (ns < 2) ns = 2;
+    if (ns > 8) ns = 8;
+    if (ns > max_stages_needed) ns = max_stages_needed < 1 ? 1 : max_stages_needed;
+    p.nstages = ns;
+    size_t red_bytes = ((size_t)p.max_rows_cta * p.nseg * 4 + 15) & ~size_t(15);
+    p.smem = (size_t)ns * stage_bytes + red_bytes + 2 * ns * sizeof(uint64_t) + 32 * 4;
+    return p;
+}
+
+cudaError_t gemv_prepare(int /*dev*/) {
+    const int cpts[] = {1, 2, 3, 4, 5, 6, 8};
+    for (int ws : {2, 4})
+        for (int epi = 0; epi <= EPI_ARGMAX; ++epi)
+            for (int c : cpts) {
+                void* k = pick(ws, epi, c);
+                cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     227 * 1024);
+                if (e != cudaSuccess) return e;
+            }
+    return cudaSuccess;
+}
+
+cudaError_t launch_gemv(const GemvPlan& p, const GemvArgs& a, int epi, cudaStream_t s, bool pdl) {
+    void* k = pick(p.wsize, epi, p.cpt);
+    if (!k || p.grid < 1) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.grid, p.n_vec, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = p.smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    void* args[] = {(void*)&p, (void*)&a};
+    return cudaLaunchKernelExC(&cfg, k, args);
+}
+
+}  // namespace vox

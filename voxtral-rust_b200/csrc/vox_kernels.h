@@ -1,0 +1,146 @@
+// vox_kernels.h -- internal interface between the host library (vox_capi.cpp)
+// and the sm_100a kernels (*.cu).  Plain structs of device pointers and
+// sizes; no torch types anywhere.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace vox {
+
+// Ring bookkeeping of one cache layer, mirrored on the device.
+//   len        = len_tokens (kv.rs:6)
+//   start      = physical ring slot of logical token 0
+//   pos_offset = pos_offset (kv.rs:7)
+struct KvState {
+    int32_t len;
+    int32_t start;
+    int64_t pos_offset;
+};
+
+// Per-step inputs of the token loop, resident on the device so that one
+// captured CUDA graph serves every step.
+struct StepState {
+    int64_t pos;       // absolute position of the token being decoded
+    int32_t tok;       // input token id
+    int32_t next_tok;  // argmax written by the last kernel of the step
+    int32_t greedy;    // 1: next_tok becomes tok for the following step
+    int32_t advance;   // 1: pos += 1 at the end of the step
+    int32_t pad[2];
+};
+
+struct ArgmaxPart {
+    float v;
+    int32_t i;
+};
+
+// Error bits written to the context's device error word.
+enum : unsigned {
+    ERR_FULL_WAIT = 1u,      // consumer waited too long for a weight stage
+    ERR_EMPTY_WAIT = 2u,     // producer waited too long for a free stage
+    ERR_DRAIN_WAIT = 4u,     // producer could not drain its copies
+    ERR_POS_RANGE = 8u,      // position beyond the RoPE table
+    ERR_TOKEN_RANGE = 16u,   // token id outside the vocabulary
+};
+
+enum : int { EPI_STORE = 0, EPI_RESID = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
+
+// Launch plan of one weight-streaming GEMV (y = W x, W row-major [rows, K]).
+struct GemvPlan {
+    int rows, K, unit;      // unit: rows per indivisible work item (2 for paired epilogues)
+    int wsize;              // bytes per weight element (2 bf16, 4 f32)
+    int nseg;               // K segments per row (one warp each)
+    int cpt;                // 16-byte chunks per lane per segment (template parameter)
+    int stage_rows;         // rows per pipeline stage
+    int nstages;            // pipeline depth
+    int grid;               // CTAs (<= SM count)
+    int max_rows_cta;       // most rows any CTA owns
+    int n_vec;              // independent input vectors (gridDim.y)
+    size_t smem;            // dynamic shared memory bytes
+};
+
+struct GemvArgs {
+    const void* W;
+    // input vector x [K] (f32), or the bf16 embedding row of step->tok
+    const float* x;
+    long long x_stride;         // between input vectors (gridDim.y)
+    const uint16_t* x_embed;
+    int vocab;
+    const StepState* step;
+    const float* norm_w;        // non-null: RMSNorm(x) with this gain first
+    float eps;
+    float* x_copy_out;          // non-null: CTA 0 stores the raw x here
+    // outputs
+    float* y;
+    long long y_stride;
+    const float* resid;
+    const float* bias;
+    // QKV epilogue: RoPE on q and k, k/v into the ring slot of the new token
+    int q_dim, kv_dim, head_dim;
+    const float* rope_cos;      // [max_pos, head_dim/2]
+    const float* rope_sin;
+    int max_pos;
+    float* k_ring;              // [n_kv, cap, head_dim]
+    float* v_ring;
+    int ring_cap;
+    int kv_window;
+    const KvState* kv_state;    // state before this step's append
+    // O-proj: commit this step's single-token append to the layer state
+    KvState* kv_commit;
+    // LM head
+    ArgmaxPart* am_part;
+    unsigned* err;
+};
+
+struct AttnArgs {
+    const float* q;             // [n_heads, hd]
+    const float* k_ring;        // [n_kv, cap, hd]
+    const float* v_ring;
+    int n_heads, n_kv, hd, cap;
+    int cfg_window;             // DecoderConfig.sliding_window (masking); 0 = none
+    const KvState* st;
+    int pre_append;             // 1: st is the state before a single-token append
+    int kv_window;              // cache window used to evict (pre_append only)
+    int nsplit;
+    float* part;                // [n_kv, nsplit, G, hd + 2]
+    unsigned* tickets;          // [n_kv], zero between launches
+    float* out;                 // [n_heads, hd]
+    float scale;
+    unsigned* err;
+};
+
+// ---- launchers (return the launch error) ----
+GemvPlan plan_gemv(int rows, int K, int unit, int wsize, int num_sms, int n_vec);
+bool gemv_supported(int K, int wsize);
+size_t gemv_max_smem();
+cudaError_t gemv_prepare(int dev);   // raise per-kernel smem limits once per device
+cudaError_t launch_gemv(const GemvPlan& p, const GemvArgs& a, int epi, cudaStream_t s, bool pdl);
+
+int attn_splits_for(int n_kv, int num_sms);
+bool attn_supported(int n_heads, int n_kv, int hd);
+size_t attn_smem_bytes(int n_heads, int n_kv, int hd);
+cudaError_t attn_prepare(int dev);
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
+
+cudaError_t launch_argmax_final(const ArgmaxPart* parts, int n, StepState* step, int32_t* tok_out,
+                                cudaStream_t s, bool pdl);
+cudaError_t launch_kv_scatter(const float* src_k, const float* src_v, float* k_ring, float* v_ring,
+                              int n_kv, int hd, int cap, int slot0, int n_tokens, cudaStream_t s);
+cudaError_t launch_kv_gather(const float* k_ring, const float* v_ring, float* dst_k, float* dst_v,
+                             int n_kv, int hd, int cap, int start, int len, cudaStream_t s);
+// Fill rows of a matrix from the counter-based generator.  Element (r, c) of
+// the logical tensor `tensor_id` ([rows, cols]) lands at
+// dst[(r * row_mul + row_add) * cols + c]; wsize 2 = bf16, 4 = f32.
+cudaError_t launch_gen_matrix(void* dst, int wsize, uint64_t seed, uint64_t tensor_id, float std,
+                              long long rows, long long cols, int row_mul, int row_add,
+                              cudaStream_t s);
+cudaError_t launch_fill_f32(float* dst, float v, long long n, cudaStream_t s);
+cudaError_t launch_rmsnorm_rows(float* out, const float* in, const float* w, long long n_rows,
+                                int dim, float eps, cudaStream_t s);
+cudaError_t launch_rope_table(float* data, const float* cos_t, const float* sin_t, long long seq_len,
+                              int n_heads, int hd, cudaStream_t s);
+cudaError_t launch_silu(float* x, long long n, cudaStream_t s);
+cudaError_t launch_softmax(float* x, long long n, cudaStream_t s);
+cudaError_t launch_add(float* dst, const float* src, long long n, cudaStream_t s);
+
+}  // namespace vox
