@@ -108,6 +108,8 @@ int vox_layer_weights_validate_bf16(const vox_decoder_config* cfg, const vox_lay
 
 /* ---- context and weights ------------------------------------------------- */
 int vox_ctx_create(const vox_decoder_config* cfg, const vox_ctx_options* opt, vox_ctx** out);
+/* Also destroys every cache still attached to the context; their handles
+ * become invalid.  Destroy caches first if you keep handles to them. */
 void vox_ctx_destroy(vox_ctx* ctx);
 /* Copy one layer's weights to the device (caller keeps ownership).  With
  * VOX_WEIGHTS_BF16 the f32 upload rounds matrices to bf16, nearest-even. */

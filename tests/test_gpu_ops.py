@@ -129,7 +129,9 @@ def test_silu_softmax_golden_and_oracle(V, ctx, oracle, ref_tests):
     rng = np.random.default_rng(7)
     x = (rng.standard_normal(9216) * 4).astype(np.float32)
     assert np.max(np.abs(V.silu_inplace(ctx, x) - oracle.silu(x))) < 1e-5
-    assert np.max(np.abs(V.softmax_inplace(ctx, x) - oracle.softmax(x))) < 1e-6
+    ref = oracle.softmax(x)
+    # the GPU sums the 9216 exponentials as a tree, the reference left to right
+    assert np.max(np.abs(V.softmax_inplace(ctx, x) - ref)) < 2e-5 * np.max(ref)
 
 
 def test_add_inplace(V, ctx, oracle):

@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import weakref
 
 import numpy as np
 
@@ -185,9 +186,12 @@ class Context:
         h = VP()
         _check(lib().vox_ctx_create(C.byref(cfg), C.byref(opt), C.byref(h)))
         self.h = h.value
+        self._caches = weakref.WeakSet()
 
     def close(self):
         if getattr(self, "h", None):
+            for kv in list(self._caches):
+                kv.close()
             lib().vox_ctx_destroy(self.h)
             self.h = None
 
@@ -314,11 +318,13 @@ class RollingKvCache:
             _check(lib().vox_kv_create_ex(ctx.h, n_layers, n_kv_heads, head_dim, sliding_window,
                                           capacity, C.byref(h)))
         self.h = h.value
+        ctx._caches.add(self)
 
     def close(self):
-        if getattr(self, "h", None):
+        # A closed context has already freed its caches (vox_ctx_destroy).
+        if getattr(self, "h", None) and getattr(self.ctx, "h", None):
             lib().vox_kv_destroy(self.h)
-            self.h = None
+        self.h = None
 
     def __del__(self):
         try:

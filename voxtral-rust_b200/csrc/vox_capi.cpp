@@ -134,6 +134,7 @@ struct vox_ctx {
     int32_t* h_tok = nullptr;      // pinned
     unsigned* h_err = nullptr;     // pinned
     cudaEvent_t ev[16] = {};
+    std::vector<vox_kv*> caches;   // caches created from this context, still alive
     uint64_t launches = 0;
     GemvPlan p_qkv{}, p_o{}, p_w13{}, p_w2{}, p_head{};
     void* scratch = nullptr;
@@ -536,6 +537,7 @@ void vox_ctx_destroy(vox_ctx* c) {
     if (!c) return;
     cudaSetDevice(c->dev);
     if (c->stream) cudaStreamSynchronize(c->stream);
+    while (!c->caches.empty()) vox_kv_destroy(c->caches.back());
     for (auto& L : c->layers) {
         cudaFree(L.wqkv);
         cudaFree(L.wo);
@@ -842,6 +844,7 @@ int vox_kv_create_ex(vox_ctx* c, size_t n_layers, size_t n_kv, size_t hd, size_t
         return fail(e == cudaErrorMemoryAllocation ? VOX_ERR_OOM : VOX_ERR_CUDA, "cache allocation: %s",
                     cudaGetErrorString(e));
     }
+    c->caches.push_back(kv);
     *out = kv;
     return VOX_OK;
 }
@@ -852,8 +855,14 @@ int vox_kv_create(vox_ctx* c, size_t n_layers, size_t n_kv, size_t hd, size_t wi
 
 void vox_kv_destroy(vox_kv* kv) {
     if (!kv) return;
-    cudaSetDevice(kv->ctx->dev);
-    cudaStreamSynchronize(kv->ctx->stream);
+    vox_ctx* c = kv->ctx;
+    cudaSetDevice(c->dev);
+    cudaStreamSynchronize(c->stream);
+    for (size_t i = 0; i < c->caches.size(); ++i)
+        if (c->caches[i] == kv) {
+            c->caches.erase(c->caches.begin() + (long)i);
+            break;
+        }
     if (kv->step_graph) cudaGraphExecDestroy(kv->step_graph);
     cudaFree(kv->k);
     cudaFree(kv->v);
