@@ -220,6 +220,27 @@ int vox_rope_interleaved_inplace(vox_ctx* ctx, float* data, size_t seq_len, size
 int vox_silu_inplace(vox_ctx* ctx, float* x, size_t n);
 int vox_softmax_inplace(vox_ctx* ctx, float* x, size_t n);
 
+/* ---- allocation-free attention (no counterpart in the reference) ---------------- */
+/* attention_gqa_step for callers that must not allocate device memory (memory
+ * owned by a pool or arena, a fixed memory budget, an allocation-free decode
+ * path).  Same math as vox_attention_gqa_step, but every pointer is DEVICE
+ * memory the caller owns: query [n_heads, head_dim], keys and values
+ * head-major [n_kv_heads, seq_len, head_dim] (this library's cache layout),
+ * out [n_heads, head_dim].  Runs on the calling thread's current device, on
+ * `stream` (a cudaStream_t, 0 = default stream), and returns without
+ * synchronising.  It calls no cudaMalloc/cudaFree: its split-K working memory
+ * is a fixed 1 MiB device array inside the library, reserved on every GPU
+ * that loads it until the process exits.  Shapes whose per-split data
+ * (n_heads * (head_dim + 2) * 4 bytes) cannot fit are rejected with
+ * VOX_ERR_UNSUPPORTED.  The first call on a device performs a one-time
+ * set-up (looks up the array's device address, sets a kernel attribute), so
+ * make that first call before any stream capture.  All calls on a device
+ * share the array: calls that can overlap on the GPU (other streams, other
+ * threads) race and must be serialised by the caller. */
+int vox_attention_gqa_step_noalloc(const float* d_query, const float* d_keys,
+                                   const float* d_values, const vox_attention_shape* shape,
+                                   float* d_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -128,6 +128,7 @@ _SIGS = {
     "vox_rope_interleaved_inplace": ([VP, F32P, SZ, SZ, SZ, SZ, C.c_float], C.c_int),
     "vox_silu_inplace": ([VP, F32P, SZ], C.c_int),
     "vox_softmax_inplace": ([VP, F32P, SZ], C.c_int),
+    "vox_attention_gqa_step_noalloc": ([VP, VP, VP, C.POINTER(AttentionShape), VP, VP], C.c_int),
 }
 
 

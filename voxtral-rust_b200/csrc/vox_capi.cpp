@@ -106,6 +106,8 @@ struct LayerDev {
 
 }  // namespace
 
+int vox::report_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
 struct vox_ctx {
     vox_decoder_config cfg{};
     vox_ctx_options opt{};

@@ -109,6 +109,9 @@ struct AttnArgs {
     unsigned* err;
 };
 
+// Record a failure for vox_last_error() and return `code` (host side).
+int report_error(int code, const char* msg);
+
 // ---- launchers (return the launch error) ----
 GemvPlan plan_gemv(int rows, int K, int unit, int wsize, int num_sms, int n_vec);
 bool gemv_supported(int K, int wsize);
