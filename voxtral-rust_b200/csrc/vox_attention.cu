@@ -9,11 +9,15 @@
 // B200 layout: one CTA per (kv head, split of the token range).  The CTA
 // serves all G query heads of its kv head, so each K/V row is read from HBM
 // once per group (the reference reads it G times).  Tiles of 32 tokens are
-// staged in shared memory; the CTA keeps an online-softmax state (running
-// max m, running sum l, unnormalised accumulator) per head.  Split results
-// go to a scratch buffer and the last CTA of each kv head (atomic ticket)
-// merges them with log-sum-exp weights in a fixed split order, so results
-// are run-to-run deterministic.
+// double-buffered in shared memory with cp.async; the CTA keeps an
+// online-softmax state (running max m, running sum l, unnormalised
+// accumulator) per head.  The number of active splits follows the live
+// length at run time (at least one tile each), so one captured launch serves
+// every step.  Split results go to a scratch buffer and the last CTA of each
+// kv head (atomic ticket) merges them: per-split weights exp(m_s - M) / L are
+// computed once per head, then every output is a dot product over the splits
+// with independent loads.  Merge order is fixed, so results are run-to-run
+// deterministic.
 //
 // The ring is head-major [n_kv, cap, hd]: logical token t of a layer lives
 // in slot (start + t) % cap, so sliding-window eviction never moves data.
@@ -28,14 +32,14 @@ namespace {
 
 constexpr int kAttnThreads = 128;
 constexpr int kTile = 32;
-constexpr int kMaxAcc = 4;   // accumulator vectors per thread (G*hd/VEC <= 512)
+constexpr int kMaxAcc = 4;      // accumulator vectors per thread (G*hd/VEC <= 512)
+constexpr int kMaxSplits = 64;  // merge weights kept in shared memory
 
 template <int VEC>
 struct VecT;
 template <>
 struct VecT<1> {
     using T = float;
-    __device__ static __forceinline__ float dot(const float& a, const float& b) { return a * b; }
 };
 template <>
 struct VecT<4> {
@@ -49,9 +53,7 @@ __device__ __forceinline__ float fdot(float acc, const float4& a, const float4& 
     acc = fmaf(a.w, b.w, acc);
     return acc;
 }
-__device__ __forceinline__ float fdot(float acc, const float& a, const float& b) {
-    return fmaf(a, b, acc);
-}
+__device__ __forceinline__ float fdot(float acc, const float& a, const float& b) { return fmaf(a, b, acc); }
 __device__ __forceinline__ void faxpy(float4& acc, float p, const float4& v) {
     acc.x = fmaf(p, v.x, acc.x);
     acc.y = fmaf(p, v.y, acc.y);
@@ -73,6 +75,44 @@ __device__ __forceinline__ float fget(const float4& a, int i) {
 }
 __device__ __forceinline__ float fget(const float& a, int) { return a; }
 
+// 16-byte global -> shared copy; zero-fills when !valid.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+    const int n = valid ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(n)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Stage tokens [t0, t0 + kTile) ∩ [.., t_end) of one kv head into smem.
+template <int VEC>
+__device__ __forceinline__ void load_tile(float* ks, float* vs, const float* kr, const float* vr, int t0,
+                                          int t_end, int start, int cap, int hd, int ldk) {
+    using T = typename VecT<VEC>::T;
+    const int hdv = hd / VEC;
+    for (int u = threadIdx.x; u < kTile * hdv; u += kAttnThreads) {
+        const int tt = u / hdv, dv = u - tt * hdv;
+        const int t = t0 + tt;
+        const bool valid = t < t_end;
+        int slot = start + (valid ? t : t0);
+        if (slot >= cap) slot -= cap;
+        const float* sk = kr + (size_t)slot * hd + dv * VEC;
+        const float* sv = vr + (size_t)slot * hd + dv * VEC;
+        float* dk = ks + tt * ldk + dv * VEC;
+        float* dv_ = vs + tt * ldk + dv * VEC;
+        if constexpr (VEC == 4) {
+            cp_async16(dk, sk, valid);
+            cp_async16(dv_, sv, valid);
+        } else {
+            *dk = valid ? *sk : 0.f;
+            *dv_ = valid ? *sv : 0.f;
+        }
+    }
+}
+
 template <int VEC>
 __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs A) {
     using T = typename VecT<VEC>::T;
@@ -85,15 +125,17 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
     const int hdv = hd / VEC;          // vectors per row
     const int pad = VEC == 4 ? 4 : 1;  // row padding (floats) against bank conflicts
     const int ldk = hd + pad;
+    const int tile_f = kTile * ldk;
 
     float* q_s = sm;                          // [G, hd]
-    float* k_s = q_s + G * hd;                // [kTile, ldk]
-    float* v_s = k_s + kTile * ldk;           // [kTile, ldk]
-    float* p_s = v_s + kTile * ldk;           // [G, kTile]
+    float* kbuf = q_s + G * hd;               // [2][kTile, ldk]
+    float* vbuf = kbuf + 2 * tile_f;          // [2][kTile, ldk]
+    float* p_s = vbuf + 2 * tile_f;           // [G, kTile]
     float* m_s = p_s + G * kTile;             // [G] running max
     float* l_s = m_s + G;                     // [G] running sum
     float* a_s = l_s + G;                     // [G] rescale factor of this tile
-    int* flag_s = reinterpret_cast<int*>(a_s + G);
+    float* w_s = a_s + G;                     // [G, kMaxSplits] merge weights
+    int* flag_s = reinterpret_cast<int*>(w_s + G * kMaxSplits);
 
     pdl_allow_dependents();
     pdl_wait_prior_grids();
@@ -105,8 +147,22 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
     const int n_live = len - mask_start;
     int per = (n_live + A.nsplit - 1) / A.nsplit;
     per = ((per + kTile - 1) / kTile) * kTile;
+    if (per < kTile) per = kTile;
+    const int n_active = (n_live + per - 1) / per;
+    float* out_h = A.out + (size_t)h * G * hd;
+    if (n_active == 0) {  // empty cache: the reference returns zeros
+        if (split == 0)
+            for (int i = tid; i < G * hd; i += kAttnThreads) out_h[i] = 0.f;
+        return;
+    }
+    if (split >= n_active) return;
     const int t_begin = mask_start + split * per;
     const int t_end = min(len, t_begin + per);
+
+    const float* kr = A.k_ring + (size_t)h * A.cap * hd;
+    const float* vr = A.v_ring + (size_t)h * A.cap * hd;
+    load_tile<VEC>(kbuf, vbuf, kr, vr, t_begin, t_end, st.start, A.cap, hd, ldk);
+    if constexpr (VEC == 4) cp_async_commit();
 
     for (int i = tid; i < G * hd; i += kAttnThreads) q_s[i] = A.q[(size_t)h * G * hd + i];
     if (tid < G) {
@@ -118,29 +174,23 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
     for (int j = 0; j < kMaxAcc; ++j) fzero(acc[j]);
     const int n_out = G * hdv;
 
-    const float* kr = A.k_ring + (size_t)h * A.cap * hd;
-    const float* vr = A.v_ring + (size_t)h * A.cap * hd;
-
-    for (int t0 = t_begin; t0 < t_end; t0 += kTile) {
-        __syncthreads();
-        // Stage K and V rows of this tile (zero beyond t_end).
-        for (int u = tid; u < kTile * hdv; u += kAttnThreads) {
-            const int tt = u / hdv, dv = u - tt * hdv;
-            const int t = t0 + tt;
-            T kv_k, kv_v;
-            if (t < t_end) {
-                int slot = st.start + t;
-                if (slot >= A.cap) slot -= A.cap;
-                kv_k = *reinterpret_cast<const T*>(kr + (size_t)slot * hd + dv * VEC);
-                kv_v = *reinterpret_cast<const T*>(vr + (size_t)slot * hd + dv * VEC);
-            } else {
-                fzero(kv_k);
-                fzero(kv_v);
-            }
-            *reinterpret_cast<T*>(k_s + tt * ldk + dv * VEC) = kv_k;
-            *reinterpret_cast<T*>(v_s + tt * ldk + dv * VEC) = kv_v;
+    int buf = 0;
+    for (int t0 = t_begin; t0 < t_end; t0 += kTile, buf ^= 1) {
+        const bool has_next = t0 + kTile < t_end;
+        if (has_next) {
+            load_tile<VEC>(kbuf + (buf ^ 1) * tile_f, vbuf + (buf ^ 1) * tile_f, kr, vr, t0 + kTile, t_end,
+                           st.start, A.cap, hd, ldk);
+            if constexpr (VEC == 4) cp_async_commit();
+        }
+        if constexpr (VEC == 4) {
+            if (has_next)
+                cp_async_wait<1>();
+            else
+                cp_async_wait<0>();
         }
         __syncthreads();
+        const float* k_s = kbuf + buf * tile_f;
+        const float* v_s = vbuf + buf * tile_f;
         // Scores: (g, t) pairs; ops.rs:108-113 dot * scale.
         for (int idx = tid; idx < G * kTile; idx += kAttnThreads) {
             const int g = idx / kTile, tt = idx - g * kTile;
@@ -184,14 +234,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
                 const int g = o / hdv, dv = o - g * hdv;
                 fscale(acc[j], a_s[g]);
                 const float* pg = p_s + g * kTile;
-                for (int tt = 0; tt < kTile; ++tt) {
-                    const float p = pg[tt];
-                    faxpy(acc[j], p, *reinterpret_cast<const T*>(v_s + tt * ldk + dv * VEC));
-                }
+#pragma unroll 8
+                for (int tt = 0; tt < kTile; ++tt)
+                    faxpy(acc[j], pg[tt], *reinterpret_cast<const T*>(v_s + tt * ldk + dv * VEC));
             }
         }
+        __syncthreads();  // the next iteration refills the other buffer of this pair
     }
-    __syncthreads();
 
     // Split partial: [G][hd] accumulator, then m, l per head.
     const int G2 = hd + 2;
@@ -213,28 +262,60 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
     __syncthreads();
     if (tid == 0) {
         const unsigned ticket = atomicAdd(&A.tickets[h], 1u);
-        flag_s[0] = (ticket == (unsigned)(A.nsplit - 1)) ? 1 : 0;
+        flag_s[0] = (ticket == (unsigned)(n_active - 1)) ? 1 : 0;
     }
     __syncthreads();
     if (!flag_s[0]) return;
     __threadfence();
 
-    // Last CTA of this kv head: merge the splits in index order.
+    // Last CTA of this kv head: merge weights w_s = exp(m_s - M) / L once per head ...
     const float* base = A.part + (size_t)h * A.nsplit * G * G2;
+    for (int g = warp; g < G; g += kAttnThreads / 32) {
+        float ms[2], ls[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int s = lane + 32 * r;
+            ms[r] = s < n_active ? __ldcg(base + ((size_t)s * G + g) * G2 + hd) : -INFINITY;
+            ls[r] = s < n_active ? __ldcg(base + ((size_t)s * G + g) * G2 + hd + 1) : 0.f;
+        }
+        float M = fmaxf(ms[0], ms[1]);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
+        float w[2], L = 0.f;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            w[r] = ms[r] == -INFINITY ? 0.f : expf(ms[r] - M);
+            L = fmaf(ls[r], w[r], L);
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xFFFFFFFFu, L, o);
+        const float invL = L > 0.f ? 1.0f / L : 0.f;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int s = lane + 32 * r;
+            if (s < n_active) w_s[g * kMaxSplits + s] = w[r] * invL;
+        }
+    }
+    __syncthreads();
+    // ... then each output is a weighted sum over the splits (independent loads).
     for (int o = tid; o < G * hd; o += kAttnThreads) {
         const int g = o / hd, d = o - g * hd;
-        float M = -INFINITY;
-        for (int s = 0; s < A.nsplit; ++s) M = fmaxf(M, __ldcg(base + ((size_t)s * G + g) * G2 + hd));
-        float L = 0.f, O = 0.f;
-        for (int s = 0; s < A.nsplit; ++s) {
-            const float* ps = base + ((size_t)s * G + g) * G2;
-            const float ms = __ldcg(ps + hd);
-            if (ms == -INFINITY) continue;
-            const float w = expf(ms - M);
-            L = fmaf(__ldcg(ps + hd + 1), w, L);
-            O = fmaf(__ldcg(ps + d), w, O);
+        const float* pd = base + (size_t)g * G2 + d;
+        const float* wg = w_s + g * kMaxSplits;
+        float O = 0.f;
+        int s = 0;
+        for (; s + 4 <= n_active; s += 4) {
+            const float x0 = __ldcg(pd + (size_t)(s + 0) * G * G2);
+            const float x1 = __ldcg(pd + (size_t)(s + 1) * G * G2);
+            const float x2 = __ldcg(pd + (size_t)(s + 2) * G * G2);
+            const float x3 = __ldcg(pd + (size_t)(s + 3) * G * G2);
+            O = fmaf(x0, wg[s], O);
+            O = fmaf(x1, wg[s + 1], O);
+            O = fmaf(x2, wg[s + 2], O);
+            O = fmaf(x3, wg[s + 3], O);
         }
-        A.out[((size_t)h * G + g) * hd + d] = (L > 0.f) ? O / L : 0.f;
+        for (; s < n_active; ++s) O = fmaf(__ldcg(pd + (size_t)s * G * G2), wg[s], O);
+        out_h[(size_t)g * hd + d] = O;
     }
     if (tid == 0) A.tickets[h] = 0u;
 }
@@ -252,14 +333,15 @@ bool attn_supported(int n_heads, int n_kv, int hd) {
 size_t attn_smem_bytes(int n_heads, int n_kv, int hd) {
     const int G = n_heads / n_kv;
     const int pad = (hd % 4 == 0) ? 4 : 1;
-    const size_t floats = (size_t)G * hd + 2 * kTile * (hd + pad) + (size_t)G * kTile + 3 * G + 4;
+    const size_t floats = (size_t)G * hd + 4 * kTile * (hd + pad) + (size_t)G * kTile + 3 * G +
+                          (size_t)G * kMaxSplits + 4;
     return floats * 4;
 }
 
 int attn_splits_for(int n_kv, int num_sms) {
     int s = (2 * num_sms + n_kv - 1) / n_kv;
     if (s < 1) s = 1;
-    if (s > 64) s = 64;
+    if (s > kMaxSplits) s = kMaxSplits;
     return s;
 }
 

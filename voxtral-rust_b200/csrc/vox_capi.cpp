@@ -10,6 +10,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -612,6 +613,11 @@ int vox_ctx_create(const vox_decoder_config* cfg, const vox_ctx_options* opt, vo
                              "%s failed: %s", #expr, cudaGetErrorString(e_)));                \
     } while (0)
 
+    if (const char* t = getenv("VOX_GEMV_TUNE")) {  // "budget_kb,ctas_per_sm,stage_mult,warps"
+        int kb = 0, ctas = 0, mult = 0, warps = 8;
+        if (sscanf(t, "%d,%d,%d,%d", &kb, &ctas, &mult, &warps) >= 3)
+            gemv_set_tuning((size_t)kb * 1024, ctas, mult, warps);
+    }
     CTX_TRY(gemv_prepare(c->dev));
     CTX_TRY(attn_prepare(c->dev));
     CTX_TRY(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));

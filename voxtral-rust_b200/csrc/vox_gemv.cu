@@ -32,10 +32,17 @@ namespace vox {
 
 namespace {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr size_t kStageBudget = 108 * 1024;   // weight ring bytes per CTA
-constexpr size_t kSmemLimit = 113 * 1024;     // two CTAs per SM
+// Consumer warps per CTA (NW, a template parameter): 8 (two CTAs per SM) or
+// 16 (one CTA per SM).  Plus one producer warp.
+// Launch shape of the weight stream: ring bytes per CTA, CTAs per SM, and
+// row pairs per warp per stage.
+struct GemvTuning {
+    size_t stage_budget = 160 * 1024;
+    int ctas_per_sm = 1;
+    int stage_mult = 1;
+    int warps = 16;
+};
+GemvTuning g_tune;
 
 template <typename WT>
 struct Elem;
@@ -78,10 +85,12 @@ __device__ __forceinline__ float swiglu(float g, float u) {
     return __fmul_rn(s, u);
 }
 
-template <typename WT, int CPT, int EPI>
-__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvPlan P, const GemvArgs A) {
+template <typename WT, int CPT, int EPI, int NW>
+__global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
+    gemv_kernel(const GemvPlan P, const GemvArgs A) {
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int EPC = Elem<WT>::kPerChunk;
+    constexpr int kConsumerWarps = NW;
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -153,14 +162,29 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvPlan P, con
     }
 
     // ---------------- consumers ----------------
-    pdl_wait_prior_grids();
-
     const int nseg = P.nseg;
     const int seg = warp % nseg;
-    const int tp = warp / nseg;               // row pair inside a stage
+    const int tp = warp / nseg;               // first row pair of this warp inside a stage
+    const int pair_step = kConsumerWarps / nseg;
     const int segc = C / nseg;
     const int c0 = seg * segc;
     const int vec = blockIdx.y;
+
+    // RMSNorm gains of this warp's K slice do not depend on earlier kernels:
+    // fetch them before waiting (small slices only, to bound registers).
+    constexpr bool kEarlyGain = CPT <= 4;
+    float gr[kEarlyGain ? CPT : 1][EPC];
+    if constexpr (kEarlyGain) {
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) {
+            const int cc = lane + 32 * i;
+#pragma unroll
+            for (int e = 0; e < EPC; ++e)
+                gr[i][e] = (A.norm_w && cc < segc) ? A.norm_w[(c0 + cc) * EPC + e] : 0.0f;
+        }
+    }
+
+    pdl_wait_prior_grids();
 
     // Input vector: x, or the embedding row of the step's token.
     const float* x = A.x ? A.x + (long long)vec * A.x_stride : nullptr;
@@ -174,27 +198,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvPlan P, con
         xe = A.x_embed + (size_t)tok * K;
     }
 
-    float inv_rms = 1.0f;
-    if (A.norm_w || (A.x_copy_out && blockIdx.x == 0)) {
-        float ss = 0.0f;
-        for (int k = tid; k < K; k += kConsumerWarps * 32) {
-            float v = xe ? bf16_bits_to_f32(xe[k]) : x[k];
-            if (A.x_copy_out && blockIdx.x == 0) A.x_copy_out[k] = v;
-            ss = fmaf(v, v, ss);
-        }
-        if (A.norm_w) {
-            ss = warp_sum(ss);
-            if (lane == 0) scratch[warp] = ss;
-            named_barrier_sync(1, kConsumerWarps * 32);
-            float tot = 0.0f;
-#pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) tot += scratch[w];
-            // math.rs:22: inv_rms = 1 / sqrt(sq_sum / dim + eps)
-            inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), A.eps)));
-        }
-    }
-
-    // This warp's slice of x in registers (normalised when asked).
+    // This warp's slice of x in registers: one round trip to L2.
     float xr[CPT][EPC];
 #pragma unroll
     for (int i = 0; i < CPT; ++i) {
@@ -203,11 +207,59 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvPlan P, con
         for (int e = 0; e < EPC; ++e) xr[i][e] = 0.0f;
         if (cc < segc) {
             const int k0 = (c0 + cc) * EPC;
+            if (xe) {
+                uint32_t ws[4];
+                if constexpr (EPC == 8) {
+                    const uint4 w = *reinterpret_cast<const uint4*>(xe + k0);
+                    ws[0] = w.x; ws[1] = w.y; ws[2] = w.z; ws[3] = w.w;
+                } else {
+                    const uint2 w = *reinterpret_cast<const uint2*>(xe + k0);
+                    ws[0] = w.x; ws[1] = w.y; ws[2] = 0u; ws[3] = 0u;
+                }
+#pragma unroll
+                for (int e = 0; e < EPC; ++e) xr[i][e] = (e & 1) ? bf16_hi(ws[e >> 1]) : bf16_lo(ws[e >> 1]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < EPC; e += 4) {
+                    const float4 v = *reinterpret_cast<const float4*>(x + k0 + e);
+                    xr[i][e] = v.x;
+                    xr[i][e + 1] = v.y;
+                    xr[i][e + 2] = v.z;
+                    xr[i][e + 3] = v.w;
+                }
+            }
+            if (A.x_copy_out && blockIdx.x == 0 && tp == 0) {
+#pragma unroll
+                for (int e = 0; e < EPC; ++e) A.x_copy_out[k0 + e] = xr[i][e];
+            }
+        }
+    }
+
+    if (A.norm_w) {
+        // Warps 0..nseg-1 (tp == 0) hold every element of x exactly once.
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < CPT; ++i)
+#pragma unroll
+            for (int e = 0; e < EPC; ++e) ss = fmaf(xr[i][e], xr[i][e], ss);
+        ss = warp_sum(ss);
+        if (lane == 0 && tp == 0) scratch[warp] = ss;
+        named_barrier_sync(1, kConsumerWarps * 32);
+        float tot = 0.0f;
+        for (int w = 0; w < nseg; ++w) tot += scratch[w];
+        // math.rs:22-24: inv_rms = 1 / sqrt(sq_sum / dim + eps); out = x * inv_rms * w
+        const float inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), A.eps)));
+#pragma unroll
+        for (int i = 0; i < CPT; ++i) {
+            const int cc = lane + 32 * i;
 #pragma unroll
             for (int e = 0; e < EPC; ++e) {
-                float v = xe ? bf16_bits_to_f32(xe[k0 + e]) : x[k0 + e];
-                if (A.norm_w) v = __fmul_rn(__fmul_rn(v, inv_rms), A.norm_w[k0 + e]);
-                xr[i][e] = v;
+                float g;
+                if constexpr (kEarlyGain)
+                    g = gr[i][e];
+                else
+                    g = cc < segc ? A.norm_w[(c0 + cc) * EPC + e] : 0.0f;
+                xr[i][e] = __fmul_rn(__fmul_rn(xr[i][e], inv_rms), g);
             }
         }
     }
@@ -220,10 +272,11 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvPlan P, con
             ok = false;
             break;
         }
-        const int ra = s * P.stage_rows + 2 * tp;   // local row index
+        for (int pr = tp; pr < P.stage_rows / 2; pr += pair_step) {
+        const int ra = s * P.stage_rows + 2 * pr;   // local row index
         if (ra < nrows) {
             const bool has_b = ra + 1 < nrows;
-            const unsigned char* rowa = stage_base + (size_t)buf * stage_bytes + (size_t)(2 * tp) * row_bytes;
+            const unsigned char* rowa = stage_base + (size_t)buf * stage_bytes + (size_t)(2 * pr) * row_bytes;
             const unsigned char* rowb = rowa + row_bytes;
             float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
 #pragma unroll
@@ -244,6 +297,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvPlan P, con
                 red[ra * nseg + seg] = sa;
                 if (has_b) red[(ra + 1) * nseg + seg] = sb;
             }
+        }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty_bar[buf]);
@@ -357,39 +411,36 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const GemvPlan P, con
     }
 }
 
-template <typename WT, int EPI>
+template <typename WT, int EPI, int NW>
 void* pick_kernel(int cpt) {
     switch (cpt) {
-        case 1: return (void*)gemv_kernel<WT, 1, EPI>;
-        case 2: return (void*)gemv_kernel<WT, 2, EPI>;
-        case 3: return (void*)gemv_kernel<WT, 3, EPI>;
-        case 4: return (void*)gemv_kernel<WT, 4, EPI>;
-        case 5: return (void*)gemv_kernel<WT, 5, EPI>;
-        case 6: return (void*)gemv_kernel<WT, 6, EPI>;
-        case 8: return (void*)gemv_kernel<WT, 8, EPI>;
+        case 1: return (void*)gemv_kernel<WT, 1, EPI, NW>;
+        case 2: return (void*)gemv_kernel<WT, 2, EPI, NW>;
+        case 3: return (void*)gemv_kernel<WT, 3, EPI, NW>;
+        case 4: return (void*)gemv_kernel<WT, 4, EPI, NW>;
+        case 5: return (void*)gemv_kernel<WT, 5, EPI, NW>;
+        case 6: return (void*)gemv_kernel<WT, 6, EPI, NW>;
+        case 8: return (void*)gemv_kernel<WT, 8, EPI, NW>;
         default: return nullptr;
     }
 }
 
-void* pick(int wsize, int epi, int cpt) {
-    if (wsize == 2) {
-        switch (epi) {
-            case EPI_STORE: return pick_kernel<uint16_t, EPI_STORE>(cpt);
-            case EPI_RESID: return pick_kernel<uint16_t, EPI_RESID>(cpt);
-            case EPI_QKV: return pick_kernel<uint16_t, EPI_QKV>(cpt);
-            case EPI_SWIGLU: return pick_kernel<uint16_t, EPI_SWIGLU>(cpt);
-            case EPI_ARGMAX: return pick_kernel<uint16_t, EPI_ARGMAX>(cpt);
-        }
-    } else {
-        switch (epi) {
-            case EPI_STORE: return pick_kernel<float, EPI_STORE>(cpt);
-            case EPI_RESID: return pick_kernel<float, EPI_RESID>(cpt);
-            case EPI_QKV: return pick_kernel<float, EPI_QKV>(cpt);
-            case EPI_SWIGLU: return pick_kernel<float, EPI_SWIGLU>(cpt);
-            case EPI_ARGMAX: return pick_kernel<float, EPI_ARGMAX>(cpt);
-        }
+template <typename WT, int NW>
+void* pick_epi(int epi, int cpt) {
+    switch (epi) {
+        case EPI_STORE: return pick_kernel<WT, EPI_STORE, NW>(cpt);
+        case EPI_RESID: return pick_kernel<WT, EPI_RESID, NW>(cpt);
+        case EPI_QKV: return pick_kernel<WT, EPI_QKV, NW>(cpt);
+        case EPI_SWIGLU: return pick_kernel<WT, EPI_SWIGLU, NW>(cpt);
+        case EPI_ARGMAX: return pick_kernel<WT, EPI_ARGMAX, NW>(cpt);
     }
     return nullptr;
+}
+
+// bf16 weights have both warp counts; the f32-weight path uses 8.
+void* pick(int wsize, int epi, int cpt, int nw) {
+    if (wsize == 2) return nw == 16 ? pick_epi<uint16_t, 16>(epi, cpt) : pick_epi<uint16_t, 8>(epi, cpt);
+    return nw == 8 ? pick_epi<float, 8>(epi, cpt) : nullptr;
 }
 
 int cpt_round(int c) {
@@ -408,7 +459,14 @@ bool gemv_supported(int K, int wsize) {
     return false;
 }
 
-size_t gemv_max_smem() { return kSmemLimit; }
+size_t gemv_max_smem() { return g_tune.stage_budget > 108 * 1024 ? 227 * 1024 - 256 : 113 * 1024; }
+
+void gemv_set_tuning(size_t stage_budget, int ctas_per_sm, int stage_mult, int warps) {
+    if (warps == 8 || warps == 16) g_tune.warps = warps;
+    if (stage_budget >= 16 * 1024) g_tune.stage_budget = stage_budget;
+    if (ctas_per_sm >= 1) g_tune.ctas_per_sm = ctas_per_sm;
+    if (stage_mult >= 1) g_tune.stage_mult = stage_mult;
+}
 
 GemvPlan plan_gemv(int rows, int K, int unit, int wsize, int num_sms, int n_vec) {
     GemvPlan p{};
@@ -441,18 +499,20 @@ GemvPlan plan_gemv(int rows, int K, int unit, int wsize, int num_sms, int n_vec)
         return p;
     }
     p.cpt = cpt_round((C / p.nseg + 31) / 32);
-    p.stage_rows = 2 * (kConsumerWarps / p.nseg);
+    p.nw = wsize == 2 ? g_tune.warps : 8;
+    p.stage_rows = 2 * (p.nw / p.nseg) * g_tune.stage_mult;
     const size_t row_bytes = (size_t)K * wsize;
     size_t stage_bytes = p.stage_rows * row_bytes;
     const int units = rows / unit;
-    p.grid = units < num_sms ? units : num_sms;
+    const int max_grid = num_sms * g_tune.ctas_per_sm;
+    p.grid = units < max_grid ? units : max_grid;
     if (p.grid < 1) p.grid = 1;
     p.max_rows_cta = ((units + p.grid - 1) / p.grid) * unit;
     // Do not reserve stages a CTA can never fill.
     int max_stages_needed = (p.max_rows_cta + p.stage_rows - 1) / p.stage_rows;
-    int ns = (int)(kStageBudget / stage_bytes);
+    int ns = (int)(g_tune.stage_budget / stage_bytes);
     if (ns < 2) ns = 2;
-    if (ns > 8) ns = 8;
+    if (ns > 16) ns = 16;
     if (ns > max_stages_needed) ns = max_stages_needed < 1 ? 1 : max_stages_needed;
     p.nstages = ns;
     size_t red_bytes = ((size_t)p.max_rows_cta * p.nseg * 4 + 15) & ~size_t(15);
@@ -465,20 +525,23 @@ cudaError_t gemv_prepare(int /*dev*/) {
     for (int ws : {2, 4})
         for (int epi = 0; epi <= EPI_ARGMAX; ++epi)
             for (int c : cpts) {
-                void* k = pick(ws, epi, c);
+                for (int nw : {8, 16}) {
+                void* k = pick(ws, epi, c, nw);
+                if (!k) continue;
                 cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                      227 * 1024);
                 if (e != cudaSuccess) return e;
+                }
             }
     return cudaSuccess;
 }
 
 cudaError_t launch_gemv(const GemvPlan& p, const GemvArgs& a, int epi, cudaStream_t s, bool pdl) {
-    void* k = pick(p.wsize, epi, p.cpt);
+    void* k = pick(p.wsize, epi, p.cpt, p.nw);
     if (!k || p.grid < 1) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.grid, p.n_vec, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3((p.nw + 1) * 32, 1, 1);
     cfg.dynamicSmemBytes = p.smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];

@@ -53,7 +53,8 @@ struct GemvPlan {
     int cpt;                // 16-byte chunks per lane per segment (template parameter)
     int stage_rows;         // rows per pipeline stage
     int nstages;            // pipeline depth
-    int grid;               // CTAs (<= SM count)
+    int nw;                 // consumer warps per CTA (8 or 16)
+    int grid;               // CTAs
     int max_rows_cta;       // most rows any CTA owns
     int n_vec;              // independent input vectors (gridDim.y)
     size_t smem;            // dynamic shared memory bytes
@@ -116,6 +117,7 @@ int report_error(int code, const char* msg);
 GemvPlan plan_gemv(int rows, int K, int unit, int wsize, int num_sms, int n_vec);
 bool gemv_supported(int K, int wsize);
 size_t gemv_max_smem();
+void gemv_set_tuning(size_t stage_budget, int ctas_per_sm, int stage_mult, int warps);
 cudaError_t gemv_prepare(int dev);   // raise per-kernel smem limits once per device
 cudaError_t launch_gemv(const GemvPlan& p, const GemvArgs& a, int epi, cudaStream_t s, bool pdl);
 
