@@ -66,7 +66,16 @@ typedef struct vox_ctx_options {
     size_t vocab;             /* vocabulary for the token loop; 0 = no embedding / LM head */
     size_t max_positions;     /* RoPE table length; positions must stay below it (default 32768) */
     int weight_dtype;         /* vox_weight_dtype */
+    int step_mode;            /* vox_step_mode: how vox_model_* run a token step */
 } vox_ctx_options;
+
+/* How vox_model_step/_prefill/_generate run a token step; both are captured
+ * in a CUDA graph.  VOX_STEP_LAYERS: five kernels per layer (QKV+RoPE+ring
+ * append, attention, o-proj, w1|w3+SwiGLU, w2) plus LM head and argmax.
+ * VOX_STEP_PERSISTENT: the whole step as one cooperative persistent kernel
+ * (bf16 weights only; falls back to VOX_STEP_LAYERS when the shapes do not
+ * fit it).  VOX_STEP_AUTO picks the faster one on B200, currently LAYERS. */
+typedef enum vox_step_mode { VOX_STEP_AUTO = 0, VOX_STEP_LAYERS = 1, VOX_STEP_PERSISTENT = 2 } vox_step_mode;
 
 typedef struct vox_f32_slice { const float* ptr; size_t len; } vox_f32_slice;
 typedef struct vox_bf16_slice { const uint16_t* ptr; size_t len; } vox_bf16_slice;

@@ -17,8 +17,9 @@ def V():
     return vox()
 
 
-def make_ctx(V, c, n_layers, vocab, seed=0, weight_dtype=0):
-    ctx = V.Context(V.DecoderConfig(**c), n_layers=n_layers, vocab=vocab, weight_dtype=weight_dtype)
+def make_ctx(V, c, n_layers, vocab, seed=0, weight_dtype=0, step_mode=0):
+    ctx = V.Context(V.DecoderConfig(**c), n_layers=n_layers, vocab=vocab, weight_dtype=weight_dtype,
+                    step_mode=step_mode)
     ctx.init_random(seed, 0.02)
     return ctx
 
@@ -50,7 +51,7 @@ def test_generator_full_layer_bit_exact(V, oracle):
             assert np.array_equal(ctx.download_matrix(0, n), ref), n
 
 
-def teacher_forced(V, oracle, c, n_layers, vocab, n_steps, window=None, seed=0, prefill=0):
+def teacher_forced(V, oracle, c, n_layers, vocab, n_steps, window=None, seed=0, prefill=0, step_mode=0):
     """Run n_steps teacher-forced steps on both sides; returns (max diff, margins)."""
     if window is not None:
         c = dict(c, sliding_window=window)
@@ -58,7 +59,7 @@ def teacher_forced(V, oracle, c, n_layers, vocab, n_steps, window=None, seed=0, 
     m = oracle_model(oracle, c, n_layers, vocab, seed)
     oc = oracle.RollingKvCache(n_layers, c["n_kv_heads"], c["head_dim"], c["sliding_window"])
     worst, margins = 0.0, []
-    with make_ctx(V, c, n_layers, vocab, seed) as ctx:
+    with make_ctx(V, c, n_layers, vocab, seed, step_mode=step_mode) as ctx:
         kv = V.RollingKvCache(ctx, n_layers, c["n_kv_heads"], c["head_dim"], c["sliding_window"])
         if prefill:
             ctx.model_prefill(kv, ids[:prefill], 0)
@@ -79,20 +80,27 @@ def teacher_forced(V, oracle, c, n_layers, vocab, n_steps, window=None, seed=0, 
     return worst, margins
 
 
-def test_mini_model_with_eviction(V, oracle):
-    worst, _ = teacher_forced(V, oracle, MINI, 3, 1000, 40, prefill=5)
+# step_mode 1: the chain of per-layer kernels (the default); 2: one persistent kernel per token.
+MODES = [1, 2]
+
+
+@pytest.mark.parametrize("step_mode", MODES)
+def test_mini_model_with_eviction(V, oracle, step_mode):
+    worst, _ = teacher_forced(V, oracle, MINI, 3, 1000, 40, prefill=5, step_mode=step_mode)
     assert worst < 1e-4
 
 
-def test_full_width_two_layers(V, oracle):
+@pytest.mark.parametrize("step_mode", MODES)
+def test_full_width_two_layers(V, oracle, step_mode):
     """dim 3072 / hidden 9216 / 32:8 heads / vocab 131072, 2 layers."""
-    worst, margins = teacher_forced(V, oracle, FULL, 2, 131072, 24, prefill=8)
+    worst, margins = teacher_forced(V, oracle, FULL, 2, 131072, 24, prefill=8, step_mode=step_mode)
     assert worst < 1e-3
 
 
-def test_full_width_eviction(V, oracle):
+@pytest.mark.parametrize("step_mode", MODES)
+def test_full_width_eviction(V, oracle, step_mode):
     """Full shapes with a 16-token window: 40 steps, eviction from step 17."""
-    worst, _ = teacher_forced(V, oracle, FULL, 2, 131072, 40, window=16, prefill=10)
+    worst, _ = teacher_forced(V, oracle, FULL, 2, 131072, 40, window=16, prefill=10, step_mode=step_mode)
     assert worst < 1e-3
 
 
@@ -109,8 +117,9 @@ def test_full_26_layer_token_loop(V, oracle):
     assert worst < 1e-3
 
 
-def test_generate_matches_stepwise_greedy(V):
-    with make_ctx(V, MINI, 2, 1000, seed=2) as ctx:
+@pytest.mark.parametrize("step_mode", MODES)
+def test_generate_matches_stepwise_greedy(V, step_mode):
+    with make_ctx(V, MINI, 2, 1000, seed=2, step_mode=step_mode) as ctx:
         kv1 = V.RollingKvCache(ctx, 2, 2, 16, 8)
         kv2 = V.RollingKvCache(ctx, 2, 2, 16, 8)
         ctx.model_prefill(kv1, [1, 2, 3], 0)

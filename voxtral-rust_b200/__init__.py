@@ -53,7 +53,10 @@ class DecoderConfig(C.Structure):
 
 class CtxOptions(C.Structure):
     _fields_ = [("device", C.c_int), ("n_layers", SZ), ("vocab", SZ), ("max_positions", SZ),
-                ("weight_dtype", C.c_int)]
+                ("weight_dtype", C.c_int), ("step_mode", C.c_int)]
+
+
+STEP_AUTO, STEP_LAYERS, STEP_PERSISTENT = 0, 1, 2
 
 
 class F32Slice(C.Structure):
@@ -179,11 +182,11 @@ class Context:
     """A CUDA device plus the decoder weights it holds."""
 
     def __init__(self, cfg: DecoderConfig, n_layers=1, vocab=0, device=0, max_positions=0,
-                 weight_dtype=WEIGHTS_BF16):
+                 weight_dtype=WEIGHTS_BF16, step_mode=STEP_AUTO):
         self.cfg = cfg
         self.n_layers, self.vocab = n_layers, vocab
         self.weight_dtype = weight_dtype
-        opt = CtxOptions(device, n_layers, vocab, max_positions, weight_dtype)
+        opt = CtxOptions(device, n_layers, vocab, max_positions, weight_dtype, step_mode)
         h = VP()
         _check(lib().vox_ctx_create(C.byref(cfg), C.byref(opt), C.byref(h)))
         self.h = h.value

@@ -242,21 +242,20 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
         __syncthreads();  // the next iteration refills the other buffer of this pair
     }
 
-    // Split partial: [G][hd] accumulator, then m, l per head.
-    const int G2 = hd + 2;
-    float* part = A.part + ((size_t)h * A.nsplit + split) * G * G2;
+    // Split partials: accumulators [n_kv, nsplit, G, hd], then (m, l) pairs
+    // [n_kv, nsplit, G, 2], so the merge can read accumulators as vectors.
+    const size_t acc_stride = (size_t)G * hd;  // floats per split
+    const size_t ml_base = (size_t)A.n_kv * A.nsplit * acc_stride;
+    float* pacc = A.part + ((size_t)h * A.nsplit + split) * acc_stride;
+    float* pml = A.part + ml_base + ((size_t)h * A.nsplit + split) * G * 2;
 #pragma unroll
     for (int j = 0; j < kMaxAcc; ++j) {
         const int o = tid + j * kAttnThreads;
-        if (o < n_out) {
-            const int g = o / hdv, dv = o - g * hdv;
-#pragma unroll
-            for (int e = 0; e < VEC; ++e) part[g * G2 + dv * VEC + e] = fget(acc[j], e);
-        }
+        if (o < n_out) *reinterpret_cast<T*>(pacc + (size_t)o * VEC) = acc[j];
     }
     if (tid < G) {
-        part[tid * G2 + hd] = m_s[tid];
-        part[tid * G2 + hd + 1] = l_s[tid];
+        pml[tid * 2] = m_s[tid];
+        pml[tid * 2 + 1] = l_s[tid];
     }
     __threadfence();
     __syncthreads();
@@ -269,14 +268,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
     __threadfence();
 
     // Last CTA of this kv head: merge weights w_s = exp(m_s - M) / L once per head ...
-    const float* base = A.part + (size_t)h * A.nsplit * G * G2;
+    const float* bacc = A.part + (size_t)h * A.nsplit * acc_stride;
+    const float* bml = A.part + ml_base + (size_t)h * A.nsplit * G * 2;
     for (int g = warp; g < G; g += kAttnThreads / 32) {
         float ms[2], ls[2];
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
             const int s = lane + 32 * r;
-            ms[r] = s < n_active ? __ldcg(base + ((size_t)s * G + g) * G2 + hd) : -INFINITY;
-            ls[r] = s < n_active ? __ldcg(base + ((size_t)s * G + g) * G2 + hd + 1) : 0.f;
+            ms[r] = s < n_active ? __ldcg(bml + ((size_t)s * G + g) * 2) : -INFINITY;
+            ls[r] = s < n_active ? __ldcg(bml + ((size_t)s * G + g) * 2 + 1) : 0.f;
         }
         float M = fmaxf(ms[0], ms[1]);
 #pragma unroll
@@ -297,25 +297,29 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
         }
     }
     __syncthreads();
-    // ... then each output is a weighted sum over the splits (independent loads).
-    for (int o = tid; o < G * hd; o += kAttnThreads) {
-        const int g = o / hd, d = o - g * hd;
-        const float* pd = base + (size_t)g * G2 + d;
+    // ... then each output vector is a weighted sum over the splits, loaded
+    // eight splits at a time with independent loads.
+    const size_t vstride = acc_stride / VEC;
+    for (int o = tid; o < n_out; o += kAttnThreads) {
+        const int g = o / hdv;
+        const T* pv = reinterpret_cast<const T*>(bacc) + o;
         const float* wg = w_s + g * kMaxSplits;
-        float O = 0.f;
-        int s = 0;
-        for (; s + 4 <= n_active; s += 4) {
-            const float x0 = __ldcg(pd + (size_t)(s + 0) * G * G2);
-            const float x1 = __ldcg(pd + (size_t)(s + 1) * G * G2);
-            const float x2 = __ldcg(pd + (size_t)(s + 2) * G * G2);
-            const float x3 = __ldcg(pd + (size_t)(s + 3) * G * G2);
-            O = fmaf(x0, wg[s], O);
-            O = fmaf(x1, wg[s + 1], O);
-            O = fmaf(x2, wg[s + 2], O);
-            O = fmaf(x3, wg[s + 3], O);
+        T sum;
+        fzero(sum);
+        for (int s0 = 0; s0 < n_active; s0 += 8) {
+            T v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (s0 + j < n_active)
+                    v[j] = __ldcg(pv + (size_t)(s0 + j) * vstride);
+                else
+                    fzero(v[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (s0 + j < n_active) faxpy(sum, wg[s0 + j], v[j]);
         }
-        for (; s < n_active; ++s) O = fmaf(__ldcg(pd + (size_t)s * G * G2), wg[s], O);
-        out_h[(size_t)g * hd + d] = O;
+        *reinterpret_cast<T*>(out_h + (size_t)o * VEC) = sum;
     }
     if (tid == 0) A.tickets[h] = 0u;
 }

@@ -42,7 +42,7 @@ struct GemvTuning {
     int stage_mult = 1;
     int warps = 16;
 };
-GemvTuning g_tune;
+constexpr GemvTuning g_tune{};
 
 template <typename WT>
 struct Elem;
@@ -460,13 +460,6 @@ bool gemv_supported(int K, int wsize) {
 }
 
 size_t gemv_max_smem() { return g_tune.stage_budget > 108 * 1024 ? 227 * 1024 - 256 : 113 * 1024; }
-
-void gemv_set_tuning(size_t stage_budget, int ctas_per_sm, int stage_mult, int warps) {
-    if (warps == 8 || warps == 16) g_tune.warps = warps;
-    if (stage_budget >= 16 * 1024) g_tune.stage_budget = stage_budget;
-    if (ctas_per_sm >= 1) g_tune.ctas_per_sm = ctas_per_sm;
-    if (stage_mult >= 1) g_tune.stage_mult = stage_mult;
-}
 
 GemvPlan plan_gemv(int rows, int K, int unit, int wsize, int num_sms, int n_vec) {
     GemvPlan p{};

@@ -26,12 +26,13 @@ def main():
     ap.add_argument("--launches", type=int, default=8)
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--context", type=int, default=512)
+    ap.add_argument("--mode", type=int, default=0, help="0 auto, 1 per-layer kernels, 2 persistent kernel")
     args = ap.parse_args()
     V = importlib.import_module("voxtral-rust_b200")
     cfg = V.DecoderConfig(dim=3072, hidden_dim=9216, n_heads=32, n_kv_heads=8, head_dim=128,
                           sliding_window=8192, norm_eps=1e-5, rope_theta=1e6)
     vocab = 131072 if args.which in ("head", "step") else 0
-    with V.Context(cfg, n_layers=args.layers, vocab=vocab) as ctx:
+    with V.Context(cfg, n_layers=args.layers, vocab=vocab, step_mode=args.mode) as ctx:
         ctx.init_random(0, 0.02)
         if args.which == "step":
             kv = V.RollingKvCache(ctx, args.layers, 8, 128, 8192)
