@@ -213,6 +213,12 @@ int vox_linear_f32(vox_ctx* ctx, const float* input, size_t n_rows, size_t in_di
                    const float* weight, size_t out_dim, const float* bias, float* out);
 int vox_linear_bf16(vox_ctx* ctx, const float* input, size_t n_rows, size_t in_dim,
                     const uint16_t* weight, size_t out_dim, const float* bias, float* out);
+/* linear (ops.rs:11-39) with bf16 weights for up to 8 input rows at once, on
+ * the tensor cores (tcgen05, f32 accumulation; each f32 input is carried as a
+ * bf16 hi + lo pair).  in_dim a multiple of 64.  The weights are streamed
+ * once for all rows: the multi-stream decode shape. */
+int vox_linear_batched_bf16(vox_ctx* ctx, const float* input, size_t n_rows, size_t in_dim,
+                            const uint16_t* weight, size_t out_dim, const float* bias, float* out);
 /* add_inplace (ops.rs:41-46). */
 int vox_add_inplace(vox_ctx* ctx, float* dst, const float* src, size_t n);
 /* attention_gqa_step (ops.rs:66-132): q [n_heads, head_dim]; keys/values

@@ -69,6 +69,35 @@ def test_linear_matches_oracle(V, ctx, oracle, n_rows, in_dim, out_dim, bf16, bi
     assert np.max(np.abs(got - ref)) < 2e-5 * scale + 1e-6
 
 
+@pytest.mark.parametrize("n_rows,in_dim,out_dim,bias", [
+    (1, 3072, 6144, False), (4, 3072, 6144, False), (8, 3072, 6144, True), (8, 4096, 3072, False),
+    (3, 9216, 3072, False), (8, 3072, 18432, False), (5, 64, 37, True), (2, 128, 129, False),
+    (8, 3072, 131072, False), (7, 640, 300, True),
+])
+def test_linear_batched_matches_oracle(V, ctx, oracle, n_rows, in_dim, out_dim, bias):
+    """Tensor-core skinny GEMM (tcgen05, f32 accumulation, x as bf16 hi + lo)
+    against the oracle's sequential f32 sums; tolerance 1e-4 of the output
+    scale sqrt(in_dim) * 0.02."""
+    rng = np.random.default_rng(in_dim * 7 + out_dim + n_rows)
+    x = rng.standard_normal(n_rows * in_dim).astype(np.float32)
+    b = rng.standard_normal(out_dim).astype(np.float32) if bias else None
+    w = oracle.gen_normal_bf16(5, in_dim, 0.02, in_dim * out_dim)
+    ref = oracle.linear_bf16(x, n_rows, in_dim, w, out_dim, b)
+    got = V.linear_batched(ctx, x, n_rows, in_dim, w, out_dim, b)
+    scale = np.sqrt(in_dim) * 0.02
+    err = float(np.max(np.abs(got - ref)))
+    assert err < 1e-4 * scale + 1e-6, f"max abs error {err:.3e} (scale {scale:.3f})"
+
+
+def test_linear_batched_limits_are_errors(V, ctx):
+    with pytest.raises(V.VoxError) as e:
+        V.linear_batched(ctx, np.zeros(9 * 64, np.float32), 9, 64, np.zeros(64 * 4, np.uint16), 4)
+    assert e.value.code == V.ERR_UNSUPPORTED
+    with pytest.raises(V.VoxError) as e:
+        V.linear_batched(ctx, np.zeros(32, np.float32), 1, 32, np.zeros(32 * 4, np.uint16), 4)
+    assert e.value.code == V.ERR_UNSUPPORTED
+
+
 def test_gqa_golden(V, ctx, ref_tests):
     t = ref_tests["gqa_matches_expanded_kv_reference"]  # ops.rs:154-237
     sh = V.AttentionShape(t["n_heads"], t["head_dim"], t["seq_len"], t["n_kv_heads"], t["sliding_window"])

@@ -125,6 +125,7 @@ _SIGS = {
     "vox_profile_gemv": ([VP, C.c_int, SZ, F32P, C.POINTER(C.c_uint64)], C.c_int),
     "vox_linear_f32": ([VP, F32P, SZ, SZ, F32P, SZ, F32P, F32P], C.c_int),
     "vox_linear_bf16": ([VP, F32P, SZ, SZ, U16P, SZ, F32P, F32P], C.c_int),
+    "vox_linear_batched_bf16": ([VP, F32P, SZ, SZ, U16P, SZ, F32P, F32P], C.c_int),
     "vox_add_inplace": ([VP, F32P, F32P, SZ], C.c_int),
     "vox_attention_gqa_step": ([VP, F32P, F32P, F32P, C.POINTER(AttentionShape), F32P], C.c_int),
     "vox_rms_norm_rows": ([VP, F32P, F32P, F32P, SZ, SZ, C.c_float], C.c_int),
@@ -393,6 +394,16 @@ def linear(ctx: Context, x, n_rows, in_dim, weight, out_dim, bias=None):
     else:
         w = _f32(weight)
         _check(lib().vox_linear_f32(ctx.h, _p(x), n_rows, in_dim, _p(w), out_dim, _p(b), _p(out)))
+    return out
+
+
+def linear_batched(ctx: Context, x, n_rows, in_dim, weight, out_dim, bias=None):
+    """linear (ops.rs:11-39) for up to 8 rows on the tensor cores; weight uint16 bf16 bits."""
+    x = _f32(x)
+    out = np.empty(n_rows * out_dim, np.float32)
+    b = _f32(bias) if bias is not None else None
+    w = np.ascontiguousarray(weight, dtype=np.uint16)
+    _check(lib().vox_linear_batched_bf16(ctx.h, _p(x), n_rows, in_dim, _p(w, U16P), out_dim, _p(b), _p(out)))
     return out
 
 

@@ -1,0 +1,420 @@
+// vox_bgemm.cu -- skinny GEMM for multi-stream decode on the 5th-generation
+// tensor cores (tcgen05 + TMEM).
+//
+// Y[b, r] = sum_k W[r, k] * X[b, k] for B <= 8 independent input vectors (the
+// reference's `linear`, crates/voxtral/src/ops.rs:11-39, with n_rows = B).
+// Weights are read once for all B streams, so the op stays HBM-bound while
+// producing B outputs per weight byte.
+//
+// Layout.  W is pre-tiled once in HBM into 128-row x 64-column bf16 blocks of
+// 16 KB, each already in the UMMA canonical K-major no-swizzle layout (8x8
+// "core matrices" of 128 bytes: core (m8, k2) of K-step s at
+// s*4 KB + (k2*16 + m8)*128, so LBO = 2 KB between K halves and SBO = 128 B
+// between 8-row groups).  A work item = one 128-row tile x a range of K
+// blocks; its blocks are contiguous, so a producer lane streams them with 1-D
+// cp.async.bulk (no tensor map, no multicast) into a 4-stage ring.
+//
+// The B operand is X converted to bf16 twice: hi = bf16(x), lo = bf16(x - hi)
+// as columns b and 8 + b of an N = 16 operand, so the product carries ~16
+// mantissa bits of the f32 activations; hi and lo are summed in the epilogue.
+//
+// One lane issues tcgen05.mma (kind::f16, M=128, N=16, K=16, f32 accumulate)
+// into a double-buffered TMEM accumulator; tcgen05.commit frees ring stages
+// and signals the epilogue warpgroup, which reads the accumulator with
+// tcgen05.ld.  Items that split K write partial tiles; the last item of a tile
+// (atomic ticket) sums them in split order, so results are deterministic.
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include "vox_device.cuh"
+
+namespace vox {
+
+namespace {
+
+constexpr int kBM = 128;                     // tile rows (UMMA M)
+constexpr int kBK = 64;                      // K elements per block
+constexpr int kBlockBytes = kBM * kBK * 2;   // 16 KB
+constexpr int kStageBlocks = 2;              // blocks per ring stage
+constexpr int kStageBytes = kStageBlocks * kBlockBytes;
+constexpr int kStages = 4;
+constexpr int kN = 16;                       // UMMA N: 8 streams x (hi, lo)
+constexpr int kThreads = 256;                // w0 producer, w1 MMA, w4..w7 epilogue, w1..w7 X prep
+constexpr int kWorkers = kThreads - 32;      // every warp but the producer
+constexpr uint32_t kTmemCols = 32;           // two 16-column accumulators
+
+// UMMA instruction descriptor: D f32 (bit 4), A and B bf16 (bits 7, 10), both
+// K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kN >> 3) << 17) |
+                            ((uint32_t)(kBM >> 4) << 24);
+
+// Shared-memory matrix descriptor, no swizzle, K-major (sm100: start address,
+// LBO and SBO in 16-byte units at bits 0, 16, 32; version 1 at bit 46;
+// layout type 0 at bits 61-63).
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;
+    return d;
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    const uint32_t zero = 0u;  // no output lane disabled
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate), "r"(zero)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+        "%13, %14, %15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint16_t f2bf(float f) {  // round to nearest even
+    const uint32_t u = __float_as_uint(f);
+    return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+
+// Work item i -> (tile, split); a CTA's items keep their split (and so the X
+// slab) when the grid is a multiple of the split count.
+struct Item {
+    int tile, ks, kb0, kb1;
+};
+__device__ __forceinline__ Item item_of(const BgArgs& A, int i) {
+    Item it;
+    it.ks = i % A.splits;
+    it.tile = i / A.splits;
+    it.kb0 = (int)((long long)A.kbt * it.ks / A.splits);
+    it.kb1 = (int)((long long)A.kbt * (it.ks + 1) / A.splits);
+    return it;
+}
+
+// Final values of one row r of a tile for every stream: y[b] times the
+// stream's RMSNorm factor inv[b].
+__device__ __forceinline__ void bg_epilogue(const BgArgs& A, int r, const float (&y)[8], const float (&inv)[8]) {
+    if (A.epi == BG_STORE) {
+        if (r < A.rows) {
+            const float bias = A.bias ? A.bias[r] : 0.0f;
+#pragma unroll
+            for (int b = 0; b < 8; ++b)
+                if (b < A.B) A.y[(size_t)b * A.y_stride + r] = __fadd_rn(bias, __fmul_rn(inv[b], y[b]));
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constant__ BgArgs A) {
+    extern __shared__ __align__(1024) unsigned char smem[];
+    unsigned char* ring = smem;                                // kStages x 32 KB
+    unsigned char* xs = smem + kStages * kStageBytes;          // X slab: one 512 B slab per K step
+    uint64_t* full = reinterpret_cast<uint64_t*>(xs + A.xslab_bytes);
+    uint64_t* empty = full + kStages;
+    uint64_t* acc_full = empty + kStages;  // [2]
+    uint64_t* acc_empty = acc_full + 2;    // [2]
+    uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    int* flag_s = reinterpret_cast<int*>(tmem_base_s + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n_items = A.tiles * A.splits;
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+        }
+        fence_barrier_init();
+    }
+    if (warp == 1) {  // TMEM accumulators: the whole warp allocates
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_addr(tmem_base_s)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tmem_fence_before();
+    __syncthreads();
+    tmem_fence_after();
+    const uint32_t tmem = *tmem_base_s;
+    pdl_allow_dependents();
+
+    // ---- producer: stream this CTA's weight blocks (weights need no PDL wait) ----
+    if (warp == 0) {
+        if (lane == 0) {
+            const uint64_t pol = l2_evict_first_policy();
+            uint32_t g = 0;
+            bool ok = true;
+            for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
+                const Item it = item_of(A, i);
+                const unsigned char* src = A.wt + ((size_t)it.tile * A.kbt + it.kb0) * kBlockBytes;
+                for (int kb = it.kb0; kb < it.kb1; kb += kStageBlocks, ++g) {
+                    const int slot = (int)(g % kStages);
+                    if (g >= (uint32_t)kStages && !mbar_wait(&empty[slot], ((g / kStages) - 1) & 1)) {
+                        raise_error(A.err, ERR_EMPTY_WAIT);
+                        ok = false;
+                        break;
+                    }
+                    const int nb = min(kStageBlocks, it.kb1 - kb);
+                    mbar_arrive_expect_tx(&full[slot], (uint32_t)(nb * kBlockBytes));
+                    bulk_copy_g2s(ring + (size_t)slot * kStageBytes, src + (size_t)(kb - it.kb0) * kBlockBytes,
+                                  (uint32_t)(nb * kBlockBytes), &full[slot], pol);
+                }
+            }
+            // no copy may be in flight when the CTA exits
+            const uint32_t first = g > (uint32_t)kStages ? g - kStages : 0u;
+            for (uint32_t s = first; s < g; ++s)
+                if (!mbar_wait(&full[s % kStages], (s / kStages) & 1)) raise_error(A.err, ERR_DRAIN_WAIT);
+        }
+        // The producer warp takes no part in the rest (its lane 0 streams while
+        // the other warps work), so the worker barriers below exclude it.
+        pdl_wait_prior_grids();
+        return;
+    }
+
+    pdl_wait_prior_grids();
+
+    // Per-stream RMSNorm factor, applied to the row sums (y = inv * W (x * g)).
+    float inv[8];
+#pragma unroll
+    for (int b = 0; b < 8; ++b) inv[b] = 1.0f;
+    if (A.norm_w) {
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            if (b < A.B) {
+                float ss = 0.0f;
+                for (int p = 0; p < A.ssp_parts; ++p) ss += __ldcg(A.ssp + (size_t)p * 8 + b);
+                inv[b] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)A.K), A.eps)));
+            }
+        }
+    }
+
+    int cur_ks = -1;
+    uint32_t g_mma = 0;
+    bool mma_ok = true;  // after a wait expires the issuer stops waiting (the result is flagged)
+    int local = 0;  // items processed by this CTA
+    for (int i = blockIdx.x; i < n_items; i += gridDim.x, ++local) {
+        const Item it = item_of(A, i);
+        const int nkb = it.kb1 - it.kb0;
+        // ---- X slab for this split, built by warps 1..7 ----
+        if (it.ks != cur_ks) {
+            if (local > 0) {  // the previous item's MMAs read the old slab: wait for their commit
+                const int pb = (local - 1) & 1;
+                if (!mbar_wait(&acc_full[pb], ((local - 1) >> 1) & 1)) raise_error(A.err, ERR_FULL_WAIT);
+            }
+            const int kbase = it.kb0 * kBK;
+            const int nk8 = nkb * kBK / 8;  // 8-element chunks per stream
+            for (int e = tid - 32; e < 8 * nk8; e += kWorkers) {
+                const int b = e / nk8;
+                const int k = (e - b * nk8) * 8;
+                uint32_t hi[4] = {0, 0, 0, 0}, lo[4] = {0, 0, 0, 0};
+                if (b < A.B) {
+                    const float* xp = A.x + (size_t)b * A.x_stride + kbase + k;
+                    const float4 a0 = __ldcg(reinterpret_cast<const float4*>(xp));
+                    const float4 a1 = __ldcg(reinterpret_cast<const float4*>(xp + 4));
+                    float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                    if (A.norm_w) {
+                        const float4 g0 = __ldg(reinterpret_cast<const float4*>(A.norm_w + kbase + k));
+                        const float4 g1 = __ldg(reinterpret_cast<const float4*>(A.norm_w + kbase + k + 4));
+                        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(v[j], gv[j]);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; j += 2) {
+                        const uint16_t h0 = f2bf(v[j]), h1 = f2bf(v[j + 1]);
+                        const uint16_t l0 = f2bf(v[j] - bf16_bits_to_f32(h0));
+                        const uint16_t l1 = f2bf(v[j + 1] - bf16_bits_to_f32(h1));
+                        hi[j >> 1] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+                        lo[j >> 1] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+                    }
+                }
+                // core (n8, k2) of K-step s at s*512 + (k2*2 + n8)*128 + row*16:
+                // hi parts are rows 0..7 (n8 = 0), lo parts rows 8..15 (n8 = 1)
+                const int s = k / 16, k2 = (k / 8) & 1;
+                unsigned char* base = xs + (size_t)s * 512 + (size_t)k2 * 256;
+                *reinterpret_cast<uint4*>(base + b * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<uint4*>(base + 128 + b * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            }
+            // generic-proxy writes must be visible to the tensor core (async proxy)
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            named_barrier_sync(1, kWorkers);
+            cur_ks = it.ks;
+        }
+
+        const int ab = local & 1;  // accumulator buffer
+        // ---- MMA issuer ----
+        if (warp == 1 && lane == 0) {
+            if (mma_ok && local >= 2 && !mbar_wait(&acc_empty[ab], ((local - 2) >> 1) & 1)) {
+                raise_error(A.err, ERR_FULL_WAIT);
+                mma_ok = false;
+            }
+            tmem_fence_after();
+            const uint32_t d = tmem + (uint32_t)(ab * kN);
+            const uint32_t xs_addr = smem_addr(xs);
+            int kstep = 0;
+            for (int kb = it.kb0; kb < it.kb1; kb += kStageBlocks, ++g_mma) {
+                const int slot = (int)(g_mma % kStages);
+                if (!mma_ok) break;
+                if (!mbar_wait(&full[slot], (g_mma / kStages) & 1)) {
+                    raise_error(A.err, ERR_FULL_WAIT);
+                    mma_ok = false;
+                    break;
+                }
+                tmem_fence_after();
+                const int nb = min(kStageBlocks, it.kb1 - kb);
+                const uint32_t a_addr = smem_addr(ring + (size_t)slot * kStageBytes);
+                for (int j = 0; j < nb * 4; ++j, ++kstep) {
+                    const uint64_t ad = umma_desc(a_addr + (uint32_t)j * 4096u, 2048u, 128u);
+                    const uint64_t bd = umma_desc(xs_addr + (uint32_t)kstep * 512u, 256u, 128u);
+                    umma_f16(d, ad, bd, kstep > 0 ? 1u : 0u);
+                }
+                umma_commit(&empty[slot]);  // frees the stage once these MMAs have read it
+            }
+            umma_commit(&acc_full[ab]);  // accumulator ready for the epilogue
+        }
+
+        // ---- epilogue warpgroup: TMEM -> registers -> partial or final rows ----
+        if (warp >= 4) {
+            const int ew = warp - 4;        // TMEM lanes 32*ew .. 32*ew + 31
+            const int row = ew * 32 + lane; // row inside the tile
+            const int r = it.tile * kBM + row;
+            if (!mbar_wait(&acc_full[ab], (local >> 1) & 1)) raise_error(A.err, ERR_FULL_WAIT);
+            tmem_fence_after();
+            uint32_t raw[16];
+            tmem_ld16(tmem + ((uint32_t)(ew * 32) << 16) + (uint32_t)(ab * kN), raw);
+            tmem_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[ab]);
+            float y[8];
+#pragma unroll
+            for (int b = 0; b < 8; ++b) y[b] = __uint_as_float(raw[b]) + __uint_as_float(raw[8 + b]);
+
+            bool final_item = true;
+            if (A.splits > 1) {
+                float* part = A.part + ((size_t)i * kBM + row) * 8;
+                *reinterpret_cast<float4*>(part) = make_float4(y[0], y[1], y[2], y[3]);
+                *reinterpret_cast<float4*>(part + 4) = make_float4(y[4], y[5], y[6], y[7]);
+                __threadfence();
+                named_barrier_sync(2, 128);
+                if (ew == 0 && lane == 0) {
+                    const unsigned t = atomicAdd(&A.tickets[it.tile], 1u);
+                    *flag_s = (t == (unsigned)(A.splits - 1)) ? 1 : 0;
+                }
+                named_barrier_sync(2, 128);
+                final_item = *flag_s != 0;
+                named_barrier_sync(2, 128);  // flag read by all before the next item rewrites it
+                if (final_item) {
+                    __threadfence();
+#pragma unroll
+                    for (int b = 0; b < 8; ++b) y[b] = 0.0f;
+                    for (int ks = 0; ks < A.splits; ++ks) {
+                        const float* p = A.part + ((size_t)(it.tile * A.splits + ks) * kBM + row) * 8;
+                        const float4 p0 = __ldcg(reinterpret_cast<const float4*>(p));
+                        const float4 p1 = __ldcg(reinterpret_cast<const float4*>(p + 4));
+                        y[0] += p0.x; y[1] += p0.y; y[2] += p0.z; y[3] += p0.w;
+                        y[4] += p1.x; y[5] += p1.y; y[6] += p1.z; y[7] += p1.w;
+                    }
+                    if (ew == 0 && lane == 0) A.tickets[it.tile] = 0u;
+                }
+            }
+            if (final_item) bg_epilogue(A, r, y, inv);
+        }
+    }
+
+    // TMEM is released by the warp that allocated it, after every reader is done.
+    tmem_fence_before();
+    named_barrier_sync(1, kWorkers);
+    if (warp == 1) {
+        tmem_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
+__global__ void tile_weights_kernel(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst, int rows,
+                                    int K, int tiles) {
+    const int kbt = K / kBK;
+    const long long total = (long long)tiles * kBM * K;
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+         e += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(e / K), k = (int)(e - (long long)r * K);
+        const int t = r / kBM, rr = r - t * kBM;
+        const int kb = k / kBK, kk = k - kb * kBK;
+        const int s = kk / 16, k2 = (kk / 8) & 1, kin = kk & 7;
+        const int m8 = rr / 8, rin = rr & 7;
+        const size_t off = ((size_t)t * kbt + kb) * (kBlockBytes / 2) + (size_t)s * 2048 +
+                           (size_t)(k2 * 16 + m8) * 64 + rin * 8 + kin;
+        dst[off] = r < rows ? src[(size_t)r * K + k] : (uint16_t)0;
+    }
+}
+
+}  // namespace
+
+size_t bgemm_smem_bytes(int K, int splits) {
+    const int kbt = K / kBK;
+    const int max_kb = (kbt + splits - 1) / splits;
+    const size_t xslab = (size_t)max_kb * 4 * 512;
+    return (size_t)kStages * kStageBytes + xslab + (2 * kStages + 4) * 8 + 16;
+}
+
+int bgemm_xslab_bytes(int K, int splits) {
+    const int kbt = K / kBK;
+    return ((kbt + splits - 1) / splits) * 4 * 512;
+}
+
+cudaError_t bgemm_prepare(int /*dev*/) {
+    return cudaFuncSetAttribute(bgemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+}
+
+cudaError_t launch_bgemm(const BgArgs& a, int grid, cudaStream_t s, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = bgemm_smem_bytes(a.K, a.splits);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    void* args[] = {(void*)&a};
+    return cudaLaunchKernelExC(&cfg, (void*)bgemm_kernel, args);
+}
+
+size_t tiled_bytes(int rows, int K) { return (size_t)((rows + kBM - 1) / kBM) * kBM * K * 2; }
+
+cudaError_t launch_tile_weights(const uint16_t* src, uint16_t* dst, int rows, int K, cudaStream_t s) {
+    const int tiles = (rows + kBM - 1) / kBM;
+    const long long total = (long long)tiles * kBM * K;
+    long long g = (total + 255) / 256;
+    if (g > 148 * 16) g = 148 * 16;
+    tile_weights_kernel<<<(int)g, 256, 0, s>>>(src, dst, rows, K, tiles);
+    return cudaGetLastError();
+}
+
+}  // namespace vox

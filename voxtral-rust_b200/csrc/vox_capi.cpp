@@ -703,6 +703,7 @@ int vox_ctx_create(const vox_decoder_config* cfg, const vox_ctx_options* opt, vo
 
     CTX_TRY(gemv_prepare(c->dev));
     CTX_TRY(attn_prepare(c->dev));
+    CTX_TRY(bgemm_prepare(c->dev));
     CTX_TRY(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     for (auto& e : c->ev) CTX_TRY(cudaEventCreate(&e));
 
@@ -1261,6 +1262,73 @@ int vox_linear_f32(vox_ctx* c, const float* input, size_t n_rows, size_t in_dim,
 int vox_linear_bf16(vox_ctx* c, const float* input, size_t n_rows, size_t in_dim, const uint16_t* weight,
                     size_t out_dim, const float* bias, float* out) {
     return linear_impl(c, input, n_rows, in_dim, weight, 2, out_dim, bias, out);
+}
+
+// K splits per 128-row tile of the tensor-core skinny GEMM: enough items to
+// cover every SM once, and few enough K blocks per split that the split's X
+// operand fits next to the 128 KB weight ring.
+static int bgemm_splits(int tiles, int kbt, int num_sms) {
+    int s = (num_sms + tiles - 1) / tiles;
+    const int min_s = (kbt + 39) / 40;
+    if (s < min_s) s = min_s;
+    if (s > kbt) s = kbt;
+    return s < 1 ? 1 : s;
+}
+
+int vox_linear_batched_bf16(vox_ctx* c, const float* input, size_t n_rows, size_t in_dim, const uint16_t* weight,
+                            size_t out_dim, const float* bias, float* out) {
+    if (!c || !input || !weight || !out) return fail(VOX_ERR_INVALID_ARG, "null argument");
+    if (n_rows == 0 || out_dim == 0) return VOX_OK;
+    if (n_rows > 8) return fail(VOX_ERR_UNSUPPORTED, "linear_batched: at most 8 rows, got %zu", n_rows);
+    if (in_dim == 0 || in_dim % 64 || in_dim > (1u << 20) || out_dim > (1u << 26))
+        return fail(VOX_ERR_UNSUPPORTED, "linear_batched: in_dim %zu must be a positive multiple of 64", in_dim);
+    CUDA_TRY(cudaSetDevice(c->dev));
+    const int rows = (int)out_dim, K = (int)in_dim;
+    const int tiles = (rows + 127) / 128, kbt = K / 64;
+    const int splits = bgemm_splits(tiles, kbt, c->num_sms);
+    const int items = tiles * splits;
+    int grid = c->num_sms - c->num_sms % splits;
+    if (grid < 1) grid = splits;
+    if (grid > items) grid = items;
+    auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
+    const size_t wb = al(out_dim * in_dim * 2), tb = al(tiled_bytes(rows, K));
+    const size_t xb = al(n_rows * in_dim * 4), yb = al(n_rows * out_dim * 4), bb = al(out_dim * 4);
+    const size_t pb = al((size_t)items * 128 * 8 * 4), kb = al((size_t)tiles * 4);
+    TRY(ensure_scratch(c, wb + tb + xb + yb + bb + pb + kb));
+    unsigned char* p = static_cast<unsigned char*>(c->scratch);
+    uint16_t* dW = reinterpret_cast<uint16_t*>(p);
+    unsigned char* dT = p + wb;
+    float* dx = reinterpret_cast<float*>(p + wb + tb);
+    float* dy = reinterpret_cast<float*>(p + wb + tb + xb);
+    float* db = reinterpret_cast<float*>(p + wb + tb + xb + yb);
+    float* dpart = reinterpret_cast<float*>(p + wb + tb + xb + yb + bb);
+    unsigned* dtick = reinterpret_cast<unsigned*>(p + wb + tb + xb + yb + bb + pb);
+    CUDA_TRY(cudaMemcpyAsync(dW, weight, out_dim * in_dim * 2, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(cudaMemcpyAsync(dx, input, n_rows * in_dim * 4, cudaMemcpyHostToDevice, c->stream));
+    if (bias) CUDA_TRY(cudaMemcpyAsync(db, bias, out_dim * 4, cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(cudaMemsetAsync(dtick, 0, (size_t)tiles * 4, c->stream));
+    CUDA_TRY(record_launch(c, launch_tile_weights(dW, reinterpret_cast<uint16_t*>(dT), rows, K, c->stream)));
+    BgArgs a{};
+    a.wt = dT;
+    a.rows = rows;
+    a.K = K;
+    a.tiles = tiles;
+    a.kbt = kbt;
+    a.splits = splits;
+    a.B = (int)n_rows;
+    a.xslab_bytes = bgemm_xslab_bytes(K, splits);
+    a.x = dx;
+    a.x_stride = (long long)in_dim;
+    a.epi = BG_STORE;
+    a.y = dy;
+    a.y_stride = (long long)out_dim;
+    a.bias = bias ? db : nullptr;
+    a.part = dpart;
+    a.tickets = dtick;
+    a.err = c->err;
+    CUDA_TRY(record_launch(c, launch_bgemm(a, grid, c->stream, false)));
+    CUDA_TRY(cudaMemcpyAsync(out, dy, n_rows * out_dim * 4, cudaMemcpyDeviceToHost, c->stream));
+    return check_device_errors(c);
 }
 
 int vox_silu_inplace(vox_ctx* c, float* x, size_t n) {

@@ -163,6 +163,52 @@ int token_splits(int n_kv, int grid);
 cudaError_t token_prepare(int dev);
 cudaError_t launch_token_step(const TokenArgs& a, int grid, cudaStream_t s);
 
+// ---- multi-stream skinny GEMM on tcgen05 (bf16 weights, B <= 8 streams) ----
+enum : int { BG_STORE = 0, BG_QKV = 1, BG_RESID = 2, BG_SWIGLU = 3, BG_ARGMAX = 4 };
+
+struct BgArgs {
+    const unsigned char* wt;    // weights pre-tiled into 128 x 64 UMMA blocks (launch_tile_weights)
+    int rows, K;                // logical weight shape [rows, K]
+    int tiles, kbt;             // 128-row tiles, 64-wide K blocks per tile
+    int splits;                 // K splits per tile
+    int B;                      // active streams (<= 8)
+    int xslab_bytes;            // shared bytes of one split's X operand
+    const float* x;             // [B, x_stride] f32 inputs
+    long long x_stride;
+    const float* norm_w;        // non-null: apply RMSNorm with this gain to x
+    const float* ssp;           // RMSNorm partial sums of squares [ssp_parts, 8]
+    int ssp_parts;
+    float eps;
+    int epi;
+    float* y;                   // [B, y_stride]
+    long long y_stride;
+    const float* bias;
+    const float* resid;
+    float* ssp_out;
+    int q_dim, kv_dim, head_dim;
+    const float* rope_cos;
+    const float* rope_sin;
+    int max_pos;
+    const StepState* steps;     // per stream
+    KvState* kv_state;
+    long long kv_state_stride;
+    float* k_ring;
+    float* v_ring;
+    long long ring_stride;      // floats between streams' rings
+    int ring_cap, kv_window;
+    ArgmaxPart* am_part;
+    float* part;                // split-K partial tiles [tiles * splits, 128, 8]
+    unsigned* tickets;          // [tiles], zero between launches
+    unsigned* err;
+};
+
+size_t bgemm_smem_bytes(int K, int splits);
+int bgemm_xslab_bytes(int K, int splits);
+cudaError_t bgemm_prepare(int dev);
+cudaError_t launch_bgemm(const BgArgs& a, int grid, cudaStream_t s, bool pdl);
+size_t tiled_bytes(int rows, int K);
+cudaError_t launch_tile_weights(const uint16_t* src, uint16_t* dst, int rows, int K, cudaStream_t s);
+
 // ---- launchers (return the launch error) ----
 GemvPlan plan_gemv(int rows, int K, int unit, int wsize, int num_sms, int n_vec);
 bool gemv_supported(int K, int wsize);
