@@ -175,6 +175,28 @@ int vox_kv_layer_device_state(const vox_kv* kv, size_t layer, int64_t out[3]);
 /* Forget every token (all layers back to len 0, pos_offset 0). */
 int vox_kv_reset(vox_kv* kv);
 
+/* ---- multi-stream caches -------------------------------------------------- */
+/* n_streams (1..8) independent RollingKvCaches (kv.rs:33-46) in one
+ * allocation, for the multi-stream step (vox_model_step_batch).  Each stream
+ * has its own ring, length and pos_offset. */
+int vox_kv_create_streams(vox_ctx* ctx, size_t n_streams, size_t n_layers, size_t n_kv_heads,
+                          size_t head_dim, size_t sliding_window, vox_kv** out);
+/* Number of streams of a cache (1 for a single-stream cache or a view). */
+int vox_kv_n_streams(const vox_kv* kv, size_t* out);
+/* A handle to stream `stream` of a multi-stream cache that every
+ * single-stream entry point accepts (append, observers, layer step,
+ * vox_model_step).  It shares the cache's memory, lives until the cache is
+ * destroyed (vox_kv_destroy on a view does nothing) and is the cache itself
+ * when it holds one stream.  Single-stream entry points reject a
+ * multi-stream cache with VOX_ERR_INVALID_ARG. */
+int vox_kv_stream(vox_kv* kv, size_t stream, vox_kv** out);
+/* Replace the contents of every layer of a single-stream cache (or view)
+ * with n_tokens tokens from the library's counter-based generator:
+ * layer l's keys are tensor tensor_id + 2l and its values tensor
+ * tensor_id + 2l + 1, each [n_tokens, n_kv_heads, head_dim] token-major,
+ * ~N(0, std^2) rounded to bf16.  len_tokens = n_tokens, pos_offset = 0;
+ * n_tokens <= sliding_window. */
+int vox_kv_fill_random(vox_kv* kv, size_t n_tokens, uint64_t seed, uint64_t tensor_id, float std);
 /* ---- decoder step (decoder.rs:88-155) -------------------------------------- */
 /* decoder_layer_forward_step: hidden [dim] f32 in, out [dim] f32 (the
  * reference returns a new Vec; here the caller owns `out`).  Appends one
@@ -196,6 +218,17 @@ int vox_model_generate(vox_ctx* ctx, vox_kv* kv, int32_t token, size_t pos, size
 /* Sequential prefill of n tokens at positions pos0.. (logits discarded). */
 int vox_model_prefill(vox_ctx* ctx, vox_kv* kv, const int32_t* tokens, size_t n, size_t pos0);
 
+/* One token for every stream of a multi-stream cache (bf16 weights): the
+ * step of vox_model_step, with every linear on the tensor cores reading each
+ * weight once for all streams.  tokens[s], positions[s] per stream;
+ * next_tokens [n_streams] and logits_out [n_streams, vocab] are nullable.
+ * Runs as one CUDA graph. */
+int vox_model_step_batch(vox_ctx* ctx, vox_kv* kv, const int32_t* tokens, const size_t* positions,
+                         int32_t* next_tokens, float* logits_out);
+/* Greedy decode of n_steps tokens for every stream on the device.
+ * tokens_out [n_steps, n_streams] (nullable). */
+int vox_model_generate_batch(vox_ctx* ctx, vox_kv* kv, const int32_t* tokens, const size_t* positions,
+                             size_t n_steps, int32_t* tokens_out);
 /* ---- profiling hook (no reference counterpart) --------------------------------- */
 /* Times one of the step's weight-streaming GEMVs on its own: n_launches
  * back-to-back launches (cycling over the layers, so every launch streams a

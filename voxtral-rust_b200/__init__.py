@@ -112,6 +112,12 @@ _SIGS = {
     "vox_kv_create": ([VP, SZ, SZ, SZ, SZ, C.POINTER(VP)], C.c_int),
     "vox_kv_create_ex": ([VP, SZ, SZ, SZ, SZ, SZ, C.POINTER(VP)], C.c_int),
     "vox_kv_destroy": ([VP], None),
+    "vox_kv_create_streams": ([VP, SZ, SZ, SZ, SZ, SZ, C.POINTER(VP)], C.c_int),
+    "vox_kv_n_streams": ([VP, C.POINTER(SZ)], C.c_int),
+    "vox_kv_stream": ([VP, SZ, C.POINTER(VP)], C.c_int),
+    "vox_kv_fill_random": ([VP, SZ, C.c_uint64, C.c_uint64, C.c_float], C.c_int),
+    "vox_model_step_batch": ([VP, VP, I32P, C.POINTER(SZ), I32P, F32P], C.c_int),
+    "vox_model_generate_batch": ([VP, VP, I32P, C.POINTER(SZ), SZ, I32P], C.c_int),
     "vox_kv_append_layer": ([VP, SZ, F32P, F32P, SZ], C.c_int),
     "vox_kv_layer_len_tokens": ([VP, SZ, C.POINTER(SZ)], C.c_int),
     "vox_kv_layer_pos_offset": ([VP, SZ, C.POINTER(SZ)], C.c_int),
@@ -304,6 +310,30 @@ class Context:
         _check(lib().vox_model_generate(self.h, cache.h, int(token), int(pos), int(n_steps), _p(out, I32P)))
         return out
 
+    # ---- multi-stream token loop (cache made with n_streams > 1) ----
+    @staticmethod
+    def _stream_inputs(cache, tokens, positions):
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        p = (SZ * cache.n_streams)(*[int(x) for x in positions])
+        if t.size != cache.n_streams or len(positions) != cache.n_streams:
+            raise ValueError("need one token and one position per stream")
+        return t, p
+
+    def model_step_batch(self, cache, tokens, positions, want_logits=False):
+        """One token per stream; returns (next tokens [B], logits [B, vocab] or None)."""
+        t, p = self._stream_inputs(cache, tokens, positions)
+        nxt = np.empty(cache.n_streams, np.int32)
+        logits = np.empty((cache.n_streams, self.vocab), np.float32) if want_logits else None
+        _check(lib().vox_model_step_batch(self.h, cache.h, _p(t, I32P), p, _p(nxt, I32P), _p(logits)))
+        return nxt, logits
+
+    def model_generate_batch(self, cache, tokens, positions, n_steps):
+        """Greedy decode of n_steps per stream; returns ids [n_steps, B]."""
+        t, p = self._stream_inputs(cache, tokens, positions)
+        out = np.empty((n_steps, cache.n_streams), np.int32)
+        _check(lib().vox_model_generate_batch(self.h, cache.h, _p(t, I32P), p, int(n_steps), _p(out, I32P)))
+        return out
+
 
 # ---------------------------------------------------------------------------
 # RollingKvCache (kv.rs)
@@ -312,12 +342,24 @@ class Context:
 class RollingKvCache:
     """RollingKvCache (kv.rs:22-101) as a device ring buffer."""
 
-    def __init__(self, ctx: Context, n_layers, n_kv_heads, head_dim, sliding_window, capacity=None):
+    def __init__(self, ctx: Context, n_layers, n_kv_heads, head_dim, sliding_window, capacity=None,
+                 n_streams=1, _view_of=None, _handle=None):
         self.ctx = ctx
         self.n_layers, self.n_kv_heads, self.head_dim = n_layers, n_kv_heads, head_dim
         self.sliding_window = sliding_window
+        self.n_streams = n_streams
+        self._parent = _view_of
+        self._views = {}
+        if _view_of is not None:  # stream view: memory owned by the parent cache
+            self.h = _handle
+            return
         h = VP()
-        if capacity is None:
+        if n_streams != 1:
+            if capacity is not None:
+                raise ValueError("multi-stream caches use capacity = sliding_window")
+            _check(lib().vox_kv_create_streams(ctx.h, n_streams, n_layers, n_kv_heads, head_dim,
+                                               sliding_window, C.byref(h)))
+        elif capacity is None:
             _check(lib().vox_kv_create(ctx.h, n_layers, n_kv_heads, head_dim, sliding_window, C.byref(h)))
         else:
             _check(lib().vox_kv_create_ex(ctx.h, n_layers, n_kv_heads, head_dim, sliding_window,
@@ -327,9 +369,26 @@ class RollingKvCache:
 
     def close(self):
         # A closed context has already freed its caches (vox_ctx_destroy).
-        if getattr(self, "h", None) and getattr(self.ctx, "h", None):
+        if self._parent is None and getattr(self, "h", None) and getattr(self.ctx, "h", None):
             lib().vox_kv_destroy(self.h)
+        for v in self._views.values():
+            v.h = None
         self.h = None
+
+    def stream(self, s):
+        """Single-stream view of stream s (shares memory; valid while this cache lives)."""
+        if self.n_streams == 1 and s == 0:
+            return self
+        if s not in self._views:
+            h = VP()
+            _check(lib().vox_kv_stream(self.h, s, C.byref(h)))
+            self._views[s] = RollingKvCache(self.ctx, self.n_layers, self.n_kv_heads, self.head_dim,
+                                            self.sliding_window, _view_of=self, _handle=h.value)
+        return self._views[s]
+
+    def fill_random(self, n_tokens, seed, tensor_id, std=1.0):
+        """Fill every layer with n_tokens generator tokens (bf16-rounded N(0, std^2))."""
+        _check(lib().vox_kv_fill_random(self.h, n_tokens, seed, tensor_id, std))
 
     def __del__(self):
         try:

@@ -120,6 +120,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int h = blockIdx.x;          // kv head
     const int split = blockIdx.y;
+    const int z = blockIdx.z;          // stream
     const int hd = A.hd;
     const int G = A.n_heads / A.n_kv;
     const int hdv = hd / VEC;          // vectors per row
@@ -140,7 +141,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
     pdl_allow_dependents();
     pdl_wait_prior_grids();
 
-    KvState st = *A.st;
+    const float* q_in = A.q + z * A.q_stride;
+    float* out = A.out + z * A.out_stride;
+    float* part = A.part + z * A.part_stride;
+    unsigned* tickets = A.tickets + (size_t)z * A.n_kv;
+    KvState st = A.st[z * A.st_stride];
     if (A.pre_append) st = kv_after_single_append(st, A.kv_window, A.cap);
     const int len = st.len;
     const int mask_start = (A.cfg_window > 0 && len > A.cfg_window) ? len - A.cfg_window : 0;
@@ -149,7 +154,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
     per = ((per + kTile - 1) / kTile) * kTile;
     if (per < kTile) per = kTile;
     const int n_active = (n_live + per - 1) / per;
-    float* out_h = A.out + (size_t)h * G * hd;
+    float* out_h = out + (size_t)h * G * hd;
     if (n_active == 0) {  // empty cache: the reference returns zeros
         if (split == 0)
             for (int i = tid; i < G * hd; i += kAttnThreads) out_h[i] = 0.f;
@@ -159,12 +164,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
     const int t_begin = mask_start + split * per;
     const int t_end = min(len, t_begin + per);
 
-    const float* kr = A.k_ring + (size_t)h * A.cap * hd;
-    const float* vr = A.v_ring + (size_t)h * A.cap * hd;
+    const float* kr = A.k_ring + z * A.ring_stride + (size_t)h * A.cap * hd;
+    const float* vr = A.v_ring + z * A.ring_stride + (size_t)h * A.cap * hd;
     load_tile<VEC>(kbuf, vbuf, kr, vr, t_begin, t_end, st.start, A.cap, hd, ldk);
     if constexpr (VEC == 4) cp_async_commit();
 
-    for (int i = tid; i < G * hd; i += kAttnThreads) q_s[i] = A.q[(size_t)h * G * hd + i];
+    for (int i = tid; i < G * hd; i += kAttnThreads) q_s[i] = q_in[(size_t)h * G * hd + i];
     if (tid < G) {
         m_s[tid] = -INFINITY;
         l_s[tid] = 0.f;
@@ -246,8 +251,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
     // [n_kv, nsplit, G, 2], so the merge can read accumulators as vectors.
     const size_t acc_stride = (size_t)G * hd;  // floats per split
     const size_t ml_base = (size_t)A.n_kv * A.nsplit * acc_stride;
-    float* pacc = A.part + ((size_t)h * A.nsplit + split) * acc_stride;
-    float* pml = A.part + ml_base + ((size_t)h * A.nsplit + split) * G * 2;
+    float* pacc = part + ((size_t)h * A.nsplit + split) * acc_stride;
+    float* pml = part + ml_base + ((size_t)h * A.nsplit + split) * G * 2;
 #pragma unroll
     for (int j = 0; j < kMaxAcc; ++j) {
         const int o = tid + j * kAttnThreads;
@@ -260,7 +265,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
     __threadfence();
     __syncthreads();
     if (tid == 0) {
-        const unsigned ticket = atomicAdd(&A.tickets[h], 1u);
+        const unsigned ticket = atomicAdd(&tickets[h], 1u);
         flag_s[0] = (ticket == (unsigned)(n_active - 1)) ? 1 : 0;
     }
     __syncthreads();
@@ -268,8 +273,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
     __threadfence();
 
     // Last CTA of this kv head: merge weights w_s = exp(m_s - M) / L once per head ...
-    const float* bacc = A.part + (size_t)h * A.nsplit * acc_stride;
-    const float* bml = A.part + ml_base + (size_t)h * A.nsplit * G * 2;
+    const float* bacc = part + (size_t)h * A.nsplit * acc_stride;
+    const float* bml = part + ml_base + (size_t)h * A.nsplit * G * 2;
     for (int g = warp; g < G; g += kAttnThreads / 32) {
         float ms[2], ls[2];
 #pragma unroll
@@ -321,7 +326,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
         }
         *reinterpret_cast<T*>(out_h + (size_t)o * VEC) = sum;
     }
-    if (tid == 0) A.tickets[h] = 0u;
+    if (tid == 0) tickets[h] = 0u;
 }
 
 }  // namespace
@@ -359,7 +364,7 @@ cudaError_t attn_prepare(int /*dev*/) {
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.n_kv, a.nsplit, 1);
+    cfg.gridDim = dim3(a.n_kv, a.nsplit, a.n_streams > 1 ? a.n_streams : 1);
     cfg.blockDim = dim3(kAttnThreads, 1, 1);
     cfg.dynamicSmemBytes = attn_smem_bytes(a.n_heads, a.n_kv, a.hd);
     cfg.stream = s;

@@ -112,16 +112,165 @@ __device__ __forceinline__ Item item_of(const BgArgs& A, int i) {
     return it;
 }
 
-// Final values of one row r of a tile for every stream: y[b] times the
-// stream's RMSNorm factor inv[b].
-__device__ __forceinline__ void bg_epilogue(const BgArgs& A, int r, const float (&y)[8], const float (&inv)[8]) {
+constexpr unsigned kFull = 0xFFFFFFFFu;
+
+// Small shared state of the epilogue warpgroup.
+struct EpiShared {
+    float inv[8];     // per-stream RMSNorm factor
+    float red[4][8];  // per-warp partial sums / maxima
+    int redi[4][8];   // per-warp argmax indices
+    int flag;         // this item completes its tile
+};
+
+// Final values y[b] of row `row` of tile `tile` for every stream, after the
+// split sum.  Runs on all 128 threads of the epilogue warpgroup (warp ew);
+// rows beyond A.rows hold zeros and store nothing.
+__device__ __forceinline__ void bg_epilogue(const BgArgs& A, int tile, int row, int lane, int ew, float (&y)[8],
+                                            EpiShared* es) {
+    const int r = tile * kBM + row;
+    const bool live = r < A.rows;
     if (A.epi == BG_STORE) {
-        if (r < A.rows) {
+        if (live) {
             const float bias = A.bias ? A.bias[r] : 0.0f;
 #pragma unroll
             for (int b = 0; b < 8; ++b)
-                if (b < A.B) A.y[(size_t)b * A.y_stride + r] = __fadd_rn(bias, __fmul_rn(inv[b], y[b]));
+                if (b < A.B) A.y[(size_t)b * A.y_stride + r] = A.bias ? __fadd_rn(bias, y[b]) : y[b];
         }
+    } else if (A.epi == BG_QKV) {
+        // RoPE pairs (2p, 2p + 1) sit in adjacent lanes (math.rs:58-61, unfused).
+        float partner[8];
+#pragma unroll
+        for (int b = 0; b < 8; ++b) partner[b] = __shfl_xor_sync(kFull, y[b], 1);
+        if (!live) return;
+        const int half = A.head_dim / 2;
+        if (r < A.q_dim + A.kv_dim) {
+            const bool is_q = r < A.q_dim;
+            const int rr = is_q ? r : r - A.q_dim;
+            const int d = rr % A.head_dim, h = rr / A.head_dim;
+            const bool odd = d & 1;
+#pragma unroll
+            for (int b = 0; b < 8; ++b) {
+                if (b >= A.B) continue;
+                long long pos = A.steps[b].pos;
+                if (pos < 0 || pos >= A.max_pos) {
+                    if (row == 0) raise_error(A.err, ERR_POS_RANGE);
+                    pos = 0;
+                }
+                const float c = A.rope_cos[pos * half + d / 2], sn = A.rope_sin[pos * half + d / 2];
+                const float ya = odd ? partner[b] : y[b], yb = odd ? y[b] : partner[b];
+                const float o = odd ? __fadd_rn(__fmul_rn(ya, sn), __fmul_rn(yb, c))
+                                    : __fsub_rn(__fmul_rn(ya, c), __fmul_rn(yb, sn));
+                if (is_q) {
+                    A.y[(size_t)b * A.y_stride + r] = o;
+                } else {
+                    const KvState post =
+                        kv_after_single_append(A.kv_state[(size_t)b * A.kv_state_stride], A.kv_window, A.ring_cap);
+                    const int slot = (post.start + post.len - 1) % A.ring_cap;
+                    A.k_ring[(size_t)b * A.ring_stride + ((size_t)h * A.ring_cap + slot) * A.head_dim + d] = o;
+                }
+            }
+        } else {
+            const int rr = r - A.q_dim - A.kv_dim;
+            const int d = rr % A.head_dim, h = rr / A.head_dim;
+#pragma unroll
+            for (int b = 0; b < 8; ++b) {
+                if (b >= A.B) continue;
+                const KvState post =
+                    kv_after_single_append(A.kv_state[(size_t)b * A.kv_state_stride], A.kv_window, A.ring_cap);
+                const int slot = (post.start + post.len - 1) % A.ring_cap;
+                A.v_ring[(size_t)b * A.ring_stride + ((size_t)h * A.ring_cap + slot) * A.head_dim + d] = y[b];
+            }
+        }
+    } else if (A.epi == BG_SWIGLU) {
+        // rows 2j (w1) and 2j + 1 (w3): act[j] = silu(gate) * up (decoder.rs:147-150)
+        float up[8];
+#pragma unroll
+        for (int b = 0; b < 8; ++b) up[b] = __shfl_xor_sync(kFull, y[b], 1);
+        if (live && !(r & 1)) {
+            const int j = r >> 1;
+#pragma unroll
+            for (int b = 0; b < 8; ++b) {
+                if (b >= A.B) continue;
+                const float sg = __fdiv_rn(y[b], __fadd_rn(1.0f, expf(-y[b])));
+                A.y[(size_t)b * A.y_stride + j] = __fmul_rn(sg, up[b]);
+            }
+        }
+    } else if (A.epi == BG_RESID) {
+        // y = resid + W x (decoder.rs:136-139, 151-152), plus this tile's sums of
+        // squares of the new hidden state for the next RMSNorm.
+        float sq[8];
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            sq[b] = 0.0f;
+            if (live && b < A.B) {
+                const float v = __fadd_rn(A.resid[(size_t)b * A.y_stride + r], y[b]);
+                A.y[(size_t)b * A.y_stride + r] = v;
+                sq[b] = __fmul_rn(v, v);
+            }
+        }
+        if (A.ssp_out) {
+#pragma unroll
+            for (int b = 0; b < 8; ++b)
+#pragma unroll
+                for (int o = 16; o; o >>= 1) sq[b] += __shfl_xor_sync(kFull, sq[b], o);
+            if (lane == 0)
+#pragma unroll
+                for (int b = 0; b < 8; ++b) es->red[ew][b] = sq[b];
+            named_barrier_sync(2, 128);
+            if (row < 8) {
+                const int b = row;
+                A.ssp_out[(size_t)tile * 8 + b] = ((es->red[0][b] + es->red[1][b]) + es->red[2][b]) + es->red[3][b];
+            }
+            named_barrier_sync(2, 128);
+        }
+    } else if (A.epi == BG_ARGMAX) {
+        // logits (optional) and the tile's best (value, lowest index) per stream
+        float best[8];
+        int bi[8];
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            best[b] = -INFINITY;
+            bi[b] = 0x7FFFFFFF;
+            if (live && b < A.B) {
+                if (A.y) A.y[(size_t)b * A.y_stride + r] = y[b];
+                if (y[b] > best[b]) {
+                    best[b] = y[b];
+                    bi[b] = r;
+                }
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+                const float ov = __shfl_xor_sync(kFull, best[b], o);
+                const int oi = __shfl_xor_sync(kFull, bi[b], o);
+                if (ov > best[b] || (ov == best[b] && oi < bi[b])) {
+                    best[b] = ov;
+                    bi[b] = oi;
+                }
+            }
+        }
+        if (lane == 0)
+#pragma unroll
+            for (int b = 0; b < 8; ++b) {
+                es->red[ew][b] = best[b];
+                es->redi[ew][b] = bi[b];
+            }
+        named_barrier_sync(2, 128);
+        if (row < 8) {
+            const int b = row;
+            float bv = es->red[0][b];
+            int bix = es->redi[0][b];
+            for (int w = 1; w < 4; ++w)
+                if (es->red[w][b] > bv || (es->red[w][b] == bv && es->redi[w][b] < bix)) {
+                    bv = es->red[w][b];
+                    bix = es->redi[w][b];
+                }
+            A.am_part[(size_t)tile * 8 + b].v = bv;
+            A.am_part[(size_t)tile * 8 + b].i = bix;
+        }
+        named_barrier_sync(2, 128);
     }
 }
 
@@ -134,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
     uint64_t* acc_full = empty + kStages;  // [2]
     uint64_t* acc_empty = acc_full + 2;    // [2]
     uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(acc_empty + 2);
-    int* flag_s = reinterpret_cast<int*>(tmem_base_s + 1);
+    EpiShared* es = reinterpret_cast<EpiShared*>(tmem_base_s + 4);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n_items = A.tiles * A.splits;
@@ -198,19 +347,26 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
 
     pdl_wait_prior_grids();
 
-    // Per-stream RMSNorm factor, applied to the row sums (y = inv * W (x * g)).
-    float inv[8];
-#pragma unroll
-    for (int b = 0; b < 8; ++b) inv[b] = 1.0f;
+    // This launch commits the single-token append of the layer's cache of
+    // every stream (the attention launch before it read the old state).
+    if (A.kv_commit && blockIdx.x == 0 && tid >= 32 && tid < 32 + A.B) {
+        KvState* st = A.kv_commit + (size_t)(tid - 32) * A.kv_state_stride;
+        *st = kv_after_single_append(*st, A.kv_window, A.ring_cap);
+    }
+    // Per-stream RMSNorm factor from the producer's partial sums of squares
+    // (math.rs:22: inv = 1 / sqrt(sum / dim + eps)), applied in the X prologue.
     if (A.norm_w) {
-#pragma unroll
-        for (int b = 0; b < 8; ++b) {
+        if (tid >= 32 && tid < 40) {
+            const int b = tid - 32;
+            float inv = 1.0f;
             if (b < A.B) {
                 float ss = 0.0f;
                 for (int p = 0; p < A.ssp_parts; ++p) ss += __ldcg(A.ssp + (size_t)p * 8 + b);
-                inv[b] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)A.K), A.eps)));
+                inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)A.K), A.eps)));
             }
+            es->inv[b] = inv;
         }
+        named_barrier_sync(1, kWorkers);
     }
 
     int cur_ks = -1;
@@ -237,12 +393,13 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
                     const float4 a0 = __ldcg(reinterpret_cast<const float4*>(xp));
                     const float4 a1 = __ldcg(reinterpret_cast<const float4*>(xp + 4));
                     float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                    if (A.norm_w) {
+                    if (A.norm_w) {  // math.rs:23-24: x * inv * w, in that order
                         const float4 g0 = __ldg(reinterpret_cast<const float4*>(A.norm_w + kbase + k));
                         const float4 g1 = __ldg(reinterpret_cast<const float4*>(A.norm_w + kbase + k + 4));
                         const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+                        const float inv = es->inv[b];
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(v[j], gv[j]);
+                        for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(__fmul_rn(v[j], inv), gv[j]);
                     }
 #pragma unroll
                     for (int j = 0; j < 8; j += 2) {
@@ -302,7 +459,6 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
         if (warp >= 4) {
             const int ew = warp - 4;        // TMEM lanes 32*ew .. 32*ew + 31
             const int row = ew * 32 + lane; // row inside the tile
-            const int r = it.tile * kBM + row;
             if (!mbar_wait(&acc_full[ab], (local >> 1) & 1)) raise_error(A.err, ERR_FULL_WAIT);
             tmem_fence_after();
             uint32_t raw[16];
@@ -323,10 +479,10 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
                 named_barrier_sync(2, 128);
                 if (ew == 0 && lane == 0) {
                     const unsigned t = atomicAdd(&A.tickets[it.tile], 1u);
-                    *flag_s = (t == (unsigned)(A.splits - 1)) ? 1 : 0;
+                    es->flag = (t == (unsigned)(A.splits - 1)) ? 1 : 0;
                 }
                 named_barrier_sync(2, 128);
-                final_item = *flag_s != 0;
+                final_item = es->flag != 0;
                 named_barrier_sync(2, 128);  // flag read by all before the next item rewrites it
                 if (final_item) {
                     __threadfence();
@@ -342,7 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
                     if (ew == 0 && lane == 0) A.tickets[it.tile] = 0u;
                 }
             }
-            if (final_item) bg_epilogue(A, r, y, inv);
+            if (final_item) bg_epilogue(A, it.tile, row, lane, ew, y, es);
         }
     }
 
@@ -373,13 +529,117 @@ __global__ void tile_weights_kernel(const uint16_t* __restrict__ src, uint16_t* 
     }
 }
 
+// Embedding rows of every stream's token (bf16 widened exactly, as
+// weights.rs:77-81) into hid [B, dim], with per-128-column sums of squares
+// for the first layer's RMSNorm.  Grid (ceil(dim / 128), B), 128 threads.
+__global__ void __launch_bounds__(128) bg_embed_kernel(const uint16_t* __restrict__ embed, int vocab, int dim,
+                                                       const StepState* steps, float* hid, float* ssp,
+                                                       unsigned* err) {
+    pdl_allow_dependents();
+    pdl_wait_prior_grids();
+    __shared__ float red[4];
+    const int b = blockIdx.y, e = blockIdx.x * 128 + threadIdx.x;
+    int tok = steps[b].tok;
+    if (tok < 0 || tok >= vocab) {
+        if (threadIdx.x == 0 && blockIdx.x == 0) raise_error(err, ERR_TOKEN_RANGE);
+        tok = 0;
+    }
+    float v = 0.0f;
+    if (e < dim) {
+        v = bf16_bits_to_f32(embed[(size_t)tok * dim + e]);
+        hid[(size_t)b * dim + e] = v;
+    }
+    float sq = __fmul_rn(v, v);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(kFull, sq, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+    __syncthreads();
+    if (threadIdx.x == 0) ssp[(size_t)blockIdx.x * 8 + b] = ((red[0] + red[1]) + red[2]) + red[3];
+}
+
+// Per-stream argmax over the LM head's per-tile candidates (lowest index on
+// ties), then the step bookkeeping of that stream.  Grid B, 256 threads.
+__global__ void __launch_bounds__(256) bg_argmax_final_kernel(const ArgmaxPart* parts, int n_tiles,
+                                                              StepState* steps, int32_t* tok_out) {
+    pdl_allow_dependents();
+    pdl_wait_prior_grids();
+    __shared__ float sv[8];
+    __shared__ int si[8];
+    const int b = blockIdx.x;
+    float best = -INFINITY;
+    int bi = 0x7FFFFFFF;
+    for (int t = threadIdx.x; t < n_tiles; t += blockDim.x) {
+        const ArgmaxPart p = parts[(size_t)t * 8 + b];
+        if (p.v > best || (p.v == best && p.i < bi)) {
+            best = p.v;
+            bi = p.i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(kFull, best, o);
+        const int oi = __shfl_xor_sync(kFull, bi, o);
+        if (ov > best || (ov == best && oi < bi)) {
+            best = ov;
+            bi = oi;
+        }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sv[warp] = best;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+            if (sv[w] > best || (sv[w] == best && si[w] < bi)) {
+                best = sv[w];
+                bi = si[w];
+            }
+        if (bi == 0x7FFFFFFF) bi = 0;  // all logits NaN: token 0, as a scan from index 0 keeps
+        StepState* st = steps + b;
+        st->next_tok = bi;
+        if (st->greedy) st->tok = bi;
+        if (st->advance) st->pos += 1;
+        if (tok_out) tok_out[b] = bi;
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_bg_embed(const uint16_t* embed, int vocab, int dim, const StepState* steps, int B, float* hid,
+                            float* ssp, unsigned* err, cudaStream_t s, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((dim + 127) / 128, B, 1);
+    cfg.blockDim = dim3(128, 1, 1);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, bg_embed_kernel, embed, vocab, dim, steps, hid, ssp, err);
+}
+
+cudaError_t launch_bg_argmax_final(const ArgmaxPart* parts, int n_tiles, StepState* steps, int B,
+                                   int32_t* tok_out, cudaStream_t s, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(B, 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, bg_argmax_final_kernel, parts, n_tiles, steps, tok_out);
+}
 
 size_t bgemm_smem_bytes(int K, int splits) {
     const int kbt = K / kBK;
     const int max_kb = (kbt + splits - 1) / splits;
     const size_t xslab = (size_t)max_kb * 4 * 512;
-    return (size_t)kStages * kStageBytes + xslab + (2 * kStages + 4) * 8 + 16;
+    return (size_t)kStages * kStageBytes + xslab + (2 * kStages + 4) * 8 + 16 + sizeof(EpiShared);
 }
 
 int bgemm_xslab_bytes(int K, int splits) {

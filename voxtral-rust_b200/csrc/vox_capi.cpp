@@ -7,6 +7,7 @@
 // launches.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -103,7 +104,62 @@ struct LayerDev {
     float* attn_norm = nullptr;
     float* ffn_norm = nullptr;
     bool ready = false;
+    // The same matrices pre-tiled for the tensor-core multi-stream GEMM
+    // (launch_tile_weights); rebuilt after every upload.
+    unsigned char *wqkv_t = nullptr, *wo_t = nullptr, *w13_t = nullptr, *w2_t = nullptr;
+    bool tiled = false;
 };
+
+// Launch shape of one multi-stream GEMM (vox_bgemm.cu).
+struct BgPlan {
+    int rows = 0, K = 0, tiles = 0, kbt = 0, splits = 1, grid = 1, xslab = 0;
+};
+
+// Device buffers of the multi-stream step, sized for 8 streams.
+struct BatchBufs {
+    bool ready = false;
+    float *hid = nullptr, *hmid = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr;
+    float* ssp = nullptr;        // RMSNorm partial sums [dim tiles, 8]
+    float* part = nullptr;       // split-K partial tiles
+    float* attn_part = nullptr;  // attention split partials, all streams
+    ArgmaxPart* am = nullptr;    // [vocab tiles, 8]
+    unsigned* tickets = nullptr;       // GEMM tiles
+    unsigned* attn_tickets = nullptr;  // [8, n_kv]
+    StepState* steps = nullptr;        // [8]
+    int32_t* tok_out = nullptr;        // [8]
+    StepState* h_steps = nullptr;      // pinned [8]
+    int32_t* h_tok = nullptr;          // pinned token history
+    size_t h_tok_cap = 0;
+    BgPlan p_qkv, p_o, p_w13, p_w2, p_head;
+};
+
+// K splits and grid of a multi-stream GEMM: the split count that minimises
+// the busiest CTA's K blocks (items per CTA x blocks per item), with at most
+// 40 K blocks per split so the split's X operand fits in shared memory.
+BgPlan make_bgplan(int rows, int K, int num_sms) {
+    BgPlan p;
+    p.rows = rows;
+    p.K = K;
+    p.tiles = (rows + 127) / 128;
+    p.kbt = K / 64;
+    long long best = -1;
+    for (int s = 1; s <= p.kbt && s <= 64; ++s) {
+        const int per = (p.kbt + s - 1) / s;
+        if (per > 40) continue;
+        int grid = num_sms - num_sms % s;
+        if (grid < s) grid = s;
+        const long long items = (long long)p.tiles * s;
+        if (grid > items) grid = (int)items;
+        const long long cost = ((items + grid - 1) / grid) * per;
+        if (best < 0 || cost < best) {
+            best = cost;
+            p.splits = s;
+            p.grid = grid;
+        }
+    }
+    p.xslab = bgemm_xslab_bytes(K, p.splits);
+    return p;
+}
 
 }  // namespace
 
@@ -149,19 +205,32 @@ struct vox_ctx {
     int tok_splits = 1;
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
+    // multi-stream path
+    unsigned char* head_t = nullptr;
+    bool head_tiled = false;
+    BatchBufs bb;
 };
 
+// A rolling cache of one stream, or of n_streams independent streams laid
+// out stream-major so that stream s is itself a single-stream cache (a view).
 struct vox_kv {
     vox_ctx* ctx = nullptr;
     size_t n_layers = 0, n_kv = 0, hd = 0, window = 0, cap = 0;
-    float* k = nullptr;          // [n_layers, n_kv, cap, hd]
+    size_t n_streams = 1;
+    float* k = nullptr;          // [n_streams, n_layers, n_kv, cap, hd]
     float* v = nullptr;
-    KvState* dstate = nullptr;   // [n_layers]
-    std::vector<HostKv> hs;
+    KvState* dstate = nullptr;   // [n_streams, n_layers]
+    std::vector<HostKv> hs_store;  // owner: host mirror [n_streams, n_layers]
+    HostKv* hs = nullptr;          // [n_layers] of this cache (stream 0 of an owner)
+    vox_kv* parent = nullptr;      // set on a stream view
+    std::vector<vox_kv*> views;    // owner: views by stream, created on demand
     cudaGraphExec_t step_graph = nullptr;
     uint64_t graph_kernels = 0;
     TokLayer* tok_layers = nullptr;  // device table of per-layer pointers (token kernel)
+    cudaGraphExec_t batch_graph = nullptr;  // multi-stream step over all streams
+    uint64_t batch_kernels = 0;
     size_t layer_elems() const { return n_kv * cap * hd; }
+    size_t stream_elems() const { return n_layers * layer_elems(); }
 };
 
 namespace {
@@ -176,6 +245,13 @@ int check_device_errors(vox_ctx* c) {
             // An aborted step leaves barrier counters and tickets half-advanced.
             if (c->tok_bar) CUDA_TRY(cudaMemsetAsync(c->tok_bar, 0, 2 * sizeof(unsigned long long), c->stream));
             CUDA_TRY(cudaMemsetAsync(c->tickets, 0, c->cfg.n_kv_heads * sizeof(unsigned), c->stream));
+            if (c->bb.ready) {
+                size_t tiles = 0;
+                for (const BgPlan* p : {&c->bb.p_qkv, &c->bb.p_o, &c->bb.p_w13, &c->bb.p_w2, &c->bb.p_head})
+                    tiles = std::max(tiles, (size_t)p->tiles);
+                CUDA_TRY(cudaMemsetAsync(c->bb.tickets, 0, tiles * sizeof(unsigned), c->stream));
+                CUDA_TRY(cudaMemsetAsync(c->bb.attn_tickets, 0, 8 * c->cfg.n_kv_heads * sizeof(unsigned), c->stream));
+            }
         }
         CUDA_TRY(cudaStreamSynchronize(c->stream));
         if (bits & (ERR_FULL_WAIT | ERR_EMPTY_WAIT | ERR_DRAIN_WAIT | ERR_GRID_WAIT))
@@ -327,6 +403,7 @@ int upload_layer(vox_ctx* c, size_t layer, const WS* w) {
     CUDA_TRY(cudaMemcpy(L.attn_norm, w->attention_norm.ptr, dim * 4, cudaMemcpyHostToDevice));
     CUDA_TRY(cudaMemcpy(L.ffn_norm, w->ffn_norm.ptr, dim * 4, cudaMemcpyHostToDevice));
     L.ready = true;
+    L.tiled = false;
     return VOX_OK;
 }
 
@@ -437,6 +514,232 @@ int enqueue_head(vox_ctx* c, bool pdl) {
     CUDA_TRY(record_launch(c, launch_gemv(c->p_head, a, EPI_ARGMAX, c->stream, pdl)));
     CUDA_TRY(record_launch(c, launch_argmax_final(c->am_part, c->p_head.grid, c->step, c->tok_out,
                                                   c->stream, pdl)));
+    return VOX_OK;
+}
+
+// ---- multi-stream step (tensor-core GEMMs, vox_bgemm.cu) ----------------------
+int batch_supported(vox_ctx* c) {
+    if (c->wsize != 2) return fail(VOX_ERR_UNSUPPORTED, "the multi-stream step needs bf16 weights");
+    const vox_decoder_config& g = c->cfg;
+    if (g.dim % 64 || c->q_dim % 64 || g.hidden_dim % 64)
+        return fail(VOX_ERR_UNSUPPORTED, "the multi-stream step needs dim, n_heads*head_dim and hidden_dim "
+                                         "to be multiples of 64");
+    return VOX_OK;
+}
+
+int tile_into(vox_ctx* c, unsigned char** dst, const void* src, int rows, int K) {
+    if (!*dst) CUDA_TRY(cudaMalloc(dst, tiled_bytes(rows, K)));
+    CUDA_TRY(record_launch(c, launch_tile_weights(static_cast<const uint16_t*>(src),
+                                                  reinterpret_cast<uint16_t*>(*dst), rows, K, c->stream)));
+    return VOX_OK;
+}
+
+// Allocate the multi-stream buffers once and (re)tile stale weights.
+int ensure_batch(vox_ctx* c) {
+    TRY(batch_supported(c));
+    BatchBufs& b = c->bb;
+    const int dim = (int)c->cfg.dim, hid = (int)c->cfg.hidden_dim, qd = (int)c->q_dim;
+    const int vocab = (int)c->opt.vocab;
+    if (!b.ready) {
+        b.p_qkv = make_bgplan((int)c->qkv_rows, dim, c->num_sms);
+        b.p_o = make_bgplan(dim, qd, c->num_sms);
+        b.p_w13 = make_bgplan(2 * hid, dim, c->num_sms);
+        b.p_w2 = make_bgplan(dim, hid, c->num_sms);
+        b.p_head = make_bgplan(vocab, dim, c->num_sms);
+        size_t part = 0, tiles = 0;
+        for (const BgPlan* p : {&b.p_qkv, &b.p_o, &b.p_w13, &b.p_w2, &b.p_head}) {
+            part = std::max(part, (size_t)p->tiles * p->splits * 128 * 8);
+            tiles = std::max(tiles, (size_t)p->tiles);
+        }
+        const size_t nkv = c->cfg.n_kv_heads, hd = c->cfg.head_dim, G = c->cfg.n_heads / nkv;
+        const size_t ns = (size_t)attn_splits_for((int)nkv, c->num_sms);
+        CUDA_TRY(dalloc(&b.hid, 8 * (size_t)dim));
+        CUDA_TRY(dalloc(&b.hmid, 8 * (size_t)dim));
+        CUDA_TRY(dalloc(&b.q, 8 * (size_t)qd));
+        CUDA_TRY(dalloc(&b.attn, 8 * (size_t)qd));
+        CUDA_TRY(dalloc(&b.act, 8 * (size_t)hid));
+        CUDA_TRY(dalloc(&b.logits, 8 * (size_t)vocab));
+        CUDA_TRY(dalloc(&b.ssp, 8 * (size_t)((dim + 127) / 128)));
+        CUDA_TRY(dalloc(&b.part, part));
+        CUDA_TRY(dalloc(&b.attn_part, 8 * nkv * ns * G * (hd + 2)));
+        CUDA_TRY(dalloc(&b.am, 8 * (size_t)b.p_head.tiles));
+        CUDA_TRY(dalloc(&b.tickets, tiles));
+        CUDA_TRY(cudaMemset(b.tickets, 0, tiles * sizeof(unsigned)));
+        CUDA_TRY(dalloc(&b.attn_tickets, 8 * nkv));
+        CUDA_TRY(cudaMemset(b.attn_tickets, 0, 8 * nkv * sizeof(unsigned)));
+        CUDA_TRY(dalloc(&b.steps, 8));
+        CUDA_TRY(cudaMemset(b.steps, 0, 8 * sizeof(StepState)));
+        CUDA_TRY(dalloc(&b.tok_out, 8));
+        CUDA_TRY(cudaMallocHost(&b.h_steps, 8 * sizeof(StepState)));
+        b.ready = true;
+    }
+    const int kvd = (int)c->kv_dim;
+    for (auto& L : c->layers) {
+        if (L.tiled) continue;
+        TRY(tile_into(c, &L.wqkv_t, L.wqkv, qd + 2 * kvd, dim));
+        TRY(tile_into(c, &L.wo_t, L.wo, dim, qd));
+        TRY(tile_into(c, &L.w13_t, L.w13, 2 * hid, dim));
+        TRY(tile_into(c, &L.w2_t, L.w2, dim, hid));
+        L.tiled = true;
+    }
+    if (!c->head_tiled) {
+        TRY(tile_into(c, &c->head_t, c->lm_head, vocab, dim));
+        c->head_tiled = true;
+    }
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    return VOX_OK;
+}
+
+BgArgs bg_args(vox_ctx* c, const BgPlan& p, const unsigned char* wt, int B, int epi) {
+    BgArgs a{};
+    a.wt = wt;
+    a.rows = p.rows;
+    a.K = p.K;
+    a.tiles = p.tiles;
+    a.kbt = p.kbt;
+    a.splits = p.splits;
+    a.B = B;
+    a.xslab_bytes = p.xslab;
+    a.eps = c->cfg.norm_eps;
+    a.epi = epi;
+    a.part = c->bb.part;
+    a.tickets = c->bb.tickets;
+    a.err = c->err;
+    a.ssp_parts = (int)((c->cfg.dim + 127) / 128);
+    return a;
+}
+
+// One token for each of the B streams of `kv`: embed, 26 x (QKV + RoPE + ring
+// append, attention, o-proj + residual + append commit, w1|w3 + SwiGLU, w2 +
+// residual), final RMSNorm + LM head + per-stream argmax.  The GEMMs read
+// each weight once for all streams.
+int enqueue_batch_step(vox_ctx* c, vox_kv* kv, bool pdl) {
+    BatchBufs& bb = c->bb;
+    const int B = (int)kv->n_streams;
+    const int dim = (int)c->cfg.dim, hid = (int)c->cfg.hidden_dim, qd = (int)c->q_dim;
+    const long long ring_stride = (long long)kv->stream_elems();
+    const int cap = (int)kv->cap, win = (int)kv->window;
+    const int nkv = (int)c->cfg.n_kv_heads, hd = (int)c->cfg.head_dim, G = (int)(c->cfg.n_heads / nkv);
+    int nsplit = attn_splits_for(nkv * B, c->num_sms);
+    CUDA_TRY(record_launch(c, launch_bg_embed(c->embed, (int)c->opt.vocab, dim, bb.steps, B, bb.hid, bb.ssp,
+                                              c->err, c->stream, pdl)));
+    for (size_t l = 0; l < c->layers.size(); ++l) {
+        const LayerDev& L = c->layers[l];
+        float* kr = kv->k + l * kv->layer_elems();
+        float* vr = kv->v + l * kv->layer_elems();
+        KvState* st = kv->dstate + l;
+
+        BgArgs a = bg_args(c, bb.p_qkv, L.wqkv_t, B, BG_QKV);
+        a.x = bb.hid;
+        a.x_stride = dim;
+        a.norm_w = L.attn_norm;
+        a.ssp = bb.ssp;
+        a.y = bb.q;
+        a.y_stride = qd;
+        a.q_dim = qd;
+        a.kv_dim = (int)c->kv_dim;
+        a.head_dim = hd;
+        a.rope_cos = c->rope_cos;
+        a.rope_sin = c->rope_sin;
+        a.max_pos = c->max_pos;
+        a.steps = bb.steps;
+        a.kv_state = st;
+        a.kv_state_stride = (long long)kv->n_layers;
+        a.k_ring = kr;
+        a.v_ring = vr;
+        a.ring_stride = ring_stride;
+        a.ring_cap = cap;
+        a.kv_window = win;
+        CUDA_TRY(record_launch(c, launch_bgemm(a, bb.p_qkv.grid, c->stream, pdl)));
+
+        AttnArgs at{};
+        at.q = bb.q;
+        at.k_ring = kr;
+        at.v_ring = vr;
+        at.n_heads = (int)c->cfg.n_heads;
+        at.n_kv = nkv;
+        at.hd = hd;
+        at.cap = cap;
+        at.cfg_window = (int)c->cfg.sliding_window;
+        at.st = st;
+        at.pre_append = 1;
+        at.kv_window = win;
+        at.nsplit = nsplit;
+        at.part = bb.attn_part;
+        at.tickets = bb.attn_tickets;
+        at.out = bb.attn;
+        at.scale = 1.0f / sqrtf((float)hd);
+        at.err = c->err;
+        at.n_streams = B;
+        at.q_stride = qd;
+        at.ring_stride = ring_stride;
+        at.out_stride = qd;
+        at.part_stride = (long long)nkv * nsplit * G * (hd + 2);
+        at.st_stride = (long long)kv->n_layers;
+        CUDA_TRY(record_launch(c, launch_attention(at, c->stream, pdl)));
+
+        a = bg_args(c, bb.p_o, L.wo_t, B, BG_RESID);
+        a.x = bb.attn;
+        a.x_stride = qd;
+        a.y = bb.hmid;
+        a.y_stride = dim;
+        a.resid = bb.hid;
+        a.ssp_out = bb.ssp;
+        a.kv_commit = st;
+        a.kv_state_stride = (long long)kv->n_layers;
+        a.kv_window = win;
+        a.ring_cap = cap;
+        CUDA_TRY(record_launch(c, launch_bgemm(a, bb.p_o.grid, c->stream, pdl)));
+
+        a = bg_args(c, bb.p_w13, L.w13_t, B, BG_SWIGLU);
+        a.x = bb.hmid;
+        a.x_stride = dim;
+        a.norm_w = L.ffn_norm;
+        a.ssp = bb.ssp;
+        a.y = bb.act;
+        a.y_stride = hid;
+        CUDA_TRY(record_launch(c, launch_bgemm(a, bb.p_w13.grid, c->stream, pdl)));
+
+        a = bg_args(c, bb.p_w2, L.w2_t, B, BG_RESID);
+        a.x = bb.act;
+        a.x_stride = hid;
+        a.y = bb.hid;
+        a.y_stride = dim;
+        a.resid = bb.hmid;
+        a.ssp_out = bb.ssp;
+        CUDA_TRY(record_launch(c, launch_bgemm(a, bb.p_w2.grid, c->stream, pdl)));
+    }
+    BgArgs a = bg_args(c, bb.p_head, c->head_t, B, BG_ARGMAX);
+    a.x = bb.hid;
+    a.x_stride = dim;
+    a.norm_w = c->final_norm;
+    a.ssp = bb.ssp;
+    a.y = bb.logits;
+    a.y_stride = (long long)c->opt.vocab;
+    a.am_part = bb.am;
+    CUDA_TRY(record_launch(c, launch_bgemm(a, bb.p_head.grid, c->stream, pdl)));
+    CUDA_TRY(record_launch(c, launch_bg_argmax_final(bb.am, bb.p_head.tiles, bb.steps, B, bb.tok_out, c->stream,
+                                                     pdl)));
+    return VOX_OK;
+}
+
+int build_batch_graph(vox_ctx* c, vox_kv* kv) {
+    if (kv->batch_graph) return VOX_OK;
+    const uint64_t before = c->launches;
+    CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_batch_step(c, kv, true);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+    if (rc != VOX_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    CUDA_TRY(e);
+    e = cudaGraphInstantiate(&kv->batch_graph, g, 0);
+    cudaGraphDestroy(g);
+    CUDA_TRY(e);
+    kv->batch_kernels = c->launches - before;
+    c->launches = before;
     return VOX_OK;
 }
 
@@ -570,7 +873,7 @@ int launch_graph(vox_ctx* c, vox_kv* kv) {
 }
 
 void mirror_single_append_all(vox_kv* kv) {
-    for (auto& s : kv->hs) host_append(s, 1, kv->window, kv->cap);
+    for (size_t l = 0; l < kv->n_layers; ++l) host_append(kv->hs[l], 1, kv->window, kv->cap);
 }
 
 int upload_state(vox_kv* kv, size_t layer) {
@@ -628,6 +931,10 @@ void vox_ctx_destroy(vox_ctx* c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     while (!c->caches.empty()) vox_kv_destroy(c->caches.back());
     for (auto& L : c->layers) {
+        cudaFree(L.wqkv_t);
+        cudaFree(L.wo_t);
+        cudaFree(L.w13_t);
+        cudaFree(L.w2_t);
         cudaFree(L.wqkv);
         cudaFree(L.wo);
         cudaFree(L.w13);
@@ -640,6 +947,15 @@ void vox_ctx_destroy(vox_ctx* c) {
                     c->tok_out, c->err, c->scratch, c->tok_bar, c->tok_part};
     for (void* p : ptrs)
         if (p) cudaFree(p);
+    {
+        BatchBufs& b = c->bb;
+        void* bp[] = {c->head_t, b.hid, b.hmid, b.q, b.attn, b.act, b.logits, b.ssp, b.part, b.attn_part, b.am,
+                      b.tickets, b.attn_tickets, b.steps, b.tok_out};
+        for (void* p : bp)
+            if (p) cudaFree(p);
+        if (b.h_steps) cudaFreeHost(b.h_steps);
+        if (b.h_tok) cudaFreeHost(b.h_tok);
+    }
     if (c->h_steps) cudaFreeHost(c->h_steps);
     if (c->h_tok) cudaFreeHost(c->h_tok);
     if (c->h_err) cudaFreeHost(c->h_err);
@@ -830,6 +1146,7 @@ int vox_ctx_upload_lm_head_bf16(vox_ctx* c, const uint16_t* head, size_t len) {
         CUDA_TRY(cudaStreamSynchronize(c->stream));
     }
     c->head_ready = true;
+    c->head_tiled = false;
     return VOX_OK;
 }
 
@@ -863,6 +1180,7 @@ int vox_ctx_init_random(vox_ctx* c, uint64_t seed, float stdv) {
         CUDA_TRY(launch_fill_f32(L.attn_norm, 1.0f, dim, s));
         CUDA_TRY(launch_fill_f32(L.ffn_norm, 1.0f, dim, s));
         L.ready = true;
+        L.tiled = false;
     }
     if (c->opt.vocab) {
         const long long V = (long long)c->opt.vocab;
@@ -873,6 +1191,7 @@ int vox_ctx_init_random(vox_ctx* c, uint64_t seed, float stdv) {
         CUDA_TRY(launch_gen_matrix(c->lm_head, ws, seed, 1000001, stdv, V, dim, 1, 0, s));
         CUDA_TRY(launch_fill_f32(c->final_norm, 1.0f, dim, s));
         c->embed_ready = c->head_ready = true;
+        c->head_tiled = false;
     }
     CUDA_TRY(cudaStreamSynchronize(s));
     return VOX_OK;
@@ -942,12 +1261,13 @@ int vox_ctx_event_elapsed_ms(vox_ctx* c, int a, int b, float* ms) {
 uint64_t vox_ctx_kernel_launches(vox_ctx* c) { return c ? c->launches : 0; }
 
 // ---- KV cache ----------------------------------------------------------------
-int vox_kv_create_ex(vox_ctx* c, size_t n_layers, size_t n_kv, size_t hd, size_t window, size_t cap,
-                     vox_kv** out) {
+static int create_cache(vox_ctx* c, size_t n_streams, size_t n_layers, size_t n_kv, size_t hd, size_t window,
+                        size_t cap, vox_kv** out) {
     if (!c || !out) return fail(VOX_ERR_INVALID_ARG, "null argument");
     *out = nullptr;
     if (n_layers == 0 || n_kv == 0 || hd == 0 || window == 0)
         return fail(VOX_ERR_INVALID_ARG, "n_layers, n_kv_heads, head_dim and sliding_window must be > 0");
+    if (n_streams == 0 || n_streams > 8) return fail(VOX_ERR_UNSUPPORTED, "n_streams must be 1..8");
     if (cap < window) return fail(VOX_ERR_INVALID_ARG, "capacity below the window");
     if (cap > (size_t)INT32_MAX / 2) return fail(VOX_ERR_UNSUPPORTED, "capacity too large");
     CUDA_TRY(cudaSetDevice(c->dev));
@@ -958,11 +1278,14 @@ int vox_kv_create_ex(vox_ctx* c, size_t n_layers, size_t n_kv, size_t hd, size_t
     kv->hd = hd;
     kv->window = window;
     kv->cap = cap;
-    kv->hs.assign(n_layers, HostKv{});
-    cudaError_t e = dalloc(&kv->k, n_layers * kv->layer_elems());
-    if (e == cudaSuccess) e = dalloc(&kv->v, n_layers * kv->layer_elems());
-    if (e == cudaSuccess) e = dalloc(&kv->dstate, n_layers);
-    if (e == cudaSuccess) e = cudaMemset(kv->dstate, 0, n_layers * sizeof(KvState));
+    kv->n_streams = n_streams;
+    kv->hs_store.assign(n_streams * n_layers, HostKv{});
+    kv->hs = kv->hs_store.data();
+    kv->views.assign(n_streams, nullptr);
+    cudaError_t e = dalloc(&kv->k, n_streams * kv->stream_elems());
+    if (e == cudaSuccess) e = dalloc(&kv->v, n_streams * kv->stream_elems());
+    if (e == cudaSuccess) e = dalloc(&kv->dstate, n_streams * n_layers);
+    if (e == cudaSuccess) e = cudaMemset(kv->dstate, 0, n_streams * n_layers * sizeof(KvState));
     if (e != cudaSuccess) {
         vox_kv_destroy(kv);
         return fail(e == cudaErrorMemoryAllocation ? VOX_ERR_OOM : VOX_ERR_CUDA, "cache allocation: %s",
@@ -973,12 +1296,73 @@ int vox_kv_create_ex(vox_ctx* c, size_t n_layers, size_t n_kv, size_t hd, size_t
     return VOX_OK;
 }
 
+// Single-stream entry points take a one-stream cache or a stream view.
+static int single_stream(const vox_kv* kv) {
+    if (kv->n_streams != 1 && !kv->parent)
+        return fail(VOX_ERR_INVALID_ARG, "cache holds %zu streams: pass a stream view (vox_kv_stream)",
+                    kv->n_streams);
+    return VOX_OK;
+}
+
+static void release_graphs(vox_kv* kv) {
+    if (kv->step_graph) cudaGraphExecDestroy(kv->step_graph);
+    if (kv->batch_graph) cudaGraphExecDestroy(kv->batch_graph);
+    if (kv->tok_layers) cudaFree(kv->tok_layers);
+    kv->step_graph = kv->batch_graph = nullptr;
+    kv->tok_layers = nullptr;
+}
+
+int vox_kv_create_ex(vox_ctx* c, size_t n_layers, size_t n_kv, size_t hd, size_t window, size_t cap,
+                     vox_kv** out) {
+    return create_cache(c, 1, n_layers, n_kv, hd, window, cap, out);
+}
+
 int vox_kv_create(vox_ctx* c, size_t n_layers, size_t n_kv, size_t hd, size_t window, vox_kv** out) {
-    return vox_kv_create_ex(c, n_layers, n_kv, hd, window, window, out);
+    return create_cache(c, 1, n_layers, n_kv, hd, window, window, out);
+}
+
+int vox_kv_create_streams(vox_ctx* c, size_t n_streams, size_t n_layers, size_t n_kv, size_t hd, size_t window,
+                          vox_kv** out) {
+    return create_cache(c, n_streams, n_layers, n_kv, hd, window, window, out);
+}
+
+int vox_kv_n_streams(const vox_kv* kv, size_t* out) {
+    if (!kv || !out) return fail(VOX_ERR_INVALID_ARG, "bad argument");
+    *out = kv->parent ? 1 : kv->n_streams;
+    return VOX_OK;
+}
+
+int vox_kv_stream(vox_kv* kv, size_t stream, vox_kv** out) {
+    if (!kv || !out) return fail(VOX_ERR_INVALID_ARG, "null argument");
+    *out = nullptr;
+    if (kv->parent) return fail(VOX_ERR_INVALID_ARG, "already a stream view");
+    if (stream >= kv->n_streams) return fail(VOX_ERR_INVALID_ARG, "stream %zu out of range", stream);
+    if (kv->n_streams == 1) {
+        *out = kv;
+        return VOX_OK;
+    }
+    if (!kv->views[stream]) {
+        vox_kv* w = new vox_kv();
+        w->ctx = kv->ctx;
+        w->n_layers = kv->n_layers;
+        w->n_kv = kv->n_kv;
+        w->hd = kv->hd;
+        w->window = kv->window;
+        w->cap = kv->cap;
+        w->n_streams = 1;
+        w->k = kv->k + stream * kv->stream_elems();
+        w->v = kv->v + stream * kv->stream_elems();
+        w->dstate = kv->dstate + stream * kv->n_layers;
+        w->hs = kv->hs_store.data() + stream * kv->n_layers;
+        w->parent = kv;
+        kv->views[stream] = w;
+    }
+    *out = kv->views[stream];
+    return VOX_OK;
 }
 
 void vox_kv_destroy(vox_kv* kv) {
-    if (!kv) return;
+    if (!kv || kv->parent) return;  // views live as long as their cache
     vox_ctx* c = kv->ctx;
     cudaSetDevice(c->dev);
     cudaStreamSynchronize(c->stream);
@@ -987,8 +1371,12 @@ void vox_kv_destroy(vox_kv* kv) {
             c->caches.erase(c->caches.begin() + (long)i);
             break;
         }
-    if (kv->step_graph) cudaGraphExecDestroy(kv->step_graph);
-    if (kv->tok_layers) cudaFree(kv->tok_layers);
+    for (vox_kv* w : kv->views)
+        if (w) {
+            release_graphs(w);
+            delete w;
+        }
+    release_graphs(kv);
     cudaFree(kv->k);
     cudaFree(kv->v);
     cudaFree(kv->dstate);
@@ -999,13 +1387,38 @@ int vox_kv_reset(vox_kv* kv) {
     if (!kv) return fail(VOX_ERR_INVALID_ARG, "cache is null");
     CUDA_TRY(cudaSetDevice(kv->ctx->dev));
     CUDA_TRY(cudaStreamSynchronize(kv->ctx->stream));
-    kv->hs.assign(kv->n_layers, HostKv{});
-    CUDA_TRY(cudaMemset(kv->dstate, 0, kv->n_layers * sizeof(KvState)));
+    const size_t n = (kv->parent ? 1 : kv->n_streams) * kv->n_layers;
+    for (size_t i = 0; i < n; ++i) kv->hs[i] = HostKv{};
+    CUDA_TRY(cudaMemset(kv->dstate, 0, n * sizeof(KvState)));
+    return VOX_OK;
+}
+
+int vox_kv_fill_random(vox_kv* kv, size_t n_tokens, uint64_t seed, uint64_t tensor_id, float stdv) {
+    if (!kv) return fail(VOX_ERR_INVALID_ARG, "cache is null");
+    TRY(single_stream(kv));
+    if (n_tokens > kv->window) return fail(VOX_ERR_INVALID_ARG, "%zu tokens exceed the window %zu", n_tokens, kv->window);
+    vox_ctx* c = kv->ctx;
+    CUDA_TRY(cudaSetDevice(c->dev));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    std::vector<KvState> d(kv->n_layers);
+    for (size_t l = 0; l < kv->n_layers; ++l) {
+        CUDA_TRY(record_launch(c, launch_kv_fill_random(kv->k + l * kv->layer_elems(), kv->v + l * kv->layer_elems(),
+                                                        (int)kv->n_kv, (int)kv->hd, (int)kv->cap, (int)n_tokens,
+                                                        seed, tensor_id + 2 * l, tensor_id + 2 * l + 1, stdv,
+                                                        c->stream)));
+        kv->hs[l] = HostKv{n_tokens, 0, 0};
+        d[l].len = (int32_t)n_tokens;
+        d[l].start = 0;
+        d[l].pos_offset = 0;
+    }
+    CUDA_TRY(cudaMemcpyAsync(kv->dstate, d.data(), d.size() * sizeof(KvState), cudaMemcpyHostToDevice, c->stream));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
     return VOX_OK;
 }
 
 int vox_kv_append_layer(vox_kv* kv, size_t layer, const float* k_new, const float* v_new, size_t n) {
     if (!kv) return fail(VOX_ERR_INVALID_ARG, "cache is null");
+    TRY(single_stream(kv));
     if (layer >= kv->n_layers) return fail(VOX_ERR_INVALID_ARG, "layer %zu out of range", layer);
     if (n == 0) return VOX_OK;  // kv.rs:55-57
     if (!k_new || !v_new) return fail(VOX_ERR_INVALID_ARG, "null k/v");
@@ -1034,18 +1447,21 @@ int vox_kv_append_layer(vox_kv* kv, size_t layer, const float* k_new, const floa
 
 int vox_kv_layer_len_tokens(const vox_kv* kv, size_t layer, size_t* out) {
     if (!kv || !out || layer >= kv->n_layers) return fail(VOX_ERR_INVALID_ARG, "bad argument");
+    TRY(single_stream(kv));
     *out = kv->hs[layer].len;
     return VOX_OK;
 }
 
 int vox_kv_layer_pos_offset(const vox_kv* kv, size_t layer, size_t* out) {
     if (!kv || !out || layer >= kv->n_layers) return fail(VOX_ERR_INVALID_ARG, "bad argument");
+    TRY(single_stream(kv));
     *out = kv->hs[layer].pos_offset;
     return VOX_OK;
 }
 
 int vox_kv_layer_device_state(const vox_kv* kv, size_t layer, int64_t out[3]) {
     if (!kv || !out || layer >= kv->n_layers) return fail(VOX_ERR_INVALID_ARG, "bad argument");
+    TRY(single_stream(kv));
     vox_ctx* c = kv->ctx;
     CUDA_TRY(cudaSetDevice(c->dev));
     KvState d{};
@@ -1059,6 +1475,7 @@ int vox_kv_layer_device_state(const vox_kv* kv, size_t layer, int64_t out[3]) {
 
 int vox_kv_layer_tensors(const vox_kv* kv, size_t layer, float* keys, float* values, size_t cap_elems) {
     if (!kv || layer >= kv->n_layers) return fail(VOX_ERR_INVALID_ARG, "bad argument");
+    TRY(single_stream(kv));
     vox_ctx* c = kv->ctx;
     const HostKv& s = kv->hs[layer];
     const size_t elems = s.len * kv->n_kv * kv->hd;
@@ -1082,6 +1499,7 @@ int vox_kv_layer_tensors(const vox_kv* kv, size_t layer, float* keys, float* val
 int vox_decoder_layer_forward_step(vox_ctx* c, size_t layer, vox_kv* kv, const float* hidden,
                                    size_t hidden_len, size_t pos, float* out, size_t out_len) {
     if (!c || !kv) return fail(VOX_ERR_INVALID_ARG, "null context or cache");
+    TRY(single_stream(kv));
     TRY(validate_cfg(&c->cfg));                                    // decoder.rs:96
     if (layer >= c->layers.size() || !c->layers[layer].ready)      // decoder.rs:97
         return fail(VOX_ERR_NOT_READY, "layer %zu weights not uploaded", layer);
@@ -1109,6 +1527,7 @@ int vox_decoder_layer_forward_step(vox_ctx* c, size_t layer, vox_kv* kv, const f
 // ---- token loop --------------------------------------------------------------------
 int vox_model_step(vox_ctx* c, vox_kv* kv, int32_t token, size_t pos, int32_t* next_token, float* logits) {
     TRY(model_ready(c, kv));
+    TRY(single_stream(kv));
     if (token < 0 || (size_t)token >= c->opt.vocab) return fail(VOX_ERR_RANGE, "token %d outside the vocabulary", token);
     if (pos >= (size_t)c->max_pos) return fail(VOX_ERR_RANGE, "position %zu beyond max_positions %d", pos, c->max_pos);
     CUDA_TRY(cudaSetDevice(c->dev));
@@ -1131,6 +1550,7 @@ int vox_model_step(vox_ctx* c, vox_kv* kv, int32_t token, size_t pos, int32_t* n
 
 int vox_model_prefill(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, size_t pos0) {
     TRY(model_ready(c, kv));
+    TRY(single_stream(kv));
     if (n == 0) return VOX_OK;
     if (!tokens) return fail(VOX_ERR_INVALID_ARG, "tokens is null");
     if (pos0 + n > (size_t)c->max_pos) return fail(VOX_ERR_RANGE, "positions beyond max_positions %d", c->max_pos);
@@ -1156,6 +1576,7 @@ int vox_model_prefill(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, s
 
 int vox_model_generate(vox_ctx* c, vox_kv* kv, int32_t token, size_t pos, size_t n_steps, int32_t* tokens_out) {
     TRY(model_ready(c, kv));
+    TRY(single_stream(kv));
     if (n_steps == 0) return VOX_OK;
     if (token < 0 || (size_t)token >= c->opt.vocab) return fail(VOX_ERR_RANGE, "token %d outside the vocabulary", token);
     if (pos + n_steps > (size_t)c->max_pos) return fail(VOX_ERR_RANGE, "positions beyond max_positions %d", c->max_pos);
@@ -1179,6 +1600,95 @@ int vox_model_generate(vox_ctx* c, vox_kv* kv, int32_t token, size_t pos, size_t
     TRY(check_device_errors(c));
     for (size_t i = 0; i < n_steps; ++i) mirror_single_append_all(kv);
     if (tokens_out) std::memcpy(tokens_out, tok_hist, n_steps * 4);
+    return VOX_OK;
+}
+
+// ---- multi-stream token loop -----------------------------------------------------
+static int batch_ready(vox_ctx* c, vox_kv* kv) {
+    TRY(model_ready(c, kv));
+    if (kv->parent) return fail(VOX_ERR_INVALID_ARG, "pass the multi-stream cache, not a stream view");
+    TRY(ensure_batch(c));
+    TRY(build_batch_graph(c, kv));
+    return VOX_OK;
+}
+
+static int check_stream_inputs(vox_ctx* c, const vox_kv* kv, const int32_t* tokens, const size_t* positions,
+                               size_t n_steps) {
+    if (!tokens || !positions) return fail(VOX_ERR_INVALID_ARG, "tokens or positions is null");
+    for (size_t s = 0; s < kv->n_streams; ++s) {
+        if (tokens[s] < 0 || (size_t)tokens[s] >= c->opt.vocab)
+            return fail(VOX_ERR_RANGE, "stream %zu: token %d outside the vocabulary", s, tokens[s]);
+        if (positions[s] + n_steps > (size_t)c->max_pos)
+            return fail(VOX_ERR_RANGE, "stream %zu: positions beyond max_positions %d", s, c->max_pos);
+    }
+    return VOX_OK;
+}
+
+static int upload_batch_steps(vox_ctx* c, const vox_kv* kv, const int32_t* tokens, const size_t* positions,
+                              int greedy) {
+    StepState* hs = c->bb.h_steps;
+    std::memset(hs, 0, 8 * sizeof(StepState));
+    for (size_t s = 0; s < kv->n_streams; ++s) {
+        hs[s].pos = (int64_t)positions[s];
+        hs[s].tok = tokens[s];
+        hs[s].greedy = greedy;
+        hs[s].advance = greedy;
+    }
+    CUDA_TRY(cudaMemcpyAsync(c->bb.steps, hs, kv->n_streams * sizeof(StepState), cudaMemcpyHostToDevice,
+                             c->stream));
+    return VOX_OK;
+}
+
+static void mirror_batch_appends(vox_kv* kv, size_t n_steps) {
+    for (HostKv& h : kv->hs_store)
+        for (size_t i = 0; i < n_steps; ++i) host_append(h, 1, kv->window, kv->cap);
+}
+
+int vox_model_step_batch(vox_ctx* c, vox_kv* kv, const int32_t* tokens, const size_t* positions,
+                         int32_t* next_tokens, float* logits) {
+    TRY(batch_ready(c, kv));
+    TRY(check_stream_inputs(c, kv, tokens, positions, 1));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));  // the pinned step slots are reused below
+    TRY(upload_batch_steps(c, kv, tokens, positions, 0));
+    CUDA_TRY(cudaGraphLaunch(kv->batch_graph, c->stream));
+    c->launches += kv->batch_kernels;
+    if (next_tokens)
+        CUDA_TRY(cudaMemcpyAsync(next_tokens, c->bb.tok_out, kv->n_streams * 4, cudaMemcpyDeviceToHost, c->stream));
+    if (logits)
+        CUDA_TRY(cudaMemcpyAsync(logits, c->bb.logits, kv->n_streams * c->opt.vocab * 4, cudaMemcpyDeviceToHost,
+                                 c->stream));
+    TRY(check_device_errors(c));
+    mirror_batch_appends(kv, 1);
+    return VOX_OK;
+}
+
+int vox_model_generate_batch(vox_ctx* c, vox_kv* kv, const int32_t* tokens, const size_t* positions,
+                             size_t n_steps, int32_t* tokens_out) {
+    TRY(batch_ready(c, kv));
+    if (n_steps == 0) return VOX_OK;
+    TRY(check_stream_inputs(c, kv, tokens, positions, n_steps));
+    BatchBufs& bb = c->bb;
+    const size_t B = kv->n_streams;
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    if (tokens_out && n_steps * B > bb.h_tok_cap) {
+        if (bb.h_tok) cudaFreeHost(bb.h_tok);
+        bb.h_tok = nullptr;
+        bb.h_tok_cap = 0;
+        size_t cap = 1024;
+        while (cap < n_steps * B) cap <<= 1;
+        CUDA_TRY(cudaMallocHost(&bb.h_tok, cap * 4));
+        bb.h_tok_cap = cap;
+    }
+    TRY(upload_batch_steps(c, kv, tokens, positions, 1));
+    for (size_t i = 0; i < n_steps; ++i) {
+        CUDA_TRY(cudaGraphLaunch(kv->batch_graph, c->stream));
+        c->launches += kv->batch_kernels;
+        if (tokens_out)
+            CUDA_TRY(cudaMemcpyAsync(bb.h_tok + i * B, bb.tok_out, B * 4, cudaMemcpyDeviceToHost, c->stream));
+    }
+    TRY(check_device_errors(c));
+    mirror_batch_appends(kv, n_steps);
+    if (tokens_out) std::memcpy(tokens_out, bb.h_tok, n_steps * B * 4);
     return VOX_OK;
 }
 

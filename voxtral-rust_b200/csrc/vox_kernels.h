@@ -109,6 +109,11 @@ struct AttnArgs {
     float* out;                 // [n_heads, hd]
     float scale;
     unsigned* err;
+    // Independent streams (gridDim.z; 0 counts as 1): stream z reads and
+    // writes every pointer above advanced by z times its stride, and uses
+    // tickets + z * n_kv.
+    int n_streams;
+    long long q_stride, ring_stride, out_stride, part_stride, st_stride;
 };
 
 // Record a failure for vox_last_error() and return `code` (host side).
@@ -176,7 +181,7 @@ struct BgArgs {
     const float* x;             // [B, x_stride] f32 inputs
     long long x_stride;
     const float* norm_w;        // non-null: apply RMSNorm with this gain to x
-    const float* ssp;           // RMSNorm partial sums of squares [ssp_parts, 8]
+    const float* ssp;           // RMSNorm partial sums of squares [ssp_parts, 8] of x
     int ssp_parts;
     float eps;
     int epi;
@@ -184,7 +189,7 @@ struct BgArgs {
     long long y_stride;
     const float* bias;
     const float* resid;
-    float* ssp_out;
+    float* ssp_out;             // BG_RESID: per-tile sums of squares of y [tiles, 8]
     int q_dim, kv_dim, head_dim;
     const float* rope_cos;
     const float* rope_sin;
@@ -196,7 +201,8 @@ struct BgArgs {
     float* v_ring;
     long long ring_stride;      // floats between streams' rings
     int ring_cap, kv_window;
-    ArgmaxPart* am_part;
+    KvState* kv_commit;         // non-null: commit one single-token append per stream
+    ArgmaxPart* am_part;        // [tiles, 8]
     float* part;                // split-K partial tiles [tiles * splits, 128, 8]
     unsigned* tickets;          // [tiles], zero between launches
     unsigned* err;
@@ -207,6 +213,10 @@ int bgemm_xslab_bytes(int K, int splits);
 cudaError_t bgemm_prepare(int dev);
 cudaError_t launch_bgemm(const BgArgs& a, int grid, cudaStream_t s, bool pdl);
 size_t tiled_bytes(int rows, int K);
+cudaError_t launch_bg_embed(const uint16_t* embed, int vocab, int dim, const StepState* steps, int B, float* hid,
+                            float* ssp, unsigned* err, cudaStream_t s, bool pdl);
+cudaError_t launch_bg_argmax_final(const ArgmaxPart* parts, int n_tiles, StepState* steps, int B,
+                                   int32_t* tok_out, cudaStream_t s, bool pdl);
 cudaError_t launch_tile_weights(const uint16_t* src, uint16_t* dst, int rows, int K, cudaStream_t s);
 
 // ---- launchers (return the launch error) ----
@@ -235,6 +245,10 @@ cudaError_t launch_gen_matrix(void* dst, int wsize, uint64_t seed, uint64_t tens
                               long long rows, long long cols, int row_mul, int row_add,
                               cudaStream_t s);
 cudaError_t launch_fill_f32(float* dst, float v, long long n, cudaStream_t s);
+// Fill tokens 0..len-1 of a ring (start slot 0) from the generator: K from
+// tensor id_k, V from id_v, each [len, n_kv, hd] token-major, bf16-rounded.
+cudaError_t launch_kv_fill_random(float* kr, float* vr, int n_kv, int hd, int cap, int len, uint64_t seed,
+                                  uint64_t id_k, uint64_t id_v, float stdv, cudaStream_t s);
 cudaError_t launch_rmsnorm_rows(float* out, const float* in, const float* w, long long n_rows,
                                 int dim, float eps, cudaStream_t s);
 cudaError_t launch_rope_table(float* data, const float* cos_t, const float* sin_t, long long seq_len,

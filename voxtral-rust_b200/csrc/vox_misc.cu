@@ -133,6 +133,23 @@ __global__ void gen_matrix_kernel(void* dst, int wsize, uint64_t key, float stdv
     }
 }
 
+// Random cache contents: logical token t of kv head h, element d, is element
+// (t * n_kv + h) * hd + d of the generator's tensor (the reference's
+// token-major layout), rounded to bf16 and stored widened in the ring slot t.
+__global__ void kv_fill_random_kernel(float* __restrict__ kr, float* __restrict__ vr, int n_kv, int hd, int cap,
+                                      long long total, uint64_t key_k, uint64_t key_v, float stdv) {
+    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+         e += (long long)gridDim.x * blockDim.x) {
+        const int d = (int)(e % hd);
+        const long long th = e / hd;
+        const int h = (int)(th % n_kv);
+        const long long t = th / n_kv;
+        const size_t dst = ((size_t)h * cap + t) * hd + d;
+        kr[dst] = bf16_bits_to_f32(f32_to_bf16_rne(__fmul_rn(gen_z(key_k, (uint64_t)e), stdv)));
+        vr[dst] = bf16_bits_to_f32(f32_to_bf16_rne(__fmul_rn(gen_z(key_v, (uint64_t)e), stdv)));
+    }
+}
+
 __global__ void fill_kernel(float* dst, float v, long long n) {
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x)
@@ -285,6 +302,16 @@ cudaError_t launch_gen_matrix(void* dst, int wsize, uint64_t seed, uint64_t tens
     const long long total = rows * cols;
     gen_matrix_kernel<<<grid_for(total, 256), 256, 0, s>>>(dst, wsize, key, stdv, rows, cols, row_mul,
                                                            row_add);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_kv_fill_random(float* kr, float* vr, int n_kv, int hd, int cap, int len, uint64_t seed,
+                                  uint64_t id_k, uint64_t id_v, float stdv, cudaStream_t s) {
+    const long long total = (long long)len * n_kv * hd;
+    if (total == 0) return cudaSuccess;
+    const uint64_t kk = host_mix64(seed ^ host_mix64(id_k + 0x632BE59BD9B4E019ull));
+    const uint64_t kvv = host_mix64(seed ^ host_mix64(id_v + 0x632BE59BD9B4E019ull));
+    kv_fill_random_kernel<<<grid_for(total, 256), 256, 0, s>>>(kr, vr, n_kv, hd, cap, total, kk, kvv, stdv);
     return cudaGetLastError();
 }
 
