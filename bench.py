@@ -13,6 +13,11 @@ With N > 1 (torchrun, one process per GPU) every rank decodes its own
 independent stream (no collective on the data path: weak scaling); value is
 the total tokens/s of all ranks over the slowest rank's time.
 
+The same run then measures the multi-stream workload (8 independent streams
+per GPU, contexts uniform in [256, 4096) with the cache prefilled from
+N(0,1) bf16, greedy decode with tensor-core GEMMs) and reports it as the
+"multi_stream" object of the JSON line (64 streams at 8 GPUs).
+
 --impl reference times the reference's CPU algorithm (the oracle port: the
 reference is Rust and cannot be built here) with all host threads on the same
 workload, rank 0 only.
@@ -28,6 +33,7 @@ import subprocess
 import sys
 import time
 
+import ctypes
 import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -43,6 +49,7 @@ LAYER_WEIGHT_BYTES = 2 * (DIM * (NH * HD) + 2 * DIM * (NKV * HD) + (NH * HD) * D
 HEAD_BYTES = 2 * VOCAB * DIM
 EMBED_ROW_BYTES = 2 * DIM
 KV_BYTES_PER_TOKEN_LAYER = 2 * NKV * HD * 4   # f32 K and V
+C_SZ = ctypes.c_size_t
 
 
 def step_bytes(ctx_len: int) -> int:
@@ -234,6 +241,54 @@ def traffic_from_profiles():
     return None
 
 
+MS_STREAMS = 8
+MS_WORKLOAD = ("26-layer decoder, 8 independent streams per GPU, contexts uniform in [256, 4096) with the KV "
+               "cache prefilled from N(0,1) bf16, greedy decode, tensor-core (tcgen05) GEMMs")
+
+
+def run_multi_stream(V, ctx, args, rank, world, dist):
+    """The multi-stream workload: 8 streams per GPU decoded together, every
+    weight read once per step for all 8.  Returns the per-rank measurements."""
+    o_ids = np.random.default_rng(1000 + rank)
+    lens = [int(x) for x in o_ids.integers(256, 4096, MS_STREAMS)]
+    kv = V.RollingKvCache(ctx, LAYERS, NKV, HD, WINDOW, n_streams=MS_STREAMS)
+    for s, n in enumerate(lens):
+        kv.stream(s).fill_random(n, 0, 5000000 + 100 * (rank * MS_STREAMS + s), 1.0)
+    toks = [int(t) for t in o_ids.integers(0, VOCAB, MS_STREAMS)]
+    pos = list(lens)
+    out = ctx.model_generate_batch(kv, toks, pos, args.warmup)
+    toks = [int(t) for t in out[-1]]
+    pos = [p + args.warmup for p in pos]
+    ctx.synchronize()
+    steps = args.ms_steps
+    if dist:
+        dist.barrier()
+    ctx.synchronize()
+    launches0 = ctx.kernel_launches()
+    ctx.record_event(4)
+    tp = (C_SZ * MS_STREAMS)(*pos)
+    ti = np.ascontiguousarray(toks, dtype=np.int32)
+    V.lib().vox_model_generate_batch(ctx.h, kv.h, ti.ctypes.data_as(V.I32P), tp, steps, None)
+    ctx.record_event(5)
+    ctx.synchronize()
+    ms = ctx.elapsed_ms(4, 5)
+    launches = ctx.kernel_launches() - launches0
+    ctx_mean = sum(lens) / MS_STREAMS + args.warmup + steps / 2
+    # end to end: host ids in, host next ids out, per step
+    pos = [p + steps for p in pos]
+    if dist:
+        dist.barrier()
+    ctx.record_event(6)
+    e2e_steps = min(steps, 64)
+    for i in range(e2e_steps):
+        nxt, _ = ctx.model_step_batch(kv, toks, [p + i for p in pos])
+        toks = [int(t) for t in nxt]
+    ctx.record_event(7)
+    e2e_ms = ctx.elapsed_ms(6, 7) / e2e_steps
+    kv.close()
+    return {"ms": ms, "steps": steps, "launches": launches, "lens": lens, "ctx_mean": ctx_mean, "e2e_ms": e2e_ms}
+
+
 def run_ours(args):
     rank, world, local = dist_env()
     V = importlib.import_module("voxtral-rust_b200")
@@ -246,7 +301,8 @@ def run_ours(args):
     cfg = V.DecoderConfig(dim=DIM, hidden_dim=HIDDEN, n_heads=NH, n_kv_heads=NKV, head_dim=HD,
                           sliding_window=WINDOW, norm_eps=1e-5, rope_theta=1e6)
     total_pos = PROMPT + args.warmup + 2 * args.steps + 8
-    ctx = V.Context(cfg, n_layers=LAYERS, vocab=VOCAB, device=local, max_positions=max(total_pos, 4096))
+    total_pos = max(total_pos, 4096 + args.warmup + args.ms_steps + 72)
+    ctx = V.Context(cfg, n_layers=LAYERS, vocab=VOCAB, device=local, max_positions=total_pos)
     ctx.init_random(seed=0, std=0.02)
     kv = V.RollingKvCache(ctx, LAYERS, NKV, HD, WINDOW)
     prompt = prompt_ids(rank, PROMPT)
@@ -291,12 +347,17 @@ def run_ours(args):
     # ---- dominant kernel on its own (w1|w3 SwiGLU GEMV, one launch per layer) ----
     k_ms, k_bytes = ctx.profile_gemv(2, LAYERS * 4)
 
+    ms_run = None if args.ms_steps == 0 else run_multi_stream(V, ctx, args, rank, world, dist)
+
     t_max, e2e_max = ms, e2e_ms
+    ms_max = ms_e2e_max = 0.0
+    if ms_run:
+        ms_max, ms_e2e_max = ms_run["ms"], ms_run["e2e_ms"]
     if dist:
         import torch
-        t = torch.tensor([ms, e2e_ms], dtype=torch.float64)
+        t = torch.tensor([ms, e2e_ms, ms_max, ms_e2e_max], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_max, e2e_max = float(t[0]), float(t[1])
+        t_max, e2e_max, ms_max, ms_e2e_max = (float(x) for x in t)
     if rank != 0:
         if dist:
             dist.barrier()
@@ -327,6 +388,20 @@ def run_ours(args):
         "step_roofline": {"achieved": step_gbs, "peak": peak, "unit": "GB/s", "frac": step_gbs / peak},
         "clocks": clk,
     }
+    if ms_run:
+        n_tok = ms_run["steps"] * MS_STREAMS * world
+        ms_bytes = (LAYERS * LAYER_WEIGHT_BYTES + HEAD_BYTES + MS_STREAMS * EMBED_ROW_BYTES +
+                    LAYERS * KV_BYTES_PER_TOKEN_LAYER * MS_STREAMS * ms_run["ctx_mean"])
+        ms_gbs = ms_bytes / (ms_max / ms_run["steps"] / 1e3) / 1e9
+        line["multi_stream"] = {
+            "metric": "decoder tokens/s (8 streams per GPU)", "value": n_tok / (ms_max / 1e3), "unit": "tokens/s",
+            "streams_per_gpu": MS_STREAMS, "total_streams": MS_STREAMS * world, "steps": ms_run["steps"],
+            "ms_per_step": ms_max / ms_run["steps"], "workload": MS_WORKLOAD,
+            "contexts_rank0": ms_run["lens"], "bytes_per_step": int(ms_bytes),
+            "step_roofline": {"achieved": ms_gbs, "peak": peak, "unit": "GB/s", "frac": ms_gbs / peak},
+            "e2e": {"value": MS_STREAMS * world / (ms_e2e_max / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 40 * MS_STREAMS, "d2h_bytes_per_step": 4 * MS_STREAMS},
+            "gpu_launches": ms_run["launches"]}
     if world == 1 and not args.no_cpu:
         rate, sample = cpu_token_rate(1, args.cpu_layer_steps, 1)
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": 1, "kind": "port", "sample": sample}
@@ -344,6 +419,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--cpu-layer-steps", type=int, default=24)
+    ap.add_argument("--ms-steps", type=int, default=512,
+                    help="greedy steps of the 8-streams-per-GPU run (0 skips it)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -240,6 +240,11 @@ int vox_model_generate_batch(vox_ctx* ctx, vox_kv* kv, const int32_t* tokens, co
 int vox_profile_gemv(vox_ctx* ctx, int which, size_t n_launches, float* avg_ms,
                      uint64_t* bytes_per_launch);
 
+/* Same for the multi-stream tensor-core GEMM with n_streams input vectors
+ * (needs the embedding and LM head): which 1 o-proj, 2 w1|w3 (SwiGLU),
+ * 3 w2, 4 LM head, 5 q|k|v (plain store). */
+int vox_profile_bgemm(vox_ctx* ctx, int which, size_t n_streams, size_t n_launches, float* avg_ms,
+                      uint64_t* bytes_per_launch);
 /* ---- op-level entry points (host buffers) ------------------------------------ */
 /* linear (ops.rs:11-39): out[n_rows, out_dim] = input[n_rows, in_dim] * W^T + bias. */
 int vox_linear_f32(vox_ctx* ctx, const float* input, size_t n_rows, size_t in_dim,

@@ -129,6 +129,7 @@ _SIGS = {
     "vox_model_generate": ([VP, VP, C.c_int32, SZ, SZ, I32P], C.c_int),
     "vox_model_prefill": ([VP, VP, I32P, SZ, SZ], C.c_int),
     "vox_profile_gemv": ([VP, C.c_int, SZ, F32P, C.POINTER(C.c_uint64)], C.c_int),
+    "vox_profile_bgemm": ([VP, C.c_int, SZ, SZ, F32P, C.POINTER(C.c_uint64)], C.c_int),
     "vox_linear_f32": ([VP, F32P, SZ, SZ, F32P, SZ, F32P, F32P], C.c_int),
     "vox_linear_bf16": ([VP, F32P, SZ, SZ, U16P, SZ, F32P, F32P], C.c_int),
     "vox_linear_batched_bf16": ([VP, F32P, SZ, SZ, U16P, SZ, F32P, F32P], C.c_int),
@@ -289,6 +290,14 @@ class Context:
         ms = C.c_float()
         nb = C.c_uint64()
         _check(lib().vox_profile_gemv(self.h, which, n_launches, C.byref(ms), C.byref(nb)))
+        return ms.value, nb.value
+
+    def profile_bgemm(self, which, n_streams, n_launches):
+        """Mean ms per launch and weight bytes per launch of one multi-stream
+        tensor-core GEMM (1 o-proj, 2 w1|w3, 3 w2, 4 LM head, 5 q|k|v)."""
+        ms = C.c_float()
+        nb = C.c_uint64()
+        _check(lib().vox_profile_bgemm(self.h, which, n_streams, n_launches, C.byref(ms), C.byref(nb)))
         return ms.value, nb.value
 
     def kernel_launches(self):

@@ -6,17 +6,20 @@
 // sum of V.  Tokens older than seq_len - sliding_window are masked (ops.rs:
 // 91-95, 102-105).
 //
-// B200 layout: one CTA per (kv head, split of the token range).  The CTA
-// serves all G query heads of its kv head, so each K/V row is read from HBM
-// once per group (the reference reads it G times).  Tiles of 32 tokens are
-// double-buffered in shared memory with cp.async; the CTA keeps an
-// online-softmax state (running max m, running sum l, unnormalised
-// accumulator) per head.  The number of active splits follows the live
-// length at run time (at least one tile each), so one captured launch serves
-// every step.  Split results go to a scratch buffer and the last CTA of each
-// kv head (atomic ticket) merges them: per-split weights exp(m_s - M) / L are
-// computed once per head, then every output is a dot product over the splits
-// with independent loads.  Merge order is fixed, so results are run-to-run
+// B200 layout: a persistent grid (every CTA that fits on the SMs) walks one
+// work list of chunks: (stream, kv head, chunk of the live token range).
+// Chunks have the same number of 32-token tiles across all streams, chosen
+// at run time from the live lengths so that every CTA gets about two, which
+// keeps streams of very different context lengths balanced and lets one
+// captured launch serve every step.  A CTA serves all G query heads of its
+// kv head, so each K/V row is read from HBM once per group (the reference
+// reads it G times).  Tiles are double-buffered in shared memory with
+// cp.async; the CTA keeps an online-softmax state (running max m, running sum
+// l, unnormalised accumulator) per head.  Chunk results go to a scratch
+// buffer and the last chunk of each (stream, kv head) to finish (atomic
+// ticket) merges them: per-chunk weights exp(m_s - M) / L are computed once
+// per head, then every output is a dot product over the chunks with
+// independent loads.  Merge order is fixed, so results are run-to-run
 // deterministic.
 //
 // The ring is head-major [n_kv, cap, hd]: logical token t of a layer lives
@@ -113,20 +116,25 @@ __device__ __forceinline__ void load_tile(float* ks, float* vs, const float* kr,
     }
 }
 
+// Work list shared by every CTA: stream z has items_z chunks of tpi_z tiles
+// per kv head; items are numbered stream-major, then kv head, then chunk.
+struct AttnPlan {
+    int len[8], mask_start[8], start[8], tpi[8], items[8], first[9];
+};
+
 template <int VEC>
 __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs A) {
     using T = typename VecT<VEC>::T;
     extern __shared__ __align__(16) float sm[];
+    __shared__ AttnPlan plan;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int h = blockIdx.x;          // kv head
-    const int split = blockIdx.y;
-    const int z = blockIdx.z;          // stream
     const int hd = A.hd;
     const int G = A.n_heads / A.n_kv;
     const int hdv = hd / VEC;          // vectors per row
     const int pad = VEC == 4 ? 4 : 1;  // row padding (floats) against bank conflicts
     const int ldk = hd + pad;
     const int tile_f = kTile * ldk;
+    const int B = A.n_streams > 1 ? A.n_streams : 1;
 
     float* q_s = sm;                          // [G, hd]
     float* kbuf = q_s + G * hd;               // [2][kTile, ldk]
@@ -141,192 +149,510 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
     pdl_allow_dependents();
     pdl_wait_prior_grids();
 
-    const float* q_in = A.q + z * A.q_stride;
-    float* out = A.out + z * A.out_stride;
-    float* part = A.part + z * A.part_stride;
-    unsigned* tickets = A.tickets + (size_t)z * A.n_kv;
-    KvState st = A.st[z * A.st_stride];
-    if (A.pre_append) st = kv_after_single_append(st, A.kv_window, A.cap);
-    const int len = st.len;
-    const int mask_start = (A.cfg_window > 0 && len > A.cfg_window) ? len - A.cfg_window : 0;
-    const int n_live = len - mask_start;
-    int per = (n_live + A.nsplit - 1) / A.nsplit;
-    per = ((per + kTile - 1) / kTile) * kTile;
-    if (per < kTile) per = kTile;
-    const int n_active = (n_live + per - 1) / per;
-    float* out_h = out + (size_t)h * G * hd;
-    if (n_active == 0) {  // empty cache: the reference returns zeros
-        if (split == 0)
-            for (int i = tid; i < G * hd; i += kAttnThreads) out_h[i] = 0.f;
-        return;
+    // Live range of every stream (ops.rs:91-95) and its share of the work:
+    // chunks of equal length across all streams, so long contexts get more
+    // CTAs, at most nsplit chunks per (stream, kv head).
+    if (tid == 0) {
+        long long total_tiles = 0;
+        for (int z = 0; z < B; ++z) {
+            KvState st = A.st[z * A.st_stride];
+            if (A.pre_append) st = kv_after_single_append(st, A.kv_window, A.cap);
+            const int len = st.len;
+            const int ms = (A.cfg_window > 0 && len > A.cfg_window) ? len - A.cfg_window : 0;
+            plan.len[z] = len;
+            plan.mask_start[z] = ms;
+            plan.start[z] = st.start;
+            plan.items[z] = (len - ms + kTile - 1) / kTile;  // live tiles, for now
+            total_tiles += (long long)plan.items[z] * A.n_kv;
+        }
+        const long long slots = 2LL * gridDim.x;
+        const int tpi_all = (int)max(1LL, (total_tiles + slots - 1) / slots);
+        int first = 0;
+        for (int z = 0; z < B; ++z) {
+            const int tiles = plan.items[z];
+            const int tpi = max(tpi_all, (tiles + A.nsplit - 1) / A.nsplit);
+            plan.tpi[z] = tpi;
+            plan.items[z] = (tiles + tpi - 1) / tpi;
+            plan.first[z] = first;
+            first += plan.items[z] * A.n_kv;
+        }
+        plan.first[B] = first;
     }
-    if (split >= n_active) return;
-    const int t_begin = mask_start + split * per;
-    const int t_end = min(len, t_begin + per);
+    __syncthreads();
 
-    const float* kr = A.k_ring + z * A.ring_stride + (size_t)h * A.cap * hd;
-    const float* vr = A.v_ring + z * A.ring_stride + (size_t)h * A.cap * hd;
-    load_tile<VEC>(kbuf, vbuf, kr, vr, t_begin, t_end, st.start, A.cap, hd, ldk);
-    if constexpr (VEC == 4) cp_async_commit();
-
-    for (int i = tid; i < G * hd; i += kAttnThreads) q_s[i] = q_in[(size_t)h * G * hd + i];
-    if (tid < G) {
-        m_s[tid] = -INFINITY;
-        l_s[tid] = 0.f;
-    }
-    T acc[kMaxAcc];
-#pragma unroll
-    for (int j = 0; j < kMaxAcc; ++j) fzero(acc[j]);
-    const int n_out = G * hdv;
-
-    int buf = 0;
-    for (int t0 = t_begin; t0 < t_end; t0 += kTile, buf ^= 1) {
-        const bool has_next = t0 + kTile < t_end;
-        if (has_next) {
-            load_tile<VEC>(kbuf + (buf ^ 1) * tile_f, vbuf + (buf ^ 1) * tile_f, kr, vr, t0 + kTile, t_end,
-                           st.start, A.cap, hd, ldk);
-            if constexpr (VEC == 4) cp_async_commit();
-        }
-        if constexpr (VEC == 4) {
-            if (has_next)
-                cp_async_wait<1>();
-            else
-                cp_async_wait<0>();
-        }
-        __syncthreads();
-        const float* k_s = kbuf + buf * tile_f;
-        const float* v_s = vbuf + buf * tile_f;
-        // Scores: (g, t) pairs; ops.rs:108-113 dot * scale.
-        for (int idx = tid; idx < G * kTile; idx += kAttnThreads) {
-            const int g = idx / kTile, tt = idx - g * kTile;
-            float s = -INFINITY;
-            if (t0 + tt < t_end) {
-                float d = 0.f;
-                const T* qv = reinterpret_cast<const T*>(q_s + g * hd);
-                const T* kv = reinterpret_cast<const T*>(k_s + tt * ldk);
-                for (int dv = 0; dv < hdv; ++dv) d = fdot(d, qv[dv], kv[dv]);
-                s = d * A.scale;
+    // Streams with nothing to attend to: the reference returns zeros.
+    if (blockIdx.x == 0)
+        for (int z = 0; z < B; ++z)
+            if (plan.items[z] == 0) {
+                float* out = A.out + z * A.out_stride;
+                for (int i = tid; i < A.n_heads * hd; i += kAttnThreads) out[i] = 0.f;
             }
-            p_s[idx] = s;
+
+    const int total = plan.first[B];
+    for (int item = blockIdx.x; item < total; item += gridDim.x) {
+        __syncthreads();  // shared buffers of the previous item are free
+        int z = 0;
+        while (z + 1 < B && item >= plan.first[z + 1]) ++z;
+        const int n_active = plan.items[z];
+        const int local = item - plan.first[z];
+        const int h = local / n_active;
+        const int split = local - h * n_active;
+        const int len = plan.len[z];
+        const int per = plan.tpi[z] * kTile;
+        const int t_begin = plan.mask_start[z] + split * per;
+        const int t_end = min(len, t_begin + per);
+        const int ring_start = plan.start[z];
+
+        const float* q_in = A.q + z * A.q_stride;
+        float* out_h = A.out + z * A.out_stride + (size_t)h * G * hd;
+        float* part = A.part + z * A.part_stride;
+        unsigned* tickets = A.tickets + (size_t)z * A.n_kv;
+        const float* kr = A.k_ring + z * A.ring_stride + (size_t)h * A.cap * hd;
+        const float* vr = A.v_ring + z * A.ring_stride + (size_t)h * A.cap * hd;
+
+        load_tile<VEC>(kbuf, vbuf, kr, vr, t_begin, t_end, ring_start, A.cap, hd, ldk);
+        if constexpr (VEC == 4) cp_async_commit();
+
+        for (int i = tid; i < G * hd; i += kAttnThreads) q_s[i] = q_in[(size_t)h * G * hd + i];
+        if (tid < G) {
+            m_s[tid] = -INFINITY;
+            l_s[tid] = 0.f;
         }
-        __syncthreads();
-        // Online softmax update, one warp per head.
-        for (int g = warp; g < G; g += kAttnThreads / 32) {
-            const float s = p_s[g * kTile + lane];
-            float mt = s;
+        T acc[kMaxAcc];
 #pragma unroll
-            for (int o = 16; o; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xFFFFFFFFu, mt, o));
-            const float m_old = m_s[g];
-            const float m_new = fmaxf(m_old, mt);
-            const float p = (s == -INFINITY) ? 0.f : expf(s - m_new);
-            float ps = p;
-#pragma unroll
-            for (int o = 16; o; o >>= 1) ps += __shfl_xor_sync(0xFFFFFFFFu, ps, o);
-            p_s[g * kTile + lane] = p;
-            if (lane == 0) {
-                const float alpha = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
-                a_s[g] = alpha;
-                l_s[g] = l_s[g] * alpha + ps;
-                m_s[g] = m_new;
+        for (int j = 0; j < kMaxAcc; ++j) fzero(acc[j]);
+        const int n_out = G * hdv;
+
+        int buf = 0;
+        for (int t0 = t_begin; t0 < t_end; t0 += kTile, buf ^= 1) {
+            const bool has_next = t0 + kTile < t_end;
+            if (has_next) {
+                load_tile<VEC>(kbuf + (buf ^ 1) * tile_f, vbuf + (buf ^ 1) * tile_f, kr, vr, t0 + kTile, t_end,
+                               ring_start, A.cap, hd, ldk);
+                if constexpr (VEC == 4) cp_async_commit();
             }
+            if constexpr (VEC == 4) {
+                if (has_next)
+                    cp_async_wait<1>();
+                else
+                    cp_async_wait<0>();
+            }
+            __syncthreads();
+            const float* k_s = kbuf + buf * tile_f;
+            const float* v_s = vbuf + buf * tile_f;
+            // Scores: (g, t) pairs; ops.rs:108-113 dot * scale.
+            for (int idx = tid; idx < G * kTile; idx += kAttnThreads) {
+                const int g = idx / kTile, tt = idx - g * kTile;
+                float s = -INFINITY;
+                if (t0 + tt < t_end) {
+                    float d = 0.f;
+                    const T* qv = reinterpret_cast<const T*>(q_s + g * hd);
+                    const T* kv = reinterpret_cast<const T*>(k_s + tt * ldk);
+                    for (int dv = 0; dv < hdv; ++dv) d = fdot(d, qv[dv], kv[dv]);
+                    s = d * A.scale;
+                }
+                p_s[idx] = s;
+            }
+            __syncthreads();
+            // Online softmax update, one warp per head.
+            for (int g = warp; g < G; g += kAttnThreads / 32) {
+                const float s = p_s[g * kTile + lane];
+                float mt = s;
+#pragma unroll
+                for (int o = 16; o; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xFFFFFFFFu, mt, o));
+                const float m_old = m_s[g];
+                const float m_new = fmaxf(m_old, mt);
+                const float p = (s == -INFINITY) ? 0.f : expf(s - m_new);
+                float ps = p;
+#pragma unroll
+                for (int o = 16; o; o >>= 1) ps += __shfl_xor_sync(0xFFFFFFFFu, ps, o);
+                p_s[g * kTile + lane] = p;
+                if (lane == 0) {
+                    const float alpha = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
+                    a_s[g] = alpha;
+                    l_s[g] = l_s[g] * alpha + ps;
+                    m_s[g] = m_new;
+                }
+            }
+            __syncthreads();
+            // PV (ops.rs:117-128): acc = acc*alpha + sum_t p_t v_t.
+#pragma unroll
+            for (int j = 0; j < kMaxAcc; ++j) {
+                const int o = tid + j * kAttnThreads;
+                if (o < n_out) {
+                    const int g = o / hdv, dv = o - g * hdv;
+                    fscale(acc[j], a_s[g]);
+                    const float* pg = p_s + g * kTile;
+#pragma unroll 8
+                    for (int tt = 0; tt < kTile; ++tt)
+                        faxpy(acc[j], pg[tt], *reinterpret_cast<const T*>(v_s + tt * ldk + dv * VEC));
+                }
+            }
+            __syncthreads();  // the next iteration refills the other buffer of this pair
         }
-        __syncthreads();
-        // PV (ops.rs:117-128): acc = acc*alpha + sum_t p_t v_t.
+
+        // Split partials: accumulators [n_kv, nsplit, G, hd], then (m, l) pairs
+        // [n_kv, nsplit, G, 2], so the merge can read accumulators as vectors.
+        const size_t acc_stride = (size_t)G * hd;  // floats per split
+        const size_t ml_base = (size_t)A.n_kv * A.nsplit * acc_stride;
+        float* pacc = part + ((size_t)h * A.nsplit + split) * acc_stride;
+        float* pml = part + ml_base + ((size_t)h * A.nsplit + split) * G * 2;
 #pragma unroll
         for (int j = 0; j < kMaxAcc; ++j) {
             const int o = tid + j * kAttnThreads;
-            if (o < n_out) {
-                const int g = o / hdv, dv = o - g * hdv;
-                fscale(acc[j], a_s[g]);
-                const float* pg = p_s + g * kTile;
-#pragma unroll 8
-                for (int tt = 0; tt < kTile; ++tt)
-                    faxpy(acc[j], pg[tt], *reinterpret_cast<const T*>(v_s + tt * ldk + dv * VEC));
+            if (o < n_out) *reinterpret_cast<T*>(pacc + (size_t)o * VEC) = acc[j];
+        }
+        if (tid < G) {
+            pml[tid * 2] = m_s[tid];
+            pml[tid * 2 + 1] = l_s[tid];
+        }
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            const unsigned ticket = atomicAdd(&tickets[h], 1u);
+            flag_s[0] = (ticket == (unsigned)(n_active - 1)) ? 1 : 0;
+        }
+        __syncthreads();
+        if (!flag_s[0]) continue;
+        __threadfence();
+
+        // Last chunk of this (stream, kv head): merge weights w_s = exp(m_s - M) / L
+        // once per head ...
+        const float* bacc = part + (size_t)h * A.nsplit * acc_stride;
+        const float* bml = part + ml_base + (size_t)h * A.nsplit * G * 2;
+        for (int g = warp; g < G; g += kAttnThreads / 32) {
+            float ms[2], ls[2];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const int s = lane + 32 * r;
+                ms[r] = s < n_active ? __ldcg(bml + ((size_t)s * G + g) * 2) : -INFINITY;
+                ls[r] = s < n_active ? __ldcg(bml + ((size_t)s * G + g) * 2 + 1) : 0.f;
+            }
+            float M = fmaxf(ms[0], ms[1]);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
+            float w[2], L = 0.f;
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                w[r] = ms[r] == -INFINITY ? 0.f : expf(ms[r] - M);
+                L = fmaf(ls[r], w[r], L);
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xFFFFFFFFu, L, o);
+            const float invL = L > 0.f ? 1.0f / L : 0.f;
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const int s = lane + 32 * r;
+                if (s < n_active) w_s[g * kMaxSplits + s] = w[r] * invL;
             }
         }
-        __syncthreads();  // the next iteration refills the other buffer of this pair
-    }
-
-    // Split partials: accumulators [n_kv, nsplit, G, hd], then (m, l) pairs
-    // [n_kv, nsplit, G, 2], so the merge can read accumulators as vectors.
-    const size_t acc_stride = (size_t)G * hd;  // floats per split
-    const size_t ml_base = (size_t)A.n_kv * A.nsplit * acc_stride;
-    float* pacc = part + ((size_t)h * A.nsplit + split) * acc_stride;
-    float* pml = part + ml_base + ((size_t)h * A.nsplit + split) * G * 2;
+        __syncthreads();
+        // ... then each output vector is a weighted sum over the chunks, loaded
+        // eight at a time with independent loads.
+        const size_t vstride = acc_stride / VEC;
+        for (int o = tid; o < n_out; o += kAttnThreads) {
+            const int g = o / hdv;
+            const T* pv = reinterpret_cast<const T*>(bacc) + o;
+            const float* wg = w_s + g * kMaxSplits;
+            T sum;
+            fzero(sum);
+            for (int s0 = 0; s0 < n_active; s0 += 8) {
+                T v[8];
 #pragma unroll
-    for (int j = 0; j < kMaxAcc; ++j) {
-        const int o = tid + j * kAttnThreads;
-        if (o < n_out) *reinterpret_cast<T*>(pacc + (size_t)o * VEC) = acc[j];
+                for (int j = 0; j < 8; ++j) {
+                    if (s0 + j < n_active)
+                        v[j] = __ldcg(pv + (size_t)(s0 + j) * vstride);
+                    else
+                        fzero(v[j]);
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    if (s0 + j < n_active) faxpy(sum, wg[s0 + j], v[j]);
+            }
+            *reinterpret_cast<T*>(out_h + (size_t)o * VEC) = sum;
+        }
+        if (tid == 0) tickets[h] = 0u;
     }
-    if (tid < G) {
-        pml[tid * 2] = m_s[tid];
-        pml[tid * 2 + 1] = l_s[tid];
+}
+
+// ---- warp-per-chunk variant for G = 4 or 8 query heads per kv head ----------
+// Each warp owns a chunk of tokens of one (stream, kv head) and reads every
+// K/V row of it exactly once, straight from HBM into registers: lane l holds
+// dims 4l..4l+3 of 32/G consecutive tokens.  The G x (32/G) partial dot
+// products are summed across the warp by a transpose-reduce (31 shuffles)
+// that leaves lane l with the score of (head l / (32/G), token l % (32/G));
+// the online-softmax update then runs on one score per lane, and the PV
+// product on the lane's four dims for all G heads.  No shared-memory staging,
+// so nothing is re-read per head.
+template <int N>
+__device__ __forceinline__ void transpose_reduce(float (&v)[N], int lane) {
+    // After the step with offset o the lane keeps the half of its values
+    // selected by bit o of its lane id; at the end lane l holds value l.
+#pragma unroll
+    for (int o = 16, n = N; o >= 1; o >>= 1, n >>= 1) {
+        const bool up = lane & o;
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) {
+            const float keep = up ? v[i + n / 2] : v[i];
+            const float send = up ? v[i] : v[i + n / 2];
+            v[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, o);
+        }
     }
-    __threadfence();
-    __syncthreads();
+}
+
+__device__ __forceinline__ float dot4(const float4& a, const float4& b) {
+    float d = a.x * b.x;
+    d = fmaf(a.y, b.y, d);
+    d = fmaf(a.z, b.z, d);
+    return fmaf(a.w, b.w, d);
+}
+
+template <int G>
+__global__ void __launch_bounds__(kAttnThreads, 3) attn_warp_kernel(const AttnArgs A) {
+    constexpr int TPG = 32 / G;           // tokens per group: G * TPG = 32 scores per step
+    constexpr int NW = kAttnThreads / 32; // warps per CTA
+    constexpr int HD = 128;               // largest head_dim (4 dims per lane)
+    __shared__ AttnPlan plan;
+    __shared__ __align__(16) float wacc[NW][G][HD];  // per-warp accumulators of the chunk
+    __shared__ float wml[NW][G][2];                  // per-warp (m, l)
+    __shared__ float w_s[G][kMaxSplits];             // merge weights
+    __shared__ int flag_s;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int hd = A.hd;
+    const int B = A.n_streams > 1 ? A.n_streams : 1;
+    const unsigned FULL = 0xFFFFFFFFu;
+
+    pdl_allow_dependents();
+    pdl_wait_prior_grids();
+
+    // Work list (same in every CTA): chunks of gpi groups per warp, i.e.
+    // NW * gpi * TPG tokens per CTA chunk, at most nsplit chunks per
+    // (stream, kv head), about two chunks per CTA overall.
     if (tid == 0) {
-        const unsigned ticket = atomicAdd(&tickets[h], 1u);
-        flag_s[0] = (ticket == (unsigned)(n_active - 1)) ? 1 : 0;
+        long long total_groups = 0;
+        for (int z = 0; z < B; ++z) {
+            KvState st = A.st[z * A.st_stride];
+            if (A.pre_append) st = kv_after_single_append(st, A.kv_window, A.cap);
+            const int len = st.len;
+            const int ms = (A.cfg_window > 0 && len > A.cfg_window) ? len - A.cfg_window : 0;
+            plan.len[z] = len;
+            plan.mask_start[z] = ms;
+            plan.start[z] = st.start;
+            plan.items[z] = (len - ms + TPG - 1) / TPG;  // live groups, for now
+            total_groups += (long long)plan.items[z] * A.n_kv;
+        }
+        const long long slots = 2LL * gridDim.x * NW;
+        const int gpi_all = (int)max(1LL, (total_groups + slots - 1) / slots);
+        int first = 0;
+        for (int z = 0; z < B; ++z) {
+            const int groups = plan.items[z];
+            const int gpc = max(gpi_all * NW, (groups + A.nsplit - 1) / A.nsplit);  // groups per chunk
+            plan.tpi[z] = gpc;
+            plan.items[z] = (groups + gpc - 1) / gpc;
+            plan.first[z] = first;
+            first += plan.items[z] * A.n_kv;
+        }
+        plan.first[B] = first;
     }
     __syncthreads();
-    if (!flag_s[0]) return;
-    __threadfence();
 
-    // Last CTA of this kv head: merge weights w_s = exp(m_s - M) / L once per head ...
-    const float* bacc = part + (size_t)h * A.nsplit * acc_stride;
-    const float* bml = part + ml_base + (size_t)h * A.nsplit * G * 2;
-    for (int g = warp; g < G; g += kAttnThreads / 32) {
-        float ms[2], ls[2];
+    if (blockIdx.x == 0)
+        for (int z = 0; z < B; ++z)
+            if (plan.items[z] == 0) {
+                float* out = A.out + z * A.out_stride;
+                for (int i = tid; i < A.n_heads * hd; i += kAttnThreads) out[i] = 0.f;
+            }
+
+    const bool dim_ok = lane * 4 < hd;
+    const int my_g = lane / TPG, my_t = lane % TPG;
+    const int hd4 = hd / 4;
+    const int n_out = G * hd4;  // float4 outputs per (stream, kv head)
+    const int total = plan.first[B];
+    for (int item = blockIdx.x; item < total; item += gridDim.x) {
+        __syncthreads();  // shared partials of the previous chunk are consumed
+        int z = 0;
+        while (z + 1 < B && item >= plan.first[z + 1]) ++z;
+        const int n_active = plan.items[z];
+        const int local = item - plan.first[z];
+        const int h = local / n_active;
+        const int split = local - h * n_active;
+        const int len = plan.len[z];
+        const int per = plan.tpi[z] * TPG;
+        const int t_begin = plan.mask_start[z] + split * per;
+        const int t_end = min(len, t_begin + per);
+        const int ring_start = plan.start[z];
+        const float* kr = A.k_ring + z * A.ring_stride + (size_t)h * A.cap * hd + lane * 4;
+        const float* vr = A.v_ring + z * A.ring_stride + (size_t)h * A.cap * hd + lane * 4;
+        const float* qh = A.q + z * A.q_stride + (size_t)h * G * hd + lane * 4;
+
+        float4 q[G], acc[G];
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const int s = lane + 32 * r;
-            ms[r] = s < n_active ? __ldcg(bml + ((size_t)s * G + g) * 2) : -INFINITY;
-            ls[r] = s < n_active ? __ldcg(bml + ((size_t)s * G + g) * 2 + 1) : 0.f;
+        for (int g = 0; g < G; ++g) {
+            q[g] = dim_ok ? *reinterpret_cast<const float4*>(qh + (size_t)g * hd) : make_float4(0.f, 0.f, 0.f, 0.f);
+            acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        float M = fmaxf(ms[0], ms[1]);
+        float m_run = -INFINITY, l_run = 0.f;  // of head my_g
+
+        // warp w takes groups w, w + NW, ... of the chunk
+        for (int t0 = t_begin + warp * TPG; t0 < t_end; t0 += NW * TPG) {
+            float4 kk[TPG], vv[TPG];
 #pragma unroll
-        for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
-        float w[2], L = 0.f;
+            for (int j = 0; j < TPG; ++j) {
+                int slot = ring_start + (t0 + j < t_end ? t0 + j : t0);
+                if (slot >= A.cap) slot -= A.cap;
+                if (dim_ok) {
+                    kk[j] = __ldg(reinterpret_cast<const float4*>(kr + (size_t)slot * hd));
+                    vv[j] = __ldg(reinterpret_cast<const float4*>(vr + (size_t)slot * hd));
+                } else {
+                    kk[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    vv[j] = kk[j];
+                }
+            }
+            // ops.rs:108-113: scores q . k * scale
+            float sc[32];
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            w[r] = ms[r] == -INFINITY ? 0.f : expf(ms[r] - M);
-            L = fmaf(ls[r], w[r], L);
+            for (int g = 0; g < G; ++g)
+#pragma unroll
+                for (int j = 0; j < TPG; ++j) sc[g * TPG + j] = dot4(q[g], kk[j]);
+            transpose_reduce<32>(sc, lane);
+            float s = sc[0] * A.scale;
+            if (t0 + my_t >= t_end) s = -INFINITY;
+            // online softmax over this group (math.rs:67-88 restated incrementally)
+            float gm = s;
+#pragma unroll
+            for (int o = TPG / 2; o >= 1; o >>= 1) gm = fmaxf(gm, __shfl_xor_sync(FULL, gm, o));
+            const float m_new = fmaxf(m_run, gm);
+            const float p = (s == -INFINITY) ? 0.f : expf(s - m_new);
+            float ps = p;
+#pragma unroll
+            for (int o = TPG / 2; o >= 1; o >>= 1) ps += __shfl_xor_sync(FULL, ps, o);
+            const float alpha = (m_run == -INFINITY) ? 0.f : expf(m_run - m_new);
+            l_run = l_run * alpha + ps;
+            m_run = m_new;
+            // PV (ops.rs:117-128) on this lane's dims for every head
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const float a = __shfl_sync(FULL, alpha, g * TPG);
+                acc[g].x *= a;
+                acc[g].y *= a;
+                acc[g].z *= a;
+                acc[g].w *= a;
+#pragma unroll
+                for (int j = 0; j < TPG; ++j) {
+                    const float pj = __shfl_sync(FULL, p, g * TPG + j);
+                    acc[g].x = fmaf(pj, vv[j].x, acc[g].x);
+                    acc[g].y = fmaf(pj, vv[j].y, acc[g].y);
+                    acc[g].z = fmaf(pj, vv[j].z, acc[g].z);
+                    acc[g].w = fmaf(pj, vv[j].w, acc[g].w);
+                }
+            }
         }
+
+        // Combine the warps of this chunk in shared memory.
+        if (dim_ok)
 #pragma unroll
-        for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(0xFFFFFFFFu, L, o);
-        const float invL = L > 0.f ? 1.0f / L : 0.f;
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const int s = lane + 32 * r;
-            if (s < n_active) w_s[g * kMaxSplits + s] = w[r] * invL;
+            for (int g = 0; g < G; ++g) *reinterpret_cast<float4*>(&wacc[warp][g][lane * 4]) = acc[g];
+        if (my_t == 0) {
+            wml[warp][my_g][0] = m_run;
+            wml[warp][my_g][1] = l_run;
         }
-    }
-    __syncthreads();
-    // ... then each output vector is a weighted sum over the splits, loaded
-    // eight splits at a time with independent loads.
-    const size_t vstride = acc_stride / VEC;
-    for (int o = tid; o < n_out; o += kAttnThreads) {
-        const int g = o / hdv;
-        const T* pv = reinterpret_cast<const T*>(bacc) + o;
-        const float* wg = w_s + g * kMaxSplits;
-        T sum;
-        fzero(sum);
-        for (int s0 = 0; s0 < n_active; s0 += 8) {
-            T v[8];
+        __syncthreads();
+        const size_t acc_stride = (size_t)G * hd;
+        const size_t ml_base = (size_t)A.n_kv * A.nsplit * acc_stride;
+        float* part = A.part + z * A.part_stride;
+        float* pacc = part + ((size_t)h * A.nsplit + split) * acc_stride;
+        float* pml = part + ml_base + ((size_t)h * A.nsplit + split) * G * 2;
+        for (int o = tid; o < n_out; o += kAttnThreads) {
+            const int g = o / hd4, d = (o - g * hd4) * 4;
+            float M = -INFINITY;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                if (s0 + j < n_active)
-                    v[j] = __ldcg(pv + (size_t)(s0 + j) * vstride);
-                else
-                    fzero(v[j]);
+            for (int w = 0; w < NW; ++w) M = fmaxf(M, wml[w][g][0]);
+            float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+            float L = 0.f;
+#pragma unroll
+            for (int w = 0; w < NW; ++w) {
+                const float mw = wml[w][g][0];
+                const float e = mw == -INFINITY ? 0.f : expf(mw - M);
+                const float4 a = *reinterpret_cast<const float4*>(&wacc[w][g][d]);
+                sum.x = fmaf(e, a.x, sum.x);
+                sum.y = fmaf(e, a.y, sum.y);
+                sum.z = fmaf(e, a.z, sum.z);
+                sum.w = fmaf(e, a.w, sum.w);
+                L = fmaf(e, wml[w][g][1], L);
+            }
+            *reinterpret_cast<float4*>(pacc + (size_t)g * hd + d) = sum;
+            if (d == 0) {
+                pml[g * 2] = M;
+                pml[g * 2 + 1] = L;
+            }
+        }
+        __threadfence();
+        __syncthreads();
+        unsigned* tickets = A.tickets + (size_t)z * A.n_kv;
+        if (tid == 0) {
+            const unsigned ticket = atomicAdd(&tickets[h], 1u);
+            flag_s = (ticket == (unsigned)(n_active - 1)) ? 1 : 0;
+        }
+        __syncthreads();
+        if (!flag_s) continue;
+        __threadfence();
+
+        // Last chunk of this (stream, kv head): merge every chunk, fixed order.
+        const float* bacc = part + (size_t)h * A.nsplit * acc_stride;
+        const float* bml = part + ml_base + (size_t)h * A.nsplit * G * 2;
+        for (int g = warp; g < G; g += NW) {
+            float ms[2], ls[2];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const int sp = lane + 32 * r;
+                ms[r] = sp < n_active ? __ldcg(bml + ((size_t)sp * G + g) * 2) : -INFINITY;
+                ls[r] = sp < n_active ? __ldcg(bml + ((size_t)sp * G + g) * 2 + 1) : 0.f;
+            }
+            float M = fmaxf(ms[0], ms[1]);
+#pragma unroll
+            for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
+            float w[2], L = 0.f;
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                w[r] = ms[r] == -INFINITY ? 0.f : expf(ms[r] - M);
+                L = fmaf(ls[r], w[r], L);
             }
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                if (s0 + j < n_active) faxpy(sum, wg[s0 + j], v[j]);
+            for (int o = 16; o; o >>= 1) L += __shfl_xor_sync(FULL, L, o);
+            const float invL = L > 0.f ? 1.0f / L : 0.f;
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                const int sp = lane + 32 * r;
+                if (sp < n_active) w_s[g][sp] = w[r] * invL;
+            }
         }
-        *reinterpret_cast<T*>(out_h + (size_t)o * VEC) = sum;
+        __syncthreads();
+        float* out = A.out + z * A.out_stride + (size_t)h * G * hd;
+        for (int o = tid; o < n_out; o += kAttnThreads) {
+            const int g = o / hd4, d = (o - g * hd4) * 4;
+            const float* pv = bacc + (size_t)g * hd + d;
+            float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int s0 = 0; s0 < n_active; s0 += 16) {  // 16 independent loads in flight
+                float4 v[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    v[j] = s0 + j < n_active ? __ldcg(reinterpret_cast<const float4*>(pv + (size_t)(s0 + j) * acc_stride))
+                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    if (s0 + j < n_active) {
+                        const float wsp = w_s[g][s0 + j];
+                        sum.x = fmaf(wsp, v[j].x, sum.x);
+                        sum.y = fmaf(wsp, v[j].y, sum.y);
+                        sum.z = fmaf(wsp, v[j].z, sum.z);
+                        sum.w = fmaf(wsp, v[j].w, sum.w);
+                    }
+                }
+            }
+            *reinterpret_cast<float4*>(out + (size_t)g * hd + d) = sum;
+        }
+        if (tid == 0) tickets[h] = 0u;
     }
-    if (tid == 0) tickets[h] = 0u;
 }
 
 }  // namespace
@@ -347,6 +673,34 @@ size_t attn_smem_bytes(int n_heads, int n_kv, int hd) {
     return floats * 4;
 }
 
+// Resident CTAs of the persistent attention grid: as many as fit on every SM.
+int attn_grid_ctas(int n_heads, int n_kv, int hd) {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+    }
+    const size_t smem = attn_smem_bytes(n_heads, n_kv, hd) + sizeof(AttnPlan) + 1024;
+    int per_sm = (int)((227 * 1024) / smem);
+    if (per_sm < 1) per_sm = 1;
+    if (per_sm > 4) per_sm = 4;
+    return sms * per_sm;
+}
+
+// Persistent grid of the warp-per-chunk kernel: three 4-warp CTAs per SM.
+int attn_warp_grid_ctas() {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
+    }
+    return 3 * sms;
+}
+
+int attn_max_splits() { return kMaxSplits; }
+
 int attn_splits_for(int n_kv, int num_sms) {
     int s = (2 * num_sms + n_kv - 1) / n_kv;
     if (s < 1) s = 1;
@@ -363,8 +717,13 @@ cudaError_t attn_prepare(int /*dev*/) {
 }
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
+    if (a.n_streams > 8 || a.nsplit < 1 || a.nsplit > kMaxSplits) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.n_kv, a.nsplit, a.n_streams > 1 ? a.n_streams : 1);
+    const int B = a.n_streams > 1 ? a.n_streams : 1;
+    int grid = attn_grid_ctas(a.n_heads, a.n_kv, a.hd);
+    const long long max_items = (long long)B * a.n_kv * a.nsplit;
+    if (grid > max_items) grid = (int)max_items;
+    cfg.gridDim = dim3(grid, 1, 1);
     cfg.blockDim = dim3(kAttnThreads, 1, 1);
     cfg.dynamicSmemBytes = attn_smem_bytes(a.n_heads, a.n_kv, a.hd);
     cfg.stream = s;
@@ -374,7 +733,15 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
     void* args[] = {(void*)&a};
+    const int G = a.n_heads / a.n_kv;
     void* k = (a.hd % 4 == 0) ? (void*)attn_split_kernel<4> : (void*)attn_split_kernel<1>;
+    if (a.hd % 4 == 0 && a.hd <= 128 && (G == 4 || G == 8)) {
+        k = G == 4 ? (void*)attn_warp_kernel<4> : (void*)attn_warp_kernel<8>;
+        cfg.dynamicSmemBytes = 0;
+        int g2 = attn_warp_grid_ctas();
+        if (g2 > max_items) g2 = (int)max_items;
+        cfg.gridDim = dim3(g2 > 0 ? g2 : 1, 1, 1);
+    }
     return cudaLaunchKernelExC(&cfg, k, args);
 }
 

@@ -537,6 +537,10 @@ int tile_into(vox_ctx* c, unsigned char** dst, const void* src, int rows, int K)
 // Allocate the multi-stream buffers once and (re)tile stale weights.
 int ensure_batch(vox_ctx* c) {
     TRY(batch_supported(c));
+    if (c->opt.vocab == 0 || !c->head_ready || !c->embed_ready)
+        return fail(VOX_ERR_NOT_READY, "the multi-stream path needs the embedding and LM head");
+    for (size_t l = 0; l < c->layers.size(); ++l)
+        if (!c->layers[l].ready) return fail(VOX_ERR_NOT_READY, "layer %zu weights not uploaded", l);
     BatchBufs& b = c->bb;
     const int dim = (int)c->cfg.dim, hid = (int)c->cfg.hidden_dim, qd = (int)c->q_dim;
     const int vocab = (int)c->opt.vocab;
@@ -552,7 +556,7 @@ int ensure_batch(vox_ctx* c) {
             tiles = std::max(tiles, (size_t)p->tiles);
         }
         const size_t nkv = c->cfg.n_kv_heads, hd = c->cfg.head_dim, G = c->cfg.n_heads / nkv;
-        const size_t ns = (size_t)attn_splits_for((int)nkv, c->num_sms);
+        const size_t ns = (size_t)attn_max_splits();
         CUDA_TRY(dalloc(&b.hid, 8 * (size_t)dim));
         CUDA_TRY(dalloc(&b.hmid, 8 * (size_t)dim));
         CUDA_TRY(dalloc(&b.q, 8 * (size_t)qd));
@@ -567,6 +571,11 @@ int ensure_batch(vox_ctx* c) {
         CUDA_TRY(cudaMemset(b.tickets, 0, tiles * sizeof(unsigned)));
         CUDA_TRY(dalloc(&b.attn_tickets, 8 * nkv));
         CUDA_TRY(cudaMemset(b.attn_tickets, 0, 8 * nkv * sizeof(unsigned)));
+        CUDA_TRY(cudaMemset(b.hid, 0, 8 * (size_t)dim * 4));
+        CUDA_TRY(cudaMemset(b.hmid, 0, 8 * (size_t)dim * 4));
+        CUDA_TRY(cudaMemset(b.attn, 0, 8 * (size_t)qd * 4));
+        CUDA_TRY(cudaMemset(b.act, 0, 8 * (size_t)hid * 4));
+        CUDA_TRY(cudaMemset(b.ssp, 0, 8 * (size_t)((dim + 127) / 128) * 4));
         CUDA_TRY(dalloc(&b.steps, 8));
         CUDA_TRY(cudaMemset(b.steps, 0, 8 * sizeof(StepState)));
         CUDA_TRY(dalloc(&b.tok_out, 8));
@@ -620,7 +629,7 @@ int enqueue_batch_step(vox_ctx* c, vox_kv* kv, bool pdl) {
     const long long ring_stride = (long long)kv->stream_elems();
     const int cap = (int)kv->cap, win = (int)kv->window;
     const int nkv = (int)c->cfg.n_kv_heads, hd = (int)c->cfg.head_dim, G = (int)(c->cfg.n_heads / nkv);
-    int nsplit = attn_splits_for(nkv * B, c->num_sms);
+    const int nsplit = attn_max_splits();  // chunks per (stream, kv head) at most
     CUDA_TRY(record_launch(c, launch_bg_embed(c->embed, (int)c->opt.vocab, dim, bb.steps, B, bb.hid, bb.ssp,
                                               c->err, c->stream, pdl)));
     for (size_t l = 0; l < c->layers.size(); ++l) {
@@ -1036,7 +1045,7 @@ int vox_ctx_create(const vox_decoder_config* cfg, const vox_ctx_options* opt, vo
             return bail(fail(VOX_ERR_UNSUPPORTED, "no GEMV plan for rows %d x K %d", p->rows, p->K));
     if (o.vocab && (c->p_head.grid < 1 || c->p_head.smem > gemv_max_smem()))
         return bail(fail(VOX_ERR_UNSUPPORTED, "no LM-head plan for vocab %zu", (size_t)o.vocab));
-    c->nsplit = attn_splits_for((int)cfg->n_kv_heads, c->num_sms);
+    c->nsplit = attn_max_splits();
 
     // Persistent token kernel: bf16 weights, a vocabulary, supported shapes,
     // cooperative launch, and one CTA per SM fitting in shared memory.
@@ -1725,6 +1734,51 @@ int vox_profile_gemv(vox_ctx* c, int which, size_t n, float* avg_ms, uint64_t* b
     CUDA_TRY(cudaEventElapsedTime(&ms, c->ev[14], c->ev[15]));
     *avg_ms = ms / (float)n;
     if (bytes_per_launch) *bytes_per_launch = (uint64_t)plan->rows * (uint64_t)plan->K * (uint64_t)c->wsize;
+    return check_device_errors(c);
+}
+
+int vox_profile_bgemm(vox_ctx* c, int which, size_t n_streams, size_t n, float* avg_ms, uint64_t* bytes_per_launch) {
+    if (!c || !avg_ms || n == 0) return fail(VOX_ERR_INVALID_ARG, "bad argument");
+    if (which < 1 || which > 5) return fail(VOX_ERR_INVALID_ARG, "which must be 1..5");
+    if (n_streams < 1 || n_streams > 8) return fail(VOX_ERR_INVALID_ARG, "n_streams must be 1..8");
+    for (size_t l = 0; l < c->layers.size(); ++l)
+        if (!c->layers[l].ready) return fail(VOX_ERR_NOT_READY, "layer %zu weights not uploaded", l);
+    CUDA_TRY(cudaSetDevice(c->dev));
+    TRY(ensure_batch(c));
+    BatchBufs& bb = c->bb;
+    const int B = (int)n_streams, dim = (int)c->cfg.dim, hid = (int)c->cfg.hidden_dim, qd = (int)c->q_dim;
+    const BgPlan& p = which == 1 ? bb.p_o : which == 2 ? bb.p_w13 : which == 3 ? bb.p_w2 : which == 4 ? bb.p_head
+                                                                                                      : bb.p_qkv;
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    CUDA_TRY(cudaEventRecord(c->ev[14], c->stream));
+    for (size_t i = 0; i < n; ++i) {
+        const LayerDev& L = c->layers[i % c->layers.size()];
+        BgArgs a;
+        if (which == 1) {
+            a = bg_args(c, p, L.wo_t, B, BG_RESID);
+            a.x = bb.attn; a.x_stride = qd; a.y = bb.hmid; a.y_stride = dim; a.resid = bb.hid; a.ssp_out = bb.ssp;
+        } else if (which == 2) {
+            a = bg_args(c, p, L.w13_t, B, BG_SWIGLU);
+            a.x = bb.hmid; a.x_stride = dim; a.norm_w = L.ffn_norm; a.ssp = bb.ssp; a.y = bb.act; a.y_stride = hid;
+        } else if (which == 3) {
+            a = bg_args(c, p, L.w2_t, B, BG_RESID);
+            a.x = bb.act; a.x_stride = hid; a.y = bb.hmid; a.y_stride = dim; a.resid = bb.hmid; a.ssp_out = bb.ssp;
+        } else if (which == 4) {
+            a = bg_args(c, p, c->head_t, B, BG_ARGMAX);
+            a.x = bb.hid; a.x_stride = dim; a.norm_w = c->final_norm; a.ssp = bb.ssp; a.y = bb.logits;
+            a.y_stride = (long long)c->opt.vocab; a.am_part = bb.am;
+        } else {
+            a = bg_args(c, p, L.wqkv_t, B, BG_STORE);
+            a.x = bb.hid; a.x_stride = dim; a.y = bb.act; a.y_stride = (long long)c->qkv_rows;
+        }
+        CUDA_TRY(record_launch(c, launch_bgemm(a, p.grid, c->stream, true)));
+    }
+    CUDA_TRY(cudaEventRecord(c->ev[15], c->stream));
+    CUDA_TRY(cudaEventSynchronize(c->ev[15]));
+    float ms = 0.f;
+    CUDA_TRY(cudaEventElapsedTime(&ms, c->ev[14], c->ev[15]));
+    *avg_ms = ms / (float)n;
+    if (bytes_per_launch) *bytes_per_launch = (uint64_t)p.rows * (uint64_t)p.K * 2u;
     return check_device_errors(c);
 }
 

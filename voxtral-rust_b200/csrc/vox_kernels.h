@@ -227,6 +227,7 @@ cudaError_t gemv_prepare(int dev);   // raise per-kernel smem limits once per de
 cudaError_t launch_gemv(const GemvPlan& p, const GemvArgs& a, int epi, cudaStream_t s, bool pdl);
 
 int attn_splits_for(int n_kv, int num_sms);
+int attn_max_splits();  // most chunks per (stream, kv head) a launch may use
 bool attn_supported(int n_heads, int n_kv, int hd);
 size_t attn_smem_bytes(int n_heads, int n_kv, int hd);
 cudaError_t attn_prepare(int dev);

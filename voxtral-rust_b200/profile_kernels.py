@@ -6,7 +6,9 @@ suitable for an ncu capture).
 
 --which o|w13|w2|head runs vox_profile_gemv (launches cycle over the layers);
 --which step runs whole token steps of a full-width model with `--layers`
-layers and the 131072-token vocabulary.
+layers and the 131072-token vocabulary; --which batch runs multi-stream steps
+of `--streams` streams (contexts uniform in [256, 4096)); --which
+bo|bw13|bw2|bhead|bqkv times one multi-stream tensor-core GEMM.
 """
 from __future__ import annotations
 
@@ -21,7 +23,9 @@ sys.path.insert(0, ROOT)
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--which", default="w13", choices=["o", "w13", "w2", "head", "step"])
+    ap.add_argument("--which", default="w13",
+                    choices=["o", "w13", "w2", "head", "step", "batch", "bo", "bw13", "bw2", "bhead", "bqkv"])
+    ap.add_argument("--streams", type=int, default=8)
     ap.add_argument("--layers", type=int, default=2)
     ap.add_argument("--launches", type=int, default=8)
     ap.add_argument("--steps", type=int, default=8)
@@ -31,7 +35,8 @@ def main():
     V = importlib.import_module("voxtral-rust_b200")
     cfg = V.DecoderConfig(dim=3072, hidden_dim=9216, n_heads=32, n_kv_heads=8, head_dim=128,
                           sliding_window=8192, norm_eps=1e-5, rope_theta=1e6)
-    vocab = 131072 if args.which in ("head", "step") else 0
+    batched = args.which.startswith("b")
+    vocab = 131072 if args.which in ("head", "step") or batched else 0
     with V.Context(cfg, n_layers=args.layers, vocab=vocab, step_mode=args.mode) as ctx:
         ctx.init_random(0, 0.02)
         if args.which == "step":
@@ -43,6 +48,30 @@ def main():
             ctx.record_event(1)
             ms = ctx.elapsed_ms(0, 1) / args.steps
             print(f"step: {ms * 1e3:.1f} us per token ({args.layers} layers + LM head)")
+            return
+        if args.which == "batch":
+            import numpy as np
+            rng = np.random.default_rng(1000)
+            lens = [int(x) for x in rng.integers(256, 4096, args.streams)]
+            kv = V.RollingKvCache(ctx, args.layers, 8, 128, 8192, n_streams=args.streams)
+            for s, n in enumerate(lens):
+                kv.stream(s).fill_random(n, 0, 5000000 + 100 * s, 1.0)
+            toks = [int(x) for x in rng.integers(0, vocab, args.streams)]
+            ctx.model_generate_batch(kv, toks, lens, 2)  # warm-up
+            pos = [n + 2 for n in lens]
+            ctx.synchronize()
+            ctx.record_event(0)
+            ctx.model_generate_batch(kv, toks, pos, args.steps)
+            ctx.record_event(1)
+            ms = ctx.elapsed_ms(0, 1) / args.steps
+            print(f"batch step: {ms * 1e3:.1f} us per step of {args.streams} streams "
+                  f"({args.layers} layers + LM head), contexts {lens}")
+            return
+        if batched:
+            which = {"bo": 1, "bw13": 2, "bw2": 3, "bhead": 4, "bqkv": 5}[args.which]
+            ctx.profile_bgemm(which, args.streams, 2)  # warm-up
+            ms, nbytes = ctx.profile_bgemm(which, args.streams, args.launches)
+            print(f"{args.which}: {ms * 1e3:.2f} us per launch, {nbytes} B, {nbytes / ms / 1e6:.1f} GB/s")
             return
         which = {"o": 1, "w13": 2, "w2": 3, "head": 4}[args.which]
         ctx.profile_gemv(which, 2)  # warm-up
