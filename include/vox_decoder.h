@@ -74,7 +74,10 @@ typedef struct vox_ctx_options {
  * append, attention, o-proj, w1|w3+SwiGLU, w2) plus LM head and argmax.
  * VOX_STEP_PERSISTENT: the whole step as one cooperative persistent kernel
  * (bf16 weights only; falls back to VOX_STEP_LAYERS when the shapes do not
- * fit it).  VOX_STEP_AUTO picks the faster one on B200, currently LAYERS. */
+ * fit it).  VOX_STEP_AUTO picks the faster one on B200, currently LAYERS.
+ * For the multi-stream step (vox_model_step_batch) PERSISTENT runs o-proj,
+ * w1|w3, w2 and the next q|k|v as one persistent launch per layer; the
+ * other modes launch every GEMM on its own. */
 typedef enum vox_step_mode { VOX_STEP_AUTO = 0, VOX_STEP_LAYERS = 1, VOX_STEP_PERSISTENT = 2 } vox_step_mode;
 
 typedef struct vox_f32_slice { const float* ptr; size_t len; } vox_f32_slice;
@@ -242,7 +245,8 @@ int vox_profile_gemv(vox_ctx* ctx, int which, size_t n_launches, float* avg_ms,
 
 /* Same for the multi-stream tensor-core GEMM with n_streams input vectors
  * (needs the embedding and LM head): which 1 o-proj, 2 w1|w3 (SwiGLU),
- * 3 w2, 4 LM head, 5 q|k|v (plain store). */
+ * 3 w2, 4 LM head, 5 q|k|v (plain store), 6 o-proj + w1|w3 + w2 + q|k|v as
+ * one persistent launch (bytes_per_launch counts all four). */
 int vox_profile_bgemm(vox_ctx* ctx, int which, size_t n_streams, size_t n_launches, float* avg_ms,
                       uint64_t* bytes_per_launch);
 /* ---- op-level entry points (host buffers) ------------------------------------ */

@@ -16,8 +16,8 @@ def V():
     return vox()
 
 
-def make_ctx(V, c, n_layers, vocab, seed=0):
-    ctx = V.Context(V.DecoderConfig(**c), n_layers=n_layers, vocab=vocab)
+def make_ctx(V, c, n_layers, vocab, seed=0, step_mode=0):
+    ctx = V.Context(V.DecoderConfig(**c), n_layers=n_layers, vocab=vocab, step_mode=step_mode)
     ctx.init_random(seed, 0.02)
     return ctx
 
@@ -33,13 +33,13 @@ def oracle_cache(oracle, c, n_layers, n_tokens, seed, tensor_id):
     return oc
 
 
-def run_batch(V, oracle, c, n_layers, vocab, lens, n_steps, seed=0, greedy=False):
+def run_batch(V, oracle, c, n_layers, vocab, lens, n_steps, seed=0, greedy=False, step_mode=0):
     """Teacher-forced (or greedy) steps of len(lens) streams on both sides."""
     B = len(lens)
     m = oracle_model(oracle, c, n_layers, vocab, seed)
     ids = oracle.gen_uniform_ids(seed, 3000001, vocab, B * n_steps).reshape(n_steps, B)
     worst = 0.0
-    with make_ctx(V, c, n_layers, vocab, seed) as ctx:
+    with make_ctx(V, c, n_layers, vocab, seed, step_mode) as ctx:
         kv = V.RollingKvCache(ctx, n_layers, c["n_kv_heads"], c["head_dim"], c["sliding_window"], n_streams=B)
         ocs = []
         for s, n in enumerate(lens):
@@ -79,8 +79,11 @@ def run_batch(V, oracle, c, n_layers, vocab, lens, n_steps, seed=0, greedy=False
     return worst
 
 
-def test_batch_step_three_streams(V, oracle):
-    run_batch(V, oracle, FULL, 2, 8192, [5, 37, 200], 3)
+@pytest.mark.parametrize("step_mode", [0, 2])
+def test_batch_step_three_streams(V, oracle, step_mode):
+    """Both ways of launching the GEMMs: one launch per GEMM (default) and one
+    persistent chain per layer (VOX_STEP_PERSISTENT)."""
+    run_batch(V, oracle, FULL, 3, 8192, [5, 37, 200], 3, step_mode=step_mode)
 
 
 def test_batch_step_eviction(V, oracle):
@@ -88,6 +91,7 @@ def test_batch_step_eviction(V, oracle):
     (kv.rs:48-88), with bit-exact len/pos_offset per stream."""
     c = dict(FULL, sliding_window=48)
     run_batch(V, oracle, c, 2, 4096, [46, 48, 1, 30], 4)
+    run_batch(V, oracle, c, 2, 4096, [47, 2], 3, step_mode=2)
 
 
 def test_batch_small_shapes_and_one_stream(V, oracle):

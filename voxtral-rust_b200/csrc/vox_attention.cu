@@ -407,11 +407,16 @@ __device__ __forceinline__ float dot4(const float4& a, const float4& b) {
     return fmaf(a.w, b.w, d);
 }
 
+constexpr int kWarpStages = 3;  // per-warp ring depth of the warp-per-chunk kernel
+
 template <int G>
-__global__ void __launch_bounds__(kAttnThreads, 3) attn_warp_kernel(const AttnArgs A) {
+__global__ void __launch_bounds__(kAttnThreads, 2) attn_warp_kernel(const AttnArgs A) {
     constexpr int TPG = 32 / G;           // tokens per group: G * TPG = 32 scores per step
     constexpr int NW = kAttnThreads / 32; // warps per CTA
     constexpr int HD = 128;               // largest head_dim (4 dims per lane)
+    constexpr int D = kWarpStages;
+    extern __shared__ __align__(128) unsigned char ring_smem[];  // [NW][D][K rows | V rows]
+    __shared__ uint64_t wbar[NW][D];
     __shared__ AttnPlan plan;
     __shared__ __align__(16) float wacc[NW][G][HD];  // per-warp accumulators of the chunk
     __shared__ float wml[NW][G][2];                  // per-warp (m, l)
@@ -422,6 +427,8 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_warp_kernel(const AttnAr
     const int B = A.n_streams > 1 ? A.n_streams : 1;
     const unsigned FULL = 0xFFFFFFFFu;
 
+    if (tid < NW * D) mbar_init(&wbar[tid / D][tid % D], 1);
+    if (tid == 0) fence_barrier_init();
     pdl_allow_dependents();
     pdl_wait_prior_grids();
 
@@ -466,6 +473,7 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_warp_kernel(const AttnAr
     const bool dim_ok = lane * 4 < hd;
     const int my_g = lane / TPG, my_t = lane % TPG;
     const int hd4 = hd / 4;
+    uint32_t phase = 0;  // parity of the next completion of each of this warp's stages
     const int n_out = G * hd4;  // float4 outputs per (stream, kv head)
     const int total = plan.first[B];
     for (int item = blockIdx.x; item < total; item += gridDim.x) {
@@ -481,8 +489,6 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_warp_kernel(const AttnAr
         const int t_begin = plan.mask_start[z] + split * per;
         const int t_end = min(len, t_begin + per);
         const int ring_start = plan.start[z];
-        const float* kr = A.k_ring + z * A.ring_stride + (size_t)h * A.cap * hd + lane * 4;
-        const float* vr = A.v_ring + z * A.ring_stride + (size_t)h * A.cap * hd + lane * 4;
         const float* qh = A.q + z * A.q_stride + (size_t)h * G * hd + lane * 4;
 
         float4 q[G], acc[G];
@@ -493,22 +499,52 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_warp_kernel(const AttnAr
         }
         float m_run = -INFINITY, l_run = 0.f;  // of head my_g
 
-        // warp w takes groups w, w + NW, ... of the chunk
-        for (int t0 = t_begin + warp * TPG; t0 < t_end; t0 += NW * TPG) {
-            float4 kk[TPG], vv[TPG];
-#pragma unroll
-            for (int j = 0; j < TPG; ++j) {
-                int slot = ring_start + (t0 + j < t_end ? t0 + j : t0);
-                if (slot >= A.cap) slot -= A.cap;
-                if (dim_ok) {
-                    kk[j] = __ldg(reinterpret_cast<const float4*>(kr + (size_t)slot * hd));
-                    vv[j] = __ldg(reinterpret_cast<const float4*>(vr + (size_t)slot * hd));
-                } else {
-                    kk[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-                    vv[j] = kk[j];
-                }
+        // Warp w takes groups w, w + NW, ... of the chunk.  Each group's K rows
+        // and V rows are contiguous in the ring (two pieces at the wrap), so
+        // lane 0 fetches them with 1-D bulk copies into the warp's own
+        // D-stage ring; all lanes then read their four dims per row.
+        const int n_groups = (t_end - t_begin + TPG - 1) / TPG;
+        const int n_my = warp < n_groups ? (n_groups - warp + NW - 1) / NW : 0;
+        const size_t row_bytes = (size_t)hd * 4;
+        const uint32_t stage_bytes = (uint32_t)(2 * TPG * row_bytes);
+        unsigned char* my_ring = ring_smem + (size_t)warp * D * stage_bytes;
+        const float* kbase = A.k_ring + z * A.ring_stride + (size_t)h * A.cap * hd;
+        const float* vbase = A.v_ring + z * A.ring_stride + (size_t)h * A.cap * hd;
+        auto issue = [&](int k) {
+            const int t0 = t_begin + (warp + NW * k) * TPG;
+            const int ntok = min(TPG, t_end - t0);
+            int slot0 = ring_start + t0;
+            if (slot0 >= A.cap) slot0 -= A.cap;
+            const int n1 = min(ntok, A.cap - slot0);
+            unsigned char* st = my_ring + (size_t)(k % D) * stage_bytes;
+            uint64_t* bar = &wbar[warp][k % D];
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive_expect_tx(bar, (uint32_t)(2 * ntok * row_bytes));
+            bulk_copy_g2s_nohint(st, kbase + (size_t)slot0 * hd, (uint32_t)(n1 * row_bytes), bar);
+            bulk_copy_g2s_nohint(st + TPG * row_bytes, vbase + (size_t)slot0 * hd, (uint32_t)(n1 * row_bytes), bar);
+            if (n1 < ntok) {
+                bulk_copy_g2s_nohint(st + n1 * row_bytes, kbase, (uint32_t)((ntok - n1) * row_bytes), bar);
+                bulk_copy_g2s_nohint(st + TPG * row_bytes + n1 * row_bytes, vbase, (uint32_t)((ntok - n1) * row_bytes),
+                                     bar);
             }
-            // ops.rs:108-113: scores q . k * scale
+        };
+        if (lane == 0)
+            for (int k = 0; k < min(D, n_my); ++k) issue(k);
+        __syncwarp();
+
+        for (int k = 0; k < n_my; ++k) {
+            const int t0 = t_begin + (warp + NW * k) * TPG;
+            const int stg = k % D;
+            if (!mbar_wait(&wbar[warp][stg], (phase >> stg) & 1u) && lane == 0) raise_error(A.err, ERR_FULL_WAIT);
+            phase ^= 1u << stg;
+            const float* ks = reinterpret_cast<const float*>(my_ring + (size_t)stg * stage_bytes) + lane * 4;
+            const float* vs = ks + TPG * hd;
+            float4 kk[TPG];
+#pragma unroll
+            for (int j = 0; j < TPG; ++j)
+                kk[j] = dim_ok ? *reinterpret_cast<const float4*>(ks + (size_t)j * hd) : make_float4(0.f, 0.f, 0.f, 0.f);
+            // ops.rs:108-113: scores q . k * scale (rows past t_end hold stale data
+            // and are masked; their sums never mix with live ones)
             float sc[32];
 #pragma unroll
             for (int g = 0; g < G; ++g)
@@ -530,6 +566,11 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_warp_kernel(const AttnAr
             l_run = l_run * alpha + ps;
             m_run = m_new;
             // PV (ops.rs:117-128) on this lane's dims for every head
+            float4 vv[TPG];
+#pragma unroll
+            for (int j = 0; j < TPG; ++j)
+                vv[j] = (dim_ok && t0 + j < t_end) ? *reinterpret_cast<const float4*>(vs + (size_t)j * hd)
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
             for (int g = 0; g < G; ++g) {
                 const float a = __shfl_sync(FULL, alpha, g * TPG);
@@ -546,6 +587,8 @@ __global__ void __launch_bounds__(kAttnThreads, 3) attn_warp_kernel(const AttnAr
                     acc[g].w = fmaf(pj, vv[j].w, acc[g].w);
                 }
             }
+            __syncwarp();  // every lane has read this stage before it is refilled
+            if (lane == 0 && k + D < n_my) issue(k + D);
         }
 
         // Combine the warps of this chunk in shared memory.
@@ -688,7 +731,7 @@ int attn_grid_ctas(int n_heads, int n_kv, int hd) {
     return sms * per_sm;
 }
 
-// Persistent grid of the warp-per-chunk kernel: three 4-warp CTAs per SM.
+// Persistent grid of the warp-per-chunk kernel: two 4-warp CTAs per SM.
 int attn_warp_grid_ctas() {
     static int sms = 0;
     if (!sms) {
@@ -696,7 +739,7 @@ int attn_warp_grid_ctas() {
         cudaGetDevice(&dev);
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
     }
-    return 3 * sms;
+    return 2 * sms;
 }
 
 int attn_max_splits() { return kMaxSplits; }
@@ -709,8 +752,11 @@ int attn_splits_for(int n_kv, int num_sms) {
 }
 
 cudaError_t attn_prepare(int /*dev*/) {
-    cudaError_t e = cudaFuncSetAttribute(attn_split_kernel<4>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaError_t e = cudaFuncSetAttribute(attn_warp_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(attn_warp_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(attn_split_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(attn_split_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 200 * 1024);
@@ -737,7 +783,7 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
     void* k = (a.hd % 4 == 0) ? (void*)attn_split_kernel<4> : (void*)attn_split_kernel<1>;
     if (a.hd % 4 == 0 && a.hd <= 128 && (G == 4 || G == 8)) {
         k = G == 4 ? (void*)attn_warp_kernel<4> : (void*)attn_warp_kernel<8>;
-        cfg.dynamicSmemBytes = 0;
+        cfg.dynamicSmemBytes = (size_t)(kAttnThreads / 32) * kWarpStages * 2 * (32 / G) * a.hd * 4;
         int g2 = attn_warp_grid_ctas();
         if (g2 > max_items) g2 = (int)max_items;
         cfg.gridDim = dim3(g2 > 0 ? g2 : 1, 1, 1);

@@ -37,7 +37,7 @@ constexpr int kBK = 64;                      // K elements per block
 constexpr int kBlockBytes = kBM * kBK * 2;   // 16 KB
 constexpr int kStageBlocks = 2;              // blocks per ring stage
 constexpr int kStageBytes = kStageBlocks * kBlockBytes;
-constexpr int kStages = 4;
+constexpr int kStages = 4;                   // 128 KB ring in flight per SM
 constexpr int kN = 16;                       // UMMA N: 8 streams x (hi, lo)
 constexpr int kThreads = 256;                // w0 producer, w1 MMA, w4..w7 epilogue, w1..w7 X prep
 constexpr int kWorkers = kThreads - 32;      // every warp but the producer
@@ -115,7 +115,10 @@ __device__ __forceinline__ Item item_of(const BgArgs& A, int i) {
 constexpr unsigned kFull = 0xFFFFFFFFu;
 
 // Small shared state of the epilogue warpgroup.
+constexpr int kMaxSspParts = 64;  // RMSNorm partial sums per stream (dim <= 8192)
+
 struct EpiShared {
+    float ssp[kMaxSspParts * 8];  // RMSNorm partial sums of squares, staged
     float inv[8];     // per-stream RMSNorm factor
     float red[4][8];  // per-warp partial sums / maxima
     int redi[4][8];   // per-warp argmax indices
@@ -203,7 +206,7 @@ __device__ __forceinline__ void bg_epilogue(const BgArgs& A, int tile, int row, 
         for (int b = 0; b < 8; ++b) {
             sq[b] = 0.0f;
             if (live && b < A.B) {
-                const float v = __fadd_rn(A.resid[(size_t)b * A.y_stride + r], y[b]);
+                const float v = __fadd_rn(__ldcg(A.resid + (size_t)b * A.y_stride + r), y[b]);
                 A.y[(size_t)b * A.y_stride + r] = v;
                 sq[b] = __fmul_rn(v, v);
             }
@@ -274,11 +277,49 @@ __device__ __forceinline__ void bg_epilogue(const BgArgs& A, int tile, int row, 
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constant__ BgArgs A) {
+// All worker threads of every CTA: wait until all `n` CTAs have counted
+// themselves into `done` (bounded; false when the wait expired).  The
+// arrival is made by the caller after its own outputs are written.
+__device__ bool wait_all_ctas(unsigned* done, unsigned n, unsigned* err, EpiShared* es) {
+    if (threadIdx.x == 32) {
+        bool ok = true;
+        uint64_t t0 = 0;
+        uint32_t it = 0;
+        while (true) {
+            unsigned v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(done) : "memory");
+            if (v >= n) break;
+            if ((++it & 63u) == 0) {
+                const uint64_t now = global_timer_ns();
+                if (t0 == 0) {
+                    t0 = now;
+                } else if (now - t0 > kWaitLimitNs) {
+                    raise_error(err, ERR_GRID_WAIT);
+                    ok = false;
+                    break;
+                }
+            }
+        }
+        es->flag = ok ? 1 : 0;
+    }
+    named_barrier_sync(1, kWorkers);
+    return es->flag != 0;
+}
+
+// One launch runs a chain of up to kBgMaxPhases GEMMs back to back (o-proj,
+// w1|w3, w2 and the next layer's q|k|v, or the LM head).  The producer lane
+// streams the weights of every phase without a break, since weights never
+// depend on earlier phases; the workers of phase p > 0 wait until every CTA
+// has finished phase p - 1 (a completion counter in global memory) before
+// they read its outputs.  The 128 KB ring holds the next phase's first
+// blocks meanwhile, so the wait costs little HBM time.  All CTAs are
+// resident together: one CTA per SM, grid <= SM count, and a dependent
+// launch cannot start before every CTA of this one has started.
+__global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constant__ BgChain C) {
     extern __shared__ __align__(1024) unsigned char smem[];
     unsigned char* ring = smem;                                // kStages x 32 KB
     unsigned char* xs = smem + kStages * kStageBytes;          // X slab: one 512 B slab per K step
-    uint64_t* full = reinterpret_cast<uint64_t*>(xs + A.xslab_bytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(xs + C.xslab_bytes);
     uint64_t* empty = full + kStages;
     uint64_t* acc_full = empty + kStages;  // [2]
     uint64_t* acc_empty = acc_full + 2;    // [2]
@@ -286,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
     EpiShared* es = reinterpret_cast<EpiShared*>(tmem_base_s + 4);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n_items = A.tiles * A.splits;
+    unsigned* const err = C.ph[0].err;
 
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -312,32 +353,36 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
     const uint32_t tmem = *tmem_base_s;
     pdl_allow_dependents();
 
-    // ---- producer: stream this CTA's weight blocks (weights need no PDL wait) ----
+    // ---- producer: stream this CTA's weight blocks of every phase ----
     if (warp == 0) {
         if (lane == 0) {
             const uint64_t pol = l2_evict_first_policy();
             uint32_t g = 0;
             bool ok = true;
-            for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
-                const Item it = item_of(A, i);
-                const unsigned char* src = A.wt + ((size_t)it.tile * A.kbt + it.kb0) * kBlockBytes;
-                for (int kb = it.kb0; kb < it.kb1; kb += kStageBlocks, ++g) {
-                    const int slot = (int)(g % kStages);
-                    if (g >= (uint32_t)kStages && !mbar_wait(&empty[slot], ((g / kStages) - 1) & 1)) {
-                        raise_error(A.err, ERR_EMPTY_WAIT);
-                        ok = false;
-                        break;
+            for (int ph = 0; ph < C.n_phases && ok; ++ph) {
+                const BgArgs& A = C.ph[ph];
+                const int n_items = A.tiles * A.splits;
+                for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
+                    const Item it = item_of(A, i);
+                    const unsigned char* src = A.wt + ((size_t)it.tile * A.kbt + it.kb0) * kBlockBytes;
+                    for (int kb = it.kb0; kb < it.kb1; kb += kStageBlocks, ++g) {
+                        const int slot = (int)(g % kStages);
+                        if (g >= (uint32_t)kStages && !mbar_wait(&empty[slot], ((g / kStages) - 1) & 1)) {
+                            raise_error(err, ERR_EMPTY_WAIT);
+                            ok = false;
+                            break;
+                        }
+                        const int nb = min(kStageBlocks, it.kb1 - kb);
+                        mbar_arrive_expect_tx(&full[slot], (uint32_t)(nb * kBlockBytes));
+                        bulk_copy_g2s(ring + (size_t)slot * kStageBytes, src + (size_t)(kb - it.kb0) * kBlockBytes,
+                                      (uint32_t)(nb * kBlockBytes), &full[slot], pol);
                     }
-                    const int nb = min(kStageBlocks, it.kb1 - kb);
-                    mbar_arrive_expect_tx(&full[slot], (uint32_t)(nb * kBlockBytes));
-                    bulk_copy_g2s(ring + (size_t)slot * kStageBytes, src + (size_t)(kb - it.kb0) * kBlockBytes,
-                                  (uint32_t)(nb * kBlockBytes), &full[slot], pol);
                 }
             }
             // no copy may be in flight when the CTA exits
             const uint32_t first = g > (uint32_t)kStages ? g - kStages : 0u;
             for (uint32_t s = first; s < g; ++s)
-                if (!mbar_wait(&full[s % kStages], (s / kStages) & 1)) raise_error(A.err, ERR_DRAIN_WAIT);
+                if (!mbar_wait(&full[s % kStages], (s / kStages) & 1)) raise_error(err, ERR_DRAIN_WAIT);
         }
         // The producer warp takes no part in the rest (its lane 0 streams while
         // the other warps work), so the worker barriers below exclude it.
@@ -347,158 +392,207 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
 
     pdl_wait_prior_grids();
 
-    // This launch commits the single-token append of the layer's cache of
-    // every stream (the attention launch before it read the old state).
-    if (A.kv_commit && blockIdx.x == 0 && tid >= 32 && tid < 32 + A.B) {
-        KvState* st = A.kv_commit + (size_t)(tid - 32) * A.kv_state_stride;
-        *st = kv_after_single_append(*st, A.kv_window, A.ring_cap);
-    }
-    // Per-stream RMSNorm factor from the producer's partial sums of squares
-    // (math.rs:22: inv = 1 / sqrt(sum / dim + eps)), applied in the X prologue.
-    if (A.norm_w) {
-        if (tid >= 32 && tid < 40) {
-            const int b = tid - 32;
-            float inv = 1.0f;
-            if (b < A.B) {
-                float ss = 0.0f;
-                for (int p = 0; p < A.ssp_parts; ++p) ss += __ldcg(A.ssp + (size_t)p * 8 + b);
-                inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)A.K), A.eps)));
-            }
-            es->inv[b] = inv;
-        }
-        named_barrier_sync(1, kWorkers);
-    }
-
-    int cur_ks = -1;
     uint32_t g_mma = 0;
     bool mma_ok = true;  // after a wait expires the issuer stops waiting (the result is flagged)
-    int local = 0;  // items processed by this CTA
-    for (int i = blockIdx.x; i < n_items; i += gridDim.x, ++local) {
-        const Item it = item_of(A, i);
-        const int nkb = it.kb1 - it.kb0;
-        // ---- X slab for this split, built by warps 1..7 ----
-        if (it.ks != cur_ks) {
-            if (local > 0) {  // the previous item's MMAs read the old slab: wait for their commit
-                const int pb = (local - 1) & 1;
-                if (!mbar_wait(&acc_full[pb], ((local - 1) >> 1) & 1)) raise_error(A.err, ERR_FULL_WAIT);
-            }
-            const int kbase = it.kb0 * kBK;
-            const int nk8 = nkb * kBK / 8;  // 8-element chunks per stream
-            for (int e = tid - 32; e < 8 * nk8; e += kWorkers) {
-                const int b = e / nk8;
-                const int k = (e - b * nk8) * 8;
-                uint32_t hi[4] = {0, 0, 0, 0}, lo[4] = {0, 0, 0, 0};
-                if (b < A.B) {
-                    const float* xp = A.x + (size_t)b * A.x_stride + kbase + k;
-                    const float4 a0 = __ldcg(reinterpret_cast<const float4*>(xp));
-                    const float4 a1 = __ldcg(reinterpret_cast<const float4*>(xp + 4));
-                    float v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                    if (A.norm_w) {  // math.rs:23-24: x * inv * w, in that order
-                        const float4 g0 = __ldg(reinterpret_cast<const float4*>(A.norm_w + kbase + k));
-                        const float4 g1 = __ldg(reinterpret_cast<const float4*>(A.norm_w + kbase + k + 4));
-                        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-                        const float inv = es->inv[b];
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(__fmul_rn(v[j], inv), gv[j]);
-                    }
-#pragma unroll
-                    for (int j = 0; j < 8; j += 2) {
-                        const uint16_t h0 = f2bf(v[j]), h1 = f2bf(v[j + 1]);
-                        const uint16_t l0 = f2bf(v[j] - bf16_bits_to_f32(h0));
-                        const uint16_t l1 = f2bf(v[j + 1] - bf16_bits_to_f32(h1));
-                        hi[j >> 1] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-                        lo[j >> 1] = (uint32_t)l0 | ((uint32_t)l1 << 16);
-                    }
-                }
-                // core (n8, k2) of K-step s at s*512 + (k2*2 + n8)*128 + row*16:
-                // hi parts are rows 0..7 (n8 = 0), lo parts rows 8..15 (n8 = 1)
-                const int s = k / 16, k2 = (k / 8) & 1;
-                unsigned char* base = xs + (size_t)s * 512 + (size_t)k2 * 256;
-                *reinterpret_cast<uint4*>(base + b * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<uint4*>(base + 128 + b * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-            }
-            // generic-proxy writes must be visible to the tensor core (async proxy)
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    int local = 0;       // items processed by this CTA, over all phases
+    for (int ph = 0; ph < C.n_phases; ++ph) {
+        const BgArgs& A = C.ph[ph];
+        if (ph > 0) {
+            // This CTA's outputs of the previous phase are written (every worker
+            // passed its epilogue); count the CTA in, then wait for all others.
             named_barrier_sync(1, kWorkers);
-            cur_ks = it.ks;
+            if (tid == 32) {
+                __threadfence();
+                atomicAdd(C.done + ph - 1, 1u);
+            }
+            if (!wait_all_ctas(C.done + ph - 1, gridDim.x, err, es)) mma_ok = false;
+        }
+        // This launch commits the single-token append of the layer's cache of
+        // every stream (the attention launch before it read the old state).
+        if (A.kv_commit && blockIdx.x == 0 && tid >= 32 && tid < 32 + A.B) {
+            KvState* st = A.kv_commit + (size_t)(tid - 32) * A.kv_state_stride;
+            *st = kv_after_single_append(*st, A.kv_window, A.ring_cap);
+        }
+        // Per-stream RMSNorm factor from the producer's partial sums of squares
+        // (math.rs:22: inv = 1 / sqrt(sum / dim + eps)), applied in the X prologue.
+        if (A.norm_w) {
+            // all partials loaded at once (one L2 round trip), summed in part order
+            const int n = A.ssp_parts * 8;
+            for (int e = tid - 32; e < n && e < kMaxSspParts * 8; e += kWorkers) es->ssp[e] = __ldcg(A.ssp + e);
+            named_barrier_sync(1, kWorkers);
+            if (tid >= 32 && tid < 40) {
+                const int b = tid - 32;
+                float inv = 1.0f;
+                if (b < A.B) {
+                    float ss = 0.0f;
+                    for (int p = 0; p < A.ssp_parts; ++p) ss += es->ssp[p * 8 + b];
+                    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)A.K), A.eps)));
+                }
+                es->inv[b] = inv;
+            }
+            named_barrier_sync(1, kWorkers);
         }
 
-        const int ab = local & 1;  // accumulator buffer
-        // ---- MMA issuer ----
-        if (warp == 1 && lane == 0) {
-            if (mma_ok && local >= 2 && !mbar_wait(&acc_empty[ab], ((local - 2) >> 1) & 1)) {
-                raise_error(A.err, ERR_FULL_WAIT);
-                mma_ok = false;
+        const int n_items = A.tiles * A.splits;
+        int cur_ks = -1;
+        for (int i = blockIdx.x; i < n_items; i += gridDim.x, ++local) {
+            const Item it = item_of(A, i);
+            const int nkb = it.kb1 - it.kb0;
+            // ---- X slab for this split, built by warps 1..7 ----
+            if (it.ks != cur_ks) {
+                if (local > 0) {  // the previous item's MMAs read the old slab: wait for their commit
+                    const int pb = (local - 1) & 1;
+                    if (!mbar_wait(&acc_full[pb], ((local - 1) >> 1) & 1)) raise_error(err, ERR_FULL_WAIT);
+                }
+                const int kbase = it.kb0 * kBK;
+                const int nk8 = nkb * kBK / 8;  // 8-element chunks per stream
+                const int n_tasks = 8 * nk8;
+                // four chunks per thread per round, all loads issued before any store
+                for (int e0 = tid - 32; e0 < n_tasks; e0 += 4 * kWorkers) {
+                    float4 xa[4][2];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int e = e0 + u * kWorkers;
+                        const int b = e / nk8;
+                        const int k = (e - b * nk8) * 8;
+                        if (e < n_tasks && b < A.B) {
+                            const float* xp = A.x + (size_t)b * A.x_stride + kbase + k;
+                            xa[u][0] = __ldcg(reinterpret_cast<const float4*>(xp));
+                            xa[u][1] = __ldcg(reinterpret_cast<const float4*>(xp + 4));
+                        } else {
+                            xa[u][0] = xa[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int e = e0 + u * kWorkers;
+                        if (e >= n_tasks) break;
+                        const int b = e / nk8;
+                        const int k = (e - b * nk8) * 8;
+                        uint32_t hi[4] = {0, 0, 0, 0}, lo[4] = {0, 0, 0, 0};
+                        if (b < A.B) {
+                            float v[8] = {xa[u][0].x, xa[u][0].y, xa[u][0].z, xa[u][0].w,
+                                          xa[u][1].x, xa[u][1].y, xa[u][1].z, xa[u][1].w};
+                            if (A.norm_w) {  // math.rs:23-24: x * inv * w, in that order
+                                const float4 g0 = __ldg(reinterpret_cast<const float4*>(A.norm_w + kbase + k));
+                                const float4 g1 = __ldg(reinterpret_cast<const float4*>(A.norm_w + kbase + k + 4));
+                                const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+                                const float inv = es->inv[b];
+#pragma unroll
+                                for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(__fmul_rn(v[j], inv), gv[j]);
+                            }
+#pragma unroll
+                            for (int j = 0; j < 8; j += 2) {
+                                const uint16_t h0 = f2bf(v[j]), h1 = f2bf(v[j + 1]);
+                                const uint16_t l0 = f2bf(v[j] - bf16_bits_to_f32(h0));
+                                const uint16_t l1 = f2bf(v[j + 1] - bf16_bits_to_f32(h1));
+                                hi[j >> 1] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+                                lo[j >> 1] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+                            }
+                        }
+                        // core (n8, k2) of K-step s at s*512 + (k2*2 + n8)*128 + row*16:
+                        // hi parts are rows 0..7 (n8 = 0), lo parts rows 8..15 (n8 = 1)
+                        const int s = k / 16, k2 = (k / 8) & 1;
+                        unsigned char* base = xs + (size_t)s * 512 + (size_t)k2 * 256;
+                        *reinterpret_cast<uint4*>(base + b * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                        *reinterpret_cast<uint4*>(base + 128 + b * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                    }
+                }
+                // generic-proxy writes must be visible to the tensor core (async proxy)
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                named_barrier_sync(1, kWorkers);
+                cur_ks = it.ks;
             }
-            tmem_fence_after();
-            const uint32_t d = tmem + (uint32_t)(ab * kN);
-            const uint32_t xs_addr = smem_addr(xs);
-            int kstep = 0;
-            for (int kb = it.kb0; kb < it.kb1; kb += kStageBlocks, ++g_mma) {
-                const int slot = (int)(g_mma % kStages);
-                if (!mma_ok) break;
-                if (!mbar_wait(&full[slot], (g_mma / kStages) & 1)) {
-                    raise_error(A.err, ERR_FULL_WAIT);
+
+            const int ab = local & 1;  // accumulator buffer
+            // ---- MMA issuer ----
+            if (warp == 1 && lane == 0) {
+                if (mma_ok && local >= 2 && !mbar_wait(&acc_empty[ab], ((local - 2) >> 1) & 1)) {
+                    raise_error(err, ERR_FULL_WAIT);
                     mma_ok = false;
-                    break;
                 }
                 tmem_fence_after();
-                const int nb = min(kStageBlocks, it.kb1 - kb);
-                const uint32_t a_addr = smem_addr(ring + (size_t)slot * kStageBytes);
-                for (int j = 0; j < nb * 4; ++j, ++kstep) {
-                    const uint64_t ad = umma_desc(a_addr + (uint32_t)j * 4096u, 2048u, 128u);
-                    const uint64_t bd = umma_desc(xs_addr + (uint32_t)kstep * 512u, 256u, 128u);
-                    umma_f16(d, ad, bd, kstep > 0 ? 1u : 0u);
-                }
-                umma_commit(&empty[slot]);  // frees the stage once these MMAs have read it
-            }
-            umma_commit(&acc_full[ab]);  // accumulator ready for the epilogue
-        }
-
-        // ---- epilogue warpgroup: TMEM -> registers -> partial or final rows ----
-        if (warp >= 4) {
-            const int ew = warp - 4;        // TMEM lanes 32*ew .. 32*ew + 31
-            const int row = ew * 32 + lane; // row inside the tile
-            if (!mbar_wait(&acc_full[ab], (local >> 1) & 1)) raise_error(A.err, ERR_FULL_WAIT);
-            tmem_fence_after();
-            uint32_t raw[16];
-            tmem_ld16(tmem + ((uint32_t)(ew * 32) << 16) + (uint32_t)(ab * kN), raw);
-            tmem_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[ab]);
-            float y[8];
-#pragma unroll
-            for (int b = 0; b < 8; ++b) y[b] = __uint_as_float(raw[b]) + __uint_as_float(raw[8 + b]);
-
-            bool final_item = true;
-            if (A.splits > 1) {
-                float* part = A.part + ((size_t)i * kBM + row) * 8;
-                *reinterpret_cast<float4*>(part) = make_float4(y[0], y[1], y[2], y[3]);
-                *reinterpret_cast<float4*>(part + 4) = make_float4(y[4], y[5], y[6], y[7]);
-                __threadfence();
-                named_barrier_sync(2, 128);
-                if (ew == 0 && lane == 0) {
-                    const unsigned t = atomicAdd(&A.tickets[it.tile], 1u);
-                    es->flag = (t == (unsigned)(A.splits - 1)) ? 1 : 0;
-                }
-                named_barrier_sync(2, 128);
-                final_item = es->flag != 0;
-                named_barrier_sync(2, 128);  // flag read by all before the next item rewrites it
-                if (final_item) {
-                    __threadfence();
-#pragma unroll
-                    for (int b = 0; b < 8; ++b) y[b] = 0.0f;
-                    for (int ks = 0; ks < A.splits; ++ks) {
-                        const float* p = A.part + ((size_t)(it.tile * A.splits + ks) * kBM + row) * 8;
-                        const float4 p0 = __ldcg(reinterpret_cast<const float4*>(p));
-                        const float4 p1 = __ldcg(reinterpret_cast<const float4*>(p + 4));
-                        y[0] += p0.x; y[1] += p0.y; y[2] += p0.z; y[3] += p0.w;
-                        y[4] += p1.x; y[5] += p1.y; y[6] += p1.z; y[7] += p1.w;
+                const uint32_t d = tmem + (uint32_t)(ab * kN);
+                const uint32_t xs_addr = smem_addr(xs);
+                int kstep = 0;
+                for (int kb = it.kb0; kb < it.kb1; kb += kStageBlocks, ++g_mma) {
+                    const int slot = (int)(g_mma % kStages);
+                    if (!mma_ok) break;
+                    if (!mbar_wait(&full[slot], (g_mma / kStages) & 1)) {
+                        raise_error(err, ERR_FULL_WAIT);
+                        mma_ok = false;
+                        break;
                     }
-                    if (ew == 0 && lane == 0) A.tickets[it.tile] = 0u;
+                    tmem_fence_after();
+                    const int nb = min(kStageBlocks, it.kb1 - kb);
+                    const uint32_t a_addr = smem_addr(ring + (size_t)slot * kStageBytes);
+                    for (int j = 0; j < nb * 4; ++j, ++kstep) {
+                        const uint64_t ad = umma_desc(a_addr + (uint32_t)j * 4096u, 2048u, 128u);
+                        const uint64_t bd = umma_desc(xs_addr + (uint32_t)kstep * 512u, 256u, 128u);
+                        umma_f16(d, ad, bd, kstep > 0 ? 1u : 0u);
+                    }
+                    umma_commit(&empty[slot]);  // frees the stage once these MMAs have read it
                 }
+                umma_commit(&acc_full[ab]);  // accumulator ready for the epilogue
             }
-            if (final_item) bg_epilogue(A, it.tile, row, lane, ew, y, es);
+            __syncwarp();  // warp 1 reconverges before any later barrier
+
+            // ---- epilogue warpgroup: TMEM -> registers -> partial or final rows ----
+            if (warp >= 4) {
+                const int ew = warp - 4;        // TMEM lanes 32*ew .. 32*ew + 31
+                const int row = ew * 32 + lane; // row inside the tile
+                if (!mbar_wait(&acc_full[ab], (local >> 1) & 1)) raise_error(err, ERR_FULL_WAIT);
+                tmem_fence_after();
+                uint32_t raw[16];
+                tmem_ld16(tmem + ((uint32_t)(ew * 32) << 16) + (uint32_t)(ab * kN), raw);
+                tmem_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[ab]);
+                float y[8];
+#pragma unroll
+                for (int b = 0; b < 8; ++b) y[b] = __uint_as_float(raw[b]) + __uint_as_float(raw[8 + b]);
+
+                bool final_item = true;
+                if (A.splits > 1) {
+                    float* part = A.part + ((size_t)i * kBM + row) * 8;
+                    *reinterpret_cast<float4*>(part) = make_float4(y[0], y[1], y[2], y[3]);
+                    *reinterpret_cast<float4*>(part + 4) = make_float4(y[4], y[5], y[6], y[7]);
+                    __threadfence();
+                    named_barrier_sync(2, 128);
+                    if (ew == 0 && lane == 0) {
+                        const unsigned t = atomicAdd(&A.tickets[it.tile], 1u);
+                        es->flag = (t == (unsigned)(A.splits - 1)) ? 1 : 0;
+                    }
+                    named_barrier_sync(2, 128);
+                    final_item = es->flag != 0;
+                    named_barrier_sync(2, 128);  // flag read by all before the next item rewrites it
+                    if (final_item) {
+                        __threadfence();
+#pragma unroll
+                        for (int b = 0; b < 8; ++b) y[b] = 0.0f;
+                        for (int k0 = 0; k0 < A.splits; k0 += 4) {  // four splits' loads in flight
+                            float4 pv[4][2];
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                if (k0 + u < A.splits) {
+                                    const float* p = A.part + ((size_t)(it.tile * A.splits + k0 + u) * kBM + row) * 8;
+                                    pv[u][0] = __ldcg(reinterpret_cast<const float4*>(p));
+                                    pv[u][1] = __ldcg(reinterpret_cast<const float4*>(p + 4));
+                                } else {
+                                    pv[u][0] = pv[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+                                }
+                            }
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {  // split order, as the partials were made
+                                y[0] += pv[u][0].x; y[1] += pv[u][0].y; y[2] += pv[u][0].z; y[3] += pv[u][0].w;
+                                y[4] += pv[u][1].x; y[5] += pv[u][1].y; y[6] += pv[u][1].z; y[7] += pv[u][1].w;
+                            }
+                        }
+                        if (ew == 0 && lane == 0) A.tickets[it.tile] = 0u;
+                    }
+                }
+                if (final_item) bg_epilogue(A, it.tile, row, lane, ew, y, es);
+            }
         }
     }
 
@@ -532,11 +626,15 @@ __global__ void tile_weights_kernel(const uint16_t* __restrict__ src, uint16_t* 
 // Embedding rows of every stream's token (bf16 widened exactly, as
 // weights.rs:77-81) into hid [B, dim], with per-128-column sums of squares
 // for the first layer's RMSNorm.  Grid (ceil(dim / 128), B), 128 threads.
+// Block (0, 0) also zeroes the step's chain completion counters: every chain
+// of the previous step has finished when this kernel runs.
 __global__ void __launch_bounds__(128) bg_embed_kernel(const uint16_t* __restrict__ embed, int vocab, int dim,
                                                        const StepState* steps, float* hid, float* ssp,
-                                                       unsigned* err) {
+                                                       unsigned* zero, int n_zero, unsigned* err) {
     pdl_allow_dependents();
     pdl_wait_prior_grids();
+    if (blockIdx.x == 0 && blockIdx.y == 0)
+        for (int i = threadIdx.x; i < n_zero; i += blockDim.x) zero[i] = 0u;
     __shared__ float red[4];
     const int b = blockIdx.y, e = blockIdx.x * 128 + threadIdx.x;
     int tok = steps[b].tok;
@@ -608,7 +706,7 @@ __global__ void __launch_bounds__(256) bg_argmax_final_kernel(const ArgmaxPart* 
 }  // namespace
 
 cudaError_t launch_bg_embed(const uint16_t* embed, int vocab, int dim, const StepState* steps, int B, float* hid,
-                            float* ssp, unsigned* err, cudaStream_t s, bool pdl) {
+                            float* ssp, unsigned* zero, int n_zero, unsigned* err, cudaStream_t s, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((dim + 127) / 128, B, 1);
     cfg.blockDim = dim3(128, 1, 1);
@@ -618,7 +716,7 @@ cudaError_t launch_bg_embed(const uint16_t* embed, int vocab, int dim, const Ste
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, bg_embed_kernel, embed, vocab, dim, steps, hid, ssp, err);
+    return cudaLaunchKernelEx(&cfg, bg_embed_kernel, embed, vocab, dim, steps, hid, ssp, zero, n_zero, err);
 }
 
 cudaError_t launch_bg_argmax_final(const ArgmaxPart* parts, int n_tiles, StepState* steps, int B,
@@ -635,34 +733,32 @@ cudaError_t launch_bg_argmax_final(const ArgmaxPart* parts, int n_tiles, StepSta
     return cudaLaunchKernelEx(&cfg, bg_argmax_final_kernel, parts, n_tiles, steps, tok_out);
 }
 
-size_t bgemm_smem_bytes(int K, int splits) {
-    const int kbt = K / kBK;
-    const int max_kb = (kbt + splits - 1) / splits;
-    const size_t xslab = (size_t)max_kb * 4 * 512;
-    return (size_t)kStages * kStageBytes + xslab + (2 * kStages + 4) * 8 + 16 + sizeof(EpiShared);
-}
-
 int bgemm_xslab_bytes(int K, int splits) {
     const int kbt = K / kBK;
     return ((kbt + splits - 1) / splits) * 4 * 512;
+}
+
+size_t bgemm_smem_bytes(int xslab_bytes) {
+    return (size_t)kStages * kStageBytes + xslab_bytes + (2 * kStages + 4) * 8 + 16 + sizeof(EpiShared);
 }
 
 cudaError_t bgemm_prepare(int /*dev*/) {
     return cudaFuncSetAttribute(bgemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
 }
 
-cudaError_t launch_bgemm(const BgArgs& a, int grid, cudaStream_t s, bool pdl) {
+cudaError_t launch_bgemm(const BgChain& c, int grid, cudaStream_t s, bool pdl) {
+    if (c.n_phases < 1 || c.n_phases > kBgMaxPhases || (c.n_phases > 1 && !c.done)) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = bgemm_smem_bytes(a.K, a.splits);
+    cfg.dynamicSmemBytes = bgemm_smem_bytes(c.xslab_bytes);
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    void* args[] = {(void*)&a};
+    void* args[] = {(void*)&c};
     return cudaLaunchKernelExC(&cfg, (void*)bgemm_kernel, args);
 }
 

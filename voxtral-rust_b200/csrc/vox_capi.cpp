@@ -130,12 +130,18 @@ struct BatchBufs {
     StepState* h_steps = nullptr;      // pinned [8]
     int32_t* h_tok = nullptr;          // pinned token history
     size_t h_tok_cap = 0;
-    BgPlan p_qkv, p_o, p_w13, p_w2, p_head;
+    BgPlan p_qkv, p_o, p_w13, p_w2, p_head;         // one GEMM per launch
+    BgPlan c_qkv, c_o, c_w13, c_w2, c_head;         // phases of the per-layer chains
+    unsigned* done = nullptr;  // chain completion counters [n_layers + 1][kBgMaxPhases]
+    int n_done = 0;
 };
 
-// K splits and grid of a multi-stream GEMM: the split count that minimises
-// the busiest CTA's K blocks (items per CTA x blocks per item), with at most
-// 40 K blocks per split so the split's X operand fits in shared memory.
+// K splits and grid of a multi-stream GEMM launched on its own: one CTA per
+// SM (the 128 KB weight ring fills it), the split count that minimises the
+// busiest CTA's K blocks (items per CTA x blocks per item), at most
+// kBgMaxBlocksPerSplit K blocks per split so the split's X operand fits in
+// shared memory.  The grid is a multiple of the split count, so a CTA keeps
+// its split (and X operand) across items.
 BgPlan make_bgplan(int rows, int K, int num_sms) {
     BgPlan p;
     p.rows = rows;
@@ -145,7 +151,7 @@ BgPlan make_bgplan(int rows, int K, int num_sms) {
     long long best = -1;
     for (int s = 1; s <= p.kbt && s <= 64; ++s) {
         const int per = (p.kbt + s - 1) / s;
-        if (per > 40) continue;
+        if (per > kBgMaxBlocksPerSplit) continue;
         int grid = num_sms - num_sms % s;
         if (grid < s) grid = s;
         const long long items = (long long)p.tiles * s;
@@ -159,6 +165,42 @@ BgPlan make_bgplan(int rows, int K, int num_sms) {
     }
     p.xslab = bgemm_xslab_bytes(K, p.splits);
     return p;
+}
+
+// Plan of one phase of a persistent GEMM chain: the grid is fixed (one CTA
+// per SM); the split count minimises the busiest CTA's K blocks, ties going
+// to fewer splits.  A CTA whose items change split rebuilds its X operand,
+// which costs about one K block.
+BgPlan make_chain_plan(int rows, int K, int grid) {
+    BgPlan p;
+    p.rows = rows;
+    p.K = K;
+    p.tiles = (rows + 127) / 128;
+    p.kbt = K / 64;
+    p.grid = grid;
+    long long best = -1;
+    for (int s = 1; s <= p.kbt && s <= 64; ++s) {
+        const int per = (p.kbt + s - 1) / s;
+        if (per > kBgMaxBlocksPerSplit) continue;
+        const long long items = (long long)p.tiles * s;
+        const long long rounds = (items + grid - 1) / grid;
+        long long cost = rounds * per;
+        if (rounds > 1 && grid % s) cost += rounds;  // X operand rebuilt between items
+        if (best < 0 || cost < best) {
+            best = cost;
+            p.splits = s;
+        }
+    }
+    p.xslab = bgemm_xslab_bytes(K, p.splits);
+    return p;
+}
+
+BgChain chain_of(const BgArgs& a, const BgPlan& p) {
+    BgChain c{};
+    c.n_phases = 1;
+    c.xslab_bytes = p.xslab;
+    c.ph[0] = a;
+    return c;
 }
 
 }  // namespace
@@ -250,6 +292,7 @@ int check_device_errors(vox_ctx* c) {
                 for (const BgPlan* p : {&c->bb.p_qkv, &c->bb.p_o, &c->bb.p_w13, &c->bb.p_w2, &c->bb.p_head})
                     tiles = std::max(tiles, (size_t)p->tiles);
                 CUDA_TRY(cudaMemsetAsync(c->bb.tickets, 0, tiles * sizeof(unsigned), c->stream));
+                CUDA_TRY(cudaMemsetAsync(c->bb.done, 0, (size_t)c->bb.n_done * sizeof(unsigned), c->stream));
                 CUDA_TRY(cudaMemsetAsync(c->bb.attn_tickets, 0, 8 * c->cfg.n_kv_heads * sizeof(unsigned), c->stream));
             }
         }
@@ -524,6 +567,7 @@ int batch_supported(vox_ctx* c) {
     if (g.dim % 64 || c->q_dim % 64 || g.hidden_dim % 64)
         return fail(VOX_ERR_UNSUPPORTED, "the multi-stream step needs dim, n_heads*head_dim and hidden_dim "
                                          "to be multiples of 64");
+    if (g.dim > 8192) return fail(VOX_ERR_UNSUPPORTED, "the multi-stream step needs dim <= 8192");
     return VOX_OK;
 }
 
@@ -550,8 +594,17 @@ int ensure_batch(vox_ctx* c) {
         b.p_w13 = make_bgplan(2 * hid, dim, c->num_sms);
         b.p_w2 = make_bgplan(dim, hid, c->num_sms);
         b.p_head = make_bgplan(vocab, dim, c->num_sms);
+        b.c_qkv = make_chain_plan((int)c->qkv_rows, dim, c->num_sms);
+        b.c_o = make_chain_plan(dim, qd, c->num_sms);
+        b.c_w13 = make_chain_plan(2 * hid, dim, c->num_sms);
+        b.c_w2 = make_chain_plan(dim, hid, c->num_sms);
+        b.c_head = make_chain_plan(vocab, dim, c->num_sms);
+        b.n_done = (int)(c->layers.size() + 1) * kBgMaxPhases;
+        CUDA_TRY(dalloc(&b.done, (size_t)b.n_done));
+        CUDA_TRY(cudaMemset(b.done, 0, (size_t)b.n_done * sizeof(unsigned)));
         size_t part = 0, tiles = 0;
-        for (const BgPlan* p : {&b.p_qkv, &b.p_o, &b.p_w13, &b.p_w2, &b.p_head}) {
+        for (const BgPlan* p : {&b.p_qkv, &b.p_o, &b.p_w13, &b.p_w2, &b.p_head, &b.c_qkv, &b.c_o, &b.c_w13,
+                                &b.c_w2, &b.c_head}) {
             part = std::max(part, (size_t)p->tiles * p->splits * 128 * 8);
             tiles = std::max(tiles, (size_t)p->tiles);
         }
@@ -631,17 +684,34 @@ int enqueue_batch_step(vox_ctx* c, vox_kv* kv, bool pdl) {
     const int nkv = (int)c->cfg.n_kv_heads, hd = (int)c->cfg.head_dim, G = (int)(c->cfg.n_heads / nkv);
     const int nsplit = attn_max_splits();  // chunks per (stream, kv head) at most
     CUDA_TRY(record_launch(c, launch_bg_embed(c->embed, (int)c->opt.vocab, dim, bb.steps, B, bb.hid, bb.ssp,
-                                              c->err, c->stream, pdl)));
-    for (size_t l = 0; l < c->layers.size(); ++l) {
-        const LayerDev& L = c->layers[l];
-        float* kr = kv->k + l * kv->layer_elems();
-        float* vr = kv->v + l * kv->layer_elems();
-        KvState* st = kv->dstate + l;
-
-        BgArgs a = bg_args(c, bb.p_qkv, L.wqkv_t, B, BG_QKV);
+                                              bb.done, bb.n_done, c->err, c->stream, pdl)));
+    const int L = (int)c->layers.size();
+    // VOX_STEP_PERSISTENT: o-proj, w1|w3, w2 and the next q|k|v (or the LM
+    // head) run as one persistent chain launch; otherwise (and by default,
+    // about 3% faster on B200) one launch per GEMM.
+    const bool chained = c->opt.step_mode == VOX_STEP_PERSISTENT;
+    const BgPlan& P_qkv = chained ? bb.c_qkv : bb.p_qkv;
+    const BgPlan& P_o = chained ? bb.c_o : bb.p_o;
+    const BgPlan& P_w13 = chained ? bb.c_w13 : bb.p_w13;
+    const BgPlan& P_w2 = chained ? bb.c_w2 : bb.p_w2;
+    const BgPlan& P_head = chained ? bb.c_head : bb.p_head;
+    auto launch_chain = [&](BgChain& ch, const BgPlan* const* plans) -> int {
+        if (chained) {
+            ch.xslab_bytes = 0;
+            for (int p = 0; p < ch.n_phases; ++p) ch.xslab_bytes = std::max(ch.xslab_bytes, ch.ph[p].xslab_bytes);
+            CUDA_TRY(record_launch(c, launch_bgemm(ch, c->num_sms, c->stream, pdl)));
+            return VOX_OK;
+        }
+        for (int p = 0; p < ch.n_phases; ++p)
+            CUDA_TRY(record_launch(c, launch_bgemm(chain_of(ch.ph[p], *plans[p]), plans[p]->grid, c->stream, pdl)));
+        return VOX_OK;
+    };
+    auto qkv_args = [&](int l) {
+        const LayerDev& Ld = c->layers[l];
+        BgArgs a = bg_args(c, P_qkv, Ld.wqkv_t, B, BG_QKV);
         a.x = bb.hid;
         a.x_stride = dim;
-        a.norm_w = L.attn_norm;
+        a.norm_w = Ld.attn_norm;
         a.ssp = bb.ssp;
         a.y = bb.q;
         a.y_stride = qd;
@@ -652,14 +722,27 @@ int enqueue_batch_step(vox_ctx* c, vox_kv* kv, bool pdl) {
         a.rope_sin = c->rope_sin;
         a.max_pos = c->max_pos;
         a.steps = bb.steps;
-        a.kv_state = st;
+        a.kv_state = kv->dstate + l;
         a.kv_state_stride = (long long)kv->n_layers;
-        a.k_ring = kr;
-        a.v_ring = vr;
+        a.k_ring = kv->k + (size_t)l * kv->layer_elems();
+        a.v_ring = kv->v + (size_t)l * kv->layer_elems();
         a.ring_stride = ring_stride;
         a.ring_cap = cap;
         a.kv_window = win;
-        CUDA_TRY(record_launch(c, launch_bgemm(a, bb.p_qkv.grid, c->stream, pdl)));
+        return a;
+    };
+    // chain 0: q|k|v of layer 0
+    {
+        BgChain ch = chain_of(qkv_args(0), P_qkv);
+        ch.done = bb.done;
+        const BgPlan* plans[1] = {&P_qkv};
+        TRY(launch_chain(ch, plans));
+    }
+    for (int l = 0; l < L; ++l) {
+        const LayerDev& Ld = c->layers[l];
+        float* kr = kv->k + (size_t)l * kv->layer_elems();
+        float* vr = kv->v + (size_t)l * kv->layer_elems();
+        KvState* st = kv->dstate + l;
 
         AttnArgs at{};
         at.q = bb.q;
@@ -687,7 +770,12 @@ int enqueue_batch_step(vox_ctx* c, vox_kv* kv, bool pdl) {
         at.st_stride = (long long)kv->n_layers;
         CUDA_TRY(record_launch(c, launch_attention(at, c->stream, pdl)));
 
-        a = bg_args(c, bb.p_o, L.wo_t, B, BG_RESID);
+        // chain l + 1: o-proj + residual (commits the append), w1|w3 + SwiGLU,
+        // w2 + residual, then layer l + 1's q|k|v or the LM head.
+        BgChain ch{};
+        ch.n_phases = 4;
+        ch.done = bb.done + (size_t)(l + 1) * kBgMaxPhases;
+        BgArgs a = bg_args(c, P_o, Ld.wo_t, B, BG_RESID);
         a.x = bb.attn;
         a.x_stride = qd;
         a.y = bb.hmid;
@@ -698,36 +786,43 @@ int enqueue_batch_step(vox_ctx* c, vox_kv* kv, bool pdl) {
         a.kv_state_stride = (long long)kv->n_layers;
         a.kv_window = win;
         a.ring_cap = cap;
-        CUDA_TRY(record_launch(c, launch_bgemm(a, bb.p_o.grid, c->stream, pdl)));
+        ch.ph[0] = a;
 
-        a = bg_args(c, bb.p_w13, L.w13_t, B, BG_SWIGLU);
+        a = bg_args(c, P_w13, Ld.w13_t, B, BG_SWIGLU);
         a.x = bb.hmid;
         a.x_stride = dim;
-        a.norm_w = L.ffn_norm;
+        a.norm_w = Ld.ffn_norm;
         a.ssp = bb.ssp;
         a.y = bb.act;
         a.y_stride = hid;
-        CUDA_TRY(record_launch(c, launch_bgemm(a, bb.p_w13.grid, c->stream, pdl)));
+        ch.ph[1] = a;
 
-        a = bg_args(c, bb.p_w2, L.w2_t, B, BG_RESID);
+        a = bg_args(c, P_w2, Ld.w2_t, B, BG_RESID);
         a.x = bb.act;
         a.x_stride = hid;
         a.y = bb.hid;
         a.y_stride = dim;
         a.resid = bb.hmid;
         a.ssp_out = bb.ssp;
-        CUDA_TRY(record_launch(c, launch_bgemm(a, bb.p_w2.grid, c->stream, pdl)));
+        ch.ph[2] = a;
+
+        if (l + 1 < L) {
+            ch.ph[3] = qkv_args(l + 1);
+        } else {
+            a = bg_args(c, P_head, c->head_t, B, BG_ARGMAX);
+            a.x = bb.hid;
+            a.x_stride = dim;
+            a.norm_w = c->final_norm;
+            a.ssp = bb.ssp;
+            a.y = bb.logits;
+            a.y_stride = (long long)c->opt.vocab;
+            a.am_part = bb.am;
+            ch.ph[3] = a;
+        }
+        const BgPlan* plans[4] = {&P_o, &P_w13, &P_w2, l + 1 < L ? &P_qkv : &P_head};
+        TRY(launch_chain(ch, plans));
     }
-    BgArgs a = bg_args(c, bb.p_head, c->head_t, B, BG_ARGMAX);
-    a.x = bb.hid;
-    a.x_stride = dim;
-    a.norm_w = c->final_norm;
-    a.ssp = bb.ssp;
-    a.y = bb.logits;
-    a.y_stride = (long long)c->opt.vocab;
-    a.am_part = bb.am;
-    CUDA_TRY(record_launch(c, launch_bgemm(a, bb.p_head.grid, c->stream, pdl)));
-    CUDA_TRY(record_launch(c, launch_bg_argmax_final(bb.am, bb.p_head.tiles, bb.steps, B, bb.tok_out, c->stream,
+    CUDA_TRY(record_launch(c, launch_bg_argmax_final(bb.am, P_head.tiles, bb.steps, B, bb.tok_out, c->stream,
                                                      pdl)));
     return VOX_OK;
 }
@@ -959,7 +1054,7 @@ void vox_ctx_destroy(vox_ctx* c) {
     {
         BatchBufs& b = c->bb;
         void* bp[] = {c->head_t, b.hid, b.hmid, b.q, b.attn, b.act, b.logits, b.ssp, b.part, b.attn_part, b.am,
-                      b.tickets, b.attn_tickets, b.steps, b.tok_out};
+                      b.tickets, b.attn_tickets, b.steps, b.tok_out, b.done};
         for (void* p : bp)
             if (p) cudaFree(p);
         if (b.h_steps) cudaFreeHost(b.h_steps);
@@ -1739,7 +1834,7 @@ int vox_profile_gemv(vox_ctx* c, int which, size_t n, float* avg_ms, uint64_t* b
 
 int vox_profile_bgemm(vox_ctx* c, int which, size_t n_streams, size_t n, float* avg_ms, uint64_t* bytes_per_launch) {
     if (!c || !avg_ms || n == 0) return fail(VOX_ERR_INVALID_ARG, "bad argument");
-    if (which < 1 || which > 5) return fail(VOX_ERR_INVALID_ARG, "which must be 1..5");
+    if (which < 1 || which > 6) return fail(VOX_ERR_INVALID_ARG, "which must be 1..6");
     if (n_streams < 1 || n_streams > 8) return fail(VOX_ERR_INVALID_ARG, "n_streams must be 1..8");
     for (size_t l = 0; l < c->layers.size(); ++l)
         if (!c->layers[l].ready) return fail(VOX_ERR_NOT_READY, "layer %zu weights not uploaded", l);
@@ -1751,7 +1846,28 @@ int vox_profile_bgemm(vox_ctx* c, int which, size_t n_streams, size_t n, float* 
                                                                                                       : bb.p_qkv;
     CUDA_TRY(cudaStreamSynchronize(c->stream));
     CUDA_TRY(cudaEventRecord(c->ev[14], c->stream));
-    for (size_t i = 0; i < n; ++i) {
+    for (size_t i = 0; i < n && which == 6; ++i) {  // o-proj, w1|w3, w2, q|k|v as one chain launch
+        const LayerDev& L = c->layers[i % c->layers.size()];
+        BgChain ch{};
+        ch.n_phases = 4;
+        ch.done = bb.done;
+        BgArgs a = bg_args(c, bb.c_o, L.wo_t, B, BG_RESID);
+        a.x = bb.attn; a.x_stride = qd; a.y = bb.hmid; a.y_stride = dim; a.resid = bb.hid; a.ssp_out = bb.ssp;
+        ch.ph[0] = a;
+        a = bg_args(c, bb.c_w13, L.w13_t, B, BG_SWIGLU);
+        a.x = bb.hmid; a.x_stride = dim; a.norm_w = L.ffn_norm; a.ssp = bb.ssp; a.y = bb.act; a.y_stride = hid;
+        ch.ph[1] = a;
+        a = bg_args(c, bb.c_w2, L.w2_t, B, BG_RESID);
+        a.x = bb.act; a.x_stride = hid; a.y = bb.hid; a.y_stride = dim; a.resid = bb.hmid; a.ssp_out = bb.ssp;
+        ch.ph[2] = a;
+        a = bg_args(c, bb.c_qkv, L.wqkv_t, B, BG_STORE);
+        a.x = bb.hid; a.x_stride = dim; a.y = bb.act; a.y_stride = (long long)c->qkv_rows;
+        ch.ph[3] = a;
+        for (int p = 0; p < 4; ++p) ch.xslab_bytes = std::max(ch.xslab_bytes, ch.ph[p].xslab_bytes);
+        CUDA_TRY(cudaMemsetAsync(bb.done, 0, kBgMaxPhases * sizeof(unsigned), c->stream));
+        CUDA_TRY(record_launch(c, launch_bgemm(ch, c->num_sms, c->stream, true)));
+    }
+    for (size_t i = 0; i < n && which != 6; ++i) {
         const LayerDev& L = c->layers[i % c->layers.size()];
         BgArgs a;
         if (which == 1) {
@@ -1771,14 +1887,16 @@ int vox_profile_bgemm(vox_ctx* c, int which, size_t n_streams, size_t n, float* 
             a = bg_args(c, p, L.wqkv_t, B, BG_STORE);
             a.x = bb.hid; a.x_stride = dim; a.y = bb.act; a.y_stride = (long long)c->qkv_rows;
         }
-        CUDA_TRY(record_launch(c, launch_bgemm(a, p.grid, c->stream, true)));
+        CUDA_TRY(record_launch(c, launch_bgemm(chain_of(a, p), p.grid, c->stream, true)));
     }
     CUDA_TRY(cudaEventRecord(c->ev[15], c->stream));
     CUDA_TRY(cudaEventSynchronize(c->ev[15]));
     float ms = 0.f;
     CUDA_TRY(cudaEventElapsedTime(&ms, c->ev[14], c->ev[15]));
     *avg_ms = ms / (float)n;
-    if (bytes_per_launch) *bytes_per_launch = (uint64_t)p.rows * (uint64_t)p.K * 2u;
+    if (bytes_per_launch)
+        *bytes_per_launch = which == 6 ? (uint64_t)(dim * qd + 2 * hid * dim + dim * hid + c->qkv_rows * dim) * 2u
+                                       : (uint64_t)p.rows * (uint64_t)p.K * 2u;
     return check_device_errors(c);
 }
 
@@ -1830,10 +1948,10 @@ int vox_linear_bf16(vox_ctx* c, const float* input, size_t n_rows, size_t in_dim
 
 // K splits per 128-row tile of the tensor-core skinny GEMM: enough items to
 // cover every SM once, and few enough K blocks per split that the split's X
-// operand fits next to the 128 KB weight ring.
+// operand fits next to the weight ring.
 static int bgemm_splits(int tiles, int kbt, int num_sms) {
     int s = (num_sms + tiles - 1) / tiles;
-    const int min_s = (kbt + 39) / 40;
+    const int min_s = (kbt + kBgMaxBlocksPerSplit - 1) / kBgMaxBlocksPerSplit;
     if (s < min_s) s = min_s;
     if (s > kbt) s = kbt;
     return s < 1 ? 1 : s;
@@ -1890,7 +2008,9 @@ int vox_linear_batched_bf16(vox_ctx* c, const float* input, size_t n_rows, size_
     a.part = dpart;
     a.tickets = dtick;
     a.err = c->err;
-    CUDA_TRY(record_launch(c, launch_bgemm(a, grid, c->stream, false)));
+    BgPlan pl{};
+    pl.xslab = a.xslab_bytes;
+    CUDA_TRY(record_launch(c, launch_bgemm(chain_of(a, pl), grid, c->stream, false)));
     CUDA_TRY(cudaMemcpyAsync(out, dy, n_rows * out_dim * 4, cudaMemcpyDeviceToHost, c->stream));
     return check_device_errors(c);
 }

@@ -84,6 +84,14 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32
         : "memory");
 }
 
+// Same without an L2 policy (data that later kernels may read again).
+__device__ __forceinline__ void bulk_copy_g2s_nohint(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+
 // Programmatic dependent launch (no-ops when launched without the attribute).
 __device__ __forceinline__ void pdl_wait_prior_grids() {
     asm volatile("griddepcontrol.wait;" ::: "memory");

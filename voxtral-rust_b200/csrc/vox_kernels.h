@@ -41,7 +41,7 @@ enum : unsigned {
     ERR_DRAIN_WAIT = 4u,     // producer could not drain its copies
     ERR_POS_RANGE = 8u,      // position beyond the RoPE table
     ERR_TOKEN_RANGE = 16u,   // token id outside the vocabulary
-    ERR_GRID_WAIT = 64u,     // a grid barrier of the token kernel expired
+    ERR_GRID_WAIT = 64u,     // a grid-wide wait (token kernel, GEMM chain) expired
 };
 
 enum : int { EPI_STORE = 0, EPI_RESID = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
@@ -208,13 +208,27 @@ struct BgArgs {
     unsigned* err;
 };
 
-size_t bgemm_smem_bytes(int K, int splits);
+// A chain of GEMMs run by one persistent launch, phase after phase; phase p
+// reads what phase p - 1 wrote (see vox_bgemm.cu).
+constexpr int kBgMaxPhases = 4;
+struct BgChain {
+    int n_phases;
+    int xslab_bytes;            // largest X operand of any phase
+    unsigned* done;             // [n_phases - 1] CTA completion counters, zero at launch
+    BgArgs ph[kBgMaxPhases];
+};
+
+// K blocks (of 64) one split may cover: its X operand (2 KB per block) sits
+// next to the 128 KB weight ring in the 227 KB of one CTA.
+constexpr int kBgMaxBlocksPerSplit = 40;
+size_t bgemm_smem_bytes(int xslab_bytes);
 int bgemm_xslab_bytes(int K, int splits);
 cudaError_t bgemm_prepare(int dev);
-cudaError_t launch_bgemm(const BgArgs& a, int grid, cudaStream_t s, bool pdl);
+// grid <= number of SMs when n_phases > 1 (all CTAs must be resident together).
+cudaError_t launch_bgemm(const BgChain& c, int grid, cudaStream_t s, bool pdl);
 size_t tiled_bytes(int rows, int K);
 cudaError_t launch_bg_embed(const uint16_t* embed, int vocab, int dim, const StepState* steps, int B, float* hid,
-                            float* ssp, unsigned* err, cudaStream_t s, bool pdl);
+                            float* ssp, unsigned* zero, int n_zero, unsigned* err, cudaStream_t s, bool pdl);
 cudaError_t launch_bg_argmax_final(const ArgmaxPart* parts, int n_tiles, StepState* steps, int B,
                                    int32_t* tok_out, cudaStream_t s, bool pdl);
 cudaError_t launch_tile_weights(const uint16_t* src, uint16_t* dst, int rows, int K, cudaStream_t s);

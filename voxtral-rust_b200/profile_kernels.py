@@ -8,7 +8,8 @@ suitable for an ncu capture).
 --which step runs whole token steps of a full-width model with `--layers`
 layers and the 131072-token vocabulary; --which batch runs multi-stream steps
 of `--streams` streams (contexts uniform in [256, 4096)); --which
-bo|bw13|bw2|bhead|bqkv times one multi-stream tensor-core GEMM.
+bo|bw13|bw2|bhead|bqkv times one multi-stream tensor-core GEMM, --which
+bchain the o-proj, w1|w3, w2, q|k|v chain as one launch.
 """
 from __future__ import annotations
 
@@ -24,7 +25,8 @@ sys.path.insert(0, ROOT)
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--which", default="w13",
-                    choices=["o", "w13", "w2", "head", "step", "batch", "bo", "bw13", "bw2", "bhead", "bqkv"])
+                    choices=["o", "w13", "w2", "head", "step", "batch", "bo", "bw13", "bw2", "bhead", "bqkv",
+                             "bchain"])
     ap.add_argument("--streams", type=int, default=8)
     ap.add_argument("--layers", type=int, default=2)
     ap.add_argument("--launches", type=int, default=8)
@@ -68,7 +70,7 @@ def main():
                   f"({args.layers} layers + LM head), contexts {lens}")
             return
         if batched:
-            which = {"bo": 1, "bw13": 2, "bw2": 3, "bhead": 4, "bqkv": 5}[args.which]
+            which = {"bo": 1, "bw13": 2, "bw2": 3, "bhead": 4, "bqkv": 5, "bchain": 6}[args.which]
             ctx.profile_bgemm(which, args.streams, 2)  # warm-up
             ms, nbytes = ctx.profile_bgemm(which, args.streams, args.launches)
             print(f"{args.which}: {ms * 1e3:.2f} us per launch, {nbytes} B, {nbytes / ms / 1e6:.1f} GB/s")
