@@ -232,6 +232,49 @@ int vox_model_step_batch(vox_ctx* ctx, vox_kv* kv, const int32_t* tokens, const 
  * tokens_out [n_steps, n_streams] (nullable). */
 int vox_model_generate_batch(vox_ctx* ctx, vox_kv* kv, const int32_t* tokens, const size_t* positions,
                              size_t n_steps, int32_t* tokens_out);
+/* ---- tensor-parallel single stream (no reference counterpart) -------------------- */
+/* One process per GPU; tp_size ranks share each layer: rank r holds the q|k|v
+ * rows of q heads [r*n_heads/T, (r+1)*n_heads/T) and of the kv heads they
+ * attend to, the matching columns of wo, w1|w3 rows [r*hidden/T, ...) and the
+ * matching columns of w2, and LM-head rows [r*vocab/T, ...).  The residual
+ * stream is all-reduced (NCCL, sum) after o-proj and after w2; the greedy
+ * token is an all-reduce (max) of (value, index) keys.  n_heads, n_kv_heads,
+ * hidden_dim and vocab must divide by tp_size; bf16 weights. */
+typedef struct vox_tp vox_tp;
+typedef struct vox_tp_shard {
+    int rank, size;
+    size_t n_heads, n_kv_heads, hidden;   /* local counts */
+    size_t vocab, vocab_local;
+    size_t q_head_begin, kv_head_begin, hidden_begin, vocab_begin;
+} vox_tp_shard;
+/* The shard a rank holds (host only; validates like vox_config_validate). */
+int vox_tp_shard_of(const vox_decoder_config* cfg, size_t vocab, int tp_rank, int tp_size, vox_tp_shard* out);
+/* NCCL unique id: made by one rank, passed to every rank's vox_tp_create. */
+int vox_tp_unique_id(unsigned char id[128]);
+/* Collective over all ranks (each blocks until all have joined).  opt: device,
+ * n_layers, vocab (required), max_positions; weight_dtype must be bf16.  The
+ * context owns a rolling cache of window cfg->sliding_window for its kv heads. */
+int vox_tp_create(const vox_decoder_config* cfg, const vox_ctx_options* opt, int tp_rank, int tp_size,
+                  const unsigned char id[128], vox_tp** out);
+/* Releases the captured graph, then the NCCL communicator, then memory. */
+void vox_tp_destroy(vox_tp* tp);
+/* This rank's shards of the weights vox_ctx_init_random makes (same generator,
+ * same tensor ids, so the ranks together hold exactly those weights). */
+int vox_tp_init_random(vox_tp* tp, uint64_t seed, float std);
+/* Full (unsharded) tensors in; each rank copies its shard. */
+int vox_tp_upload_layer_bf16(vox_tp* tp, size_t layer, const vox_layer_weights_bf16* w);
+int vox_tp_upload_embed_bf16(vox_tp* tp, const uint16_t* embed, size_t len);
+int vox_tp_upload_lm_head_bf16(vox_tp* tp, const uint16_t* lm_head, size_t len, const float* final_norm);
+/* Collective token steps (every rank calls them with the same arguments).
+ * logits_local (nullable) receives this rank's [vocab/T] slice of the logits. */
+int vox_tp_step(vox_tp* tp, int32_t token, size_t pos, int32_t* next_token, float* logits_local);
+int vox_tp_prefill(vox_tp* tp, const int32_t* tokens, size_t n, size_t pos0);
+int vox_tp_generate(vox_tp* tp, int32_t token, size_t pos, size_t n_steps, int32_t* tokens_out);
+/* Device ring state of a layer: len_tokens, start slot, pos_offset. */
+int vox_tp_kv_state(const vox_tp* tp, size_t layer, int64_t out[3]);
+int vox_tp_record_event(vox_tp* tp, int slot);  /* slots 0..7 */
+int vox_tp_event_elapsed_ms(vox_tp* tp, int slot_a, int slot_b, float* ms);
+uint64_t vox_tp_kernel_launches(const vox_tp* tp);
 /* ---- profiling hook (no reference counterpart) --------------------------------- */
 /* Times one of the step's weight-streaming GEMVs on its own: n_launches
  * back-to-back launches (cycling over the layers, so every launch streams a

@@ -1,0 +1,80 @@
+"""One rank of the tensor-parallel parity check (run by tests/test_gpu_tp.py
+under torch.distributed.run, one process per GPU): this rank's logit slice
+and the greedy tokens against the oracle's full model."""
+import argparse
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+from tests.vox_testlib import FULL, assert_logits_close, config_dict, oracle_model, top2_margin, vox  # noqa: E402
+
+CASES = {
+    # small shapes, window 64 so the ring evicts during the run
+    "small": (config_dict(dim=256, hidden_dim=512, n_heads=8, n_kv_heads=2, head_dim=32, sliding_window=64,
+                          rope_theta=1e4), 2, 1024, 80),
+    "full": (FULL, 2, 8192, 6),
+}
+
+
+def main():
+    import datetime
+
+    import torch.distributed as dist
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default="small", choices=sorted(CASES))
+    args = ap.parse_args()
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+    V = vox()
+    from oracle import oracle as o
+    o.build()
+    o.set_threads(max(1, (os.cpu_count() or 2) // world))
+    c, n_layers, vocab, n_steps = CASES[args.case]
+    uid = V.share_tp_unique_id(rank)
+    seed = 0
+    m = oracle_model(o, c, n_layers, vocab, seed)
+    oc = o.RollingKvCache(n_layers, c["n_kv_heads"], c["head_dim"], c["sliding_window"])
+    ids = o.gen_uniform_ids(seed, 3000000, vocab, n_steps)
+    failures = []
+    with V.TensorParallelDecoder(V.DecoderConfig(**c), rank, world, uid, n_layers, vocab, device=local) as tp:
+        tp.init_random(seed, 0.02)
+        sh = tp.shard
+        lo, hi = sh.vocab_begin, sh.vocab_begin + sh.vocab_local
+        worst = 0.0
+        for p in range(n_steps):
+            tok, logits = tp.step(int(ids[p]), p, want_logits=True)
+            ref_logits, ref_tok = m.step(oc, int(ids[p]), p)
+            try:
+                worst = max(worst, assert_logits_close(logits, ref_logits[lo:hi], f"rank {rank} step {p}"))
+                assert tok == ref_tok, f"step {p}: {tok} != {ref_tok} (margin {top2_margin(ref_logits):.3e})"
+            except AssertionError as e:
+                failures.append(str(e))
+                break
+        for l in range(n_layers):
+            ln, start, off = tp.kv_state(l)
+            want = (oc.layer_len_tokens(l), oc.layer_pos_offset(l))
+            if (ln, off) != want:
+                failures.append(f"layer {l}: ring state {(ln, off)} != {want}")
+        # greedy continuation on the device against the oracle's
+        pos = n_steps
+        tok0 = int(ids[-1])
+        got = tp.generate(tok0, pos, 3)
+        t = tok0
+        for i in range(3):
+            ref_logits, t = m.step(oc, t, pos + i)
+            if got[i] != t:
+                failures.append(f"greedy step {i}: {got[i]} != {t}")
+                break
+    print(f"rank {rank}: case {args.case}, worst logit diff {worst:.3e}, failures {failures}", flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    sys.exit(1 if failures else 0)
+
+
+if __name__ == "__main__":
+    main()

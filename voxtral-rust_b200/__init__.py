@@ -80,6 +80,14 @@ class LayerWeightsBF16(C.Structure):
                 ("w1", BF16Slice), ("w2", BF16Slice), ("w3", BF16Slice)]
 
 
+class TpShard(C.Structure):
+    """vox_tp_shard: the slice of the model one tensor-parallel rank holds."""
+
+    _fields_ = [("rank", C.c_int), ("size", C.c_int), ("n_heads", SZ), ("n_kv_heads", SZ), ("hidden", SZ),
+                ("vocab", SZ), ("vocab_local", SZ), ("q_head_begin", SZ), ("kv_head_begin", SZ),
+                ("hidden_begin", SZ), ("vocab_begin", SZ)]
+
+
 class AttentionShape(C.Structure):
     """AttentionShape (ops.rs:49-56)."""
 
@@ -129,6 +137,22 @@ _SIGS = {
     "vox_model_generate": ([VP, VP, C.c_int32, SZ, SZ, I32P], C.c_int),
     "vox_model_prefill": ([VP, VP, I32P, SZ, SZ], C.c_int),
     "vox_profile_gemv": ([VP, C.c_int, SZ, F32P, C.POINTER(C.c_uint64)], C.c_int),
+    "vox_tp_shard_of": ([C.POINTER(DecoderConfig), SZ, C.c_int, C.c_int, C.POINTER(TpShard)], C.c_int),
+    "vox_tp_unique_id": ([C.c_char_p], C.c_int),
+    "vox_tp_create": ([C.POINTER(DecoderConfig), C.POINTER(CtxOptions), C.c_int, C.c_int, C.c_char_p,
+                       C.POINTER(VP)], C.c_int),
+    "vox_tp_destroy": ([VP], None),
+    "vox_tp_init_random": ([VP, C.c_uint64, C.c_float], C.c_int),
+    "vox_tp_upload_layer_bf16": ([VP, SZ, C.c_void_p], C.c_int),
+    "vox_tp_upload_embed_bf16": ([VP, U16P, SZ], C.c_int),
+    "vox_tp_upload_lm_head_bf16": ([VP, U16P, SZ, F32P], C.c_int),
+    "vox_tp_step": ([VP, C.c_int32, SZ, I32P, F32P], C.c_int),
+    "vox_tp_prefill": ([VP, I32P, SZ, SZ], C.c_int),
+    "vox_tp_generate": ([VP, C.c_int32, SZ, SZ, I32P], C.c_int),
+    "vox_tp_kv_state": ([VP, SZ, C.POINTER(C.c_int64)], C.c_int),
+    "vox_tp_record_event": ([VP, C.c_int], C.c_int),
+    "vox_tp_event_elapsed_ms": ([VP, C.c_int, C.c_int, F32P], C.c_int),
+    "vox_tp_kernel_launches": ([VP], C.c_uint64),
     "vox_profile_bgemm": ([VP, C.c_int, SZ, SZ, F32P, C.POINTER(C.c_uint64)], C.c_int),
     "vox_linear_f32": ([VP, F32P, SZ, SZ, F32P, SZ, F32P, F32P], C.c_int),
     "vox_linear_bf16": ([VP, F32P, SZ, SZ, U16P, SZ, F32P, F32P], C.c_int),
@@ -436,6 +460,100 @@ class RollingKvCache:
 
     def reset(self):
         _check(lib().vox_kv_reset(self.h))
+
+
+# ---------------------------------------------------------------------------
+# Tensor-parallel single stream (one process per GPU)
+# ---------------------------------------------------------------------------
+
+def tp_shard(cfg: DecoderConfig, vocab, rank, size) -> TpShard:
+    """The shard rank `rank` of `size` holds (host only)."""
+    out = TpShard()
+    _check(lib().vox_tp_shard_of(C.byref(cfg), vocab, rank, size, C.byref(out)))
+    return out
+
+
+def tp_unique_id() -> bytes:
+    buf = C.create_string_buffer(128)
+    _check(lib().vox_tp_unique_id(buf))
+    return buf.raw
+
+
+def share_tp_unique_id(rank, make=tp_unique_id, group=None) -> bytes:
+    """Rank 0 makes the NCCL id; every rank of the torch.distributed group
+    receives it (any backend: the id travels as a Python object)."""
+    import torch.distributed as dist
+    box = [make() if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0, group=group)
+    uid = box[0]
+    if not isinstance(uid, (bytes, bytearray)) or len(uid) != 128:
+        raise ValueError("bad NCCL unique id")
+    return bytes(uid)
+
+
+class TensorParallelDecoder:
+    """The token loop sharded over tp_size GPUs (one object per rank)."""
+
+    def __init__(self, cfg: DecoderConfig, rank, size, uid: bytes, n_layers, vocab, device=0, max_positions=0):
+        self.cfg, self.rank, self.size = cfg, rank, size
+        self.n_layers, self.vocab = n_layers, vocab
+        self.shard = tp_shard(cfg, vocab, rank, size)
+        opt = CtxOptions(device, n_layers, vocab, max_positions, WEIGHTS_BF16, STEP_AUTO)
+        h = VP()
+        _check(lib().vox_tp_create(C.byref(cfg), C.byref(opt), rank, size, uid, C.byref(h)))
+        self.h = h.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().vox_tp_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def init_random(self, seed=0, std=0.02):
+        _check(lib().vox_tp_init_random(self.h, seed, std))
+
+    def step(self, token, pos, want_logits=False):
+        """One collective step; returns (next token, this rank's logit slice)."""
+        nxt = C.c_int32()
+        logits = np.empty(self.shard.vocab_local, np.float32) if want_logits else None
+        _check(lib().vox_tp_step(self.h, int(token), int(pos), C.byref(nxt), _p(logits)))
+        return nxt.value, logits
+
+    def prefill(self, tokens, pos0=0):
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        _check(lib().vox_tp_prefill(self.h, _p(t, I32P), t.size, int(pos0)))
+
+    def generate(self, token, pos, n_steps):
+        out = np.empty(n_steps, np.int32)
+        _check(lib().vox_tp_generate(self.h, int(token), int(pos), int(n_steps), _p(out, I32P)))
+        return out
+
+    def kv_state(self, layer):
+        out = (C.c_int64 * 3)()
+        _check(lib().vox_tp_kv_state(self.h, layer, out))
+        return tuple(out)
+
+    def record_event(self, slot):
+        _check(lib().vox_tp_record_event(self.h, slot))
+
+    def elapsed_ms(self, a, b):
+        ms = C.c_float()
+        _check(lib().vox_tp_event_elapsed_ms(self.h, a, b, C.byref(ms)))
+        return ms.value
+
+    def kernel_launches(self):
+        return int(lib().vox_tp_kernel_launches(self.h))
 
 
 # ---------------------------------------------------------------------------

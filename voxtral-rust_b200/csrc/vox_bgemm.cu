@@ -12,7 +12,7 @@
 // s*4 KB + (k2*16 + m8)*128, so LBO = 2 KB between K halves and SBO = 128 B
 // between 8-row groups).  A work item = one 128-row tile x a range of K
 // blocks; its blocks are contiguous, so a producer lane streams them with 1-D
-// cp.async.bulk (no tensor map, no multicast) into a 4-stage ring.
+// cp.async.bulk (no tensor map, one destination CTA) into a 4-stage ring.
 //
 // The B operand is X converted to bf16 twice: hi = bf16(x), lo = bf16(x - hi)
 // as columns b and 8 + b of an N = 16 operand, so the product carries ~16

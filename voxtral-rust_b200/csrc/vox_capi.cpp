@@ -17,6 +17,7 @@
 #include <vector>
 
 #include "../../include/vox_decoder.h"
+#include "vox_host.h"
 #include "vox_kernels.h"
 
 using namespace vox;
@@ -48,53 +49,6 @@ int fail(int code, const char* fmt, ...) {
         int rc_ = (expr);          \
         if (rc_ != VOX_OK) return rc_; \
     } while (0)
-
-template <class T>
-cudaError_t dalloc(T** p, size_t n) {
-    *p = nullptr;
-    if (n == 0) n = 1;
-    return cudaMalloc(reinterpret_cast<void**>(p), n * sizeof(T));
-}
-
-uint16_t f32_to_bf16(float f) {
-    uint32_t u;
-    std::memcpy(&u, &f, 4);
-    if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu)) return 0x7FC0;
-    return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
-}
-float bf16_to_f32(uint16_t h) {
-    uint32_t u = (uint32_t)h << 16;
-    float f;
-    std::memcpy(&f, &u, 4);
-    return f;
-}
-
-// Host mirror of one cache layer: the reference's (len_tokens, pos_offset)
-// plus the physical ring start.
-struct HostKv {
-    size_t len = 0, start = 0, pos_offset = 0;
-};
-
-// kv.rs:48-88 append bookkeeping for n tokens.  Returns the ring slot of the
-// first new token, or -1 if the result would not fit in `cap` slots.
-long long host_append(HostKv& s, size_t n, size_t window, size_t cap) {
-    if (n == 0) return (long long)((s.start + s.len) % cap);
-    HostKv t = s;
-    size_t requested = t.len + n;
-    size_t drop = requested > window ? requested - window : 0;
-    if (drop > 0) {
-        size_t keep = t.len > drop ? t.len - drop : 0;
-        size_t phys = t.len < drop ? t.len : drop;
-        t.start = (t.start + phys) % cap;
-        t.len = keep;
-        t.pos_offset += drop;
-    }
-    if (t.len + n > cap) return -1;
-    long long slot0 = (long long)((t.start + t.len) % cap);
-    t.len += n;
-    s = t;
-    return slot0;
-}
 
 struct LayerDev {
     void* wqkv = nullptr;   // [q_dim + 2 kv_dim, dim]: wq rows, wk rows, wv rows
@@ -206,6 +160,16 @@ BgChain chain_of(const BgArgs& a, const BgPlan& p) {
 }  // namespace
 
 int vox::report_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
+int vox::report_errorf(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
 
 struct vox_ctx {
     vox_decoder_config cfg{};

@@ -74,7 +74,7 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
 }
 
 // 1-D bulk copy global -> this CTA's shared memory, completing on `bar`.
-// dst and src 16-byte aligned, bytes a multiple of 16.  No multicast.
+// dst and src 16-byte aligned, bytes a multiple of 16.  One destination CTA.
 __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes,
                                               uint64_t* bar, uint64_t policy) {
     asm volatile(

@@ -12,7 +12,7 @@
 //
 // Work split: CTA b owns a contiguous band of rows, hence one contiguous
 // byte range of W.  Warp 8 is a producer: one lane streams the band into a
-// ring of shared-memory stages with cp.async.bulk (TMA, no multicast) and
+// ring of shared-memory stages with cp.async.bulk (TMA, this CTA only) and
 // mbarrier completion.  Warps 0..7 consume: warp w always handles K segment
 // (w % nseg) of row pair (w / nseg) of each stage, so its slice of x lives
 // in registers for the whole kernel and shared memory carries weights only.

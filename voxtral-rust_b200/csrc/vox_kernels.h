@@ -249,6 +249,12 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 
 cudaError_t launch_argmax_final(const ArgmaxPart* parts, int n, StepState* step, int32_t* tok_out,
                                 cudaStream_t s, bool pdl);
+// Tensor-parallel argmax: this rank's best (value, index + index_offset) as
+// an order-preserving 64-bit key (max-reduced across ranks), then the step
+// bookkeeping from the reduced key.
+cudaError_t launch_tp_argmax_key(const ArgmaxPart* parts, int n, long long index_offset, unsigned long long* key,
+                                 cudaStream_t s, bool pdl);
+cudaError_t launch_tp_argmax_apply(const unsigned long long* key, StepState* step, int32_t* tok_out, cudaStream_t s);
 cudaError_t launch_kv_scatter(const float* src_k, const float* src_v, float* k_ring, float* v_ring,
                               int n_kv, int hd, int cap, int slot0, int n_tokens, cudaStream_t s);
 cudaError_t launch_kv_gather(const float* k_ring, const float* v_ring, float* dst_k, float* dst_v,
@@ -259,6 +265,11 @@ cudaError_t launch_kv_gather(const float* k_ring, const float* v_ring, float* ds
 cudaError_t launch_gen_matrix(void* dst, int wsize, uint64_t seed, uint64_t tensor_id, float std,
                               long long rows, long long cols, int row_mul, int row_add,
                               cudaStream_t s);
+// Same for a [rows, cols] block whose element (0, 0) is (row0, col0) of a
+// tensor with full_cols columns (tensor-parallel shards).
+cudaError_t launch_gen_matrix_part(void* dst, int wsize, uint64_t seed, uint64_t tensor_id, float std,
+                                   long long rows, long long cols, int row_mul, int row_add, long long row0,
+                                   long long col0, long long full_cols, cudaStream_t s);
 cudaError_t launch_fill_f32(float* dst, float v, long long n, cudaStream_t s);
 // Fill tokens 0..len-1 of a ring (start slot 0) from the generator: K from
 // tensor id_k, V from id_v, each [len, n_kv, hd] token-major, bf16-rounded.

@@ -56,6 +56,71 @@ __global__ void __launch_bounds__(256) argmax_final_kernel(const ArgmaxPart* par
     }
 }
 
+// ---- tensor-parallel argmax: one (value, index) key per rank --------------------
+// Order-preserving key: a larger key is a larger value, or the same value at a
+// lower global index; 0 means "no finite candidate" (all NaN).
+__global__ void __launch_bounds__(256) tp_argmax_key_kernel(const ArgmaxPart* parts, int n, long long index_offset,
+                                                           unsigned long long* key) {
+    pdl_allow_dependents();
+    pdl_wait_prior_grids();
+    __shared__ float sv[8];
+    __shared__ int si[8];
+    float best = -INFINITY;
+    int bi = 0x7FFFFFFF;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = parts[i].v;
+        const int idx = parts[i].i;
+        if (v > best || (v == best && idx < bi)) {
+            best = v;
+            bi = idx;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+        const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) {
+            best = ov;
+            bi = oi;
+        }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sv[warp] = best;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+            if (sv[w] > best || (sv[w] == best && si[w] < bi)) {
+                best = sv[w];
+                bi = si[w];
+            }
+        unsigned long long k = 0ull;
+        if (bi != 0x7FFFFFFF) {
+            if (best == 0.0f) best = 0.0f;  // -0 and +0 compare equal: same key
+            const uint32_t u = __float_as_uint(best);
+            const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+            const uint32_t gi = (uint32_t)(index_offset + bi);
+            k = ((unsigned long long)ord << 32) | (unsigned long long)(0xFFFFFFFFu - gi);
+        }
+        *key = k;
+    }
+}
+
+__global__ void tp_argmax_apply_kernel(const unsigned long long* key, StepState* step, int32_t* tok_out) {
+    pdl_allow_dependents();
+    pdl_wait_prior_grids();
+    if (threadIdx.x == 0) {
+        const unsigned long long k = *key;
+        const int idx = k == 0ull ? 0 : (int)(0xFFFFFFFFu - (uint32_t)k);  // all NaN: token 0
+        step->next_tok = idx;
+        if (step->greedy) step->tok = idx;
+        if (step->advance) step->pos += 1;
+        if (tok_out) *tok_out = idx;
+    }
+}
+
 // ---- KV ring scatter / gather -------------------------------------------------
 // src is token-major [n, n_kv, hd] (the reference's layout); ring head-major.
 __global__ void kv_scatter_kernel(const float* __restrict__ sk, const float* __restrict__ sv,
@@ -118,14 +183,19 @@ __device__ __forceinline__ uint16_t f32_to_bf16_rne(float f) {
     return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
 }
 
+// Element (r, c) of a [rows, cols] block of the logical tensor, whose
+// top-left element is (row0, col0) of a tensor with full_cols columns; the
+// generator is indexed by the logical element.
 __global__ void gen_matrix_kernel(void* dst, int wsize, uint64_t key, float stdv, long long rows,
-                                  long long cols, int row_mul, int row_add) {
+                                  long long cols, int row_mul, int row_add, long long row0, long long col0,
+                                  long long full_cols) {
     const long long total = rows * cols;
     for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
          e += (long long)gridDim.x * blockDim.x) {
         const long long r = e / cols, c = e - r * cols;
         const size_t o = (size_t)(r * row_mul + row_add) * cols + c;
-        const float v = __fmul_rn(gen_z(key, (uint64_t)e), stdv);
+        const uint64_t le = (uint64_t)((row0 + r) * full_cols + col0 + c);
+        const float v = __fmul_rn(gen_z(key, le), stdv);
         if (wsize == 2)
             reinterpret_cast<uint16_t*>(dst)[o] = f32_to_bf16_rne(v);
         else
@@ -279,6 +349,25 @@ cudaError_t launch_argmax_final(const ArgmaxPart* parts, int n, StepState* step,
     return cudaLaunchKernelEx(&cfg, argmax_final_kernel, parts, n, step, tok_out);
 }
 
+cudaError_t launch_tp_argmax_key(const ArgmaxPart* parts, int n, long long index_offset, unsigned long long* key,
+                                 cudaStream_t s, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, tp_argmax_key_kernel, parts, n, index_offset, key);
+}
+
+cudaError_t launch_tp_argmax_apply(const unsigned long long* key, StepState* step, int32_t* tok_out, cudaStream_t s) {
+    tp_argmax_apply_kernel<<<1, 32, 0, s>>>(key, step, tok_out);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_kv_scatter(const float* sk, const float* sv, float* kr, float* vr, int n_kv, int hd,
                               int cap, int slot0, int n_tokens, cudaStream_t s) {
     const long long total = (long long)n_tokens * n_kv * hd;
@@ -298,10 +387,17 @@ cudaError_t launch_kv_gather(const float* kr, const float* vr, float* dk, float*
 cudaError_t launch_gen_matrix(void* dst, int wsize, uint64_t seed, uint64_t tensor_id, float stdv,
                               long long rows, long long cols, int row_mul, int row_add,
                               cudaStream_t s) {
+    return launch_gen_matrix_part(dst, wsize, seed, tensor_id, stdv, rows, cols, row_mul, row_add, 0, 0, cols, s);
+}
+
+cudaError_t launch_gen_matrix_part(void* dst, int wsize, uint64_t seed, uint64_t tensor_id, float stdv,
+                                   long long rows, long long cols, int row_mul, int row_add, long long row0,
+                                   long long col0, long long full_cols, cudaStream_t s) {
     const uint64_t key = host_mix64(seed ^ host_mix64(tensor_id + 0x632BE59BD9B4E019ull));
     const long long total = rows * cols;
+    if (total == 0) return cudaSuccess;
     gen_matrix_kernel<<<grid_for(total, 256), 256, 0, s>>>(dst, wsize, key, stdv, rows, cols, row_mul,
-                                                           row_add);
+                                                           row_add, row0, col0, full_cols);
     return cudaGetLastError();
 }
 

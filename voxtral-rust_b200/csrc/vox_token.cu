@@ -11,8 +11,8 @@
 // One CTA per SM, launched cooperatively so that all CTAs are resident:
 //   * warp 16 (producer): one lane streams this CTA's band of EVERY weight
 //     matrix of the step -- wqkv, wo, w1|w3, w2 of each layer, then the LM
-//     head -- into a 3 x 48 KB shared-memory ring with cp.async.bulk (TMA, no
-//     multicast).  Weights never depend on activations, so the producer never
+//     head -- into a 3 x 48 KB shared-memory ring with cp.async.bulk (TMA,
+//     this CTA only).  Weights never depend on activations, so the producer never
 //     waits for a phase to finish: HBM keeps streaming across layer and
 //     phase boundaries and through the attention phases.
 //   * warps 0..15 (consumers): walk the phases.  Between phases they meet at
