@@ -13,6 +13,9 @@ With N > 1 (torchrun, one process per GPU) every rank decodes its own
 independent stream (no collective on the data path: weak scaling); value is
 the total tokens/s of all ranks over the slowest rank's time.
 
+With N > 1 the ranks then decode one stream together, tensor parallel
+(2048-token context, 1024 greedy steps), reported as "tensor_parallel".
+
 The same run then measures the multi-stream workload (8 independent streams
 per GPU, contexts uniform in [256, 4096) with the cache prefilled from
 N(0,1) bf16, greedy decode with tensor-core GEMMs) and reports it as the
@@ -289,6 +292,38 @@ def run_multi_stream(V, ctx, args, rank, world, dist):
     return {"ms": ms, "steps": steps, "launches": launches, "lens": lens, "ctx_mean": ctx_mean, "e2e_ms": e2e_ms}
 
 
+TP_CONTEXT = 2048
+TP_WORKLOAD = ("26-layer decoder, batch 1, tensor parallel over all GPUs (q|k|v, w1|w3 and LM head "
+               "column-sharded, o-proj and w2 row-sharded; the 3072-wide residual is all-reduced after "
+               "o-proj and w2 by stores into the other GPUs' memory fused into the GEMVs), prefill of "
+               "2048 random ids then greedy decode")
+
+
+def run_tensor_parallel(V, args, rank, world, local, dist):
+    """One stream decoded by all ranks together; returns this rank's timings."""
+    cfg = V.DecoderConfig(dim=DIM, hidden_dim=HIDDEN, n_heads=NH, n_kv_heads=NKV, head_dim=HD,
+                          sliding_window=WINDOW, norm_eps=1e-5, rope_theta=1e6)
+    uid = V.share_tp_unique_id(rank)
+    steps = args.tp_steps
+    with V.TensorParallelDecoder(cfg, rank, world, uid, LAYERS, VOCAB, device=local,
+                                 max_positions=TP_CONTEXT + args.warmup + steps + 8) as tp:
+        tp.init_random(0, 0.02)
+        tp.connect_peers()  # exchange over NVLink peer memory, fused into the GEMVs
+        prompt = prompt_ids(0, TP_CONTEXT)  # the same ids on every rank
+        tp.prefill(prompt, 0)
+        pos = TP_CONTEXT
+        toks = tp.generate(int(prompt[-1]), pos, args.warmup)
+        pos += args.warmup
+        dist.barrier()
+        launches0 = tp.kernel_launches()
+        tp.record_event(0)
+        V.lib().vox_tp_generate(tp.h, int(toks[-1]), pos, steps, None)
+        tp.record_event(1)
+        ms = tp.elapsed_ms(0, 1)
+        launches = tp.kernel_launches() - launches0
+    return {"ms": ms, "steps": steps, "launches": launches, "ctx": [pos, pos + steps]}
+
+
 def run_ours(args):
     rank, world, local = dist_env()
     V = importlib.import_module("voxtral-rust_b200")
@@ -348,16 +383,22 @@ def run_ours(args):
     k_ms, k_bytes = ctx.profile_gemv(2, LAYERS * 4)
 
     ms_run = None if args.ms_steps == 0 else run_multi_stream(V, ctx, args, rank, world, dist)
+    tp_run = None
+    if world > 1 and args.tp_steps > 0:
+        ctx.close()  # release the replica's memory first
+        tp_run = run_tensor_parallel(V, args, rank, world, local, dist)
 
     t_max, e2e_max = ms, e2e_ms
-    ms_max = ms_e2e_max = 0.0
+    ms_max = ms_e2e_max = tp_max = 0.0
     if ms_run:
         ms_max, ms_e2e_max = ms_run["ms"], ms_run["e2e_ms"]
+    if tp_run:
+        tp_max = tp_run["ms"]
     if dist:
         import torch
-        t = torch.tensor([ms, e2e_ms, ms_max, ms_e2e_max], dtype=torch.float64)
+        t = torch.tensor([ms, e2e_ms, ms_max, ms_e2e_max, tp_max], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_max, e2e_max, ms_max, ms_e2e_max = (float(x) for x in t)
+        t_max, e2e_max, ms_max, ms_e2e_max, tp_max = (float(x) for x in t)
     if rank != 0:
         if dist:
             dist.barrier()
@@ -402,6 +443,18 @@ def run_ours(args):
             "e2e": {"value": MS_STREAMS * world / (ms_e2e_max / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": 40 * MS_STREAMS, "d2h_bytes_per_step": 4 * MS_STREAMS},
             "gpu_launches": ms_run["launches"]}
+    if tp_run:
+        tp_steps = tp_run["steps"]
+        tp_ctx = sum(tp_run["ctx"]) / 2
+        tp_bytes = step_bytes(int(tp_ctx))  # weights + KV of the whole model, split over the ranks
+        tp_gbs = tp_bytes / (tp_max / tp_steps / 1e3) / 1e9
+        line["tensor_parallel"] = {
+            "metric": "decoder tokens/s (1 stream, tensor parallel)", "tp": world,
+            "value": tp_steps / (tp_max / 1e3), "unit": "tokens/s", "ms_per_token": tp_max / tp_steps,
+            "steps": tp_steps, "workload": TP_WORKLOAD, "context": tp_run["ctx"],
+            "step_roofline": {"achieved": tp_gbs, "peak": peak * world, "unit": "GB/s",
+                              "frac": tp_gbs / (peak * world), "note": "aggregate HBM of all ranks"},
+            "gpu_launches": tp_run["launches"]}
     if world == 1 and not args.no_cpu:
         rate, sample = cpu_token_rate(1, args.cpu_layer_steps, 1)
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": 1, "kind": "port", "sample": sample}
@@ -421,6 +474,8 @@ def main():
     ap.add_argument("--cpu-layer-steps", type=int, default=24)
     ap.add_argument("--ms-steps", type=int, default=512,
                     help="greedy steps of the 8-streams-per-GPU run (0 skips it)")
+    ap.add_argument("--tp-steps", type=int, default=1024,
+                    help="greedy steps of the tensor-parallel run when N > 1 (0 skips it)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -256,6 +256,13 @@ int vox_tp_unique_id(unsigned char id[128]);
  * context owns a rolling cache of window cfg->sliding_window for its kv heads. */
 int vox_tp_create(const vox_decoder_config* cfg, const vox_ctx_options* opt, int tp_rank, int tp_size,
                   const unsigned char id[128], vox_tp** out);
+/* Peer-memory exchange (replaces the NCCL all-reduces with stores into the
+ * other GPUs' memory, fused into the GEMVs): every rank exports the CUDA IPC
+ * handle of its exchange area, the host gathers all of them in rank order
+ * ([tp_size][64] bytes) and every rank connects.  Collective; call between
+ * steps on all ranks, or never (NCCL stays in use). */
+int vox_tp_ipc_handle(vox_tp* tp, unsigned char out[64]);
+int vox_tp_connect_peers(vox_tp* tp, const unsigned char* handles);
 /* Releases the captured graph, then the NCCL communicator, then memory. */
 void vox_tp_destroy(vox_tp* tp);
 /* This rank's shards of the weights vox_ctx_init_random makes (same generator,

@@ -27,11 +27,11 @@ def _port():
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("case", ["small", "full"])
-def test_tensor_parallel_two_gpus(case):
+@pytest.mark.parametrize("case,exchange", [("small", "nccl"), ("small", "peer"), ("full", "peer")])
+def test_tensor_parallel_two_gpus(case, exchange):
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
-           os.path.join(ROOT, "tests", "tp_worker.py"), "--case", case]
+           os.path.join(ROOT, "tests", "tp_worker.py"), "--case", case, "--exchange", exchange]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-4000:]

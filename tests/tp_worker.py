@@ -26,6 +26,8 @@ def main():
     import torch.distributed as dist
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default="small", choices=sorted(CASES))
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="peer: stores into the other GPUs' memory fused into the GEMVs; nccl: all-reduce")
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -43,6 +45,8 @@ def main():
     failures = []
     with V.TensorParallelDecoder(V.DecoderConfig(**c), rank, world, uid, n_layers, vocab, device=local) as tp:
         tp.init_random(seed, 0.02)
+        if args.exchange == "peer":
+            tp.connect_peers()
         sh = tp.shard
         lo, hi = sh.vocab_begin, sh.vocab_begin + sh.vocab_local
         worst = 0.0
@@ -70,7 +74,8 @@ def main():
             if got[i] != t:
                 failures.append(f"greedy step {i}: {got[i]} != {t}")
                 break
-    print(f"rank {rank}: case {args.case}, worst logit diff {worst:.3e}, failures {failures}", flush=True)
+    print(f"rank {rank}: case {args.case} ({args.exchange}), worst logit diff {worst:.3e}, failures {failures}",
+          flush=True)
     dist.barrier()
     dist.destroy_process_group()
     sys.exit(1 if failures else 0)

@@ -142,6 +142,8 @@ _SIGS = {
     "vox_tp_create": ([C.POINTER(DecoderConfig), C.POINTER(CtxOptions), C.c_int, C.c_int, C.c_char_p,
                        C.POINTER(VP)], C.c_int),
     "vox_tp_destroy": ([VP], None),
+    "vox_tp_ipc_handle": ([VP, C.c_char_p], C.c_int),
+    "vox_tp_connect_peers": ([VP, C.c_char_p], C.c_int),
     "vox_tp_init_random": ([VP, C.c_uint64, C.c_float], C.c_int),
     "vox_tp_upload_layer_bf16": ([VP, SZ, C.c_void_p], C.c_int),
     "vox_tp_upload_embed_bf16": ([VP, U16P, SZ], C.c_int),
@@ -522,6 +524,16 @@ class TensorParallelDecoder:
 
     def init_random(self, seed=0, std=0.02):
         _check(lib().vox_tp_init_random(self.h, seed, std))
+
+    def connect_peers(self, group=None):
+        """Switch the exchange to NVLink peer memory: all-gather every rank's
+        CUDA IPC handle over the torch.distributed group, then map them."""
+        import torch.distributed as dist
+        buf = C.create_string_buffer(64)
+        _check(lib().vox_tp_ipc_handle(self.h, buf))
+        handles = [None] * self.size
+        dist.all_gather_object(handles, buf.raw, group=group)
+        _check(lib().vox_tp_connect_peers(self.h, b"".join(handles)))
 
     def step(self, token, pos, want_logits=False):
         """One collective step; returns (next token, this rank's logit slice)."""

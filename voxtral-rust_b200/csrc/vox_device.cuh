@@ -122,6 +122,24 @@ __device__ __forceinline__ void raise_error(unsigned* err, unsigned bit) {
     if (err) atomicOr(err, bit);
 }
 
+// Bounded wait until a 64-bit counter (written by other GPUs) reaches
+// target; false on timeout.
+__device__ __forceinline__ bool wait_counter_sys(const unsigned long long* c, unsigned long long target) {
+    uint64_t t0 = 0;
+    for (uint32_t it = 0;; ++it) {
+        unsigned long long v;
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(c) : "memory");
+        if (v >= target) return true;
+        if ((it & 63u) == 63u) {
+            const uint64_t now = global_timer_ns();
+            if (t0 == 0)
+                t0 = now;
+            else if (now - t0 > kWaitLimitNs)
+                return false;
+        }
+    }
+}
+
 // State of a cache layer after appending one token (kv.rs:48-88 with n = 1).
 __device__ __forceinline__ KvState kv_after_single_append(KvState s, int window, int cap) {
     int requested = s.len + 1;

@@ -186,6 +186,16 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
 
     pdl_wait_prior_grids();
 
+    // Tensor-parallel input: wait until every rank's partial sums for this
+    // exchange point have arrived (bounded), then x = their sum, in rank order.
+    const bool xsum = A.xch && A.xch_in >= 0;
+    if (xsum) {
+        if (tid == 0) {
+            const unsigned long long target = (__ldcg(A.tp_steps) + 1ull) * A.xch_arrivals;
+            if (!wait_counter_sys(A.xa.counter(A.xch[A.xa.rank], A.xch_in), target)) raise_error(A.err, ERR_PEER_WAIT);
+        }
+        named_barrier_sync(1, kConsumerWarps * 32);
+    }
     // Input vector: x, or the embedding row of the step's token.
     const float* x = A.x ? A.x + (long long)vec * A.x_stride : nullptr;
     const uint16_t* xe = nullptr;
@@ -218,6 +228,19 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
                 }
 #pragma unroll
                 for (int e = 0; e < EPC; ++e) xr[i][e] = (e & 1) ? bf16_hi(ws[e >> 1]) : bf16_lo(ws[e >> 1]);
+            } else if (xsum) {
+                unsigned char* own = A.xch[A.xa.rank];
+                for (int src = 0; src < A.xa.size; ++src) {
+                    const float* sl = A.xa.slot(own, A.xch_in, src);
+#pragma unroll
+                    for (int e = 0; e < EPC; e += 4) {
+                        const float4 v = __ldcg(reinterpret_cast<const float4*>(sl + k0 + e));
+                        xr[i][e] += v.x;
+                        xr[i][e + 1] += v.y;
+                        xr[i][e + 2] += v.z;
+                        xr[i][e + 3] += v.w;
+                    }
+                }
             } else {
 #pragma unroll
                 for (int e = 0; e < EPC; e += 4) {
@@ -323,12 +346,23 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
         }
     } else if constexpr (EPI == EPI_RESID) {
         float* y = A.y + (long long)vec * A.y_stride;
+        const bool xout = A.xch && A.xch_out >= 0;
         for (int lr = tid; lr < nrows; lr += nthr) {
             const int r = r0 + lr;
-            y[r] = __fadd_rn(A.resid[r], row_sum(lr));
+            const float v = __fadd_rn(A.resid[r], row_sum(lr));
+            y[r] = v;
+            if (xout)  // tensor parallel: this rank's partial rows into every rank's slot
+                for (int p = 0; p < A.xa.size; ++p) A.xa.slot(A.xch[p], A.xch_out, A.xa.rank)[r] = v;
         }
         if (A.kv_commit && blockIdx.x == 0 && tid == 0)
             *A.kv_commit = kv_after_single_append(*A.kv_commit, A.kv_window, A.ring_cap);
+        if (xout) {
+            named_barrier_sync(1, nthr);  // every row of this CTA is stored
+            if (tid == 0) {
+                __threadfence_system();
+                for (int p = 0; p < A.xa.size; ++p) atomicAdd_system(A.xa.counter(A.xch[p], A.xch_out), 1ull);
+            }
+        }
     } else if constexpr (EPI == EPI_QKV) {
         const long long pos = A.step->pos;
         const bool pos_ok = pos >= 0 && pos < A.max_pos;

@@ -42,6 +42,29 @@ enum : unsigned {
     ERR_POS_RANGE = 8u,      // position beyond the RoPE table
     ERR_TOKEN_RANGE = 16u,   // token id outside the vocabulary
     ERR_GRID_WAIT = 64u,     // a grid-wide wait (token kernel, GEMM chain) expired
+    ERR_PEER_WAIT = 128u,    // a wait for another GPU's data expired (tensor-parallel exchange)
+};
+
+// Tensor-parallel exchange area of one rank (device memory, shared with the
+// other ranks through CUDA IPC): [points][size][dim] f32 receive slots (slot
+// (k, r) holds rank r's partial sums for exchange point k), then [points]
+// arrival counters, then [size] argmax keys and the key arrival counter.
+// Counters only grow: point k has received step s's data once it reaches
+// (s + 1) * arrivals-per-step.
+struct XchArea {
+    int rank, size, points, dim;
+    __host__ __device__ size_t slot_floats() const { return (size_t)points * size * dim; }
+    __host__ __device__ size_t bytes() const { return slot_floats() * 4 + ((size_t)points + size + 1) * 8; }
+    __host__ __device__ float* slot(unsigned char* base, int point, int src) const {
+        return reinterpret_cast<float*>(base) + ((size_t)point * size + src) * dim;
+    }
+    __host__ __device__ unsigned long long* counter(unsigned char* base, int point) const {
+        return reinterpret_cast<unsigned long long*>(base + slot_floats() * 4) + point;
+    }
+    __host__ __device__ unsigned long long* keys(unsigned char* base) const {
+        return reinterpret_cast<unsigned long long*>(base + slot_floats() * 4) + points;
+    }
+    __host__ __device__ unsigned long long* key_counter(unsigned char* base) const { return keys(base) + size; }
 };
 
 enum : int { EPI_STORE = 0, EPI_RESID = 1, EPI_QKV = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
@@ -92,6 +115,14 @@ struct GemvArgs {
     // LM head
     ArgmaxPart* am_part;
     unsigned* err;
+    // Tensor-parallel exchange over peer memory (null xch: off).  xch[p] is
+    // rank p's exchange area (a peer mapping for p != rank).
+    unsigned char* const* xch;
+    XchArea xa;
+    int xch_out;                      // >= 0: rows also go to slot (xch_out, rank) of every rank
+    int xch_in;                       // >= 0: x = sum over ranks of this rank's slots (xch_in, *)
+    unsigned long long xch_arrivals;  // arrivals per step at point xch_in (size x producer grid)
+    const unsigned long long* tp_steps;  // steps this rank has completed
 };
 
 struct AttnArgs {
@@ -255,6 +286,11 @@ cudaError_t launch_argmax_final(const ArgmaxPart* parts, int n, StepState* step,
 cudaError_t launch_tp_argmax_key(const ArgmaxPart* parts, int n, long long index_offset, unsigned long long* key,
                                  cudaStream_t s, bool pdl);
 cudaError_t launch_tp_argmax_apply(const unsigned long long* key, StepState* step, int32_t* tok_out, cudaStream_t s);
+// Same over peer memory in one launch: this rank's key to every rank, wait
+// for all keys, take the max, apply it, count the step in tp_steps.
+cudaError_t launch_tp_argmax_xch(const ArgmaxPart* parts, int n, long long index_offset, unsigned char* const* xch,
+                                 XchArea xa, unsigned long long* tp_steps, StepState* step, int32_t* tok_out,
+                                 unsigned* err, cudaStream_t s, bool pdl);
 cudaError_t launch_kv_scatter(const float* src_k, const float* src_v, float* k_ring, float* v_ring,
                               int n_kv, int hd, int cap, int slot0, int n_tokens, cudaStream_t s);
 cudaError_t launch_kv_gather(const float* k_ring, const float* v_ring, float* dst_k, float* dst_v,

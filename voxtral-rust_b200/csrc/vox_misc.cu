@@ -59,6 +59,23 @@ __global__ void __launch_bounds__(256) argmax_final_kernel(const ArgmaxPart* par
 // ---- tensor-parallel argmax: one (value, index) key per rank --------------------
 // Order-preserving key: a larger key is a larger value, or the same value at a
 // lower global index; 0 means "no finite candidate" (all NaN).
+__device__ __forceinline__ unsigned long long tp_argmax_key(float best, int bi, long long index_offset) {
+    if (bi == 0x7FFFFFFF) return 0ull;
+    if (best == 0.0f) best = 0.0f;  // -0 and +0 compare equal: same key
+    const uint32_t u = __float_as_uint(best);
+    const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    const uint32_t gi = (uint32_t)(index_offset + bi);
+    return ((unsigned long long)ord << 32) | (unsigned long long)(0xFFFFFFFFu - gi);
+}
+
+__device__ __forceinline__ void tp_apply_key(unsigned long long k, StepState* step, int32_t* tok_out) {
+    const int idx = k == 0ull ? 0 : (int)(0xFFFFFFFFu - (uint32_t)k);  // all NaN: token 0
+    step->next_tok = idx;
+    if (step->greedy) step->tok = idx;
+    if (step->advance) step->pos += 1;
+    if (tok_out) *tok_out = idx;
+}
+
 __global__ void __launch_bounds__(256) tp_argmax_key_kernel(const ArgmaxPart* parts, int n, long long index_offset,
                                                            unsigned long long* key) {
     pdl_allow_dependents();
@@ -96,29 +113,75 @@ __global__ void __launch_bounds__(256) tp_argmax_key_kernel(const ArgmaxPart* pa
                 best = sv[w];
                 bi = si[w];
             }
-        unsigned long long k = 0ull;
-        if (bi != 0x7FFFFFFF) {
-            if (best == 0.0f) best = 0.0f;  // -0 and +0 compare equal: same key
-            const uint32_t u = __float_as_uint(best);
-            const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-            const uint32_t gi = (uint32_t)(index_offset + bi);
-            k = ((unsigned long long)ord << 32) | (unsigned long long)(0xFFFFFFFFu - gi);
+        *key = tp_argmax_key(best, bi, index_offset);
+    }
+}
+
+// One block: the rank's best candidate, exchanged with every rank through
+// peer memory, then the global argmax and the step bookkeeping.
+__global__ void __launch_bounds__(256) tp_argmax_xch_kernel(const ArgmaxPart* parts, int n, long long index_offset,
+                                                           unsigned char* const* xch, XchArea xa,
+                                                           unsigned long long* tp_steps, StepState* step,
+                                                           int32_t* tok_out, unsigned* err) {
+    pdl_allow_dependents();
+    pdl_wait_prior_grids();
+    __shared__ float sv[8];
+    __shared__ int si[8];
+    float best = -INFINITY;
+    int bi = 0x7FFFFFFF;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = parts[i].v;
+        const int idx = parts[i].i;
+        if (v > best || (v == best && idx < bi)) {
+            best = v;
+            bi = idx;
         }
-        *key = k;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xFFFFFFFFu, best, o);
+        const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) {
+            best = ov;
+            bi = oi;
+        }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sv[warp] = best;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+            if (sv[w] > best || (sv[w] == best && si[w] < bi)) {
+                best = sv[w];
+                bi = si[w];
+            }
+        const unsigned long long mine = tp_argmax_key(best, bi, index_offset);
+        for (int p = 0; p < xa.size; ++p) xa.keys(xch[p])[xa.rank] = mine;
+        __threadfence_system();
+        for (int p = 0; p < xa.size; ++p) atomicAdd_system(xa.key_counter(xch[p]), 1ull);
+        unsigned char* own = xch[xa.rank];
+        const unsigned long long done = *reinterpret_cast<volatile unsigned long long*>(tp_steps);
+        unsigned long long k = 0ull;
+        if (wait_counter_sys(xa.key_counter(own), (done + 1ull) * (unsigned long long)xa.size)) {
+            for (int r = 0; r < xa.size; ++r) {
+                const unsigned long long kr = __ldcg(xa.keys(own) + r);
+                if (kr > k) k = kr;
+            }
+        } else {
+            raise_error(err, ERR_PEER_WAIT);
+        }
+        tp_apply_key(k, step, tok_out);
+        *tp_steps = done + 1ull;
     }
 }
 
 __global__ void tp_argmax_apply_kernel(const unsigned long long* key, StepState* step, int32_t* tok_out) {
     pdl_allow_dependents();
     pdl_wait_prior_grids();
-    if (threadIdx.x == 0) {
-        const unsigned long long k = *key;
-        const int idx = k == 0ull ? 0 : (int)(0xFFFFFFFFu - (uint32_t)k);  // all NaN: token 0
-        step->next_tok = idx;
-        if (step->greedy) step->tok = idx;
-        if (step->advance) step->pos += 1;
-        if (tok_out) *tok_out = idx;
-    }
+    if (threadIdx.x == 0) tp_apply_key(*key, step, tok_out);
 }
 
 // ---- KV ring scatter / gather -------------------------------------------------
@@ -361,6 +424,22 @@ cudaError_t launch_tp_argmax_key(const ArgmaxPart* parts, int n, long long index
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, tp_argmax_key_kernel, parts, n, index_offset, key);
+}
+
+cudaError_t launch_tp_argmax_xch(const ArgmaxPart* parts, int n, long long index_offset, unsigned char* const* xch,
+                                 XchArea xa, unsigned long long* tp_steps, StepState* step, int32_t* tok_out,
+                                 unsigned* err, cudaStream_t s, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, tp_argmax_xch_kernel, parts, n, index_offset, xch, xa, tp_steps, step, tok_out,
+                              err);
 }
 
 cudaError_t launch_tp_argmax_apply(const unsigned long long* key, StepState* step, int32_t* tok_out, cudaStream_t s) {

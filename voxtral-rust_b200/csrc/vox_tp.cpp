@@ -12,6 +12,15 @@
 // argmax is one 64-bit all-reduce (max) of an order-preserving (value,
 // index) key.  Embedding, RMSNorms and residual stream are replicated.
 //
+// After vox_tp_connect_peers the exchange runs over NVLink peer memory
+// instead, fused into the GEMVs: the o-proj / w2 epilogue stores its rows
+// into a receive slot of every rank and bumps each rank's arrival counter
+// (system-scope fence + atomic); the next GEMV's prologue waits (bounded) for
+// all ranks' arrivals and sums the slots in rank order, so every rank holds
+// bit-identical activations, while its producer warp already streams
+// weights.  The argmax keys travel the same way in one kernel.  The areas
+// are mapped with CUDA IPC (one process per GPU).
+//
 // The per-rank kernels are the single-stream ones (vox_gemv.cu,
 // vox_attention.cu) run on the local shapes.  NCCL is loaded at run time
 // (dlopen of libnccl.so.2), so the library itself does not depend on it.
@@ -134,6 +143,13 @@ struct vox_tp {
     int32_t* h_tok = nullptr;       // pinned
     unsigned* h_err = nullptr;      // pinned
     cudaEvent_t ev[8] = {};
+    // exchange over peer memory (after vox_tp_connect_peers); NCCL otherwise
+    XchArea xa{};
+    unsigned char* xch_own = nullptr;           // this rank's exchange area (IPC-exported)
+    std::vector<unsigned char*> peer_maps;      // opened IPC mappings of the other ranks' areas
+    unsigned char** xch_ptrs = nullptr;         // device array [size]: every rank's area
+    unsigned long long* tp_steps = nullptr;     // steps completed (device)
+    bool p2p = false;
     size_t layer_elems() const { return sh.n_kv_heads * cap * cfg.head_dim; }
 };
 
@@ -147,7 +163,7 @@ int check_errors(vox_tp* t) {
     TP_CUDA(cudaMemsetAsync(t->err, 0, sizeof(unsigned), t->stream));
     TP_CUDA(cudaMemsetAsync(t->tickets, 0, t->sh.n_kv_heads * sizeof(unsigned), t->stream));
     TP_CUDA(cudaStreamSynchronize(t->stream));
-    if (bits & (ERR_FULL_WAIT | ERR_EMPTY_WAIT | ERR_DRAIN_WAIT))
+    if (bits & (ERR_FULL_WAIT | ERR_EMPTY_WAIT | ERR_DRAIN_WAIT | ERR_PEER_WAIT))
         return report_errorf(VOX_ERR_DEVICE_TIMEOUT, "a bounded wait inside a kernel expired (bits 0x%x)", bits);
     if (bits & ERR_POS_RANGE) return report_errorf(VOX_ERR_RANGE, "position beyond the RoPE table");
     if (bits & ERR_TOKEN_RANGE) return report_errorf(VOX_ERR_RANGE, "token id outside the vocabulary");
@@ -159,8 +175,18 @@ GemvArgs base(vox_tp* t) {
     a.step = t->step;
     a.eps = t->cfg.norm_eps;
     a.err = t->err;
+    a.xch_out = a.xch_in = -1;
+    if (t->p2p) {
+        a.xch = t->xch_ptrs;
+        a.xa = t->xa;
+        a.tp_steps = t->tp_steps;
+    }
     return a;
 }
+
+// Exchange points: 2l after layer l's o-proj, 2l + 1 after its w2.
+int point_after_o(size_t l) { return (int)(2 * l); }
+int point_after_w2(size_t l) { return (int)(2 * l + 1); }
 
 // One layer (decoder.rs:88-155) on this rank's shard, two all-reduces.
 int enqueue_layer(vox_tp* t, size_t l) {
@@ -177,6 +203,10 @@ int enqueue_layer(vox_tp* t, size_t l) {
     if (l == 0) {
         a.x_embed = t->embed;
         a.vocab = (int)s.vocab;
+        a.x_copy_out = t->hid;
+    } else if (t->p2p) {  // x = sum of the ranks' w2 partials of layer l - 1
+        a.xch_in = point_after_w2(l - 1);
+        a.xch_arrivals = (unsigned long long)s.size * t->p_w2.grid;
         a.x_copy_out = t->hid;
     } else {
         a.x = t->hid;
@@ -225,12 +255,20 @@ int enqueue_layer(vox_tp* t, size_t l) {
     a.kv_commit = st;
     a.kv_window = win;
     a.ring_cap = cap;
+    if (t->p2p) a.xch_out = point_after_o(l);
     TP_CUDA(launch_gemv(t->p_o, a, EPI_RESID, t->stream, true));
-    TP_NCCL(t->api, t->api->all_reduce(t->hmid, t->hmid, dim, ncclFloat32, ncclSum, t->comm, t->stream));
+    if (!t->p2p)
+        TP_NCCL(t->api, t->api->all_reduce(t->hmid, t->hmid, dim, ncclFloat32, ncclSum, t->comm, t->stream));
 
     a = base(t);
     a.W = L.w13;
-    a.x = t->hmid;
+    if (t->p2p) {
+        a.xch_in = point_after_o(l);
+        a.xch_arrivals = (unsigned long long)s.size * t->p_o.grid;
+        a.x_copy_out = t->hmid;  // the reduced vector, for w2's residual
+    } else {
+        a.x = t->hmid;
+    }
     a.norm_w = L.ffn_norm;
     a.y = t->act;
     TP_CUDA(launch_gemv(t->p_w13, a, EPI_SWIGLU, t->stream, true));
@@ -240,19 +278,31 @@ int enqueue_layer(vox_tp* t, size_t l) {
     a.x = t->act;
     a.y = t->hid;
     a.resid = s.rank == 0 ? t->hmid : t->zeros;
+    if (t->p2p) a.xch_out = point_after_w2(l);
     TP_CUDA(launch_gemv(t->p_w2, a, EPI_RESID, t->stream, true));
-    TP_NCCL(t->api, t->api->all_reduce(t->hid, t->hid, dim, ncclFloat32, ncclSum, t->comm, t->stream));
+    if (!t->p2p)
+        TP_NCCL(t->api, t->api->all_reduce(t->hid, t->hid, dim, ncclFloat32, ncclSum, t->comm, t->stream));
     return VOX_OK;
 }
 
 int enqueue_head(vox_tp* t) {
     GemvArgs a = base(t);
     a.W = t->head;
-    a.x = t->hid;
+    if (t->p2p) {
+        a.xch_in = point_after_w2(t->layers.size() - 1);
+        a.xch_arrivals = (unsigned long long)t->sh.size * t->p_w2.grid;
+    } else {
+        a.x = t->hid;
+    }
     a.norm_w = t->final_norm;
     a.y = t->logits;
     a.am_part = t->am_part;
     TP_CUDA(launch_gemv(t->p_head, a, EPI_ARGMAX, t->stream, true));
+    if (t->p2p) {
+        TP_CUDA(launch_tp_argmax_xch(t->am_part, t->p_head.grid, (long long)t->sh.vocab_begin, t->xch_ptrs, t->xa,
+                                     t->tp_steps, t->step, t->tok_out, t->err, t->stream, true));
+        return VOX_OK;
+    }
     TP_CUDA(launch_tp_argmax_key(t->am_part, t->p_head.grid, (long long)t->sh.vocab_begin, t->key, t->stream, true));
     TP_NCCL(t->api, t->api->all_reduce(t->key, t->key, 1, ncclUint64, ncclMax, t->comm, t->stream));
     TP_CUDA(launch_tp_argmax_apply(t->key, t->step, t->tok_out, t->stream));
@@ -275,7 +325,7 @@ int build_graph(vox_tp* t) {
     e = cudaGraphInstantiate(&t->graph, g, 0);
     cudaGraphDestroy(g);
     TP_CUDA(e);
-    t->graph_kernels = t->layers.size() * 5 + 3;
+    t->graph_kernels = t->layers.size() * 5 + (t->p2p ? 2 : 3);
     return VOX_OK;
 }
 
@@ -377,6 +427,11 @@ void vox_tp_destroy(vox_tp* t) {
     if (t->stream) cudaStreamSynchronize(t->stream);
     if (t->graph) cudaGraphExecDestroy(t->graph);  // holds NCCL calls: release before the communicator
     if (t->comm && t->api) t->api->comm_destroy(t->comm);
+    for (unsigned char* m : t->peer_maps)
+        if (m) cudaIpcCloseMemHandle(m);
+    if (t->xch_ptrs) cudaFree(t->xch_ptrs);
+    if (t->xch_own) cudaFree(t->xch_own);
+    if (t->tp_steps) cudaFree(t->tp_steps);
     for (auto& L : t->layers) {
         void* p[] = {L.wqkv, L.wo, L.w13, L.w2, L.attn_norm, L.ffn_norm};
         for (void* q : p)
@@ -489,6 +544,14 @@ int vox_tp_create(const vox_decoder_config* cfg, const vox_ctx_options* opt, int
     CREATE_TRY(dalloc(&t->v, o.n_layers * t->layer_elems()));
     CREATE_TRY(dalloc(&t->dstate, o.n_layers));
     CREATE_TRY(cudaMemset(t->dstate, 0, o.n_layers * sizeof(KvState)));
+    t->xa.rank = tp_rank;
+    t->xa.size = tp_size;
+    t->xa.points = (int)(2 * o.n_layers);
+    t->xa.dim = (int)dim;
+    CREATE_TRY(cudaMalloc(&t->xch_own, t->xa.bytes()));
+    CREATE_TRY(cudaMemset(t->xch_own, 0, t->xa.bytes()));
+    CREATE_TRY(dalloc(&t->tp_steps, 1));
+    CREATE_TRY(cudaMemset(t->tp_steps, 0, sizeof(unsigned long long)));
     CREATE_TRY(cudaMallocHost(&t->h_tok, 4));
     CREATE_TRY(cudaMallocHost(&t->h_err, sizeof(unsigned)));
     if (ensure_host_steps(t, 1024) != VOX_OK) return bail(VOX_ERR_OOM);
@@ -517,6 +580,50 @@ int vox_tp_create(const vox_decoder_config* cfg, const vox_ctx_options* opt, int
         return bail(report_errorf(VOX_ERR_CUDA, "ncclCommInitRank failed: %s", api->error_string(r)));
     }
     *out = t;
+    return VOX_OK;
+}
+
+int vox_tp_ipc_handle(vox_tp* t, unsigned char out[64]) {
+    if (!t || !out) return report_errorf(VOX_ERR_INVALID_ARG, "null argument");
+    TP_CUDA(cudaSetDevice(t->dev));
+    cudaIpcMemHandle_t h;
+    TP_CUDA(cudaIpcGetMemHandle(&h, t->xch_own));
+    static_assert(sizeof(h) == 64, "CUDA IPC handle size");
+    memcpy(out, &h, 64);
+    return VOX_OK;
+}
+
+int vox_tp_connect_peers(vox_tp* t, const unsigned char* handles) {
+    if (!t || !handles) return report_errorf(VOX_ERR_INVALID_ARG, "null argument");
+    if (t->p2p) return VOX_OK;
+    TP_CUDA(cudaSetDevice(t->dev));
+    TP_CUDA(cudaStreamSynchronize(t->stream));
+    const int T = t->sh.size;
+    std::vector<unsigned char*> ptrs(T, nullptr);
+    for (int p = 0; p < T; ++p) {
+        if (p == t->sh.rank) {
+            ptrs[p] = t->xch_own;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, handles + (size_t)p * 64, 64);
+        void* m = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&m, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (unsigned char* q : t->peer_maps) cudaIpcCloseMemHandle(q);
+            t->peer_maps.clear();
+            return report_errorf(VOX_ERR_CUDA, "mapping rank %d's exchange area failed: %s", p, cudaGetErrorString(e));
+        }
+        ptrs[p] = static_cast<unsigned char*>(m);
+        t->peer_maps.push_back(ptrs[p]);
+    }
+    TP_CUDA(dalloc(&t->xch_ptrs, (size_t)T));
+    TP_CUDA(cudaMemcpy(t->xch_ptrs, ptrs.data(), T * sizeof(unsigned char*), cudaMemcpyHostToDevice));
+    if (t->graph) {  // the next step is captured again with the peer-memory exchange
+        cudaGraphExecDestroy(t->graph);
+        t->graph = nullptr;
+    }
+    t->p2p = true;
     return VOX_OK;
 }
 
