@@ -407,14 +407,13 @@ __device__ __forceinline__ float dot4(const float4& a, const float4& b) {
     return fmaf(a.w, b.w, d);
 }
 
-constexpr int kWarpStages = 3;  // per-warp ring depth of the warp-per-chunk kernel
-
-template <int G>
-__global__ void __launch_bounds__(kAttnThreads, 2) attn_warp_kernel(const AttnArgs A) {
+// Warp-per-chunk kernel, D-stage per-warp ring.  At most 128 registers, so
+// that one CTA fits on an SM beside a GEMV CTA and launches early.
+template <int G, int D>
+__global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnArgs A) {
     constexpr int TPG = 32 / G;           // tokens per group: G * TPG = 32 scores per step
     constexpr int NW = kAttnThreads / 32; // warps per CTA
     constexpr int HD = 128;               // largest head_dim (4 dims per lane)
-    constexpr int D = kWarpStages;
     extern __shared__ __align__(128) unsigned char ring_smem[];  // [NW][D][K rows | V rows]
     __shared__ uint64_t wbar[NW][D];
     __shared__ AttnPlan plan;
@@ -752,10 +751,12 @@ int attn_splits_for(int n_kv, int num_sms) {
 }
 
 cudaError_t attn_prepare(int /*dev*/) {
-    cudaError_t e = cudaFuncSetAttribute(attn_warp_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(attn_warp_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return e;
+    cudaError_t e = cudaSuccess;
+    for (void* k : {(void*)attn_warp_kernel<4, 2>, (void*)attn_warp_kernel<4, 3>, (void*)attn_warp_kernel<8, 2>,
+                    (void*)attn_warp_kernel<8, 3>}) {
+        e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e != cudaSuccess) return e;
+    }
     e = cudaFuncSetAttribute(attn_split_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(attn_split_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -782,8 +783,12 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
     const int G = a.n_heads / a.n_kv;
     void* k = (a.hd % 4 == 0) ? (void*)attn_split_kernel<4> : (void*)attn_split_kernel<1>;
     if (a.hd % 4 == 0 && a.hd <= 128 && (G == 4 || G == 8)) {
-        k = G == 4 ? (void*)attn_warp_kernel<4> : (void*)attn_warp_kernel<8>;
-        cfg.dynamicSmemBytes = (size_t)(kAttnThreads / 32) * kWarpStages * 2 * (32 / G) * a.hd * 4;
+        // one stream: a 2-stage ring keeps the CTA small enough to sit beside a
+        // GEMV CTA; several streams (long, bandwidth-bound scans): 3 stages
+        const int D = B > 1 ? 3 : 2;
+        k = G == 4 ? (D == 2 ? (void*)attn_warp_kernel<4, 2> : (void*)attn_warp_kernel<4, 3>)
+                   : (D == 2 ? (void*)attn_warp_kernel<8, 2> : (void*)attn_warp_kernel<8, 3>);
+        cfg.dynamicSmemBytes = (size_t)(kAttnThreads / 32) * D * 2 * (32 / G) * a.hd * 4;
         int g2 = attn_warp_grid_ctas();
         if (g2 > max_items) g2 = (int)max_items;
         cfg.gridDim = dim3(g2 > 0 ? g2 : 1, 1, 1);
