@@ -143,3 +143,35 @@ def test_model_step_range_errors(V):
         with pytest.raises(V.VoxError) as e:
             ctx.model_step(kv, 0, 1 << 20)
         assert e.value.code == V.ERR_RANGE
+
+
+@pytest.mark.parametrize("step_mode", MODES)
+def test_full_window_rolling_eviction(V, oracle, step_mode):
+    """Rolling-window stress at the full window: the cache holds 8190 of 8192
+    tokens (filled from the generator on both sides), then teacher-forced
+    steps run through the first evictions; logits, argmax and the ring state
+    (len, pos_offset, physical start) are checked after every step."""
+    c, n_layers, vocab, fill, n_steps = FULL, 4, 8192, 8190, 6
+    m = oracle_model(oracle, c, n_layers, vocab, 0)
+    oc = oracle.RollingKvCache(n_layers, c["n_kv_heads"], c["head_dim"], c["sliding_window"])
+    n = fill * c["n_kv_heads"] * c["head_dim"]
+    for l in range(n_layers):
+        k = oracle.bf16_to_f32(oracle.gen_normal_bf16(0, 5000000 + 2 * l, 1.0, n))
+        v = oracle.bf16_to_f32(oracle.gen_normal_bf16(0, 5000000 + 2 * l + 1, 1.0, n))
+        oc.layer_set(l, k, v, fill, 0)
+    ids = oracle.gen_uniform_ids(0, 3000003, vocab, n_steps)
+    with make_ctx(V, c, n_layers, vocab, 0, step_mode=step_mode) as ctx:
+        kv = V.RollingKvCache(ctx, n_layers, c["n_kv_heads"], c["head_dim"], c["sliding_window"])
+        kv.fill_random(fill, 0, 5000000, 1.0)
+        for i in range(n_steps):
+            pos = fill + i
+            tok, logits = ctx.model_step(kv, int(ids[i]), pos, want_logits=True)
+            ref_logits, ref_tok = m.step(oc, int(ids[i]), pos)
+            assert_logits_close(logits, ref_logits, f"step {i}")
+            assert tok == ref_tok, f"step {i}: {tok} != {ref_tok} (margin {top2_margin(ref_logits):.3e})"
+            want_len, want_off = oc.layer_len_tokens(0), oc.layer_pos_offset(0)
+            assert (kv.layer_len_tokens(0), kv.layer_pos_offset(0)) == (want_len, want_off)
+            ln, start, off = kv.device_state(n_layers - 1)
+            # the ring starts at slot 0 and drops `off` tokens in all: start = off mod window
+            assert (ln, off, start) == (want_len, want_off, want_off % c["sliding_window"])
+        assert oc.layer_pos_offset(0) == fill + n_steps - c["sliding_window"] > 0

@@ -32,6 +32,8 @@ def main():
     ap.add_argument("--launches", type=int, default=8)
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--context", type=int, default=512)
+    ap.add_argument("--fill", action="store_true",
+                    help="step: fill the cache from the generator instead of prefilling tokens")
     ap.add_argument("--mode", type=int, default=0, help="0 auto, 1 per-layer kernels, 2 persistent kernel")
     args = ap.parse_args()
     V = importlib.import_module("voxtral-rust_b200")
@@ -43,7 +45,10 @@ def main():
         ctx.init_random(0, 0.02)
         if args.which == "step":
             kv = V.RollingKvCache(ctx, args.layers, 8, 128, 8192)
-            ctx.model_prefill(kv, [i % vocab for i in range(args.context)], 0)
+            if args.fill:
+                kv.fill_random(args.context, 0, 5000000, 1.0)
+            else:
+                ctx.model_prefill(kv, [i % vocab for i in range(args.context)], 0)
             ctx.synchronize()
             ctx.record_event(0)
             ctx.model_generate(kv, 1, args.context, args.steps)
