@@ -407,8 +407,7 @@ __device__ __forceinline__ float dot4(const float4& a, const float4& b) {
     return fmaf(a.w, b.w, d);
 }
 
-// Warp-per-chunk kernel, D-stage per-warp ring.  At most 128 registers, so
-// that one CTA fits on an SM beside a GEMV CTA and launches early.
+// Warp-per-chunk kernel, D-stage per-warp ring; at most 128 registers, three CTAs per SM.
 template <int G, int D>
 __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnArgs A) {
     constexpr int TPG = 32 / G;           // tokens per group: G * TPG = 32 scores per step
@@ -730,7 +729,8 @@ int attn_grid_ctas(int n_heads, int n_kv, int hd) {
     return sms * per_sm;
 }
 
-// Persistent grid of the warp-per-chunk kernel: two 4-warp CTAs per SM.
+// Persistent grid of the warp-per-chunk kernel: three 4-warp CTAs per SM
+// (2-stage rings: 64 KB + 10 KB of shared memory, at most 128 registers).
 int attn_warp_grid_ctas() {
     static int sms = 0;
     if (!sms) {
@@ -738,7 +738,7 @@ int attn_warp_grid_ctas() {
         cudaGetDevice(&dev);
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
     }
-    return 2 * sms;
+    return 3 * sms;
 }
 
 int attn_max_splits() { return kMaxSplits; }
@@ -783,9 +783,8 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
     const int G = a.n_heads / a.n_kv;
     void* k = (a.hd % 4 == 0) ? (void*)attn_split_kernel<4> : (void*)attn_split_kernel<1>;
     if (a.hd % 4 == 0 && a.hd <= 128 && (G == 4 || G == 8)) {
-        // one stream: a 2-stage ring keeps the CTA small enough to sit beside a
-        // GEMV CTA; several streams (long, bandwidth-bound scans): 3 stages
-        const int D = B > 1 ? 3 : 2;
+        // 2-stage rings: three CTAs (12 warps) per SM
+        const int D = 2;
         k = G == 4 ? (D == 2 ? (void*)attn_warp_kernel<4, 2> : (void*)attn_warp_kernel<4, 3>)
                    : (D == 2 ? (void*)attn_warp_kernel<8, 2> : (void*)attn_warp_kernel<8, 3>);
         cfg.dynamicSmemBytes = (size_t)(kAttnThreads / 32) * D * 2 * (32 / G) * a.hd * 4;
