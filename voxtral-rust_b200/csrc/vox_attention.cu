@@ -185,7 +185,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
         for (int z = 0; z < B; ++z)
             if (plan.items[z] == 0) {
                 float* out = A.out + z * A.out_stride;
-                for (int i = tid; i < A.n_heads * hd; i += kAttnThreads) out[i] = 0.f;
+                for (int i = tid; i < A.n_heads * hd; i += kAttnThreads) {
+                    out[i] = 0.f;
+                    if (A.xop) xop_store(A.xop, i, z, 0.f);
+                }
             }
 
     const int total = plan.first[B];
@@ -370,6 +373,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnArgs
                     if (s0 + j < n_active) faxpy(sum, wg[s0 + j], v[j]);
             }
             *reinterpret_cast<T*>(out_h + (size_t)o * VEC) = sum;
+            if (A.xop)
+#pragma unroll
+                for (int i = 0; i < VEC; ++i) xop_store(A.xop, h * G * hd + o * VEC + i, z, fget(sum, i));
         }
         if (tid == 0) tickets[h] = 0u;
     }
@@ -465,7 +471,10 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnAr
         for (int z = 0; z < B; ++z)
             if (plan.items[z] == 0) {
                 float* out = A.out + z * A.out_stride;
-                for (int i = tid; i < A.n_heads * hd; i += kAttnThreads) out[i] = 0.f;
+                for (int i = tid; i < A.n_heads * hd; i += kAttnThreads) {
+                    out[i] = 0.f;
+                    if (A.xop) xop_store(A.xop, i, z, 0.f);
+                }
             }
 
     const bool dim_ok = lane * 4 < hd;
@@ -691,6 +700,13 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnAr
                 }
             }
             *reinterpret_cast<float4*>(out + (size_t)g * hd + d) = sum;
+            if (A.xop) {
+                const int k0 = (h * G + g) * hd + d;
+                xop_store(A.xop, k0, z, sum.x);
+                xop_store(A.xop, k0 + 1, z, sum.y);
+                xop_store(A.xop, k0 + 2, z, sum.z);
+                xop_store(A.xop, k0 + 3, z, sum.w);
+            }
         }
         if (tid == 0) tickets[h] = 0u;
     }

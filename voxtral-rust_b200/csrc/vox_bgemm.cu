@@ -195,7 +195,9 @@ __device__ __forceinline__ void bg_epilogue(const BgArgs& A, int tile, int row, 
             for (int b = 0; b < 8; ++b) {
                 if (b >= A.B) continue;
                 const float sg = __fdiv_rn(y[b], __fadd_rn(1.0f, expf(-y[b])));
-                A.y[(size_t)b * A.y_stride + j] = __fmul_rn(sg, up[b]);
+                const float act = __fmul_rn(sg, up[b]);
+                A.y[(size_t)b * A.y_stride + j] = act;
+                if (A.xop_out) xop_store(A.xop_out, j, b, act);
             }
         }
     } else if (A.epi == BG_RESID) {
@@ -209,6 +211,7 @@ __device__ __forceinline__ void bg_epilogue(const BgArgs& A, int tile, int row, 
                 const float v = __fadd_rn(__ldcg(A.resid + (size_t)b * A.y_stride + r), y[b]);
                 A.y[(size_t)b * A.y_stride + r] = v;
                 sq[b] = __fmul_rn(v, v);
+                if (A.xop_out) xop_store(A.xop_out, r, b, A.xop_gain ? __fmul_rn(v, A.xop_gain[r]) : v);
             }
         }
         if (A.ssp_out) {
@@ -323,7 +326,8 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
     uint64_t* empty = full + kStages;
     uint64_t* acc_full = empty + kStages;  // [2]
     uint64_t* acc_empty = acc_full + 2;    // [2]
-    uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    uint64_t* xbar = acc_empty + 2;        // X operand bulk copy
+    uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(xbar + 2);
     EpiShared* es = reinterpret_cast<EpiShared*>(tmem_base_s + 4);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -338,6 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
         }
+        mbar_init(xbar, 1);
         fence_barrier_init();
     }
     if (warp == 1) {  // TMEM accumulators: the whole warp allocates
@@ -352,6 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
     tmem_fence_after();
     const uint32_t tmem = *tmem_base_s;
     pdl_allow_dependents();
+    uint32_t xphase = 0;  // parity of the next X-operand copy (MMA lane only)
 
     // ---- producer: stream this CTA's weight blocks of every phase ----
     if (warp == 0) {
@@ -415,7 +421,8 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
         }
         // Per-stream RMSNorm factor from the producer's partial sums of squares
         // (math.rs:22: inv = 1 / sqrt(sum / dim + eps)), applied in the X prologue.
-        if (A.norm_w) {
+        const bool xop = A.xop != nullptr;
+        if (A.norm_w && !xop) {
             // all partials loaded at once (one L2 round trip), summed in part order
             const int n = A.ssp_parts * 8;
             for (int e = tid - 32; e < n && e < kMaxSspParts * 8; e += kWorkers) es->ssp[e] = __ldcg(A.ssp + e);
@@ -431,6 +438,23 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
                 es->inv[b] = inv;
             }
             named_barrier_sync(1, kWorkers);
+        } else if (A.norm_w && warp >= 4) {
+            // X operand already holds x * g: the epilogue warpgroup scales the
+            // row sums by inv (y = inv * W (x * g)) while the MMAs run
+            const int n = A.ssp_parts * 8;
+            for (int e = tid - 128; e < n && e < kMaxSspParts * 8; e += 128) es->ssp[e] = __ldcg(A.ssp + e);
+            named_barrier_sync(2, 128);
+            if (tid >= 128 && tid < 136) {
+                const int b = tid - 128;
+                float inv = 1.0f;
+                if (b < A.B) {
+                    float ss = 0.0f;
+                    for (int p = 0; p < A.ssp_parts; ++p) ss += es->ssp[p * 8 + b];
+                    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)A.K), A.eps)));
+                }
+                es->inv[b] = inv;
+            }
+            named_barrier_sync(2, 128);
         }
 
         const int n_items = A.tiles * A.splits;
@@ -438,8 +462,9 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
         for (int i = blockIdx.x; i < n_items; i += gridDim.x, ++local) {
             const Item it = item_of(A, i);
             const int nkb = it.kb1 - it.kb0;
-            // ---- X slab for this split, built by warps 1..7 ----
-            if (it.ks != cur_ks) {
+            // ---- X slab for this split: built by warps 1..7, or copied (XOP) ----
+            const bool new_x = it.ks != cur_ks;
+            if (new_x && !xop) {
                 if (local > 0) {  // the previous item's MMAs read the old slab: wait for their commit
                     const int pb = (local - 1) & 1;
                     if (!mbar_wait(&acc_full[pb], ((local - 1) >> 1) & 1)) raise_error(err, ERR_FULL_WAIT);
@@ -501,12 +526,25 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
                 // generic-proxy writes must be visible to the tensor core (async proxy)
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 named_barrier_sync(1, kWorkers);
-                cur_ks = it.ks;
             }
+            cur_ks = it.ks;
 
             const int ab = local & 1;  // accumulator buffer
             // ---- MMA issuer ----
             if (warp == 1 && lane == 0) {
+                if (xop && new_x) {
+                    // the previous item's MMAs read the old slab: wait for their commit
+                    if (local > 0 && !mbar_wait(&acc_full[(local - 1) & 1], ((local - 1) >> 1) & 1))
+                        raise_error(err, ERR_FULL_WAIT);
+                    const uint32_t xb = (uint32_t)(nkb * 2048);
+                    mbar_arrive_expect_tx(xbar, xb);
+                    bulk_copy_g2s_nohint(xs, A.xop + (size_t)it.kb0 * 2048, xb, xbar);
+                    if (!mbar_wait(xbar, xphase)) {
+                        raise_error(err, ERR_FULL_WAIT);
+                        mma_ok = false;
+                    }
+                    xphase ^= 1u;
+                }
                 if (mma_ok && local >= 2 && !mbar_wait(&acc_empty[ab], ((local - 2) >> 1) & 1)) {
                     raise_error(err, ERR_FULL_WAIT);
                     mma_ok = false;
@@ -591,7 +629,12 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
                         if (ew == 0 && lane == 0) A.tickets[it.tile] = 0u;
                     }
                 }
-                if (final_item) bg_epilogue(A, it.tile, row, lane, ew, y, es);
+                if (final_item) {
+                    if (xop && A.norm_w)
+#pragma unroll
+                        for (int b = 0; b < 8; ++b) y[b] = __fmul_rn(es->inv[b], y[b]);
+                    bg_epilogue(A, it.tile, row, lane, ew, y, es);
+                }
             }
         }
     }
@@ -630,7 +673,8 @@ __global__ void tile_weights_kernel(const uint16_t* __restrict__ src, uint16_t* 
 // of the previous step has finished when this kernel runs.
 __global__ void __launch_bounds__(128) bg_embed_kernel(const uint16_t* __restrict__ embed, int vocab, int dim,
                                                        const StepState* steps, float* hid, float* ssp,
-                                                       unsigned* zero, int n_zero, unsigned* err) {
+                                                       unsigned char* xop, const float* xop_gain, unsigned* zero,
+                                                       int n_zero, unsigned* err) {
     pdl_allow_dependents();
     pdl_wait_prior_grids();
     if (blockIdx.x == 0 && blockIdx.y == 0)
@@ -646,6 +690,7 @@ __global__ void __launch_bounds__(128) bg_embed_kernel(const uint16_t* __restric
     if (e < dim) {
         v = bf16_bits_to_f32(embed[(size_t)tok * dim + e]);
         hid[(size_t)b * dim + e] = v;
+        if (xop) xop_store(xop, e, b, xop_gain ? __fmul_rn(v, xop_gain[e]) : v);
     }
     float sq = __fmul_rn(v, v);
 #pragma unroll
@@ -706,7 +751,8 @@ __global__ void __launch_bounds__(256) bg_argmax_final_kernel(const ArgmaxPart* 
 }  // namespace
 
 cudaError_t launch_bg_embed(const uint16_t* embed, int vocab, int dim, const StepState* steps, int B, float* hid,
-                            float* ssp, unsigned* zero, int n_zero, unsigned* err, cudaStream_t s, bool pdl) {
+                            float* ssp, unsigned char* xop, const float* xop_gain, unsigned* zero, int n_zero,
+                            unsigned* err, cudaStream_t s, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((dim + 127) / 128, B, 1);
     cfg.blockDim = dim3(128, 1, 1);
@@ -716,7 +762,8 @@ cudaError_t launch_bg_embed(const uint16_t* embed, int vocab, int dim, const Ste
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, bg_embed_kernel, embed, vocab, dim, steps, hid, ssp, zero, n_zero, err);
+    return cudaLaunchKernelEx(&cfg, bg_embed_kernel, embed, vocab, dim, steps, hid, ssp, xop, xop_gain, zero, n_zero,
+                              err);
 }
 
 cudaError_t launch_bg_argmax_final(const ArgmaxPart* parts, int n_tiles, StepState* steps, int B,
@@ -739,7 +786,7 @@ int bgemm_xslab_bytes(int K, int splits) {
 }
 
 size_t bgemm_smem_bytes(int xslab_bytes) {
-    return (size_t)kStages * kStageBytes + xslab_bytes + (2 * kStages + 4) * 8 + 16 + sizeof(EpiShared);
+    return (size_t)kStages * kStageBytes + xslab_bytes + (2 * kStages + 6) * 8 + 16 + sizeof(EpiShared);
 }
 
 cudaError_t bgemm_prepare(int /*dev*/) {

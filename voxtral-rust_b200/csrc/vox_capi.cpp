@@ -88,6 +88,9 @@ struct BatchBufs {
     BgPlan c_qkv, c_o, c_w13, c_w2, c_head;         // phases of the per-layer chains
     unsigned* done = nullptr;  // chain completion counters [n_layers + 1][kBgMaxPhases]
     int n_done = 0;
+    // X operands in XOP layout, written by the producing kernel: hid * attn_norm
+    // (q|k|v, LM head), attention output (o-proj), hmid * ffn_norm (w1|w3), act (w2)
+    unsigned char *xop_a = nullptr, *xop_o = nullptr, *xop_f = nullptr, *xop_h = nullptr;
 };
 
 // K splits and grid of a multi-stream GEMM launched on its own: one CTA per
@@ -593,6 +596,13 @@ int ensure_batch(vox_ctx* c) {
         CUDA_TRY(cudaMemset(b.attn, 0, 8 * (size_t)qd * 4));
         CUDA_TRY(cudaMemset(b.act, 0, 8 * (size_t)hid * 4));
         CUDA_TRY(cudaMemset(b.ssp, 0, 8 * (size_t)((dim + 127) / 128) * 4));
+        CUDA_TRY(dalloc(&b.xop_a, xop_bytes(dim)));
+        CUDA_TRY(dalloc(&b.xop_o, xop_bytes(qd)));
+        CUDA_TRY(dalloc(&b.xop_f, xop_bytes(dim)));
+        CUDA_TRY(dalloc(&b.xop_h, xop_bytes(hid)));
+        for (unsigned char* x : {b.xop_a, b.xop_f}) CUDA_TRY(cudaMemset(x, 0, xop_bytes(dim)));
+        CUDA_TRY(cudaMemset(b.xop_o, 0, xop_bytes(qd)));
+        CUDA_TRY(cudaMemset(b.xop_h, 0, xop_bytes(hid)));
         CUDA_TRY(dalloc(&b.steps, 8));
         CUDA_TRY(cudaMemset(b.steps, 0, 8 * sizeof(StepState)));
         CUDA_TRY(dalloc(&b.tok_out, 8));
@@ -648,7 +658,8 @@ int enqueue_batch_step(vox_ctx* c, vox_kv* kv, bool pdl) {
     const int nkv = (int)c->cfg.n_kv_heads, hd = (int)c->cfg.head_dim, G = (int)(c->cfg.n_heads / nkv);
     const int nsplit = attn_max_splits();  // chunks per (stream, kv head) at most
     CUDA_TRY(record_launch(c, launch_bg_embed(c->embed, (int)c->opt.vocab, dim, bb.steps, B, bb.hid, bb.ssp,
-                                              bb.done, bb.n_done, c->err, c->stream, pdl)));
+                                              bb.xop_a, c->layers[0].attn_norm, bb.done, bb.n_done, c->err,
+                                              c->stream, pdl)));
     const int L = (int)c->layers.size();
     // VOX_STEP_PERSISTENT: o-proj, w1|w3, w2 and the next q|k|v (or the LM
     // head) run as one persistent chain launch; otherwise (and by default,
@@ -673,8 +684,7 @@ int enqueue_batch_step(vox_ctx* c, vox_kv* kv, bool pdl) {
     auto qkv_args = [&](int l) {
         const LayerDev& Ld = c->layers[l];
         BgArgs a = bg_args(c, P_qkv, Ld.wqkv_t, B, BG_QKV);
-        a.x = bb.hid;
-        a.x_stride = dim;
+        a.xop = bb.xop_a;  // hid * attn_norm, written by the embedding or the previous w2
         a.norm_w = Ld.attn_norm;
         a.ssp = bb.ssp;
         a.y = bb.q;
@@ -732,6 +742,7 @@ int enqueue_batch_step(vox_ctx* c, vox_kv* kv, bool pdl) {
         at.out_stride = qd;
         at.part_stride = (long long)nkv * nsplit * G * (hd + 2);
         at.st_stride = (long long)kv->n_layers;
+        at.xop = bb.xop_o;
         CUDA_TRY(record_launch(c, launch_attention(at, c->stream, pdl)));
 
         // chain l + 1: o-proj + residual (commits the append), w1|w3 + SwiGLU,
@@ -740,12 +751,13 @@ int enqueue_batch_step(vox_ctx* c, vox_kv* kv, bool pdl) {
         ch.n_phases = 4;
         ch.done = bb.done + (size_t)(l + 1) * kBgMaxPhases;
         BgArgs a = bg_args(c, P_o, Ld.wo_t, B, BG_RESID);
-        a.x = bb.attn;
-        a.x_stride = qd;
+        a.xop = bb.xop_o;
         a.y = bb.hmid;
         a.y_stride = dim;
         a.resid = bb.hid;
         a.ssp_out = bb.ssp;
+        a.xop_out = bb.xop_f;
+        a.xop_gain = Ld.ffn_norm;
         a.kv_commit = st;
         a.kv_state_stride = (long long)kv->n_layers;
         a.kv_window = win;
@@ -753,29 +765,29 @@ int enqueue_batch_step(vox_ctx* c, vox_kv* kv, bool pdl) {
         ch.ph[0] = a;
 
         a = bg_args(c, P_w13, Ld.w13_t, B, BG_SWIGLU);
-        a.x = bb.hmid;
-        a.x_stride = dim;
+        a.xop = bb.xop_f;
         a.norm_w = Ld.ffn_norm;
         a.ssp = bb.ssp;
         a.y = bb.act;
         a.y_stride = hid;
+        a.xop_out = bb.xop_h;
         ch.ph[1] = a;
 
         a = bg_args(c, P_w2, Ld.w2_t, B, BG_RESID);
-        a.x = bb.act;
-        a.x_stride = hid;
+        a.xop = bb.xop_h;
         a.y = bb.hid;
         a.y_stride = dim;
         a.resid = bb.hmid;
         a.ssp_out = bb.ssp;
+        a.xop_out = bb.xop_a;  // the next q|k|v's (or the LM head's) operand
+        a.xop_gain = l + 1 < L ? c->layers[l + 1].attn_norm : c->final_norm;
         ch.ph[2] = a;
 
         if (l + 1 < L) {
             ch.ph[3] = qkv_args(l + 1);
         } else {
             a = bg_args(c, P_head, c->head_t, B, BG_ARGMAX);
-            a.x = bb.hid;
-            a.x_stride = dim;
+            a.xop = bb.xop_a;
             a.norm_w = c->final_norm;
             a.ssp = bb.ssp;
             a.y = bb.logits;
@@ -1018,7 +1030,7 @@ void vox_ctx_destroy(vox_ctx* c) {
     {
         BatchBufs& b = c->bb;
         void* bp[] = {c->head_t, b.hid, b.hmid, b.q, b.attn, b.act, b.logits, b.ssp, b.part, b.attn_part, b.am,
-                      b.tickets, b.attn_tickets, b.steps, b.tok_out, b.done};
+                      b.tickets, b.attn_tickets, b.steps, b.tok_out, b.done, b.xop_a, b.xop_o, b.xop_f, b.xop_h};
         for (void* p : bp)
             if (p) cudaFree(p);
         if (b.h_steps) cudaFreeHost(b.h_steps);

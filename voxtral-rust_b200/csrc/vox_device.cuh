@@ -140,6 +140,23 @@ __device__ __forceinline__ bool wait_counter_sys(const unsigned long long* c, un
     }
 }
 
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {  // round to nearest even
+    const uint32_t u = __float_as_uint(f);
+    return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+
+// Element k of stream b into an X operand in XOP layout (vox_kernels.h):
+// v as bf16 hi = bf16(v) and lo = bf16(v - hi).
+__device__ __forceinline__ void xop_store(unsigned char* xop, int k, int b, float v) {
+    const uint16_t h = f32_to_bf16_bits(v);
+    const uint16_t l = f32_to_bf16_bits(v - bf16_bits_to_f32(h));
+    const int kk = k & 63;
+    uint16_t* base = reinterpret_cast<uint16_t*>(xop + (size_t)(k >> 6) * 2048 + (kk >> 4) * 512 +
+                                                 ((kk >> 3) & 1) * 256) + (kk & 7);
+    base[b * 8] = h;       // rows 0..7: hi
+    base[64 + b * 8] = l;  // rows 8..15 (128 bytes on): lo
+}
+
 // State of a cache layer after appending one token (kv.rs:48-88 with n = 1).
 __device__ __forceinline__ KvState kv_after_single_append(KvState s, int window, int cap) {
     int requested = s.len + 1;

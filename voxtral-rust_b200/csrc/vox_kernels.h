@@ -145,7 +145,18 @@ struct AttnArgs {
     // tickets + z * n_kv.
     int n_streams;
     long long q_stride, ring_stride, out_stride, part_stride, st_stride;
+    // non-null: the output also goes to this X operand of the next GEMM
+    // (XOP layout, stream z in row z; see XOP_BYTES below)
+    unsigned char* xop;
 };
+
+// X operand of the multi-stream GEMM in global memory ("XOP" layout): for a
+// vector set of width K (8 streams), K / 64 blocks of 2 KB, each the bf16
+// hi/lo image the tensor core reads from shared memory: element k of stream b
+// at block k / 64, K-step (k % 64) / 16, half (k / 8) % 2, then hi in rows
+// 0..7 and lo in rows 8..15 (row b), element k % 8.  A producer kernel writes
+// its outputs there directly, so the GEMM loads its slice with one bulk copy.
+inline size_t xop_bytes(int K) { return (size_t)(K / 64) * 2048; }
 
 // Record a failure for vox_last_error() and return `code` (host side).
 int report_error(int code, const char* msg);
@@ -209,7 +220,8 @@ struct BgArgs {
     int splits;                 // K splits per tile
     int B;                      // active streams (<= 8)
     int xslab_bytes;            // shared bytes of one split's X operand
-    const float* x;             // [B, x_stride] f32 inputs
+    const float* x;             // [B, x_stride] f32 inputs (X operand built in the kernel), or
+    const unsigned char* xop;   // the X operand already in XOP layout (one bulk copy per split)
     long long x_stride;
     const float* norm_w;        // non-null: apply RMSNorm with this gain to x
     const float* ssp;           // RMSNorm partial sums of squares [ssp_parts, 8] of x
@@ -221,6 +233,8 @@ struct BgArgs {
     const float* bias;
     const float* resid;
     float* ssp_out;             // BG_RESID: per-tile sums of squares of y [tiles, 8]
+    unsigned char* xop_out;     // BG_RESID / BG_SWIGLU: also write y (times xop_gain) in XOP layout
+    const float* xop_gain;      // per-element gain for xop_out (the next RMSNorm's); null = 1
     int q_dim, kv_dim, head_dim;
     const float* rope_cos;
     const float* rope_sin;
@@ -259,7 +273,8 @@ cudaError_t bgemm_prepare(int dev);
 cudaError_t launch_bgemm(const BgChain& c, int grid, cudaStream_t s, bool pdl);
 size_t tiled_bytes(int rows, int K);
 cudaError_t launch_bg_embed(const uint16_t* embed, int vocab, int dim, const StepState* steps, int B, float* hid,
-                            float* ssp, unsigned* zero, int n_zero, unsigned* err, cudaStream_t s, bool pdl);
+                            float* ssp, unsigned char* xop, const float* xop_gain, unsigned* zero, int n_zero,
+                            unsigned* err, cudaStream_t s, bool pdl);
 cudaError_t launch_bg_argmax_final(const ArgmaxPart* parts, int n_tiles, StepState* steps, int B,
                                    int32_t* tok_out, cudaStream_t s, bool pdl);
 cudaError_t launch_tile_weights(const uint16_t* src, uint16_t* dst, int rows, int K, cudaStream_t s);
