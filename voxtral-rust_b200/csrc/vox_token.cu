@@ -38,8 +38,6 @@ constexpr int kThreads = (kNW + 1) * 32;       // + producer warp
 constexpr int kConsumers = kNW * 32;
 constexpr uint32_t kSlotBytes = 48 * 1024;
 constexpr int kSlots = 3;
-constexpr int kAttnThreads = 128;
-constexpr int kTile = 32;
 constexpr int kMaxSplits = 64;
 constexpr int kMaxCpt = 3;  // x slice of at most 3 x 8 floats per lane
 constexpr unsigned kAbortMask = ERR_FULL_WAIT | ERR_EMPTY_WAIT | ERR_DRAIN_WAIT | ERR_GRID_WAIT;
@@ -55,8 +53,7 @@ __host__ __device__ inline int band_max_rows(const TokGemv& g, int grid) {
 
 __host__ __device__ inline Layout token_layout(const TokenArgs& a, int grid) {
     const int G = a.n_heads / a.n_kv;
-    const size_t attn_f = (size_t)G * a.hd + 4 * kTile * (a.hd + 4) + (size_t)G * kTile + 3 * G +
-                          (size_t)G * kMaxSplits + 8;
+    const size_t attn_f = (size_t)kNW * G * a.hd + (size_t)kNW * G * 2 + (size_t)G * kMaxSplits + 8;
     size_t red_f = 0;
     const TokGemv* gs[5] = {&a.g_qkv, &a.g_o, &a.g_w13, &a.g_w2, &a.g_head};
     for (int i = 0; i < 5; ++i) {
@@ -244,16 +241,6 @@ __device__ __noinline__ void producer(const TokenArgs& A, unsigned char* ring, u
         if (!mbar_wait(&full[st % kSlots], (st / kSlots) & 1)) raise_error(A.err, ERR_DRAIN_WAIT);
 }
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
-    const int n = valid ? 16 : 0;
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(n)
-                 : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
 // ---------------------------------------------------------------------------
 // Consumers: one GEMV phase (same math and epilogues as gemv_kernel).
 // ---------------------------------------------------------------------------
@@ -500,178 +487,196 @@ __device__ void gemv_dispatch(const TokenArgs& A, const TokGemv& P, const PhaseI
 // ---------------------------------------------------------------------------
 // Consumers: attention phase (ops.rs:66-132), threads 0..127.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void attn_sync() { named_barrier_sync(2, kAttnThreads); }
+__device__ __forceinline__ void attn_sync() { named_barrier_sync(2, kConsumers); }
 
-__device__ __forceinline__ void tile_load(float* ks, float* vs, const float* kr, const float* vr, int t0,
-                                          int t_end, int start, int cap, int hd, int ldk) {
-    const int hdv = hd / 4;
-    for (int u = threadIdx.x; u < kTile * hdv; u += kAttnThreads) {
-        const int tt = u / hdv, dv = u - tt * hdv;
-        const int t = t0 + tt;
-        const bool valid = t < t_end;
-        int slot = start + (valid ? t : t0);
-        if (slot >= cap) slot -= cap;
-        cp_async16(ks + tt * ldk + dv * 4, kr + (size_t)slot * hd + dv * 4, valid);
-        cp_async16(vs + tt * ldk + dv * 4, vr + (size_t)slot * hd + dv * 4, valid);
+// Sum of 32 per-lane partial values across the warp, leaving lane l with the
+// total of value l (31 shuffles; lane bit o picks the half it keeps).
+__device__ __forceinline__ void tok_transpose_reduce(float (&v)[32], int lane) {
+#pragma unroll
+    for (int o = 16, n = 32; o >= 1; o >>= 1, n >>= 1) {
+        const bool up = lane & o;
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) {
+            const float keep = up ? v[i + n / 2] : v[i];
+            const float send = up ? v[i] : v[i + n / 2];
+            v[i] = keep + __shfl_xor_sync(0xFFFFFFFFu, send, o);
+        }
     }
-    cp_async_commit();
 }
 
-__device__ __noinline__ void attn_phase(const TokenArgs& A, const TokLayer& L, float* work) {
+// Attention phase, all 16 consumer warps.  Each warp takes 32/G-token groups
+// of one kv head (lane l holds dims 4l..4l+3 of q for the G heads); K and V
+// rows come from L2 into registers (this launch's QKV phase wrote the new
+// token), so the weight ring stays with the producer.  Scores by a
+// transpose-reduce (lane l ends with head l/(32/G), token l%(32/G)), online
+// softmax per warp, PV on the lane's four dims.  The 16 warps of a CTA
+// combine in shared memory into one chunk partial; the last chunk of a kv
+// head (atomic ticket) merges the chunks in a fixed order.
+template <int G>
+__device__ __forceinline__ void attn_phase_warp(const TokenArgs& A, const TokLayer& L, float* work) {
+    constexpr int TPG = 32 / G;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int hd = A.hd, G = A.n_heads / A.n_kv, hdv = hd / 4, ldk = hd + 4, tile_f = kTile * ldk;
-    float* q_s = work;
-    float* kbuf = q_s + G * hd;
-    float* vbuf = kbuf + 2 * tile_f;
-    float* p_s = vbuf + 2 * tile_f;
-    float* m_s = p_s + G * kTile;
-    float* l_s = m_s + G;
-    float* a_s = l_s + G;
-    float* w_s = a_s + G;
+    const int hd = A.hd, hd4 = hd / 4;
+    const unsigned FULL = 0xFFFFFFFFu;
+    float* wacc = work;                              // [kNW][G][hd]
+    float* wml = wacc + (size_t)kNW * G * hd;        // [kNW][G][2]
+    float* w_s = wml + kNW * G * 2;                  // [G][kMaxSplits]
     int* flag_s = reinterpret_cast<int*>(w_s + G * kMaxSplits);
 
     const KvState st = kv_after_single_append(load_state(L.st), A.kv_window, A.cap);
     const int len = st.len;
     const int mask_start = (A.cfg_window > 0 && len > A.cfg_window) ? len - A.cfg_window : 0;
     const int n_live = len - mask_start;
-    const int S = A.splits;
-    int per = (n_live + S - 1) / S;
-    per = ((per + kTile - 1) / kTile) * kTile;
-    if (per < kTile) per = kTile;
-    const int n_active = (n_live + per - 1) / per;
+    const int groups = (n_live + TPG - 1) / TPG;
+    // groups per warp so that every warp of the grid has about one batch, and
+    // at most kMaxSplits chunks (of kNW x gpw groups) per kv head
+    const long long W = (long long)gridDim.x * kNW;
+    int gpw = (int)max(1LL, ((long long)A.n_kv * groups + W - 1) / W);
+    while ((groups + kNW * gpw - 1) / (kNW * gpw) > kMaxSplits) ++gpw;
+    const int cgroups = kNW * gpw;                   // groups per chunk
+    const int n_chunks = (groups + cgroups - 1) / cgroups;
+    const bool dim_ok = lane * 4 < hd;
+    const int my_g = lane / TPG, my_t = lane % TPG;
+    const size_t acc_stride = (size_t)G * hd;
+    const size_t ml_base = (size_t)A.n_kv * A.splits * acc_stride;
 
-    for (int item = blockIdx.x; item < A.n_kv * S; item += gridDim.x) {
-        const int h = item / S, split = item - h * S;
-        if (split >= n_active) continue;
-        const int t_begin = mask_start + split * per;
-        const int t_end = min(len, t_begin + per);
-        const float* kr = L.k_ring + (size_t)h * A.cap * hd;
-        const float* vr = L.v_ring + (size_t)h * A.cap * hd;
-        attn_sync();  // smem of the previous item is free
-        tile_load(kbuf, vbuf, kr, vr, t_begin, t_end, st.start, A.cap, hd, ldk);
-        for (int i = tid; i < G * hd; i += kAttnThreads) q_s[i] = __ldcg(A.q + (size_t)h * G * hd + i);
-        if (tid < G) {
-            m_s[tid] = -INFINITY;
-            l_s[tid] = 0.f;
+    if (n_chunks == 0) {  // empty cache: the reference returns zeros
+        if (blockIdx.x == 0)
+            for (int i = tid; i < A.n_heads * hd; i += kConsumers) A.attn[i] = 0.f;
+        return;
+    }
+    for (int item = blockIdx.x; item < A.n_kv * n_chunks; item += gridDim.x) {
+        const int h = item / n_chunks, chunk = item - h * n_chunks;
+        const float* kr = L.k_ring + (size_t)h * A.cap * hd + lane * 4;
+        const float* vr = L.v_ring + (size_t)h * A.cap * hd + lane * 4;
+        const float* qh = A.q + (size_t)h * G * hd + lane * 4;
+        float4 q[G], acc[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            q[g] = dim_ok ? __ldcg(reinterpret_cast<const float4*>(qh + (size_t)g * hd)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        float4 acc[4];
+        float m_run = -INFINITY, l_run = 0.f;  // of head my_g
+        for (int i = 0; i < gpw; ++i) {
+            const int grp = chunk * cgroups + warp + kNW * i;
+            if (grp >= groups) break;
+            const int t0 = mask_start + grp * TPG;
+            int slot0 = st.start + t0;
+            if (slot0 >= A.cap) slot0 -= A.cap;
+            float4 kk[TPG];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-        const int n_out = G * hdv;
-        int buf = 0;
-        for (int t0 = t_begin; t0 < t_end; t0 += kTile, buf ^= 1) {
-            const bool has_next = t0 + kTile < t_end;
-            if (has_next) {
-                tile_load(kbuf + (buf ^ 1) * tile_f, vbuf + (buf ^ 1) * tile_f, kr, vr, t0 + kTile, t_end,
-                          st.start, A.cap, hd, ldk);
-                cp_async_wait<1>();
-            } else {
-                cp_async_wait<0>();
+            for (int j = 0; j < TPG; ++j) {
+                int slot = slot0 + j;
+                if (slot >= A.cap) slot -= A.cap;
+                kk[j] = (dim_ok && t0 + j < len) ? __ldcg(reinterpret_cast<const float4*>(kr + (size_t)slot * hd))
+                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            attn_sync();
-            const float* k_s = kbuf + buf * tile_f;
-            const float* v_s = vbuf + buf * tile_f;
-            for (int idx = tid; idx < G * kTile; idx += kAttnThreads) {
-                const int g = idx / kTile, tt = idx - g * kTile;
-                float sc = -INFINITY;
-                if (t0 + tt < t_end) {
-                    float d = 0.f;
-                    const float4* qv = reinterpret_cast<const float4*>(q_s + g * hd);
-                    const float4* kv = reinterpret_cast<const float4*>(k_s + tt * ldk);
-                    for (int dv = 0; dv < hdv; ++dv) {
-                        const float4 a = qv[dv], b = kv[dv];
-                        d = fmaf(a.x, b.x, d);
-                        d = fmaf(a.y, b.y, d);
-                        d = fmaf(a.z, b.z, d);
-                        d = fmaf(a.w, b.w, d);
-                    }
-                    sc = d * A.scale;  // ops.rs:108-113
+            float sc[32];  // ops.rs:108-113: q . k * scale
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+#pragma unroll
+                for (int j = 0; j < TPG; ++j) {
+                    float d = q[g].x * kk[j].x;
+                    d = fmaf(q[g].y, kk[j].y, d);
+                    d = fmaf(q[g].z, kk[j].z, d);
+                    sc[g * TPG + j] = fmaf(q[g].w, kk[j].w, d);
                 }
-                p_s[idx] = sc;
+            tok_transpose_reduce(sc, lane);
+            float4 vv[TPG];
+#pragma unroll
+            for (int j = 0; j < TPG; ++j) {
+                int slot = slot0 + j;
+                if (slot >= A.cap) slot -= A.cap;
+                vv[j] = (dim_ok && t0 + j < len) ? __ldcg(reinterpret_cast<const float4*>(vr + (size_t)slot * hd))
+                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            attn_sync();
-            for (int g = warp; g < G; g += kAttnThreads / 32) {
-                const float sc = p_s[g * kTile + lane];
-                float mt = sc;
+            float sv = sc[0] * A.scale;
+            if (t0 + my_t >= len) sv = -INFINITY;
+            float gm = sv;  // online softmax (math.rs:67-88 restated incrementally)
 #pragma unroll
-                for (int o = 16; o; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xFFFFFFFFu, mt, o));
-                const float m_old = m_s[g];
-                const float m_new = fmaxf(m_old, mt);
-                const float p = (sc == -INFINITY) ? 0.f : expf(sc - m_new);
-                float ps = p;
+            for (int o = TPG / 2; o >= 1; o >>= 1) gm = fmaxf(gm, __shfl_xor_sync(FULL, gm, o));
+            const float m_new = fmaxf(m_run, gm);
+            const float p = (sv == -INFINITY) ? 0.f : expf(sv - m_new);
+            float ps = p;
 #pragma unroll
-                for (int o = 16; o; o >>= 1) ps += __shfl_xor_sync(0xFFFFFFFFu, ps, o);
-                p_s[g * kTile + lane] = p;
-                if (lane == 0) {
-                    const float alpha = (m_old == -INFINITY) ? 0.f : expf(m_old - m_new);
-                    a_s[g] = alpha;
-                    l_s[g] = l_s[g] * alpha + ps;
-                    m_s[g] = m_new;
-                }
-            }
-            attn_sync();
+            for (int o = TPG / 2; o >= 1; o >>= 1) ps += __shfl_xor_sync(FULL, ps, o);
+            const float alpha = (m_run == -INFINITY) ? 0.f : expf(m_run - m_new);
+            l_run = l_run * alpha + ps;
+            m_run = m_new;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int o = tid + j * kAttnThreads;
-                if (o < n_out) {
-                    const int g = o / hdv, dv = o - g * hdv;
-                    const float al = a_s[g];
-                    acc[j].x *= al;
-                    acc[j].y *= al;
-                    acc[j].z *= al;
-                    acc[j].w *= al;
-                    const float* pg = p_s + g * kTile;
-#pragma unroll 8
-                    for (int tt = 0; tt < kTile; ++tt) {
-                        const float p = pg[tt];
-                        const float4 v = *reinterpret_cast<const float4*>(v_s + tt * ldk + dv * 4);
-                        acc[j].x = fmaf(p, v.x, acc[j].x);
-                        acc[j].y = fmaf(p, v.y, acc[j].y);
-                        acc[j].z = fmaf(p, v.z, acc[j].z);
-                        acc[j].w = fmaf(p, v.w, acc[j].w);
-                    }
+            for (int g = 0; g < G; ++g) {  // PV (ops.rs:117-128)
+                const float a = __shfl_sync(FULL, alpha, g * TPG);
+                acc[g].x *= a;
+                acc[g].y *= a;
+                acc[g].z *= a;
+                acc[g].w *= a;
+#pragma unroll
+                for (int j = 0; j < TPG; ++j) {
+                    const float pj = __shfl_sync(FULL, p, g * TPG + j);
+                    acc[g].x = fmaf(pj, vv[j].x, acc[g].x);
+                    acc[g].y = fmaf(pj, vv[j].y, acc[g].y);
+                    acc[g].z = fmaf(pj, vv[j].z, acc[g].z);
+                    acc[g].w = fmaf(pj, vv[j].w, acc[g].w);
                 }
             }
-            attn_sync();
         }
-        // accumulators [n_kv, S, G, hd], then (m, l) pairs [n_kv, S, G, 2]
-        const size_t acc_stride = (size_t)G * hd;
-        const size_t ml_base = (size_t)A.n_kv * S * acc_stride;
-        float4* pacc = reinterpret_cast<float4*>(A.attn_part + ((size_t)h * S + split) * acc_stride);
-        float* pml = A.attn_part + ml_base + ((size_t)h * S + split) * G * 2;
+        // combine the CTA's warps into one chunk partial
+        attn_sync();  // the previous item's readers of the shared partials are done
+        if (dim_ok)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int o = tid + j * kAttnThreads;
-            if (o < n_out) pacc[o] = acc[j];
+            for (int g = 0; g < G; ++g) *reinterpret_cast<float4*>(wacc + ((size_t)warp * G + g) * hd + lane * 4) = acc[g];
+        if (my_t == 0) {
+            wml[(warp * G + my_g) * 2] = m_run;
+            wml[(warp * G + my_g) * 2 + 1] = l_run;
         }
-        if (tid < G) {
-            pml[tid * 2] = m_s[tid];
-            pml[tid * 2 + 1] = l_s[tid];
+        attn_sync();
+        float* pacc = A.attn_part + ((size_t)h * A.splits + chunk) * acc_stride;
+        float* pml = A.attn_part + ml_base + ((size_t)h * A.splits + chunk) * G * 2;
+        for (int o = tid; o < G * hd4; o += kConsumers) {
+            const int g = o / hd4, d = (o - g * hd4) * 4;
+            float M = -INFINITY;
+            for (int w = 0; w < kNW; ++w) M = fmaxf(M, wml[(w * G + g) * 2]);
+            float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+            float Ls = 0.f;
+            for (int w = 0; w < kNW; ++w) {
+                const float mw = wml[(w * G + g) * 2];
+                const float e = mw == -INFINITY ? 0.f : expf(mw - M);
+                const float4 a = *reinterpret_cast<const float4*>(wacc + ((size_t)w * G + g) * hd + d);
+                sum.x = fmaf(e, a.x, sum.x);
+                sum.y = fmaf(e, a.y, sum.y);
+                sum.z = fmaf(e, a.z, sum.z);
+                sum.w = fmaf(e, a.w, sum.w);
+                Ls = fmaf(e, wml[(w * G + g) * 2 + 1], Ls);
+            }
+            *reinterpret_cast<float4*>(pacc + (size_t)g * hd + d) = sum;
+            if (d == 0) {
+                pml[g * 2] = M;
+                pml[g * 2 + 1] = Ls;
+            }
         }
         __threadfence();
         attn_sync();
         if (tid == 0) {
             const unsigned ticket = atomicAdd(&A.tickets[h], 1u);
-            flag_s[0] = (ticket == (unsigned)(n_active - 1)) ? 1 : 0;
+            *flag_s = (ticket == (unsigned)(n_chunks - 1)) ? 1 : 0;
         }
         attn_sync();
-        if (!flag_s[0]) continue;
+        if (!*flag_s) continue;
         __threadfence();
-        // Last CTA of kv head h: merge weights once per head, then every output
-        // vector is a weighted sum over the splits (eight independent loads at a time).
-        const float4* bacc = reinterpret_cast<const float4*>(A.attn_part + (size_t)h * S * acc_stride);
-        const float* bml = A.attn_part + ml_base + (size_t)h * S * G * 2;
-        for (int g = warp; g < G; g += kAttnThreads / 32) {
+        // last chunk of kv head h: merge weights once per head, then sums
+        const float* bacc = A.attn_part + (size_t)h * A.splits * acc_stride;
+        const float* bml = A.attn_part + ml_base + (size_t)h * A.splits * G * 2;
+        for (int g = warp; g < G; g += kNW) {
             float ms[2], ls[2];
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
-                const int s = lane + 32 * r;
-                ms[r] = s < n_active ? __ldcg(bml + ((size_t)s * G + g) * 2) : -INFINITY;
-                ls[r] = s < n_active ? __ldcg(bml + ((size_t)s * G + g) * 2 + 1) : 0.f;
+                const int sp = lane + 32 * r;
+                ms[r] = sp < n_chunks ? __ldcg(bml + ((size_t)sp * G + g) * 2) : -INFINITY;
+                ls[r] = sp < n_chunks ? __ldcg(bml + ((size_t)sp * G + g) * 2 + 1) : 0.f;
             }
             float M = fmaxf(ms[0], ms[1]);
 #pragma unroll
-            for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
+            for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
             float w[2], Lsum = 0.f;
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
@@ -679,40 +684,48 @@ __device__ __noinline__ void attn_phase(const TokenArgs& A, const TokLayer& L, f
                 Lsum = fmaf(ls[r], w[r], Lsum);
             }
 #pragma unroll
-            for (int o = 16; o; o >>= 1) Lsum += __shfl_xor_sync(0xFFFFFFFFu, Lsum, o);
+            for (int o = 16; o; o >>= 1) Lsum += __shfl_xor_sync(FULL, Lsum, o);
             const float invL = Lsum > 0.f ? 1.0f / Lsum : 0.f;
 #pragma unroll
             for (int r = 0; r < 2; ++r) {
-                const int s = lane + 32 * r;
-                if (s < n_active) w_s[g * kMaxSplits + s] = w[r] * invL;
+                const int sp = lane + 32 * r;
+                if (sp < n_chunks) w_s[g * kMaxSplits + sp] = w[r] * invL;
             }
         }
         attn_sync();
-        const size_t vstride = acc_stride / 4;
-        float4* out4 = reinterpret_cast<float4*>(A.attn + (size_t)h * G * hd);
-        for (int o = tid; o < n_out; o += kAttnThreads) {
-            const int g = o / hdv;
-            const float* wg = w_s + g * kMaxSplits;
+        float* out = A.attn + (size_t)h * G * hd;
+        for (int o = tid; o < G * hd4; o += kConsumers) {
+            const int g = o / hd4, d = (o - g * hd4) * 4;
+            const float* pv = bacc + (size_t)g * hd + d;
             float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int s0 = 0; s0 < n_active; s0 += 8) {
-                float4 v[8];
+            for (int s0 = 0; s0 < n_chunks; s0 += 16) {
+                float4 v[16];
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    v[j] = s0 + j < n_active ? __ldcg(bacc + o + (size_t)(s0 + j) * vstride)
+                for (int j = 0; j < 16; ++j)
+                    v[j] = s0 + j < n_chunks ? __ldcg(reinterpret_cast<const float4*>(pv + (size_t)(s0 + j) * acc_stride))
                                              : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float wj = s0 + j < n_active ? wg[s0 + j] : 0.f;
-                    sum.x = fmaf(wj, v[j].x, sum.x);
-                    sum.y = fmaf(wj, v[j].y, sum.y);
-                    sum.z = fmaf(wj, v[j].z, sum.z);
-                    sum.w = fmaf(wj, v[j].w, sum.w);
+                for (int j = 0; j < 16; ++j) {
+                    if (s0 + j < n_chunks) {
+                        const float wj = w_s[g * kMaxSplits + s0 + j];
+                        sum.x = fmaf(wj, v[j].x, sum.x);
+                        sum.y = fmaf(wj, v[j].y, sum.y);
+                        sum.z = fmaf(wj, v[j].z, sum.z);
+                        sum.w = fmaf(wj, v[j].w, sum.w);
+                    }
                 }
             }
-            out4[o] = sum;
+            *reinterpret_cast<float4*>(out + (size_t)g * hd + d) = sum;
         }
         if (tid == 0) A.tickets[h] = 0u;
     }
+}
+
+__device__ void attn_phase(const TokenArgs& A, const TokLayer& L, float* work) {
+    if (A.n_heads == 4 * A.n_kv)
+        attn_phase_warp<4>(A, L, work);
+    else
+        attn_phase_warp<8>(A, L, work);
 }
 
 // ---------------------------------------------------------------------------
@@ -782,7 +795,7 @@ __global__ void __launch_bounds__(kThreads, 1) token_step_kernel(const __grid_co
         }
         sync();
         // 2) attention over the ring (decoder.rs:121-135)
-        if (ok && tid < kAttnThreads) attn_phase(A, *L, work);
+        if (ok) attn_phase(A, *L, work);
         sync();
         // 3) o-proj + residual (decoder.rs:136-139); commits the append
         if (ok) {
@@ -896,9 +909,9 @@ bool token_kernel_supported(int dim, int hidden, int q_dim, int n_heads, int n_k
     if (!token_plan(q_dim, dim, 2, &t) || !token_plan(dim, q_dim, 1, &t) || !token_plan(2 * hidden, dim, 2, &t) ||
         !token_plan(dim, hidden, 1, &t))
         return false;
-    if (n_kv <= 0 || n_heads % n_kv || hd % 4) return false;
+    if (n_kv <= 0 || n_heads % n_kv || hd % 4 || hd > 128) return false;
     const int G = n_heads / n_kv;
-    return G * hd / 4 <= 4 * kAttnThreads && G <= 4 * (kAttnThreads / 32) * 8;
+    return G == 4 || G == 8;
 }
 
 size_t token_smem_bytes(const TokenArgs& a, int grid) { return token_layout(a, grid).total; }
