@@ -413,7 +413,7 @@ __device__ __forceinline__ float dot4(const float4& a, const float4& b) {
     return fmaf(a.w, b.w, d);
 }
 
-// Warp-per-chunk kernel, D-stage per-warp ring; at most 128 registers, three CTAs per SM.
+// Warp-per-chunk kernel, D-stage per-warp ring; at most 128 registers, four CTAs per SM.
 template <int G, int D>
 __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnArgs A) {
     constexpr int TPG = 32 / G;           // tokens per group: G * TPG = 32 scores per step
@@ -745,8 +745,9 @@ int attn_grid_ctas(int n_heads, int n_kv, int hd) {
     return sms * per_sm;
 }
 
-// Persistent grid of the warp-per-chunk kernel: three 4-warp CTAs per SM
-// (2-stage rings: 64 KB + 10 KB of shared memory, at most 128 registers).
+// Persistent grid of the warp-per-chunk kernel: four 4-warp CTAs per SM
+// (1-stage rings: 32 KB + 10 KB of shared memory, at most 128 registers;
+// more warps hide the load latency better than deeper rings per warp).
 int attn_warp_grid_ctas() {
     static int sms = 0;
     if (!sms) {
@@ -754,7 +755,7 @@ int attn_warp_grid_ctas() {
         cudaGetDevice(&dev);
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
     }
-    return 3 * sms;
+    return 4 * sms;
 }
 
 int attn_max_splits() { return kMaxSplits; }
@@ -768,8 +769,8 @@ int attn_splits_for(int n_kv, int num_sms) {
 
 cudaError_t attn_prepare(int /*dev*/) {
     cudaError_t e = cudaSuccess;
-    for (void* k : {(void*)attn_warp_kernel<4, 2>, (void*)attn_warp_kernel<4, 3>, (void*)attn_warp_kernel<8, 2>,
-                    (void*)attn_warp_kernel<8, 3>}) {
+    for (void* k : {(void*)attn_warp_kernel<4, 1>, (void*)attn_warp_kernel<4, 2>, (void*)attn_warp_kernel<8, 1>,
+                    (void*)attn_warp_kernel<8, 2>}) {
         e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         if (e != cudaSuccess) return e;
     }
@@ -799,10 +800,10 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
     const int G = a.n_heads / a.n_kv;
     void* k = (a.hd % 4 == 0) ? (void*)attn_split_kernel<4> : (void*)attn_split_kernel<1>;
     if (a.hd % 4 == 0 && a.hd <= 128 && (G == 4 || G == 8)) {
-        // 2-stage rings: three CTAs (12 warps) per SM
-        const int D = 2;
-        k = G == 4 ? (D == 2 ? (void*)attn_warp_kernel<4, 2> : (void*)attn_warp_kernel<4, 3>)
-                   : (D == 2 ? (void*)attn_warp_kernel<8, 2> : (void*)attn_warp_kernel<8, 3>);
+        // 1-stage rings: four CTAs (16 warps) per SM
+        const int D = 1;
+        k = G == 4 ? (D == 1 ? (void*)attn_warp_kernel<4, 1> : (void*)attn_warp_kernel<4, 2>)
+                   : (D == 1 ? (void*)attn_warp_kernel<8, 1> : (void*)attn_warp_kernel<8, 2>);
         cfg.dynamicSmemBytes = (size_t)(kAttnThreads / 32) * D * 2 * (32 / G) * a.hd * 4;
         int g2 = attn_warp_grid_ctas();
         if (g2 > max_items) g2 = (int)max_items;
