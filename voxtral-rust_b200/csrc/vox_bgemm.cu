@@ -125,19 +125,81 @@ struct EpiShared {
     int flag;         // this item completes its tile
 };
 
+// Inputs of a row's epilogue that do not depend on the product: the
+// residual row (BG_RESID), the rotation factors and ring slots (BG_QKV), the
+// bias (BG_STORE).  The epilogue warps load them while the MMAs of the item
+// run, so the last item of a tile (the critical path of the launch) issues
+// only stores after its split sum.  Every producer of these values finished
+// before this phase started (grid dependency or phase barrier).
+struct EpiInputs {
+    float a[8], c[8];  // residual or cos (a), sin (c)
+    int slot[8];       // ring slot of the appended token per stream
+    float s;           // bias or RMSNorm gain of the row
+};
+
+__device__ __forceinline__ void bg_epilogue_inputs(const BgArgs& A, int tile, int row, EpiInputs& in) {
+    const int r = tile * kBM + row;
+    const bool live = r < A.rows;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+        in.a[b] = 0.0f;
+        in.c[b] = 0.0f;
+        in.slot[b] = 0;
+    }
+    in.s = 0.0f;
+    if (!live) return;
+    if (A.epi == BG_STORE) {
+        if (A.bias) in.s = A.bias[r];
+    } else if (A.epi == BG_RESID) {
+#pragma unroll
+        for (int b = 0; b < 8; ++b)
+            if (b < A.B) in.a[b] = __ldcg(A.resid + (size_t)b * A.y_stride + r);
+        in.s = A.xop_out && A.xop_gain ? A.xop_gain[r] : 1.0f;
+    } else if (A.epi == BG_QKV) {
+        const int half = A.head_dim / 2;
+        const bool rope = r < A.q_dim + A.kv_dim, is_q = r < A.q_dim;
+        const int rr = is_q ? r : rope ? r - A.q_dim : r - A.q_dim - A.kv_dim;
+        const int d = rr % A.head_dim;
+        // positions and cache states of the 8 streams in one round trip, then
+        // the rotation table rows in a second
+        long long pos[8];
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            pos[b] = 0;
+            if (b >= A.B) continue;
+            if (rope) pos[b] = A.steps[b].pos;
+            if (!is_q) {
+                const KvState post =
+                    kv_after_single_append(A.kv_state[(size_t)b * A.kv_state_stride], A.kv_window, A.ring_cap);
+                in.slot[b] = (post.start + post.len - 1) % A.ring_cap;
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            if (!rope || b >= A.B) continue;
+            long long p = pos[b];
+            if (p < 0 || p >= A.max_pos) {
+                if (row == 0) raise_error(A.err, ERR_POS_RANGE);
+                p = 0;
+            }
+            in.a[b] = A.rope_cos[p * half + d / 2];
+            in.c[b] = A.rope_sin[p * half + d / 2];
+        }
+    }
+}
+
 // Final values y[b] of row `row` of tile `tile` for every stream, after the
 // split sum.  Runs on all 128 threads of the epilogue warpgroup (warp ew);
 // rows beyond A.rows hold zeros and store nothing.
 __device__ __forceinline__ void bg_epilogue(const BgArgs& A, int tile, int row, int lane, int ew, float (&y)[8],
-                                            EpiShared* es) {
+                                            const EpiInputs& in, EpiShared* es) {
     const int r = tile * kBM + row;
     const bool live = r < A.rows;
     if (A.epi == BG_STORE) {
         if (live) {
-            const float bias = A.bias ? A.bias[r] : 0.0f;
 #pragma unroll
             for (int b = 0; b < 8; ++b)
-                if (b < A.B) A.y[(size_t)b * A.y_stride + r] = A.bias ? __fadd_rn(bias, y[b]) : y[b];
+                if (b < A.B) A.y[(size_t)b * A.y_stride + r] = A.bias ? __fadd_rn(in.s, y[b]) : y[b];
         }
     } else if (A.epi == BG_QKV) {
         // RoPE pairs (2p, 2p + 1) sit in adjacent lanes (math.rs:58-61, unfused).
@@ -145,44 +207,24 @@ __device__ __forceinline__ void bg_epilogue(const BgArgs& A, int tile, int row, 
 #pragma unroll
         for (int b = 0; b < 8; ++b) partner[b] = __shfl_xor_sync(kFull, y[b], 1);
         if (!live) return;
-        const int half = A.head_dim / 2;
-        if (r < A.q_dim + A.kv_dim) {
-            const bool is_q = r < A.q_dim;
-            const int rr = is_q ? r : r - A.q_dim;
-            const int d = rr % A.head_dim, h = rr / A.head_dim;
-            const bool odd = d & 1;
+        const bool rope = r < A.q_dim + A.kv_dim, is_q = r < A.q_dim;
+        const int rr = is_q ? r : rope ? r - A.q_dim : r - A.q_dim - A.kv_dim;
+        const int d = rr % A.head_dim, h = rr / A.head_dim;
+        const bool odd = d & 1;
+        float* const ring = rope ? A.k_ring : A.v_ring;
 #pragma unroll
-            for (int b = 0; b < 8; ++b) {
-                if (b >= A.B) continue;
-                long long pos = A.steps[b].pos;
-                if (pos < 0 || pos >= A.max_pos) {
-                    if (row == 0) raise_error(A.err, ERR_POS_RANGE);
-                    pos = 0;
-                }
-                const float c = A.rope_cos[pos * half + d / 2], sn = A.rope_sin[pos * half + d / 2];
+        for (int b = 0; b < 8; ++b) {
+            if (b >= A.B) continue;
+            float o = y[b];
+            if (rope) {
+                const float c = in.a[b], sn = in.c[b];
                 const float ya = odd ? partner[b] : y[b], yb = odd ? y[b] : partner[b];
-                const float o = odd ? __fadd_rn(__fmul_rn(ya, sn), __fmul_rn(yb, c))
-                                    : __fsub_rn(__fmul_rn(ya, c), __fmul_rn(yb, sn));
-                if (is_q) {
-                    A.y[(size_t)b * A.y_stride + r] = o;
-                } else {
-                    const KvState post =
-                        kv_after_single_append(A.kv_state[(size_t)b * A.kv_state_stride], A.kv_window, A.ring_cap);
-                    const int slot = (post.start + post.len - 1) % A.ring_cap;
-                    A.k_ring[(size_t)b * A.ring_stride + ((size_t)h * A.ring_cap + slot) * A.head_dim + d] = o;
-                }
+                o = odd ? __fadd_rn(__fmul_rn(ya, sn), __fmul_rn(yb, c)) : __fsub_rn(__fmul_rn(ya, c), __fmul_rn(yb, sn));
             }
-        } else {
-            const int rr = r - A.q_dim - A.kv_dim;
-            const int d = rr % A.head_dim, h = rr / A.head_dim;
-#pragma unroll
-            for (int b = 0; b < 8; ++b) {
-                if (b >= A.B) continue;
-                const KvState post =
-                    kv_after_single_append(A.kv_state[(size_t)b * A.kv_state_stride], A.kv_window, A.ring_cap);
-                const int slot = (post.start + post.len - 1) % A.ring_cap;
-                A.v_ring[(size_t)b * A.ring_stride + ((size_t)h * A.ring_cap + slot) * A.head_dim + d] = y[b];
-            }
+            if (is_q)
+                A.y[(size_t)b * A.y_stride + r] = o;
+            else
+                ring[(size_t)b * A.ring_stride + ((size_t)h * A.ring_cap + in.slot[b]) * A.head_dim + d] = o;
         }
     } else if (A.epi == BG_SWIGLU) {
         // rows 2j (w1) and 2j + 1 (w3): act[j] = silu(gate) * up (decoder.rs:147-150)
@@ -208,10 +250,10 @@ __device__ __forceinline__ void bg_epilogue(const BgArgs& A, int tile, int row, 
         for (int b = 0; b < 8; ++b) {
             sq[b] = 0.0f;
             if (live && b < A.B) {
-                const float v = __fadd_rn(__ldcg(A.resid + (size_t)b * A.y_stride + r), y[b]);
+                const float v = __fadd_rn(in.a[b], y[b]);
                 A.y[(size_t)b * A.y_stride + r] = v;
                 sq[b] = __fmul_rn(v, v);
-                if (A.xop_out) xop_store(A.xop_out, r, b, A.xop_gain ? __fmul_rn(v, A.xop_gain[r]) : v);
+                if (A.xop_out) xop_store(A.xop_out, r, b, A.xop_gain ? __fmul_rn(v, in.s) : v);
             }
         }
         if (A.ssp_out) {
@@ -579,6 +621,8 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
             if (warp >= 4) {
                 const int ew = warp - 4;        // TMEM lanes 32*ew .. 32*ew + 31
                 const int row = ew * 32 + lane; // row inside the tile
+                EpiInputs in;
+                bg_epilogue_inputs(A, it.tile, row, in);
                 if (!mbar_wait(&acc_full[ab], (local >> 1) & 1)) raise_error(err, ERR_FULL_WAIT);
                 tmem_fence_after();
                 uint32_t raw[16];
@@ -633,7 +677,7 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
                     if (xop && A.norm_w)
 #pragma unroll
                         for (int b = 0; b < 8; ++b) y[b] = __fmul_rn(es->inv[b], y[b]);
-                    bg_epilogue(A, it.tile, row, lane, ew, y, es);
+                    bg_epilogue(A, it.tile, row, lane, ew, y, in, es);
                 }
             }
         }
