@@ -557,6 +557,15 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnAr
             for (int g = 0; g < G; ++g)
 #pragma unroll
                 for (int j = 0; j < TPG; ++j) sc[g * TPG + j] = dot4(q[g], kk[j]);
+            // V rows into registers now, so the slot is refilled while the
+            // scores are reduced and the PV product runs
+            float4 vv[TPG];
+#pragma unroll
+            for (int j = 0; j < TPG; ++j)
+                vv[j] = (dim_ok && t0 + j < t_end) ? *reinterpret_cast<const float4*>(vs + (size_t)j * hd)
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+            __syncwarp();  // every lane has read this stage before it is refilled
+            if (lane == 0 && k + D < n_my) issue(k + D);
             transpose_reduce<32>(sc, lane);
             float s = sc[0] * A.scale;
             if (t0 + my_t >= t_end) s = -INFINITY;
@@ -573,11 +582,6 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnAr
             l_run = l_run * alpha + ps;
             m_run = m_new;
             // PV (ops.rs:117-128) on this lane's dims for every head
-            float4 vv[TPG];
-#pragma unroll
-            for (int j = 0; j < TPG; ++j)
-                vv[j] = (dim_ok && t0 + j < t_end) ? *reinterpret_cast<const float4*>(vs + (size_t)j * hd)
-                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
             for (int g = 0; g < G; ++g) {
                 const float a = __shfl_sync(FULL, alpha, g * TPG);
@@ -594,8 +598,6 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnAr
                     acc[g].w = fmaf(pj, vv[j].w, acc[g].w);
                 }
             }
-            __syncwarp();  // every lane has read this stage before it is refilled
-            if (lane == 0 && k + D < n_my) issue(k + D);
         }
 
         // Combine the warps of this chunk in shared memory.
