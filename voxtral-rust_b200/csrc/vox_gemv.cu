@@ -114,7 +114,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
     uint64_t* full_bar = reinterpret_cast<uint64_t*>(
         smem + (((size_t)NS * stage_bytes + (size_t)P.max_rows_cta * P.nseg * 4 + 15) & ~size_t(15)));
     uint64_t* empty_bar = full_bar + NS;
-    float* scratch = reinterpret_cast<float*>(empty_bar + NS);  // 16 floats + 16 ints
+    float* scratch = reinterpret_cast<float*>(empty_bar + NS);  // 16 floats + 16 ints + 16 floats
 
     if (tid == 0) {
         for (int s = 0; s < NS; ++s) {
@@ -251,13 +251,24 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
                     xr[i][e + 3] = v.w;
                 }
             }
-            if (A.x_copy_out && blockIdx.x == 0 && tp == 0) {
+        }
+    }
+    // Stores only after every load of x is issued, so the loads above make one
+    // round trip (a store between them could alias them).
+    if (A.x_copy_out && blockIdx.x == 0 && tp == 0) {
 #pragma unroll
-                for (int e = 0; e < EPC; ++e) A.x_copy_out[k0 + e] = xr[i][e];
-            }
+        for (int i = 0; i < CPT; ++i) {
+            const int cc = lane + 32 * i;
+            if (cc < segc)
+#pragma unroll
+                for (int e = 0; e < EPC; ++e) A.x_copy_out[(c0 + cc) * EPC + e] = xr[i][e];
         }
     }
 
+    // RMSNorm (math.rs:22-24) deferred to the epilogue: the dot products use
+    // x * g, and each row sum is scaled by inv_rms = 1 / sqrt(sum(x^2) / K + eps)
+    // once the partial sums of squares (staged in scratch[32..]) are complete, so
+    // the stage loop starts without a CTA-wide reduction.
     if (A.norm_w) {
         // Warps 0..nseg-1 (tp == 0) hold every element of x exactly once.
         float ss = 0.0f;
@@ -266,12 +277,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
 #pragma unroll
             for (int e = 0; e < EPC; ++e) ss = fmaf(xr[i][e], xr[i][e], ss);
         ss = warp_sum(ss);
-        if (lane == 0 && tp == 0) scratch[warp] = ss;
-        named_barrier_sync(1, kConsumerWarps * 32);
-        float tot = 0.0f;
-        for (int w = 0; w < nseg; ++w) tot += scratch[w];
-        // math.rs:22-24: inv_rms = 1 / sqrt(sq_sum / dim + eps); out = x * inv_rms * w
-        const float inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), A.eps)));
+        if (lane == 0 && tp == 0) scratch[32 + warp] = ss;
 #pragma unroll
         for (int i = 0; i < CPT; ++i) {
             const int cc = lane + 32 * i;
@@ -282,7 +288,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
                     g = gr[i][e];
                 else
                     g = cc < segc ? A.norm_w[(c0 + cc) * EPC + e] : 0.0f;
-                xr[i][e] = __fmul_rn(__fmul_rn(xr[i][e], inv_rms), g);
+                xr[i][e] = __fmul_rn(xr[i][e], g);
             }
         }
     }
@@ -330,10 +336,16 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
 
     // ---------------- epilogue ----------------
     const int nthr = kConsumerWarps * 32;
+    float inv_rms = 1.0f;
+    if (A.norm_w) {
+        float tot = 0.0f;
+        for (int w = 0; w < nseg; ++w) tot += scratch[32 + w];
+        inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)K), A.eps)));
+    }
     auto row_sum = [&](int lr) {
         float v = 0.0f;
         for (int q = 0; q < nseg; ++q) v += red[lr * nseg + q];
-        return v;
+        return A.norm_w ? __fmul_rn(inv_rms, v) : v;
     };
 
     if constexpr (EPI == EPI_STORE) {
@@ -543,7 +555,7 @@ GemvPlan plan_gemv(int rows, int K, int unit, int wsize, int num_sms, int n_vec)
     if (ns > max_stages_needed) ns = max_stages_needed < 1 ? 1 : max_stages_needed;
     p.nstages = ns;
     size_t red_bytes = ((size_t)p.max_rows_cta * p.nseg * 4 + 15) & ~size_t(15);
-    p.smem = (size_t)ns * stage_bytes + red_bytes + 2 * ns * sizeof(uint64_t) + 32 * 4;
+    p.smem = (size_t)ns * stage_bytes + red_bytes + 2 * ns * sizeof(uint64_t) + 48 * 4;
     return p;
 }
 
