@@ -208,6 +208,22 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
         xe = A.x_embed + (size_t)tok * K;
     }
 
+    // Epilogue inputs that do not depend on this product (the residual row,
+    // the position and ring state of the q|k|v epilogue), loaded now so the
+    // epilogue, which ends the launch, only stores.  Every producer of these
+    // values finished before the dependency wait above.  Thread t's first
+    // epilogue row (pair) is t.
+    [[maybe_unused]] float pre_res = 0.0f, pre_c = 1.0f, pre_s = 0.0f;
+    [[maybe_unused]] long long pre_pos = 0;
+    [[maybe_unused]] KvState pre_st{};
+    if constexpr (EPI == EPI_RESID) {
+        if (tid < nrows) pre_res = A.resid[r0 + tid];
+        if (A.kv_commit && blockIdx.x == 0 && tid == 0) pre_st = *A.kv_commit;
+    } else if constexpr (EPI == EPI_QKV) {
+        pre_pos = A.step->pos;
+        pre_st = *A.kv_state;
+    }
+
     // This warp's slice of x in registers: one round trip to L2.
     float xr[CPT][EPC];
 #pragma unroll
@@ -262,6 +278,17 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
             if (cc < segc)
 #pragma unroll
                 for (int e = 0; e < EPC; ++e) A.x_copy_out[(c0 + cc) * EPC + e] = xr[i][e];
+        }
+    }
+
+    if constexpr (EPI == EPI_QKV) {  // rotation factors of thread t's row pair (needs the position)
+        const bool pos_ok = pre_pos >= 0 && pre_pos < A.max_pos;
+        const int r = r0 + 2 * tid;
+        if (2 * tid < nrows && r < A.q_dim + A.kv_dim) {
+            const int rr = r < A.q_dim ? r : r - A.q_dim;
+            const int d = rr % A.head_dim, half = A.head_dim / 2;
+            pre_c = A.rope_cos[(pos_ok ? pre_pos : 0) * half + d / 2];
+            pre_s = A.rope_sin[(pos_ok ? pre_pos : 0) * half + d / 2];
         }
     }
 
@@ -361,13 +388,13 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
         const bool xout = A.xch && A.xch_out >= 0;
         for (int lr = tid; lr < nrows; lr += nthr) {
             const int r = r0 + lr;
-            const float v = __fadd_rn(A.resid[r], row_sum(lr));
+            const float v = __fadd_rn(lr == tid ? pre_res : A.resid[r], row_sum(lr));
             y[r] = v;
             if (xout)  // tensor parallel: this rank's partial rows into every rank's slot
                 for (int p = 0; p < A.xa.size; ++p) A.xa.slot(A.xch[p], A.xch_out, A.xa.rank)[r] = v;
         }
         if (A.kv_commit && blockIdx.x == 0 && tid == 0)
-            *A.kv_commit = kv_after_single_append(*A.kv_commit, A.kv_window, A.ring_cap);
+            *A.kv_commit = kv_after_single_append(pre_st, A.kv_window, A.ring_cap);
         if (xout) {
             named_barrier_sync(1, nthr);  // every row of this CTA is stored
             if (tid == 0) {
@@ -376,13 +403,13 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
             }
         }
     } else if constexpr (EPI == EPI_QKV) {
-        const long long pos = A.step->pos;
+        const long long pos = pre_pos;
         const bool pos_ok = pos >= 0 && pos < A.max_pos;
         if (!pos_ok && tid == 0 && blockIdx.x == 0) raise_error(A.err, ERR_POS_RANGE);
         const int half = A.head_dim / 2;
         const float* ct = A.rope_cos + (pos_ok ? pos : 0) * half;
         const float* st = A.rope_sin + (pos_ok ? pos : 0) * half;
-        const KvState post = kv_after_single_append(*A.kv_state, A.kv_window, A.ring_cap);
+        const KvState post = kv_after_single_append(pre_st, A.kv_window, A.ring_cap);
         const int slot = (post.start + post.len - 1) % A.ring_cap;
         for (int pp = tid; pp < nrows / 2; pp += nthr) {
             const int r = r0 + 2 * pp;
@@ -391,7 +418,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
                 // math.rs:58-61: (x0*c - x1*s, x0*s + x1*c), unfused
                 const int rr = r < A.q_dim ? r : r - A.q_dim;
                 const int d = rr % A.head_dim;
-                const float c = ct[d / 2], sn = st[d / 2];
+                const float c = pp == tid ? pre_c : ct[d / 2], sn = pp == tid ? pre_s : st[d / 2];
                 const float o0 = __fsub_rn(__fmul_rn(ya, c), __fmul_rn(yb, sn));
                 const float o1 = __fadd_rn(__fmul_rn(ya, sn), __fmul_rn(yb, c));
                 if (r < A.q_dim) {
