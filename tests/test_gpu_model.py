@@ -175,3 +175,40 @@ def test_full_window_rolling_eviction(V, oracle, step_mode):
             # the ring starts at slot 0 and drops `off` tokens in all: start = off mod window
             assert (ln, off, start) == (want_len, want_off, want_off % c["sliding_window"])
         assert oc.layer_pos_offset(0) == fill + n_steps - c["sliding_window"] > 0
+
+
+@pytest.mark.parametrize("fill", [2045, 3000])
+def test_attention_kernel_switch(V, oracle, fill):
+    """Single-stream steps run attention as one thread-block cluster per kv
+    head up to 2048 live tokens (kAttnClusterMaxTokens) and as the split-K
+    kernel above it: teacher-forced steps across the switch (2046 -> 2051
+    tokens) and above it, against the oracle; generate and step agree."""
+    c, n_layers, vocab, n_steps = FULL, 2, 8192, 6
+    m = oracle_model(oracle, c, n_layers, vocab, 0)
+    oc = oracle.RollingKvCache(n_layers, c["n_kv_heads"], c["head_dim"], c["sliding_window"])
+    n = fill * c["n_kv_heads"] * c["head_dim"]
+    for l in range(n_layers):
+        k = oracle.bf16_to_f32(oracle.gen_normal_bf16(0, 5000000 + 2 * l, 1.0, n))
+        v = oracle.bf16_to_f32(oracle.gen_normal_bf16(0, 5000000 + 2 * l + 1, 1.0, n))
+        oc.layer_set(l, k, v, fill, 0)
+    ids = oracle.gen_uniform_ids(0, 3000004, vocab, n_steps)
+    with make_ctx(V, c, n_layers, vocab, 0) as ctx:
+        kv = V.RollingKvCache(ctx, n_layers, c["n_kv_heads"], c["head_dim"], c["sliding_window"])
+        kv.fill_random(fill, 0, 5000000, 1.0)
+        for i in range(n_steps):
+            pos = fill + i
+            tok, logits = ctx.model_step(kv, int(ids[i]), pos, want_logits=True)
+            ref_logits, ref_tok = m.step(oc, int(ids[i]), pos)
+            assert_logits_close(logits, ref_logits, f"step {i}")
+            assert tok == ref_tok, f"step {i}: {tok} != {ref_tok} (margin {top2_margin(ref_logits):.3e})"
+        # greedy generate across the switch equals step-by-step greedy
+        kv2 = V.RollingKvCache(ctx, n_layers, c["n_kv_heads"], c["head_dim"], c["sliding_window"])
+        kv3 = V.RollingKvCache(ctx, n_layers, c["n_kv_heads"], c["head_dim"], c["sliding_window"])
+        kv2.fill_random(fill, 0, 5000000, 1.0)
+        kv3.fill_random(fill, 0, 5000000, 1.0)
+        gen = ctx.model_generate(kv2, int(ids[0]), fill, n_steps)
+        tok, toks = int(ids[0]), []
+        for i in range(n_steps):
+            tok, _ = ctx.model_step(kv3, tok, fill + i)
+            toks.append(tok)
+        assert gen.tolist() == toks

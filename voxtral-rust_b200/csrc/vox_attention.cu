@@ -37,6 +37,9 @@ constexpr int kAttnThreads = 128;
 constexpr int kTile = 32;
 constexpr int kMaxAcc = 4;      // accumulator vectors per thread (G*hd/VEC <= 512)
 constexpr int kMaxSplits = 64;  // merge weights kept in shared memory
+// Most live tokens per kv head for which one stream's attention runs as one
+// thread-block cluster per kv head (attn_cluster_kernel).
+constexpr int kAttnClusterMaxTokens = 2048;
 
 template <int VEC>
 struct VecT;
@@ -413,6 +416,134 @@ __device__ __forceinline__ float dot4(const float4& a, const float4& b) {
     return fmaf(a.w, b.w, d);
 }
 
+// One chunk [t_begin, t_end) of kv head h of stream z, run by every warp of
+// the CTA: warp w takes groups w, w + NW, ... of the chunk.  Each group's K
+// rows and V rows are contiguous in the ring (two pieces at the wrap), so lane
+// 0 fetches them with 1-D bulk copies into the warp's own D-stage slot ring;
+// all lanes then read their four dims per row.  Leaves each warp's
+// accumulators in wacc[warp] and its (m, l) per head in wml[warp]; the caller
+// synchronizes before combining them.
+template <int G, int D>
+__device__ __forceinline__ void attn_chunk_warps(const AttnArgs& A, int z, int h, int t_begin, int t_end,
+                                                 int ring_start, unsigned char* ring_smem, uint64_t (*wbar)[D],
+                                                 float (*wacc)[G][128], float (*wml)[G][2], uint32_t& phase) {
+    constexpr int TPG = 32 / G;
+    constexpr int NW = kAttnThreads / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int hd = A.hd;
+    const unsigned FULL = 0xFFFFFFFFu;
+    const bool dim_ok = lane * 4 < hd;
+    const int my_g = lane / TPG, my_t = lane % TPG;
+    const float* qh = A.q + z * A.q_stride + (size_t)h * G * hd + lane * 4;
+
+    float4 q[G], acc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        q[g] = dim_ok ? *reinterpret_cast<const float4*>(qh + (size_t)g * hd) : make_float4(0.f, 0.f, 0.f, 0.f);
+        acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float m_run = -INFINITY, l_run = 0.f;  // of head my_g
+
+    const int n_groups = (t_end - t_begin + TPG - 1) / TPG;
+    const int n_my = warp < n_groups ? (n_groups - warp + NW - 1) / NW : 0;
+    const size_t row_bytes = (size_t)hd * 4;
+    const uint32_t stage_bytes = (uint32_t)(2 * TPG * row_bytes);
+    unsigned char* my_ring = ring_smem + (size_t)warp * D * stage_bytes;
+    const float* kbase = A.k_ring + z * A.ring_stride + (size_t)h * A.cap * hd;
+    const float* vbase = A.v_ring + z * A.ring_stride + (size_t)h * A.cap * hd;
+    auto issue = [&](int k) {
+        const int t0 = t_begin + (warp + NW * k) * TPG;
+        const int ntok = min(TPG, t_end - t0);
+        int slot0 = ring_start + t0;
+        if (slot0 >= A.cap) slot0 -= A.cap;
+        const int n1 = min(ntok, A.cap - slot0);
+        unsigned char* st = my_ring + (size_t)(k % D) * stage_bytes;
+        uint64_t* bar = &wbar[warp][k % D];
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive_expect_tx(bar, (uint32_t)(2 * ntok * row_bytes));
+        bulk_copy_g2s_nohint(st, kbase + (size_t)slot0 * hd, (uint32_t)(n1 * row_bytes), bar);
+        bulk_copy_g2s_nohint(st + TPG * row_bytes, vbase + (size_t)slot0 * hd, (uint32_t)(n1 * row_bytes), bar);
+        if (n1 < ntok) {
+            bulk_copy_g2s_nohint(st + n1 * row_bytes, kbase, (uint32_t)((ntok - n1) * row_bytes), bar);
+            bulk_copy_g2s_nohint(st + TPG * row_bytes + n1 * row_bytes, vbase, (uint32_t)((ntok - n1) * row_bytes),
+                                 bar);
+        }
+    };
+    if (lane == 0)
+        for (int k = 0; k < min(D, n_my); ++k) issue(k);
+    __syncwarp();
+
+    for (int k = 0; k < n_my; ++k) {
+        const int t0 = t_begin + (warp + NW * k) * TPG;
+        const int stg = k % D;
+        if (!mbar_wait(&wbar[warp][stg], (phase >> stg) & 1u) && lane == 0) raise_error(A.err, ERR_FULL_WAIT);
+        phase ^= 1u << stg;
+        const float* ks = reinterpret_cast<const float*>(my_ring + (size_t)stg * stage_bytes) + lane * 4;
+        const float* vs = ks + TPG * hd;
+        float4 kk[TPG];
+#pragma unroll
+        for (int j = 0; j < TPG; ++j)
+            kk[j] = dim_ok ? *reinterpret_cast<const float4*>(ks + (size_t)j * hd) : make_float4(0.f, 0.f, 0.f, 0.f);
+        // ops.rs:108-113: scores q . k * scale (rows past t_end hold stale data
+        // and are masked; their sums never mix with live ones)
+        float sc[32];
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int j = 0; j < TPG; ++j) sc[g * TPG + j] = dot4(q[g], kk[j]);
+        // V rows into registers now, so the slot is refilled while the
+        // scores are reduced and the PV product runs
+        float4 vv[TPG];
+#pragma unroll
+        for (int j = 0; j < TPG; ++j)
+            vv[j] = (dim_ok && t0 + j < t_end) ? *reinterpret_cast<const float4*>(vs + (size_t)j * hd)
+                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        __syncwarp();  // every lane has read this stage before it is refilled
+        if (lane == 0 && k + D < n_my) issue(k + D);
+        transpose_reduce<32>(sc, lane);
+        float s = sc[0] * A.scale;
+        if (t0 + my_t >= t_end) s = -INFINITY;
+        // online softmax over this group (math.rs:67-88 restated incrementally)
+        float gm = s;
+#pragma unroll
+        for (int o = TPG / 2; o >= 1; o >>= 1) gm = fmaxf(gm, __shfl_xor_sync(FULL, gm, o));
+        const float m_new = fmaxf(m_run, gm);
+        const float p = (s == -INFINITY) ? 0.f : expf(s - m_new);
+        float ps = p;
+#pragma unroll
+        for (int o = TPG / 2; o >= 1; o >>= 1) ps += __shfl_xor_sync(FULL, ps, o);
+        const float alpha = (m_run == -INFINITY) ? 0.f : expf(m_run - m_new);
+        l_run = l_run * alpha + ps;
+        m_run = m_new;
+        // PV (ops.rs:117-128) on this lane's dims for every head
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float a = __shfl_sync(FULL, alpha, g * TPG);
+            acc[g].x *= a;
+            acc[g].y *= a;
+            acc[g].z *= a;
+            acc[g].w *= a;
+#pragma unroll
+            for (int j = 0; j < TPG; ++j) {
+                const float pj = __shfl_sync(FULL, p, g * TPG + j);
+                acc[g].x = fmaf(pj, vv[j].x, acc[g].x);
+                acc[g].y = fmaf(pj, vv[j].y, acc[g].y);
+                acc[g].z = fmaf(pj, vv[j].z, acc[g].z);
+                acc[g].w = fmaf(pj, vv[j].w, acc[g].w);
+            }
+        }
+    }
+
+    // Combine the warps of this chunk in shared memory.
+    if (dim_ok)
+#pragma unroll
+        for (int g = 0; g < G; ++g) *reinterpret_cast<float4*>(&wacc[warp][g][lane * 4]) = acc[g];
+    if (my_t == 0) {
+        wml[warp][my_g][0] = m_run;
+        wml[warp][my_g][1] = l_run;
+    }
+}
+
 // Warp-per-chunk kernel, D-stage per-warp ring; at most 128 registers, four CTAs per SM.
 template <int G, int D>
 __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnArgs A) {
@@ -477,8 +608,6 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnAr
                 }
             }
 
-    const bool dim_ok = lane * 4 < hd;
-    const int my_g = lane / TPG, my_t = lane % TPG;
     const int hd4 = hd / 4;
     uint32_t phase = 0;  // parity of the next completion of each of this warp's stages
     const int n_out = G * hd4;  // float4 outputs per (stream, kv head)
@@ -496,118 +625,8 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnAr
         const int t_begin = plan.mask_start[z] + split * per;
         const int t_end = min(len, t_begin + per);
         const int ring_start = plan.start[z];
-        const float* qh = A.q + z * A.q_stride + (size_t)h * G * hd + lane * 4;
 
-        float4 q[G], acc[G];
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            q[g] = dim_ok ? *reinterpret_cast<const float4*>(qh + (size_t)g * hd) : make_float4(0.f, 0.f, 0.f, 0.f);
-            acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        float m_run = -INFINITY, l_run = 0.f;  // of head my_g
-
-        // Warp w takes groups w, w + NW, ... of the chunk.  Each group's K rows
-        // and V rows are contiguous in the ring (two pieces at the wrap), so
-        // lane 0 fetches them with 1-D bulk copies into the warp's own
-        // D-stage ring; all lanes then read their four dims per row.
-        const int n_groups = (t_end - t_begin + TPG - 1) / TPG;
-        const int n_my = warp < n_groups ? (n_groups - warp + NW - 1) / NW : 0;
-        const size_t row_bytes = (size_t)hd * 4;
-        const uint32_t stage_bytes = (uint32_t)(2 * TPG * row_bytes);
-        unsigned char* my_ring = ring_smem + (size_t)warp * D * stage_bytes;
-        const float* kbase = A.k_ring + z * A.ring_stride + (size_t)h * A.cap * hd;
-        const float* vbase = A.v_ring + z * A.ring_stride + (size_t)h * A.cap * hd;
-        auto issue = [&](int k) {
-            const int t0 = t_begin + (warp + NW * k) * TPG;
-            const int ntok = min(TPG, t_end - t0);
-            int slot0 = ring_start + t0;
-            if (slot0 >= A.cap) slot0 -= A.cap;
-            const int n1 = min(ntok, A.cap - slot0);
-            unsigned char* st = my_ring + (size_t)(k % D) * stage_bytes;
-            uint64_t* bar = &wbar[warp][k % D];
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive_expect_tx(bar, (uint32_t)(2 * ntok * row_bytes));
-            bulk_copy_g2s_nohint(st, kbase + (size_t)slot0 * hd, (uint32_t)(n1 * row_bytes), bar);
-            bulk_copy_g2s_nohint(st + TPG * row_bytes, vbase + (size_t)slot0 * hd, (uint32_t)(n1 * row_bytes), bar);
-            if (n1 < ntok) {
-                bulk_copy_g2s_nohint(st + n1 * row_bytes, kbase, (uint32_t)((ntok - n1) * row_bytes), bar);
-                bulk_copy_g2s_nohint(st + TPG * row_bytes + n1 * row_bytes, vbase, (uint32_t)((ntok - n1) * row_bytes),
-                                     bar);
-            }
-        };
-        if (lane == 0)
-            for (int k = 0; k < min(D, n_my); ++k) issue(k);
-        __syncwarp();
-
-        for (int k = 0; k < n_my; ++k) {
-            const int t0 = t_begin + (warp + NW * k) * TPG;
-            const int stg = k % D;
-            if (!mbar_wait(&wbar[warp][stg], (phase >> stg) & 1u) && lane == 0) raise_error(A.err, ERR_FULL_WAIT);
-            phase ^= 1u << stg;
-            const float* ks = reinterpret_cast<const float*>(my_ring + (size_t)stg * stage_bytes) + lane * 4;
-            const float* vs = ks + TPG * hd;
-            float4 kk[TPG];
-#pragma unroll
-            for (int j = 0; j < TPG; ++j)
-                kk[j] = dim_ok ? *reinterpret_cast<const float4*>(ks + (size_t)j * hd) : make_float4(0.f, 0.f, 0.f, 0.f);
-            // ops.rs:108-113: scores q . k * scale (rows past t_end hold stale data
-            // and are masked; their sums never mix with live ones)
-            float sc[32];
-#pragma unroll
-            for (int g = 0; g < G; ++g)
-#pragma unroll
-                for (int j = 0; j < TPG; ++j) sc[g * TPG + j] = dot4(q[g], kk[j]);
-            // V rows into registers now, so the slot is refilled while the
-            // scores are reduced and the PV product runs
-            float4 vv[TPG];
-#pragma unroll
-            for (int j = 0; j < TPG; ++j)
-                vv[j] = (dim_ok && t0 + j < t_end) ? *reinterpret_cast<const float4*>(vs + (size_t)j * hd)
-                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-            __syncwarp();  // every lane has read this stage before it is refilled
-            if (lane == 0 && k + D < n_my) issue(k + D);
-            transpose_reduce<32>(sc, lane);
-            float s = sc[0] * A.scale;
-            if (t0 + my_t >= t_end) s = -INFINITY;
-            // online softmax over this group (math.rs:67-88 restated incrementally)
-            float gm = s;
-#pragma unroll
-            for (int o = TPG / 2; o >= 1; o >>= 1) gm = fmaxf(gm, __shfl_xor_sync(FULL, gm, o));
-            const float m_new = fmaxf(m_run, gm);
-            const float p = (s == -INFINITY) ? 0.f : expf(s - m_new);
-            float ps = p;
-#pragma unroll
-            for (int o = TPG / 2; o >= 1; o >>= 1) ps += __shfl_xor_sync(FULL, ps, o);
-            const float alpha = (m_run == -INFINITY) ? 0.f : expf(m_run - m_new);
-            l_run = l_run * alpha + ps;
-            m_run = m_new;
-            // PV (ops.rs:117-128) on this lane's dims for every head
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const float a = __shfl_sync(FULL, alpha, g * TPG);
-                acc[g].x *= a;
-                acc[g].y *= a;
-                acc[g].z *= a;
-                acc[g].w *= a;
-#pragma unroll
-                for (int j = 0; j < TPG; ++j) {
-                    const float pj = __shfl_sync(FULL, p, g * TPG + j);
-                    acc[g].x = fmaf(pj, vv[j].x, acc[g].x);
-                    acc[g].y = fmaf(pj, vv[j].y, acc[g].y);
-                    acc[g].z = fmaf(pj, vv[j].z, acc[g].z);
-                    acc[g].w = fmaf(pj, vv[j].w, acc[g].w);
-                }
-            }
-        }
-
-        // Combine the warps of this chunk in shared memory.
-        if (dim_ok)
-#pragma unroll
-            for (int g = 0; g < G; ++g) *reinterpret_cast<float4*>(&wacc[warp][g][lane * 4]) = acc[g];
-        if (my_t == 0) {
-            wml[warp][my_g][0] = m_run;
-            wml[warp][my_g][1] = l_run;
-        }
+        attn_chunk_warps<G, D>(A, z, h, t_begin, t_end, ring_start, ring_smem, wbar, wacc, wml, phase);
         __syncthreads();
         const size_t acc_stride = (size_t)G * hd;
         const size_t ml_base = (size_t)A.n_kv * A.nsplit * acc_stride;
@@ -724,6 +743,151 @@ bool attn_supported(int n_heads, int n_kv, int hd) {
     return (G * hd / vec) <= kMaxAcc * kAttnThreads;
 }
 
+// ---- cluster variant for one stream and short contexts ----------------------
+// One thread-block cluster of CS CTAs per kv head: the CTAs split the head's
+// live tokens evenly, run the warp-per-group loop above, combine their warps in
+// shared memory, and store the CTA's (m, l, acc) straight into the leader's
+// shared memory (st.shared::cluster).  After one cluster barrier the leader
+// merges the CS partials in rank order.  No partials in global memory, no
+// tickets and no merge loads: the round trips that dominate attention over a
+// few hundred tokens are gone.  The context is known on the host, which picks
+// this kernel only up to kAttnClusterMaxTokens live tokens.
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
+    uint32_t d;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
+    return d;
+}
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float4 v) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+                 "f"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ void st_cluster_v2(uint32_t addr, float a, float b) {
+    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+template <int G, int CS>
+__global__ void __launch_bounds__(kAttnThreads, 4) attn_cluster_kernel(const AttnArgs A) {
+    constexpr int TPG = 32 / G;
+    constexpr int NW = kAttnThreads / 32;
+    constexpr int HD = 128;
+    // [NW][K rows | V rows] slots, then the leader's merge buffer:
+    // acc [CS][G][hd] followed by (m, l) [CS][G][2]
+    extern __shared__ __align__(128) unsigned char ring_smem[];
+    __shared__ uint64_t wbar[NW][1];
+    __shared__ __align__(16) float wacc[NW][G][HD];
+    __shared__ float wml[NW][G][2];
+    __shared__ int range_s[3];  // t_begin, t_end, ring start
+    const int tid = threadIdx.x;
+    const int hd = A.hd, hd4 = hd / 4, n_out = G * hd4;
+    const uint32_t rank = cluster_rank();
+    const int h = blockIdx.x / CS;
+    float* macc = reinterpret_cast<float*>(ring_smem + (size_t)NW * 2 * TPG * hd * 4);
+    float* mml = macc + (size_t)CS * G * hd;
+
+    if (tid < NW) mbar_init(&wbar[tid][0], 1);
+    if (tid == 0) fence_barrier_init();
+    // First cluster phase: every CTA of the cluster has started.  Its wait sits
+    // just before the first store into the leader's shared memory, so it costs
+    // nothing on the path (a CTA may write another's shared memory only once
+    // that CTA is running).
+    cluster_arrive_relaxed();
+    pdl_allow_dependents();
+    pdl_wait_prior_grids();
+    if (tid == 0) {
+        KvState st = A.st[0];
+        if (A.pre_append) st = kv_after_single_append(st, A.kv_window, A.cap);
+        const int len = st.len;
+        const int ms = (A.cfg_window > 0 && len > A.cfg_window) ? len - A.cfg_window : 0;
+        const int groups = (len - ms + TPG - 1) / TPG;
+        const int gpc = (groups + CS - 1) / CS;  // groups of this CTA
+        const int g0 = min(groups, (int)rank * gpc), g1 = min(groups, g0 + gpc);
+        range_s[0] = ms + g0 * TPG;
+        range_s[1] = min(len, ms + g1 * TPG);
+        range_s[2] = st.start;
+    }
+    __syncthreads();
+    uint32_t phase = 0;
+    attn_chunk_warps<G, 1>(A, 0, h, range_s[0], range_s[1], range_s[2], ring_smem, wbar, wacc, wml, phase);
+    __syncthreads();
+
+    // This CTA's partial into the leader's buffer, slot `rank`.
+    cluster_wait();
+    const uint32_t lacc = cluster_map(smem_addr(macc), 0), lml = cluster_map(smem_addr(mml), 0);
+    for (int o = tid; o < n_out; o += kAttnThreads) {
+        const int g = o / hd4, d = (o - g * hd4) * 4;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, wml[w][g][0]);
+        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+        float L = 0.f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            const float mw = wml[w][g][0];
+            const float e = mw == -INFINITY ? 0.f : expf(mw - M);
+            const float4 a = *reinterpret_cast<const float4*>(&wacc[w][g][d]);
+            sum.x = fmaf(e, a.x, sum.x);
+            sum.y = fmaf(e, a.y, sum.y);
+            sum.z = fmaf(e, a.z, sum.z);
+            sum.w = fmaf(e, a.w, sum.w);
+            L = fmaf(e, wml[w][g][1], L);
+        }
+        st_cluster_v4(lacc + (uint32_t)((((size_t)rank * G + g) * hd + d) * 4), sum);
+        if (d == 0) st_cluster_v2(lml + (uint32_t)(((size_t)rank * G + g) * 2 * 4), M, L);
+    }
+    cluster_sync_all();  // every partial has landed in the leader's buffer
+    if (rank != 0) return;
+
+    // Merge the CS partials in rank order (the same weights as the global merge).
+    float* out = A.out + (size_t)h * G * hd;
+    for (int o = tid; o < n_out; o += kAttnThreads) {
+        const int g = o / hd4, d = (o - g * hd4) * 4;
+        float M = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < CS; ++r) M = fmaxf(M, mml[(r * G + g) * 2]);
+        float w[CS], L = 0.f;
+#pragma unroll
+        for (int r = 0; r < CS; ++r) {
+            const float mr = mml[(r * G + g) * 2];
+            w[r] = mr == -INFINITY ? 0.f : expf(mr - M);
+            L = fmaf(mml[(r * G + g) * 2 + 1], w[r], L);
+        }
+        const float invL = L > 0.f ? 1.0f / L : 0.f;
+        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int r = 0; r < CS; ++r) {
+            const float wr = w[r] * invL;
+            const float4 a = *reinterpret_cast<const float4*>(macc + ((size_t)r * G + g) * hd + d);
+            sum.x = fmaf(wr, a.x, sum.x);
+            sum.y = fmaf(wr, a.y, sum.y);
+            sum.z = fmaf(wr, a.z, sum.z);
+            sum.w = fmaf(wr, a.w, sum.w);
+        }
+        *reinterpret_cast<float4*>(out + (size_t)g * hd + d) = sum;
+        if (A.xop) {
+            const int k0 = (h * G + g) * hd + d;
+            xop_store(A.xop, k0, 0, sum.x);
+            xop_store(A.xop, k0 + 1, 0, sum.y);
+            xop_store(A.xop, k0 + 2, 0, sum.z);
+            xop_store(A.xop, k0 + 3, 0, sum.w);
+        }
+    }
+}
+
 size_t attn_smem_bytes(int n_heads, int n_kv, int hd) {
     const int G = n_heads / n_kv;
     const int pad = (hd % 4 == 0) ? 4 : 1;
@@ -780,6 +944,85 @@ cudaError_t attn_prepare(int /*dev*/) {
     if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(attn_split_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 200 * 1024);
+}
+
+namespace {
+size_t attn_cluster_smem(int G, int hd, int cs) {
+    return (size_t)(kAttnThreads / 32) * 2 * (32 / G) * hd * 4 + (size_t)cs * G * (hd + 2) * 4;
+}
+void* attn_cluster_fn(int G, int cs) {
+    if (G == 4) return cs == 16 ? (void*)attn_cluster_kernel<4, 16> : (void*)attn_cluster_kernel<4, 8>;
+    return cs == 16 ? (void*)attn_cluster_kernel<8, 16> : (void*)attn_cluster_kernel<8, 8>;
+}
+}  // namespace
+
+int attn_cluster_size(int n_heads, int n_kv, int hd) {
+    const int G = n_kv > 0 ? n_heads / n_kv : 0;
+    if (n_kv <= 0 || n_heads % n_kv || (G != 4 && G != 8) || hd % 4 || hd <= 0 || hd > 128) return 0;
+    // 16 CTAs per kv head where the device can hold every cluster at once
+    // (a non-portable size), else the portable 8.
+    static int cached[2][129] = {};
+    int& c = cached[G == 8][hd];
+    if (c == 0) {
+        c = -1;
+        for (int cs : {16, 8}) {
+            void* k = attn_cluster_fn(G, cs);
+            if (cs == 16 && cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+                cudaGetLastError();
+                continue;
+            }
+            if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)attn_cluster_smem(G, 128, cs)) != cudaSuccess) {  // any head_dim
+                cudaGetLastError();
+                continue;
+            }
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(n_kv * cs, 1, 1);
+            cfg.blockDim = dim3(kAttnThreads, 1, 1);
+            cfg.dynamicSmemBytes = attn_cluster_smem(G, hd, cs);
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = cs;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, k, &cfg) != cudaSuccess) {
+                cudaGetLastError();
+                continue;
+            }
+            if (n >= n_kv) {
+                c = cs;
+                break;
+            }
+        }
+    }
+    return c > 0 ? c : 0;
+}
+
+int attn_cluster_max_tokens() { return kAttnClusterMaxTokens; }
+
+cudaError_t launch_attention_cluster(const AttnArgs& a, cudaStream_t s, bool pdl) {
+    const int cs = attn_cluster_size(a.n_heads, a.n_kv, a.hd);
+    if (cs == 0 || a.n_streams > 1) return cudaErrorInvalidValue;
+    const int G = a.n_heads / a.n_kv;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.n_kv * cs, 1, 1);
+    cfg.blockDim = dim3(kAttnThreads, 1, 1);
+    cfg.dynamicSmemBytes = attn_cluster_smem(G, a.hd, cs);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    void* args[] = {(void*)&a};
+    return cudaLaunchKernelExC(&cfg, attn_cluster_fn(G, cs), args);
 }
 
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {

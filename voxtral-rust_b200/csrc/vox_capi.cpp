@@ -235,6 +235,8 @@ struct vox_kv {
     std::vector<vox_kv*> views;    // owner: views by stream, created on demand
     cudaGraphExec_t step_graph = nullptr;
     uint64_t graph_kernels = 0;
+    cudaGraphExec_t step_graph_short = nullptr;  // same step, cluster attention (short contexts)
+    uint64_t graph_kernels_short = 0;
     TokLayer* tok_layers = nullptr;  // device table of per-layer pointers (token kernel)
     cudaGraphExec_t batch_graph = nullptr;  // multi-stream step over all streams
     uint64_t batch_kernels = 0;
@@ -431,7 +433,7 @@ GemvArgs base_args(vox_ctx* c) {
 }
 
 // Enqueue one decoder layer (decoder.rs:88-155) as five kernels.
-int enqueue_layer(vox_ctx* c, vox_kv* kv, size_t l, bool from_embed, bool pdl) {
+int enqueue_layer(vox_ctx* c, vox_kv* kv, size_t l, bool from_embed, bool pdl, bool short_attn = false) {
     const LayerDev& L = c->layers[l];
     float* kr = kv->k + l * kv->layer_elems();
     float* vr = kv->v + l * kv->layer_elems();
@@ -482,7 +484,8 @@ int enqueue_layer(vox_ctx* c, vox_kv* kv, size_t l, bool from_embed, bool pdl) {
     at.out = c->attn;
     at.scale = 1.0f / sqrtf((float)c->cfg.head_dim);
     at.err = c->err;
-    CUDA_TRY(record_launch(c, launch_attention(at, c->stream, pdl)));
+    CUDA_TRY(record_launch(c, short_attn ? launch_attention_cluster(at, c->stream, pdl)
+                                         : launch_attention(at, c->stream, pdl)));
 
     // 3) o-proj + residual (decoder.rs:136-139); commits the append.
     a = base_args(c);
@@ -905,16 +908,19 @@ int build_token_layers(vox_ctx* c, vox_kv* kv) {
     return VOX_OK;
 }
 
-int build_step_graph(vox_ctx* c, vox_kv* kv) {
-    if (kv->step_graph) return VOX_OK;
-    if (c->tok_ok) TRY(build_token_layers(c, kv));
+// One token step as a CUDA graph.  Single-stream steps get two graphs when
+// the shape allows: attention as one cluster per kv head (contexts up to
+// attn_cluster_max_tokens()) or the persistent split-K kernel; launch_graph
+// picks one per step from the context length the host already knows.
+static int capture_step(vox_ctx* c, vox_kv* kv, bool short_attn, cudaGraphExec_t* out, uint64_t* kernels) {
     const uint64_t before = c->launches;
     CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
     int rc = VOX_OK;
     if (c->tok_ok) {
         rc = enqueue_token_kernel(c, kv);
     } else {
-        for (size_t l = 0; l < c->layers.size() && rc == VOX_OK; ++l) rc = enqueue_layer(c, kv, l, l == 0, true);
+        for (size_t l = 0; l < c->layers.size() && rc == VOX_OK; ++l)
+            rc = enqueue_layer(c, kv, l, l == 0, true, short_attn);
         if (rc == VOX_OK) rc = enqueue_head(c, true);
     }
     cudaGraph_t g = nullptr;
@@ -924,11 +930,21 @@ int build_step_graph(vox_ctx* c, vox_kv* kv) {
         return rc;
     }
     CUDA_TRY(e);
-    e = cudaGraphInstantiate(&kv->step_graph, g, 0);
+    e = cudaGraphInstantiate(out, g, 0);
     cudaGraphDestroy(g);
     CUDA_TRY(e);
-    kv->graph_kernels = c->launches - before;
+    *kernels = c->launches - before;
     c->launches = before;
+    return VOX_OK;
+}
+
+int build_step_graph(vox_ctx* c, vox_kv* kv) {
+    if (kv->step_graph) return VOX_OK;
+    if (c->tok_ok) TRY(build_token_layers(c, kv));
+    TRY(capture_step(c, kv, false, &kv->step_graph, &kv->graph_kernels));
+    if (!c->tok_ok &&
+        attn_cluster_size((int)c->cfg.n_heads, (int)c->cfg.n_kv_heads, (int)c->cfg.head_dim) > 0)
+        TRY(capture_step(c, kv, true, &kv->step_graph_short, &kv->graph_kernels_short));
     return VOX_OK;
 }
 
@@ -946,9 +962,21 @@ int ensure_host_steps(vox_ctx* c, size_t n) {
     return VOX_OK;
 }
 
-int launch_graph(vox_ctx* c, vox_kv* kv) {
-    CUDA_TRY(cudaGraphLaunch(kv->step_graph, c->stream));
-    c->launches += kv->graph_kernels;
+// Live tokens the attention of every layer reads after `steps` more
+// single-token appends (kv.rs:48-88 eviction, then the config's window mask).
+size_t live_tokens_after(const vox_ctx* c, const vox_kv* kv, size_t steps) {
+    size_t n = 0;
+    for (size_t l = 0; l < kv->n_layers; ++l) n = std::max(n, kv->hs[l].len);
+    n = std::min(n + steps, kv->window);
+    if (c->cfg.sliding_window > 0) n = std::min(n, (size_t)c->cfg.sliding_window);
+    return n;
+}
+
+// `live` = live tokens of this step's attention (after its append).
+int launch_graph(vox_ctx* c, vox_kv* kv, size_t live) {
+    const bool use_short = kv->step_graph_short && live <= (size_t)attn_cluster_max_tokens();
+    CUDA_TRY(cudaGraphLaunch(use_short ? kv->step_graph_short : kv->step_graph, c->stream));
+    c->launches += use_short ? kv->graph_kernels_short : kv->graph_kernels;
     return VOX_OK;
 }
 
@@ -1386,9 +1414,10 @@ static int single_stream(const vox_kv* kv) {
 
 static void release_graphs(vox_kv* kv) {
     if (kv->step_graph) cudaGraphExecDestroy(kv->step_graph);
+    if (kv->step_graph_short) cudaGraphExecDestroy(kv->step_graph_short);
     if (kv->batch_graph) cudaGraphExecDestroy(kv->batch_graph);
     if (kv->tok_layers) cudaFree(kv->tok_layers);
-    kv->step_graph = kv->batch_graph = nullptr;
+    kv->step_graph = kv->step_graph_short = kv->batch_graph = nullptr;
     kv->tok_layers = nullptr;
 }
 
@@ -1618,7 +1647,7 @@ int vox_model_step(vox_ctx* c, vox_kv* kv, int32_t token, size_t pos, int32_t* n
     hs->pos = (int64_t)pos;
     hs->tok = token;
     CUDA_TRY(cudaMemcpyAsync(c->step, hs, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
-    TRY(launch_graph(c, kv));
+    TRY(launch_graph(c, kv, live_tokens_after(c, kv, 1)));
     CUDA_TRY(cudaMemcpyAsync(c->h_tok, c->tok_out, 4, cudaMemcpyDeviceToHost, c->stream));
     if (logits)
         CUDA_TRY(cudaMemcpyAsync(logits, c->logits, c->opt.vocab * 4, cudaMemcpyDeviceToHost, c->stream));
@@ -1647,7 +1676,7 @@ int vox_model_prefill(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, s
         hs->pos = (int64_t)(pos0 + i);
         hs->tok = tokens[i];
         CUDA_TRY(cudaMemcpyAsync(c->step, hs, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
-        TRY(launch_graph(c, kv));
+        TRY(launch_graph(c, kv, live_tokens_after(c, kv, i + 1)));
     }
     TRY(check_device_errors(c));
     for (size_t i = 0; i < n; ++i) mirror_single_append_all(kv);
@@ -1673,7 +1702,7 @@ int vox_model_generate(vox_ctx* c, vox_kv* kv, int32_t token, size_t pos, size_t
     CUDA_TRY(cudaMemcpyAsync(c->step, hs, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
     int32_t* tok_hist = reinterpret_cast<int32_t*>(c->h_steps + 1);  // pinned staging for the ids
     for (size_t i = 0; i < n_steps; ++i) {
-        TRY(launch_graph(c, kv));
+        TRY(launch_graph(c, kv, live_tokens_after(c, kv, i + 1)));
         if (tokens_out)
             CUDA_TRY(cudaMemcpyAsync(tok_hist + i, c->tok_out, 4, cudaMemcpyDeviceToHost, c->stream));
     }

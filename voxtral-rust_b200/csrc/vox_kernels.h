@@ -292,6 +292,13 @@ bool attn_supported(int n_heads, int n_kv, int hd);
 size_t attn_smem_bytes(int n_heads, int n_kv, int hd);
 cudaError_t attn_prepare(int dev);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
+// One stream, short context: one thread-block cluster per kv head merging in
+// distributed shared memory.  attn_cluster_size is 16 or 8 CTAs per kv head,
+// or 0 when this shape or device cannot run it; the host uses it for at most
+// attn_cluster_max_tokens() live tokens.
+int attn_cluster_size(int n_heads, int n_kv, int hd);
+int attn_cluster_max_tokens();
+cudaError_t launch_attention_cluster(const AttnArgs& a, cudaStream_t s, bool pdl);
 
 cudaError_t launch_argmax_final(const ArgmaxPart* parts, int n, StepState* step, int32_t* tok_out,
                                 cudaStream_t s, bool pdl);
