@@ -177,11 +177,11 @@ def test_full_window_rolling_eviction(V, oracle, step_mode):
         assert oc.layer_pos_offset(0) == fill + n_steps - c["sliding_window"] > 0
 
 
-@pytest.mark.parametrize("fill", [2045, 3000])
+@pytest.mark.parametrize("fill", [3581, 5000])
 def test_attention_kernel_switch(V, oracle, fill):
     """Single-stream steps run attention as one thread-block cluster per kv
-    head up to 2048 live tokens (kAttnClusterMaxTokens) and as the split-K
-    kernel above it: teacher-forced steps across the switch (2046 -> 2051
+    head up to 3584 live tokens (kAttnClusterMaxTokens) and as the split-K
+    kernel above it: teacher-forced steps across the switch (3582 -> 3587
     tokens) and above it, against the oracle; generate and step agree."""
     c, n_layers, vocab, n_steps = FULL, 2, 8192, 6
     m = oracle_model(oracle, c, n_layers, vocab, 0)

@@ -39,7 +39,7 @@ constexpr int kMaxAcc = 4;      // accumulator vectors per thread (G*hd/VEC <= 5
 constexpr int kMaxSplits = 64;  // merge weights kept in shared memory
 // Most live tokens per kv head for which one stream's attention runs as one
 // thread-block cluster per kv head (attn_cluster_kernel).
-constexpr int kAttnClusterMaxTokens = 2048;
+constexpr int kAttnClusterMaxTokens = 3584;
 
 template <int VEC>
 struct VecT;
