@@ -422,15 +422,15 @@ __device__ __forceinline__ float dot4(const float4& a, const float4& b) {
 // 0 fetches them with 1-D bulk copies into the warp's own D-stage slot ring;
 // all lanes then read their four dims per row.  Leaves each warp's
 // accumulators in wacc[warp] and its (m, l) per head in wml[warp]; the caller
-// synchronizes before combining them.
+// synchronizes before combining them.  warp, lane and hd are the caller's
+// (computed once per kernel: passing them keeps the caller's registers).
 template <int G, int D>
 __device__ __forceinline__ void attn_chunk_warps(const AttnArgs& A, int z, int h, int t_begin, int t_end,
                                                  int ring_start, unsigned char* ring_smem, uint64_t (*wbar)[D],
-                                                 float (*wacc)[G][128], float (*wml)[G][2], uint32_t& phase) {
+                                                 float (*wacc)[G][128], float (*wml)[G][2], uint32_t& phase,
+                                                 const int warp, const int lane, const int hd) {
     constexpr int TPG = 32 / G;
     constexpr int NW = kAttnThreads / 32;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int hd = A.hd;
     const unsigned FULL = 0xFFFFFFFFu;
     const bool dim_ok = lane * 4 < hd;
     const int my_g = lane / TPG, my_t = lane % TPG;
@@ -626,7 +626,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnAr
         const int t_end = min(len, t_begin + per);
         const int ring_start = plan.start[z];
 
-        attn_chunk_warps<G, D>(A, z, h, t_begin, t_end, ring_start, ring_smem, wbar, wacc, wml, phase);
+        attn_chunk_warps<G, D>(A, z, h, t_begin, t_end, ring_start, ring_smem, wbar, wacc, wml, phase, warp, lane, hd);
         __syncthreads();
         const size_t acc_stride = (size_t)G * hd;
         const size_t ml_base = (size_t)A.n_kv * A.nsplit * acc_stride;
@@ -822,7 +822,8 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_cluster_kernel(const Att
     }
     __syncthreads();
     uint32_t phase = 0;
-    attn_chunk_warps<G, 1>(A, 0, h, range_s[0], range_s[1], range_s[2], ring_smem, wbar, wacc, wml, phase);
+    attn_chunk_warps<G, 1>(A, 0, h, range_s[0], range_s[1], range_s[2], ring_smem, wbar, wacc, wml, phase,
+                           tid >> 5, tid & 31, hd);
     __syncthreads();
 
     // This CTA's partial into the leader's buffer, slot `rank`.
