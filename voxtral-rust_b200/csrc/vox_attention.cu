@@ -807,7 +807,11 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_cluster_kernel(const Att
     // that CTA is running).
     cluster_arrive_relaxed();
     pdl_allow_dependents();
-    pdl_wait_prior_grids();
+    // The ring state is read before the dependency wait: in a step graph only
+    // the o-proj of an earlier step writes it (it commits this layer's append
+    // after this kernel), and consecutive graph launches are fully ordered, so
+    // the value is final.  q and the newest K/V row come from the q|k|v launch
+    // just before and are read after the wait.
     if (tid == 0) {
         KvState st = A.st[0];
         if (A.pre_append) st = kv_after_single_append(st, A.kv_window, A.cap);
@@ -820,6 +824,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_cluster_kernel(const Att
         range_s[1] = min(len, ms + g1 * TPG);
         range_s[2] = st.start;
     }
+    pdl_wait_prior_grids();
     __syncthreads();
     uint32_t phase = 0;
     attn_chunk_warps<G, 1>(A, 0, h, range_s[0], range_s[1], range_s[2], ring_smem, wbar, wacc, wml, phase,

@@ -295,7 +295,9 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 // One stream, short context: one thread-block cluster per kv head merging in
 // distributed shared memory.  attn_cluster_size is 16 or 8 CTAs per kv head,
 // or 0 when this shape or device cannot run it; the host uses it for at most
-// attn_cluster_max_tokens() live tokens.
+// attn_cluster_max_tokens() live tokens.  It reads the ring state before its
+// grid-dependency wait, so no kernel that may still run when it starts may
+// write a.st (true in the step graphs, where only a later o-proj commits it).
 int attn_cluster_size(int n_heads, int n_kv, int hd);
 int attn_cluster_max_tokens();
 cudaError_t launch_attention_cluster(const AttnArgs& a, cudaStream_t s, bool pdl);
