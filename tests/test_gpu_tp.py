@@ -27,7 +27,8 @@ def _port():
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("case,exchange", [("small", "nccl"), ("small", "peer"), ("full", "peer")])
+@pytest.mark.parametrize("case,exchange", [("small", "nccl"), ("small", "peer"), ("full", "peer"),
+                                           ("switch", "peer")])
 def test_tensor_parallel_two_gpus(case, exchange):
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_port()),

@@ -12,11 +12,16 @@ sys.path.insert(0, ROOT)
 
 from tests.vox_testlib import FULL, assert_logits_close, config_dict, oracle_model, top2_margin, vox  # noqa: E402
 
+SMALL = config_dict(dim=256, hidden_dim=512, n_heads=8, n_kv_heads=2, head_dim=32, sliding_window=64,
+                    rope_theta=1e4)
+# (config, layers, vocab, checked steps, prefilled tokens before them)
 CASES = {
     # small shapes, window 64 so the ring evicts during the run
-    "small": (config_dict(dim=256, hidden_dim=512, n_heads=8, n_kv_heads=2, head_dim=32, sliding_window=64,
-                          rope_theta=1e4), 2, 1024, 80),
-    "full": (FULL, 2, 8192, 6),
+    "small": (SMALL, 2, 1024, 80, 0),
+    "full": (FULL, 2, 8192, 6, 0),
+    # past the prompt, the checked steps cross the context at which attention
+    # switches from one cluster per kv head to the split-K kernel (3584 tokens)
+    "switch": (dict(SMALL, sliding_window=8192), 2, 1024, 8, 3578),
 }
 
 
@@ -36,12 +41,12 @@ def main():
     from oracle import oracle as o
     o.build()
     o.set_threads(max(1, (os.cpu_count() or 2) // world))
-    c, n_layers, vocab, n_steps = CASES[args.case]
+    c, n_layers, vocab, n_steps, n_pre = CASES[args.case]
     uid = V.share_tp_unique_id(rank)
     seed = 0
     m = oracle_model(o, c, n_layers, vocab, seed)
     oc = o.RollingKvCache(n_layers, c["n_kv_heads"], c["head_dim"], c["sliding_window"])
-    ids = o.gen_uniform_ids(seed, 3000000, vocab, n_steps)
+    ids = o.gen_uniform_ids(seed, 3000000, vocab, n_pre + n_steps)
     failures = []
     with V.TensorParallelDecoder(V.DecoderConfig(**c), rank, world, uid, n_layers, vocab, device=local) as tp:
         tp.init_random(seed, 0.02)
@@ -50,7 +55,11 @@ def main():
         sh = tp.shard
         lo, hi = sh.vocab_begin, sh.vocab_begin + sh.vocab_local
         worst = 0.0
-        for p in range(n_steps):
+        if n_pre:
+            tp.prefill([int(i) for i in ids[:n_pre]], 0)
+            for p in range(n_pre):
+                m.step(oc, int(ids[p]), p, want_logits=False)
+        for p in range(n_pre, n_pre + n_steps):
             tok, logits = tp.step(int(ids[p]), p, want_logits=True)
             ref_logits, ref_tok = m.step(oc, int(ids[p]), p)
             try:
@@ -65,7 +74,7 @@ def main():
             if (ln, off) != want:
                 failures.append(f"layer {l}: ring state {(ln, off)} != {want}")
         # greedy continuation on the device against the oracle's
-        pos = n_steps
+        pos = n_pre + n_steps
         tok0 = int(ids[-1])
         got = tp.generate(tok0, pos, 3)
         t = tok0

@@ -137,6 +137,7 @@ struct vox_tp {
     std::vector<HostKv> hs;
     GemvPlan p_qkv{}, p_o{}, p_w13{}, p_w2{}, p_head{};
     cudaGraphExec_t graph = nullptr;
+    cudaGraphExec_t graph_short = nullptr;  // same step, cluster attention (short contexts)
     uint64_t graph_kernels = 0, launches = 0;
     StepState* h_steps = nullptr;  // pinned
     size_t h_steps_cap = 0;
@@ -189,7 +190,7 @@ int point_after_o(size_t l) { return (int)(2 * l); }
 int point_after_w2(size_t l) { return (int)(2 * l + 1); }
 
 // One layer (decoder.rs:88-155) on this rank's shard, two all-reduces.
-int enqueue_layer(vox_tp* t, size_t l) {
+int enqueue_layer(vox_tp* t, size_t l, bool short_attn) {
     const TpLayer& L = t->layers[l];
     const vox_tp_shard& s = t->sh;
     float* kr = t->k + l * t->layer_elems();
@@ -244,7 +245,7 @@ int enqueue_layer(vox_tp* t, size_t l) {
     at.out = t->attn;
     at.scale = 1.0f / sqrtf((float)hd);
     at.err = t->err;
-    TP_CUDA(launch_attention(at, t->stream, true));
+    TP_CUDA(short_attn ? launch_attention_cluster(at, t->stream, true) : launch_attention(at, t->stream, true));
 
     // o-proj partial (+ residual on rank 0), commit of the append, all-reduce
     a = base(t);
@@ -309,11 +310,14 @@ int enqueue_head(vox_tp* t) {
     return VOX_OK;
 }
 
-int build_graph(vox_tp* t) {
-    if (t->graph) return VOX_OK;
+// The step as a CUDA graph.  As on one GPU, a second graph runs attention as
+// one thread-block cluster per local kv head for contexts up to
+// attn_cluster_max_tokens(); every rank decodes the same tokens, so every rank
+// picks the same graph and the collectives stay in step.
+int capture_step(vox_tp* t, bool short_attn, cudaGraphExec_t* out) {
     TP_CUDA(cudaStreamBeginCapture(t->stream, cudaStreamCaptureModeThreadLocal));
     int rc = VOX_OK;
-    for (size_t l = 0; l < t->layers.size() && rc == VOX_OK; ++l) rc = enqueue_layer(t, l);
+    for (size_t l = 0; l < t->layers.size() && rc == VOX_OK; ++l) rc = enqueue_layer(t, l, short_attn);
     if (rc == VOX_OK) rc = enqueue_head(t);
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamEndCapture(t->stream, &g);
@@ -322,11 +326,25 @@ int build_graph(vox_tp* t) {
         return rc;
     }
     TP_CUDA(e);
-    e = cudaGraphInstantiate(&t->graph, g, 0);
+    e = cudaGraphInstantiate(out, g, 0);
     cudaGraphDestroy(g);
     TP_CUDA(e);
+    return VOX_OK;
+}
+
+int build_graph(vox_tp* t) {
+    if (t->graph) return VOX_OK;
+    TP_TRY(capture_step(t, false, &t->graph));
+    if (attn_cluster_size((int)t->sh.n_heads, (int)t->sh.n_kv_heads, (int)t->cfg.head_dim) > 0)
+        TP_TRY(capture_step(t, true, &t->graph_short));
     t->graph_kernels = t->layers.size() * 5 + (t->p2p ? 2 : 3);
     return VOX_OK;
+}
+
+void release_graphs(vox_tp* t) {
+    if (t->graph) cudaGraphExecDestroy(t->graph);
+    if (t->graph_short) cudaGraphExecDestroy(t->graph_short);
+    t->graph = t->graph_short = nullptr;
 }
 
 int ready(vox_tp* t) {
@@ -353,8 +371,15 @@ int ensure_host_steps(vox_tp* t, size_t n) {
     return VOX_OK;
 }
 
-int launch_step(vox_tp* t) {
-    TP_CUDA(cudaGraphLaunch(t->graph, t->stream));
+// `steps` = this step's index + 1 in the current call: the attention reads
+// the cache after that many more appends.
+int launch_step(vox_tp* t, size_t steps) {
+    size_t live = 0;
+    for (const HostKv& h : t->hs) live = std::max(live, h.len);
+    live = std::min(live + steps, t->window);
+    if (t->cfg.sliding_window > 0) live = std::min(live, (size_t)t->cfg.sliding_window);
+    const bool use_short = t->graph_short && live <= (size_t)attn_cluster_max_tokens();
+    TP_CUDA(cudaGraphLaunch(use_short ? t->graph_short : t->graph, t->stream));
     t->launches += t->graph_kernels;
     return VOX_OK;
 }
@@ -425,7 +450,7 @@ void vox_tp_destroy(vox_tp* t) {
     if (!t) return;
     cudaSetDevice(t->dev);
     if (t->stream) cudaStreamSynchronize(t->stream);
-    if (t->graph) cudaGraphExecDestroy(t->graph);  // holds NCCL calls: release before the communicator
+    release_graphs(t);  // they hold NCCL calls: release before the communicator
     if (t->comm && t->api) t->api->comm_destroy(t->comm);
     for (unsigned char* m : t->peer_maps)
         if (m) cudaIpcCloseMemHandle(m);
@@ -619,10 +644,7 @@ int vox_tp_connect_peers(vox_tp* t, const unsigned char* handles) {
     }
     TP_CUDA(dalloc(&t->xch_ptrs, (size_t)T));
     TP_CUDA(cudaMemcpy(t->xch_ptrs, ptrs.data(), T * sizeof(unsigned char*), cudaMemcpyHostToDevice));
-    if (t->graph) {  // the next step is captured again with the peer-memory exchange
-        cudaGraphExecDestroy(t->graph);
-        t->graph = nullptr;
-    }
+    release_graphs(t);  // the next step is captured again with the peer-memory exchange
     t->p2p = true;
     return VOX_OK;
 }
@@ -737,7 +759,7 @@ int vox_tp_step(vox_tp* t, int32_t token, size_t pos, int32_t* next_token, float
     hs->pos = (int64_t)pos;
     hs->tok = token;
     TP_CUDA(cudaMemcpyAsync(t->step, hs, sizeof(StepState), cudaMemcpyHostToDevice, t->stream));
-    TP_TRY(launch_step(t));
+    TP_TRY(launch_step(t, 1));
     TP_CUDA(cudaMemcpyAsync(t->h_tok, t->tok_out, 4, cudaMemcpyDeviceToHost, t->stream));
     if (logits_local)
         TP_CUDA(cudaMemcpyAsync(logits_local, t->logits, t->sh.vocab_local * 4, cudaMemcpyDeviceToHost, t->stream));
@@ -763,7 +785,7 @@ int vox_tp_prefill(vox_tp* t, const int32_t* tokens, size_t n, size_t pos0) {
         hs->pos = (int64_t)(pos0 + i);
         hs->tok = tokens[i];
         TP_CUDA(cudaMemcpyAsync(t->step, hs, sizeof(StepState), cudaMemcpyHostToDevice, t->stream));
-        TP_TRY(launch_step(t));
+        TP_TRY(launch_step(t, i + 1));
     }
     TP_TRY(check_errors(t));
     mirror(t, n);
@@ -786,7 +808,7 @@ int vox_tp_generate(vox_tp* t, int32_t token, size_t pos, size_t n_steps, int32_
     TP_CUDA(cudaMemcpyAsync(t->step, hs, sizeof(StepState), cudaMemcpyHostToDevice, t->stream));
     int32_t* hist = reinterpret_cast<int32_t*>(t->h_steps + 1);
     for (size_t i = 0; i < n_steps; ++i) {
-        TP_TRY(launch_step(t));
+        TP_TRY(launch_step(t, i + 1));
         if (tokens_out) TP_CUDA(cudaMemcpyAsync(hist + i, t->tok_out, 4, cudaMemcpyDeviceToHost, t->stream));
     }
     TP_TRY(check_errors(t));
