@@ -27,6 +27,8 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <mutex>
+
 #include "vox_device.cuh"
 
 namespace vox {
@@ -966,9 +968,15 @@ int attn_cluster_size(int n_heads, int n_kv, int hd) {
     const int G = n_kv > 0 ? n_heads / n_kv : 0;
     if (n_kv <= 0 || n_heads % n_kv || (G != 4 && G != 8) || hd % 4 || hd <= 0 || hd > 128) return 0;
     // 16 CTAs per kv head where the device can hold every cluster at once
-    // (a non-portable size), else the portable 8.
-    static int cached[2][129] = {};
-    int& c = cached[G == 8][hd];
+    // (a non-portable size), else the portable 8.  Function attributes belong
+    // to a device, so the answer is kept per device (and per shape).
+    constexpr int kMaxDevices = 64;
+    static std::mutex mu;
+    static int cached[kMaxDevices][2][129] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+    std::lock_guard<std::mutex> lock(mu);
+    int& c = cached[dev][G == 8][hd];
     if (c == 0) {
         c = -1;
         for (int cs : {16, 8}) {
