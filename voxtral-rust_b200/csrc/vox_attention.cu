@@ -125,6 +125,7 @@ __device__ __forceinline__ void load_tile(float* ks, float* vs, const float* kr,
 // per kv head; items are numbered stream-major, then kv head, then chunk.
 struct AttnPlan {
     int len[8], mask_start[8], start[8], tpi[8], items[8], first[9];
+    int firstn[9];  // warp kernel: prefix sums of the chunks that are not a pair's last
 };
 
 template <int VEC>
@@ -597,6 +598,16 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnAr
             first += plan.items[z] * A.n_kv;
         }
         plan.first[B] = first;
+        // Item order: every (stream, kv head)'s chunks but its last, then all
+        // the last chunks.  The last chunks land in the CTAs' final round, so the
+        // merge (run by the chunk that finishes last, normally one of these)
+        // comes after a CTA's own chunks instead of delaying its next one.
+        int fn = 0;
+        for (int z = 0; z < B; ++z) {
+            plan.firstn[z] = fn;
+            fn += (plan.items[z] > 0 ? plan.items[z] - 1 : 0) * A.n_kv;
+        }
+        plan.firstn[B] = fn;
     }
     __syncthreads();
 
@@ -616,12 +627,22 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnAr
     const int total = plan.first[B];
     for (int item = blockIdx.x; item < total; item += gridDim.x) {
         __syncthreads();  // shared partials of the previous chunk are consumed
-        int z = 0;
-        while (z + 1 < B && item >= plan.first[z + 1]) ++z;
+        int z = 0, h, split;
+        if (item < plan.firstn[B]) {  // a chunk other than its pair's last (the pair has >= 2)
+            while (z + 1 < B && item >= plan.firstn[z + 1]) ++z;
+            const int local = item - plan.firstn[z], per_head = plan.items[z] - 1;
+            h = local / per_head;
+            split = local - h * per_head;
+        } else {  // the last chunk of pair j, pairs in (stream, kv head) order
+            int j = item - plan.firstn[B];
+            while (plan.items[z] == 0 || j >= A.n_kv) {
+                if (plan.items[z] > 0) j -= A.n_kv;
+                ++z;
+            }
+            h = j;
+            split = plan.items[z] - 1;
+        }
         const int n_active = plan.items[z];
-        const int local = item - plan.first[z];
-        const int h = local / n_active;
-        const int split = local - h * n_active;
         const int len = plan.len[z];
         const int per = plan.tpi[z] * TPG;
         const int t_begin = plan.mask_start[z] + split * per;
