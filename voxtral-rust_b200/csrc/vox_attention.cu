@@ -568,7 +568,6 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnAr
     if (tid < NW * D) mbar_init(&wbar[tid / D][tid % D], 1);
     if (tid == 0) fence_barrier_init();
     pdl_allow_dependents();
-    pdl_wait_prior_grids();
 
     // Work list (same in every CTA): chunks of gpi groups per warp, i.e.
     // NW * gpi * TPG tokens per CTA chunk, at most nsplit chunks per
@@ -609,6 +608,12 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnAr
         }
         plan.firstn[B] = fn;
     }
+    // The plan above reads the ring states before the dependency wait: they are
+    // written only by the o-proj after this kernel (it commits the layer's
+    // append) and by host-ordered copies and kernels that never let their
+    // dependents start early, so no kernel still running can change them.  q,
+    // the newest K/V row and the output buffer are touched only after the wait.
+    pdl_wait_prior_grids();
     __syncthreads();
 
     if (blockIdx.x == 0)
