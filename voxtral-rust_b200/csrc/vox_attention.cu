@@ -419,6 +419,36 @@ __device__ __forceinline__ float dot4(const float4& a, const float4& b) {
     return fmaf(a.w, b.w, d);
 }
 
+// Bulk copies of group k of `warp` in chunk [t_begin, t_end) (K rows, then V
+// rows, two pieces each at the ring's wrap) into the warp's slot k % D,
+// completing on that slot's mbarrier.  Called by lane 0.
+template <int G, int D>
+__device__ __forceinline__ void attn_issue_group(const AttnArgs& A, int z, int h, int t_begin, int t_end,
+                                                 int ring_start, unsigned char* ring_smem, uint64_t (*wbar)[D],
+                                                 int warp, int k, int hd) {
+    constexpr int TPG = 32 / G;
+    constexpr int NW = kAttnThreads / 32;
+    const size_t row_bytes = (size_t)hd * 4;
+    const uint32_t stage_bytes = (uint32_t)(2 * TPG * row_bytes);
+    const float* kbase = A.k_ring + z * A.ring_stride + (size_t)h * A.cap * hd;
+    const float* vbase = A.v_ring + z * A.ring_stride + (size_t)h * A.cap * hd;
+    const int t0 = t_begin + (warp + NW * k) * TPG;
+    const int ntok = min(TPG, t_end - t0);
+    int slot0 = ring_start + t0;
+    if (slot0 >= A.cap) slot0 -= A.cap;
+    const int n1 = min(ntok, A.cap - slot0);
+    unsigned char* st = ring_smem + ((size_t)warp * D + k % D) * stage_bytes;
+    uint64_t* bar = &wbar[warp][k % D];
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_arrive_expect_tx(bar, (uint32_t)(2 * ntok * row_bytes));
+    bulk_copy_g2s_nohint(st, kbase + (size_t)slot0 * hd, (uint32_t)(n1 * row_bytes), bar);
+    bulk_copy_g2s_nohint(st + TPG * row_bytes, vbase + (size_t)slot0 * hd, (uint32_t)(n1 * row_bytes), bar);
+    if (n1 < ntok) {
+        bulk_copy_g2s_nohint(st + n1 * row_bytes, kbase, (uint32_t)((ntok - n1) * row_bytes), bar);
+        bulk_copy_g2s_nohint(st + TPG * row_bytes + n1 * row_bytes, vbase, (uint32_t)((ntok - n1) * row_bytes), bar);
+    }
+}
+
 // One chunk [t_begin, t_end) of kv head h of stream z, run by every warp of
 // the CTA: warp w takes groups w, w + NW, ... of the chunk.  Each group's K
 // rows and V rows are contiguous in the ring (two pieces at the wrap), so lane
@@ -426,12 +456,14 @@ __device__ __forceinline__ float dot4(const float4& a, const float4& b) {
 // all lanes then read their four dims per row.  Leaves each warp's
 // accumulators in wacc[warp] and its (m, l) per head in wml[warp]; the caller
 // synchronizes before combining them.  warp, lane and hd are the caller's
-// (computed once per kernel: passing them keeps the caller's registers).
+// (computed once per kernel: passing them keeps the caller's registers);
+// pre_issued groups of this warp were already copied by the caller.
 template <int G, int D>
 __device__ __forceinline__ void attn_chunk_warps(const AttnArgs& A, int z, int h, int t_begin, int t_end,
                                                  int ring_start, unsigned char* ring_smem, uint64_t (*wbar)[D],
                                                  float (*wacc)[G][128], float (*wml)[G][2], uint32_t& phase,
-                                                 const int warp, const int lane, const int hd) {
+                                                 const int warp, const int lane, const int hd,
+                                                 const int pre_issued = 0) {
     constexpr int TPG = 32 / G;
     constexpr int NW = kAttnThreads / 32;
     const unsigned FULL = 0xFFFFFFFFu;
@@ -455,25 +487,10 @@ __device__ __forceinline__ void attn_chunk_warps(const AttnArgs& A, int z, int h
     const float* kbase = A.k_ring + z * A.ring_stride + (size_t)h * A.cap * hd;
     const float* vbase = A.v_ring + z * A.ring_stride + (size_t)h * A.cap * hd;
     auto issue = [&](int k) {
-        const int t0 = t_begin + (warp + NW * k) * TPG;
-        const int ntok = min(TPG, t_end - t0);
-        int slot0 = ring_start + t0;
-        if (slot0 >= A.cap) slot0 -= A.cap;
-        const int n1 = min(ntok, A.cap - slot0);
-        unsigned char* st = my_ring + (size_t)(k % D) * stage_bytes;
-        uint64_t* bar = &wbar[warp][k % D];
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_arrive_expect_tx(bar, (uint32_t)(2 * ntok * row_bytes));
-        bulk_copy_g2s_nohint(st, kbase + (size_t)slot0 * hd, (uint32_t)(n1 * row_bytes), bar);
-        bulk_copy_g2s_nohint(st + TPG * row_bytes, vbase + (size_t)slot0 * hd, (uint32_t)(n1 * row_bytes), bar);
-        if (n1 < ntok) {
-            bulk_copy_g2s_nohint(st + n1 * row_bytes, kbase, (uint32_t)((ntok - n1) * row_bytes), bar);
-            bulk_copy_g2s_nohint(st + TPG * row_bytes + n1 * row_bytes, vbase, (uint32_t)((ntok - n1) * row_bytes),
-                                 bar);
-        }
+        attn_issue_group<G, D>(A, z, h, t_begin, t_end, ring_start, ring_smem, wbar, warp, k, hd);
     };
     if (lane == 0)
-        for (int k = 0; k < min(D, n_my); ++k) issue(k);
+        for (int k = pre_issued; k < min(D, n_my); ++k) issue(k);
     __syncwarp();
 
     for (int k = 0; k < n_my; ++k) {
@@ -819,7 +836,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_cluster_kernel(const Att
     __shared__ uint64_t wbar[NW][1];
     __shared__ __align__(16) float wacc[NW][G][HD];
     __shared__ float wml[NW][G][2];
-    __shared__ int range_s[3];  // t_begin, t_end, ring start
+    __shared__ int range_s[4];  // t_begin, t_end, ring start, live length
     const int tid = threadIdx.x;
     const int hd = A.hd, hd4 = hd / 4, n_out = G * hd4;
     const uint32_t rank = cluster_rank();
@@ -851,12 +868,27 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_cluster_kernel(const Att
         range_s[0] = ms + g0 * TPG;
         range_s[1] = min(len, ms + g1 * TPG);
         range_s[2] = st.start;
+        range_s[3] = len;
+    }
+    __syncthreads();
+    // Every K/V row but the one the q|k|v launch just appended (token len - 1,
+    // the end of the newest group) is final: a warp whose first group ends
+    // before it copies that group now, ahead of the dependency wait.
+    int pre = 0;
+    {
+        const int warp = tid >> 5, t0 = range_s[0] + warp * TPG;
+        const int ntok = min(TPG, range_s[1] - t0);
+        if (ntok > 0 && (t0 + ntok < range_s[3] || !A.pre_append)) {
+            if ((tid & 31) == 0)
+                attn_issue_group<G, 1>(A, 0, h, range_s[0], range_s[1], range_s[2], ring_smem, wbar, warp, 0, hd);
+            pre = 1;
+        }
+        __syncwarp();
     }
     pdl_wait_prior_grids();
-    __syncthreads();
     uint32_t phase = 0;
     attn_chunk_warps<G, 1>(A, 0, h, range_s[0], range_s[1], range_s[2], ring_smem, wbar, wacc, wml, phase,
-                           tid >> 5, tid & 31, hd);
+                           tid >> 5, tid & 31, hd, pre);
     __syncthreads();
 
     // This CTA's partial into the leader's buffer, slot `rank`.
