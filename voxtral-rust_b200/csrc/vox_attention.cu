@@ -630,8 +630,47 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnAr
     // append) and by host-ordered copies and kernels that never let their
     // dependents start early, so no kernel still running can change them.  q,
     // the newest K/V row and the output buffer are touched only after the wait.
-    pdl_wait_prior_grids();
     __syncthreads();
+
+    // Item i -> (stream z, kv head h, chunk split): every pair's chunks but
+    // its last, then the last chunks (see the plan above).
+    auto map_item = [&](int item, int& z, int& h, int& split) {
+        z = 0;
+        if (item < plan.firstn[B]) {  // a chunk other than its pair's last (the pair has >= 2)
+            while (z + 1 < B && item >= plan.firstn[z + 1]) ++z;
+            const int local = item - plan.firstn[z], per_head = plan.items[z] - 1;
+            h = local / per_head;
+            split = local - h * per_head;
+        } else {  // the last chunk of pair j, pairs in (stream, kv head) order
+            int j = item - plan.firstn[B];
+            while (plan.items[z] == 0 || j >= A.n_kv) {
+                if (plan.items[z] > 0) j -= A.n_kv;
+                ++z;
+            }
+            h = j;
+            split = plan.items[z] - 1;
+        }
+    };
+    // Every K/V row but the ones the q|k|v launch just appended (token len - 1
+    // of each stream) is final, so each warp copies the first group of this
+    // CTA's first chunk now, ahead of the dependency wait, unless that group
+    // holds the newest token.
+    int pre = 0;
+    if ((int)blockIdx.x < plan.first[B]) {
+        int z, h, split;
+        map_item(blockIdx.x, z, h, split);
+        const int per = plan.tpi[z] * TPG;
+        const int t_begin = plan.mask_start[z] + split * per;
+        const int t_end = min(plan.len[z], t_begin + per);
+        const int t0 = t_begin + warp * TPG, ntok = min(TPG, t_end - t0);
+        if (ntok > 0 && (t0 + ntok < plan.len[z] || !A.pre_append)) {
+            if (lane == 0)
+                attn_issue_group<G, D>(A, z, h, t_begin, t_end, plan.start[z], ring_smem, wbar, warp, 0, hd);
+            pre = 1;
+        }
+        __syncwarp();
+    }
+    pdl_wait_prior_grids();
 
     if (blockIdx.x == 0)
         for (int z = 0; z < B; ++z)
@@ -649,21 +688,8 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnAr
     const int total = plan.first[B];
     for (int item = blockIdx.x; item < total; item += gridDim.x) {
         __syncthreads();  // shared partials of the previous chunk are consumed
-        int z = 0, h, split;
-        if (item < plan.firstn[B]) {  // a chunk other than its pair's last (the pair has >= 2)
-            while (z + 1 < B && item >= plan.firstn[z + 1]) ++z;
-            const int local = item - plan.firstn[z], per_head = plan.items[z] - 1;
-            h = local / per_head;
-            split = local - h * per_head;
-        } else {  // the last chunk of pair j, pairs in (stream, kv head) order
-            int j = item - plan.firstn[B];
-            while (plan.items[z] == 0 || j >= A.n_kv) {
-                if (plan.items[z] > 0) j -= A.n_kv;
-                ++z;
-            }
-            h = j;
-            split = plan.items[z] - 1;
-        }
+        int z, h, split;
+        map_item(item, z, h, split);
         const int n_active = plan.items[z];
         const int len = plan.len[z];
         const int per = plan.tpi[z] * TPG;
@@ -671,7 +697,8 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnAr
         const int t_end = min(len, t_begin + per);
         const int ring_start = plan.start[z];
 
-        attn_chunk_warps<G, D>(A, z, h, t_begin, t_end, ring_start, ring_smem, wbar, wacc, wml, phase, warp, lane, hd);
+        attn_chunk_warps<G, D>(A, z, h, t_begin, t_end, ring_start, ring_smem, wbar, wacc, wml, phase, warp, lane, hd,
+                               item == (int)blockIdx.x ? pre : 0);
         __syncthreads();
         const size_t acc_stride = (size_t)G * hd;
         const size_t ml_base = (size_t)A.n_kv * A.nsplit * acc_stride;
