@@ -879,11 +879,12 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_cluster_kernel(const Att
     // that CTA is running).
     cluster_arrive_relaxed();
     pdl_allow_dependents();
-    // The ring state is read before the dependency wait: in a step graph only
-    // the o-proj of an earlier step writes it (it commits this layer's append
-    // after this kernel), and consecutive graph launches are fully ordered, so
-    // the value is final.  q and the newest K/V row come from the q|k|v launch
-    // just before and are read after the wait.
+    // The ring state is read before the dependency wait.  In a step graph the
+    // only writer is the o-proj launch that commits each layer's append: this
+    // step's runs after this kernel, and earlier steps' finished before this
+    // graph began (consecutive graph launches are fully ordered).  q and the
+    // newest K/V row come from the q|k|v launch just before and are read after
+    // the wait.
     if (tid == 0) {
         KvState st = A.st[0];
         if (A.pre_append) st = kv_after_single_append(st, A.kv_window, A.cap);
