@@ -343,7 +343,14 @@ int vox_softmax_inplace(vox_ctx* ctx, float* x, size_t n);
  * set-up (looks up the array's device address, sets a kernel attribute), so
  * make that first call before any stream capture.  All calls on a device
  * share the array: calls that can overlap on the GPU (other streams, other
- * threads) race and must be serialised by the caller. */
+ * threads) race and must be serialised by the caller.  The array's device
+ * address is looked up once per device: do not use this entry point on a
+ * device after resetting it (cudaDeviceReset).  Errors are reported for the
+ * arguments and for the launch only: the call returns before the kernel
+ * runs, so a bounded wait that expires inside the kernel (the output is then
+ * incomplete) is not reported; use vox_attention_gqa_step where that status
+ * is needed.  A CUDA error already pending on the calling thread is reported
+ * as VOX_ERR_CUDA and nothing is launched. */
 int vox_attention_gqa_step_noalloc(const float* d_query, const float* d_keys,
                                    const float* d_values, const vox_attention_shape* shape,
                                    float* d_out, void* stream);

@@ -113,7 +113,7 @@ int vo_decoder_layer_forward_step(const vo_config* cfg, size_t layer_idx,
                                   const float* hidden, size_t hidden_len,
                                   size_t pos, float* out);
 
-/* ---- composed token loop (not in the reference) -------- */
+/* ---- composed token loop (not in the reference: it has one layer step) */
 typedef struct vo_model {
     vo_config cfg;
     size_t n_layers;

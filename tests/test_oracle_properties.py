@@ -137,3 +137,23 @@ def test_model_step_composes_layer_steps(oracle):
         assert np.array_equal(logits, ref)
         assert am == int(np.argmax(ref))
     assert cache.layer_len_tokens(1) == 4 and cache.layer_pos_offset(1) == 2
+
+
+def test_kv_index_simulation_matches_oracle_cache(oracle):
+    """The index-only restatement of kv.rs:48-88 used by the 16384-step device
+    test agrees with the oracle's kv.rs port on random append sequences."""
+    from tests.vox_testlib import kv_index_after_append
+    rng = np.random.default_rng(5)
+    W = 7
+    oc = oracle.RollingKvCache(1, 1, 2, W)
+    s = (0, 0, 0)
+    for _ in range(300):
+        n = int(rng.integers(0, 10))
+        oc.append_layer(0, np.zeros(n * 2, np.float32), np.zeros(n * 2, np.float32), n)
+        s = kv_index_after_append(*s, n, W, 64)
+        assert (s[0], s[2]) == (oc.layer_len_tokens(0), oc.layer_pos_offset(0))
+    # single-token appends over 3 windows: the ring start is pos_offset mod window
+    s = (0, 0, 0)
+    for i in range(3 * W):
+        s = kv_index_after_append(*s, 1, W, W)
+        assert s == (min(i + 1, W), max(0, i + 1 - W) % W, max(0, i + 1 - W))

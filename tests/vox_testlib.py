@@ -81,3 +81,19 @@ def top2_margin(logits):
     i = int(np.argmax(logits))
     rest = np.delete(logits, i)
     return float(logits[i] - rest.max())
+
+
+def kv_index_after_append(len_tokens, start, pos_offset, n_new, window, cap):
+    """kv.rs:48-88 on indices only: drop = len + n - window (saturating); keep =
+    len - drop (saturating; 0 clears); pos_offset += drop; len += n.  The
+    physical start slot of the device ring advances by the tokens dropped
+    that were present.  Returns (len_tokens, start, pos_offset)."""
+    if n_new == 0:
+        return len_tokens, start, pos_offset
+    drop = max(0, len_tokens + n_new - window)
+    if drop > 0:
+        keep = max(0, len_tokens - drop)
+        start = (start + min(len_tokens, drop)) % cap
+        len_tokens = keep
+        pos_offset += drop
+    return len_tokens + n_new, start, pos_offset

@@ -13,6 +13,9 @@
 // reserved until the process exits.  Every call on a device uses the same
 // array: calls whose kernels can overlap on the GPU (different streams, or
 // different host threads) race on it and must be serialised by the caller.
+// The array's device address is looked up once per device; a caller that
+// resets a device (cudaDeviceReset) must not call this entry point on it
+// afterwards.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -24,10 +27,12 @@ namespace vox {
 
 namespace {
 
-// Fixed scratch: a 256-byte descriptor block, the tickets, then the partials.
+// Fixed scratch: a 256-byte descriptor block (the token-range state at 0, the
+// device error word at kErrOffset), the tickets, then the partials.
 constexpr size_t kNoAllocScratchBytes = size_t(1) << 20;  // 1 MiB per device
 static __device__ __align__(256) unsigned char g_attn_scratch[kNoAllocScratchBytes];
 
+constexpr size_t kErrOffset = 64;
 constexpr size_t kTicketOffset = 256;
 constexpr int kMaxDevices = 64;
 
@@ -43,7 +48,7 @@ DeviceSetup g_setup[kMaxDevices];
 size_t round256(size_t b) { return (b + 255) & ~size_t(255); }
 
 // Writes the token-range descriptor (len = seq_len, start 0) and clears the
-// tickets: the previous call leaves its values behind.
+// error word and the tickets: the previous call leaves its values behind.
 __global__ void noalloc_prepare_kernel(int seq_len, int n_kv) {
     KvState* st = reinterpret_cast<KvState*>(g_attn_scratch);
     unsigned* tickets = reinterpret_cast<unsigned*>(g_attn_scratch + kTicketOffset);
@@ -51,6 +56,7 @@ __global__ void noalloc_prepare_kernel(int seq_len, int n_kv) {
         st->len = seq_len;
         st->start = 0;
         st->pos_offset = 0;
+        *reinterpret_cast<unsigned*>(g_attn_scratch + kErrOffset) = 0u;
     }
     for (int i = threadIdx.x; i < n_kv; i += blockDim.x) tickets[i] = 0u;
 }
@@ -114,6 +120,10 @@ extern "C" int vox_attention_gqa_step_noalloc(const float* d_query, const float*
                             "attention needs more than the 1 MiB no-alloc scratch "
                             "(n_heads * (head_dim + 2) * 4 bytes per split must fit)");
 
+    // An error left by earlier work of the caller is reported as such (and
+    // left in place for the caller), not mistaken for a launch failure here.
+    if (cudaPeekAtLastError() != cudaSuccess)
+        return report_error(VOX_ERR_CUDA, "an earlier CUDA error is pending on this thread; nothing was launched");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     noalloc_prepare_kernel<<<1, 64, 0, st>>>((int)sh->seq_len, (int)nkv);
     if (cudaGetLastError() != cudaSuccess) return report_error(VOX_ERR_CUDA, "prepare launch failed");
@@ -134,8 +144,12 @@ extern "C" int vox_attention_gqa_step_noalloc(const float* d_query, const float*
     at.tickets = reinterpret_cast<unsigned*>(s->scratch + kTicketOffset);
     at.out = d_out;
     at.scale = 1.0f / sqrtf((float)hd);  // ops.rs:89
-    at.err = nullptr;
-    if (launch_attention(at, st, false) != cudaSuccess)
+    // A bounded wait that expires inside the kernel sets a bit here; the call
+    // returns before the kernel runs, so it cannot report it (see the header).
+    at.err = reinterpret_cast<unsigned*>(s->scratch + kErrOffset);
+    if (launch_attention(at, st, false) != cudaSuccess) {
+        (void)cudaGetLastError();
         return report_error(VOX_ERR_CUDA, "attention launch failed");
+    }
     return VOX_OK;
 }
