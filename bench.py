@@ -16,6 +16,12 @@ the total tokens/s of all ranks over the slowest rank's time.
 With N > 1 the ranks then decode one stream together, tensor parallel
 (2048-token context, 1024 greedy steps), reported as "tensor_parallel".
 
+Two more single-stream objects time --ctx-steps greedy steps from a cache
+pre-filled with generator tokens: "long_context" at 1536 tokens (the end
+context of the 512 + 1024-step workload) and "rolling" at the full 8192-token
+window, where every step evicts the oldest token; the rolling object also
+reports the ring state after the run against the kv.rs:48-88 index rule.
+
 The same run then measures the multi-stream workload (8 independent streams
 per GPU, contexts uniform in [256, 4096) with the cache prefilled from
 N(0,1) bf16, greedy decode with tensor-core GEMMs) and reports it as the
@@ -45,6 +51,7 @@ sys.path.insert(0, ROOT)
 DIM, HIDDEN, NH, NKV, HD = 3072, 9216, 32, 8, 128
 LAYERS, VOCAB, WINDOW = 26, 131072, 8192
 PROMPT = 512
+LONG_CONTEXT = 1536
 METRIC = "decoder tokens/s (1 stream per GPU)"
 WORKLOAD = "26-layer decoder token loop, batch 1, prefill 512 random ids then greedy decode, KV window 8192"
 
@@ -115,6 +122,68 @@ class ClockSampler:
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+class NvmlClockSampler:
+    """SM clock and clock-event reasons read through NVML every 2 ms on a
+    thread (read-only queries), so that even a 30 ms timed region gets samples;
+    falls back to the nvidia-smi sampler when NVML is unavailable."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.fallback = None
+        self.samples, self.reasons = [], set()
+        self.max_mhz = 0.0
+        self._stop = None
+        self._thread = None
+
+    def start(self):
+        try:
+            import threading
+
+            import pynvml as N
+            N.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+            idx = int(vis.split(",")[self.gpu]) if vis and vis.split(",")[self.gpu].isdigit() else self.gpu
+            h = N.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = float(N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM))
+            get_reasons = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                N.nvmlDeviceGetCurrentClocksThrottleReasons
+        except Exception:
+            self.fallback = ClockSampler(self.gpu)
+            self.fallback.start()
+            return
+        self._stop = threading.Event()
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append(float(N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)))
+                    bits = int(get_reasons(h))
+                    for b, name in self.REASONS.items():
+                        if bits & b:
+                            self.reasons.add(name)
+                except Exception:
+                    pass
+                self._stop.wait(0.002)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
+
+    def stop(self):
+        if self.fallback is not None:
+            return self.fallback.stop()
+        if self._thread is None:
+            return None
+        self._stop.set()
+        self._thread.join()
+        if not self.samples:
+            return None
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples), "source": "nvml"}
 
 
 # ---------------------------------------------------------------------------
@@ -292,6 +361,47 @@ def run_multi_stream(V, ctx, args, rank, world, dist):
     return {"ms": ms, "steps": steps, "launches": launches, "lens": lens, "ctx_mean": ctx_mean, "e2e_ms": e2e_ms}
 
 
+def run_context(V, ctx, args, rank, dist, fill, steps):
+    """Greedy decode from a cache pre-filled with `fill` generator tokens
+    (N(0,1) rounded to bf16, stored f32) at positions fill.., timed on the
+    device.  With fill = the window every step evicts the oldest token; the
+    ring state of every layer is then checked against kv.rs:48-88 on
+    indices.  Returns the per-rank measurements."""
+    kv = V.RollingKvCache(ctx, LAYERS, NKV, HD, WINDOW)
+    kv.fill_random(fill, 0, 5000000 + 7919 * rank, 1.0)
+    tok = int(prompt_ids(rank + 77, 1)[0])
+    out = ctx.model_generate(kv, tok, fill, args.warmup)
+    tok, pos = int(out[-1]), fill + args.warmup
+    ctx.synchronize()
+    if dist:
+        dist.barrier()
+    launches0 = ctx.kernel_launches()
+    ctx.record_event(8)
+    V.lib().vox_model_generate(ctx.h, kv.h, tok, pos, steps, None)
+    ctx.record_event(9)
+    ctx.synchronize()
+    ms = ctx.elapsed_ms(8, 9)
+    launches = ctx.kernel_launches() - launches0
+    n_app = args.warmup + steps
+    want = (min(fill + n_app, WINDOW), (max(0, fill + n_app - WINDOW)) % WINDOW, max(0, fill + n_app - WINDOW))
+    ring_ok = all(tuple(kv.device_state(l)) == want for l in range(LAYERS))
+    ctx_a, ctx_b = min(pos, WINDOW), min(pos + steps, WINDOW)
+    kv.close()
+    return {"ms": ms, "steps": steps, "launches": launches, "context": [ctx_a, ctx_b], "ring_ok": ring_ok,
+            "ring_state": list(want)}
+
+
+def context_object(run, t_max, world, peak, workload):
+    steps = run["steps"]
+    mean_ctx = sum(run["context"]) / 2
+    gbs = step_bytes(int(mean_ctx)) / (t_max / steps / 1e3) / 1e9
+    return {"metric": "decoder tokens/s (1 stream per GPU)", "value": steps * world / (t_max / 1e3),
+            "unit": "tokens/s", "ms_per_step": t_max / steps, "steps": steps, "context": run["context"],
+            "workload": workload, "bytes_per_step": step_bytes(int(mean_ctx)),
+            "step_roofline": {"achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak},
+            "gpu_launches": run["launches"]}
+
+
 TP_CONTEXT = 2048
 TP_WORKLOAD = ("26-layer decoder, batch 1, tensor parallel over all GPUs (q|k|v, w1|w3 and LM head "
                "column-sharded, o-proj and w2 row-sharded; the 3072-wide residual is all-reduced after "
@@ -337,6 +447,7 @@ def run_ours(args):
                           sliding_window=WINDOW, norm_eps=1e-5, rope_theta=1e6)
     total_pos = PROMPT + args.warmup + 2 * args.steps + 8
     total_pos = max(total_pos, 4096 + args.warmup + args.ms_steps + 72)
+    total_pos = max(total_pos, WINDOW + args.warmup + args.ctx_steps + 8)
     ctx = V.Context(cfg, n_layers=LAYERS, vocab=VOCAB, device=local, max_positions=total_pos)
     ctx.init_random(seed=0, std=0.02)
     kv = V.RollingKvCache(ctx, LAYERS, NKV, HD, WINDOW)
@@ -351,7 +462,7 @@ def run_ours(args):
     ctx.synchronize()
 
     # ---- device-resident timed region ----
-    clocks = ClockSampler(local)
+    clocks = NvmlClockSampler(local)
     clocks.start()
     if dist:
         dist.barrier()
@@ -382,6 +493,8 @@ def run_ours(args):
     # ---- dominant kernel on its own (w1|w3 SwiGLU GEMV, one launch per layer) ----
     k_ms, k_bytes = ctx.profile_gemv(2, LAYERS * 4)
 
+    long_run = None if args.ctx_steps == 0 else run_context(V, ctx, args, rank, dist, LONG_CONTEXT, args.ctx_steps)
+    roll_run = None if args.ctx_steps == 0 else run_context(V, ctx, args, rank, dist, WINDOW, args.ctx_steps)
     ms_run = None if args.ms_steps == 0 else run_multi_stream(V, ctx, args, rank, world, dist)
     tp_run = None
     if world > 1 and args.tp_steps > 0:
@@ -389,16 +502,22 @@ def run_ours(args):
         tp_run = run_tensor_parallel(V, args, rank, world, local, dist)
 
     t_max, e2e_max = ms, e2e_ms
-    ms_max = ms_e2e_max = tp_max = 0.0
+    ms_max = ms_e2e_max = tp_max = long_max = roll_max = 0.0
     if ms_run:
         ms_max, ms_e2e_max = ms_run["ms"], ms_run["e2e_ms"]
     if tp_run:
         tp_max = tp_run["ms"]
+    if long_run:
+        long_max, roll_max = long_run["ms"], roll_run["ms"]
     if dist:
         import torch
-        t = torch.tensor([ms, e2e_ms, ms_max, ms_e2e_max, tp_max], dtype=torch.float64)
+        t = torch.tensor([ms, e2e_ms, ms_max, ms_e2e_max, tp_max, long_max, roll_max], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_max, e2e_max, ms_max, ms_e2e_max, tp_max = (float(x) for x in t)
+        t_max, e2e_max, ms_max, ms_e2e_max, tp_max, long_max, roll_max = (float(x) for x in t)
+        if roll_run:
+            ok = torch.tensor([1.0 if roll_run["ring_ok"] and long_run["ring_ok"] else 0.0])
+            dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+            roll_run["ring_ok"] = long_run["ring_ok"] = bool(ok.item() > 0)
     if rank != 0:
         if dist:
             dist.barrier()
@@ -429,6 +548,19 @@ def run_ours(args):
         "step_roofline": {"achieved": step_gbs, "peak": peak, "unit": "GB/s", "frac": step_gbs / peak},
         "clocks": clk,
     }
+    if long_run:
+        line["long_context"] = context_object(
+            long_run, long_max, world, peak,
+            f"as the headline line, cache pre-filled to {LONG_CONTEXT} tokens (the end context of the "
+            f"512 + 1024-step run), greedy decode")
+        line["rolling"] = context_object(
+            roll_run, roll_max, world, peak,
+            f"rolling-window stress: cache pre-filled to the full {WINDOW}-token window, greedy decode, "
+            f"every step evicts the oldest token (ring index arithmetic, no copy)")
+        line["rolling"]["ring_state_after"] = {"len_tokens": roll_run["ring_state"][0],
+                                               "start": roll_run["ring_state"][1],
+                                               "pos_offset": roll_run["ring_state"][2],
+                                               "matches_kv_rs_index_rule": roll_run["ring_ok"]}
     if ms_run:
         n_tok = ms_run["steps"] * MS_STREAMS * world
         ms_bytes = (LAYERS * LAYER_WEIGHT_BYTES + HEAD_BYTES + MS_STREAMS * EMBED_ROW_BYTES +
@@ -472,6 +604,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--cpu-layer-steps", type=int, default=24)
+    ap.add_argument("--ctx-steps", type=int, default=256,
+                    help="greedy steps of the long-context (1536) and full-window rolling runs (0 skips them)")
     ap.add_argument("--ms-steps", type=int, default=512,
                     help="greedy steps of the 8-streams-per-GPU run (0 skips it)")
     ap.add_argument("--tp-steps", type=int, default=1024,

@@ -282,6 +282,73 @@ int vox_tp_kv_state(const vox_tp* tp, size_t layer, int64_t out[3]);
 int vox_tp_record_event(vox_tp* tp, int slot);  /* slots 0..7 */
 int vox_tp_event_elapsed_ms(vox_tp* tp, int slot_a, int slot_b, float* ms);
 uint64_t vox_tp_kernel_launches(const vox_tp* tp);
+/* ---- streaming decode driver (stream.rs, pipeline.rs) ---------------------------- */
+/* StreamPromptConfig (stream.rs:4-9). */
+typedef struct vox_stream_prompt_config {
+    size_t left_pad_tokens;
+    size_t delay_tokens;
+    size_t eos_extra_tokens;
+} vox_stream_prompt_config;
+/* StreamPromptConfig::default (stream.rs:11-19): 32 / 6 / 10. */
+void vox_stream_prompt_config_default(vox_stream_prompt_config* out);
+/* StreamPromptConfig::right_pad_tokens (stream.rs:21-25). */
+size_t vox_stream_right_pad_tokens(const vox_stream_prompt_config* cfg);
+/* build_prompt_ids (stream.rs:26-34): [bos] + [pad] * (left_pad + delay).
+ * Returns the prompt length and writes at most cap ids (out nullable). */
+size_t vox_stream_build_prompt_ids(uint32_t bos_id, uint32_t streaming_pad_id,
+                                   const vox_stream_prompt_config* cfg, uint32_t* out, size_t cap);
+/* decode_ready (stream.rs:36-38) and decodable_token_budget (stream.rs:47-53). */
+int vox_stream_decode_ready(size_t total_adapter_tokens, size_t prompt_len);
+size_t vox_stream_decodable_token_budget(size_t total_adapter_tokens, size_t prompt_len);
+/* finish_zero_padding_samples (stream.rs:60-69); 0 if samples_per_token is 0. */
+size_t vox_stream_finish_zero_padding_samples(size_t consumed_samples, size_t samples_per_token,
+                                              const vox_stream_prompt_config* cfg);
+
+/* PipelineConfig (pipeline.rs:12-18). */
+typedef struct vox_pipeline_config {
+    uint32_t bos_id;
+    uint32_t streaming_pad_id;
+    size_t samples_per_token;
+    vox_stream_prompt_config prompt;
+} vox_pipeline_config;
+/* PipelineState (pipeline.rs:28-90) driving the token loop.  With ctx and kv
+ * NULL it is the reference's planner only (push / decodable_now /
+ * mark_decoded / finish_padding_samples).  With a context and a
+ * single-stream cache it also decodes on the device: adapter rows pushed
+ * with vox_pipeline_push_adapter_tokens go to a device ring of
+ * adapter_capacity positions (>= the prompt length), and
+ * vox_pipeline_decode runs the schedule of the design document
+ * (docs/plans/2026-02-11-voxtral-rust-design.md:40-46): with a prompt of L
+ * ids, positions 0..L-2 are prefilled with adapter[p] + tok_embed(prompt[p]),
+ * position L-1 yields the first token, and every later position p feeds
+ * adapter[p] + tok_embed(previous token), greedy, on the device.  Destroy a
+ * pipeline before its cache and context. */
+typedef struct vox_pipeline vox_pipeline;
+int vox_pipeline_create(vox_ctx* ctx, vox_kv* kv, const vox_pipeline_config* cfg, size_t adapter_capacity,
+                        vox_pipeline** out);
+void vox_pipeline_destroy(vox_pipeline* p);
+/* PipelineState::prompt_ids: returns the length, writes at most cap ids. */
+size_t vox_pipeline_prompt_ids(const vox_pipeline* p, uint32_t* out, size_t cap);
+size_t vox_pipeline_adapter_tokens_total(const vox_pipeline* p);   /* pipeline.rs:54 */
+size_t vox_pipeline_generated_tokens(const vox_pipeline* p);       /* pipeline.rs:58 */
+size_t vox_pipeline_decodable_now(const vox_pipeline* p);          /* pipeline.rs:68-71 */
+int vox_pipeline_is_finished(const vox_pipeline* p);               /* pipeline.rs:87 */
+/* push_adapter_tokens (pipeline.rs:62-67).  rows [n_tokens, dim] f32 host
+ * memory (NULL allowed for a planner-only pipeline).  VOX_ERR_RANGE if the
+ * ring would overwrite positions not yet handed to vox_pipeline_decode. */
+int vox_pipeline_push_adapter_tokens(vox_pipeline* p, const float* rows, size_t n_tokens);
+/* mark_decoded (pipeline.rs:73-76), planner-only pipelines: a pipeline with a
+ * context counts the tokens vox_pipeline_decode produces itself.
+ * VOX_ERR_INVALID_ARG when n_tokens > decodable_now (the reference's
+ * debug_assert). */
+int vox_pipeline_mark_decoded(vox_pipeline* p, size_t n_tokens);
+/* Decode min(max_tokens, decodable_now) tokens on the device (the first call
+ * also prefills the prompt); tokens_out receives them, *n_out their count. */
+int vox_pipeline_decode(vox_pipeline* p, size_t max_tokens, int32_t* tokens_out, size_t* n_out);
+/* finish_padding_samples (pipeline.rs:78-85): marks the pipeline finished and
+ * returns the zero samples to append. */
+size_t vox_pipeline_finish_padding_samples(vox_pipeline* p, size_t consumed_audio_samples);
+
 /* ---- profiling hook (no reference counterpart) --------------------------------- */
 /* Times one of the step's weight-streaming GEMVs on its own: n_launches
  * back-to-back launches (cycling over the layers, so every launch streams a

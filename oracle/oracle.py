@@ -14,6 +14,7 @@ import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB_PATH = os.path.join(_HERE, "_build", "libvoxoracle.so")
+
 _lib = None
 
 F32P = C.POINTER(C.c_float)
@@ -48,6 +49,18 @@ class VoModel(C.Structure):
         ("layers", C.POINTER(VoLayerWeights)), ("embed", U16P),
         ("final_norm", F32P), ("lm_head", U16P),
     ]
+
+
+class VoStreamPromptConfig(C.Structure):
+    """StreamPromptConfig (stream.rs:4-9)."""
+
+    _fields_ = [("left_pad_tokens", SZ), ("delay_tokens", SZ), ("eos_extra_tokens", SZ)]
+
+
+class VoPipeline(C.Structure):
+    _fields_ = [("bos_id", C.c_uint32), ("streaming_pad_id", C.c_uint32), ("samples_per_token", SZ),
+                ("prompt", VoStreamPromptConfig), ("prompt_len", SZ), ("adapter_tokens_total", SZ),
+                ("generated_tokens", SZ), ("finished", C.c_int)]
 
 
 def build():
@@ -88,6 +101,25 @@ def lib():
         L.vo_decoder_layer_forward_step.argtypes = [
             C.POINTER(VoConfig), SZ, C.POINTER(VoLayerWeights), C.c_void_p, F32P, SZ, SZ, F32P]
         L.vo_model_step.argtypes = [C.POINTER(VoModel), C.c_void_p, C.c_int32, SZ, F32P, I32P]
+        L.vo_model_step_adapter.argtypes = [C.POINTER(VoModel), C.c_void_p, C.c_int32, F32P, SZ, F32P, I32P]
+        L.vo_stream_right_pad_tokens.argtypes = [C.POINTER(VoStreamPromptConfig)]
+        L.vo_stream_right_pad_tokens.restype = SZ
+        L.vo_stream_build_prompt_ids.argtypes = [C.c_uint32, C.c_uint32, C.POINTER(VoStreamPromptConfig),
+                                                 C.POINTER(C.c_uint32), SZ]
+        L.vo_stream_build_prompt_ids.restype = SZ
+        L.vo_stream_decode_ready.argtypes = [SZ, SZ]
+        L.vo_stream_decodable_token_budget.argtypes = [SZ, SZ]
+        L.vo_stream_decodable_token_budget.restype = SZ
+        L.vo_stream_finish_zero_padding_samples.argtypes = [SZ, SZ, C.POINTER(VoStreamPromptConfig)]
+        L.vo_stream_finish_zero_padding_samples.restype = SZ
+        L.vo_pipeline_init.argtypes = [C.POINTER(VoPipeline), C.c_uint32, C.c_uint32, SZ,
+                                       C.POINTER(VoStreamPromptConfig)]
+        L.vo_pipeline_push_adapter_tokens.argtypes = [C.POINTER(VoPipeline), SZ]
+        L.vo_pipeline_decodable_now.argtypes = [C.POINTER(VoPipeline)]
+        L.vo_pipeline_decodable_now.restype = SZ
+        L.vo_pipeline_mark_decoded.argtypes = [C.POINTER(VoPipeline), SZ]
+        L.vo_pipeline_finish_padding_samples.argtypes = [C.POINTER(VoPipeline), SZ]
+        L.vo_pipeline_finish_padding_samples.restype = SZ
         L.vo_gen_normal_f32.argtypes = [C.c_uint64, C.c_uint64, C.c_float, C.c_uint64, SZ, F32P]
         L.vo_gen_normal_bf16.argtypes = [C.c_uint64, C.c_uint64, C.c_float, C.c_uint64, SZ, U16P]
         L.vo_gen_uniform_ids.argtypes = [C.c_uint64, C.c_uint64, C.c_uint32, C.c_uint64, SZ, I32P]
@@ -294,6 +326,103 @@ class Model:
         if rc:
             raise ValueError(f"oracle model step failed with code {rc}")
         return logits, am.value
+
+
+    def step_adapter(self, cache, token, adapter_row, pos, want_logits=True):
+        """Streaming input: x = adapter_row + tok_embed(token)."""
+        logits = np.zeros(self.vocab, np.float32) if want_logits else None
+        am = C.c_int32(-1)
+        row = _f32(adapter_row)
+        rc = lib().vo_model_step_adapter(C.byref(self.c), cache.h, int(token), _p(row), int(pos),
+                                         _p(logits) if want_logits else None, C.byref(am))
+        if rc:
+            raise ValueError(f"oracle adapter step failed with code {rc}")
+        return logits, am.value
+
+    def stream_decode(self, cache, prompt_ids, adapter, n_tokens, generated=(), want_logits=False):
+        """The streaming schedule of docs/plans/2026-02-11-voxtral-rust-design.md:40-46
+        composed over the layer step.  With L = len(prompt_ids) and no token
+        generated yet: positions 0..L-2 are prefilled with adapter[p] +
+        tok_embed(prompt[p]); position L-1 takes adapter[L-1] +
+        tok_embed(prompt[L-1]) and yields the first token; every later
+        position p takes adapter[p] + tok_embed(previous token).  `generated`
+        lists tokens produced by earlier calls on the same cache.  Returns the
+        next n_tokens greedy tokens (and their logits if asked)."""
+        L = len(prompt_ids)
+        adapter = np.asarray(adapter, np.float32)
+        done = len(generated)
+        out, lg = [], []
+        if done == 0 and n_tokens > 0:
+            for p in range(L - 1):
+                self.step_adapter(cache, int(prompt_ids[p]), adapter[p], p, want_logits=False)
+        prev = int(prompt_ids[L - 1]) if done == 0 else int(generated[-1])
+        for i in range(n_tokens):
+            pos = L - 1 + done + i
+            logits, prev = self.step_adapter(cache, prev, adapter[pos], pos, want_logits=want_logits)
+            out.append(prev)
+            lg.append(logits)
+        return (out, lg) if want_logits else out
+
+
+# ---- streaming schedule (stream.rs, pipeline.rs) -------------------------------
+
+def stream_prompt_config(left_pad_tokens=32, delay_tokens=6, eos_extra_tokens=10):
+    """StreamPromptConfig; the defaults are StreamPromptConfig::default (stream.rs:11-19)."""
+    return VoStreamPromptConfig(left_pad_tokens, delay_tokens, eos_extra_tokens)
+
+
+def stream_right_pad_tokens(cfg):
+    return lib().vo_stream_right_pad_tokens(C.byref(cfg))
+
+
+def stream_build_prompt_ids(bos_id, pad_id, cfg):
+    n = lib().vo_stream_build_prompt_ids(bos_id, pad_id, C.byref(cfg), None, 0)
+    out = (C.c_uint32 * max(n, 1))()
+    lib().vo_stream_build_prompt_ids(bos_id, pad_id, C.byref(cfg), out, n)
+    return [int(out[i]) for i in range(n)]
+
+
+def stream_decode_ready(total, prompt_len):
+    return bool(lib().vo_stream_decode_ready(total, prompt_len))
+
+
+def stream_decodable_token_budget(total, prompt_len):
+    return lib().vo_stream_decodable_token_budget(total, prompt_len)
+
+
+def stream_finish_zero_padding_samples(consumed, samples_per_token, cfg):
+    return lib().vo_stream_finish_zero_padding_samples(consumed, samples_per_token, C.byref(cfg))
+
+
+class PipelineState:
+    """PipelineState (pipeline.rs:28-90), planner only."""
+
+    def __init__(self, bos_id, streaming_pad_id, samples_per_token, prompt_cfg):
+        self.c = VoPipeline()
+        lib().vo_pipeline_init(C.byref(self.c), bos_id, streaming_pad_id, samples_per_token, C.byref(prompt_cfg))
+        self.prompt_ids = stream_build_prompt_ids(bos_id, streaming_pad_id, prompt_cfg)
+
+    def adapter_tokens_total(self):
+        return self.c.adapter_tokens_total
+
+    def generated_tokens(self):
+        return self.c.generated_tokens
+
+    def push_adapter_tokens(self, n):
+        lib().vo_pipeline_push_adapter_tokens(C.byref(self.c), n)
+
+    def decodable_now(self):
+        return lib().vo_pipeline_decodable_now(C.byref(self.c))
+
+    def mark_decoded(self, n):
+        if lib().vo_pipeline_mark_decoded(C.byref(self.c), n):
+            raise ValueError("mark_decoded beyond decodable_now")
+
+    def finish_padding_samples(self, consumed):
+        return lib().vo_pipeline_finish_padding_samples(C.byref(self.c), consumed)
+
+    def is_finished(self):
+        return bool(self.c.finished)
 
 
 # ---- seeded synthetic data ---------------------------------------------------

@@ -408,14 +408,12 @@ int vo_decoder_layer_forward_step(const vo_config* cfg, size_t layer_idx,
  * absolute position; final RMSNorm (gain final_norm, eps norm_eps);
  * logits = linear(x, lm_head); argmax with the lowest index winning ties.
  * ====================================================================== */
-int vo_model_step(const vo_model* m, vo_kv* cache, int32_t token, size_t pos,
-                  float* logits_out, int32_t* argmax_out) {
+/* Layers, final norm, LM head and argmax from the input vector x (consumed). */
+static int model_forward(const vo_model* m, vo_kv* cache, float* x, size_t pos,
+                         float* logits_out, int32_t* argmax_out) {
     const vo_config* cfg = &m->cfg;
     size_t dim = cfg->dim;
-    if (token < 0 || (size_t)token >= m->vocab) return VO_ERR_ARG;
-    float* x = (float*)malloc(dim * sizeof(float));
     float* y = (float*)malloc(dim * sizeof(float));
-    for (size_t i = 0; i < dim; ++i) x[i] = bf16_to_f32(m->embed[(size_t)token * dim + i]);
     for (size_t l = 0; l < m->n_layers; ++l) {
         int rc = vo_decoder_layer_forward_step(cfg, l, &m->layers[l], cache, x, dim, pos, y);
         if (rc) { free(x); free(y); return rc; }
@@ -433,6 +431,102 @@ int vo_model_step(const vo_model* m, vo_kv* cache, int32_t token, size_t pos,
     if (!logits_out) free(logits);
     free(x); free(y);
     return VO_OK;
+}
+
+int vo_model_step(const vo_model* m, vo_kv* cache, int32_t token, size_t pos,
+                  float* logits_out, int32_t* argmax_out) {
+    size_t dim = m->cfg.dim;
+    if (token < 0 || (size_t)token >= m->vocab) return VO_ERR_ARG;
+    float* x = (float*)malloc(dim * sizeof(float));
+    for (size_t i = 0; i < dim; ++i) x[i] = bf16_to_f32(m->embed[(size_t)token * dim + i]);
+    return model_forward(m, cache, x, pos, logits_out, argmax_out);
+}
+
+/* Streaming input (docs/plans/2026-02-11-voxtral-rust-design.md:40-46): the
+ * decoder input at an adapter position is adapter[pos] + tok_embed(token),
+ * one f32 addition per element. */
+int vo_model_step_adapter(const vo_model* m, vo_kv* cache, int32_t token,
+                          const float* adapter_row, size_t pos,
+                          float* logits_out, int32_t* argmax_out) {
+    size_t dim = m->cfg.dim;
+    if (token < 0 || (size_t)token >= m->vocab || !adapter_row) return VO_ERR_ARG;
+    float* x = (float*)malloc(dim * sizeof(float));
+    for (size_t i = 0; i < dim; ++i)
+        x[i] = adapter_row[i] + bf16_to_f32(m->embed[(size_t)token * dim + i]);
+    return model_forward(m, cache, x, pos, logits_out, argmax_out);
+}
+
+/* ======================================================================
+ * stream.rs / pipeline.rs: the streaming schedule (integer bookkeeping).
+ * ====================================================================== */
+
+/* StreamPromptConfig::right_pad_tokens (stream.rs:21-25). */
+size_t vo_stream_right_pad_tokens(const vo_stream_prompt_config* c) {
+    return c->delay_tokens + 1 + c->eos_extra_tokens;
+}
+
+/* build_prompt_ids (stream.rs:26-34): [bos] + [pad] * (left_pad + delay).
+ * Returns the prompt length; writes at most cap ids. */
+size_t vo_stream_build_prompt_ids(uint32_t bos_id, uint32_t pad_id,
+                                  const vo_stream_prompt_config* c,
+                                  uint32_t* out, size_t cap) {
+    size_t n = 1 + c->left_pad_tokens + c->delay_tokens;
+    for (size_t i = 0; i < n && i < cap; ++i) out[i] = i == 0 ? bos_id : pad_id;
+    return n;
+}
+
+/* decode_ready (stream.rs:36-38). */
+int vo_stream_decode_ready(size_t total_adapter_tokens, size_t prompt_len) {
+    return total_adapter_tokens >= prompt_len;
+}
+
+/* decodable_token_budget (stream.rs:47-53): N - L + 1 when N >= L, else 0. */
+size_t vo_stream_decodable_token_budget(size_t total_adapter_tokens, size_t prompt_len) {
+    return total_adapter_tokens < prompt_len ? 0 : total_adapter_tokens - prompt_len + 1;
+}
+
+/* finish_zero_padding_samples (stream.rs:60-69): align to the token
+ * boundary, then (delay + 1 + eos_extra) token steps of zeros. */
+size_t vo_stream_finish_zero_padding_samples(size_t consumed_samples, size_t samples_per_token,
+                                             const vo_stream_prompt_config* c) {
+    if (samples_per_token == 0) return 0;
+    size_t rem = consumed_samples % samples_per_token;
+    size_t align = rem == 0 ? 0 : samples_per_token - rem;
+    return align + vo_stream_right_pad_tokens(c) * samples_per_token;
+}
+
+/* PipelineState (pipeline.rs:28-90). */
+void vo_pipeline_init(vo_pipeline* p, uint32_t bos_id, uint32_t pad_id, size_t samples_per_token,
+                      const vo_stream_prompt_config* prompt) {
+    p->bos_id = bos_id;
+    p->streaming_pad_id = pad_id;
+    p->samples_per_token = samples_per_token;
+    p->prompt = *prompt;
+    p->prompt_len = 1 + prompt->left_pad_tokens + prompt->delay_tokens;
+    p->adapter_tokens_total = 0;
+    p->generated_tokens = 0;
+    p->finished = 0;
+}
+
+void vo_pipeline_push_adapter_tokens(vo_pipeline* p, size_t n_tokens) {
+    p->adapter_tokens_total += n_tokens;  /* pipeline.rs:62-67 */
+}
+
+size_t vo_pipeline_decodable_now(const vo_pipeline* p) {
+    size_t total = vo_stream_decodable_token_budget(p->adapter_tokens_total, p->prompt_len);
+    return total > p->generated_tokens ? total - p->generated_tokens : 0;  /* saturating_sub */
+}
+
+/* pipeline.rs:73-76; the reference debug_asserts n <= decodable_now. */
+int vo_pipeline_mark_decoded(vo_pipeline* p, size_t n_tokens) {
+    if (n_tokens > vo_pipeline_decodable_now(p)) return VO_ERR_ARG;
+    p->generated_tokens += n_tokens;
+    return VO_OK;
+}
+
+size_t vo_pipeline_finish_padding_samples(vo_pipeline* p, size_t consumed_audio_samples) {
+    p->finished = 1;
+    return vo_stream_finish_zero_padding_samples(consumed_audio_samples, p->samples_per_token, &p->prompt);
 }
 
 /* ======================================================================

@@ -126,6 +126,43 @@ typedef struct vo_model {
 
 int vo_model_step(const vo_model* m, vo_kv* cache, int32_t token, size_t pos,
                   float* logits_out, int32_t* argmax_out);
+/* Streaming input: x = adapter_row + widen(embed[token]) (design doc :40-46). */
+int vo_model_step_adapter(const vo_model* m, vo_kv* cache, int32_t token,
+                          const float* adapter_row, size_t pos,
+                          float* logits_out, int32_t* argmax_out);
+
+/* ---- streaming schedule (stream.rs, pipeline.rs) ------------------------ */
+typedef struct vo_stream_prompt_config {   /* StreamPromptConfig (stream.rs:4-9) */
+    size_t left_pad_tokens;
+    size_t delay_tokens;
+    size_t eos_extra_tokens;
+} vo_stream_prompt_config;
+
+size_t vo_stream_right_pad_tokens(const vo_stream_prompt_config* c);
+size_t vo_stream_build_prompt_ids(uint32_t bos_id, uint32_t pad_id,
+                                  const vo_stream_prompt_config* c,
+                                  uint32_t* out, size_t cap);
+int vo_stream_decode_ready(size_t total_adapter_tokens, size_t prompt_len);
+size_t vo_stream_decodable_token_budget(size_t total_adapter_tokens, size_t prompt_len);
+size_t vo_stream_finish_zero_padding_samples(size_t consumed_samples, size_t samples_per_token,
+                                             const vo_stream_prompt_config* c);
+
+typedef struct vo_pipeline {               /* PipelineState (pipeline.rs:28-35) */
+    uint32_t bos_id, streaming_pad_id;
+    size_t samples_per_token;
+    vo_stream_prompt_config prompt;
+    size_t prompt_len;
+    size_t adapter_tokens_total;
+    size_t generated_tokens;
+    int finished;
+} vo_pipeline;
+
+void vo_pipeline_init(vo_pipeline* p, uint32_t bos_id, uint32_t pad_id, size_t samples_per_token,
+                      const vo_stream_prompt_config* prompt);
+void vo_pipeline_push_adapter_tokens(vo_pipeline* p, size_t n_tokens);
+size_t vo_pipeline_decodable_now(const vo_pipeline* p);
+int vo_pipeline_mark_decoded(vo_pipeline* p, size_t n_tokens);
+size_t vo_pipeline_finish_padding_samples(vo_pipeline* p, size_t consumed_audio_samples);
 
 /* ---- seeded synthetic data (counter-based, bit-exact on any IEEE target) */
 void vo_gen_normal_f32(uint64_t seed, uint64_t tensor_id, float std_scale,

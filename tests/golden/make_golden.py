@@ -13,6 +13,10 @@ text and re-run against the oracle and the CUDA library):
   kv.rs:109-136    compacts_when_exceeding_window
   kv.rs:139-151    layers_are_isolated
   decoder.rs:185-214 decoder_step_grows_and_compacts_cache (LCG seed 7, x0.05)
+  stream.rs:78-91   prompt_and_budget_formulas_match_reference_schedule
+  stream.rs:93-102  finish_padding_matches_alignment_plus_right_budget
+  pipeline.rs:99-130  planner_tracks_budget_across_chunks
+  pipeline.rs:132-144 planner_finish_padding_formula
 
 The 32-bit LCG below is the one the reference tests use
 (seed = seed*1664525 + 1013904223; value = (seed>>8)/2^24*2-1, in f32).
@@ -171,6 +175,37 @@ def reference_unit_tests():
         "config": cfg, "weights": {k_: v_.tolist() for k_, v_ in w.items()},
         "steps": 6, "hidden_rule": "hidden[i] = pos*0.1 + i*0.01 (f32), rewritten before every step",
         "expect_len": 4, "expect_pos_offset": 2,
+    }
+    # stream.rs:78-91 (default StreamPromptConfig: left pad 32, delay 6, eos extra 10)
+    tests["prompt_and_budget_formulas_match_reference_schedule"] = {
+        "cite": "crates/voxtral/src/stream.rs:78-91",
+        "bos_id": 1, "streaming_pad_id": 32, "prompt": {"left_pad_tokens": 32, "delay_tokens": 6,
+                                                        "eos_extra_tokens": 10},
+        "expect_prompt_len": 1 + 32 + 6, "expect_first": 1, "expect_rest": 32,
+        # (total adapter tokens relative to the prompt length, decode_ready, budget)
+        "budget_cases": [[-1, False, 0], [0, True, 1], [9, None, 10]],
+    }
+    # stream.rs:93-102
+    tests["finish_padding_matches_alignment_plus_right_budget"] = {
+        "cite": "crates/voxtral/src/stream.rs:93-102",
+        "consumed": 3 * 1280 + 640, "samples_per_token": 1280, "expect": 640 + 17 * 1280,
+    }
+    # pipeline.rs:99-130: a sequence of (op, argument, expected) on one PipelineState
+    tests["planner_tracks_budget_across_chunks"] = {
+        "cite": "crates/voxtral/src/pipeline.rs:99-130",
+        "bos_id": 1, "streaming_pad_id": 32, "samples_per_token": 1280,
+        "expect_prompt_len": 39,
+        "ops": [["decodable_now", None, 0], ["push", 20, None], ["decodable_now", None, 0],
+                ["push", 19, None], ["adapter_tokens_total", None, 39], ["decodable_now", None, 1],
+                ["mark_decoded", 1, None], ["generated_tokens", None, 1], ["decodable_now", None, 0],
+                ["push", 10, None], ["decodable_now", None, 10], ["mark_decoded", 7, None],
+                ["decodable_now", None, 3]],
+    }
+    # pipeline.rs:132-144
+    tests["planner_finish_padding_formula"] = {
+        "cite": "crates/voxtral/src/pipeline.rs:132-144",
+        "bos_id": 1, "streaming_pad_id": 32, "samples_per_token": 1280,
+        "consumed": 3 * 1280 + 640, "expect": 640 + 17 * 1280, "expect_finished": True,
     }
     return tests
 

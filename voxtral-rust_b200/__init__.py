@@ -95,6 +95,26 @@ class AttentionShape(C.Structure):
                 ("sliding_window", SZ)]
 
 
+class StreamPromptConfig(C.Structure):
+    """StreamPromptConfig (stream.rs:4-9); StreamPromptConfig() is the default 32/6/10."""
+
+    _fields_ = [("left_pad_tokens", SZ), ("delay_tokens", SZ), ("eos_extra_tokens", SZ)]
+
+    def __init__(self, left_pad_tokens=32, delay_tokens=6, eos_extra_tokens=10):
+        super().__init__(left_pad_tokens, delay_tokens, eos_extra_tokens)
+
+    def right_pad_tokens(self):
+        """StreamPromptConfig::right_pad_tokens (stream.rs:21-25)."""
+        return int(lib().vox_stream_right_pad_tokens(C.byref(self)))
+
+
+class PipelineConfig(C.Structure):
+    """PipelineConfig (pipeline.rs:12-18)."""
+
+    _fields_ = [("bos_id", C.c_uint32), ("streaming_pad_id", C.c_uint32), ("samples_per_token", SZ),
+                ("prompt", StreamPromptConfig)]
+
+
 _lib = None
 
 _SIGS = {
@@ -166,6 +186,24 @@ _SIGS = {
     "vox_silu_inplace": ([VP, F32P, SZ], C.c_int),
     "vox_softmax_inplace": ([VP, F32P, SZ], C.c_int),
     "vox_attention_gqa_step_noalloc": ([VP, VP, VP, C.POINTER(AttentionShape), VP, VP], C.c_int),
+    "vox_stream_prompt_config_default": ([C.POINTER(StreamPromptConfig)], None),
+    "vox_stream_right_pad_tokens": ([C.POINTER(StreamPromptConfig)], SZ),
+    "vox_stream_build_prompt_ids": ([C.c_uint32, C.c_uint32, C.POINTER(StreamPromptConfig),
+                                     C.POINTER(C.c_uint32), SZ], SZ),
+    "vox_stream_decode_ready": ([SZ, SZ], C.c_int),
+    "vox_stream_decodable_token_budget": ([SZ, SZ], SZ),
+    "vox_stream_finish_zero_padding_samples": ([SZ, SZ, C.POINTER(StreamPromptConfig)], SZ),
+    "vox_pipeline_create": ([VP, VP, C.POINTER(PipelineConfig), SZ, C.POINTER(VP)], C.c_int),
+    "vox_pipeline_destroy": ([VP], None),
+    "vox_pipeline_prompt_ids": ([VP, C.POINTER(C.c_uint32), SZ], SZ),
+    "vox_pipeline_adapter_tokens_total": ([VP], SZ),
+    "vox_pipeline_generated_tokens": ([VP], SZ),
+    "vox_pipeline_decodable_now": ([VP], SZ),
+    "vox_pipeline_is_finished": ([VP], C.c_int),
+    "vox_pipeline_push_adapter_tokens": ([VP, F32P, SZ], C.c_int),
+    "vox_pipeline_mark_decoded": ([VP, SZ], C.c_int),
+    "vox_pipeline_decode": ([VP, SZ, I32P, C.POINTER(SZ)], C.c_int),
+    "vox_pipeline_finish_padding_samples": ([VP, SZ], SZ),
 }
 
 
@@ -462,6 +500,108 @@ class RollingKvCache:
 
     def reset(self):
         _check(lib().vox_kv_reset(self.h))
+
+
+# ---------------------------------------------------------------------------
+# Streaming decode driver (stream.rs, pipeline.rs)
+# ---------------------------------------------------------------------------
+
+def build_prompt_ids(bos_id, streaming_pad_id, cfg: StreamPromptConfig):
+    """build_prompt_ids (stream.rs:26-34)."""
+    n = lib().vox_stream_build_prompt_ids(bos_id, streaming_pad_id, C.byref(cfg), None, 0)
+    out = (C.c_uint32 * max(n, 1))()
+    lib().vox_stream_build_prompt_ids(bos_id, streaming_pad_id, C.byref(cfg), out, n)
+    return [int(out[i]) for i in range(n)]
+
+
+def decode_ready(total_adapter_tokens, prompt_len):
+    """decode_ready (stream.rs:36-38)."""
+    return bool(lib().vox_stream_decode_ready(total_adapter_tokens, prompt_len))
+
+
+def decodable_token_budget(total_adapter_tokens, prompt_len):
+    """decodable_token_budget (stream.rs:47-53)."""
+    return int(lib().vox_stream_decodable_token_budget(total_adapter_tokens, prompt_len))
+
+
+def finish_zero_padding_samples(consumed_samples, samples_per_token, cfg: StreamPromptConfig):
+    """finish_zero_padding_samples (stream.rs:60-69)."""
+    return int(lib().vox_stream_finish_zero_padding_samples(consumed_samples, samples_per_token, C.byref(cfg)))
+
+
+class PipelineState:
+    """PipelineState (pipeline.rs:28-90).  Without a context it is the
+    reference's planner; with a Context and a single-stream RollingKvCache it
+    also decodes: push_adapter_tokens uploads adapter rows [n, dim] to a
+    device ring and decode() runs the streaming schedule on the device."""
+
+    def __init__(self, cfg: PipelineConfig, ctx: Context = None, cache: RollingKvCache = None,
+                 adapter_capacity=4096):
+        h = VP()
+        _check(lib().vox_pipeline_create(ctx.h if ctx else None, cache.h if cache else None, C.byref(cfg),
+                                         adapter_capacity, C.byref(h)))
+        self.h = h.value
+        self.ctx, self.cache = ctx, cache
+        self.dim = ctx.cfg.dim if ctx else 0
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().vox_pipeline_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def prompt_ids(self):
+        n = lib().vox_pipeline_prompt_ids(self.h, None, 0)
+        out = (C.c_uint32 * max(n, 1))()
+        lib().vox_pipeline_prompt_ids(self.h, out, n)
+        return [int(out[i]) for i in range(n)]
+
+    def adapter_tokens_total(self):
+        return int(lib().vox_pipeline_adapter_tokens_total(self.h))
+
+    def generated_tokens(self):
+        return int(lib().vox_pipeline_generated_tokens(self.h))
+
+    def decodable_now(self):
+        return int(lib().vox_pipeline_decodable_now(self.h))
+
+    def is_finished(self):
+        return bool(lib().vox_pipeline_is_finished(self.h))
+
+    def push_adapter_tokens(self, n_tokens_or_rows):
+        """push_adapter_tokens: a count (planner) or adapter rows [n, dim] (decoding pipeline)."""
+        if isinstance(n_tokens_or_rows, (int, np.integer)):
+            _check(lib().vox_pipeline_push_adapter_tokens(self.h, None, int(n_tokens_or_rows)))
+            return
+        rows = _f32(n_tokens_or_rows)
+        if self.dim == 0 or rows.size % self.dim:
+            raise ValueError("adapter rows must be [n, dim] for a pipeline with a context")
+        _check(lib().vox_pipeline_push_adapter_tokens(self.h, _p(rows), rows.size // self.dim))
+
+    def mark_decoded(self, n_tokens):
+        _check(lib().vox_pipeline_mark_decoded(self.h, int(n_tokens)))
+
+    def decode(self, max_tokens=None):
+        """Decode every decodable token (or at most max_tokens) on the device."""
+        n = self.decodable_now() if max_tokens is None else int(max_tokens)
+        out = np.empty(max(n, 1), np.int32)
+        got = SZ()
+        _check(lib().vox_pipeline_decode(self.h, n, _p(out, I32P), C.byref(got)))
+        return out[:got.value].copy()
+
+    def finish_padding_samples(self, consumed_audio_samples):
+        return int(lib().vox_pipeline_finish_padding_samples(self.h, int(consumed_audio_samples)))
 
 
 # ---------------------------------------------------------------------------

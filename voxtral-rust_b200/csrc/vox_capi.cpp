@@ -18,6 +18,7 @@
 
 #include "../../include/vox_decoder.h"
 #include "vox_host.h"
+#include "vox_internal.h"
 #include "vox_kernels.h"
 
 using namespace vox;
@@ -432,8 +433,12 @@ GemvArgs base_args(vox_ctx* c) {
     return a;
 }
 
-// Enqueue one decoder layer (decoder.rs:88-155) as five kernels.
-int enqueue_layer(vox_ctx* c, vox_kv* kv, size_t l, bool from_embed, bool pdl, bool short_attn = false) {
+// Enqueue one decoder layer (decoder.rs:88-155) as five kernels.  With
+// from_embed the input is the embedding row of the step's token, plus the
+// row of `adapter` (an [adapter_cap, dim] ring) at the step's position when
+// given: the streaming decoder input.
+int enqueue_layer(vox_ctx* c, vox_kv* kv, size_t l, bool from_embed, bool pdl, bool short_attn = false,
+                  const float* adapter = nullptr, int adapter_cap = 0) {
     const LayerDev& L = c->layers[l];
     float* kr = kv->k + l * kv->layer_elems();
     float* vr = kv->v + l * kv->layer_elems();
@@ -446,6 +451,8 @@ int enqueue_layer(vox_ctx* c, vox_kv* kv, size_t l, bool from_embed, bool pdl, b
     if (from_embed) {
         a.x_embed = c->embed;
         a.vocab = (int)c->opt.vocab;
+        a.x_adapter = adapter;
+        a.adapter_cap = adapter_cap;
         a.x_copy_out = c->hid;
     } else {
         a.x = c->hid;
@@ -912,15 +919,17 @@ int build_token_layers(vox_ctx* c, vox_kv* kv) {
 // the shape allows: attention as one cluster per kv head (contexts up to
 // attn_cluster_max_tokens()) or the persistent split-K kernel; launch_graph
 // picks one per step from the context length the host already knows.
-static int capture_step(vox_ctx* c, vox_kv* kv, bool short_attn, cudaGraphExec_t* out, uint64_t* kernels) {
+// With `adapter` the step always runs as the chain of layer kernels.
+static int capture_step(vox_ctx* c, vox_kv* kv, bool short_attn, cudaGraphExec_t* out, uint64_t* kernels,
+                        const float* adapter = nullptr, int adapter_cap = 0) {
     const uint64_t before = c->launches;
     CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
     int rc = VOX_OK;
-    if (c->tok_ok) {
+    if (c->tok_ok && !adapter) {
         rc = enqueue_token_kernel(c, kv);
     } else {
         for (size_t l = 0; l < c->layers.size() && rc == VOX_OK; ++l)
-            rc = enqueue_layer(c, kv, l, l == 0, true, short_attn);
+            rc = enqueue_layer(c, kv, l, l == 0, true, short_attn, adapter, adapter_cap);
         if (rc == VOX_OK) rc = enqueue_head(c, true);
     }
     cudaGraph_t g = nullptr;
@@ -2162,3 +2171,92 @@ int vox_attention_gqa_step(vox_ctx* c, const float* q, const float* keys, const 
 }
 
 }  // extern "C"
+
+// ---- interface for the other host files (vox_internal.h) -------------------------
+namespace vox {
+
+int ctx_info(const vox_ctx* c, CtxInfo* out) {
+    if (!c || !out) return fail(VOX_ERR_INVALID_ARG, "null context");
+    out->device = c->dev;
+    out->stream = c->stream;
+    out->dim = c->cfg.dim;
+    out->vocab = c->opt.vocab;
+    out->n_layers = c->layers.size();
+    out->max_pos = c->max_pos;
+    return VOX_OK;
+}
+
+int ctx_model_ready(vox_ctx* c, vox_kv* kv) {
+    TRY(model_ready(c, kv));
+    return single_stream(kv);
+}
+
+void release_step_graphs(StepGraphs* g) {
+    if (!g) return;
+    if (g->full) cudaGraphExecDestroy(g->full);
+    if (g->short_attn) cudaGraphExecDestroy(g->short_attn);
+    *g = StepGraphs{};
+}
+
+int capture_adapter_graphs(vox_ctx* c, vox_kv* kv, const float* adapter, int adapter_cap, StepGraphs* g) {
+    TRY(ctx_model_ready(c, kv));
+    if (!adapter || adapter_cap <= 0) return fail(VOX_ERR_INVALID_ARG, "adapter ring missing");
+    CUDA_TRY(cudaSetDevice(c->dev));
+    release_step_graphs(g);
+    TRY(capture_step(c, kv, false, &g->full, &g->k_full, adapter, adapter_cap));
+    if (attn_cluster_size((int)c->cfg.n_heads, (int)c->cfg.n_kv_heads, (int)c->cfg.head_dim) > 0)
+        TRY(capture_step(c, kv, true, &g->short_attn, &g->k_short, adapter, adapter_cap));
+    return VOX_OK;
+}
+
+int run_step_graphs(vox_ctx* c, vox_kv* kv, const StepGraphs& g, const int32_t* fixed, size_t n_fixed,
+                    size_t pos0, int32_t greedy_tok, size_t n_greedy, int32_t* tokens_out) {
+    TRY(ctx_model_ready(c, kv));
+    if (!g.full) return fail(VOX_ERR_INVALID_ARG, "step graphs not captured");
+    if (n_fixed + n_greedy == 0) return VOX_OK;
+    if (n_fixed && !fixed) return fail(VOX_ERR_INVALID_ARG, "tokens are null");
+    if (pos0 + n_fixed + n_greedy > (size_t)c->max_pos)
+        return fail(VOX_ERR_RANGE, "positions beyond max_positions %d", c->max_pos);
+    for (size_t i = 0; i < n_fixed; ++i)
+        if (fixed[i] < 0 || (size_t)fixed[i] >= c->opt.vocab)
+            return fail(VOX_ERR_RANGE, "token %d outside the vocabulary", fixed[i]);
+    if (n_greedy && (greedy_tok < 0 || (size_t)greedy_tok >= c->opt.vocab))
+        return fail(VOX_ERR_RANGE, "token %d outside the vocabulary", greedy_tok);
+    CUDA_TRY(cudaSetDevice(c->dev));
+    CUDA_TRY(cudaStreamSynchronize(c->stream));
+    TRY(ensure_host_steps(c, n_fixed + 1 + n_greedy));
+    auto launch = [&](size_t live) -> int {
+        const bool use_short = g.short_attn && live <= (size_t)attn_cluster_max_tokens();
+        CUDA_TRY(cudaGraphLaunch(use_short ? g.short_attn : g.full, c->stream));
+        c->launches += use_short ? g.k_short : g.k_full;
+        return VOX_OK;
+    };
+    for (size_t i = 0; i < n_fixed; ++i) {
+        StepState* hs = c->h_steps + i;
+        std::memset(hs, 0, sizeof(StepState));
+        hs->pos = (int64_t)(pos0 + i);
+        hs->tok = fixed[i];
+        CUDA_TRY(cudaMemcpyAsync(c->step, hs, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
+        TRY(launch(live_tokens_after(c, kv, i + 1)));
+    }
+    int32_t* tok_hist = reinterpret_cast<int32_t*>(c->h_steps + n_fixed + 1);
+    if (n_greedy) {
+        StepState* hs = c->h_steps + n_fixed;
+        std::memset(hs, 0, sizeof(StepState));
+        hs->pos = (int64_t)(pos0 + n_fixed);
+        hs->tok = greedy_tok;
+        hs->greedy = 1;
+        hs->advance = 1;
+        CUDA_TRY(cudaMemcpyAsync(c->step, hs, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
+        for (size_t i = 0; i < n_greedy; ++i) {
+            TRY(launch(live_tokens_after(c, kv, n_fixed + i + 1)));
+            CUDA_TRY(cudaMemcpyAsync(tok_hist + i, c->tok_out, 4, cudaMemcpyDeviceToHost, c->stream));
+        }
+    }
+    TRY(check_device_errors(c));
+    for (size_t i = 0; i < n_fixed + n_greedy; ++i) mirror_single_append_all(kv);
+    if (tokens_out && n_greedy) std::memcpy(tokens_out, tok_hist, n_greedy * 4);
+    return VOX_OK;
+}
+
+}  // namespace vox

@@ -199,6 +199,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
     // Input vector: x, or the embedding row of the step's token.
     const float* x = A.x ? A.x + (long long)vec * A.x_stride : nullptr;
     const uint16_t* xe = nullptr;
+    const float* xad = nullptr;
     if (A.x_embed) {
         int tok = A.step->tok;
         if (tok < 0 || tok >= A.vocab) {
@@ -206,6 +207,10 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
             tok = 0;
         }
         xe = A.x_embed + (size_t)tok * K;
+        if (A.x_adapter) {
+            const long long p = A.step->pos;
+            xad = A.x_adapter + (size_t)(p < 0 ? 0 : p % A.adapter_cap) * K;
+        }
     }
 
     // Epilogue inputs that do not depend on this product (the residual row,
@@ -244,6 +249,16 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
                 }
 #pragma unroll
                 for (int e = 0; e < EPC; ++e) xr[i][e] = (e & 1) ? bf16_hi(ws[e >> 1]) : bf16_lo(ws[e >> 1]);
+                if (xad) {  // adapter[pos] + tok_embed(token), one f32 add
+#pragma unroll
+                    for (int e = 0; e < EPC; e += 4) {
+                        const float4 a = *reinterpret_cast<const float4*>(xad + k0 + e);
+                        xr[i][e] = __fadd_rn(a.x, xr[i][e]);
+                        xr[i][e + 1] = __fadd_rn(a.y, xr[i][e + 1]);
+                        xr[i][e + 2] = __fadd_rn(a.z, xr[i][e + 2]);
+                        xr[i][e + 3] = __fadd_rn(a.w, xr[i][e + 3]);
+                    }
+                }
             } else if (xsum) {
                 unsigned char* own = A.xch[A.xa.rank];
                 for (int src = 0; src < A.xa.size; ++src) {

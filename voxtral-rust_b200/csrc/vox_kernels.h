@@ -91,6 +91,10 @@ struct GemvArgs {
     long long x_stride;         // between input vectors (gridDim.y)
     const uint16_t* x_embed;
     int vocab;
+    // non-null with x_embed: x = adapter row + embedding row, the streaming
+    // decoder input (adapter ring [adapter_cap, K] f32, row = pos mod cap)
+    const float* x_adapter;
+    int adapter_cap;
     const StepState* step;
     const float* norm_w;        // non-null: RMSNorm(x) with this gain first
     float eps;
