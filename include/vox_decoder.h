@@ -41,7 +41,9 @@ typedef enum vox_status {
     VOX_ERR_OOM = 6,            /* device or pinned allocation failed */
     VOX_ERR_NOT_READY = 7,      /* weights needed by the call were never uploaded */
     VOX_ERR_DEVICE_TIMEOUT = 8, /* a bounded wait inside a kernel expired */
-    VOX_ERR_RANGE = 9           /* position beyond the RoPE table, token outside the vocab */
+    VOX_ERR_RANGE = 9,          /* position beyond the RoPE table, token outside the vocab */
+    VOX_ERR_IO = 10,            /* a file could not be opened or mapped */
+    VOX_ERR_FORMAT = 11         /* malformed file (safetensors header, tekken.json) or unsupported dtype */
 } vox_status;
 
 typedef enum vox_weight_dtype { VOX_WEIGHTS_BF16 = 0, VOX_WEIGHTS_F32 = 1 } vox_weight_dtype;
@@ -348,6 +350,50 @@ int vox_pipeline_decode(vox_pipeline* p, size_t max_tokens, int32_t* tokens_out,
 /* finish_padding_samples (pipeline.rs:78-85): marks the pipeline finished and
  * returns the zero samples to append. */
 size_t vox_pipeline_finish_padding_samples(vox_pipeline* p, size_t consumed_audio_samples);
+
+/* ---- safetensors checkpoints (weights.rs) --------------------------------------- */
+/* WeightStore (weights.rs:16-42): a read-only memory map of a .safetensors
+ * file whose header is validated at open (8-byte little-endian length <= 1e8,
+ * JSON {name: {dtype, shape, data_offsets}} + optional "__metadata__",
+ * tensors packed back to back covering the data section exactly, each of
+ * numel * element-size bytes).  VOX_ERR_IO if the file cannot be read,
+ * VOX_ERR_FORMAT if it is not valid safetensors. */
+typedef struct vox_weights vox_weights;
+typedef enum vox_tensor_dtype {
+    VOX_DT_BOOL = 0, VOX_DT_U8, VOX_DT_I8, VOX_DT_F8_E5M2, VOX_DT_F8_E4M3, VOX_DT_I16, VOX_DT_U16,
+    VOX_DT_F16, VOX_DT_BF16, VOX_DT_I32, VOX_DT_U32, VOX_DT_F32, VOX_DT_F64, VOX_DT_I64, VOX_DT_U64
+} vox_tensor_dtype;
+int vox_weights_open(const char* path, vox_weights** out);
+void vox_weights_close(vox_weights* w);
+/* names (weights.rs:44-47): count, then the i-th name (in data-offset order;
+ * the reference's order is unspecified).  NULL when i is out of range. */
+size_t vox_weights_count(const vox_weights* w);
+const char* vox_weights_name(const vox_weights* w, size_t i);
+/* dtype (vox_tensor_dtype), rank and up to shape_cap dims of a tensor. */
+int vox_weights_info(const vox_weights* w, const char* name, int* dtype, size_t* shape, size_t shape_cap,
+                     size_t* ndim);
+/* tensor_f32 (weights.rs:49-93): F32 copied, BF16 widened exactly
+ * (bits << 16); any other dtype is VOX_ERR_FORMAT ("unsupported dtype").
+ * *n_elems receives the element count; out NULL is a size query. */
+int vox_weights_tensor_f32(const vox_weights* w, const char* name, float* out, size_t cap_elems,
+                           size_t* n_elems);
+/* Load a decoder checkpoint into a context (copies to the device; the file
+ * can be closed afterwards).  Tensor names, as in the reference's checkpoint
+ * (e2e_model_env.rs:23-32 checks the first two):
+ *   layers.{l}.attention.{wq,wk,wv,wo}.weight, layers.{l}.attention_norm.weight,
+ *   layers.{l}.feed_forward.{w1,w2,w3}.weight, layers.{l}.ffn_norm.weight
+ *   for l < n_layers; with a vocabulary also VOX_CKPT_EMBED, VOX_CKPT_FINAL_NORM
+ *   and VOX_CKPT_LM_HEAD (absent = the LM head is tied to the embedding,
+ *   params.rs tied_embeddings).  BF16 or F32 tensors; matrices are rounded to
+ *   the context's weight dtype (nearest even), norms kept in f32.  Shapes are
+ *   checked by element count against the context's config.  The reference
+ *   parses ada_rms_norm_t_cond (params.rs:24-27) but its decoder never applies
+ *   it; neither does this loader (a caller can fold a fixed modulation into
+ *   ffn_norm through vox_ctx_upload_layer_*). */
+#define VOX_CKPT_EMBED "mm_streams_embeddings.embedding_module.tok_embeddings.weight"
+#define VOX_CKPT_LM_HEAD "output.weight"
+#define VOX_CKPT_FINAL_NORM "norm.weight"
+int vox_ctx_load_checkpoint(vox_ctx* ctx, const vox_weights* w);
 
 /* ---- profiling hook (no reference counterpart) --------------------------------- */
 /* Times one of the step's weight-streaming GEMVs on its own: n_launches

@@ -17,6 +17,7 @@ text and re-run against the oracle and the CUDA library):
   stream.rs:93-102  finish_padding_matches_alignment_plus_right_budget
   pipeline.rs:99-130  planner_tracks_budget_across_chunks
   pipeline.rs:132-144 planner_finish_padding_formula
+  weights.rs:141-193  loads_f32_and_bf16_tensors
 
 The 32-bit LCG below is the one the reference tests use
 (seed = seed*1664525 + 1013904223; value = (seed>>8)/2^24*2-1, in f32).
@@ -206,6 +207,12 @@ def reference_unit_tests():
         "cite": "crates/voxtral/src/pipeline.rs:132-144",
         "bos_id": 1, "streaming_pad_id": 32, "samples_per_token": 1280,
         "consumed": 3 * 1280 + 640, "expect": 640 + 17 * 1280, "expect_finished": True,
+    }
+    # weights.rs:141-193: an F32 [2, 2] tensor "a" and a BF16 [2] tensor "b"
+    tests["loads_f32_and_bf16_tensors"] = {
+        "cite": "crates/voxtral/src/weights.rs:141-193",
+        "a": {"dtype": "F32", "shape": [2, 2], "values": [1.0, 2.5, -3.0, 4.25]},
+        "b": {"dtype": "BF16", "shape": [2], "words": [0x3F80, 0xC000], "expect": [1.0, -2.0], "tol": 1e-6},
     }
     return tests
 

@@ -28,7 +28,7 @@ SZ = C.c_size_t
 VP = C.c_void_p
 
 OK, ERR_INVALID_ARG, ERR_CONFIG, ERR_SHAPE, ERR_UNSUPPORTED, ERR_CUDA, ERR_OOM, ERR_NOT_READY, \
-    ERR_DEVICE_TIMEOUT, ERR_RANGE = range(10)
+    ERR_DEVICE_TIMEOUT, ERR_RANGE, ERR_IO, ERR_FORMAT = range(12)
 WEIGHTS_BF16, WEIGHTS_F32 = 0, 1
 
 
@@ -186,6 +186,13 @@ _SIGS = {
     "vox_silu_inplace": ([VP, F32P, SZ], C.c_int),
     "vox_softmax_inplace": ([VP, F32P, SZ], C.c_int),
     "vox_attention_gqa_step_noalloc": ([VP, VP, VP, C.POINTER(AttentionShape), VP, VP], C.c_int),
+    "vox_weights_open": ([C.c_char_p, C.POINTER(VP)], C.c_int),
+    "vox_weights_close": ([VP], None),
+    "vox_weights_count": ([VP], SZ),
+    "vox_weights_name": ([VP, SZ], C.c_char_p),
+    "vox_weights_info": ([VP, C.c_char_p, C.POINTER(C.c_int), C.POINTER(SZ), SZ, C.POINTER(SZ)], C.c_int),
+    "vox_weights_tensor_f32": ([VP, C.c_char_p, F32P, SZ, C.POINTER(SZ)], C.c_int),
+    "vox_ctx_load_checkpoint": ([VP, VP], C.c_int),
     "vox_stream_prompt_config_default": ([C.POINTER(StreamPromptConfig)], None),
     "vox_stream_right_pad_tokens": ([C.POINTER(StreamPromptConfig)], SZ),
     "vox_stream_build_prompt_ids": ([C.c_uint32, C.c_uint32, C.POINTER(StreamPromptConfig),
@@ -500,6 +507,74 @@ class RollingKvCache:
 
     def reset(self):
         _check(lib().vox_kv_reset(self.h))
+
+
+# ---------------------------------------------------------------------------
+# safetensors checkpoints (weights.rs)
+# ---------------------------------------------------------------------------
+
+DTYPES = ("BOOL", "U8", "I8", "F8_E5M2", "F8_E4M3", "I16", "U16", "F16", "BF16", "I32", "U32", "F32", "F64",
+          "I64", "U64")
+CKPT_EMBED = "mm_streams_embeddings.embedding_module.tok_embeddings.weight"
+CKPT_LM_HEAD = "output.weight"
+CKPT_FINAL_NORM = "norm.weight"
+
+
+class WeightStore:
+    """WeightStore (weights.rs:16-93): a memory-mapped, header-validated
+    .safetensors file."""
+
+    def __init__(self, path):
+        h = VP()
+        _check(lib().vox_weights_open(os.fsencode(path), C.byref(h)))
+        self.h = h.value
+
+    @classmethod
+    def open(cls, path):
+        return cls(path)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().vox_weights_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def names(self):
+        """names (weights.rs:44-47)."""
+        n = lib().vox_weights_count(self.h)
+        return [lib().vox_weights_name(self.h, i).decode() for i in range(n)]
+
+    def info(self, name):
+        """(dtype name, shape) of a tensor."""
+        dt, nd = C.c_int(), SZ()
+        shape = (SZ * 16)()
+        _check(lib().vox_weights_info(self.h, name.encode(), C.byref(dt), shape, 16, C.byref(nd)))
+        return DTYPES[dt.value], [int(shape[i]) for i in range(nd.value)]
+
+    def tensor_f32(self, name):
+        """tensor_f32 (weights.rs:49-93): returns (shape, data f32)."""
+        n = SZ()
+        _check(lib().vox_weights_tensor_f32(self.h, name.encode(), None, 0, C.byref(n)))
+        out = np.empty(n.value, np.float32)
+        _check(lib().vox_weights_tensor_f32(self.h, name.encode(), _p(out), n.value, C.byref(n)))
+        return self.info(name)[1], out
+
+
+def load_checkpoint(ctx: Context, store: WeightStore):
+    """Upload a decoder checkpoint (layers.{l}.*, embedding, final norm, LM
+    head or tied embedding) into a context."""
+    _check(lib().vox_ctx_load_checkpoint(ctx.h, store.h))
 
 
 # ---------------------------------------------------------------------------

@@ -2179,6 +2179,8 @@ int ctx_info(const vox_ctx* c, CtxInfo* out) {
     if (!c || !out) return fail(VOX_ERR_INVALID_ARG, "null context");
     out->device = c->dev;
     out->stream = c->stream;
+    out->cfg = c->cfg;
+    out->weight_dtype = c->wsize == 4 ? VOX_WEIGHTS_F32 : VOX_WEIGHTS_BF16;
     out->dim = c->cfg.dim;
     out->vocab = c->opt.vocab;
     out->n_layers = c->layers.size();

@@ -15,8 +15,10 @@ namespace vox {
 struct CtxInfo {
     int device;
     cudaStream_t stream;
+    vox_decoder_config cfg;
     size_t dim, vocab, n_layers;
     int max_pos;
+    int weight_dtype;  // vox_weight_dtype
 };
 
 int ctx_info(const vox_ctx* c, CtxInfo* out);
