@@ -395,6 +395,44 @@ int vox_weights_tensor_f32(const vox_weights* w, const char* name, float* out, s
 #define VOX_CKPT_FINAL_NORM "norm.weight"
 int vox_ctx_load_checkpoint(vox_ctx* ctx, const vox_weights* w);
 
+/* ---- Tekken tokenizer decode (tokenizer.rs) ------------------------------------- */
+/* TekkenTokenizer (tokenizer.rs:26-214): ids -> bytes -> text after the token
+ * loop's argmax.  Functions returning int without a status return 1 for the
+ * reference's Some and 0 for None. */
+typedef struct vox_tekken vox_tekken;
+/* TekkenAudioConfig (tokenizer.rs:17-23). */
+typedef struct vox_tekken_audio_config {
+    uint32_t sampling_rate;
+    float frame_rate;
+    size_t transcription_delay_ms;
+    size_t streaming_n_left_pad_tokens;
+} vox_tekken_audio_config;
+/* from_json_str (tokenizer.rs:72-130) / from_path (:132-137): VOX_ERR_FORMAT
+ * for malformed JSON, missing or mistyped fields, default_vocab_size 0 or
+ * invalid base64 (standard alphabet, canonical padding); VOX_ERR_IO if the
+ * file cannot be read. */
+int vox_tekken_from_json(const char* json, size_t len, vox_tekken** out);
+int vox_tekken_from_path(const char* path, vox_tekken** out);
+void vox_tekken_destroy(vox_tekken* t);
+size_t vox_tekken_default_vocab_size(const vox_tekken* t);      /* tokenizer.rs:139 */
+size_t vox_tekken_special_token_count(const vox_tekken* t);     /* tokenizer.rs:143 */
+/* special_id (tokenizer.rs:147); bos "<s>", eos "</s>", "[STREAMING_PAD]". */
+int vox_tekken_special_id(const vox_tekken* t, const char* text, uint32_t* id);
+int vox_tekken_audio(const vox_tekken* t, vox_tekken_audio_config* out);     /* tokenizer.rs:163 */
+/* transcription_delay_tokens (tokenizer.rs:167-171): round(ms / 1000 * frame_rate). */
+int vox_tekken_transcription_delay_tokens(const vox_tekken* t, size_t* out);
+/* default_prompt_ids (tokenizer.rs:173-184): [bos] + [pad] * (left pad + delay);
+ * *len = length, at most cap ids written. */
+int vox_tekken_default_prompt_ids(const vox_tekken* t, uint32_t* out, size_t cap, size_t* len);
+/* decode_token_bytes (tokenizer.rs:186-203): None for ids beyond the vocab,
+ * control specials and vocab ids without bytes.  *bytes stays valid while
+ * the tokenizer lives. */
+int vox_tekken_decode_token_bytes(const vox_tekken* t, uint32_t token_id, const uint8_t** bytes, size_t* len);
+/* decode_to_utf8_lossy (tokenizer.rs:204-213): concatenated bytes decoded as
+ * UTF-8 with each maximal invalid subpart replaced by U+FFFD.  Returns the
+ * text's byte length; writes at most cap - 1 bytes plus a NUL (out nullable). */
+size_t vox_tekken_decode_to_utf8_lossy(const vox_tekken* t, const uint32_t* ids, size_t n, char* out, size_t cap);
+
 /* ---- profiling hook (no reference counterpart) --------------------------------- */
 /* Times one of the step's weight-streaming GEMVs on its own: n_launches
  * back-to-back launches (cycling over the layers, so every launch streams a

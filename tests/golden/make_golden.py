@@ -18,6 +18,8 @@ text and re-run against the oracle and the CUDA library):
   pipeline.rs:99-130  planner_tracks_budget_across_chunks
   pipeline.rs:132-144 planner_finish_padding_formula
   weights.rs:141-193  loads_f32_and_bf16_tensors
+  tokenizer.rs:219-257 tokenizer_decodes_basic_tokens
+  tokenizer.rs:259-286 default_prompt_has_expected_length
 
 The 32-bit LCG below is the one the reference tests use
 (seed = seed*1664525 + 1013904223; value = (seed>>8)/2^24*2-1, in f32).
@@ -213,6 +215,35 @@ def reference_unit_tests():
         "cite": "crates/voxtral/src/weights.rs:141-193",
         "a": {"dtype": "F32", "shape": [2, 2], "values": [1.0, 2.5, -3.0, 4.25]},
         "b": {"dtype": "BF16", "shape": [2], "words": [0x3F80, 0xC000], "expect": [1.0, -2.0], "tol": 1e-6},
+    }
+    # tokenizer.rs:219-257: 16-id vocabulary, 4 specials, ranks 0..2 = "A", "B", "C"
+    audio = {"sampling_rate": 16000, "frame_rate": 12.5, "transcription_delay_ms": 480,
+             "streaming_n_left_pad_tokens": 32}
+    tests["tokenizer_decodes_basic_tokens"] = {
+        "cite": "crates/voxtral/src/tokenizer.rs:219-257",
+        "json": json.dumps({
+            "config": {"default_vocab_size": 16, "default_num_special_tokens": 4},
+            "special_tokens": [{"rank": 0, "token_str": "<unk>", "is_control": True},
+                               {"rank": 1, "token_str": "<s>", "is_control": True},
+                               {"rank": 2, "token_str": "</s>", "is_control": True},
+                               {"rank": 3, "token_str": "[STREAMING_PAD]", "is_control": True}],
+            "vocab": [{"rank": 0, "token_bytes": "QQ=="}, {"rank": 1, "token_bytes": "Qg=="},
+                      {"rank": 2, "token_bytes": "Qw=="}],
+            "audio": audio}),
+        "expect": {"default_vocab_size": 16, "special_token_count": 4, "bos_id": 1, "eos_id": 2,
+                   "streaming_pad_id": 3, "transcription_delay_tokens": 6},
+        "decode_ids": [1, 4, 5, 6, 2], "decode_expect": "ABC",
+    }
+    # tokenizer.rs:259-286: rank 0 missing, empty vocabulary
+    tests["default_prompt_has_expected_length"] = {
+        "cite": "crates/voxtral/src/tokenizer.rs:259-286",
+        "json": json.dumps({
+            "config": {"default_vocab_size": 8, "default_num_special_tokens": 4},
+            "special_tokens": [{"rank": 1, "token_str": "<s>", "is_control": True},
+                               {"rank": 2, "token_str": "</s>", "is_control": True},
+                               {"rank": 3, "token_str": "[STREAMING_PAD]", "is_control": True}],
+            "vocab": [], "audio": audio}),
+        "expect_len": 1 + 32 + 6, "expect_first": 1, "expect_rest": 3,
     }
     return tests
 

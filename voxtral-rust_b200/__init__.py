@@ -108,6 +108,13 @@ class StreamPromptConfig(C.Structure):
         return int(lib().vox_stream_right_pad_tokens(C.byref(self)))
 
 
+class TekkenAudioConfig(C.Structure):
+    """TekkenAudioConfig (tokenizer.rs:17-23)."""
+
+    _fields_ = [("sampling_rate", C.c_uint32), ("frame_rate", C.c_float), ("transcription_delay_ms", SZ),
+                ("streaming_n_left_pad_tokens", SZ)]
+
+
 class PipelineConfig(C.Structure):
     """PipelineConfig (pipeline.rs:12-18)."""
 
@@ -193,6 +200,17 @@ _SIGS = {
     "vox_weights_info": ([VP, C.c_char_p, C.POINTER(C.c_int), C.POINTER(SZ), SZ, C.POINTER(SZ)], C.c_int),
     "vox_weights_tensor_f32": ([VP, C.c_char_p, F32P, SZ, C.POINTER(SZ)], C.c_int),
     "vox_ctx_load_checkpoint": ([VP, VP], C.c_int),
+    "vox_tekken_from_json": ([C.c_char_p, SZ, C.POINTER(VP)], C.c_int),
+    "vox_tekken_from_path": ([C.c_char_p, C.POINTER(VP)], C.c_int),
+    "vox_tekken_destroy": ([VP], None),
+    "vox_tekken_default_vocab_size": ([VP], SZ),
+    "vox_tekken_special_token_count": ([VP], SZ),
+    "vox_tekken_special_id": ([VP, C.c_char_p, C.POINTER(C.c_uint32)], C.c_int),
+    "vox_tekken_audio": ([VP, C.POINTER(TekkenAudioConfig)], C.c_int),
+    "vox_tekken_transcription_delay_tokens": ([VP, C.POINTER(SZ)], C.c_int),
+    "vox_tekken_default_prompt_ids": ([VP, C.POINTER(C.c_uint32), SZ, C.POINTER(SZ)], C.c_int),
+    "vox_tekken_decode_token_bytes": ([VP, C.c_uint32, C.POINTER(C.POINTER(C.c_uint8)), C.POINTER(SZ)], C.c_int),
+    "vox_tekken_decode_to_utf8_lossy": ([VP, C.POINTER(C.c_uint32), SZ, C.c_char_p, SZ], SZ),
     "vox_stream_prompt_config_default": ([C.POINTER(StreamPromptConfig)], None),
     "vox_stream_right_pad_tokens": ([C.POINTER(StreamPromptConfig)], SZ),
     "vox_stream_build_prompt_ids": ([C.c_uint32, C.c_uint32, C.POINTER(StreamPromptConfig),
@@ -575,6 +593,89 @@ def load_checkpoint(ctx: Context, store: WeightStore):
     """Upload a decoder checkpoint (layers.{l}.*, embedding, final norm, LM
     head or tied embedding) into a context."""
     _check(lib().vox_ctx_load_checkpoint(ctx.h, store.h))
+
+
+# ---------------------------------------------------------------------------
+# Tekken tokenizer decode (tokenizer.rs)
+# ---------------------------------------------------------------------------
+
+class TekkenTokenizer:
+    """TekkenTokenizer (tokenizer.rs:26-214); Option results are None."""
+
+    def __init__(self, _handle):
+        self.h = _handle
+
+    @classmethod
+    def from_json_str(cls, text):
+        b = text.encode() if isinstance(text, str) else bytes(text)
+        h = VP()
+        _check(lib().vox_tekken_from_json(b, len(b), C.byref(h)))
+        return cls(h.value)
+
+    @classmethod
+    def from_path(cls, path):
+        h = VP()
+        _check(lib().vox_tekken_from_path(os.fsencode(path), C.byref(h)))
+        return cls(h.value)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().vox_tekken_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def default_vocab_size(self):
+        return int(lib().vox_tekken_default_vocab_size(self.h))
+
+    def special_token_count(self):
+        return int(lib().vox_tekken_special_token_count(self.h))
+
+    def special_id(self, text):
+        v = C.c_uint32()
+        return int(v.value) if lib().vox_tekken_special_id(self.h, text.encode(), C.byref(v)) else None
+
+    def bos_id(self):
+        return self.special_id("<s>")
+
+    def eos_id(self):
+        return self.special_id("</s>")
+
+    def streaming_pad_id(self):
+        return self.special_id("[STREAMING_PAD]")
+
+    def audio(self):
+        a = TekkenAudioConfig()
+        return a if lib().vox_tekken_audio(self.h, C.byref(a)) else None
+
+    def transcription_delay_tokens(self):
+        v = SZ()
+        return int(v.value) if lib().vox_tekken_transcription_delay_tokens(self.h, C.byref(v)) else None
+
+    def default_prompt_ids(self):
+        n = SZ()
+        if not lib().vox_tekken_default_prompt_ids(self.h, None, 0, C.byref(n)):
+            return None
+        out = (C.c_uint32 * max(n.value, 1))()
+        lib().vox_tekken_default_prompt_ids(self.h, out, n.value, C.byref(n))
+        return [int(out[i]) for i in range(n.value)]
+
+    def decode_token_bytes(self, token_id):
+        p, n = C.POINTER(C.c_uint8)(), SZ()
+        if not lib().vox_tekken_decode_token_bytes(self.h, int(token_id) & 0xFFFFFFFF, C.byref(p), C.byref(n)):
+            return None
+        return bytes(C.string_at(p, n.value)) if n.value else b""
+
+    def decode_to_utf8_lossy(self, token_ids):
+        ids = (C.c_uint32 * max(len(token_ids), 1))(*[int(i) & 0xFFFFFFFF for i in token_ids])
+        n = lib().vox_tekken_decode_to_utf8_lossy(self.h, ids, len(token_ids), None, 0)
+        buf = C.create_string_buffer(n + 1)
+        lib().vox_tekken_decode_to_utf8_lossy(self.h, ids, len(token_ids), buf, n + 1)
+        return buf.raw[:n].decode("utf-8")
 
 
 # ---------------------------------------------------------------------------
