@@ -409,8 +409,46 @@ TP_WORKLOAD = ("26-layer decoder, batch 1, tensor parallel over all GPUs (q|k|v,
                "2048 random ids then greedy decode")
 
 
-def run_tensor_parallel(V, args, rank, world, local, dist):
-    """One stream decoded by all ranks together; returns this rank's timings."""
+TP_PARITY_PROMPT, TP_PARITY_FORCED, TP_PARITY_GREEDY = 31, 4, 64
+
+
+def tp_parity_reference(V, ctx):
+    """The parity sequence on this rank's single-GPU Context (the same weights
+    the tensor-parallel ranks hold): a 31-id prompt prefilled, 4
+    teacher-forced steps with their logits, then 64 greedy steps."""
+    ids = prompt_ids(4242, TP_PARITY_PROMPT + TP_PARITY_FORCED)
+    kv = V.RollingKvCache(ctx, LAYERS, NKV, HD, WINDOW)
+    ctx.model_prefill(kv, ids[:TP_PARITY_PROMPT], 0)
+    logits, toks = [], []
+    for i in range(TP_PARITY_FORCED):
+        t, lg = ctx.model_step(kv, int(ids[TP_PARITY_PROMPT + i]), TP_PARITY_PROMPT + i, want_logits=True)
+        logits.append(lg)
+        toks.append(t)
+    pos = TP_PARITY_PROMPT + TP_PARITY_FORCED
+    toks += [int(x) for x in ctx.model_generate(kv, toks[-1], pos, TP_PARITY_GREEDY)]
+    kv.close()
+    return ids, logits, toks
+
+
+def tp_parity_check(tp, ids, ref_logits, ref_toks):
+    """The same sequence through the tensor-parallel decoder: this rank's
+    logit slice against the reference's, and every token."""
+    tp.reset()
+    tp.prefill([int(i) for i in ids[:TP_PARITY_PROMPT]], 0)
+    lo, hi = tp.shard.vocab_begin, tp.shard.vocab_begin + tp.shard.vocab_local
+    diff, toks = 0.0, []
+    for i in range(TP_PARITY_FORCED):
+        t, lg = tp.step(int(ids[TP_PARITY_PROMPT + i]), TP_PARITY_PROMPT + i, want_logits=True)
+        diff = max(diff, float(np.max(np.abs(lg.astype(np.float64) - ref_logits[i][lo:hi]))))
+        toks.append(t)
+    pos = TP_PARITY_PROMPT + TP_PARITY_FORCED
+    toks += [int(x) for x in tp.generate(toks[-1], pos, TP_PARITY_GREEDY)]
+    return diff, toks == ref_toks
+
+
+def run_tensor_parallel(V, args, rank, world, local, dist, parity_ref=None):
+    """One stream decoded by all ranks together; returns this rank's timings
+    (and, given the single-GPU reference sequence, the parity result)."""
     cfg = V.DecoderConfig(dim=DIM, hidden_dim=HIDDEN, n_heads=NH, n_kv_heads=NKV, head_dim=HD,
                           sliding_window=WINDOW, norm_eps=1e-5, rope_theta=1e6)
     uid = V.share_tp_unique_id(rank)
@@ -431,7 +469,10 @@ def run_tensor_parallel(V, args, rank, world, local, dist):
         tp.record_event(1)
         ms = tp.elapsed_ms(0, 1)
         launches = tp.kernel_launches() - launches0
-    return {"ms": ms, "steps": steps, "launches": launches, "ctx": [pos, pos + steps]}
+        parity = None
+        if parity_ref is not None:
+            parity = tp_parity_check(tp, *parity_ref)
+    return {"ms": ms, "steps": steps, "launches": launches, "ctx": [pos, pos + steps], "parity": parity}
 
 
 def run_ours(args):
@@ -498,8 +539,9 @@ def run_ours(args):
     ms_run = None if args.ms_steps == 0 else run_multi_stream(V, ctx, args, rank, world, dist)
     tp_run = None
     if world > 1 and args.tp_steps > 0:
+        parity_ref = tp_parity_reference(V, ctx)
         ctx.close()  # release the replica's memory first
-        tp_run = run_tensor_parallel(V, args, rank, world, local, dist)
+        tp_run = run_tensor_parallel(V, args, rank, world, local, dist, parity_ref)
 
     t_max, e2e_max = ms, e2e_ms
     ms_max = ms_e2e_max = tp_max = long_max = roll_max = 0.0
@@ -518,6 +560,10 @@ def run_ours(args):
             ok = torch.tensor([1.0 if roll_run["ring_ok"] and long_run["ring_ok"] else 0.0])
             dist.all_reduce(ok, op=dist.ReduceOp.MIN)
             roll_run["ring_ok"] = long_run["ring_ok"] = bool(ok.item() > 0)
+        if tp_run and tp_run["parity"] is not None:
+            d = torch.tensor([tp_run["parity"][0], 0.0 if tp_run["parity"][1] else 1.0], dtype=torch.float64)
+            dist.all_reduce(d, op=dist.ReduceOp.MAX)
+            tp_run["parity"] = (float(d[0]), bool(d[1] == 0.0))
     if rank != 0:
         if dist:
             dist.barrier()
@@ -587,6 +633,12 @@ def run_ours(args):
             "step_roofline": {"achieved": tp_gbs, "peak": peak * world, "unit": "GB/s",
                               "frac": tp_gbs / (peak * world), "note": "aggregate HBM of all ranks"},
             "gpu_launches": tp_run["launches"]}
+        if tp_run["parity"] is not None:
+            line["tensor_parallel"]["parity"] = {
+                "against": "the single-GPU Context on the same weights (each rank's logit slice)",
+                "tokens_identical": tp_run["parity"][1], "n_steps": TP_PARITY_FORCED + TP_PARITY_GREEDY,
+                "teacher_forced_steps": TP_PARITY_FORCED, "greedy_steps": TP_PARITY_GREEDY,
+                "max_abs_logit_diff": tp_run["parity"][0]}
     if world == 1 and not args.no_cpu:
         rate, sample = cpu_token_rate(1, args.cpu_layer_steps, 1)
         line["cpu_baseline"] = {"value": rate, "unit": "tokens/s", "cores": 1, "kind": "port", "sample": sample}

@@ -281,6 +281,9 @@ int vox_tp_prefill(vox_tp* tp, const int32_t* tokens, size_t n, size_t pos0);
 int vox_tp_generate(vox_tp* tp, int32_t token, size_t pos, size_t n_steps, int32_t* tokens_out);
 /* Device ring state of a layer: len_tokens, start slot, pos_offset. */
 int vox_tp_kv_state(const vox_tp* tp, size_t layer, int64_t out[3]);
+/* Forget every cached token (all layers back to len 0, pos_offset 0); local,
+ * call it on every rank between the same two steps. */
+int vox_tp_reset(vox_tp* tp);
 int vox_tp_record_event(vox_tp* tp, int slot);  /* slots 0..7 */
 int vox_tp_event_elapsed_ms(vox_tp* tp, int slot_a, int slot_b, float* ms);
 uint64_t vox_tp_kernel_launches(const vox_tp* tp);

@@ -1,5 +1,6 @@
-"""Tensor-parallel decoding on 2 GPUs (one process per GPU, NCCL all-reduce
-of the residual stream) against the oracle; skipped on a single GPU."""
+"""Tensor-parallel decoding on 2, 4 and 8 GPUs (one process per GPU; the
+residual stream exchanged through peer memory or NCCL) against the oracle;
+each world size is skipped when the box has fewer GPUs."""
 import os
 import socket
 import subprocess
@@ -26,12 +27,14 @@ def _port():
         return s.getsockname()[1]
 
 
-@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("case,exchange", [("small", "nccl"), ("small", "peer"), ("full", "peer"),
                                            ("switch", "peer")])
-def test_tensor_parallel_two_gpus(case, exchange):
+def test_tensor_parallel(case, exchange, world):
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
+           "--nproc-per-node", str(world), "--master-addr", "127.0.0.1", "--master-port", str(_port()),
            os.path.join(ROOT, "tests", "tp_worker.py"), "--case", case, "--exchange", exchange]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True)

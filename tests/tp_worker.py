@@ -1,6 +1,6 @@
 """One rank of the tensor-parallel parity check (run by tests/test_gpu_tp.py
-under torch.distributed.run, one process per GPU): this rank's logit slice
-and the greedy tokens against the oracle's full model."""
+under torch.distributed.run, one process per GPU, 2, 4 or 8 ranks): this
+rank's logit slice and the greedy tokens against the oracle's full model."""
 import argparse
 import os
 import sys
@@ -12,7 +12,8 @@ sys.path.insert(0, ROOT)
 
 from tests.vox_testlib import FULL, assert_logits_close, config_dict, oracle_model, top2_margin, vox  # noqa: E402
 
-SMALL = config_dict(dim=256, hidden_dim=512, n_heads=8, n_kv_heads=2, head_dim=32, sliding_window=64,
+# 8 kv heads (4 q heads each, the model's group) so that every case shards 2, 4 and 8 ways
+SMALL = config_dict(dim=256, hidden_dim=512, n_heads=32, n_kv_heads=8, head_dim=32, sliding_window=64,
                     rope_theta=1e4)
 # (config, layers, vocab, checked steps, prefilled tokens before them)
 CASES = {

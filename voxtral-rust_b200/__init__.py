@@ -179,6 +179,7 @@ _SIGS = {
     "vox_tp_prefill": ([VP, I32P, SZ, SZ], C.c_int),
     "vox_tp_generate": ([VP, C.c_int32, SZ, SZ, I32P], C.c_int),
     "vox_tp_kv_state": ([VP, SZ, C.POINTER(C.c_int64)], C.c_int),
+    "vox_tp_reset": ([VP], C.c_int),
     "vox_tp_record_event": ([VP, C.c_int], C.c_int),
     "vox_tp_event_elapsed_ms": ([VP, C.c_int, C.c_int, F32P], C.c_int),
     "vox_tp_kernel_launches": ([VP], C.c_uint64),
@@ -871,6 +872,10 @@ class TensorParallelDecoder:
         out = (C.c_int64 * 3)()
         _check(lib().vox_tp_kv_state(self.h, layer, out))
         return tuple(out)
+
+    def reset(self):
+        """Empty the rank's cache (every rank, between the same two steps)."""
+        _check(lib().vox_tp_reset(self.h))
 
     def record_event(self, slot):
         _check(lib().vox_tp_record_event(self.h, slot))

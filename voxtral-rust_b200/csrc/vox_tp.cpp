@@ -829,6 +829,16 @@ int vox_tp_kv_state(const vox_tp* t, size_t layer, int64_t out[3]) {
     return VOX_OK;
 }
 
+int vox_tp_reset(vox_tp* t) {
+    if (!t) return report_errorf(VOX_ERR_INVALID_ARG, "tensor-parallel context is null");
+    TP_CUDA(cudaSetDevice(t->dev));
+    TP_CUDA(cudaStreamSynchronize(t->stream));
+    TP_CUDA(cudaMemsetAsync(t->dstate, 0, t->layers.size() * sizeof(KvState), t->stream));
+    TP_CUDA(cudaStreamSynchronize(t->stream));
+    for (HostKv& h : t->hs) h = HostKv{};
+    return VOX_OK;
+}
+
 int vox_tp_record_event(vox_tp* t, int slot) {
     if (!t || slot < 0 || slot >= 8) return report_errorf(VOX_ERR_INVALID_ARG, "bad event slot");
     TP_CUDA(cudaEventRecord(t->ev[slot], t->stream));
