@@ -284,6 +284,13 @@ int vox_tp_kv_state(const vox_tp* tp, size_t layer, int64_t out[3]);
 /* Forget every cached token (all layers back to len 0, pos_offset 0); local,
  * call it on every rank between the same two steps. */
 int vox_tp_reset(vox_tp* tp);
+/* Watchdog bound (default 30000 ms) on every wait of a step: a step that does
+ * not finish in time (another rank stopped calling) returns
+ * VOX_ERR_DEVICE_TIMEOUT after aborting the NCCL communicator (asynchronous
+ * NCCL errors abort it at once); with the peer-memory exchange the kernels'
+ * own bounded waits (2 s) end the step.  The context is then unusable: every
+ * later step fails; destroy it. */
+int vox_tp_set_timeout_ms(vox_tp* tp, unsigned timeout_ms);
 int vox_tp_record_event(vox_tp* tp, int slot);  /* slots 0..7 */
 int vox_tp_event_elapsed_ms(vox_tp* tp, int slot_a, int slot_b, float* ms);
 uint64_t vox_tp_kernel_launches(const vox_tp* tp);

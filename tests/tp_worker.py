@@ -26,12 +26,49 @@ CASES = {
 }
 
 
+def leave(V, dist, rank, world, local):
+    """Failure detection with the peer-memory exchange: every rank runs three
+    steps, then the last rank stops calling (it stays alive, between steps,
+    with nothing in flight).  The others' next step must end with
+    VOX_ERR_DEVICE_TIMEOUT through the kernels' bounded peer waits, and the
+    context must refuse further steps.  NCCL is not used here."""
+    import time
+    c = SMALL
+    uid = V.share_tp_unique_id(rank)
+    failures = []
+    with V.TensorParallelDecoder(V.DecoderConfig(**c), rank, world, uid, 2, 1024, device=local) as tp:
+        tp.init_random(0, 0.02)
+        tp.connect_peers()
+        tp.set_timeout_ms(20000)
+        for p in range(3):
+            tp.step(5 + p, p)
+        if rank != world - 1:
+            t0 = time.time()
+            try:
+                tp.step(9, 3)
+                failures.append("the step after a rank stopped did not fail")
+            except V.VoxError as e:
+                if e.code != V.ERR_DEVICE_TIMEOUT:
+                    failures.append(f"unexpected error {e}")
+            if time.time() - t0 > 15:
+                failures.append(f"the failed step took {time.time() - t0:.1f} s")
+            try:
+                tp.step(9, 4)
+                failures.append("a broken context accepted another step")
+            except V.VoxError as e:
+                if e.code != V.ERR_DEVICE_TIMEOUT:
+                    failures.append(f"unexpected error {e}")
+        dist.barrier()  # the stopped rank waits here, alive, until the others are done
+    print(f"rank {rank}: case leave (peer), failures {failures}", flush=True)
+    return failures
+
+
 def main():
     import datetime
 
     import torch.distributed as dist
     ap = argparse.ArgumentParser()
-    ap.add_argument("--case", default="small", choices=sorted(CASES))
+    ap.add_argument("--case", default="small", choices=sorted(CASES) + ["leave"])
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="peer: stores into the other GPUs' memory fused into the GEMVs; nccl: all-reduce")
     args = ap.parse_args()
@@ -39,6 +76,11 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", rank))
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
     V = vox()
+    if args.case == "leave":
+        failures = leave(V, dist, rank, world, local)
+        dist.barrier()
+        dist.destroy_process_group()
+        sys.exit(1 if failures else 0)
     from oracle import oracle as o
     o.build()
     o.set_threads(max(1, (os.cpu_count() or 2) // world))

@@ -180,6 +180,7 @@ _SIGS = {
     "vox_tp_generate": ([VP, C.c_int32, SZ, SZ, I32P], C.c_int),
     "vox_tp_kv_state": ([VP, SZ, C.POINTER(C.c_int64)], C.c_int),
     "vox_tp_reset": ([VP], C.c_int),
+    "vox_tp_set_timeout_ms": ([VP, C.c_uint], C.c_int),
     "vox_tp_record_event": ([VP, C.c_int], C.c_int),
     "vox_tp_event_elapsed_ms": ([VP, C.c_int, C.c_int, F32P], C.c_int),
     "vox_tp_kernel_launches": ([VP], C.c_uint64),
@@ -876,6 +877,10 @@ class TensorParallelDecoder:
     def reset(self):
         """Empty the rank's cache (every rank, between the same two steps)."""
         _check(lib().vox_tp_reset(self.h))
+
+    def set_timeout_ms(self, ms):
+        """Watchdog bound on every wait of a step (vox_tp_set_timeout_ms)."""
+        _check(lib().vox_tp_set_timeout_ms(self.h, int(ms)))
 
     def record_event(self, slot):
         _check(lib().vox_tp_record_event(self.h, slot))

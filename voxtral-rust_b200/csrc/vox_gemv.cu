@@ -192,7 +192,11 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
     if (xsum) {
         if (tid == 0) {
             const unsigned long long target = (__ldcg(A.tp_steps) + 1ull) * A.xch_arrivals;
-            if (!wait_counter_sys(A.xa.counter(A.xch[A.xa.rank], A.xch_in), target)) raise_error(A.err, ERR_PEER_WAIT);
+            // Once one wait of the step has expired (a rank stopped), the rest
+            // are skipped so that the step ends within one wait limit.
+            const bool expired = (*reinterpret_cast<volatile unsigned*>(A.err) & ERR_PEER_WAIT) != 0u;
+            if (!expired && !wait_counter_sys(A.xa.counter(A.xch[A.xa.rank], A.xch_in), target))
+                raise_error(A.err, ERR_PEER_WAIT);
         }
         named_barrier_sync(1, kConsumerWarps * 32);
     }

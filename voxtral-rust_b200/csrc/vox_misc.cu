@@ -165,7 +165,8 @@ __global__ void __launch_bounds__(256) tp_argmax_xch_kernel(const ArgmaxPart* pa
         unsigned char* own = xch[xa.rank];
         const unsigned long long done = *reinterpret_cast<volatile unsigned long long*>(tp_steps);
         unsigned long long k = 0ull;
-        if (wait_counter_sys(xa.key_counter(own), (done + 1ull) * (unsigned long long)xa.size)) {
+        const bool expired = (*reinterpret_cast<volatile unsigned*>(err) & ERR_PEER_WAIT) != 0u;
+        if (!expired && wait_counter_sys(xa.key_counter(own), (done + 1ull) * (unsigned long long)xa.size)) {
             for (int r = 0; r < xa.size; ++r) {
                 const unsigned long long kr = __ldcg(xa.keys(own) + r);
                 if (kr > k) k = kr;

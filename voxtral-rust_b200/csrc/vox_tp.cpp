@@ -35,6 +35,7 @@
 #include "../../include/vox_decoder.h"
 #include "vox_host.h"
 #include "vox_kernels.h"
+#include "vox_watchdog.h"
 
 using namespace vox;
 
@@ -62,6 +63,9 @@ struct NcclApi {
                                cudaStream_t) = nullptr;
     ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
     const char* (*error_string)(ncclResult_t) = nullptr;
+    // watchdog (optional symbols): poll for asynchronous errors, abort a stuck communicator
+    ncclResult_t (*comm_get_async_error)(ncclComm_t, ncclResult_t*) = nullptr;
+    ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
 };
 
 int nccl(const NcclApi** out) {
@@ -77,6 +81,9 @@ int nccl(const NcclApi** out) {
             api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
             api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
             api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+            api.comm_get_async_error =
+                reinterpret_cast<decltype(api.comm_get_async_error)>(dlsym(h, "ncclCommGetAsyncError"));
+            api.comm_abort = reinterpret_cast<decltype(api.comm_abort)>(dlsym(h, "ncclCommAbort"));
             api.ok = api.get_unique_id && api.comm_init_rank && api.all_reduce && api.comm_destroy &&
                      api.error_string;
         }
@@ -151,19 +158,61 @@ struct vox_tp {
     unsigned char** xch_ptrs = nullptr;         // device array [size]: every rank's area
     unsigned long long* tp_steps = nullptr;     // steps completed (device)
     bool p2p = false;
+    // watchdog: every host wait on the stream is bounded by timeout_ms; a
+    // step that does not finish in time (a rank stopped) aborts the NCCL
+    // communicator and leaves the context broken (every later call fails)
+    unsigned timeout_ms = 30000;
+    bool broken = false;
     size_t layer_elems() const { return sh.n_kv_heads * cap * cfg.head_dim; }
 };
 
 namespace {
 
+// Wait for the stream with the watchdog (vox_watchdog.h): poll, abort the
+// communicator on an asynchronous NCCL error or after timeout_ms.
+int tp_wait(vox_tp* t) {
+    cudaError_t stream_err = cudaSuccess;
+    ncclResult_t async_err = ncclSuccess;
+    auto query = [&]() {
+        stream_err = cudaStreamQuery(t->stream);
+        return stream_err == cudaSuccess ? 0 : stream_err == cudaErrorNotReady ? 1 : 2;
+    };
+    auto async_error = [&]() {
+        if (!t->comm || !t->api || !t->api->comm_get_async_error) return false;
+        ncclResult_t ar = ncclSuccess;
+        if (t->api->comm_get_async_error(t->comm, &ar) != ncclSuccess) return false;
+        async_err = ar;
+        return ar != ncclSuccess && ar != ncclInProgress;
+    };
+    auto abort = [&]() {
+        t->broken = true;
+        if (t->comm && t->api && t->api->comm_abort) t->api->comm_abort(t->comm);
+        if (t->api && t->api->comm_abort) t->comm = nullptr;
+    };
+    switch (watchdog_wait(query, async_error, abort, t->timeout_ms)) {
+        case kWatchdogIdle:
+            return VOX_OK;
+        case kWatchdogAsyncError:
+            return report_errorf(VOX_ERR_CUDA, "NCCL reported an asynchronous error (%s); communicator aborted",
+                                 t->api->error_string(async_err));
+        case kWatchdogTimeout:
+            return report_errorf(VOX_ERR_DEVICE_TIMEOUT,
+                                 "tensor-parallel step not finished after %u ms (a rank stopped?); the context is "
+                                 "no longer usable", t->timeout_ms);
+        default:
+            return report_errorf(VOX_ERR_CUDA, "tensor-parallel stream failed: %s", cudaGetErrorString(stream_err));
+    }
+}
+
 int check_errors(vox_tp* t) {
     TP_CUDA(cudaMemcpyAsync(t->h_err, t->err, sizeof(unsigned), cudaMemcpyDeviceToHost, t->stream));
-    TP_CUDA(cudaStreamSynchronize(t->stream));
+    TP_TRY(tp_wait(t));
     const unsigned bits = *t->h_err;
     if (!bits) return VOX_OK;
     TP_CUDA(cudaMemsetAsync(t->err, 0, sizeof(unsigned), t->stream));
     TP_CUDA(cudaMemsetAsync(t->tickets, 0, t->sh.n_kv_heads * sizeof(unsigned), t->stream));
-    TP_CUDA(cudaStreamSynchronize(t->stream));
+    TP_TRY(tp_wait(t));
+    if (bits & ERR_PEER_WAIT) t->broken = true;  // the ranks' exchange counters no longer agree
     if (bits & (ERR_FULL_WAIT | ERR_EMPTY_WAIT | ERR_DRAIN_WAIT | ERR_PEER_WAIT))
         return report_errorf(VOX_ERR_DEVICE_TIMEOUT, "a bounded wait inside a kernel expired (bits 0x%x)", bits);
     if (bits & ERR_POS_RANGE) return report_errorf(VOX_ERR_RANGE, "position beyond the RoPE table");
@@ -349,6 +398,8 @@ void release_graphs(vox_tp* t) {
 
 int ready(vox_tp* t) {
     if (!t) return report_errorf(VOX_ERR_INVALID_ARG, "tensor-parallel context is null");
+    if (t->broken)
+        return report_errorf(VOX_ERR_DEVICE_TIMEOUT, "a previous step timed out (a rank stopped); destroy this context");
     if (!t->embed_ready || !t->head_ready) return report_errorf(VOX_ERR_NOT_READY, "embedding or LM head not uploaded");
     for (size_t l = 0; l < t->layers.size(); ++l)
         if (!t->layers[l].ready) return report_errorf(VOX_ERR_NOT_READY, "layer %zu weights not uploaded", l);
@@ -449,7 +500,12 @@ int vox_tp_unique_id(unsigned char id[128]) {
 void vox_tp_destroy(vox_tp* t) {
     if (!t) return;
     cudaSetDevice(t->dev);
-    if (t->stream) cudaStreamSynchronize(t->stream);
+    if (t->stream) {
+        const unsigned keep = t->timeout_ms;
+        if (tp_wait(t) != VOX_OK) cudaGetLastError();  // bounded: aborts a stuck communicator
+        t->timeout_ms = keep;
+        cudaStreamSynchronize(t->stream);
+    }
     release_graphs(t);  // they hold NCCL calls: release before the communicator
     if (t->comm && t->api) t->api->comm_destroy(t->comm);
     for (unsigned char* m : t->peer_maps)
@@ -753,7 +809,7 @@ int vox_tp_step(vox_tp* t, int32_t token, size_t pos, int32_t* next_token, float
     TP_TRY(ready(t));
     if (token < 0 || (size_t)token >= t->sh.vocab) return report_errorf(VOX_ERR_RANGE, "token %d outside the vocabulary", token);
     if (pos >= (size_t)t->max_pos) return report_errorf(VOX_ERR_RANGE, "position %zu beyond max_positions", pos);
-    TP_CUDA(cudaStreamSynchronize(t->stream));
+    TP_TRY(tp_wait(t));
     StepState* hs = t->h_steps;
     memset(hs, 0, sizeof(StepState));
     hs->pos = (int64_t)pos;
@@ -777,7 +833,7 @@ int vox_tp_prefill(vox_tp* t, const int32_t* tokens, size_t n, size_t pos0) {
     for (size_t i = 0; i < n; ++i)
         if (tokens[i] < 0 || (size_t)tokens[i] >= t->sh.vocab)
             return report_errorf(VOX_ERR_RANGE, "token %d outside the vocabulary", tokens[i]);
-    TP_CUDA(cudaStreamSynchronize(t->stream));
+    TP_TRY(tp_wait(t));
     TP_TRY(ensure_host_steps(t, n));
     for (size_t i = 0; i < n; ++i) {
         StepState* hs = t->h_steps + i;
@@ -797,7 +853,7 @@ int vox_tp_generate(vox_tp* t, int32_t token, size_t pos, size_t n_steps, int32_
     if (n_steps == 0) return VOX_OK;
     if (token < 0 || (size_t)token >= t->sh.vocab) return report_errorf(VOX_ERR_RANGE, "token %d outside the vocabulary", token);
     if (pos + n_steps > (size_t)t->max_pos) return report_errorf(VOX_ERR_RANGE, "positions beyond max_positions");
-    TP_CUDA(cudaStreamSynchronize(t->stream));
+    TP_TRY(tp_wait(t));
     TP_TRY(ensure_host_steps(t, n_steps + 1));
     StepState* hs = t->h_steps;
     memset(hs, 0, sizeof(StepState));
@@ -826,6 +882,12 @@ int vox_tp_kv_state(const vox_tp* t, size_t layer, int64_t out[3]) {
     out[0] = d.len;
     out[1] = d.start;
     out[2] = d.pos_offset;
+    return VOX_OK;
+}
+
+int vox_tp_set_timeout_ms(vox_tp* t, unsigned timeout_ms) {
+    if (!t || timeout_ms == 0) return report_errorf(VOX_ERR_INVALID_ARG, "null context or zero timeout");
+    t->timeout_ms = timeout_ms;
     return VOX_OK;
 }
 
