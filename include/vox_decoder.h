@@ -443,6 +443,48 @@ int vox_tekken_decode_token_bytes(const vox_tekken* t, uint32_t token_id, const 
  * text's byte length; writes at most cap - 1 bytes plus a NUL (out nullable). */
 size_t vox_tekken_decode_to_utf8_lossy(const vox_tekken* t, const uint32_t* ids, size_t n, char* out, size_t cap);
 
+/* ---- encoder front end on the GPU (mel.rs, conv.rs) -------------------------------- */
+/* MelCtx (mel.rs:114-272): incremental log-mel frames [frames, 128] of 16 kHz
+ * audio (periodic Hann 400, hop 160, 201-bin DFT, Slaney mel filters, log10
+ * clamp), computed on `device`.  The internal buffer starts with
+ * 200 + left_pad_samples zeros, as MelCtx::new does. */
+typedef struct vox_mel vox_mel;
+int vox_mel_create(int device, size_t left_pad_samples, vox_mel** out);
+void vox_mel_destroy(vox_mel* m);
+size_t vox_mel_left_pad_samples(const vox_mel* m);                  /* mel.rs:154 */
+/* feed (mel.rs:159-166): append samples, compute every complete frame;
+ * *new_frames (nullable) receives how many. */
+int vox_mel_feed(vox_mel* m, const float* samples, size_t n, size_t* new_frames);
+/* finish (mel.rs:170-202): right_pad_samples zeros, a 200-sample reflection,
+ * the remaining frames, then the last frame dropped. */
+int vox_mel_finish(vox_mel* m, size_t right_pad_samples);
+size_t vox_mel_frames(const vox_mel* m);
+/* data (mel.rs:206): frames [first, first + n) copied to out [n, 128]. */
+int vox_mel_data(vox_mel* m, size_t first_frame, size_t n_frames, float* out);
+
+/* ConvStemState (conv.rs:134-347) with ConvStemWeights (conv.rs:80-87):
+ * conv0 (mel_bins -> dim, kernel 3, stride 1) and conv1 (dim -> dim, kernel 3,
+ * stride 2), causal, GELU (tanh form) after each, on `device`.  Weights are
+ * [dim, cin, 3] f32 host arrays (copied). */
+typedef struct vox_conv_stem vox_conv_stem;
+int vox_conv_stem_create(int device, size_t mel_bins, size_t dim, const float* conv0_weight,
+                         const float* conv0_bias, const float* conv1_weight, const float* conv1_bias,
+                         vox_conv_stem** out);
+void vox_conv_stem_destroy(vox_conv_stem* s);
+/* process (conv.rs:163-334): mel_new [n_new, mel_bins] host; out [*n_out, dim]
+ * host with room for out_cap_rows rows (n_new / 2 + 1 always suffice). */
+int vox_conv_stem_process(vox_conv_stem* s, const float* mel_new, size_t n_new, float* out,
+                          size_t out_cap_rows, size_t* n_out);
+/* causal_conv1d_colmajor (conv.rs:28-73) for kernel 3, stride 1 or 2, with
+ * gelu_inplace (conv.rs:11-19) after it when apply_gelu; input [cin, length]
+ * and output [cout, vox_conv_out_len(length, 3, stride)] column-major host
+ * arrays; bias nullable. */
+size_t vox_conv_out_len(size_t length, size_t kernel, size_t stride);
+int vox_causal_conv1d_gelu(int device, const float* input, const float* weight, const float* bias, size_t cin,
+                           size_t cout, size_t length, size_t stride, int apply_gelu, float* output);
+/* Kernel launches issued by a mel context and a conv stem (either nullable). */
+uint64_t vox_encoder_kernel_launches(const vox_mel* m, const vox_conv_stem* s);
+
 /* ---- profiling hook (no reference counterpart) --------------------------------- */
 /* Times one of the step's weight-streaming GEMVs on its own: n_launches
  * back-to-back launches (cycling over the layers, so every launch streams a

@@ -126,6 +126,30 @@ def lib():
         L.vo_f32_to_bf16_rne.argtypes = [C.c_float]
         L.vo_f32_to_bf16_rne.restype = C.c_uint16
         L.vo_set_threads.argtypes = [C.c_int]
+        L.vo_mel_build_filters.argtypes = [F32P]
+        L.vo_mel_build_dft.argtypes = [F32P, F32P]
+        L.vo_mel_build_window.argtypes = [F32P]
+        L.vo_mel_new.argtypes = [SZ]
+        L.vo_mel_new.restype = C.c_void_p
+        L.vo_mel_free.argtypes = [C.c_void_p]
+        L.vo_mel_left_pad_samples.argtypes = [C.c_void_p]
+        L.vo_mel_left_pad_samples.restype = SZ
+        L.vo_mel_feed.argtypes = [C.c_void_p, F32P, SZ]
+        L.vo_mel_feed.restype = SZ
+        L.vo_mel_finish.argtypes = [C.c_void_p, SZ]
+        L.vo_mel_frames.argtypes = [C.c_void_p]
+        L.vo_mel_frames.restype = SZ
+        L.vo_mel_data.argtypes = [C.c_void_p]
+        L.vo_mel_data.restype = F32P
+        L.vo_gelu_inplace.argtypes = [F32P, SZ]
+        L.vo_conv_out_len.argtypes = [SZ, SZ, SZ]
+        L.vo_conv_out_len.restype = SZ
+        L.vo_causal_conv1d_colmajor.argtypes = [F32P, F32P, F32P, F32P, SZ, SZ, SZ, SZ, SZ]
+        L.vo_conv_stem_new.argtypes = [SZ, SZ]
+        L.vo_conv_stem_new.restype = C.c_void_p
+        L.vo_conv_stem_free.argtypes = [C.c_void_p]
+        L.vo_conv_stem_process.argtypes = [C.c_void_p, F32P, F32P, F32P, F32P, F32P, SZ, F32P]
+        L.vo_conv_stem_process.restype = SZ
         _lib = L
     return _lib
 
@@ -423,6 +447,91 @@ class PipelineState:
 
     def is_finished(self):
         return bool(self.c.finished)
+
+
+# ---- encoder front end (mel.rs, conv.rs) ---------------------------------------
+
+MEL_BINS, N_FREQ, N_FFT = 128, 201, 400
+
+
+def mel_tables():
+    """(filters [128, 201], dft cos [201, 400], dft sin [201, 400], Hann [400]) (mel.rs:42-106)."""
+    f = np.zeros(MEL_BINS * N_FREQ, np.float32)
+    c = np.zeros(N_FREQ * N_FFT, np.float32)
+    s_ = np.zeros(N_FREQ * N_FFT, np.float32)
+    w = np.zeros(N_FFT, np.float32)
+    lib().vo_mel_build_filters(_p(f))
+    lib().vo_mel_build_dft(_p(c), _p(s_))
+    lib().vo_mel_build_window(_p(w))
+    return f.reshape(MEL_BINS, N_FREQ), c.reshape(N_FREQ, N_FFT), s_.reshape(N_FREQ, N_FFT), w
+
+
+class MelCtx:
+    """MelCtx (mel.rs:114-272): incremental log-mel frames [frames, 128]."""
+
+    def __init__(self, left_pad_samples=0):
+        self.h = lib().vo_mel_new(left_pad_samples)
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().vo_mel_free(self.h)
+            self.h = None
+
+    def left_pad_samples(self):
+        return lib().vo_mel_left_pad_samples(self.h)
+
+    def feed(self, x):
+        x = _f32(x)
+        return lib().vo_mel_feed(self.h, _p(x), x.size)
+
+    def finish(self, right_pad_samples=0):
+        lib().vo_mel_finish(self.h, right_pad_samples)
+
+    def data(self):
+        n = lib().vo_mel_frames(self.h)
+        if n == 0:
+            return np.zeros((0, MEL_BINS), np.float32), 0
+        p = lib().vo_mel_data(self.h)
+        return np.ctypeslib.as_array(p, shape=(n * MEL_BINS,)).copy().reshape(n, MEL_BINS), n
+
+
+def gelu(x):
+    """gelu_inplace (conv.rs:11-19) on a copy."""
+    y = _f32(x).copy()
+    lib().vo_gelu_inplace(_p(y), y.size)
+    return y
+
+
+def causal_conv1d_colmajor(x, w, b, cin, cout, length, kernel, stride):
+    """causal_conv1d_colmajor (conv.rs:28-73): x [cin, length] -> [cout, out_len]."""
+    n = lib().vo_conv_out_len(length, kernel, stride)
+    out = np.zeros(cout * n, np.float32)
+    xx, ww = _f32(x), _f32(w)
+    bb = _f32(b) if b is not None else None
+    lib().vo_causal_conv1d_colmajor(_p(out), _p(xx), _p(ww), _p(bb) if bb is not None else None,
+                                    cin, cout, length, kernel, stride)
+    return out.reshape(cout, n)
+
+
+class ConvStemState:
+    """ConvStemState (conv.rs:134-347): mel frames [n, mel_bins] -> positions [m, dim]."""
+
+    def __init__(self, mel_bins, dim, w0, b0, w1, b1):
+        self.h = lib().vo_conv_stem_new(mel_bins, dim)
+        self.mel_bins, self.dim = mel_bins, dim
+        self.w = [_f32(w0), _f32(b0), _f32(w1), _f32(b1)]
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().vo_conv_stem_free(self.h)
+            self.h = None
+
+    def process(self, mel_new):
+        mel_new = _f32(mel_new)
+        n = mel_new.size // self.mel_bins
+        out = np.zeros((n // 2 + 2) * self.dim, np.float32)
+        m = lib().vo_conv_stem_process(self.h, *[_p(a) for a in self.w], _p(mel_new), n, _p(out))
+        return out[:m * self.dim].reshape(m, self.dim)
 
 
 # ---- seeded synthetic data ---------------------------------------------------

@@ -173,6 +173,29 @@ void vo_gen_uniform_ids(uint64_t seed, uint64_t tensor_id, uint32_t bound,
                         uint64_t first, size_t n, int32_t* out);
 uint16_t vo_f32_to_bf16_rne(float f);
 
+/* ---- encoder front end (mel.rs, conv.rs; vox_oracle_encoder.c) ---------- */
+typedef struct vo_mel vo_mel;
+void vo_mel_build_filters(float* filters);          /* [128, 201] */
+void vo_mel_build_dft(float* cos_t, float* sin_t);  /* [201, 400] each */
+void vo_mel_build_window(float* w);                 /* [400] */
+vo_mel* vo_mel_new(size_t left_pad_samples);
+void vo_mel_free(vo_mel* m);
+size_t vo_mel_left_pad_samples(const vo_mel* m);
+size_t vo_mel_feed(vo_mel* m, const float* x, size_t n);
+void vo_mel_finish(vo_mel* m, size_t right_pad_samples);
+size_t vo_mel_frames(const vo_mel* m);
+const float* vo_mel_data(const vo_mel* m);          /* [frames, 128] */
+
+void vo_gelu_inplace(float* x, size_t n);
+size_t vo_conv_out_len(size_t length, size_t kernel, size_t stride);
+void vo_causal_conv1d_colmajor(float* output, const float* input, const float* weight, const float* bias,
+                               size_t cin, size_t cout, size_t length, size_t kernel, size_t stride);
+typedef struct vo_conv_stem vo_conv_stem;
+vo_conv_stem* vo_conv_stem_new(size_t mel_bins, size_t dim);
+void vo_conv_stem_free(vo_conv_stem* s);
+size_t vo_conv_stem_process(vo_conv_stem* s, const float* w0, const float* b0, const float* w1, const float* b1,
+                            const float* mel_new, size_t n_new, float* out);
+
 #ifdef __cplusplus
 }
 #endif

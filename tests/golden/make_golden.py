@@ -20,6 +20,9 @@ text and re-run against the oracle and the CUDA library):
   weights.rs:141-193  loads_f32_and_bf16_tensors
   tokenizer.rs:219-257 tokenizer_decodes_basic_tokens
   tokenizer.rs:259-286 default_prompt_has_expected_length
+  mel.rs:277-294   silence_has_constant_value
+  mel.rs:296-310   finish_drops_last_frame
+  conv.rs:472-568  incremental_conv_matches_offline_even_length (LCG seed 1 x0.01, mel seed 123)
 
 The 32-bit LCG below is the one the reference tests use
 (seed = seed*1664525 + 1013904223; value = (seed>>8)/2^24*2-1, in f32).
@@ -244,6 +247,32 @@ def reference_unit_tests():
                                {"rank": 3, "token_str": "[STREAMING_PAD]", "is_control": True}],
             "vocab": [], "audio": audio}),
         "expect_len": 1 + 32 + 6, "expect_first": 1, "expect_rest": 3,
+    }
+    # mel.rs:277-294 and :296-310 (MelCtx with no extra left padding)
+    tests["silence_has_constant_value"] = {
+        "cite": "crates/voxtral/src/mel.rs:277-294",
+        "left_pad_samples": 0, "expect_left_pad": 200, "feed_zeros": 400, "expect_frames": 2,
+        "expect_value": -0.625, "tol": 1e-6,
+    }
+    fed = 1600
+    tests["finish_drops_last_frame"] = {
+        "cite": "crates/voxtral/src/mel.rs:296-310",
+        "feed_zeros": fed, "expect_frames_after_finish": ((200 + fed + 200 - 400) // 160 + 1) - 1,
+    }
+    # conv.rs:472-568: ConvStemWeights::fake (conv.rs:92-131) draws conv0_weight,
+    # conv0_bias, conv1_weight, conv1_bias in that order from one LCG (seed 1), x0.01
+    mel_bins, dim, frames = 8, 16, 40
+    st = 1
+    w0, st = lcg_values(st, dim * mel_bins * 3, 0.01)
+    b0, st = lcg_values(st, dim, 0.01)
+    w1, st = lcg_values(st, dim * dim * 3, 0.01)
+    b1, st = lcg_values(st, dim, 0.01)
+    mel, _ = lcg_values(123, frames * mel_bins)
+    tests["incremental_conv_matches_offline_even_length"] = {
+        "cite": "crates/voxtral/src/conv.rs:472-568",
+        "mel_bins": mel_bins, "dim": dim, "frames": frames, "chunks": [7, 3, 11, 5, 14],
+        "conv0_weight": w0.tolist(), "conv0_bias": b0.tolist(), "conv1_weight": w1.tolist(),
+        "conv1_bias": b1.tolist(), "mel": mel.tolist(), "conv0_bit_exact": True, "tol": 1e-4,
     }
     return tests
 

@@ -213,6 +213,19 @@ _SIGS = {
     "vox_tekken_default_prompt_ids": ([VP, C.POINTER(C.c_uint32), SZ, C.POINTER(SZ)], C.c_int),
     "vox_tekken_decode_token_bytes": ([VP, C.c_uint32, C.POINTER(C.POINTER(C.c_uint8)), C.POINTER(SZ)], C.c_int),
     "vox_tekken_decode_to_utf8_lossy": ([VP, C.POINTER(C.c_uint32), SZ, C.c_char_p, SZ], SZ),
+    "vox_mel_create": ([C.c_int, SZ, C.POINTER(VP)], C.c_int),
+    "vox_mel_destroy": ([VP], None),
+    "vox_mel_left_pad_samples": ([VP], SZ),
+    "vox_mel_feed": ([VP, F32P, SZ, C.POINTER(SZ)], C.c_int),
+    "vox_mel_finish": ([VP, SZ], C.c_int),
+    "vox_mel_frames": ([VP], SZ),
+    "vox_mel_data": ([VP, SZ, SZ, F32P], C.c_int),
+    "vox_conv_stem_create": ([C.c_int, SZ, SZ, F32P, F32P, F32P, F32P, C.POINTER(VP)], C.c_int),
+    "vox_conv_stem_destroy": ([VP], None),
+    "vox_conv_stem_process": ([VP, F32P, SZ, F32P, SZ, C.POINTER(SZ)], C.c_int),
+    "vox_conv_out_len": ([SZ, SZ, SZ], SZ),
+    "vox_causal_conv1d_gelu": ([C.c_int, F32P, F32P, F32P, SZ, SZ, SZ, SZ, C.c_int, F32P], C.c_int),
+    "vox_encoder_kernel_launches": ([VP, VP], C.c_uint64),
     "vox_stream_prompt_config_default": ([C.POINTER(StreamPromptConfig)], None),
     "vox_stream_right_pad_tokens": ([C.POINTER(StreamPromptConfig)], SZ),
     "vox_stream_build_prompt_ids": ([C.c_uint32, C.c_uint32, C.POINTER(StreamPromptConfig),
@@ -595,6 +608,102 @@ def load_checkpoint(ctx: Context, store: WeightStore):
     """Upload a decoder checkpoint (layers.{l}.*, embedding, final norm, LM
     head or tied embedding) into a context."""
     _check(lib().vox_ctx_load_checkpoint(ctx.h, store.h))
+
+
+# ---------------------------------------------------------------------------
+# Encoder front end (mel.rs, conv.rs) on the GPU
+# ---------------------------------------------------------------------------
+
+MEL_BINS = 128
+
+
+class MelCtx:
+    """MelCtx (mel.rs:114-272) on the GPU: incremental log-mel frames [n, 128]."""
+
+    def __init__(self, left_pad_samples=0, device=0):
+        h = VP()
+        _check(lib().vox_mel_create(device, left_pad_samples, C.byref(h)))
+        self.h = h.value
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().vox_mel_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def left_pad_samples(self):
+        return int(lib().vox_mel_left_pad_samples(self.h))
+
+    def feed(self, samples):
+        x = _f32(samples)
+        n = SZ()
+        _check(lib().vox_mel_feed(self.h, _p(x), x.size, C.byref(n)))
+        return n.value
+
+    def finish(self, right_pad_samples=0):
+        _check(lib().vox_mel_finish(self.h, int(right_pad_samples)))
+
+    def frames(self):
+        return int(lib().vox_mel_frames(self.h))
+
+    def data(self, first=0, n=None):
+        """(frames [n, 128], total frame count), as MelCtx::data."""
+        total = self.frames()
+        n = total - first if n is None else n
+        out = np.empty((max(n, 0), MEL_BINS), np.float32)
+        if n > 0:
+            _check(lib().vox_mel_data(self.h, first, n, _p(out)))
+        return out, total
+
+
+class ConvStemState:
+    """ConvStemState (conv.rs:134-347) on the GPU; weights [dim, cin, 3] f32."""
+
+    def __init__(self, mel_bins, dim, conv0_weight, conv0_bias, conv1_weight, conv1_bias, device=0):
+        ws = [_f32(conv0_weight), _f32(conv0_bias), _f32(conv1_weight), _f32(conv1_bias)]
+        if ws[0].size != dim * mel_bins * 3 or ws[2].size != dim * dim * 3 or ws[1].size != dim or ws[3].size != dim:
+            raise ValueError("conv stem weight shapes do not match mel_bins / dim")
+        h = VP()
+        _check(lib().vox_conv_stem_create(device, mel_bins, dim, *[_p(w) for w in ws], C.byref(h)))
+        self.h = h.value
+        self.mel_bins, self.dim = mel_bins, dim
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().vox_conv_stem_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def process(self, mel_new):
+        """New mel frames [n, mel_bins] -> new positions [m, dim]."""
+        mel = _f32(mel_new)
+        n = mel.size // self.mel_bins
+        cap = n // 2 + 1
+        out = np.empty((cap, self.dim), np.float32)
+        got = SZ()
+        _check(lib().vox_conv_stem_process(self.h, _p(mel), n, _p(out), cap, C.byref(got)))
+        return out[:got.value].copy()
+
+
+def causal_conv1d_gelu(x, weight, bias, cin, cout, length, stride, gelu=True, device=0):
+    """causal_conv1d_colmajor (conv.rs:28-73), kernel 3, (+ gelu_inplace) on the GPU."""
+    n = int(lib().vox_conv_out_len(length, 3, stride))
+    out = np.zeros((cout, n), np.float32)
+    xx, ww = _f32(x), _f32(weight)
+    bb = _f32(bias) if bias is not None else None
+    _check(lib().vox_causal_conv1d_gelu(device, _p(xx), _p(ww), _p(bb), cin, cout, length, stride, 1 if gelu else 0,
+                                        _p(out)))
+    return out
 
 
 # ---------------------------------------------------------------------------

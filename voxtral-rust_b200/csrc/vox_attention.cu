@@ -873,8 +873,6 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_cluster_kernel(const Att
 
     if (tid < NW) mbar_init(&wbar[tid][0], 1);
     if (tid == 0) fence_barrier_init();
-    // The next launch's weights into L2 while this kernel waits on latency.
-    if (tid == 32) prefetch_share_l2(A.l2_prefetch, A.l2_prefetch_bytes, blockIdx.x, gridDim.x);
     // First cluster phase: every CTA of the cluster has started.  Its wait sits
     // just before the first store into the leader's shared memory, so it costs
     // nothing on the path (a CTA may write another's shared memory only once

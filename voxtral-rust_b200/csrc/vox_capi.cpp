@@ -215,8 +215,6 @@ struct vox_ctx {
     int tok_splits = 1;
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
-    // attention prefetches the o-proj weights into L2 (VOX_L2_PREFETCH=0 turns it off)
-    bool l2_prefetch_oproj = true;
     // multi-stream path
     unsigned char* head_t = nullptr;
     bool head_tiled = false;
@@ -493,10 +491,6 @@ int enqueue_layer(vox_ctx* c, vox_kv* kv, size_t l, bool from_embed, bool pdl, b
     at.out = c->attn;
     at.scale = 1.0f / sqrtf((float)c->cfg.head_dim);
     at.err = c->err;
-    if (c->l2_prefetch_oproj) {  // o-proj's weights, fetched into L2 during attention
-        at.l2_prefetch = static_cast<const unsigned char*>(L.wo);
-        at.l2_prefetch_bytes = (long long)(c->cfg.dim * c->q_dim * c->wsize);
-    }
     CUDA_TRY(record_launch(c, short_attn ? launch_attention_cluster(at, c->stream, pdl)
                                          : launch_attention(at, c->stream, pdl)));
 
@@ -1117,7 +1111,6 @@ int vox_ctx_create(const vox_decoder_config* cfg, const vox_ctx_options* opt, vo
                     prop.major, prop.minor);
 
     vox_ctx* c = new vox_ctx();
-    if (const char* e = std::getenv("VOX_L2_PREFETCH")) c->l2_prefetch_oproj = e[0] != '0';
     c->cfg = *cfg;
     c->opt = o;
     c->dev = o.device;

@@ -93,24 +93,6 @@ __device__ __forceinline__ void bulk_copy_g2s_nohint(void* dst, const void* src,
 }
 
 // Programmatic dependent launch (no-ops when launched without the attribute).
-// Prefetch [p, p + bytes) into L2 (no shared memory, no completion to wait
-// for); p 16-byte aligned, bytes a multiple of 16.
-__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
-// This CTA's share of a range split evenly (in 16-byte units) over the grid,
-// prefetched into L2 in pieces of at most 32 KB.  One thread calls it.
-__device__ __forceinline__ void prefetch_share_l2(const unsigned char* base, long long bytes, int cta, int n_cta) {
-    if (!base || bytes <= 0) return;
-    const long long units = bytes >> 4;
-    const long long u0 = units * cta / n_cta, u1 = units * (cta + 1) / n_cta;
-    for (long long u = u0; u < u1; u += 2048) {
-        const long long n = (u1 - u) < 2048 ? (u1 - u) : 2048;
-        bulk_prefetch_l2(base + (u << 4), (uint32_t)(n << 4));
-    }
-}
-
 __device__ __forceinline__ void pdl_wait_prior_grids() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
 }

@@ -152,11 +152,6 @@ struct AttnArgs {
     // non-null: the output also goes to this X operand of the next GEMM
     // (XOP layout, stream z in row z; see XOP_BYTES below)
     unsigned char* xop;
-    // non-null: the CTAs split [l2_prefetch, + l2_prefetch_bytes) among them
-    // and prefetch it into L2 at kernel start (the weights of the launch that
-    // follows, fetched while attention is latency-bound); 16-byte aligned
-    const unsigned char* l2_prefetch;
-    long long l2_prefetch_bytes;
 };
 
 // X operand of the multi-stream GEMM in global memory ("XOP" layout): for a
