@@ -22,6 +22,10 @@ context of the 512 + 1024-step workload) and "rolling" at the full 8192-token
 window, where every step evicts the oldest token; the rolling object also
 reports the ring state after the run against the kv.rs:48-88 index rule.
 
+An "encoder" object streams 10 s of synthetic audio per GPU through the
+encoder front end (log-mel + conv stem) in 80 ms chunks and reports audio
+seconds per second, beside the oracle on a 2 s sample.
+
 The same run then measures the multi-stream workload (8 independent streams
 per GPU, contexts uniform in [256, 4096) with the cache prefilled from
 N(0,1) bf16, greedy decode with tensor-core GEMMs) and reports it as the
@@ -409,6 +413,56 @@ TP_WORKLOAD = ("26-layer decoder, batch 1, tensor parallel over all GPUs (q|k|v,
                "2048 random ids then greedy decode")
 
 
+ENC_DIM, ENC_CHUNK, ENC_SECONDS = 1280, 1280, 10
+
+
+def run_encoder(V, local, cpu_sample_s=2.0):
+    """The encoder front end streaming synthetic 16 kHz audio (N(0, 0.1^2)) in
+    80 ms chunks (1280 samples, one decoder position each): log-mel + the
+    causal conv stem (128 mel bins -> dim 1280, weights ~N(0, 0.02) rounded to
+    bf16), through the public host-buffer API, so every chunk's samples go
+    host -> device and its positions device -> host.  Returns GPU and oracle
+    (1 thread, a cpu_sample_s-second sample) timings per second of audio."""
+    from oracle import oracle as o
+    o.build()
+    rng = np.random.default_rng(11)
+    audio = (0.1 * rng.standard_normal(16000 * ENC_SECONDS)).astype(np.float32)
+    w0 = o.bf16_to_f32(o.gen_normal_bf16(0, 7000, 0.02, ENC_DIM * 128 * 3))
+    w1 = o.bf16_to_f32(o.gen_normal_bf16(0, 7001, 0.02, ENC_DIM * ENC_DIM * 3))
+    b0 = o.gen_normal_f32(0, 7002, 0.02, ENC_DIM)
+    b1 = o.gen_normal_f32(0, 7003, 0.02, ENC_DIM)
+
+    def stream(mel, stem, n_samples):
+        positions, done = 0, 0
+        while done < n_samples:
+            before = mel.frames()
+            mel.feed(audio[done:done + ENC_CHUNK])
+            frames, _ = mel.data(before, mel.frames() - before)
+            positions += stem.process(frames).shape[0]
+            done += ENC_CHUNK
+        return positions
+
+    mel, stem = V.MelCtx(0, device=local), V.ConvStemState(128, ENC_DIM, w0, b0, w1, b1, device=local)
+    stream(mel, stem, 16000)  # warm-up second
+    mel.close()
+    stem.close()
+    mel, stem = V.MelCtx(0, device=local), V.ConvStemState(128, ENC_DIM, w0, b0, w1, b1, device=local)
+    t0 = time.perf_counter()
+    n_pos = stream(mel, stem, audio.size)
+    gpu_s = time.perf_counter() - t0
+    launches = int(V.lib().vox_encoder_kernel_launches(mel.h, stem.h))
+    mel.close()
+    stem.close()
+    o.set_threads(1)
+    n_cpu = int(16000 * cpu_sample_s)
+    omel, ostem = o.MelCtx(0), o.ConvStemState(128, ENC_DIM, w0, b0, w1, b1)
+    t0 = time.perf_counter()
+    stream(omel, ostem, n_cpu)
+    cpu_s = time.perf_counter() - t0
+    return {"audio_s": ENC_SECONDS, "gpu_s": gpu_s, "positions": n_pos, "launches": launches,
+            "cpu_audio_s": cpu_sample_s, "cpu_s": cpu_s}
+
+
 TP_PARITY_PROMPT, TP_PARITY_FORCED, TP_PARITY_GREEDY = 31, 4, 64
 
 
@@ -537,6 +591,7 @@ def run_ours(args):
     long_run = None if args.ctx_steps == 0 else run_context(V, ctx, args, rank, dist, LONG_CONTEXT, args.ctx_steps)
     roll_run = None if args.ctx_steps == 0 else run_context(V, ctx, args, rank, dist, WINDOW, args.ctx_steps)
     ms_run = None if args.ms_steps == 0 else run_multi_stream(V, ctx, args, rank, world, dist)
+    enc_run = None if args.no_encoder else run_encoder(V, local)
     tp_run = None
     if world > 1 and args.tp_steps > 0:
         parity_ref = tp_parity_reference(V, ctx)
@@ -544,7 +599,9 @@ def run_ours(args):
         tp_run = run_tensor_parallel(V, args, rank, world, local, dist, parity_ref)
 
     t_max, e2e_max = ms, e2e_ms
-    ms_max = ms_e2e_max = tp_max = long_max = roll_max = 0.0
+    ms_max = ms_e2e_max = tp_max = long_max = roll_max = enc_max = 0.0
+    if enc_run:
+        enc_max = enc_run["gpu_s"]
     if ms_run:
         ms_max, ms_e2e_max = ms_run["ms"], ms_run["e2e_ms"]
     if tp_run:
@@ -553,9 +610,9 @@ def run_ours(args):
         long_max, roll_max = long_run["ms"], roll_run["ms"]
     if dist:
         import torch
-        t = torch.tensor([ms, e2e_ms, ms_max, ms_e2e_max, tp_max, long_max, roll_max], dtype=torch.float64)
+        t = torch.tensor([ms, e2e_ms, ms_max, ms_e2e_max, tp_max, long_max, roll_max, enc_max], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_max, e2e_max, ms_max, ms_e2e_max, tp_max, long_max, roll_max = (float(x) for x in t)
+        t_max, e2e_max, ms_max, ms_e2e_max, tp_max, long_max, roll_max, enc_max = (float(x) for x in t)
         if roll_run:
             ok = torch.tensor([1.0 if roll_run["ring_ok"] and long_run["ring_ok"] else 0.0])
             dist.all_reduce(ok, op=dist.ReduceOp.MIN)
@@ -607,6 +664,21 @@ def run_ours(args):
                                                "start": roll_run["ring_state"][1],
                                                "pos_offset": roll_run["ring_state"][2],
                                                "matches_kv_rs_index_rule": roll_run["ring_ok"]}
+    if enc_run:
+        chunks = enc_run["audio_s"] * 16000 // ENC_CHUNK
+        line["encoder"] = {
+            "metric": "encoder front end: audio seconds processed per second (log-mel + conv stem)",
+            "value": enc_run["audio_s"] * world / enc_max, "unit": "audio s/s", "streams": world,
+            "workload": (f"{enc_run['audio_s']} s of 16 kHz synthetic audio per GPU in 80 ms chunks (1280 samples): "
+                         f"MelCtx feed (128 bins) then ConvStemState process (conv0 128->{ENC_DIM}, conv1 "
+                         f"{ENC_DIM}->{ENC_DIM} stride 2, GELU), host buffers in and out"),
+            "ms_per_chunk": enc_max * 1e3 / chunks, "positions_per_stream": enc_run["positions"],
+            "gpu_launches": enc_run["launches"],
+            "e2e": {"value": enc_run["audio_s"] * world / enc_max, "unit": "audio s/s",
+                    "h2d_bytes_per_step": ENC_CHUNK * 4 + 8 * 128 * 4, "d2h_bytes_per_step": 8 * 128 * 4 + 4 * ENC_DIM * 4},
+            "cpu_baseline": {"value": enc_run["cpu_audio_s"] / enc_run["cpu_s"], "unit": "audio s/s", "cores": 1,
+                             "kind": "port", "sample": f"{enc_run['cpu_audio_s']} s of the same audio, same chunks, "
+                                                       f"oracle MelCtx + ConvStemState, 1 thread"}}
     if ms_run:
         n_tok = ms_run["steps"] * MS_STREAMS * world
         ms_bytes = (LAYERS * LAYER_WEIGHT_BYTES + HEAD_BYTES + MS_STREAMS * EMBED_ROW_BYTES +
@@ -656,6 +728,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--cpu-layer-steps", type=int, default=24)
+    ap.add_argument("--no-encoder", action="store_true", help="skip the encoder front-end run")
     ap.add_argument("--ctx-steps", type=int, default=256,
                     help="greedy steps of the long-context (1536) and full-window rolling runs (0 skips them)")
     ap.add_argument("--ms-steps", type=int, default=512,

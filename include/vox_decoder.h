@@ -71,15 +71,12 @@ typedef struct vox_ctx_options {
     int step_mode;            /* vox_step_mode: how vox_model_* run a token step */
 } vox_ctx_options;
 
-/* How vox_model_step/_prefill/_generate run a token step; both are captured
- * in a CUDA graph.  VOX_STEP_LAYERS: five kernels per layer (QKV+RoPE+ring
- * append, attention, o-proj, w1|w3+SwiGLU, w2) plus LM head and argmax.
- * VOX_STEP_PERSISTENT: the whole step as one cooperative persistent kernel
- * (bf16 weights only; falls back to VOX_STEP_LAYERS when the shapes do not
- * fit it).  VOX_STEP_AUTO picks the faster one on B200, currently LAYERS.
- * For the multi-stream step (vox_model_step_batch) PERSISTENT runs o-proj,
- * w1|w3, w2 and the next q|k|v as one persistent launch per layer; the
- * other modes launch every GEMM on its own. */
+/* How the multi-stream step (vox_model_step_batch / _generate_batch) runs its
+ * GEMMs; single-stream steps always run five kernels per layer (QKV + RoPE +
+ * ring append, attention, o-proj, w1|w3 + SwiGLU, w2) plus LM head and argmax,
+ * captured in a CUDA graph.  VOX_STEP_PERSISTENT runs o-proj, w1|w3, w2 and the
+ * next q|k|v as one persistent launch per layer; VOX_STEP_AUTO and
+ * VOX_STEP_LAYERS launch every GEMM on its own (the faster choice on B200). */
 typedef enum vox_step_mode { VOX_STEP_AUTO = 0, VOX_STEP_LAYERS = 1, VOX_STEP_PERSISTENT = 2 } vox_step_mode;
 
 typedef struct vox_f32_slice { const float* ptr; size_t len; } vox_f32_slice;

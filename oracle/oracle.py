@@ -487,12 +487,18 @@ class MelCtx:
     def finish(self, right_pad_samples=0):
         lib().vo_mel_finish(self.h, right_pad_samples)
 
-    def data(self):
-        n = lib().vo_mel_frames(self.h)
-        if n == 0:
-            return np.zeros((0, MEL_BINS), np.float32), 0
+    def frames(self):
+        return lib().vo_mel_frames(self.h)
+
+    def data(self, first=0, n=None):
+        """(frames [first, first + n) as [n, 128], total frame count)."""
+        total = lib().vo_mel_frames(self.h)
+        n = total - first if n is None else n
+        if total == 0 or n <= 0:
+            return np.zeros((0, MEL_BINS), np.float32), total
         p = lib().vo_mel_data(self.h)
-        return np.ctypeslib.as_array(p, shape=(n * MEL_BINS,)).copy().reshape(n, MEL_BINS), n
+        a = np.ctypeslib.as_array(p, shape=(total * MEL_BINS,)).reshape(total, MEL_BINS)
+        return a[first:first + n].copy(), total
 
 
 def gelu(x):

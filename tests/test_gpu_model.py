@@ -80,7 +80,8 @@ def teacher_forced(V, oracle, c, n_layers, vocab, n_steps, window=None, seed=0, 
     return worst, margins
 
 
-# step_mode 1: the chain of per-layer kernels (the default); 2: one persistent kernel per token.
+# step_mode 1 (the chain of per-layer kernels, the default); 2 selects the
+# multi-stream persistent GEMM chain and leaves single-stream steps unchanged.
 MODES = [1, 2]
 
 

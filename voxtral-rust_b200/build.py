@@ -21,7 +21,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-ffp-contract=off",
           "-I", CSRC, "-I", os.path.join(ROOT, "include")]
-SOURCES = ["vox_gemv.cu", "vox_attention.cu", "vox_misc.cu", "vox_noalloc.cu", "vox_token.cu", "vox_bgemm.cu",
+SOURCES = ["vox_gemv.cu", "vox_attention.cu", "vox_misc.cu", "vox_noalloc.cu", "vox_bgemm.cu",
            "vox_encoder.cu",
            "vox_capi.cpp", "vox_tp.cpp", "vox_stream.cpp", "vox_weights.cpp",
            "vox_tokenizer.cpp"]

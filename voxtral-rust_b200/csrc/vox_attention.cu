@@ -42,6 +42,13 @@ constexpr int kMaxSplits = 64;  // merge weights kept in shared memory
 // Most live tokens per kv head for which one stream's attention runs as one
 // thread-block cluster per kv head (attn_cluster_kernel).
 constexpr int kAttnClusterMaxTokens = 3584;
+// Warps of a cluster-attention CTA.  Three warps at 136 registers (13056) fit
+// beside a weight-streaming GEMV CTA (17 warps at 96 registers, 52224; at most
+// 148 KB of shared memory) in one SM's 65536 registers and 228 KB: the GEMV
+// launch before attention (q|k|v) and the one after it (o-proj) then share
+// SMs with the attention CTAs, so attention's prologue overlaps the q|k|v
+// tail and o-proj streams its weights while attention computes.
+constexpr int kClusterWarps = 4;
 
 template <int VEC>
 struct VecT;
@@ -422,12 +429,11 @@ __device__ __forceinline__ float dot4(const float4& a, const float4& b) {
 // Bulk copies of group k of `warp` in chunk [t_begin, t_end) (K rows, then V
 // rows, two pieces each at the ring's wrap) into the warp's slot k % D,
 // completing on that slot's mbarrier.  Called by lane 0.
-template <int G, int D>
+template <int G, int D, int NW = kAttnThreads / 32>
 __device__ __forceinline__ void attn_issue_group(const AttnArgs& A, int z, int h, int t_begin, int t_end,
                                                  int ring_start, unsigned char* ring_smem, uint64_t (*wbar)[D],
                                                  int warp, int k, int hd) {
     constexpr int TPG = 32 / G;
-    constexpr int NW = kAttnThreads / 32;
     const size_t row_bytes = (size_t)hd * 4;
     const uint32_t stage_bytes = (uint32_t)(2 * TPG * row_bytes);
     const float* kbase = A.k_ring + z * A.ring_stride + (size_t)h * A.cap * hd;
@@ -458,14 +464,13 @@ __device__ __forceinline__ void attn_issue_group(const AttnArgs& A, int z, int h
 // synchronizes before combining them.  warp, lane and hd are the caller's
 // (computed once per kernel: passing them keeps the caller's registers);
 // pre_issued groups of this warp were already copied by the caller.
-template <int G, int D>
+template <int G, int D, int NW = kAttnThreads / 32>
 __device__ __forceinline__ void attn_chunk_warps(const AttnArgs& A, int z, int h, int t_begin, int t_end,
                                                  int ring_start, unsigned char* ring_smem, uint64_t (*wbar)[D],
                                                  float (*wacc)[G][128], float (*wml)[G][2], uint32_t& phase,
                                                  const int warp, const int lane, const int hd,
                                                  const int pre_issued = 0) {
     constexpr int TPG = 32 / G;
-    constexpr int NW = kAttnThreads / 32;
     const unsigned FULL = 0xFFFFFFFFu;
     const bool dim_ok = lane * 4 < hd;
     const int my_g = lane / TPG, my_t = lane % TPG;
@@ -487,7 +492,7 @@ __device__ __forceinline__ void attn_chunk_warps(const AttnArgs& A, int z, int h
     const float* kbase = A.k_ring + z * A.ring_stride + (size_t)h * A.cap * hd;
     const float* vbase = A.v_ring + z * A.ring_stride + (size_t)h * A.cap * hd;
     auto issue = [&](int k) {
-        attn_issue_group<G, D>(A, z, h, t_begin, t_end, ring_start, ring_smem, wbar, warp, k, hd);
+        attn_issue_group<G, D, NW>(A, z, h, t_begin, t_end, ring_start, ring_smem, wbar, warp, k, hd);
     };
     if (lane == 0)
         for (int k = pre_issued; k < min(D, n_my); ++k) issue(k);
@@ -852,10 +857,12 @@ __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// 136 registers: 3 warps x 4352 + a GEMV CTA's 17 x 3072 = 65280 <= 65536.
 template <int G, int CS>
-__global__ void __launch_bounds__(kAttnThreads, 4) attn_cluster_kernel(const AttnArgs A) {
+__global__ void __maxnreg__(136) attn_cluster_kernel(const AttnArgs A) {
     constexpr int TPG = 32 / G;
-    constexpr int NW = kAttnThreads / 32;
+    constexpr int NW = kClusterWarps;
+    constexpr int NT = NW * 32;
     constexpr int HD = 128;
     // [NW][K rows | V rows] slots, then the leader's merge buffer:
     // acc [CS][G][hd] followed by (m, l) [CS][G][2]
@@ -908,21 +915,21 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_cluster_kernel(const Att
         const int ntok = min(TPG, range_s[1] - t0);
         if (ntok > 0 && (t0 + ntok < range_s[3] || !A.pre_append)) {
             if ((tid & 31) == 0)
-                attn_issue_group<G, 1>(A, 0, h, range_s[0], range_s[1], range_s[2], ring_smem, wbar, warp, 0, hd);
+                attn_issue_group<G, 1, NW>(A, 0, h, range_s[0], range_s[1], range_s[2], ring_smem, wbar, warp, 0, hd);
             pre = 1;
         }
         __syncwarp();
     }
     pdl_wait_prior_grids();
     uint32_t phase = 0;
-    attn_chunk_warps<G, 1>(A, 0, h, range_s[0], range_s[1], range_s[2], ring_smem, wbar, wacc, wml, phase,
+    attn_chunk_warps<G, 1, NW>(A, 0, h, range_s[0], range_s[1], range_s[2], ring_smem, wbar, wacc, wml, phase,
                            tid >> 5, tid & 31, hd, pre);
     __syncthreads();
 
     // This CTA's partial into the leader's buffer, slot `rank`.
     cluster_wait();
     const uint32_t lacc = cluster_map(smem_addr(macc), 0), lml = cluster_map(smem_addr(mml), 0);
-    for (int o = tid; o < n_out; o += kAttnThreads) {
+    for (int o = tid; o < n_out; o += NT) {
         const int g = o / hd4, d = (o - g * hd4) * 4;
         float M = -INFINITY;
 #pragma unroll
@@ -948,7 +955,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_cluster_kernel(const Att
 
     // Merge the CS partials in rank order (the same weights as the global merge).
     float* out = A.out + (size_t)h * G * hd;
-    for (int o = tid; o < n_out; o += kAttnThreads) {
+    for (int o = tid; o < n_out; o += NT) {
         const int g = o / hd4, d = (o - g * hd4) * 4;
         float M = -INFINITY;
 #pragma unroll
@@ -1042,7 +1049,7 @@ cudaError_t attn_prepare(int /*dev*/) {
 
 namespace {
 size_t attn_cluster_smem(int G, int hd, int cs) {
-    return (size_t)(kAttnThreads / 32) * 2 * (32 / G) * hd * 4 + (size_t)cs * G * (hd + 2) * 4;
+    return (size_t)kClusterWarps * 2 * (32 / G) * hd * 4 + (size_t)cs * G * (hd + 2) * 4;
 }
 void* attn_cluster_fn(int G, int cs) {
     if (G == 4) return cs == 16 ? (void*)attn_cluster_kernel<4, 16> : (void*)attn_cluster_kernel<4, 8>;
@@ -1076,9 +1083,13 @@ int attn_cluster_size(int n_heads, int n_kv, int hd) {
                 cudaGetLastError();
                 continue;
             }
+            // the whole 228 KB for shared memory, so that a GEMV CTA fits beside this one
+            if (cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+                cudaGetLastError();
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3(n_kv * cs, 1, 1);
-            cfg.blockDim = dim3(kAttnThreads, 1, 1);
+            cfg.blockDim = dim3(kClusterWarps * 32, 1, 1);
             cfg.dynamicSmemBytes = attn_cluster_smem(G, hd, cs);
             cudaLaunchAttribute attr[1];
             attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1109,7 +1120,7 @@ cudaError_t launch_attention_cluster(const AttnArgs& a, cudaStream_t s, bool pdl
     const int G = a.n_heads / a.n_kv;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.n_kv * cs, 1, 1);
-    cfg.blockDim = dim3(kAttnThreads, 1, 1);
+    cfg.blockDim = dim3(kClusterWarps * 32, 1, 1);
     cfg.dynamicSmemBytes = attn_cluster_smem(G, a.hd, cs);
     cfg.stream = s;
     cudaLaunchAttribute attr[2];

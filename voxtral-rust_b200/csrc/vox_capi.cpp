@@ -206,13 +206,6 @@ struct vox_ctx {
     std::vector<vox_kv*> caches;   // caches created from this context, still alive
     uint64_t launches = 0;
     GemvPlan p_qkv{}, p_o{}, p_w13{}, p_w2{}, p_head{};
-    // persistent token kernel
-    bool tok_ok = false;
-    int tok_grid = 0;
-    TokGemv t_qkv{}, t_o{}, t_w13{}, t_w2{}, t_head{};
-    unsigned long long* tok_bar = nullptr;   // [2]: counter, base of the next launch
-    float* tok_part = nullptr;
-    int tok_splits = 1;
     void* scratch = nullptr;
     size_t scratch_bytes = 0;
     // multi-stream path
@@ -238,7 +231,6 @@ struct vox_kv {
     uint64_t graph_kernels = 0;
     cudaGraphExec_t step_graph_short = nullptr;  // same step, cluster attention (short contexts)
     uint64_t graph_kernels_short = 0;
-    TokLayer* tok_layers = nullptr;  // device table of per-layer pointers (token kernel)
     cudaGraphExec_t batch_graph = nullptr;  // multi-stream step over all streams
     uint64_t batch_kernels = 0;
     size_t layer_elems() const { return n_kv * cap * hd; }
@@ -255,7 +247,6 @@ int check_device_errors(vox_ctx* c) {
         CUDA_TRY(cudaMemsetAsync(c->err, 0, sizeof(unsigned), c->stream));
         if (bits & (ERR_FULL_WAIT | ERR_EMPTY_WAIT | ERR_DRAIN_WAIT | ERR_GRID_WAIT)) {
             // An aborted step leaves barrier counters and tickets half-advanced.
-            if (c->tok_bar) CUDA_TRY(cudaMemsetAsync(c->tok_bar, 0, 2 * sizeof(unsigned long long), c->stream));
             CUDA_TRY(cudaMemsetAsync(c->tickets, 0, c->cfg.n_kv_heads * sizeof(unsigned), c->stream));
             if (c->bb.ready) {
                 size_t tiles = 0;
@@ -847,91 +838,18 @@ int model_ready(vox_ctx* c, vox_kv* kv) {
     return VOX_OK;
 }
 
-// One token step as the persistent kernel (vox_token.cu).
-int enqueue_token_kernel(vox_ctx* c, vox_kv* kv) {
-    TokenArgs a{};
-    a.layers = kv->tok_layers;
-    a.n_layers = (int)c->layers.size();
-    a.dim = (int)c->cfg.dim;
-    a.hidden = (int)c->cfg.hidden_dim;
-    a.q_dim = (int)c->q_dim;
-    a.kv_dim = (int)c->kv_dim;
-    a.hd = (int)c->cfg.head_dim;
-    a.n_heads = (int)c->cfg.n_heads;
-    a.n_kv = (int)c->cfg.n_kv_heads;
-    a.cap = (int)kv->cap;
-    a.kv_window = (int)kv->window;
-    a.cfg_window = (int)c->cfg.sliding_window;
-    a.vocab = (int)c->opt.vocab;
-    a.max_pos = c->max_pos;
-    a.eps = c->cfg.norm_eps;
-    a.scale = 1.0f / sqrtf((float)c->cfg.head_dim);
-    a.embed = c->embed;
-    a.lm_head = static_cast<const uint16_t*>(c->lm_head);
-    a.final_norm = c->final_norm;
-    a.rope_cos = c->rope_cos;
-    a.rope_sin = c->rope_sin;
-    a.step = c->step;
-    a.hid = c->hid;
-    a.hmid = c->hmid;
-    a.q = c->q;
-    a.attn = c->attn;
-    a.act = c->act;
-    a.logits = c->logits;
-    a.attn_part = c->tok_part;
-    a.tickets = c->tickets;
-    a.splits = c->tok_splits;
-    a.am_part = c->am_part;
-    a.tok_out = c->tok_out;
-    a.bar = c->tok_bar;
-    a.bar_base = c->tok_bar + 1;
-    a.err = c->err;
-    a.g_qkv = c->t_qkv;
-    a.g_o = c->t_o;
-    a.g_w13 = c->t_w13;
-    a.g_w2 = c->t_w2;
-    a.g_head = c->t_head;
-    CUDA_TRY(record_launch(c, launch_token_step(a, c->tok_grid, c->stream)));
-    return VOX_OK;
-}
-
-int build_token_layers(vox_ctx* c, vox_kv* kv) {
-    if (kv->tok_layers) return VOX_OK;
-    std::vector<TokLayer> t(c->layers.size());
-    for (size_t l = 0; l < t.size(); ++l) {
-        const LayerDev& L = c->layers[l];
-        t[l].wqkv = static_cast<const uint16_t*>(L.wqkv);
-        t[l].wo = static_cast<const uint16_t*>(L.wo);
-        t[l].w13 = static_cast<const uint16_t*>(L.w13);
-        t[l].w2 = static_cast<const uint16_t*>(L.w2);
-        t[l].attn_norm = L.attn_norm;
-        t[l].ffn_norm = L.ffn_norm;
-        t[l].k_ring = kv->k + l * kv->layer_elems();
-        t[l].v_ring = kv->v + l * kv->layer_elems();
-        t[l].st = kv->dstate + l;
-    }
-    CUDA_TRY(dalloc(&kv->tok_layers, t.size()));
-    CUDA_TRY(cudaMemcpy(kv->tok_layers, t.data(), t.size() * sizeof(TokLayer), cudaMemcpyHostToDevice));
-    return VOX_OK;
-}
-
 // One token step as a CUDA graph.  Single-stream steps get two graphs when
 // the shape allows: attention as one cluster per kv head (contexts up to
 // attn_cluster_max_tokens()) or the persistent split-K kernel; launch_graph
 // picks one per step from the context length the host already knows.
-// With `adapter` the step always runs as the chain of layer kernels.
 static int capture_step(vox_ctx* c, vox_kv* kv, bool short_attn, cudaGraphExec_t* out, uint64_t* kernels,
                         const float* adapter = nullptr, int adapter_cap = 0) {
     const uint64_t before = c->launches;
     CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
     int rc = VOX_OK;
-    if (c->tok_ok && !adapter) {
-        rc = enqueue_token_kernel(c, kv);
-    } else {
-        for (size_t l = 0; l < c->layers.size() && rc == VOX_OK; ++l)
-            rc = enqueue_layer(c, kv, l, l == 0, true, short_attn, adapter, adapter_cap);
-        if (rc == VOX_OK) rc = enqueue_head(c, true);
-    }
+    for (size_t l = 0; l < c->layers.size() && rc == VOX_OK; ++l)
+        rc = enqueue_layer(c, kv, l, l == 0, true, short_attn, adapter, adapter_cap);
+    if (rc == VOX_OK) rc = enqueue_head(c, true);
     cudaGraph_t g = nullptr;
     cudaError_t e = cudaStreamEndCapture(c->stream, &g);
     if (rc != VOX_OK) {
@@ -949,10 +867,8 @@ static int capture_step(vox_ctx* c, vox_kv* kv, bool short_attn, cudaGraphExec_t
 
 int build_step_graph(vox_ctx* c, vox_kv* kv) {
     if (kv->step_graph) return VOX_OK;
-    if (c->tok_ok) TRY(build_token_layers(c, kv));
     TRY(capture_step(c, kv, false, &kv->step_graph, &kv->graph_kernels));
-    if (!c->tok_ok &&
-        attn_cluster_size((int)c->cfg.n_heads, (int)c->cfg.n_kv_heads, (int)c->cfg.head_dim) > 0)
+    if (attn_cluster_size((int)c->cfg.n_heads, (int)c->cfg.n_kv_heads, (int)c->cfg.head_dim) > 0)
         TRY(capture_step(c, kv, true, &kv->step_graph_short, &kv->graph_kernels_short));
     return VOX_OK;
 }
@@ -1061,7 +977,7 @@ void vox_ctx_destroy(vox_ctx* c) {
     }
     void* ptrs[] = {c->embed, c->lm_head, c->final_norm, c->rope_cos, c->rope_sin, c->hid, c->hmid,
                     c->q, c->attn, c->act, c->logits, c->am_part, c->attn_part, c->tickets, c->step,
-                    c->tok_out, c->err, c->scratch, c->tok_bar, c->tok_part};
+                    c->tok_out, c->err, c->scratch};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     {
@@ -1155,33 +1071,6 @@ int vox_ctx_create(const vox_decoder_config* cfg, const vox_ctx_options* opt, vo
         return bail(fail(VOX_ERR_UNSUPPORTED, "no LM-head plan for vocab %zu", (size_t)o.vocab));
     c->nsplit = attn_max_splits();
 
-    // Persistent token kernel: bf16 weights, a vocabulary, supported shapes,
-    // cooperative launch, and one CTA per SM fitting in shared memory.
-    if (o.step_mode == VOX_STEP_PERSISTENT && wsize == 2 && o.vocab &&
-        token_kernel_supported(dimi, hidi, (int)c->q_dim, (int)cfg->n_heads, (int)cfg->n_kv_heads, (int)hd) &&
-        token_plan((int)c->qkv_rows, dimi, 2, &c->t_qkv) && token_plan(dimi, (int)c->q_dim, 1, &c->t_o) &&
-        token_plan(2 * hidi, dimi, 2, &c->t_w13) && token_plan(dimi, hidi, 1, &c->t_w2) &&
-        token_plan((int)o.vocab, dimi, 1, &c->t_head)) {
-        int coop = 0;
-        CTX_TRY(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->dev));
-        TokenArgs probe{};
-        probe.n_heads = (int)cfg->n_heads;
-        probe.n_kv = (int)cfg->n_kv_heads;
-        probe.hd = (int)hd;
-        probe.vocab = (int)o.vocab;
-        probe.g_qkv = c->t_qkv;
-        probe.g_o = c->t_o;
-        probe.g_w13 = c->t_w13;
-        probe.g_w2 = c->t_w2;
-        probe.g_head = c->t_head;
-        if (coop && token_smem_bytes(probe, c->num_sms) <= 227 * 1024) {
-            CTX_TRY(token_prepare(c->dev));
-            c->tok_ok = true;
-            c->tok_grid = c->num_sms;
-            c->tok_splits = token_splits((int)cfg->n_kv_heads, c->tok_grid);
-        }
-    }
-
     // Activations and scratch.
     CTX_TRY(dalloc(&c->hid, dim));
     CTX_TRY(dalloc(&c->hmid, dim));
@@ -1199,11 +1088,6 @@ int vox_ctx_create(const vox_decoder_config* cfg, const vox_ctx_options* opt, vo
     CTX_TRY(dalloc(&c->tok_out, 1));
     CTX_TRY(dalloc(&c->err, 1));
     CTX_TRY(cudaMemset(c->err, 0, sizeof(unsigned)));
-    if (c->tok_ok) {
-        CTX_TRY(dalloc(&c->tok_bar, 2));
-        CTX_TRY(cudaMemset(c->tok_bar, 0, 2 * sizeof(unsigned long long)));
-        CTX_TRY(dalloc(&c->tok_part, cfg->n_kv_heads * (size_t)c->tok_splits * G * (hd + 2)));
-    }
     CTX_TRY(cudaMallocHost(&c->h_tok, sizeof(int32_t)));
     CTX_TRY(cudaMallocHost(&c->h_err, sizeof(unsigned)));
     if (ensure_host_steps(c, 1024) != VOX_OK) return bail(VOX_ERR_OOM);
@@ -1425,9 +1309,7 @@ static void release_graphs(vox_kv* kv) {
     if (kv->step_graph) cudaGraphExecDestroy(kv->step_graph);
     if (kv->step_graph_short) cudaGraphExecDestroy(kv->step_graph_short);
     if (kv->batch_graph) cudaGraphExecDestroy(kv->batch_graph);
-    if (kv->tok_layers) cudaFree(kv->tok_layers);
     kv->step_graph = kv->step_graph_short = kv->batch_graph = nullptr;
-    kv->tok_layers = nullptr;
 }
 
 int vox_kv_create_ex(vox_ctx* c, size_t n_layers, size_t n_kv, size_t hd, size_t window, size_t cap,

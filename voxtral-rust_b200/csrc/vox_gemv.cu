@@ -24,6 +24,8 @@
 // reading x.  Consecutive GEMVs therefore overlap one kernel's tail with the
 // next kernel's weight fetch.
 #include <cuda_runtime.h>
+
+#include <cstdlib>
 #include <math.h>
 
 #include "vox_device.cuh"
@@ -595,7 +597,12 @@ GemvPlan plan_gemv(int rows, int K, int unit, int wsize, int num_sms, int n_vec)
     p.max_rows_cta = ((units + p.grid - 1) / p.grid) * unit;
     // Do not reserve stages a CTA can never fill.
     int max_stages_needed = (p.max_rows_cta + p.stage_rows - 1) / p.stage_rows;
-    int ns = (int)(g_tune.stage_budget / stage_bytes);
+    size_t budget = g_tune.stage_budget;
+    if (const char* e = std::getenv("VOX_GEMV_RING_KB")) {  // tuning knob for measurements
+        const long kb = std::atol(e);
+        if (kb >= 32 && kb <= 220) budget = (size_t)kb * 1024;
+    }
+    int ns = (int)(budget / stage_bytes);
     if (ns < 2) ns = 2;
     if (ns > 16) ns = 16;
     if (ns > max_stages_needed) ns = max_stages_needed < 1 ? 1 : max_stages_needed;

@@ -165,55 +165,6 @@ inline size_t xop_bytes(int K) { return (size_t)(K / 64) * 2048; }
 // Record a failure for vox_last_error() and return `code` (host side).
 int report_error(int code, const char* msg);
 
-// ---- persistent token-step kernel (bf16 weights) ----
-struct TokLayer {
-    const uint16_t* wqkv;   // [q_dim + 2 kv_dim, dim]
-    const uint16_t* wo;     // [dim, q_dim]
-    const uint16_t* w13;    // [2 hidden, dim], rows interleaved w1/w3
-    const uint16_t* w2;     // [dim, hidden]
-    const float* attn_norm;
-    const float* ffn_norm;
-    float* k_ring;          // [n_kv, cap, hd]
-    float* v_ring;
-    KvState* st;
-};
-
-// Per-GEMV launch shape inside the token kernel.
-struct TokGemv {
-    int rows, K, unit, nseg, cpt, stage_rows;
-};
-
-struct TokenArgs {
-    const TokLayer* layers;
-    int n_layers;
-    int dim, hidden, q_dim, kv_dim, hd, n_heads, n_kv;
-    int cap, kv_window, cfg_window, vocab, max_pos;
-    float eps, scale;
-    const uint16_t* embed;
-    const uint16_t* lm_head;
-    const float* final_norm;
-    const float* rope_cos;
-    const float* rope_sin;
-    StepState* step;
-    float *hid, *hmid, *q, *attn, *act, *logits;
-    float* attn_part;              // accumulators [n_kv, splits, G, hd], then (m, l) [.., 2]
-    unsigned* tickets;             // [n_kv]
-    int splits;                    // max splits per kv head
-    ArgmaxPart* am_part;           // [grid]
-    int32_t* tok_out;
-    unsigned long long* bar;       // grid barrier counter (monotonic)
-    unsigned long long* bar_base;  // counter value at the start of the next launch
-    unsigned* err;
-    TokGemv g_qkv, g_o, g_w13, g_w2, g_head;
-};
-
-bool token_kernel_supported(int dim, int hidden, int q_dim, int n_heads, int n_kv, int hd);
-bool token_plan(int rows, int K, int unit, TokGemv* out);
-size_t token_smem_bytes(const TokenArgs& a, int grid);
-int token_splits(int n_kv, int grid);
-cudaError_t token_prepare(int dev);
-cudaError_t launch_token_step(const TokenArgs& a, int grid, cudaStream_t s);
-
 // ---- multi-stream skinny GEMM on tcgen05 (bf16 weights, B <= 8 streams) ----
 enum : int { BG_STORE = 0, BG_QKV = 1, BG_RESID = 2, BG_SWIGLU = 3, BG_ARGMAX = 4 };
 
