@@ -1059,11 +1059,11 @@ int vox_ctx_create(const vox_decoder_config* cfg, const vox_ctx_options* opt, vo
     const size_t dim = cfg->dim, hid = cfg->hidden_dim, hd = cfg->head_dim;
     // Launch plans.
     const int dimi = (int)dim, hidi = (int)hid;
-    c->p_qkv = plan_gemv((int)c->qkv_rows, dimi, 2, wsize, c->num_sms, 1);
-    c->p_o = plan_gemv(dimi, (int)c->q_dim, 1, wsize, c->num_sms, 1);
-    c->p_w13 = plan_gemv(2 * hidi, dimi, 2, wsize, c->num_sms, 1);
-    c->p_w2 = plan_gemv(dimi, hidi, 1, wsize, c->num_sms, 1);
-    if (o.vocab) c->p_head = plan_gemv((int)o.vocab, dimi, 1, wsize, c->num_sms, 1);
+    c->p_qkv = plan_gemv((int)c->qkv_rows, dimi, 2, wsize, c->num_sms, 1, kGemvPaired);
+    c->p_o = plan_gemv(dimi, (int)c->q_dim, 1, wsize, c->num_sms, 1, kGemvPaired);
+    c->p_w13 = plan_gemv(2 * hidi, dimi, 2, wsize, c->num_sms, 1, kGemvPaired);
+    c->p_w2 = plan_gemv(dimi, hidi, 1, wsize, c->num_sms, 1, kGemvPaired);
+    if (o.vocab) c->p_head = plan_gemv((int)o.vocab, dimi, 1, wsize, c->num_sms, 1, kGemvPaired);
     for (const GemvPlan* p : {&c->p_qkv, &c->p_o, &c->p_w13, &c->p_w2})
         if (p->grid < 1 || p->smem > gemv_max_smem())
             return bail(fail(VOX_ERR_UNSUPPORTED, "no GEMV plan for rows %d x K %d", p->rows, p->K));

@@ -24,8 +24,6 @@
 // reading x.  Consecutive GEMVs therefore overlap one kernel's tail with the
 // next kernel's weight fetch.
 #include <cuda_runtime.h>
-
-#include <cstdlib>
 #include <math.h>
 
 #include "vox_device.cuh"
@@ -34,17 +32,8 @@ namespace vox {
 
 namespace {
 
-// Consumer warps per CTA (NW, a template parameter): 8 (two CTAs per SM) or
-// 16 (one CTA per SM).  Plus one producer warp.
-// Launch shape of the weight stream: ring bytes per CTA, CTAs per SM, and
-// row pairs per warp per stage.
-struct GemvTuning {
-    size_t stage_budget = 160 * 1024;
-    int ctas_per_sm = 1;
-    int stage_mult = 1;
-    int warps = 16;
-};
-constexpr GemvTuning g_tune{};
+// Pipeline shape inside a CTA: row pairs per warp per stage.
+constexpr int kStageMult = 1;
 
 template <typename WT>
 struct Elem;
@@ -553,9 +542,9 @@ bool gemv_supported(int K, int wsize) {
     return false;
 }
 
-size_t gemv_max_smem() { return g_tune.stage_budget > 108 * 1024 ? 227 * 1024 - 256 : 113 * 1024; }
+size_t gemv_max_smem() { return 227 * 1024 - 256; }
 
-GemvPlan plan_gemv(int rows, int K, int unit, int wsize, int num_sms, int n_vec) {
+GemvPlan plan_gemv(int rows, int K, int unit, int wsize, int num_sms, int n_vec, GemvShape shape) {
     GemvPlan p{};
     p.rows = rows;
     p.K = K;
@@ -586,23 +575,20 @@ GemvPlan plan_gemv(int rows, int K, int unit, int wsize, int num_sms, int n_vec)
         return p;
     }
     p.cpt = cpt_round((C / p.nseg + 31) / 32);
-    p.nw = wsize == 2 ? g_tune.warps : 8;
-    p.stage_rows = 2 * (p.nw / p.nseg) * g_tune.stage_mult;
+    const int warps = shape.warps == 8 ? 8 : 16;
+    const int ctas_per_sm = shape.ctas_per_sm == 2 ? 2 : 1;
+    p.nw = wsize == 2 ? warps : 8;
+    p.stage_rows = 2 * (p.nw / p.nseg) * kStageMult;
     const size_t row_bytes = (size_t)K * wsize;
     size_t stage_bytes = p.stage_rows * row_bytes;
     const int units = rows / unit;
-    const int max_grid = num_sms * g_tune.ctas_per_sm;
+    const int max_grid = num_sms * ctas_per_sm;
     p.grid = units < max_grid ? units : max_grid;
     if (p.grid < 1) p.grid = 1;
     p.max_rows_cta = ((units + p.grid - 1) / p.grid) * unit;
     // Do not reserve stages a CTA can never fill.
     int max_stages_needed = (p.max_rows_cta + p.stage_rows - 1) / p.stage_rows;
-    size_t budget = g_tune.stage_budget;
-    if (const char* e = std::getenv("VOX_GEMV_RING_KB")) {  // tuning knob for measurements
-        const long kb = std::atol(e);
-        if (kb >= 32 && kb <= 220) budget = (size_t)kb * 1024;
-    }
-    int ns = (int)(budget / stage_bytes);
+    int ns = (int)(shape.ring_bytes / stage_bytes);
     if (ns < 2) ns = 2;
     if (ns > 16) ns = 16;
     if (ns > max_stages_needed) ns = max_stages_needed < 1 ? 1 : max_stages_needed;

@@ -235,7 +235,23 @@ cudaError_t launch_bg_argmax_final(const ArgmaxPart* parts, int n_tiles, StepSta
 cudaError_t launch_tile_weights(const uint16_t* src, uint16_t* dst, int rows, int K, cudaStream_t s);
 
 // ---- launchers (return the launch error) ----
-GemvPlan plan_gemv(int rows, int K, int unit, int wsize, int num_sms, int n_vec);
+// Launch shape of a weight-streaming GEMV: consumer warps per CTA (8 or 16,
+// plus one producer warp), CTAs per SM (1 or 2) and shared-memory ring bytes
+// per CTA.  Measured on the 26-layer single-GPU step (256 steps, context
+// 520-776): two 8-warp CTAs per SM with 72-88 KB rings beat one 16-warp CTA
+// with a 160 KB ring (1.566 vs 1.571 ms per token, w1|w3 alone 5.75 vs 5.68
+// TB/s; 64 KB rings lose): a CTA of the next launch can start streaming on an
+// SM while the other CTA of this launch is still in its tail, and an attention
+// CTA fits beside one GEMV CTA.  Tensor-parallel shards keep the wide shape,
+// whose fewer CTAs mean fewer peer arrivals per exchange.
+struct GemvShape {
+    int warps;
+    int ctas_per_sm;
+    size_t ring_bytes;
+};
+constexpr GemvShape kGemvPaired{8, 2, 80 * 1024};
+constexpr GemvShape kGemvWide{16, 1, 160 * 1024};
+GemvPlan plan_gemv(int rows, int K, int unit, int wsize, int num_sms, int n_vec, GemvShape shape = kGemvWide);
 bool gemv_supported(int K, int wsize);
 size_t gemv_max_smem();
 cudaError_t gemv_prepare(int dev);   // raise per-kernel smem limits once per device
