@@ -5,7 +5,9 @@ suitable for an ncu capture).
     python voxtral-rust_b200/profile_kernels.py --which step --layers 2 --steps 8
 
 --which o|w13|w2|head runs vox_profile_gemv (launches cycle over the layers);
---which step runs whole token steps of a full-width model with `--layers`
+--which encoder streams `--seconds` of synthetic 16 kHz audio through the
+encoder front end (log-mel + conv stem, 128 mel bins -> dim 1280) in 80 ms
+chunks; --which step runs whole token steps of a full-width model with `--layers`
 layers and the 131072-token vocabulary; --which batch runs multi-stream steps
 of `--streams` streams (contexts uniform in [256, 4096)); --which
 bo|bw13|bw2|bhead|bqkv times one multi-stream tensor-core GEMM, --which
@@ -26,7 +28,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--which", default="w13",
                     choices=["o", "w13", "w2", "head", "step", "batch", "bo", "bw13", "bw2", "bhead", "bqkv",
-                             "bchain"])
+                             "bchain", "encoder"])
+    ap.add_argument("--seconds", type=float, default=2.0)
     ap.add_argument("--streams", type=int, default=8)
     ap.add_argument("--layers", type=int, default=2)
     ap.add_argument("--launches", type=int, default=8)
@@ -37,6 +40,27 @@ def main():
     ap.add_argument("--mode", type=int, default=0, help="0 auto, 1 per-layer kernels, 2 persistent kernel")
     args = ap.parse_args()
     V = importlib.import_module("voxtral-rust_b200")
+    if args.which == "encoder":
+        import time
+
+        import numpy as np
+        rng = np.random.default_rng(11)
+        dim = 1280
+        w0 = (0.02 * rng.standard_normal(dim * 128 * 3)).astype(np.float32)
+        w1 = (0.02 * rng.standard_normal(dim * dim * 3)).astype(np.float32)
+        b0 = (0.02 * rng.standard_normal(dim)).astype(np.float32)
+        b1 = (0.02 * rng.standard_normal(dim)).astype(np.float32)
+        audio = (0.1 * rng.standard_normal(int(16000 * args.seconds))).astype(np.float32)
+        mel, stem = V.MelCtx(0), V.ConvStemState(128, dim, w0, b0, w1, b1)
+        t0, n_pos = time.perf_counter(), 0
+        for i in range(0, audio.size, 1280):
+            before = mel.frames()
+            mel.feed(audio[i:i + 1280])
+            frames, _ = mel.data(before, mel.frames() - before)
+            n_pos += stem.process(frames).shape[0]
+        dt = time.perf_counter() - t0
+        print(f"encoder: {args.seconds:.1f} s of audio in {dt * 1e3:.1f} ms, {n_pos} positions")
+        return
     cfg = V.DecoderConfig(dim=3072, hidden_dim=9216, n_heads=32, n_kv_heads=8, head_dim=128,
                           sliding_window=8192, norm_eps=1e-5, rope_theta=1e6)
     batched = args.which.startswith("b")
