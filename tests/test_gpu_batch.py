@@ -134,3 +134,29 @@ def test_batch_errors(V):
         assert view.layer_len_tokens(0) == 1 and kv.stream(0).layer_len_tokens(0) == 0
         with pytest.raises(V.VoxError):
             V.RollingKvCache(ctx, 2, 2, 32, 64, n_streams=9)
+
+
+def test_batch_greedy_26_layers_subset_of_streams(V, oracle):
+    """The multi-stream workload of the benchmark on the full 26-layer model:
+    8 streams with caches prefilled to the bench's contexts (uniform in
+    [256, 4096) from seed 1000), 64 greedy steps decoded together on the
+    device; streams 0 and 5 checked token by token against the oracle's own
+    greedy continuation (a subset, as the oracle costs about 0.2 s per token)."""
+    c, n_layers, vocab, n_steps = FULL, 26, 131072, 64
+    rng = np.random.default_rng(1000)
+    lens = [int(x) for x in rng.integers(256, 4096, 8)]
+    first = [int(t) for t in rng.integers(0, vocab, 8)]
+    m = oracle_model(oracle, c, n_layers, vocab, 0)
+    with make_ctx(V, c, n_layers, vocab, 0) as ctx:
+        kv = V.RollingKvCache(ctx, n_layers, c["n_kv_heads"], c["head_dim"], c["sliding_window"], n_streams=8)
+        for s, n in enumerate(lens):
+            kv.stream(s).fill_random(n, 0, KV_ID + 100 * s, 1.0)
+        got = ctx.model_generate_batch(kv, first, lens, n_steps)
+        kv.close()
+    for s in (0, 5):
+        oc = oracle_cache(oracle, c, n_layers, lens[s], 0, KV_ID + 100 * s)
+        tok, margins = first[s], []
+        for i in range(n_steps):
+            logits, tok = m.step(oc, tok, lens[s] + i)
+            margins.append(top2_margin(logits))
+            assert got[i, s] == tok, f"stream {s} step {i}: {got[i, s]} != {tok} (margin {margins[-1]:.3e})"

@@ -14,13 +14,16 @@
 // as mel.rs:42-106.
 //
 // Conv stem: the reference's chunk bookkeeping (mel tail, conv0 residual for
-// the stride-2 alignment, conv0 tail) runs on the host over device buffers;
-// each causal convolution is one kernel: thread (oc) of a CTA computes PT
-// consecutive output positions, summing bias + in[ic][t] * w[oc][ic][k] over
-// ic then k as conv.rs:60-68 does (weights transposed to [ic][k][oc] at
-// upload so a warp's weight loads are contiguous), then the tanh-approximated
-// GELU (conv.rs:11-19).  Sums are bit-identical to the reference's; tanhf
-// may differ in the last place.
+// the stride-2 alignment, conv0 tail) runs on the host over device buffers.
+// Each causal convolution of the stem is two kernels: the sum over input
+// channels split into ranges across CTAs (a chunk has only a few output
+// positions, so the split is what spreads the 19.7 MB weight read of conv1
+// over the SMs), then a fixed-order reduction of the ranges with the bias and
+// the tanh-approximated GELU (conv.rs:11-19).  Weights are transposed to
+// [ic][k][oc] at upload so a warp's weight loads are contiguous.  The
+// op-level call (vox_causal_conv1d_gelu) keeps the reference's own order: one
+// thread per output channel sums bias + in[ic][t] * w[oc][ic][k] over ic then
+// k as conv.rs:60-68 does, bit-identical; tanhf may differ in the last place.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -101,6 +104,7 @@ __global__ void __launch_bounds__(256) log_mel_kernel(const float* __restrict__ 
     __syncthreads();
     if (tid < kNfreq) {
         float re = 0.0f, im = 0.0f;
+#pragma unroll 16  // table loads run ahead; the sums keep their order
         for (int n = 0; n < kNfft; ++n) {
             const float w = wnd[n];
             re = __fadd_rn(re, __fmul_rn(w, cos_t[n * kNfreq + tid]));
@@ -111,6 +115,7 @@ __global__ void __launch_bounds__(256) log_mel_kernel(const float* __restrict__ 
     __syncthreads();
     if (tid < kMelBins) {
         float sum = 0.0f;
+#pragma unroll 8
         for (int k = 0; k < kNfreq; ++k) sum = __fadd_rn(sum, __fmul_rn(filt_t[k * kMelBins + tid], power[k]));
         if (sum < 1e-10f) sum = 1e-10f;
         float val = log10f(sum);
@@ -160,6 +165,75 @@ __global__ void __launch_bounds__(128) causal_conv3_gelu_kernel(const float* __r
         }
         out[(size_t)oc * out_len + ol0 + p] = v;
     }
+}
+
+// The conv stem's form of the same convolution: the sum over input channels is
+// split into `gridDim.y` contiguous ranges so that a streaming chunk (a few
+// output positions) still spreads the weight read over every SM; part[s] holds
+// split s's sums [cout, out_len] (bias not included).  conv_reduce_gelu_kernel
+// adds the splits in order, then the bias, then the GELU: deterministic, and
+// equal to the sequential sum within float rounding.
+__global__ void __launch_bounds__(128) conv3_split_kernel(const float* __restrict__ in, int length,
+                                                          const float* __restrict__ wt, int cin, int cout, int stride,
+                                                          int out_len, int splits, float* __restrict__ part) {
+    const int oc = blockIdx.x * blockDim.x + threadIdx.x;
+    const int s = blockIdx.y;
+    const int ol0 = blockIdx.z * kConvPT;
+    if (oc >= cout) return;
+    const int ic0 = (int)((long long)cin * s / splits), ic1 = (int)((long long)cin * (s + 1) / splits);
+    const int left_pad = 3 - stride;
+    float sum[kConvPT];
+#pragma unroll
+    for (int p = 0; p < kConvPT; ++p) sum[p] = 0.0f;
+    int ic = ic0;
+    for (; ic + 4 <= ic1; ic += 4) {  // four channels' weights in flight per thread
+        float w[4][3];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int k = 0; k < 3; ++k) w[u][k] = __ldg(wt + ((size_t)(ic + u) * 3 + k) * cout + oc);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const float* row = in + (size_t)(ic + u) * length;
+#pragma unroll
+            for (int k = 0; k < 3; ++k)
+#pragma unroll
+                for (int p = 0; p < kConvPT; ++p) {
+                    const int il = (ol0 + p) * stride - left_pad + k;
+                    if (ol0 + p < out_len && il >= 0 && il < length) sum[p] = fmaf(__ldg(row + il), w[u][k], sum[p]);
+                }
+        }
+    }
+    for (; ic < ic1; ++ic) {
+        const float* row = in + (size_t)ic * length;
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            const float w = __ldg(wt + ((size_t)ic * 3 + k) * cout + oc);
+#pragma unroll
+            for (int p = 0; p < kConvPT; ++p) {
+                const int il = (ol0 + p) * stride - left_pad + k;
+                if (ol0 + p < out_len && il >= 0 && il < length) sum[p] = fmaf(__ldg(row + il), w, sum[p]);
+            }
+        }
+    }
+    float* dst = part + ((size_t)s * cout + oc) * out_len;
+#pragma unroll
+    for (int p = 0; p < kConvPT; ++p)
+        if (ol0 + p < out_len) dst[ol0 + p] = sum[p];
+}
+
+// out[oc][t] = gelu(bias[oc] + sum over splits of part[s][oc][t]), splits in order.
+__global__ void conv_reduce_gelu_kernel(const float* __restrict__ part, int splits, const float* __restrict__ bias,
+                                        int cout, int out_len, float* __restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long n = (long long)cout * out_len;
+    if (i >= n) return;
+    float v = part[i];
+    for (int s = 1; s < splits; ++s) v += part[(size_t)s * n + i];
+    v = __fadd_rn(bias[i / out_len], v);
+    const float x3 = __fmul_rn(__fmul_rn(v, v), v);
+    const float inner = __fmul_rn(0.7978846f, __fadd_rn(v, __fmul_rn(0.044715f, x3)));
+    out[i] = __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, tanhf(inner)));
 }
 
 // dst[d * dst_len + dst_off + j] = src[d * src_len + src_off + j] for j < n, d < rows.
@@ -226,12 +300,28 @@ struct DBuf {
     }
 };
 
+// Split count of the conv stem's convolutions: enough CTAs for two per SM,
+// at least 8 input channels per split.
+int conv_splits(size_t cin, size_t cout, size_t out_len, int num_sms) {
+    const long long base = (long long)((cout + 127) / 128) * (long long)((out_len + kConvPT - 1) / kConvPT);
+    long long want = (2LL * num_sms + base - 1) / base;
+    const long long most = (long long)(cin / 8) > 0 ? (long long)(cin / 8) : 1;
+    if (want > most) want = most;
+    if (want > 64) want = 64;
+    return want < 1 ? 1 : (int)want;
+}
+
+// conv + bias + GELU into out [cout, out_len]; part: room for splits x cout x out_len floats.
 int launch_conv(const float* in, size_t length, const float* wt, const float* bias, size_t cin, size_t cout,
-                size_t stride, size_t out_len, float* out, cudaStream_t s) {
+                size_t stride, size_t out_len, float* out, float* part, int splits, cudaStream_t s) {
     if (out_len == 0) return VOX_OK;
-    dim3 grid((unsigned)((cout + 127) / 128), (unsigned)((out_len + kConvPT - 1) / kConvPT));
-    causal_conv3_gelu_kernel<<<grid, 128, 0, s>>>(in, (int)length, wt, bias, (int)cin, (int)cout, (int)stride,
-                                                  (int)out_len, out, 1);
+    dim3 grid((unsigned)((cout + 127) / 128), (unsigned)splits, (unsigned)((out_len + kConvPT - 1) / kConvPT));
+    conv3_split_kernel<<<grid, 128, 0, s>>>(in, (int)length, wt, (int)cin, (int)cout, (int)stride, (int)out_len,
+                                            splits, part);
+    ENC_CUDA(cudaGetLastError());
+    const long long n = (long long)cout * (long long)out_len;
+    conv_reduce_gelu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(part, splits, bias, (int)cout, (int)out_len,
+                                                                        out);
     ENC_CUDA(cudaGetLastError());
     return VOX_OK;
 }
@@ -400,8 +490,9 @@ struct vox_conv_stem {
     float* residual = nullptr;     // [dim] device
     size_t residual_count = 0;
     bool initialized = false;
-    DBuf conv_in, conv0, feed, c1_in, c1_out, rows;
+    DBuf conv_in, conv0, feed, c1_in, c1_out, rows, part;
     std::vector<float> h_in;
+    int num_sms = 148;
     uint64_t launches = 0;
 };
 
@@ -429,6 +520,8 @@ extern "C" int vox_conv_stem_create(int device, size_t mel_bins, size_t dim, con
     ENC_CUDA(cudaSetDevice(device));
     auto* s = new vox_conv_stem();
     s->dev = device;
+    if (cudaDeviceGetAttribute(&s->num_sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || s->num_sms <= 0)
+        s->num_sms = 148;
     s->mel_bins = mel_bins;
     s->dim = dim;
     s->mel_tail.assign(mel_bins * 2, 0.0f);
@@ -458,7 +551,7 @@ extern "C" void vox_conv_stem_destroy(vox_conv_stem* s) {
     if (s->stream) cudaStreamSynchronize(s->stream);
     for (float* p : {s->w0t, s->b0, s->w1t, s->b1, s->conv0_tail, s->residual})
         if (p) cudaFree(p);
-    for (DBuf* b : {&s->conv_in, &s->conv0, &s->feed, &s->c1_in, &s->c1_out, &s->rows}) b->release();
+    for (DBuf* b : {&s->conv_in, &s->conv0, &s->feed, &s->c1_in, &s->c1_out, &s->rows, &s->part}) b->release();
     if (s->stream) cudaStreamDestroy(s->stream);
     delete s;
 }
@@ -495,8 +588,12 @@ extern "C" int vox_conv_stem_process(vox_conv_stem* s, const float* mel_new, siz
     ENC_TRY(s->conv_in.reserve(M * L, st));
     ENC_TRY(s->conv0.reserve(D * L, st));
     ENC_CUDA(cudaMemcpyAsync(s->conv_in.p, s->h_in.data(), M * L * 4, cudaMemcpyHostToDevice, st));
-    ENC_TRY(launch_conv(s->conv_in.p, L, s->w0t, s->b0, M, D, 1, L, s->conv0.p, st));  // stride 1: out_len = L
-    ++s->launches;
+    {  // stride 1: out_len = L
+        const int sp = conv_splits(M, D, L, s->num_sms);
+        ENC_TRY(s->part.reserve((size_t)sp * D * L, st));
+        ENC_TRY(launch_conv(s->conv_in.p, L, s->w0t, s->b0, M, D, 1, L, s->conv0.p, s->part.p, sp, st));
+        s->launches += 2;
+    }
     const size_t c0_len = n_new;  // new conv0 columns start at column `pre`
 
     // stride alignment for conv1 (conv.rs:227-272)
@@ -520,8 +617,12 @@ extern "C" int vox_conv_stem_process(vox_conv_stem* s, const float* mel_new, siz
     ENC_TRY(launch_copy_cols(s->conv0_tail, 2, 0, s->c1_in.p, c1_len, c1_len - 2, 2, D, st));
     const size_t c1_out_len = c1_len / 2, discard = is_first ? 0 : 1;
     ENC_TRY(s->c1_out.reserve(D * c1_out_len, st));
-    ENC_TRY(launch_conv(s->c1_in.p, c1_len, s->w1t, s->b1, D, D, 2, c1_out_len, s->c1_out.p, st));
-    ++s->launches;
+    {
+        const int sp = conv_splits(D, D, c1_out_len, s->num_sms);
+        ENC_TRY(s->part.reserve((size_t)sp * D * c1_out_len, st));
+        ENC_TRY(launch_conv(s->c1_in.p, c1_len, s->w1t, s->b1, D, D, 2, c1_out_len, s->c1_out.p, s->part.p, sp, st));
+        s->launches += 2;
+    }
     const size_t n = c1_out_len > discard ? c1_out_len - discard : 0;
     if (n > out_cap_rows) return report_errorf(VOX_ERR_SHAPE, "output holds %zu of %zu positions", out_cap_rows, n);
     if (n) {
