@@ -79,6 +79,17 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def tensor_peak():
+    """Dense bf16 tensor-core TFLOP/s: the measured burst figure (a prefill is
+    a burst of a few milliseconds), else the fallback."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        if "bf16_tflops" in d:
+            return float(d["bf16_tflops"]), "measured (burst)"
+    return 1590.0, "fallback"
+
+
 def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
@@ -395,6 +406,44 @@ def run_context(V, ctx, args, rank, dist, fill, steps):
             "ring_state": list(want)}
 
 
+PREFILL_FLOPS_PER_TOKEN = LAYER_WEIGHT_BYTES  # 2 FLOPs per bf16 weight (2 bytes) per token
+
+
+def run_prefill(V, ctx, rank, dist, reps=3):
+    """The 512-id prompt of the token-loop workload through vox_model_prefill
+    (tensor-core passes) into an empty cache, timed on the device and by the
+    host wall clock around the call (host ids in, the call returns when the
+    cache is written); the same prompt as 512 token steps
+    (vox_model_prefill_steps) once, for comparison.  Returns per-rank times."""
+    kv = V.RollingKvCache(ctx, LAYERS, NKV, HD, WINDOW)
+    prompt = prompt_ids(rank + 31, PROMPT)
+    ctx.model_prefill(kv, prompt, 0)  # warm-up (tiles the weights once)
+    dev, wall = [], []
+    for _ in range(reps):
+        kv.reset()
+        ctx.synchronize()
+        if dist:
+            dist.barrier()
+        t0 = time.perf_counter()
+        ctx.record_event(10)
+        launches0 = ctx.kernel_launches()
+        ctx.model_prefill(kv, prompt, 0)
+        ctx.record_event(11)
+        ctx.synchronize()
+        wall.append((time.perf_counter() - t0) * 1e3)
+        dev.append(ctx.elapsed_ms(10, 11))
+        launches = ctx.kernel_launches() - launches0
+    ok = all(tuple(kv.device_state(l)) == (PROMPT, 0, 0) for l in range(LAYERS))
+    kv.reset()
+    ctx.record_event(12)
+    ctx.model_prefill_steps(kv, prompt, 0)
+    ctx.record_event(13)
+    ctx.synchronize()
+    steps_ms = ctx.elapsed_ms(12, 13)
+    kv.close()
+    return {"ms": min(dev), "wall_ms": min(wall), "steps_ms": steps_ms, "launches": launches, "ring_ok": ok}
+
+
 def context_object(run, t_max, world, peak, workload):
     steps = run["steps"]
     mean_ctx = sum(run["context"]) / 2
@@ -590,6 +639,7 @@ def run_ours(args):
 
     long_run = None if args.ctx_steps == 0 else run_context(V, ctx, args, rank, dist, LONG_CONTEXT, args.ctx_steps)
     roll_run = None if args.ctx_steps == 0 else run_context(V, ctx, args, rank, dist, WINDOW, args.ctx_steps)
+    pf_run = None if args.no_prefill else run_prefill(V, ctx, rank, dist)
     ms_run = None if args.ms_steps == 0 else run_multi_stream(V, ctx, args, rank, world, dist)
     enc_run = None if args.no_encoder else run_encoder(V, local)
     tp_run = None
@@ -599,7 +649,9 @@ def run_ours(args):
         tp_run = run_tensor_parallel(V, args, rank, world, local, dist, parity_ref)
 
     t_max, e2e_max = ms, e2e_ms
-    ms_max = ms_e2e_max = tp_max = long_max = roll_max = enc_max = 0.0
+    ms_max = ms_e2e_max = tp_max = long_max = roll_max = enc_max = pf_max = pf_wall_max = pf_steps_max = 0.0
+    if pf_run:
+        pf_max, pf_wall_max, pf_steps_max = pf_run["ms"], pf_run["wall_ms"], pf_run["steps_ms"]
     if enc_run:
         enc_max = enc_run["gpu_s"]
     if ms_run:
@@ -610,9 +662,11 @@ def run_ours(args):
         long_max, roll_max = long_run["ms"], roll_run["ms"]
     if dist:
         import torch
-        t = torch.tensor([ms, e2e_ms, ms_max, ms_e2e_max, tp_max, long_max, roll_max, enc_max], dtype=torch.float64)
+        t = torch.tensor([ms, e2e_ms, ms_max, ms_e2e_max, tp_max, long_max, roll_max, enc_max, pf_max, pf_wall_max,
+                          pf_steps_max], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_max, e2e_max, ms_max, ms_e2e_max, tp_max, long_max, roll_max, enc_max = (float(x) for x in t)
+        (t_max, e2e_max, ms_max, ms_e2e_max, tp_max, long_max, roll_max, enc_max, pf_max, pf_wall_max,
+         pf_steps_max) = (float(x) for x in t)
         if roll_run:
             ok = torch.tensor([1.0 if roll_run["ring_ok"] and long_run["ring_ok"] else 0.0])
             dist.all_reduce(ok, op=dist.ReduceOp.MIN)
@@ -664,6 +718,24 @@ def run_ours(args):
                                                "start": roll_run["ring_state"][1],
                                                "pos_offset": roll_run["ring_state"][2],
                                                "matches_kv_rs_index_rule": roll_run["ring_ok"]}
+    if pf_run:
+        flops = PREFILL_FLOPS_PER_TOKEN * LAYERS * PROMPT
+        tflops = flops / (pf_max / 1e3) / 1e12
+        tpeak, tpeak_kind = tensor_peak()
+        line["prefill"] = {
+            "metric": "prompt prefill tokens/s (tensor-core passes)", "value": PROMPT * world / (pf_max / 1e3),
+            "unit": "tokens/s", "ms": pf_max, "prompt_tokens": PROMPT, "gpu_launches": pf_run["launches"],
+            "workload": (f"the {PROMPT}-id prompt of the token-loop workload into an empty cache, 26 layers: "
+                         f"vox_model_prefill, one pass of dense tcgen05 GEMMs over all {PROMPT} tokens "
+                         f"(activations as bf16 hi + lo parts), causal attention, ring append"),
+            "e2e": {"value": PROMPT * world / (pf_wall_max / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 4 * PROMPT, "d2h_bytes_per_step": 4},
+            "token_steps_ms": pf_steps_max, "speedup_vs_token_steps": pf_steps_max / pf_max,
+            "ring_state_ok": pf_run["ring_ok"],
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": tpeak, "peak_kind": tpeak_kind,
+                         "unit": "TFLOP/s", "frac": tflops / tpeak,
+                         "flops": flops, "note": "algorithmic FLOPs of the 26 layers' linears (2 per weight per "
+                                                 "token); the hi/lo split doubles the tensor-core work"}}
     if enc_run:
         chunks = enc_run["audio_s"] * 16000 // ENC_CHUNK
         line["encoder"] = {
@@ -729,6 +801,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--cpu-layer-steps", type=int, default=24)
     ap.add_argument("--no-encoder", action="store_true", help="skip the encoder front-end run")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prompt prefill run")
     ap.add_argument("--ctx-steps", type=int, default=256,
                     help="greedy steps of the long-context (1536) and full-window rolling runs (0 skips them)")
     ap.add_argument("--ms-steps", type=int, default=512,

@@ -217,8 +217,17 @@ int vox_model_step(vox_ctx* ctx, vox_kv* kv, int32_t token, size_t pos, int32_t*
  * on the device (each step's argmax feeds the next).  tokens_out [n_steps]. */
 int vox_model_generate(vox_ctx* ctx, vox_kv* kv, int32_t token, size_t pos, size_t n_steps,
                        int32_t* tokens_out);
-/* Sequential prefill of n tokens at positions pos0.. (logits discarded). */
+/* Prefill of n tokens at positions pos0.. (logits discarded): the cache ends
+ * as n single-token steps (decoder.rs:88-155, kv.rs:48-88) leave it, within
+ * float tolerance.  With bf16 weights (every K a multiple of 64, at most 4 q
+ * heads per kv head, head_dim 32/64/128/256) and n >= 2, passes of up to 512
+ * tokens run each layer at once: dense tensor-core GEMMs over all the pass's
+ * tokens, causal attention over the cache plus the pass, keys and values
+ * appended at the slots the token loop would use.  Otherwise, as
+ * vox_model_prefill_steps. */
 int vox_model_prefill(vox_ctx* ctx, vox_kv* kv, const int32_t* tokens, size_t n, size_t pos0);
+/* The same prefill as n sequential token steps (one CUDA graph launch each). */
+int vox_model_prefill_steps(vox_ctx* ctx, vox_kv* kv, const int32_t* tokens, size_t n, size_t pos0);
 
 /* One token for every stream of a multi-stream cache (bf16 weights): the
  * step of vox_model_step, with every linear on the tensor cores reading each

@@ -163,6 +163,7 @@ _SIGS = {
     "vox_model_step": ([VP, VP, C.c_int32, SZ, I32P, F32P], C.c_int),
     "vox_model_generate": ([VP, VP, C.c_int32, SZ, SZ, I32P], C.c_int),
     "vox_model_prefill": ([VP, VP, I32P, SZ, SZ], C.c_int),
+    "vox_model_prefill_steps": ([VP, VP, I32P, SZ, SZ], C.c_int),
     "vox_profile_gemv": ([VP, C.c_int, SZ, F32P, C.POINTER(C.c_uint64)], C.c_int),
     "vox_tp_shard_of": ([C.POINTER(DecoderConfig), SZ, C.c_int, C.c_int, C.POINTER(TpShard)], C.c_int),
     "vox_tp_unique_id": ([C.c_char_p], C.c_int),
@@ -415,8 +416,14 @@ class Context:
         return nxt.value, logits
 
     def model_prefill(self, cache, tokens, pos0=0):
+        """Prefill (tensor-core passes where the shape allows, else token steps)."""
         t = np.ascontiguousarray(tokens, dtype=np.int32)
         _check(lib().vox_model_prefill(self.h, cache.h, _p(t, I32P), t.size, int(pos0)))
+
+    def model_prefill_steps(self, cache, tokens, pos0=0):
+        """Prefill as one token step per id."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        _check(lib().vox_model_prefill_steps(self.h, cache.h, _p(t, I32P), t.size, int(pos0)))
 
     def model_generate(self, cache, token, pos, n_steps):
         out = np.empty(n_steps, np.int32)

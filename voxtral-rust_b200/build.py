@@ -22,10 +22,10 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-ffp-contract=off",
           "-I", CSRC, "-I", os.path.join(ROOT, "include")]
 SOURCES = ["vox_gemv.cu", "vox_attention.cu", "vox_misc.cu", "vox_noalloc.cu", "vox_bgemm.cu",
-           "vox_encoder.cu",
+           "vox_prefill.cu", "vox_encoder.cu",
            "vox_capi.cpp", "vox_tp.cpp", "vox_stream.cpp", "vox_weights.cpp",
            "vox_tokenizer.cpp"]
-HEADERS = ["vox_kernels.h", "vox_device.cuh", "vox_host.h", "vox_internal.h", "vox_json.h",
+HEADERS = ["vox_kernels.h", "vox_device.cuh", "vox_tcgen05.cuh", "vox_host.h", "vox_internal.h", "vox_json.h",
            "vox_watchdog.h"]
 
 

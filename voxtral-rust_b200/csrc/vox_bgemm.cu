@@ -27,6 +27,7 @@
 #include <math.h>
 
 #include "vox_device.cuh"
+#include "vox_tcgen05.cuh"
 
 namespace vox {
 
@@ -43,55 +44,7 @@ constexpr int kThreads = 256;                // w0 producer, w1 MMA, w4..w7 epil
 constexpr int kWorkers = kThreads - 32;      // every warp but the producer
 constexpr uint32_t kTmemCols = 32;           // two 16-column accumulators
 
-// UMMA instruction descriptor: D f32 (bit 4), A and B bf16 (bits 7, 10), both
-// K-major, N >> 3 at bit 17, M >> 4 at bit 24.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kN >> 3) << 17) |
-                            ((uint32_t)(kBM >> 4) << 24);
-
-// Shared-memory matrix descriptor, no swizzle, K-major (sm100: start address,
-// LBO and SBO in 16-byte units at bits 0, 16, 32; version 1 at bit 46;
-// layout type 0 at bits 61-63).
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
-    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
-    d |= (uint64_t)1 << 46;
-    return d;
-}
-
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-    const uint32_t zero = 0u;  // no output lane disabled
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate), "r"(zero)
-        : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                     smem_addr(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tmem_fence_before() {
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_fence_after() {
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
-        "%13, %14, %15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
+constexpr uint32_t kIdesc = umma_idesc_bf16(kBM, kN);
 
 __device__ __forceinline__ uint16_t f2bf(float f) {  // round to nearest even
     const uint32_t u = __float_as_uint(f);
@@ -609,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1) bgemm_kernel(const __grid_constan
                     for (int j = 0; j < nb * 4; ++j, ++kstep) {
                         const uint64_t ad = umma_desc(a_addr + (uint32_t)j * 4096u, 2048u, 128u);
                         const uint64_t bd = umma_desc(xs_addr + (uint32_t)kstep * 512u, 256u, 128u);
-                        umma_f16(d, ad, bd, kstep > 0 ? 1u : 0u);
+                        umma_f16(d, ad, bd, kIdesc, kstep > 0 ? 1u : 0u);
                     }
                     umma_commit(&empty[slot]);  // frees the stage once these MMAs have read it
                 }

@@ -94,6 +94,47 @@ struct BatchBufs {
     unsigned char *xop_a = nullptr, *xop_o = nullptr, *xop_f = nullptr, *xop_h = nullptr;
 };
 
+// Device buffers of the batched prefill (vox_prefill.cu), sized for one pass
+// of up to kPrefillPass tokens; `part` grows with the largest split plan.
+constexpr int kPrefillPass = 512;
+struct PrefillBufs {
+    bool ready = false;
+    float *h = nullptr, *q = nullptr, *kc = nullptr, *vc = nullptr, *attn = nullptr, *part = nullptr;
+    size_t part_floats = 0;
+    unsigned char* xop = nullptr;
+    int32_t* tokens = nullptr;    // [kPrefillPass]
+    int32_t* h_tokens = nullptr;  // pinned staging
+};
+
+// Launch shape of one prefill GEMM: the K split count that minimises the
+// busiest CTA's K blocks (rounds of items x blocks per item) over
+// tiles x token blocks x splits items, at least 4 K blocks per split, ties to
+// fewer splits (each split writes and rereads a [T, rows] partial).
+struct PfPlan {
+    int rows = 0, K = 0, tiles = 0, kbt = 0, splits = 1, grid = 1;
+};
+PfPlan make_pfplan(int rows, int K, int nblocks, int num_sms) {
+    PfPlan p;
+    p.rows = rows;
+    p.K = K;
+    p.tiles = (rows + 127) / 128;
+    p.kbt = K / 64;
+    const long long base = (long long)p.tiles * nblocks;
+    long long best = -1;
+    for (int s = 1; s <= 16 && s <= p.kbt; ++s) {
+        if (s > 1 && p.kbt / s < 4) break;
+        const long long items = base * s;
+        const long long grid = std::min<long long>(items, num_sms);
+        const long long cost = ((items + grid - 1) / grid) * ((p.kbt + s - 1) / s);
+        if (best < 0 || cost < best) {
+            best = cost;
+            p.splits = s;
+            p.grid = (int)grid;
+        }
+    }
+    return p;
+}
+
 // K splits and grid of a multi-stream GEMM launched on its own: one CTA per
 // SM (the 128 KB weight ring fills it), the split count that minimises the
 // busiest CTA's K blocks (items per CTA x blocks per item), at most
@@ -212,6 +253,7 @@ struct vox_ctx {
     unsigned char* head_t = nullptr;
     bool head_tiled = false;
     BatchBufs bb;
+    PrefillBufs pf;
 };
 
 // A rolling cache of one stream, or of n_streams independent streams laid
@@ -546,6 +588,20 @@ int tile_into(vox_ctx* c, unsigned char** dst, const void* src, int rows, int K)
     return VOX_OK;
 }
 
+// (Re)tile the layer matrices whose tiled copy is stale (enqueued only).
+int tile_layers(vox_ctx* c) {
+    const int dim = (int)c->cfg.dim, hid = (int)c->cfg.hidden_dim, qd = (int)c->q_dim, kvd = (int)c->kv_dim;
+    for (auto& L : c->layers) {
+        if (L.tiled) continue;
+        TRY(tile_into(c, &L.wqkv_t, L.wqkv, qd + 2 * kvd, dim));
+        TRY(tile_into(c, &L.wo_t, L.wo, dim, qd));
+        TRY(tile_into(c, &L.w13_t, L.w13, 2 * hid, dim));
+        TRY(tile_into(c, &L.w2_t, L.w2, dim, hid));
+        L.tiled = true;
+    }
+    return VOX_OK;
+}
+
 // Allocate the multi-stream buffers once and (re)tile stale weights.
 int ensure_batch(vox_ctx* c) {
     TRY(batch_supported(c));
@@ -610,21 +666,213 @@ int ensure_batch(vox_ctx* c) {
         CUDA_TRY(cudaMallocHost(&b.h_steps, 8 * sizeof(StepState)));
         b.ready = true;
     }
-    const int kvd = (int)c->kv_dim;
-    for (auto& L : c->layers) {
-        if (L.tiled) continue;
-        TRY(tile_into(c, &L.wqkv_t, L.wqkv, qd + 2 * kvd, dim));
-        TRY(tile_into(c, &L.wo_t, L.wo, dim, qd));
-        TRY(tile_into(c, &L.w13_t, L.w13, 2 * hid, dim));
-        TRY(tile_into(c, &L.w2_t, L.w2, dim, hid));
-        L.tiled = true;
-    }
+    TRY(tile_layers(c));
     if (!c->head_tiled) {
         TRY(tile_into(c, &c->head_t, c->lm_head, vocab, dim));
         c->head_tiled = true;
     }
     CUDA_TRY(cudaStreamSynchronize(c->stream));
     return VOX_OK;
+}
+
+// ---- batched prefill (tensor-core GEMMs, vox_prefill.cu) ------------------------
+// Shapes the batched prefill handles: bf16 weights, every K a multiple of 64,
+// at most 4 q heads per kv head, head_dim 32, 64, 128 or 256.
+bool prefill_batched_supported(const vox_ctx* c) {
+    const vox_decoder_config& g = c->cfg;
+    if (c->wsize != 2 || c->opt.vocab == 0) return false;
+    if (g.dim % 64 || c->q_dim % 64 || g.hidden_dim % 64) return false;
+    const size_t G = g.n_heads / g.n_kv_heads;
+    if (G < 1 || G > 4) return false;
+    return g.head_dim == 32 || g.head_dim == 64 || g.head_dim == 128 || g.head_dim == 256;
+}
+
+int ensure_prefill(vox_ctx* c) {
+    PrefillBufs& f = c->pf;
+    if (f.ready) return VOX_OK;
+    const size_t T = kPrefillPass, dim = c->cfg.dim, qd = c->q_dim, kvd = c->kv_dim, hid = c->cfg.hidden_dim;
+    const size_t kmax = std::max(std::max(dim, qd), hid);
+    CUDA_TRY(dalloc(&f.h, T * dim));
+    CUDA_TRY(dalloc(&f.q, T * qd));
+    CUDA_TRY(dalloc(&f.kc, T * kvd));
+    CUDA_TRY(dalloc(&f.vc, T * kvd));
+    CUDA_TRY(dalloc(&f.attn, T * qd));
+    CUDA_TRY(cudaMalloc(&f.xop, pf_xop_bytes((int)T, (int)kmax)));
+    CUDA_TRY(dalloc(&f.tokens, T));
+    CUDA_TRY(cudaMallocHost(&f.h_tokens, T * sizeof(int32_t)));
+    f.ready = true;
+    return VOX_OK;
+}
+
+int ensure_prefill_part(vox_ctx* c, size_t floats) {
+    PrefillBufs& f = c->pf;
+    if (floats <= f.part_floats) return VOX_OK;
+    if (f.part) {
+        CUDA_TRY(cudaStreamSynchronize(c->stream));
+        cudaFree(f.part);
+        f.part = nullptr;
+        f.part_floats = 0;
+    }
+    CUDA_TRY(dalloc(&f.part, floats));
+    f.part_floats = floats;
+    return VOX_OK;
+}
+
+int enqueue_pf_gemm(vox_ctx* c, const PfPlan& p, const unsigned char* wt, int tn, int nblocks, int T) {
+    PfGemmArgs a{};
+    a.wt = wt;
+    a.xop = c->pf.xop;
+    a.part = c->pf.part;
+    a.rows = p.rows;
+    a.kbt = p.kbt;
+    a.tiles = p.tiles;
+    a.tn = tn;
+    a.nblocks = nblocks;
+    a.T = T;
+    a.splits = p.splits;
+    a.err = c->err;
+    CUDA_TRY(record_launch(c, launch_pf_gemm(a, p.grid, c->stream)));
+    return VOX_OK;
+}
+
+// Prefill of tokens[0..n) at positions pos0.. through every layer, one pass
+// of up to kPrefillPass tokens at a time (decoder.rs:88-155 for each token,
+// kv.rs:48-88 appends in token order).  With `adapter` the first layer's
+// input of position p is adapter[p mod adapter_cap] + widen(embed[token]).
+// The last layer's attention output, o-proj and FFN feed only the logits,
+// which a prefill discards, so they are not computed.  Synchronises once.
+int prefill_batched(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, size_t pos0, const float* adapter,
+                    int adapter_cap) {
+    TRY(tile_layers(c));
+    TRY(ensure_prefill(c));
+    PrefillBufs& f = c->pf;
+    const vox_decoder_config& g = c->cfg;
+    const int dim = (int)g.dim, qd = (int)c->q_dim, kvd = (int)c->kv_dim, hid = (int)g.hidden_dim;
+    const int rows_qkv = qd + 2 * kvd;
+    const size_t nl = c->layers.size();
+    int win = (int)kv->window;
+    if (g.sliding_window > 0) win = std::min(win, (int)g.sliding_window);
+    for (size_t i0 = 0; i0 < n; i0 += kPrefillPass) {
+        const int T = (int)std::min<size_t>(kPrefillPass, n - i0);
+        const int tn = T >= 128 ? 128 : (T + 15) / 16 * 16;
+        const int nblocks = (T + tn - 1) / tn, Tp = nblocks * tn;
+        const PfPlan pq = make_pfplan(rows_qkv, dim, nblocks, c->num_sms);
+        const PfPlan po = make_pfplan(dim, qd, nblocks, c->num_sms);
+        const PfPlan p13 = make_pfplan(2 * hid, dim, nblocks, c->num_sms);
+        const PfPlan p2 = make_pfplan(dim, hid, nblocks, c->num_sms);
+        size_t part = 0;
+        for (const PfPlan* p : {&pq, &po, &p13, &p2}) part = std::max(part, (size_t)p->splits * T * p->rows);
+        TRY(ensure_prefill_part(c, part));
+        // the staging buffer is reused: the previous pass's copy must be done
+        CUDA_TRY(cudaStreamSynchronize(c->stream));
+        std::memcpy(f.h_tokens, tokens + i0, (size_t)T * sizeof(int32_t));
+        CUDA_TRY(cudaMemcpyAsync(f.tokens, f.h_tokens, (size_t)T * sizeof(int32_t), cudaMemcpyHostToDevice,
+                                 c->stream));
+        const long long p0 = (long long)(pos0 + i0);
+
+        PfNormArgs na{};
+        na.h = f.h;
+        na.embed = c->embed;
+        na.tokens = f.tokens;
+        na.vocab = (int)c->opt.vocab;
+        na.adapter = adapter;
+        na.adapter_cap = adapter_cap;
+        na.pos0 = p0;
+        na.gain = c->layers[0].attn_norm;
+        na.eps = g.norm_eps;
+        na.xop = f.xop;
+        na.tn = tn;
+        na.T = T;
+        na.dim = dim;
+        na.err = c->err;
+        CUDA_TRY(record_launch(c, launch_pf_norm(na, Tp, c->stream)));
+
+        for (size_t l = 0; l < nl; ++l) {
+            const LayerDev& L = c->layers[l];
+            const bool last = l + 1 == nl;
+            float* kr = kv->k + l * kv->layer_elems();
+            float* vr = kv->v + l * kv->layer_elems();
+            // 1) q|k|v for every token, RoPE at its position
+            TRY(enqueue_pf_gemm(c, pq, L.wqkv_t, tn, nblocks, T));
+            PfQkvArgs qa{};
+            qa.part = f.part;
+            qa.splits = pq.splits;
+            qa.T = T;
+            qa.q_dim = qd;
+            qa.kv_dim = kvd;
+            qa.head_dim = (int)g.head_dim;
+            qa.rope_cos = c->rope_cos;
+            qa.rope_sin = c->rope_sin;
+            qa.max_pos = c->max_pos;
+            qa.pos0 = p0;
+            qa.q = f.q;
+            qa.kc = f.kc;
+            qa.vc = f.vc;
+            qa.err = c->err;
+            CUDA_TRY(record_launch(c, launch_pf_qkv(qa, c->stream)));
+            HostKv& hs = kv->hs[l];
+            // 2) causal attention over the cache before the pass + the pass
+            if (!last) {
+                PfAttnArgs aa{};
+                aa.q = f.q;
+                aa.kc = f.kc;
+                aa.vc = f.vc;
+                aa.k_ring = kr;
+                aa.v_ring = vr;
+                aa.T = T;
+                aa.n_heads = (int)g.n_heads;
+                aa.n_kv = (int)g.n_kv_heads;
+                aa.head_dim = (int)g.head_dim;
+                aa.cap = (int)kv->cap;
+                aa.len0 = (int)hs.len;
+                aa.start0 = (int)hs.start;
+                aa.win = win;
+                aa.scale = 1.0f / sqrtf((float)g.head_dim);
+                aa.out = f.attn;
+                CUDA_TRY(record_launch(c, launch_pf_attn(aa, c->stream)));
+                CUDA_TRY(record_launch(c, launch_pf_split(f.attn, T, Tp, qd, f.xop, tn, c->stream)));
+            }
+            // 3) the pass's keys and values into the ring, state after T appends
+            PfCommitArgs ca{};
+            ca.kc = f.kc;
+            ca.vc = f.vc;
+            ca.k_ring = kr;
+            ca.v_ring = vr;
+            ca.T = T;
+            ca.kv_dim = kvd;
+            ca.head_dim = (int)g.head_dim;
+            ca.cap = (int)kv->cap;
+            ca.end0 = (long long)((hs.start + hs.len) % kv->cap);
+            ca.state = kv->dstate + l;
+            for (int t = 0; t < T; ++t) host_append(hs, 1, kv->window, kv->cap);
+            ca.final_state.len = (int32_t)hs.len;
+            ca.final_state.start = (int32_t)hs.start;
+            ca.final_state.pos_offset = (int64_t)hs.pos_offset;
+            CUDA_TRY(record_launch(c, launch_pf_commit(ca, c->stream)));
+            if (last) break;
+            // 4) o-proj + residual, RMSNorm -> w1|w3 -> SwiGLU -> w2 + residual
+            TRY(enqueue_pf_gemm(c, po, L.wo_t, tn, nblocks, T));
+            na = PfNormArgs{};
+            na.h = f.h;
+            na.part = f.part;
+            na.splits = po.splits;
+            na.gain = L.ffn_norm;
+            na.eps = g.norm_eps;
+            na.xop = f.xop;
+            na.tn = tn;
+            na.T = T;
+            na.dim = dim;
+            na.err = c->err;
+            CUDA_TRY(record_launch(c, launch_pf_norm(na, Tp, c->stream)));
+            TRY(enqueue_pf_gemm(c, p13, L.w13_t, tn, nblocks, T));
+            CUDA_TRY(record_launch(c, launch_pf_swiglu(f.part, p13.splits, T, Tp, hid, f.xop, tn, c->stream)));
+            TRY(enqueue_pf_gemm(c, p2, L.w2_t, tn, nblocks, T));
+            na.splits = p2.splits;
+            na.gain = c->layers[l + 1].attn_norm;
+            CUDA_TRY(record_launch(c, launch_pf_norm(na, Tp, c->stream)));
+        }
+    }
+    return check_device_errors(c);
 }
 
 BgArgs bg_args(vox_ctx* c, const BgPlan& p, const unsigned char* wt, int B, int epi) {
@@ -989,6 +1237,13 @@ void vox_ctx_destroy(vox_ctx* c) {
         if (b.h_steps) cudaFreeHost(b.h_steps);
         if (b.h_tok) cudaFreeHost(b.h_tok);
     }
+    {
+        PrefillBufs& f = c->pf;
+        void* fp[] = {f.h, f.q, f.kc, f.vc, f.attn, f.part, f.xop, f.tokens};
+        for (void* p : fp)
+            if (p) cudaFree(p);
+        if (f.h_tokens) cudaFreeHost(f.h_tokens);
+    }
     if (c->h_steps) cudaFreeHost(c->h_steps);
     if (c->h_tok) cudaFreeHost(c->h_tok);
     if (c->h_err) cudaFreeHost(c->h_err);
@@ -1053,6 +1308,7 @@ int vox_ctx_create(const vox_decoder_config* cfg, const vox_ctx_options* opt, vo
     CTX_TRY(gemv_prepare(c->dev));
     CTX_TRY(attn_prepare(c->dev));
     CTX_TRY(bgemm_prepare(c->dev));
+    CTX_TRY(pf_prepare());
     CTX_TRY(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
     for (auto& e : c->ev) CTX_TRY(cudaEventCreate(&e));
 
@@ -1548,7 +1804,7 @@ int vox_model_step(vox_ctx* c, vox_kv* kv, int32_t token, size_t pos, int32_t* n
     return VOX_OK;
 }
 
-int vox_model_prefill(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, size_t pos0) {
+static int prefill_checks(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, size_t pos0) {
     TRY(model_ready(c, kv));
     TRY(single_stream(kv));
     if (n == 0) return VOX_OK;
@@ -1557,6 +1813,19 @@ int vox_model_prefill(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, s
     for (size_t i = 0; i < n; ++i)
         if (tokens[i] < 0 || (size_t)tokens[i] >= c->opt.vocab)
             return fail(VOX_ERR_RANGE, "token %d outside the vocabulary", tokens[i]);
+    return VOX_OK;
+}
+
+int vox_model_prefill(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, size_t pos0) {
+    TRY(prefill_checks(c, kv, tokens, n, pos0));
+    if (n < 2 || !prefill_batched_supported(c)) return vox_model_prefill_steps(c, kv, tokens, n, pos0);
+    CUDA_TRY(cudaSetDevice(c->dev));
+    return prefill_batched(c, kv, tokens, n, pos0, nullptr, 0);
+}
+
+int vox_model_prefill_steps(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, size_t pos0) {
+    TRY(prefill_checks(c, kv, tokens, n, pos0));
+    if (n == 0) return VOX_OK;
     CUDA_TRY(cudaSetDevice(c->dev));
     TRY(build_step_graph(c, kv));
     CUDA_TRY(cudaStreamSynchronize(c->stream));
@@ -2090,6 +2359,8 @@ int capture_adapter_graphs(vox_ctx* c, vox_kv* kv, const float* adapter, int ada
     TRY(capture_step(c, kv, false, &g->full, &g->k_full, adapter, adapter_cap));
     if (attn_cluster_size((int)c->cfg.n_heads, (int)c->cfg.n_kv_heads, (int)c->cfg.head_dim) > 0)
         TRY(capture_step(c, kv, true, &g->short_attn, &g->k_short, adapter, adapter_cap));
+    g->adapter = adapter;
+    g->adapter_cap = adapter_cap;
     return VOX_OK;
 }
 
@@ -2107,6 +2378,13 @@ int run_step_graphs(vox_ctx* c, vox_kv* kv, const StepGraphs& g, const int32_t* 
     if (n_greedy && (greedy_tok < 0 || (size_t)greedy_tok >= c->opt.vocab))
         return fail(VOX_ERR_RANGE, "token %d outside the vocabulary", greedy_tok);
     CUDA_TRY(cudaSetDevice(c->dev));
+    if (n_fixed >= 2 && prefill_batched_supported(c)) {  // the cache's mirror follows inside
+        TRY(prefill_batched(c, kv, fixed, n_fixed, pos0, g.adapter, g.adapter_cap));
+        pos0 += n_fixed;
+        fixed = nullptr;
+        n_fixed = 0;
+        if (n_greedy == 0) return VOX_OK;
+    }
     CUDA_TRY(cudaStreamSynchronize(c->stream));
     TRY(ensure_host_steps(c, n_fixed + 1 + n_greedy));
     auto launch = [&](size_t live) -> int {

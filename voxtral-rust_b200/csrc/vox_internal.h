@@ -33,12 +33,14 @@ int ctx_model_ready(vox_ctx* c, vox_kv* kv);
 struct StepGraphs {
     cudaGraphExec_t full = nullptr, short_attn = nullptr;
     uint64_t k_full = 0, k_short = 0;
+    const float* adapter = nullptr;  // the ring the graphs read
+    int adapter_cap = 0;
 };
 int capture_adapter_graphs(vox_ctx* c, vox_kv* kv, const float* adapter, int adapter_cap, StepGraphs* g);
 void release_step_graphs(StepGraphs* g);
 
-// n_fixed steps with the given tokens at positions pos0.. (outputs dropped),
-// then n_greedy greedy steps starting from greedy_tok at pos0 + n_fixed, each
+// n_fixed steps with the given tokens at positions pos0.. (outputs dropped;
+// a batched tensor-core prefill when the shape allows and n_fixed >= 2), then n_greedy greedy steps starting from greedy_tok at pos0 + n_fixed, each
 // step's argmax feeding the next; tokens_out[n_greedy] (nullable).  One
 // synchronisation at the end; the cache's host mirror follows the appends.
 int run_step_graphs(vox_ctx* c, vox_kv* kv, const StepGraphs& g, const int32_t* fixed, size_t n_fixed,

@@ -234,6 +234,89 @@ cudaError_t launch_bg_argmax_final(const ArgmaxPart* parts, int n_tiles, StepSta
                                    int32_t* tok_out, cudaStream_t s, bool pdl);
 cudaError_t launch_tile_weights(const uint16_t* src, uint16_t* dst, int rows, int K, cudaStream_t s);
 
+// ---- batched prompt prefill (vox_prefill.cu) ----
+// Prefill operand: per token block (tn tokens) and 64-wide K block one slab of
+// 2 tn rows (bf16 hi rows, then lo rows) x 64 in UMMA canonical K-major layout.
+inline size_t pf_xop_bytes(int t_pad, int K) { return (size_t)t_pad * 2 * K * 2; }
+
+struct PfGemmArgs {
+    const unsigned char* wt;    // weights pre-tiled into 128 x 64 UMMA blocks (launch_tile_weights)
+    const unsigned char* xop;   // prefill operand of the pass
+    float* part;                // [splits, T, rows] K-split partial products
+    int rows, kbt, tiles;       // weight shape: rows, 64-wide K blocks, 128-row tiles
+    int tn, nblocks, T;         // tokens per block (16..128, multiple of 16), blocks, live tokens
+    int splits;                 // K splits (<= kbt)
+    unsigned* err;
+};
+
+struct PfNormArgs {
+    float* h;                   // [T, dim] hidden rows, updated in place
+    const float* part;          // residual mode: [splits, T, dim] partials added to h
+    int splits;
+    const uint16_t* embed;      // embedding mode: rows of the token ids (bf16), h overwritten
+    const int32_t* tokens;      // [T]
+    int vocab;
+    const float* adapter;       // embedding mode, nullable: adapter ring [adapter_cap, dim]
+    int adapter_cap;
+    long long pos0;             // position of token 0 of the pass
+    const float* gain;          // RMSNorm gain of the next linear
+    float eps;
+    unsigned char* xop;         // nullable: prefill operand of the next linear
+    int tn;
+    int T, dim;
+    unsigned* err;
+};
+
+struct PfQkvArgs {
+    const float* part;          // [splits, T, q_dim + 2 kv_dim]
+    int splits, T;
+    int q_dim, kv_dim, head_dim;
+    const float* rope_cos;
+    const float* rope_sin;
+    int max_pos;
+    long long pos0;
+    float* q;                   // [T, q_dim]
+    float* kc;                  // [T, kv_dim] the pass's keys (RoPE applied)
+    float* vc;                  // [T, kv_dim] the pass's values
+    unsigned* err;
+};
+
+struct PfAttnArgs {
+    const float* q;             // [T, n_heads * head_dim]
+    const float* kc;            // [T, n_kv * head_dim]
+    const float* vc;
+    const float* k_ring;        // layer ring [n_kv, cap, head_dim]
+    const float* v_ring;
+    int T, n_heads, n_kv, head_dim, cap;
+    int len0, start0;           // the layer's cache before the pass
+    int win;                    // keys a token sees: min(cache window, attention window)
+    float scale;
+    float* out;                 // [T, n_heads * head_dim]
+};
+
+struct PfCommitArgs {
+    const float* kc;
+    const float* vc;
+    float* k_ring;
+    float* v_ring;
+    int T, kv_dim, head_dim, cap;
+    long long end0;             // (start0 + len0) % cap before the pass
+    KvState* state;
+    KvState final_state;        // state after T single-token appends
+};
+
+size_t pf_gemm_smem_bytes();
+cudaError_t pf_prepare();
+cudaError_t launch_pf_gemm(const PfGemmArgs& a, int grid, cudaStream_t s);
+// Tp = padded tokens (blocks x tn): one CTA each.
+cudaError_t launch_pf_norm(const PfNormArgs& a, int Tp, cudaStream_t s);
+cudaError_t launch_pf_qkv(const PfQkvArgs& a, cudaStream_t s);
+cudaError_t launch_pf_attn(const PfAttnArgs& a, cudaStream_t s);
+cudaError_t launch_pf_split(const float* src, int T, int Tp, int K, unsigned char* xop, int tn, cudaStream_t s);
+cudaError_t launch_pf_swiglu(const float* part, int splits, int T, int Tp, int hidden, unsigned char* xop, int tn,
+                             cudaStream_t s);
+cudaError_t launch_pf_commit(const PfCommitArgs& a, cudaStream_t s);
+
 // ---- launchers (return the launch error) ----
 // Launch shape of a weight-streaming GEMV: consumer warps per CTA (8 or 16,
 // plus one producer warp), CTAs per SM (1 or 2) and shared-memory ring bytes
