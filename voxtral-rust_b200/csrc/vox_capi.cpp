@@ -101,19 +101,23 @@ struct PrefillBufs {
     bool ready = false;
     float *h = nullptr, *q = nullptr, *kc = nullptr, *vc = nullptr, *attn = nullptr, *part = nullptr;
     size_t part_floats = 0;
+    float* ssp = nullptr;        // [kPrefillPass, ceil(dim / 512)] RMSNorm partial sums
+    float* attn_part = nullptr;  // attention chunk partials
+    size_t attn_part_floats = 0;
     unsigned char* xop = nullptr;
     int32_t* tokens = nullptr;    // [kPrefillPass]
     int32_t* h_tokens = nullptr;  // pinned staging
 };
 
 // Launch shape of one prefill GEMM: the K split count that minimises the
-// busiest CTA's K blocks (rounds of items x blocks per item) over
-// tiles x token blocks x splits items, at least 4 K blocks per split, ties to
-// fewer splits (each split writes and rereads a [T, rows] partial).
+// busiest CTA's work over tiles x token blocks x splits items, at least 4 K
+// blocks per split, ties to fewer splits.  An item costs its K blocks (48 KB
+// of operands each) plus its epilogue: a 128-row x tn-token f32 tile written
+// and read back once by the consumer, about 3 K blocks' worth at tn = 128.
 struct PfPlan {
     int rows = 0, K = 0, tiles = 0, kbt = 0, splits = 1, grid = 1;
 };
-PfPlan make_pfplan(int rows, int K, int nblocks, int num_sms) {
+PfPlan make_pfplan(int rows, int K, int nblocks, int tn, int num_sms) {
     PfPlan p;
     p.rows = rows;
     p.K = K;
@@ -125,7 +129,8 @@ PfPlan make_pfplan(int rows, int K, int nblocks, int num_sms) {
         if (s > 1 && p.kbt / s < 4) break;
         const long long items = base * s;
         const long long grid = std::min<long long>(items, num_sms);
-        const long long cost = ((items + grid - 1) / grid) * ((p.kbt + s - 1) / s);
+        const long long epi = (3 * tn + 127) / 128;
+        const long long cost = ((items + grid - 1) / grid) * ((p.kbt + s - 1) / s + epi);
         if (best < 0 || cost < best) {
             best = cost;
             p.splits = s;
@@ -699,30 +704,48 @@ int ensure_prefill(vox_ctx* c) {
     CUDA_TRY(dalloc(&f.attn, T * qd));
     CUDA_TRY(cudaMalloc(&f.xop, pf_xop_bytes((int)T, (int)kmax)));
     CUDA_TRY(dalloc(&f.tokens, T));
+    CUDA_TRY(dalloc(&f.ssp, T * ((dim + 511) / 512)));
     CUDA_TRY(cudaMallocHost(&f.h_tokens, T * sizeof(int32_t)));
     f.ready = true;
     return VOX_OK;
 }
 
-int ensure_prefill_part(vox_ctx* c, size_t floats) {
-    PrefillBufs& f = c->pf;
-    if (floats <= f.part_floats) return VOX_OK;
-    if (f.part) {
+// Grow-only device scratch (the stream is drained before a buffer is replaced).
+int ensure_scratch(vox_ctx* c, float** buf, size_t* have, size_t floats) {
+    if (floats <= *have) return VOX_OK;
+    if (*buf) {
         CUDA_TRY(cudaStreamSynchronize(c->stream));
-        cudaFree(f.part);
-        f.part = nullptr;
-        f.part_floats = 0;
+        cudaFree(*buf);
+        *buf = nullptr;
+        *have = 0;
     }
-    CUDA_TRY(dalloc(&f.part, floats));
-    f.part_floats = floats;
+    CUDA_TRY(dalloc(buf, floats));
+    *have = floats;
     return VOX_OK;
 }
 
-int enqueue_pf_gemm(vox_ctx* c, const PfPlan& p, const unsigned char* wt, int tn, int nblocks, int T) {
+// Hidden rows of the pass (embedding or residual) and their RMSNorm into the
+// prefill operand of the next linear.
+int enqueue_pf_norm(vox_ctx* c, PfNormArgs a) {
+    a.h = c->pf.h;
+    a.ssp = c->pf.ssp;
+    a.ssp_chunks = ((int)c->cfg.dim + 511) / 512;
+    a.dim = (int)c->cfg.dim;
+    a.eps = c->cfg.norm_eps;
+    a.xop = c->pf.xop;
+    a.err = c->err;
+    CUDA_TRY(record_launch(c, launch_pf_resid(a, c->stream)));
+    CUDA_TRY(record_launch(c, launch_pf_norm_xop(a, c->stream)));
+    return VOX_OK;
+}
+
+int enqueue_pf_gemm(vox_ctx* c, const PfPlan& p, const unsigned char* wt, int tn, int nblocks, int T,
+                    float* act = nullptr) {
     PfGemmArgs a{};
     a.wt = wt;
     a.xop = c->pf.xop;
     a.part = c->pf.part;
+    a.act = act;
     a.rows = p.rows;
     a.kbt = p.kbt;
     a.tiles = p.tiles;
@@ -756,13 +779,13 @@ int prefill_batched(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, siz
         const int T = (int)std::min<size_t>(kPrefillPass, n - i0);
         const int tn = T >= 128 ? 128 : (T + 15) / 16 * 16;
         const int nblocks = (T + tn - 1) / tn, Tp = nblocks * tn;
-        const PfPlan pq = make_pfplan(rows_qkv, dim, nblocks, c->num_sms);
-        const PfPlan po = make_pfplan(dim, qd, nblocks, c->num_sms);
-        const PfPlan p13 = make_pfplan(2 * hid, dim, nblocks, c->num_sms);
-        const PfPlan p2 = make_pfplan(dim, hid, nblocks, c->num_sms);
+        const PfPlan pq = make_pfplan(rows_qkv, dim, nblocks, tn, c->num_sms);
+        const PfPlan po = make_pfplan(dim, qd, nblocks, tn, c->num_sms);
+        const PfPlan p13 = make_pfplan(2 * hid, dim, nblocks, tn, c->num_sms);
+        const PfPlan p2 = make_pfplan(dim, hid, nblocks, tn, c->num_sms);
         size_t part = 0;
         for (const PfPlan* p : {&pq, &po, &p13, &p2}) part = std::max(part, (size_t)p->splits * T * p->rows);
-        TRY(ensure_prefill_part(c, part));
+        TRY(ensure_scratch(c, &f.part, &f.part_floats, part));
         // the staging buffer is reused: the previous pass's copy must be done
         CUDA_TRY(cudaStreamSynchronize(c->stream));
         std::memcpy(f.h_tokens, tokens + i0, (size_t)T * sizeof(int32_t));
@@ -771,7 +794,6 @@ int prefill_batched(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, siz
         const long long p0 = (long long)(pos0 + i0);
 
         PfNormArgs na{};
-        na.h = f.h;
         na.embed = c->embed;
         na.tokens = f.tokens;
         na.vocab = (int)c->opt.vocab;
@@ -779,13 +801,10 @@ int prefill_batched(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, siz
         na.adapter_cap = adapter_cap;
         na.pos0 = p0;
         na.gain = c->layers[0].attn_norm;
-        na.eps = g.norm_eps;
-        na.xop = f.xop;
         na.tn = tn;
         na.T = T;
-        na.dim = dim;
-        na.err = c->err;
-        CUDA_TRY(record_launch(c, launch_pf_norm(na, Tp, c->stream)));
+        na.Tp = Tp;
+        TRY(enqueue_pf_norm(c, na));
 
         for (size_t l = 0; l < nl; ++l) {
             const LayerDev& L = c->layers[l];
@@ -815,8 +834,8 @@ int prefill_batched(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, siz
             if (!last) {
                 PfAttnArgs aa{};
                 aa.q = f.q;
-                aa.kc = f.kc;
-                aa.vc = f.vc;
+                aa.kc_in = f.kc;
+                aa.vc_in = f.vc;
                 aa.k_ring = kr;
                 aa.v_ring = vr;
                 aa.T = T;
@@ -827,9 +846,17 @@ int prefill_batched(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, siz
                 aa.len0 = (int)hs.len;
                 aa.start0 = (int)hs.start;
                 aa.win = win;
+                // chunks of >= 128 keys, at most about 8 per 16-token block
+                const int span = std::min((int)hs.len + T, win) + 15;
+                aa.kc = std::max(128, ((span + 7) / 8 + 31) / 32 * 32);
+                aa.cmax = pf_attn_cmax(T, aa.len0, win, aa.kc);
+                TRY(ensure_scratch(c, &f.attn_part, &f.attn_part_floats,
+                                   pf_attn_part_floats(T, aa.n_kv, aa.head_dim, aa.cmax)));
+                aa.part = f.attn_part;
                 aa.scale = 1.0f / sqrtf((float)g.head_dim);
                 aa.out = f.attn;
                 CUDA_TRY(record_launch(c, launch_pf_attn(aa, c->stream)));
+                CUDA_TRY(record_launch(c, launch_pf_attn_merge(aa, c->stream)));
                 CUDA_TRY(record_launch(c, launch_pf_split(f.attn, T, Tp, qd, f.xop, tn, c->stream)));
             }
             // 3) the pass's keys and values into the ring, state after T appends
@@ -853,23 +880,24 @@ int prefill_batched(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, siz
             // 4) o-proj + residual, RMSNorm -> w1|w3 -> SwiGLU -> w2 + residual
             TRY(enqueue_pf_gemm(c, po, L.wo_t, tn, nblocks, T));
             na = PfNormArgs{};
-            na.h = f.h;
             na.part = f.part;
             na.splits = po.splits;
             na.gain = L.ffn_norm;
-            na.eps = g.norm_eps;
-            na.xop = f.xop;
             na.tn = tn;
             na.T = T;
-            na.dim = dim;
-            na.err = c->err;
-            CUDA_TRY(record_launch(c, launch_pf_norm(na, Tp, c->stream)));
-            TRY(enqueue_pf_gemm(c, p13, L.w13_t, tn, nblocks, T));
-            CUDA_TRY(record_launch(c, launch_pf_swiglu(f.part, p13.splits, T, Tp, hid, f.xop, tn, c->stream)));
+            na.Tp = Tp;
+            TRY(enqueue_pf_norm(c, na));
+            if (p13.splits == 1) {  // SwiGLU in the GEMM epilogue, then the w2 operand
+                TRY(enqueue_pf_gemm(c, p13, L.w13_t, tn, nblocks, T, f.part));
+                CUDA_TRY(record_launch(c, launch_pf_split(f.part, T, Tp, hid, f.xop, tn, c->stream)));
+            } else {
+                TRY(enqueue_pf_gemm(c, p13, L.w13_t, tn, nblocks, T));
+                CUDA_TRY(record_launch(c, launch_pf_swiglu(f.part, p13.splits, T, Tp, hid, f.xop, tn, c->stream)));
+            }
             TRY(enqueue_pf_gemm(c, p2, L.w2_t, tn, nblocks, T));
             na.splits = p2.splits;
             na.gain = c->layers[l + 1].attn_norm;
-            CUDA_TRY(record_launch(c, launch_pf_norm(na, Tp, c->stream)));
+            TRY(enqueue_pf_norm(c, na));
         }
     }
     return check_device_errors(c);
@@ -1239,7 +1267,7 @@ void vox_ctx_destroy(vox_ctx* c) {
     }
     {
         PrefillBufs& f = c->pf;
-        void* fp[] = {f.h, f.q, f.kc, f.vc, f.attn, f.part, f.xop, f.tokens};
+        void* fp[] = {f.h, f.q, f.kc, f.vc, f.attn, f.part, f.xop, f.tokens, f.ssp, f.attn_part};
         for (void* p : fp)
             if (p) cudaFree(p);
         if (f.h_tokens) cudaFreeHost(f.h_tokens);

@@ -242,7 +242,8 @@ inline size_t pf_xop_bytes(int t_pad, int K) { return (size_t)t_pad * 2 * K * 2;
 struct PfGemmArgs {
     const unsigned char* wt;    // weights pre-tiled into 128 x 64 UMMA blocks (launch_tile_weights)
     const unsigned char* xop;   // prefill operand of the pass
-    float* part;                // [splits, T, rows] K-split partial products
+    float* part;                // [splits, T, rows] K-split partial products, or
+    float* act;                 // non-null (splits 1, w1|w3 rows interleaved): SiLU(gate) * up [T, rows / 2]
     int rows, kbt, tiles;       // weight shape: rows, 64-wide K blocks, 128-row tiles
     int tn, nblocks, T;         // tokens per block (16..128, multiple of 16), blocks, live tokens
     int splits;                 // K splits (<= kbt)
@@ -251,6 +252,9 @@ struct PfGemmArgs {
 
 struct PfNormArgs {
     float* h;                   // [T, dim] hidden rows, updated in place
+    float* ssp;                 // [T, ssp_chunks] sums of squares per 512-element chunk
+    int ssp_chunks;             // ceil(dim / 512)
+    int Tp;                     // padded tokens (operand rows)
     const float* part;          // residual mode: [splits, T, dim] partials added to h
     int splits;
     const uint16_t* embed;      // embedding mode: rows of the token ids (bf16), h overwritten
@@ -283,13 +287,15 @@ struct PfQkvArgs {
 
 struct PfAttnArgs {
     const float* q;             // [T, n_heads * head_dim]
-    const float* kc;            // [T, n_kv * head_dim]
-    const float* vc;
+    const float* kc_in;         // [T, n_kv * head_dim] the pass's keys
+    const float* vc_in;
     const float* k_ring;        // layer ring [n_kv, cap, head_dim]
     const float* v_ring;
     int T, n_heads, n_kv, head_dim, cap;
     int len0, start0;           // the layer's cache before the pass
     int win;                    // keys a token sees: min(cache window, attention window)
+    int kc, cmax;               // keys per chunk (multiple of 32), most chunks of any 16-token block
+    float* part;                // chunk partials, pf_attn_part_floats
     float scale;
     float* out;                 // [T, n_heads * head_dim]
 };
@@ -308,10 +314,16 @@ struct PfCommitArgs {
 size_t pf_gemm_smem_bytes();
 cudaError_t pf_prepare();
 cudaError_t launch_pf_gemm(const PfGemmArgs& a, int grid, cudaStream_t s);
-// Tp = padded tokens (blocks x tn): one CTA each.
-cudaError_t launch_pf_norm(const PfNormArgs& a, int Tp, cudaStream_t s);
+// The hidden rows (embedding + adapter, or residual + split sums) and their
+// sums of squares; then RMSNorm x gain into the operand (Tp = padded tokens,
+// blocks x tn, a multiple of 16).
+cudaError_t launch_pf_resid(const PfNormArgs& a, cudaStream_t s);
+cudaError_t launch_pf_norm_xop(const PfNormArgs& a, cudaStream_t s);
 cudaError_t launch_pf_qkv(const PfQkvArgs& a, cudaStream_t s);
+int pf_attn_cmax(int T, int len0, int win, int kc);
+size_t pf_attn_part_floats(int T, int n_kv, int head_dim, int cmax);
 cudaError_t launch_pf_attn(const PfAttnArgs& a, cudaStream_t s);
+cudaError_t launch_pf_attn_merge(const PfAttnArgs& a, cudaStream_t s);
 cudaError_t launch_pf_split(const float* src, int T, int Tp, int K, unsigned char* xop, int tn, cudaStream_t s);
 cudaError_t launch_pf_swiglu(const float* part, int splits, int T, int Tp, int hidden, unsigned char* xop, int tn,
                              cudaStream_t s);

@@ -172,16 +172,36 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
             tmem_fence_after();
             const int r = it.tile * 128 + row;
             const bool live = r < A.rows;
-            float* out = A.part + (size_t)it.ks * A.T * A.rows + r;
             const int t0 = it.nb * A.tn;
             const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * 256);
-            for (int c = 0; c < A.tn; c += 16) {
-                uint32_t hi[16], lo[16];
-                tmem_ld16x2(taddr + (uint32_t)c, taddr + (uint32_t)(A.tn + c), hi, lo);
+            if (A.act) {
+                // rows 2j (gate) and 2j + 1 (up) sit in adjacent lanes: SiLU(gate) * up
+                // (math.rs:4-9, decoder.rs:147-150) straight to act[t, j]
+                float* out = A.act + (r >> 1);
+                const int hidden = A.rows >> 1;
+                for (int c = 0; c < A.tn; c += 16) {
+                    uint32_t hi[16], lo[16];
+                    tmem_ld16x2(taddr + (uint32_t)c, taddr + (uint32_t)(A.tn + c), hi, lo);
 #pragma unroll
-                for (int u = 0; u < 16; ++u) {
-                    const int t = t0 + c + u;
-                    if (live && t < A.T) out[(size_t)t * A.rows] = __uint_as_float(hi[u]) + __uint_as_float(lo[u]);
+                    for (int u = 0; u < 16; ++u) {
+                        const int t = t0 + c + u;
+                        const float y = __uint_as_float(hi[u]) + __uint_as_float(lo[u]);
+                        const float up = __shfl_xor_sync(kFull, y, 1);
+                        if (live && !(lane & 1) && t < A.T)
+                            out[(size_t)t * hidden] = __fmul_rn(__fdiv_rn(y, __fadd_rn(1.0f, expf(-y))), up);
+                    }
+                }
+            } else {
+                float* out = A.part + (size_t)it.ks * A.T * A.rows + r;
+                for (int c = 0; c < A.tn; c += 16) {
+                    uint32_t hi[16], lo[16];
+                    tmem_ld16x2(taddr + (uint32_t)c, taddr + (uint32_t)(A.tn + c), hi, lo);
+#pragma unroll
+                    for (int u = 0; u < 16; ++u) {
+                        const int t = t0 + c + u;
+                        if (live && t < A.T)
+                            out[(size_t)t * A.rows] = __uint_as_float(hi[u]) + __uint_as_float(lo[u]);
+                    }
                 }
             }
             tmem_fence_before();
@@ -227,67 +247,100 @@ __device__ __forceinline__ float pf_sum(const float* part, int splits, int T, in
     return y;
 }
 
-// One CTA per token of the padded pass.  The hidden row h[t] becomes either
-// the embedding row of the token (plus the adapter row at its position), or
-// h[t] + (the GEMM's split sum) (decoder.rs:138-139, 151-152); then RMSNorm
-// (math.rs:17-25) times the gain goes into the prefill operand.  Padding
-// tokens (t >= T) write zero rows.
-__global__ void __launch_bounds__(256) pf_norm_kernel(const __grid_constant__ PfNormArgs A) {
-    __shared__ float red[8];
-    const int t = blockIdx.x, tid = threadIdx.x;
-    const bool live = t < A.T;
+// Operand tiles: 32 tokens x 64 elements staged in shared memory, read from
+// row-major f32 rows (consecutive threads on consecutive elements of a row)
+// and written to the prefill operand with eight consecutive threads on eight
+// consecutive tokens of one 8-element chunk (one 128-byte core-matrix row
+// group for hi, one for lo).  Grid (K / 64, ceil(Tp / 32)), 256 threads.
+constexpr int kPfTT = 32;
+
+__device__ __forceinline__ void pf_tile_store(const float (*tile)[65], int t0, int Tp, int k0, int kbt,
+                                              unsigned char* xop, int tn) {
+    const int c = threadIdx.x >> 5, tok = threadIdx.x & 31, t = t0 + tok;
+    if (t >= Tp) return;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = tile[tok][c * 8 + j];
+    pf_store8(xop, tn, kbt, t, k0 + c * 8, v);
+}
+
+// h[t] becomes either the embedding row of the token (plus the adapter row at
+// its position), or h[t] + (the GEMM's split sum) (decoder.rs:138-139,
+// 151-152); per 512-element chunk of the row its sum of squares goes to
+// ssp[t, chunk] (the next RMSNorm's, summed in chunk order).  Grid
+// (ceil(dim / 512), T), 128 threads, four elements each.
+__global__ void __launch_bounds__(128) pf_resid_kernel(const __grid_constant__ PfNormArgs A) {
+    __shared__ float red[4];
+    const int t = blockIdx.y, e = blockIdx.x * 512 + threadIdx.x * 4;
     float ss = 0.0f;
-    if (live) {
-        float* h = A.h + (size_t)t * A.dim;
+    if (e < A.dim) {
+        float* h = A.h + (size_t)t * A.dim + e;
+        float v[4];
         if (A.embed) {
             int tok = A.tokens[t];
             if (tok < 0 || tok >= A.vocab) {
-                if (tid == 0) raise_error(A.err, ERR_TOKEN_RANGE);
+                if (threadIdx.x == 0) raise_error(A.err, ERR_TOKEN_RANGE);
                 tok = 0;
             }
-            const uint16_t* er = A.embed + (size_t)tok * A.dim;
-            const float* ad = A.adapter ? A.adapter + (size_t)((A.pos0 + t) % A.adapter_cap) * A.dim : nullptr;
-            for (int e = tid; e < A.dim; e += 256) {
-                float v = bf16_bits_to_f32(er[e]);
-                if (ad) v = __fadd_rn(ad[e], v);
-                h[e] = v;
-                ss += __fmul_rn(v, v);
+            const uint2 w = *reinterpret_cast<const uint2*>(A.embed + (size_t)tok * A.dim + e);
+            v[0] = bf16_lo(w.x); v[1] = bf16_hi(w.x); v[2] = bf16_lo(w.y); v[3] = bf16_hi(w.y);
+            if (A.adapter) {
+                const float4 a = *reinterpret_cast<const float4*>(
+                    A.adapter + (size_t)((A.pos0 + t) % A.adapter_cap) * A.dim + e);
+                v[0] = __fadd_rn(a.x, v[0]); v[1] = __fadd_rn(a.y, v[1]);
+                v[2] = __fadd_rn(a.z, v[2]); v[3] = __fadd_rn(a.w, v[3]);
             }
         } else {
-            for (int e = tid; e < A.dim; e += 256) {
-                const float v = __fadd_rn(h[e], pf_sum(A.part, A.splits, A.T, A.dim, t, e));
-                h[e] = v;
-                ss += __fmul_rn(v, v);
+            const float4 x = *reinterpret_cast<const float4*>(h);
+            float4 p = *reinterpret_cast<const float4*>(A.part + (size_t)t * A.dim + e);
+            for (int s = 1; s < A.splits; ++s) {
+                const float4 q = *reinterpret_cast<const float4*>(A.part + ((size_t)s * A.T + t) * A.dim + e);
+                p.x += q.x; p.y += q.y; p.z += q.z; p.w += q.w;
             }
+            v[0] = __fadd_rn(x.x, p.x); v[1] = __fadd_rn(x.y, p.y);
+            v[2] = __fadd_rn(x.z, p.z); v[3] = __fadd_rn(x.w, p.w);
         }
+        *reinterpret_cast<float4*>(h) = make_float4(v[0], v[1], v[2], v[3]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ss += __fmul_rn(v[j], v[j]);
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
-    if ((tid & 31) == 0) red[tid >> 5] = ss;
-    __syncthreads();  // also orders this block's h writes before the reads below
-    if (!A.xop) return;
-    float tot = 0.0f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) tot += red[w];
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)A.dim), A.eps)));
-    const float* h = A.h + (size_t)t * A.dim;
-    for (int k8 = tid; k8 < A.dim / 8; k8 += 256) {
-        float v[8];
-        if (live) {
-            const float4 a = *reinterpret_cast<const float4*>(h + k8 * 8);
-            const float4 b = *reinterpret_cast<const float4*>(h + k8 * 8 + 4);
-            const float4 g0 = __ldg(reinterpret_cast<const float4*>(A.gain + k8 * 8));
-            const float4 g1 = __ldg(reinterpret_cast<const float4*>(A.gain + k8 * 8 + 4));
-            const float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-            const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(__fmul_rn(x[j], inv), g[j]);  // math.rs:23-24 order
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = 0.0f;
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0)
+        A.ssp[(size_t)t * A.ssp_chunks + blockIdx.x] = ((red[0] + red[1]) + red[2]) + red[3];
+}
+
+// RMSNorm (math.rs:17-25: inv = 1 / sqrt(sum / dim + eps), then x * inv * w)
+// of the rows pf_resid_kernel wrote, into the prefill operand of the next
+// linear; zero rows for padding tokens.
+__global__ void __launch_bounds__(256) pf_norm_xop_kernel(const __grid_constant__ PfNormArgs A) {
+    __shared__ float tile[kPfTT][65];
+    __shared__ float inv_s[kPfTT];
+    const int tid = threadIdx.x, k0 = blockIdx.x * 64, t0 = blockIdx.y * kPfTT;
+    if (tid < kPfTT) {
+        const int t = t0 + tid;
+        float inv = 0.0f;
+        if (t < A.T) {
+            float ss = 0.0f;
+            for (int c = 0; c < A.ssp_chunks; ++c) ss += A.ssp[(size_t)t * A.ssp_chunks + c];
+            inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)A.dim), A.eps)));
         }
-        pf_store8(A.xop, A.tn, A.dim / 64, t, k8 * 8, v);
+        inv_s[tid] = inv;
     }
+    __syncthreads();
+    const int k = tid & 63;
+    const float g = A.gain[k0 + k];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        const int tok = r * 4 + (tid >> 6), t = t0 + tok;
+        float v = 0.0f;
+        if (t < A.T) v = __fmul_rn(__fmul_rn(A.h[(size_t)t * A.dim + k0 + k], inv_s[tok]), g);
+        tile[tok][k] = v;
+    }
+    __syncthreads();
+    pf_tile_store(tile, t0, A.Tp, k0, A.dim / 64, A.xop, A.tn);
 }
 
 // q|k|v split sums -> RoPE (math.rs:30-65) on q and k at position pos0 + t ->
@@ -323,212 +376,272 @@ __global__ void __launch_bounds__(256) pf_qkv_kernel(const __grid_constant__ PfQ
     }
 }
 
-// Causal attention of a pass (ops.rs:66-132 per token).  Logical key j of the
-// sequence "cache before the pass, then the pass's tokens": j < len0 is ring
-// slot (start0 + j) % cap, j >= len0 is pass token j - len0.  Token t sees
-// keys [len0 + t + 1 - n_t, len0 + t] with n_t = min(len0 + t + 1, win).
-// Grid (ceil(T / 8), n_kv), 4 warps: warp w takes q head w of the kv head's
-// group for 8 tokens; 32-key tiles of K and V staged in shared memory, online
-// softmax.  C = head_dim / 32.
-constexpr int kPfQB = 8, kPfKT = 32;
+// Causal attention of a pass (ops.rs:66-132 per token), split over the keys.
+// Logical key j of the sequence "cache before the pass, then the pass's
+// tokens": j < len0 is ring slot (start0 + j) % cap, j >= len0 is pass token
+// j - len0.  Token t sees keys [len0 + t + 1 - n_t, len0 + t] with n_t =
+// min(len0 + t + 1, win).  A block of 16 tokens covers the union of its
+// tokens' ranges, cut into chunks of `kc` keys; CTA (block * cmax + chunk, kv
+// head) runs one chunk (CTAs past their block's last chunk exit at once)
+// with 8 warps: warp w takes q head w % 4 of the group for tokens
+// 8 * (w / 4) .. + 7.  32-key tiles of K and V move into shared memory with
+// cp.async, double-buffered; online softmax; the chunk's (o, m, l) per token
+// and head go to `part` and pf_attn_merge_kernel combines the chunks in order.
+// C = head_dim / 32.
+constexpr int kPfQB = 16, kPfKT = 32, kPfAttnThreads = 256;
+
+__device__ __forceinline__ void cp_async16(float* dst, const float* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__host__ __device__ constexpr int pf_attn_smem_floats(int hd) {
+    return 2 * 2 * kPfKT * (hd + 4) + 4 * kPfQB * hd + 8 * 8 * kPfKT;
+}
+
+// First and last logical key of token t of the pass.
+__device__ __forceinline__ int pf_first_key(const PfAttnArgs& A, int t) {
+    const int hi = A.len0 + t;
+    return hi + 1 - min(hi + 1, A.win);
+}
+
+// Partial record of (block, chunk, kv head, head in group, token in block):
+// o[head_dim] (unnormalised), m, l.
+__device__ __forceinline__ float* pf_attn_rec(const PfAttnArgs& A, int qb, int c, int hk, int g, int q) {
+    const size_t idx = ((((size_t)qb * A.cmax + c) * A.n_kv + hk) * 4 + g) * kPfQB + q;
+    return A.part + idx * (size_t)(A.head_dim + 2);
+}
 
 template <int C>
-__global__ void __launch_bounds__(128) pf_attn_kernel(const __grid_constant__ PfAttnArgs A) {
+__global__ void __launch_bounds__(kPfAttnThreads) pf_attn_kernel(const __grid_constant__ PfAttnArgs A) {
     extern __shared__ __align__(16) float sm[];
     constexpr int HD = 32 * C, KS = HD + 4;  // padded key rows: conflict-free float4 reads
-    float* Ks = sm;                          // [32][KS]
-    float* Vs = Ks + kPfKT * KS;             // [32][KS]
-    float* Qs = Vs + kPfKT * KS;             // [4][8][HD]
-    float* Ps = Qs + 4 * kPfQB * HD;         // [4][8][32]
+    float* Kst = sm;                         // [2][32][KS]
+    float* Vst = Kst + 2 * kPfKT * KS;       // [2][32][KS]
+    float* Qs = Vst + 2 * kPfKT * KS;        // [4][16][HD]
+    float* Ps = Qs + 4 * kPfQB * HD;         // [8][8][32]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int hk = blockIdx.y, G = A.n_heads / A.n_kv;
-    const int t0 = blockIdx.x * kPfQB, nq = min(kPfQB, A.T - t0);
+    const int qblk = blockIdx.x / A.cmax, chunk = blockIdx.x % A.cmax;
+    const int g = warp & 3, qb = (warp >> 2) * 8;  // q head in the group, first token of the warp
+    const int t0 = qblk * kPfQB, nq = min(kPfQB, A.T - t0);
     const int qd = A.n_heads * HD, kvd = A.n_kv * HD;
-    const bool active = warp < G;
-    const int h = hk * G + warp;  // this warp's q head
+    const int b_lo = pf_first_key(A, t0), b_hi = A.len0 + t0 + nq - 1;
+    const int j_lo = b_lo + chunk * A.kc;
+    if (j_lo > b_hi) return;  // this block has fewer chunks (uniform across the CTA)
+    const int j_hi = min(b_hi, j_lo + A.kc - 1);
+    const bool active = g < G && qb < nq;
 
-    // the queries of the group's heads for these tokens (ops.rs scales the dot)
-    for (int e = tid; e < 4 * kPfQB * HD; e += 128) {
+    for (int e = tid; e < 4 * kPfQB * HD; e += kPfAttnThreads) {
         const int w = e / (kPfQB * HD), qi = (e / HD) % kPfQB, d = e % HD;
         Qs[e] = (w < G && qi < nq) ? A.q[(size_t)(t0 + qi) * qd + (size_t)(hk * G + w) * HD + d] : 0.0f;
     }
-    auto first_key = [&](int t) {
-        const int hi = A.len0 + t;
-        const int cnt = min(hi + 1, A.win);
-        return hi + 1 - cnt;
-    };
-    const int j_lo = first_key(t0), j_hi = A.len0 + t0 + nq - 1;
+    const int n_tiles = (j_hi - j_lo) / kPfKT + 1;
+    const float* kr = A.k_ring + (size_t)hk * A.cap * HD;
+    const float* vr = A.v_ring + (size_t)hk * A.cap * HD;
 
-    float o[kPfQB][C], m[kPfQB], l[kPfQB];
+    auto issue = [&](int tile) {
+        const int j0 = j_lo + tile * kPfKT;
+        float* ks = Kst + (tile & 1) * kPfKT * KS;
+        float* vs = Vst + (tile & 1) * kPfKT * KS;
+        for (int e = tid; e < kPfKT * (HD / 4); e += kPfAttnThreads) {
+            const int kk = e / (HD / 4), d4 = (e - kk * (HD / 4)) * 4;
+            const int j = j0 + kk;
+            const float *ksrc = A.kc_in, *vsrc = A.vc_in;  // any valid address when j is past the range
+            if (j <= j_hi) {
+                if (j < A.len0) {
+                    const size_t slot = (size_t)((A.start0 + j) % A.cap);
+                    ksrc = kr + slot * HD + d4;
+                    vsrc = vr + slot * HD + d4;
+                } else {
+                    ksrc = A.kc_in + (size_t)(j - A.len0) * kvd + (size_t)hk * HD + d4;
+                    vsrc = A.vc_in + (size_t)(j - A.len0) * kvd + (size_t)hk * HD + d4;
+                }
+            }
+            cp_async16(ks + kk * KS + d4, ksrc, j <= j_hi);
+            cp_async16(vs + kk * KS + d4, vsrc, j <= j_hi);
+        }
+        cp_async_commit();
+    };
+
+    float o[8][C], m[8], l[8];
 #pragma unroll
-    for (int qi = 0; qi < kPfQB; ++qi) {
+    for (int qi = 0; qi < 8; ++qi) {
         m[qi] = -INFINITY;
         l[qi] = 0.0f;
 #pragma unroll
         for (int c = 0; c < C; ++c) o[qi][c] = 0.0f;
     }
-    const float* kr = A.k_ring + (size_t)hk * A.cap * HD;
-    const float* vr = A.v_ring + (size_t)hk * A.cap * HD;
-    float* P = Ps + warp * kPfQB * 32;
+    float* P = Ps + warp * 8 * kPfKT;
+    const float* q = Qs + (g * kPfQB + qb) * HD;
 
-    for (int j0 = j_lo; j0 <= j_hi; j0 += kPfKT) {
-        __syncthreads();  // previous tile fully consumed (and Qs written, first time)
-        for (int e = tid; e < kPfKT * (HD / 4); e += 128) {
-            const int kk = e / (HD / 4), d4 = (e - kk * (HD / 4)) * 4;
-            const int j = j0 + kk;
-            float4 kv4 = make_float4(0.f, 0.f, 0.f, 0.f), vv4 = kv4;
-            if (j <= j_hi) {
-                const float *ks, *vs;
-                if (j < A.len0) {
-                    const size_t slot = (size_t)((A.start0 + j) % A.cap);
-                    ks = kr + slot * HD;
-                    vs = vr + slot * HD;
-                } else {
-                    ks = A.kc + (size_t)(j - A.len0) * kvd + (size_t)hk * HD;
-                    vs = A.vc + (size_t)(j - A.len0) * kvd + (size_t)hk * HD;
-                }
-                kv4 = *reinterpret_cast<const float4*>(ks + d4);
-                vv4 = *reinterpret_cast<const float4*>(vs + d4);
-            }
-            *reinterpret_cast<float4*>(Ks + kk * KS + d4) = kv4;
-            *reinterpret_cast<float4*>(Vs + kk * KS + d4) = vv4;
+    issue(0);
+    for (int tile = 0; tile < n_tiles; ++tile) {
+        if (tile + 1 < n_tiles) {
+            issue(tile + 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
-        __syncthreads();
-        if (!active) continue;
-        // scores of key j0 + lane for the 8 tokens
-        const float* q = Qs + warp * kPfQB * HD;
-        float s[kPfQB];
+        __syncthreads();  // this tile (and the queries) visible to every warp
+        if (active) {
+            const float* krow = Kst + (tile & 1) * kPfKT * KS + lane * KS;
+            const float* vs = Vst + (tile & 1) * kPfKT * KS;
+            float s[8];
 #pragma unroll
-        for (int qi = 0; qi < kPfQB; ++qi) s[qi] = 0.0f;
-        const float* krow = Ks + lane * KS;
+            for (int qi = 0; qi < 8; ++qi) s[qi] = 0.0f;
 #pragma unroll 4
-        for (int d = 0; d < HD; d += 4) {
-            const float4 k4 = *reinterpret_cast<const float4*>(krow + d);
+            for (int d = 0; d < HD; d += 4) {
+                const float4 k4 = *reinterpret_cast<const float4*>(krow + d);
 #pragma unroll
-            for (int qi = 0; qi < kPfQB; ++qi) {
-                const float4 q4 = *reinterpret_cast<const float4*>(q + qi * HD + d);
-                s[qi] = fmaf(q4.x, k4.x, s[qi]);
-                s[qi] = fmaf(q4.y, k4.y, s[qi]);
-                s[qi] = fmaf(q4.z, k4.z, s[qi]);
-                s[qi] = fmaf(q4.w, k4.w, s[qi]);
-            }
-        }
-        const int j = j0 + lane;
-#pragma unroll
-        for (int qi = 0; qi < kPfQB; ++qi) {
-            const int t = t0 + qi;
-            const bool ok = qi < nq && j >= first_key(t) && j <= A.len0 + t;
-            float sc = ok ? s[qi] * A.scale : -INFINITY;
-            float mt = sc;
-#pragma unroll
-            for (int off = 16; off; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(kFull, mt, off));
-            const float mn = fmaxf(m[qi], mt);
-            float p = 0.0f, corr = 1.0f;
-            if (mn != -INFINITY) {
-                p = ok ? expf(sc - mn) : 0.0f;
-                corr = m[qi] == -INFINITY ? 0.0f : expf(m[qi] - mn);
-            }
-            float ps = p;
-#pragma unroll
-            for (int off = 16; off; off >>= 1) ps += __shfl_xor_sync(kFull, ps, off);
-            l[qi] = l[qi] * corr + ps;
-            m[qi] = mn;
-#pragma unroll
-            for (int c = 0; c < C; ++c) o[qi][c] *= corr;
-            P[qi * 32 + lane] = p;
-        }
-        __syncwarp();
-#pragma unroll 4
-        for (int kk = 0; kk < kPfKT; kk += 4) {
-            float v[4][C];
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-#pragma unroll
-                for (int c = 0; c < C; ++c) v[u][c] = Vs[(kk + u) * KS + lane + 32 * c];
-#pragma unroll
-            for (int qi = 0; qi < kPfQB; ++qi) {
-                const float4 p4 = *reinterpret_cast<const float4*>(P + qi * 32 + kk);
-#pragma unroll
-                for (int c = 0; c < C; ++c) {
-                    o[qi][c] = fmaf(p4.x, v[0][c], o[qi][c]);
-                    o[qi][c] = fmaf(p4.y, v[1][c], o[qi][c]);
-                    o[qi][c] = fmaf(p4.z, v[2][c], o[qi][c]);
-                    o[qi][c] = fmaf(p4.w, v[3][c], o[qi][c]);
+                for (int qi = 0; qi < 8; ++qi) {
+                    const float4 q4 = *reinterpret_cast<const float4*>(q + qi * HD + d);
+                    s[qi] = fmaf(q4.x, k4.x, s[qi]);
+                    s[qi] = fmaf(q4.y, k4.y, s[qi]);
+                    s[qi] = fmaf(q4.z, k4.z, s[qi]);
+                    s[qi] = fmaf(q4.w, k4.w, s[qi]);
                 }
             }
+            const int j = j_lo + tile * kPfKT + lane;
+#pragma unroll
+            for (int qi = 0; qi < 8; ++qi) {
+                const int t = t0 + qb + qi;
+                const bool ok = qb + qi < nq && j <= j_hi && j >= pf_first_key(A, t) && j <= A.len0 + t;
+                const float sc = ok ? s[qi] * A.scale : -INFINITY;
+                float mt = sc;
+#pragma unroll
+                for (int off = 16; off; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(kFull, mt, off));
+                const float mn = fmaxf(m[qi], mt);
+                float p = 0.0f, corr = 1.0f;
+                if (mn != -INFINITY) {
+                    p = ok ? expf(sc - mn) : 0.0f;
+                    corr = m[qi] == -INFINITY ? 0.0f : expf(m[qi] - mn);
+                }
+                float ps = p;
+#pragma unroll
+                for (int off = 16; off; off >>= 1) ps += __shfl_xor_sync(kFull, ps, off);
+                l[qi] = l[qi] * corr + ps;
+                m[qi] = mn;
+#pragma unroll
+                for (int c = 0; c < C; ++c) o[qi][c] *= corr;
+                P[qi * kPfKT + lane] = p;
+            }
+            __syncwarp();
+#pragma unroll 2
+            for (int kk = 0; kk < kPfKT; kk += 4) {
+                float v[4][C];
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+#pragma unroll
+                    for (int c = 0; c < C; ++c) v[u][c] = vs[(kk + u) * KS + lane + 32 * c];
+#pragma unroll
+                for (int qi = 0; qi < 8; ++qi) {
+                    const float4 p4 = *reinterpret_cast<const float4*>(P + qi * kPfKT + kk);
+#pragma unroll
+                    for (int c = 0; c < C; ++c) {
+                        o[qi][c] = fmaf(p4.x, v[0][c], o[qi][c]);
+                        o[qi][c] = fmaf(p4.y, v[1][c], o[qi][c]);
+                        o[qi][c] = fmaf(p4.z, v[2][c], o[qi][c]);
+                        o[qi][c] = fmaf(p4.w, v[3][c], o[qi][c]);
+                    }
+                }
+            }
+            __syncwarp();
         }
-        __syncwarp();
+        __syncthreads();  // every warp done with this stage before the next issue rewrites it
     }
     if (!active) return;
 #pragma unroll
-    for (int qi = 0; qi < kPfQB; ++qi) {
-        if (qi >= nq) break;
-        float* dst = A.out + (size_t)(t0 + qi) * qd + (size_t)h * HD;
-        const float inv = l[qi] > 0.0f ? 1.0f / l[qi] : 0.0f;
+    for (int qi = 0; qi < 8; ++qi) {
+        if (qb + qi >= nq) break;
+        float* rec = pf_attn_rec(A, qblk, chunk, hk, g, qb + qi);
 #pragma unroll
-        for (int c = 0; c < C; ++c) dst[lane + 32 * c] = o[qi][c] * inv;
+        for (int c = 0; c < C; ++c) rec[lane + 32 * c] = o[qi][c];
+        if (lane == 0) {
+            rec[HD] = m[qi];
+            rec[HD + 1] = l[qi];
+        }
     }
 }
 
-// f32 rows [T, K] -> prefill operand (zero rows for padding tokens).  One
-// thread per (token, 8 elements).
+// out[t, head] = (sum_c o_c e^(m_c - M)) / (sum_c l_c e^(m_c - M)) over the
+// chunks of the token's block in chunk order (M = max m_c).  Grid (T, n_kv),
+// one warp per head of the group, C = head_dim / 32 elements per lane.
+template <int C>
+__global__ void __launch_bounds__(128) pf_attn_merge_kernel(const __grid_constant__ PfAttnArgs A) {
+    constexpr int HD = 32 * C;
+    const int t = blockIdx.x, hk = blockIdx.y, g = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = A.n_heads / A.n_kv;
+    if (g >= G) return;
+    const int qblk = t / kPfQB, q = t % kPfQB, t0 = qblk * kPfQB, nq = min(kPfQB, A.T - t0);
+    const int b_lo = pf_first_key(A, t0), b_hi = A.len0 + t0 + nq - 1;
+    const int nch = (b_hi - b_lo) / A.kc + 1;
+    float M = -INFINITY;
+    for (int c = 0; c < nch; ++c) M = fmaxf(M, pf_attn_rec(A, qblk, c, hk, g, q)[HD]);
+    float L = 0.0f, acc[C];
+#pragma unroll
+    for (int i = 0; i < C; ++i) acc[i] = 0.0f;
+    for (int c = 0; c < nch; ++c) {
+        const float* rec = pf_attn_rec(A, qblk, c, hk, g, q);
+        const float mc = rec[HD];
+        if (mc == -INFINITY) continue;  // no key of this chunk is visible to the token
+        const float w = expf(mc - M);
+        L += rec[HD + 1] * w;
+#pragma unroll
+        for (int i = 0; i < C; ++i) acc[i] = fmaf(rec[lane + 32 * i], w, acc[i]);
+    }
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+    float* out = A.out + (size_t)t * A.n_heads * HD + (size_t)(hk * G + g) * HD;
+#pragma unroll
+    for (int i = 0; i < C; ++i) out[lane + 32 * i] = acc[i] * inv;
+}
+
+// f32 rows [T, K] -> prefill operand (zero rows for padding tokens), through
+// a shared-memory tile (see pf_tile_store).
 __global__ void __launch_bounds__(256) pf_split_kernel(const float* __restrict__ src, int T, int Tp, int K,
                                                        unsigned char* xop, int tn) {
-    const int k8s = K / 8;
-    const long long total = (long long)Tp * k8s;
-    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
-         e += (long long)gridDim.x * blockDim.x) {
-        const int t = (int)(e / k8s), k = 8 * (int)(e - (long long)t * k8s);
-        float v[8];
-        if (t < T) {
-            const float4 a = *reinterpret_cast<const float4*>(src + (size_t)t * K + k);
-            const float4 b = *reinterpret_cast<const float4*>(src + (size_t)t * K + k + 4);
-            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-            v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-        } else {
+    __shared__ float tile[kPfTT][65];
+    const int tid = threadIdx.x, k0 = blockIdx.x * 64, t0 = blockIdx.y * kPfTT, k = tid & 63;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = 0.0f;
-        }
-        pf_store8(xop, tn, K / 64, t, k, v);
+    for (int r = 0; r < 8; ++r) {
+        const int tok = r * 4 + (tid >> 6), t = t0 + tok;
+        tile[tok][k] = t < T ? src[(size_t)t * K + k0 + k] : 0.0f;
     }
+    __syncthreads();
+    pf_tile_store(tile, t0, Tp, k0, K / 64, xop, tn);
 }
 
 // w1|w3 split sums (row 2j = gate j, row 2j + 1 = up j) -> SiLU(gate) * up
-// (math.rs:4-9, decoder.rs:147-150) -> prefill operand of w2.
+// (math.rs:4-9, decoder.rs:147-150) -> prefill operand of w2, through a
+// shared-memory tile (see pf_tile_store).
 __global__ void __launch_bounds__(256) pf_swiglu_kernel(const float* __restrict__ part, int splits, int T, int Tp,
                                                         int hidden, unsigned char* xop, int tn) {
-    const int j8s = hidden / 8, rows = 2 * hidden;
-    const long long total = (long long)Tp * j8s;
-    for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
-         e += (long long)gridDim.x * blockDim.x) {
-        const int t = (int)(e / j8s), j0 = 8 * (int)(e - (long long)t * j8s);
-        float v[8];
+    __shared__ float tile[kPfTT][65];
+    const int tid = threadIdx.x, j0 = blockIdx.x * 64, t0 = blockIdx.y * kPfTT, jj = tid & 63;
+    const int rows = 2 * hidden;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+        const int tok = r * 4 + (tid >> 6), t = t0 + tok;
+        float v = 0.0f;
         if (t < T) {
-            float y[16];
-#pragma unroll
-            for (int u = 0; u < 16; u += 4) {
-                const float4 a = *reinterpret_cast<const float4*>(part + (size_t)t * rows + 2 * j0 + u);
-                y[u] = a.x; y[u + 1] = a.y; y[u + 2] = a.z; y[u + 3] = a.w;
-            }
+            float2 y = *reinterpret_cast<const float2*>(part + (size_t)t * rows + 2 * (j0 + jj));
             for (int s = 1; s < splits; ++s) {
-                const float* p = part + ((size_t)s * T + t) * rows + 2 * j0;
-#pragma unroll
-                for (int u = 0; u < 16; u += 4) {
-                    const float4 a = *reinterpret_cast<const float4*>(p + u);
-                    y[u] += a.x; y[u + 1] += a.y; y[u + 2] += a.z; y[u + 3] += a.w;
-                }
+                const float2 q = *reinterpret_cast<const float2*>(part + ((size_t)s * T + t) * rows + 2 * (j0 + jj));
+                y.x += q.x;
+                y.y += q.y;
             }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float g = y[2 * j], up = y[2 * j + 1];
-                v[j] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), up);
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = 0.0f;
+            v = __fmul_rn(__fdiv_rn(y.x, __fadd_rn(1.0f, expf(-y.x))), y.y);
         }
-        pf_store8(xop, tn, hidden / 64, t, j0, v);
+        tile[tok][jj] = v;
     }
+    __syncthreads();
+    pf_tile_store(tile, t0, Tp, j0, hidden / 64, xop, tn);
 }
 
 // The pass's keys and values into the ring at the slots T single-token
@@ -565,7 +678,7 @@ size_t pf_gemm_smem_bytes() { return (size_t)kPfStages * kPfStageBytes + (2 * kP
 cudaError_t pf_prepare() {
     cudaError_t e = cudaFuncSetAttribute(pf_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)pf_gemm_smem_bytes());
-    const auto attn_smem = [](int hd) { return (2 * kPfKT * (hd + 4) + 4 * kPfQB * hd + 4 * kPfQB * 32) * 4; };
+    const auto attn_smem = [](int hd) { return pf_attn_smem_floats(hd) * 4; };
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(pf_attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem(32));
     if (e == cudaSuccess)
@@ -578,15 +691,23 @@ cudaError_t pf_prepare() {
 }
 
 cudaError_t launch_pf_gemm(const PfGemmArgs& a, int grid, cudaStream_t s) {
-    if (a.tn < 16 || a.tn > 128 || a.tn % 16 || a.splits < 1 || a.splits > a.kbt || grid < 1)
+    if (a.tn < 16 || a.tn > 128 || a.tn % 16 || a.splits < 1 || a.splits > a.kbt || grid < 1 ||
+        (a.act && (a.splits != 1 || a.rows % 2)))
         return cudaErrorInvalidValue;
     pf_gemm_kernel<<<grid, kPfThreads, pf_gemm_smem_bytes(), s>>>(a);
     return cudaGetLastError();
 }
 
-cudaError_t launch_pf_norm(const PfNormArgs& a, int Tp, cudaStream_t s) {
-    if (a.dim % 64 || (a.xop && a.tn % 16) || (a.embed && !a.tokens)) return cudaErrorInvalidValue;
-    pf_norm_kernel<<<Tp, 256, 0, s>>>(a);
+cudaError_t launch_pf_resid(const PfNormArgs& a, cudaStream_t s) {
+    if (a.dim % 64 || !a.ssp || a.ssp_chunks != (a.dim + 511) / 512 || (a.embed && !a.tokens))
+        return cudaErrorInvalidValue;
+    pf_resid_kernel<<<dim3(a.ssp_chunks, a.T), 128, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_pf_norm_xop(const PfNormArgs& a, cudaStream_t s) {
+    if (a.dim % 64 || a.tn % 16 || a.Tp % 16 || !a.xop || !a.ssp) return cudaErrorInvalidValue;
+    pf_norm_xop_kernel<<<dim3(a.dim / 64, (a.Tp + kPfTT - 1) / kPfTT), 256, 0, s>>>(a);
     return cudaGetLastError();
 }
 
@@ -597,33 +718,62 @@ cudaError_t launch_pf_qkv(const PfQkvArgs& a, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+int pf_attn_cmax(int T, int len0, int win, int kc) {
+    int worst = 0;
+    for (int t0 = 0; t0 < T; t0 += kPfQB) {
+        const int nq = T - t0 < kPfQB ? T - t0 : kPfQB;
+        const int hi0 = len0 + t0, lo = hi0 + 1 - (hi0 + 1 < win ? hi0 + 1 : win);
+        const int n = (len0 + t0 + nq - 1 - lo) / kc + 1;
+        worst = n > worst ? n : worst;
+    }
+    return worst;
+}
+
+size_t pf_attn_part_floats(int T, int n_kv, int head_dim, int cmax) {
+    return (size_t)((T + kPfQB - 1) / kPfQB) * cmax * n_kv * 4 * kPfQB * (head_dim + 2);
+}
+
 cudaError_t launch_pf_attn(const PfAttnArgs& a, cudaStream_t s) {
     const int G = a.n_kv > 0 ? a.n_heads / a.n_kv : 0;
-    if (G < 1 || G > 4 || a.n_heads % a.n_kv || a.win < 1) return cudaErrorInvalidValue;
+    if (G < 1 || G > 4 || a.n_heads % a.n_kv || a.win < 1 || a.kc < kPfKT || a.kc % kPfKT || a.cmax < 1 ||
+        !a.part)
+        return cudaErrorInvalidValue;
     const int C = a.head_dim / 32;
     if (a.head_dim % 32 || (C != 1 && C != 2 && C != 4 && C != 8)) return cudaErrorInvalidValue;
-    const dim3 grid((a.T + kPfQB - 1) / kPfQB, a.n_kv);
-    const size_t smem = (size_t)(2 * kPfKT * (a.head_dim + 4) + 4 * kPfQB * a.head_dim + 4 * kPfQB * 32) * 4;
+    const dim3 grid((unsigned)(((a.T + kPfQB - 1) / kPfQB) * a.cmax), a.n_kv);
+    const size_t smem = (size_t)pf_attn_smem_floats(a.head_dim) * 4;
     switch (C) {
-        case 1: pf_attn_kernel<1><<<grid, 128, smem, s>>>(a); break;
-        case 2: pf_attn_kernel<2><<<grid, 128, smem, s>>>(a); break;
-        case 4: pf_attn_kernel<4><<<grid, 128, smem, s>>>(a); break;
-        default: pf_attn_kernel<8><<<grid, 128, smem, s>>>(a); break;
+        case 1: pf_attn_kernel<1><<<grid, kPfAttnThreads, smem, s>>>(a); break;
+        case 2: pf_attn_kernel<2><<<grid, kPfAttnThreads, smem, s>>>(a); break;
+        case 4: pf_attn_kernel<4><<<grid, kPfAttnThreads, smem, s>>>(a); break;
+        default: pf_attn_kernel<8><<<grid, kPfAttnThreads, smem, s>>>(a); break;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_pf_attn_merge(const PfAttnArgs& a, cudaStream_t s) {
+    const dim3 grid(a.T, a.n_kv);
+    switch (a.head_dim / 32) {
+        case 1: pf_attn_merge_kernel<1><<<grid, 128, 0, s>>>(a); break;
+        case 2: pf_attn_merge_kernel<2><<<grid, 128, 0, s>>>(a); break;
+        case 4: pf_attn_merge_kernel<4><<<grid, 128, 0, s>>>(a); break;
+        case 8: pf_attn_merge_kernel<8><<<grid, 128, 0, s>>>(a); break;
+        default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
 }
 
 cudaError_t launch_pf_split(const float* src, int T, int Tp, int K, unsigned char* xop, int tn, cudaStream_t s) {
-    if (K % 64 || tn % 16) return cudaErrorInvalidValue;
-    pf_split_kernel<<<grid_for((long long)Tp * (K / 8), 256), 256, 0, s>>>(src, T, Tp, K, xop, tn);
+    if (K % 64 || tn % 16 || Tp % 16) return cudaErrorInvalidValue;
+    pf_split_kernel<<<dim3(K / 64, (Tp + kPfTT - 1) / kPfTT), 256, 0, s>>>(src, T, Tp, K, xop, tn);
     return cudaGetLastError();
 }
 
 cudaError_t launch_pf_swiglu(const float* part, int splits, int T, int Tp, int hidden, unsigned char* xop, int tn,
                              cudaStream_t s) {
-    if (hidden % 64 || tn % 16) return cudaErrorInvalidValue;
-    pf_swiglu_kernel<<<grid_for((long long)Tp * (hidden / 8), 256), 256, 0, s>>>(part, splits, T, Tp, hidden, xop,
-                                                                                 tn);
+    if (hidden % 64 || tn % 16 || Tp % 16) return cudaErrorInvalidValue;
+    pf_swiglu_kernel<<<dim3(hidden / 64, (Tp + kPfTT - 1) / kPfTT), 256, 0, s>>>(part, splits, T, Tp, hidden,
+                                                                                 xop, tn);
     return cudaGetLastError();
 }
 
