@@ -11,7 +11,9 @@ chunks; --which step runs whole token steps of a full-width model with `--layers
 layers and the 131072-token vocabulary; --which batch runs multi-stream steps
 of `--streams` streams (contexts uniform in [256, 4096)); --which
 bo|bw13|bw2|bhead|bqkv times one multi-stream tensor-core GEMM, --which
-bchain the o-proj, w1|w3, w2, q|k|v chain as one launch.
+bchain the o-proj, w1|w3, w2, q|k|v chain as one launch; --which prefill
+runs `--steps` prefills of `--context` tokens into an empty cache of a
+full-width model with `--layers` layers (vocabulary 131072).
 """
 from __future__ import annotations
 
@@ -28,7 +30,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--which", default="w13",
                     choices=["o", "w13", "w2", "head", "step", "batch", "bo", "bw13", "bw2", "bhead", "bqkv",
-                             "bchain", "encoder"])
+                             "bchain", "encoder", "prefill"])
     ap.add_argument("--seconds", type=float, default=2.0)
     ap.add_argument("--streams", type=int, default=8)
     ap.add_argument("--layers", type=int, default=2)
@@ -64,7 +66,7 @@ def main():
     cfg = V.DecoderConfig(dim=3072, hidden_dim=9216, n_heads=32, n_kv_heads=8, head_dim=128,
                           sliding_window=8192, norm_eps=1e-5, rope_theta=1e6)
     batched = args.which.startswith("b")
-    vocab = 131072 if args.which in ("head", "step") or batched else 0
+    vocab = 131072 if args.which in ("head", "step", "prefill") or batched else 0
     with V.Context(cfg, n_layers=args.layers, vocab=vocab, step_mode=args.mode) as ctx:
         ctx.init_random(0, 0.02)
         if args.which == "step":
@@ -79,6 +81,20 @@ def main():
             ctx.record_event(1)
             ms = ctx.elapsed_ms(0, 1) / args.steps
             print(f"step: {ms * 1e3:.1f} us per token ({args.layers} layers + LM head)")
+            return
+        if args.which == "prefill":
+            kv = V.RollingKvCache(ctx, args.layers, 8, 128, 8192)
+            ids = [(7919 * i) % vocab for i in range(args.context)]
+            best = None
+            for _ in range(args.steps):
+                kv.reset()
+                ctx.synchronize()
+                ctx.record_event(0)
+                ctx.model_prefill(kv, ids, 0)
+                ctx.record_event(1)
+                ms = ctx.elapsed_ms(0, 1)
+                best = ms if best is None else min(best, ms)
+            print(f"prefill: {args.context} tokens through {args.layers} layers in {best:.3f} ms")
             return
         if args.which == "batch":
             import numpy as np
