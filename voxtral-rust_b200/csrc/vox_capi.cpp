@@ -1344,7 +1344,7 @@ int vox_ctx_create(const vox_decoder_config* cfg, const vox_ctx_options* opt, vo
     // Launch plans.
     const int dimi = (int)dim, hidi = (int)hid;
     c->p_qkv = plan_gemv((int)c->qkv_rows, dimi, 2, wsize, c->num_sms, 1, kGemvPaired);
-    c->p_o = plan_gemv(dimi, (int)c->q_dim, 1, wsize, c->num_sms, 1, kGemvPaired);
+    c->p_o = plan_gemv(dimi, (int)c->q_dim, 1, wsize, c->num_sms, 1, kGemvLean);
     c->p_w13 = plan_gemv(2 * hidi, dimi, 2, wsize, c->num_sms, 1, kGemvPaired);
     c->p_w2 = plan_gemv(dimi, hidi, 1, wsize, c->num_sms, 1, kGemvPaired);
     if (o.vocab) c->p_head = plan_gemv((int)o.vocab, dimi, 1, wsize, c->num_sms, 1, kGemvPaired);

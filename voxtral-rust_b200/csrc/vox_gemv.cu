@@ -77,8 +77,7 @@ __device__ __forceinline__ float swiglu(float g, float u) {
 }
 
 template <typename WT, int CPT, int EPI, int NW>
-__global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
-    gemv_kernel(const GemvPlan P, const GemvArgs A) {
+__device__ __forceinline__ void gemv_body(const GemvPlan& P, const GemvArgs& A) {
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int EPC = Elem<WT>::kPerChunk;
     constexpr int kConsumerWarps = NW;
@@ -494,6 +493,19 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
     }
 }
 
+template <typename WT, int CPT, int EPI, int NW>
+__global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1)
+    gemv_kernel(const GemvPlan P, const GemvArgs A) {
+    gemv_body<WT, CPT, EPI, NW>(P, A);
+}
+
+// 8 consumer warps at <= 80 registers: two such CTAs fit on an SM beside an
+// attention CTA (o-proj streams its weights while attention runs).
+template <typename WT, int CPT, int EPI, int NW>
+__global__ void __maxnreg__(80) gemv_kernel_lean(const GemvPlan P, const GemvArgs A) {
+    gemv_body<WT, CPT, EPI, NW>(P, A);
+}
+
 template <typename WT, int EPI, int NW>
 void* pick_kernel(int cpt) {
     switch (cpt) {
@@ -517,6 +529,19 @@ void* pick_epi(int epi, int cpt) {
         case EPI_SWIGLU: return pick_kernel<WT, EPI_SWIGLU, NW>(cpt);
         case EPI_ARGMAX: return pick_kernel<WT, EPI_ARGMAX, NW>(cpt);
     }
+    return nullptr;
+}
+
+// The lean kernels exist for the launches next to attention: o-proj (after)
+// and q|k|v (before), at most 2 chunks per lane.
+void* pick_lean(int wsize, int epi, int cpt, int nw) {
+    if (wsize != 2 || nw != 8) return nullptr;
+    if (epi == EPI_RESID)
+        return cpt == 1 ? (void*)gemv_kernel_lean<uint16_t, 1, EPI_RESID, 8>
+                        : cpt == 2 ? (void*)gemv_kernel_lean<uint16_t, 2, EPI_RESID, 8> : nullptr;
+    if (epi == EPI_QKV)
+        return cpt == 1 ? (void*)gemv_kernel_lean<uint16_t, 1, EPI_QKV, 8>
+                        : cpt == 2 ? (void*)gemv_kernel_lean<uint16_t, 2, EPI_QKV, 8> : nullptr;
     return nullptr;
 }
 
@@ -556,10 +581,12 @@ GemvPlan plan_gemv(int rows, int K, int unit, int wsize, int num_sms, int n_vec,
     // Fewest segments whose per-lane chunk count stays <= 4 (x slice in
     // registers); otherwise the widest split that fits.
     p.nseg = -1;
+    p.lean = 0;
     for (int nseg = 1; nseg <= 8; nseg *= 2) {
         if (C % nseg) continue;
-        if ((C / nseg + 31) / 32 <= 4) {
+        if ((C / nseg + 31) / 32 <= (shape.lean ? 2 : 4)) {
             p.nseg = nseg;
+            p.lean = shape.lean && wsize == 2 && shape.warps == 8 ? 1 : 0;
             break;
         }
     }
@@ -599,6 +626,12 @@ GemvPlan plan_gemv(int rows, int K, int unit, int wsize, int num_sms, int n_vec,
 }
 
 cudaError_t gemv_prepare(int /*dev*/) {
+    for (int epi : {EPI_RESID, EPI_QKV})
+        for (int c : {1, 2}) {
+            cudaError_t e = cudaFuncSetAttribute(pick_lean(2, epi, c, 8), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 227 * 1024);
+            if (e != cudaSuccess) return e;
+        }
     const int cpts[] = {1, 2, 3, 4, 5, 6, 8};
     for (int ws : {2, 4})
         for (int epi = 0; epi <= EPI_ARGMAX; ++epi)
@@ -615,7 +648,7 @@ cudaError_t gemv_prepare(int /*dev*/) {
 }
 
 cudaError_t launch_gemv(const GemvPlan& p, const GemvArgs& a, int epi, cudaStream_t s, bool pdl) {
-    void* k = pick(p.wsize, epi, p.cpt, p.nw);
+    void* k = p.lean ? pick_lean(p.wsize, epi, p.cpt, p.nw) : pick(p.wsize, epi, p.cpt, p.nw);
     if (!k || p.grid < 1) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.grid, p.n_vec, 1);

@@ -82,6 +82,7 @@ struct GemvPlan {
     int max_rows_cta;       // most rows any CTA owns
     int n_vec;              // independent input vectors (gridDim.y)
     size_t smem;            // dynamic shared memory bytes
+    int lean;               // 1: the <= 80-register kernel (o-proj beside attention)
 };
 
 struct GemvArgs {
@@ -337,15 +338,22 @@ cudaError_t launch_pf_commit(const PfCommitArgs& a, cudaStream_t s);
 // with a 160 KB ring (1.566 vs 1.571 ms per token, w1|w3 alone 5.75 vs 5.68
 // TB/s; 64 KB rings lose): a CTA of the next launch can start streaming on an
 // SM while the other CTA of this launch is still in its tail, and an attention
-// CTA fits beside one GEMV CTA.  Tensor-parallel shards keep the wide shape,
-// whose fewer CTAs mean fewer peer arrivals per exchange.
+// CTA fits beside one GEMV CTA.  The o-proj launch, which follows attention,
+// uses the lean shape: the 80-register kernel with K cut into 8 segments (at
+// most 2 chunks per lane, no spills) and a 72 KB ring, so two o-proj CTAs fit
+// beside a cluster-attention CTA and stream their weights while attention
+// runs (1.559 vs 1.574 ms per token, context 520-776; the same shape for
+// q|k|v, before attention, measured 1.619 vs 1.567).  Tensor-parallel shards
+// keep the wide shape, whose fewer CTAs mean fewer peer arrivals per exchange.
 struct GemvShape {
     int warps;
     int ctas_per_sm;
     size_t ring_bytes;
+    int lean;
 };
-constexpr GemvShape kGemvPaired{8, 2, 80 * 1024};
-constexpr GemvShape kGemvWide{16, 1, 160 * 1024};
+constexpr GemvShape kGemvPaired{8, 2, 80 * 1024, 0};
+constexpr GemvShape kGemvLean{8, 2, 72 * 1024, 1};
+constexpr GemvShape kGemvWide{16, 1, 160 * 1024, 0};
 GemvPlan plan_gemv(int rows, int K, int unit, int wsize, int num_sms, int n_vec, GemvShape shape = kGemvWide);
 bool gemv_supported(int K, int wsize);
 size_t gemv_max_smem();
