@@ -92,6 +92,12 @@ __device__ __forceinline__ void bulk_copy_g2s_nohint(void* dst, const void* src,
                  : "memory");
 }
 
+// Fire-and-forget prefetch of [src, src + bytes) into L2 (16-byte aligned,
+// bytes a multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Programmatic dependent launch (no-ops when launched without the attribute).
 __device__ __forceinline__ void pdl_wait_prior_grids() {
     asm volatile("griddepcontrol.wait;" ::: "memory");

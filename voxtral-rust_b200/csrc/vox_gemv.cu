@@ -141,6 +141,19 @@ __device__ __forceinline__ void gemv_body(const GemvPlan& P, const GemvArgs& A) 
                               Wband + (size_t)s * stage_bytes, bytes, &full_bar[buf], pol);
                 ++issued;
             }
+            if (ok && A.pf_W && (int)blockIdx.x < A.pf_grid) {
+                const int nu = A.pf_rows / A.pf_unit;
+                const int v0 = (int)((long long)nu * blockIdx.x / A.pf_grid);
+                const int v1 = (int)((long long)nu * (blockIdx.x + 1) / A.pf_grid);
+                long long nb = (long long)(v1 - v0) * A.pf_unit * A.pf_row_bytes;
+                if (nb > A.pf_max_bytes) nb = A.pf_max_bytes;
+                const unsigned char* src =
+                    reinterpret_cast<const unsigned char*>(A.pf_W) + (long long)v0 * A.pf_unit * A.pf_row_bytes;
+                for (long long o = 0; o + 16 <= nb; o += 16384) {
+                    const long long n = nb - o < 16384 ? nb - o : 16384;
+                    bulk_prefetch_l2(src + o, (uint32_t)(n & ~15ll));
+                }
+            }
             if (!ok) {
                 // Leave no copy in flight: wait (bounded) for the last issued stages.
                 for (int s = max(0, issued - NS); s < issued; ++s)

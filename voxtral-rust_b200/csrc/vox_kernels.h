@@ -128,6 +128,13 @@ struct GemvArgs {
     int xch_in;                       // >= 0: x = sum over ranks of this rank's slots (xch_in, *)
     unsigned long long xch_arrivals;  // arrivals per step at point xch_in (size x producer grid)
     const unsigned long long* tp_steps;  // steps this rank has completed
+    // Next weight launch (non-null pf_W): once this CTA's producer has issued
+    // its last copy it prefetches into L2 the first pf_max_bytes of the band
+    // the same-index CTA of that launch streams.
+    const void* pf_W;
+    long long pf_row_bytes;
+    int pf_rows, pf_unit, pf_grid;
+    int pf_max_bytes;
 };
 
 struct AttnArgs {
