@@ -471,23 +471,8 @@ GemvArgs base_args(vox_ctx* c) {
     return a;
 }
 
-// L2 prefetch of the next weight launch by each GEMV CTA's producer, bytes per
-// CTA.  The launches of a step stream back to back, and the next launch's CTAs
-// only find room on an SM once this launch's CTAs leave, all at about the same
-// time; bytes prefetched into L2 during the tail keep HBM busy across the
-// boundary.  Measured on the 26-layer step (context 520-776), ms per token:
-// none 1.569, 16 KB 1.546, 24 KB 1.538, 32 KB 1.537, 40 KB 1.542, 48 KB 1.552,
-// 56 KB 1.564, 80 KB 1.588, 160 KB 1.580 (larger prefetches slow the tail of
-// the launch that issues them).
-constexpr int kGemvPrefetchBytes = 32 * 1024;
-
 void set_prefetch(GemvArgs& a, const void* W, const GemvPlan& p, int wsize) {
-    a.pf_W = W;
-    a.pf_row_bytes = (long long)p.K * wsize;
-    a.pf_rows = p.rows;
-    a.pf_unit = p.unit;
-    a.pf_grid = p.grid;
-    a.pf_max_bytes = kGemvPrefetchBytes;
+    gemv_set_prefetch(a, W, p, wsize);
 }
 
 // Enqueue one decoder layer (decoder.rs:88-155) as five kernels.  With

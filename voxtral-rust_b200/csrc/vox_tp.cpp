@@ -274,6 +274,7 @@ int enqueue_layer(vox_tp* t, size_t l, bool short_attn) {
     a.ring_cap = cap;
     a.kv_window = win;
     a.kv_state = st;
+    gemv_set_prefetch(a, L.wo, t->p_o, 2);
     TP_CUDA(launch_gemv(t->p_qkv, a, EPI_QKV, t->stream, true));
 
     AttnArgs at{};
@@ -306,6 +307,7 @@ int enqueue_layer(vox_tp* t, size_t l, bool short_attn) {
     a.kv_window = win;
     a.ring_cap = cap;
     if (t->p2p) a.xch_out = point_after_o(l);
+    gemv_set_prefetch(a, L.w13, t->p_w13, 2);
     TP_CUDA(launch_gemv(t->p_o, a, EPI_RESID, t->stream, true));
     if (!t->p2p)
         TP_NCCL(t->api, t->api->all_reduce(t->hmid, t->hmid, dim, ncclFloat32, ncclSum, t->comm, t->stream));
@@ -321,6 +323,7 @@ int enqueue_layer(vox_tp* t, size_t l, bool short_attn) {
     }
     a.norm_w = L.ffn_norm;
     a.y = t->act;
+    gemv_set_prefetch(a, L.w2, t->p_w2, 2);
     TP_CUDA(launch_gemv(t->p_w13, a, EPI_SWIGLU, t->stream, true));
 
     a = base(t);
@@ -329,6 +332,10 @@ int enqueue_layer(vox_tp* t, size_t l, bool short_attn) {
     a.y = t->hid;
     a.resid = s.rank == 0 ? t->hmid : t->zeros;
     if (t->p2p) a.xch_out = point_after_w2(l);
+    if (l + 1 < t->layers.size())
+        gemv_set_prefetch(a, t->layers[l + 1].wqkv, t->p_qkv, 2);
+    else if (t->head)
+        gemv_set_prefetch(a, t->head, t->p_head, 2);
     TP_CUDA(launch_gemv(t->p_w2, a, EPI_RESID, t->stream, true));
     if (!t->p2p)
         TP_NCCL(t->api, t->api->all_reduce(t->hid, t->hid, dim, ncclFloat32, ncclSum, t->comm, t->stream));
