@@ -350,8 +350,9 @@ cudaError_t launch_pf_commit(const PfCommitArgs& a, cudaStream_t s);
 // most 2 chunks per lane, no spills) and a 72 KB ring, so two o-proj CTAs fit
 // beside a cluster-attention CTA and stream their weights while attention
 // runs (1.559 vs 1.574 ms per token, context 520-776; the same shape for
-// q|k|v, before attention, measured 1.619 vs 1.567).  Tensor-parallel shards
-// keep the wide shape, whose fewer CTAs mean fewer peer arrivals per exchange.
+// q|k|v, before attention, measured 1.619 vs 1.567).  Tensor-parallel o-proj
+// and w2 keep the wide shape, whose fewer CTAs mean fewer peer arrivals per
+// exchange.
 struct GemvShape {
     int warps;
     int ctas_per_sm;

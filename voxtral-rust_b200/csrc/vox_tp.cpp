@@ -600,9 +600,12 @@ int vox_tp_create(const vox_decoder_config* cfg, const vox_ctx_options* opt, int
     CREATE_TRY(cudaStreamCreateWithFlags(&t->stream, cudaStreamNonBlocking));
     for (auto& e : t->ev) CREATE_TRY(cudaEventCreate(&e));
     const int dimi = (int)dim, hidi = (int)sh.hidden;
-    t->p_qkv = plan_gemv((int)(q_l + 2 * kv_l), dimi, 2, 2, t->num_sms, 1);
+    // o-proj and w2 end in the peer exchange: the wide shape (fewer CTAs, fewer
+    // arrivals per exchange); q|k|v and w1|w3 in the paired shape (TP 2:
+    // 1.719 vs 1.752-1.766 ms per token).
+    t->p_qkv = plan_gemv((int)(q_l + 2 * kv_l), dimi, 2, 2, t->num_sms, 1, kGemvPaired);
     t->p_o = plan_gemv(dimi, (int)q_l, 1, 2, t->num_sms, 1);
-    t->p_w13 = plan_gemv(2 * hidi, dimi, 2, 2, t->num_sms, 1);
+    t->p_w13 = plan_gemv(2 * hidi, dimi, 2, 2, t->num_sms, 1, kGemvPaired);
     t->p_w2 = plan_gemv(dimi, hidi, 1, 2, t->num_sms, 1);
     t->p_head = plan_gemv((int)sh.vocab_local, dimi, 1, 2, t->num_sms, 1);
     for (const GemvPlan* p : {&t->p_qkv, &t->p_o, &t->p_w13, &t->p_w2, &t->p_head})
