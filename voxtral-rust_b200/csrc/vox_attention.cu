@@ -42,13 +42,16 @@ constexpr int kMaxSplits = 64;  // merge weights kept in shared memory
 // Most live tokens per kv head for which one stream's attention runs as one
 // thread-block cluster per kv head (attn_cluster_kernel).
 constexpr int kAttnClusterMaxTokens = 3584;
-// Warps of a cluster-attention CTA.  Three warps at 136 registers (13056) fit
-// beside a weight-streaming GEMV CTA (17 warps at 96 registers, 52224; at most
-// 148 KB of shared memory) in one SM's 65536 registers and 228 KB: the GEMV
-// launch before attention (q|k|v) and the one after it (o-proj) then share
-// SMs with the attention CTAs, so attention's prologue overlaps the q|k|v
-// tail and o-proj streams its weights while attention computes.
+// Warps of a cluster-attention CTA and K/V ring stages per warp.  A CTA (4
+// warps at 136 registers, 17408; 2 stages: 64 KB of K/V slots, the 33 KB merge
+// buffer and 8 KB of static state) fits on an SM beside two lean o-proj GEMV
+// CTAs (9 warps at 80 registers and a 48 KB ring each): 63488 registers and
+// about 205 KB of shared memory, so o-proj streams its weights while attention
+// runs.  The second stage lets a warp's first two 8-token groups load before
+// the dependency wait: 1.514 vs 1.537 ms per token at context 520-776, 1.577 vs
+// 1.621 at 1536 (three stages with 32 KB o-proj rings: 1.519 / 1.617).
 constexpr int kClusterWarps = 4;
+constexpr int kClusterStages = 2;
 
 template <int VEC>
 struct VecT;
@@ -867,7 +870,8 @@ __global__ void __maxnreg__(136) attn_cluster_kernel(const AttnArgs A) {
     // [NW][K rows | V rows] slots, then the leader's merge buffer:
     // acc [CS][G][hd] followed by (m, l) [CS][G][2]
     extern __shared__ __align__(128) unsigned char ring_smem[];
-    __shared__ uint64_t wbar[NW][1];
+    constexpr int D = kClusterStages;
+    __shared__ uint64_t wbar[NW][D];
     __shared__ __align__(16) float wacc[NW][G][HD];
     __shared__ float wml[NW][G][2];
     __shared__ int range_s[4];  // t_begin, t_end, ring start, live length
@@ -875,10 +879,10 @@ __global__ void __maxnreg__(136) attn_cluster_kernel(const AttnArgs A) {
     const int hd = A.hd, hd4 = hd / 4, n_out = G * hd4;
     const uint32_t rank = cluster_rank();
     const int h = blockIdx.x / CS;
-    float* macc = reinterpret_cast<float*>(ring_smem + (size_t)NW * 2 * TPG * hd * 4);
+    float* macc = reinterpret_cast<float*>(ring_smem + (size_t)NW * D * 2 * TPG * hd * 4);
     float* mml = macc + (size_t)CS * G * hd;
 
-    if (tid < NW) mbar_init(&wbar[tid][0], 1);
+    if (tid < NW * D) mbar_init(&wbar[tid / D][tid % D], 1);
     if (tid == 0) fence_barrier_init();
     // First cluster phase: every CTA of the cluster has started.  Its wait sits
     // just before the first store into the leader's shared memory, so it costs
@@ -910,19 +914,19 @@ __global__ void __maxnreg__(136) attn_cluster_kernel(const AttnArgs A) {
     // the end of the newest group) is final: a warp whose first group ends
     // before it copies that group now, ahead of the dependency wait.
     int pre = 0;
-    {
-        const int warp = tid >> 5, t0 = range_s[0] + warp * TPG;
+    for (int k = 0; k < D; ++k) {
+        const int warp = tid >> 5, t0 = range_s[0] + (warp + NW * k) * TPG;
         const int ntok = min(TPG, range_s[1] - t0);
-        if (ntok > 0 && (t0 + ntok < range_s[3] || !A.pre_append)) {
+        if (pre == k && ntok > 0 && (t0 + ntok < range_s[3] || !A.pre_append)) {
             if ((tid & 31) == 0)
-                attn_issue_group<G, 1, NW>(A, 0, h, range_s[0], range_s[1], range_s[2], ring_smem, wbar, warp, 0, hd);
-            pre = 1;
+                attn_issue_group<G, D, NW>(A, 0, h, range_s[0], range_s[1], range_s[2], ring_smem, wbar, warp, k, hd);
+            pre = k + 1;
         }
         __syncwarp();
     }
     pdl_wait_prior_grids();
     uint32_t phase = 0;
-    attn_chunk_warps<G, 1, NW>(A, 0, h, range_s[0], range_s[1], range_s[2], ring_smem, wbar, wacc, wml, phase,
+    attn_chunk_warps<G, D, NW>(A, 0, h, range_s[0], range_s[1], range_s[2], ring_smem, wbar, wacc, wml, phase,
                            tid >> 5, tid & 31, hd, pre);
     __syncthreads();
 
@@ -1049,7 +1053,7 @@ cudaError_t attn_prepare(int /*dev*/) {
 
 namespace {
 size_t attn_cluster_smem(int G, int hd, int cs) {
-    return (size_t)kClusterWarps * 2 * (32 / G) * hd * 4 + (size_t)cs * G * (hd + 2) * 4;
+    return (size_t)kClusterWarps * kClusterStages * 2 * (32 / G) * hd * 4 + (size_t)cs * G * (hd + 2) * 4;
 }
 void* attn_cluster_fn(int G, int cs) {
     if (G == 4) return cs == 16 ? (void*)attn_cluster_kernel<4, 16> : (void*)attn_cluster_kernel<4, 8>;

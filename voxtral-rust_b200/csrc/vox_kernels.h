@@ -347,10 +347,11 @@ cudaError_t launch_pf_commit(const PfCommitArgs& a, cudaStream_t s);
 // SM while the other CTA of this launch is still in its tail, and an attention
 // CTA fits beside one GEMV CTA.  The o-proj launch, which follows attention,
 // uses the lean shape: the 80-register kernel with K cut into 8 segments (at
-// most 2 chunks per lane, no spills) and a 72 KB ring, so two o-proj CTAs fit
-// beside a cluster-attention CTA and stream their weights while attention
-// runs (1.559 vs 1.574 ms per token, context 520-776; the same shape for
-// q|k|v, before attention, measured 1.619 vs 1.567).  Tensor-parallel o-proj
+// most 2 chunks per lane, no spills) and a 48 KB ring, so two o-proj CTAs fit
+// beside a cluster-attention CTA with its two-stage K/V ring and stream their
+// weights while attention runs (with a 72 KB ring beside one-stage attention:
+// 1.559 vs 1.574 ms per token, context 520-776; the same shape for q|k|v,
+// before attention, measured 1.619 vs 1.567).  Tensor-parallel o-proj
 // and w2 keep the wide shape, whose fewer CTAs mean fewer peer arrivals per
 // exchange.
 struct GemvShape {
@@ -360,7 +361,7 @@ struct GemvShape {
     int lean;
 };
 constexpr GemvShape kGemvPaired{8, 2, 80 * 1024, 0};
-constexpr GemvShape kGemvLean{8, 2, 72 * 1024, 1};
+constexpr GemvShape kGemvLean{8, 2, 48 * 1024, 1};
 constexpr GemvShape kGemvWide{16, 1, 160 * 1024, 0};
 GemvPlan plan_gemv(int rows, int K, int unit, int wsize, int num_sms, int n_vec, GemvShape shape = kGemvWide);
 bool gemv_supported(int K, int wsize);
