@@ -596,7 +596,7 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnAr
 
     // Work list (same in every CTA): chunks of gpi groups per warp, i.e.
     // NW * gpi * TPG tokens per CTA chunk, at most nsplit chunks per
-    // (stream, kv head), about two chunks per CTA overall.
+    // (stream, kv head), about one (several streams) or two chunks per CTA.
     if (tid == 0) {
         long long total_groups = 0;
         for (int z = 0; z < B; ++z) {
@@ -610,7 +610,9 @@ __global__ void __launch_bounds__(kAttnThreads, 4) attn_warp_kernel(const AttnAr
             plan.items[z] = (len - ms + TPG - 1) / TPG;  // live groups, for now
             total_groups += (long long)plan.items[z] * A.n_kv;
         }
-        const long long slots = 2LL * gridDim.x * NW;
+        // one chunk per warp slot for several streams (8 streams: 2.698 vs 2.738 ms
+        // per step with two), two for a single stream
+        const long long slots = (B > 1 ? 1LL : 2LL) * gridDim.x * NW;
         const int gpi_all = (int)max(1LL, (total_groups + slots - 1) / slots);
         int first = 0;
         for (int z = 0; z < B; ++z) {
