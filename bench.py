@@ -444,6 +444,35 @@ def run_prefill(V, ctx, rank, dist, reps=3):
     return {"ms": min(dev), "wall_ms": min(wall), "steps_ms": steps_ms, "launches": launches, "ring_ok": ok}
 
 
+JOB_DECODE = 1024
+
+
+def run_config1_job(V, ctx, rank, dist):
+    """Config 1 as one job: the 512-id prompt (vox_model_prefill) then 1024 greedy
+    steps (vox_model_generate) into an empty cache, timed on the device and by the
+    host clock around the two calls (host ids in, the 1024 generated ids out)."""
+    kv = V.RollingKvCache(ctx, LAYERS, NKV, HD, WINDOW)
+    prompt = prompt_ids(rank + 53, PROMPT)
+    ctx.model_prefill(kv, prompt, 0)  # warm-up of both graphs and passes
+    ctx.model_generate(kv, int(prompt[-1]), PROMPT, 8)
+    kv.reset()
+    ctx.synchronize()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    ctx.record_event(14)
+    ctx.model_prefill(kv, prompt[:-1], 0)
+    ctx.record_event(15)
+    out = ctx.model_generate(kv, int(prompt[-1]), PROMPT - 1, JOB_DECODE)
+    ctx.record_event(13)
+    ctx.synchronize()
+    wall = (time.perf_counter() - t0) * 1e3
+    pre_ms, total_ms = ctx.elapsed_ms(14, 15), ctx.elapsed_ms(14, 13)
+    ok = all(tuple(kv.device_state(l))[0] == PROMPT - 1 + JOB_DECODE for l in range(LAYERS))
+    kv.close()
+    return {"prefill_ms": pre_ms, "ms": total_ms, "wall_ms": wall, "tokens": int(out.size), "ring_ok": ok}
+
+
 def context_object(run, t_max, world, peak, workload):
     steps = run["steps"]
     mean_ctx = sum(run["context"]) / 2
@@ -640,6 +669,7 @@ def run_ours(args):
     long_run = None if args.ctx_steps == 0 else run_context(V, ctx, args, rank, dist, LONG_CONTEXT, args.ctx_steps)
     roll_run = None if args.ctx_steps == 0 else run_context(V, ctx, args, rank, dist, WINDOW, args.ctx_steps)
     pf_run = None if args.no_prefill else run_prefill(V, ctx, rank, dist)
+    job_run = None if args.no_prefill else run_config1_job(V, ctx, rank, dist)
     ms_run = None if args.ms_steps == 0 else run_multi_stream(V, ctx, args, rank, world, dist)
     enc_run = None if args.no_encoder else run_encoder(V, local)
     tp_run = None
@@ -650,6 +680,9 @@ def run_ours(args):
 
     t_max, e2e_max = ms, e2e_ms
     ms_max = ms_e2e_max = tp_max = long_max = roll_max = enc_max = pf_max = pf_wall_max = pf_steps_max = 0.0
+    job_max = job_wall_max = job_pre_max = 0.0
+    if job_run:
+        job_max, job_wall_max, job_pre_max = job_run["ms"], job_run["wall_ms"], job_run["prefill_ms"]
     if pf_run:
         pf_max, pf_wall_max, pf_steps_max = pf_run["ms"], pf_run["wall_ms"], pf_run["steps_ms"]
     if enc_run:
@@ -663,10 +696,10 @@ def run_ours(args):
     if dist:
         import torch
         t = torch.tensor([ms, e2e_ms, ms_max, ms_e2e_max, tp_max, long_max, roll_max, enc_max, pf_max, pf_wall_max,
-                          pf_steps_max], dtype=torch.float64)
+                          pf_steps_max, job_max, job_wall_max, job_pre_max], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         (t_max, e2e_max, ms_max, ms_e2e_max, tp_max, long_max, roll_max, enc_max, pf_max, pf_wall_max,
-         pf_steps_max) = (float(x) for x in t)
+         pf_steps_max, job_max, job_wall_max, job_pre_max) = (float(x) for x in t)
         if roll_run:
             ok = torch.tensor([1.0 if roll_run["ring_ok"] and long_run["ring_ok"] else 0.0])
             dist.all_reduce(ok, op=dist.ReduceOp.MIN)
@@ -736,6 +769,17 @@ def run_ours(args):
                          "unit": "TFLOP/s", "frac": tflops / tpeak,
                          "flops": flops, "note": "algorithmic FLOPs of the 26 layers' linears (2 per weight per "
                                                  "token); the hi/lo split doubles the tensor-core work"}}
+    if job_run:
+        line["config1_job"] = {
+            "metric": "config 1 job: generated tokens/s (512-id prompt prefilled, then 1024 greedy steps)",
+            "value": JOB_DECODE * world / (job_max / 1e3), "unit": "tokens/s", "ms": job_max,
+            "prefill_ms": job_pre_max, "decode_ms": job_max - job_pre_max,
+            "workload": (f"per GPU: the {PROMPT}-id prompt of config 1 (positions 0..{PROMPT - 2} through "
+                         f"vox_model_prefill, the last id starts the decode) then {JOB_DECODE} greedy steps "
+                         f"(vox_model_generate) from an empty 26-layer cache, window {WINDOW}"),
+            "e2e": {"value": JOB_DECODE * world / (job_wall_max / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 4 * PROMPT, "d2h_bytes_per_step": 4 * JOB_DECODE},
+            "ring_state_ok": job_run["ring_ok"]}
     if enc_run:
         chunks = enc_run["audio_s"] * 16000 // ENC_CHUNK
         line["encoder"] = {
