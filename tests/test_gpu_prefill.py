@@ -147,6 +147,23 @@ def test_prefill_short_prompts_and_one_token(V, oracle):
     run_case(V, oracle, NARROW, 2, 4096, 149, 4, calls=[1, 2, 17, 129])
 
 
+# 4 q heads per kv head at head_dim 128 take the tensor-core attention
+# (32-token blocks, 64-key tiles); the narrow width keeps the oracle fast.
+NARROW_G4 = config_dict(dim=512, hidden_dim=1024, n_heads=4, n_kv_heads=1, head_dim=128, sliding_window=4096,
+                        rope_theta=1e6)
+
+
+@pytest.mark.parametrize("window,cache_window,prompt,calls", [
+    (4096, None, 750, [700, 50]),      # two passes, then a call on the filled cache
+    (64, None, 300, None),             # evictions inside the pass
+    (48, 128, 200, None),              # attention window below the cache window
+    (4096, None, 149, [1, 2, 17, 129]),  # ragged blocks of 2, 17 and 129 tokens
+])
+def test_prefill_tensor_core_attention(V, oracle, window, cache_window, prompt, calls):
+    c = dict(NARROW_G4, sliding_window=window)
+    run_case(V, oracle, c, 2, 4096, prompt, 6, window=cache_window, calls=calls)
+
+
 def test_prefill_matches_token_steps(V):
     """The batched prefill and vox_model_prefill_steps leave the same ring
     state and caches within tolerance (26 layers at full width)."""

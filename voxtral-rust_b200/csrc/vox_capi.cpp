@@ -857,16 +857,21 @@ int prefill_batched(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, siz
                 aa.len0 = (int)hs.len;
                 aa.start0 = (int)hs.start;
                 aa.win = win;
-                // chunks of >= 128 keys, at most about 8 per 16-token block
-                const int span = std::min((int)hs.len + T, win) + 15;
-                aa.kc = std::max(128, ((span + 7) / 8 + 31) / 32 * 32);
-                aa.cmax = pf_attn_cmax(T, aa.len0, win, aa.kc);
+                // tensor-core blocks of 32 tokens (4 q heads per kv head, head_dim
+                // 128), else CUDA-core blocks of 16; chunks of >= 128 keys, at
+                // most about 8 per block
+                const bool tc = pf_attn_tc_supported(aa.n_heads, aa.n_kv, aa.head_dim);
+                aa.qb = tc ? 32 : 16;
+                const int span = std::min((int)hs.len + T, win) + aa.qb - 1, kt = tc ? 64 : 32;
+                aa.kc = std::max(128, ((span + 7) / 8 + kt - 1) / kt * kt);
+                aa.cmax = pf_attn_cmax(T, aa.len0, win, aa.kc, aa.qb);
+                aa.err = c->err;
                 TRY(ensure_scratch(c, &f.attn_part, &f.attn_part_floats,
-                                   pf_attn_part_floats(T, aa.n_kv, aa.head_dim, aa.cmax)));
+                                   pf_attn_part_floats(T, aa.n_kv, aa.head_dim, aa.cmax, aa.qb)));
                 aa.part = f.attn_part;
                 aa.scale = 1.0f / sqrtf((float)g.head_dim);
                 aa.out = f.attn;
-                CUDA_TRY(record_launch(c, launch_pf_attn(aa, c->stream)));
+                CUDA_TRY(record_launch(c, tc ? launch_pf_attn_tc(aa, c->stream) : launch_pf_attn(aa, c->stream)));
                 CUDA_TRY(record_launch(c, launch_pf_attn_merge(aa, c->stream)));
                 CUDA_TRY(record_launch(c, launch_pf_split(f.attn, T, Tp, qd, f.xop, tn, c->stream)));
             }

@@ -302,7 +302,9 @@ struct PfAttnArgs {
     int T, n_heads, n_kv, head_dim, cap;
     int len0, start0;           // the layer's cache before the pass
     int win;                    // keys a token sees: min(cache window, attention window)
-    int kc, cmax;               // keys per chunk (multiple of 32), most chunks of any 16-token block
+    int qb;                     // tokens per block: 16 (CUDA-core kernel) or 32 (tensor-core kernel)
+    int kc, cmax;               // keys per chunk (multiple of 32, or 64 for tensor cores), most chunks of any block
+    unsigned* err;
     float* part;                // chunk partials, pf_attn_part_floats
     float scale;
     float* out;                 // [T, n_heads * head_dim]
@@ -328,8 +330,11 @@ cudaError_t launch_pf_gemm(const PfGemmArgs& a, int grid, cudaStream_t s);
 cudaError_t launch_pf_resid(const PfNormArgs& a, cudaStream_t s);
 cudaError_t launch_pf_norm_xop(const PfNormArgs& a, cudaStream_t s);
 cudaError_t launch_pf_qkv(const PfQkvArgs& a, cudaStream_t s);
-int pf_attn_cmax(int T, int len0, int win, int kc);
-size_t pf_attn_part_floats(int T, int n_kv, int head_dim, int cmax);
+int pf_attn_cmax(int T, int len0, int win, int kc, int qb);
+size_t pf_attn_part_floats(int T, int n_kv, int head_dim, int cmax, int qb);
+// Tensor-core variant (4 q heads per kv head, head_dim 128; qb 32, kc a multiple of 64).
+bool pf_attn_tc_supported(int n_heads, int n_kv, int head_dim);
+cudaError_t launch_pf_attn_tc(const PfAttnArgs& a, cudaStream_t s);
 cudaError_t launch_pf_attn(const PfAttnArgs& a, cudaStream_t s);
 cudaError_t launch_pf_attn_merge(const PfAttnArgs& a, cudaStream_t s);
 cudaError_t launch_pf_split(const float* src, int T, int Tp, int K, unsigned char* xop, int tn, cudaStream_t s);

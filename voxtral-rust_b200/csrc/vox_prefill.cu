@@ -414,7 +414,7 @@ __device__ __forceinline__ int pf_first_key(const PfAttnArgs& A, int t) {
 // Partial record of (block, chunk, kv head, head in group, token in block):
 // o[head_dim] (unnormalised), m, l.
 __device__ __forceinline__ float* pf_attn_rec(const PfAttnArgs& A, int qb, int c, int hk, int g, int q) {
-    const size_t idx = ((((size_t)qb * A.cmax + c) * A.n_kv + hk) * 4 + g) * kPfQB + q;
+    const size_t idx = ((((size_t)qb * A.cmax + c) * A.n_kv + hk) * 4 + g) * A.qb + q;
     return A.part + idx * (size_t)(A.head_dim + 2);
 }
 
@@ -579,7 +579,7 @@ __global__ void __launch_bounds__(128) pf_attn_merge_kernel(const __grid_constan
     const int t = blockIdx.x, hk = blockIdx.y, g = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = A.n_heads / A.n_kv;
     if (g >= G) return;
-    const int qblk = t / kPfQB, q = t % kPfQB, t0 = qblk * kPfQB, nq = min(kPfQB, A.T - t0);
+    const int qblk = t / A.qb, q = t % A.qb, t0 = qblk * A.qb, nq = min(A.qb, A.T - t0);
     const int b_lo = pf_first_key(A, t0), b_hi = A.len0 + t0 + nq - 1;
     const int nch = (b_hi - b_lo) / A.kc + 1;
     float M = -INFINITY;
@@ -600,6 +600,303 @@ __global__ void __launch_bounds__(128) pf_attn_merge_kernel(const __grid_constan
     float* out = A.out + (size_t)t * A.n_heads * HD + (size_t)(hk * G + g) * HD;
 #pragma unroll
     for (int i = 0; i < C; ++i) out[lane + 32 * i] = acc[i] * inv;
+}
+
+// ---- tensor-core attention of a pass (4 q heads per kv head, head_dim 128) ----
+// The same chunks and records as pf_attn_kernel, for blocks of 32 tokens: the
+// 32 tokens x 4 q heads of a CTA are the M = 128 rows of two tcgen05 products
+// per 64-key tile, S = Q K^T (K = head_dim) and O_tile = P V (K = 64 keys).
+// Both operands of each product are f32 values split into bf16 hi and lo
+// parts; hi*hi + hi*lo + lo*hi accumulate in f32 in TMEM (about 16 mantissa
+// bits per operand; the lo*lo term is below f32 rounding).  Row r = g * 32 +
+// tt (q head g of the group, token tt of the block) is TMEM lane r; warps w
+// and w + 4 read lane quarter w % 4, warp w < 4 the first half of the row's
+// columns and warp w + 4 the second.  Per tile they run the online softmax
+// of the reference's attention (ops.rs:66-132, math.rs:67-88, restated
+// incrementally: the row maximum is exchanged through shared memory, each
+// half keeps its own running sum l under the common correction), write P's
+// hi and lo parts for the second product, and add their half of O_tile into
+// registers with the correction.
+//
+// Keys and values arrive as f32 rows through cp.async into one padded
+// staging buffer: the next tile's copies are issued as soon as this tile's
+// rows are converted, so they overlap the two products and the softmax.  P
+// reuses the K operand's space (the S product has finished reading K when the
+// softmax writes P).  Operands in shared memory in the UMMA canonical K-major
+// layout without swizzle (vox_tcgen05.cuh).
+constexpr int kTcQB = 32, kTcKT = 64, kTcThreads = 256, kTcHD = 128;
+constexpr int kTcQBytes = 128 * kTcHD * 2;    // one of Q hi / Q lo (32 KB)
+constexpr int kTcKBytes = kTcKT * kTcHD * 2;  // one of K hi / K lo, later P hi / P lo (16 KB)
+constexpr int kTcVBytes = kTcHD * kTcKT * 2;  // one of V^T hi / lo (16 KB)
+constexpr int kTcFS = kTcHD + 4;              // staging row stride (floats): conflict-free float4 reads
+constexpr int kTcFBytes = 128 * kTcFS * 4;    // 128 Q rows, or 64 K rows + 64 V rows
+constexpr int kTcSmem = 2 * (kTcQBytes + kTcKBytes + kTcVBytes) + kTcFBytes + 2 * 128 * 4 + 64;
+static_assert(kTcKBytes == 128 * kTcKT * 2, "P (128 rows x 64 keys) fits the K operand's space");
+
+// Byte offset of element (row, k) of an operand with `rows` rows (a multiple
+// of 8) in canonical K-major layout: K step k / 16 at rows * 32 bytes each,
+// core matrix ((k / 8) % 2, row / 8), 16 bytes per row, 2 per element.
+__device__ __forceinline__ uint32_t kmaj_off(int row, int k, int rows) {
+    return (uint32_t)((k >> 4) * rows * 32 + ((k >> 3) & 1) * rows * 16 + (row >> 3) * 128 + (row & 7) * 16 +
+                      (k & 7) * 2);
+}
+
+// Eight consecutive elements (k % 8 == 0) of one row as bf16 hi and lo.
+__device__ __forceinline__ void tc_put8(unsigned char* hi_base, unsigned char* lo_base, uint32_t off,
+                                        const float (&v)[8]) {
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+        const uint16_t h0 = f32_to_bf16_bits(v[j]), h1 = f32_to_bf16_bits(v[j + 1]);
+        const uint16_t l0 = f32_to_bf16_bits(v[j] - bf16_bits_to_f32(h0));
+        const uint16_t l1 = f32_to_bf16_bits(v[j + 1] - bf16_bits_to_f32(h1));
+        hi[j >> 1] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+        lo[j >> 1] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+    }
+    *reinterpret_cast<uint4*>(hi_base + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(lo_base + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+}
+
+__device__ __forceinline__ void ld8_shared(const float* src, float (&v)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(src);
+    const float4 b = *reinterpret_cast<const float4*>(src + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) pf_attn_tc_kernel(const __grid_constant__ PfAttnArgs A) {
+    extern __shared__ __align__(1024) unsigned char tsm[];
+    unsigned char* Qh = tsm;
+    unsigned char* Ql = Qh + kTcQBytes;
+    unsigned char* Kh = Ql + kTcQBytes;  // K hi, then P hi
+    unsigned char* Kl = Kh + kTcKBytes;  // K lo, then P lo
+    unsigned char* Vh = Kl + kTcKBytes;
+    unsigned char* Vl = Vh + kTcVBytes;
+    float* F = reinterpret_cast<float*>(Vl + kTcVBytes);  // staging rows, stride kTcFS
+    float* red = F + 128 * kTcFS;                          // [2][128] half-row maxima, then sums
+    uint64_t* bar_s = reinterpret_cast<uint64_t*>(red + 2 * 128);
+    uint64_t* bar_o = bar_s + 1;
+    uint32_t* tmem_s = reinterpret_cast<uint32_t*>(bar_o + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int hk = blockIdx.y;
+    const int qblk = blockIdx.x / A.cmax, chunk = blockIdx.x % A.cmax;
+    const int t0 = qblk * kTcQB, nq = min(kTcQB, A.T - t0);
+    const int qd = A.n_heads * kTcHD, kvd = A.n_kv * kTcHD;
+    const int b_lo = pf_first_key(A, t0), b_hi = A.len0 + t0 + nq - 1;
+    const int j_lo = b_lo + chunk * A.kc;
+    if (j_lo > b_hi) return;  // this block has fewer chunks (uniform across the CTA)
+    const int j_hi = min(b_hi, j_lo + A.kc - 1);
+    const int n_tiles = (j_hi - j_lo) / kTcKT + 1;
+    const float* kr = A.k_ring + (size_t)hk * A.cap * kTcHD;
+    const float* vr = A.v_ring + (size_t)hk * A.cap * kTcHD;
+
+    // f32 rows of one tile into F: keys at rows 0..63, values at 64..127
+    // (rows past j_hi zero-filled); 16 bytes per copy, a warp per row pair
+    auto issue_tile = [&](int j0) {
+#pragma unroll 4
+        for (int e = tid; e < kTcKT * (kTcHD / 4); e += kTcThreads) {
+            const int kk = e >> 5, c4 = (e & 31) * 4, j = j0 + kk;
+            const float *ks = A.kc_in, *vs = A.vc_in;  // any valid address when j is past the range
+            if (j <= j_hi) {
+                if (j < A.len0) {
+                    int slot = A.start0 + j;  // start0 < cap and j < len0 <= cap
+                    if (slot >= A.cap) slot -= A.cap;
+                    ks = kr + (size_t)slot * kTcHD + c4;
+                    vs = vr + (size_t)slot * kTcHD + c4;
+                } else {
+                    ks = A.kc_in + (size_t)(j - A.len0) * kvd + (size_t)hk * kTcHD + c4;
+                    vs = A.vc_in + (size_t)(j - A.len0) * kvd + (size_t)hk * kTcHD + c4;
+                }
+            }
+            cp_async16(F + kk * kTcFS + c4, ks, j <= j_hi);
+            cp_async16(F + (kTcKT + kk) * kTcFS + c4, vs, j <= j_hi);
+        }
+        cp_async_commit();
+    };
+
+    // Q rows (token t0 + tt, q head 4 hk + g) through F
+#pragma unroll 4
+    for (int e = tid; e < 128 * (kTcHD / 4); e += kTcThreads) {
+        const int r = e >> 5, c4 = (e & 31) * 4, tt = r & 31, g = r >> 5;
+        const bool ok = tt < nq;
+        const float* src = ok ? A.q + (size_t)(t0 + tt) * qd + (size_t)(hk * 4 + g) * kTcHD + c4 : A.q;
+        cp_async16(F + r * kTcFS + c4, src, ok);
+    }
+    cp_async_commit();
+    if (tid == 0) {
+        mbar_init(bar_s, 1);
+        mbar_init(bar_o, 1);
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_s)),
+                     "r"(256)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+    // consecutive threads take consecutive rows: conflict-free 16-byte reads
+    // (padded stride) and 16-byte operand stores
+    for (int e = tid; e < 128 * (kTcHD / 8); e += kTcThreads) {
+        const int r = e & 127, d0 = (e >> 7) * 8;
+        float v[8];
+        ld8_shared(F + r * kTcFS + d0, v);
+        tc_put8(Qh, Ql, kmaj_off(r, d0, 128), v);
+    }
+    __syncthreads();  // F free again
+    issue_tile(j_lo);
+    tmem_fence_before();
+    __syncthreads();
+    tmem_fence_after();
+    const uint32_t tmem = *tmem_s;
+    const uint32_t tS = tmem, tO = tmem + 128;  // S: columns 0..63, O_tile: 128..255
+
+    const int q4 = warp & 3, half = warp >> 2;  // TMEM lane quarter, column half
+    const int row = q4 * 32 + lane, tt = lane, g = q4;
+    const int t = t0 + tt;
+    const int kfirst = pf_first_key(A, t), klast = A.len0 + t;
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    float acc[kTcHD / 2];
+#pragma unroll
+    for (int d = 0; d < kTcHD / 2; ++d) acc[d] = 0.0f;
+    float m_run = -INFINITY, l_run = 0.0f;
+    constexpr uint32_t idS = umma_idesc_bf16(128, kTcKT), idO = umma_idesc_bf16(128, kTcHD);
+    uint32_t phase = 0;
+
+    for (int tile = 0; tile < n_tiles; ++tile) {
+        const int j0 = j_lo + tile * kTcKT;
+        cp_async_wait<0>();
+        __syncthreads();  // this tile's rows in F; the previous products read
+        // K rows (B operand, N = 64 keys) and V^T (B operand, N = 128 dims) as hi / lo
+        for (int e = tid; e < kTcKT * (kTcHD / 8); e += kTcThreads) {
+            const int kk = e & 63, d0 = (e >> 6) * 8;
+            float v[8];
+            ld8_shared(F + kk * kTcFS + d0, v);
+            tc_put8(Kh, Kl, kmaj_off(kk, d0, kTcKT), v);
+        }
+        for (int e = tid; e < kTcHD * (kTcKT / 8); e += kTcThreads) {
+            const int d = e & 127, k0 = (e >> 7) * 8;
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = F[(kTcKT + k0 + u) * kTcFS + d];
+            tc_put8(Vh, Vl, kmaj_off(d, k0, kTcHD), v);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
+        tmem_fence_before();
+        __syncthreads();  // operands written, F free
+        tmem_fence_after();
+        if (tile + 1 < n_tiles) issue_tile(j0 + kTcKT);
+        if (tid == 0) {
+            const uint32_t qh = smem_addr(Qh), ql = smem_addr(Ql), kh = smem_addr(Kh), kl = smem_addr(Kl);
+#pragma unroll
+            for (int s = 0; s < kTcHD / 16; ++s) {
+                const uint64_t ah = umma_desc(qh + s * 4096u, 2048u, 128u);
+                const uint64_t al = umma_desc(ql + s * 4096u, 2048u, 128u);
+                const uint64_t bh = umma_desc(kh + s * 2048u, 1024u, 128u);
+                const uint64_t bl = umma_desc(kl + s * 2048u, 1024u, 128u);
+                umma_f16(tS, ah, bh, idS, s > 0 ? 1u : 0u);
+                umma_f16(tS, ah, bl, idS, 1u);
+                umma_f16(tS, al, bh, idS, 1u);
+            }
+            umma_commit(bar_s);
+        }
+        if (!mbar_wait(bar_s, phase) && lane == 0) raise_error(A.err, ERR_FULL_WAIT);
+        tmem_fence_after();
+        // this half's 32 scores of the row, masked and scaled
+        uint32_t sr[32];
+        {
+            uint32_t a[16], b[16];
+            tmem_ld16x2(tS + lane_base + half * 32, tS + lane_base + half * 32 + 16, a, b);
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                sr[u] = a[u];
+                sr[16 + u] = b[u];
+            }
+        }
+        float mt = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+            const int j = j0 + half * 32 + c;
+            const bool ok = tt < nq && j <= j_hi && j >= kfirst && j <= klast;
+            const float sc = ok ? __uint_as_float(sr[c]) * A.scale : -INFINITY;
+            sr[c] = __float_as_uint(sc);
+            mt = fmaxf(mt, sc);
+        }
+        red[half * 128 + row] = mt;
+        __syncthreads();  // maxima exchanged; every S product done, so K's space takes P
+        const float mn = fmaxf(m_run, fmaxf(red[row], red[128 + row]));
+        float ps = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 32; c += 8) {
+            float pv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const float sc = __uint_as_float(sr[c + u]);
+                pv[u] = (mn == -INFINITY || sc == -INFINITY) ? 0.0f : expf(sc - mn);
+                ps += pv[u];
+            }
+            tc_put8(Kh, Kl, kmaj_off(row, half * 32 + c, 128), pv);
+        }
+        const float corr = mn == -INFINITY ? 1.0f : (m_run == -INFINITY ? 0.0f : expf(m_run - mn));
+        l_run = l_run * corr + ps;
+        m_run = mn;
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        tmem_fence_before();
+        __syncthreads();  // P written, the scores and the maxima read
+        tmem_fence_after();
+        if (tid == 0) {
+            const uint32_t ph = smem_addr(Kh), pl = smem_addr(Kl), vh = smem_addr(Vh), vl = smem_addr(Vl);
+#pragma unroll
+            for (int s = 0; s < kTcKT / 16; ++s) {
+                const uint64_t ah = umma_desc(ph + s * 4096u, 2048u, 128u);
+                const uint64_t al = umma_desc(pl + s * 4096u, 2048u, 128u);
+                const uint64_t bh = umma_desc(vh + s * 4096u, 2048u, 128u);
+                const uint64_t bl = umma_desc(vl + s * 4096u, 2048u, 128u);
+                umma_f16(tO, ah, bh, idO, s > 0 ? 1u : 0u);
+                umma_f16(tO, ah, bl, idO, 1u);
+                umma_f16(tO, al, bh, idO, 1u);
+            }
+            umma_commit(bar_o);
+        }
+        if (!mbar_wait(bar_o, phase) && lane == 0) raise_error(A.err, ERR_FULL_WAIT);
+        tmem_fence_after();
+#pragma unroll
+        for (int c = 0; c < kTcHD / 2; c += 32) {
+            uint32_t a[16], b[16];
+            const uint32_t ta = tO + lane_base + half * 64 + c;
+            tmem_ld16x2(ta, ta + 16, a, b);
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                acc[c + u] = fmaf(acc[c + u], corr, __uint_as_float(a[u]));
+                acc[c + 16 + u] = fmaf(acc[c + 16 + u], corr, __uint_as_float(b[u]));
+            }
+        }
+        phase ^= 1u;
+        tmem_fence_before();
+    }
+    // the two halves' sums under the same corrections add to the row's l
+    __syncthreads();
+    red[half * 128 + row] = l_run;
+    __syncthreads();
+    if (tt < nq) {
+        float* rec = pf_attn_rec(A, qblk, chunk, hk, g, tt);
+        // records are head_dim + 2 floats: 8-byte, not 16-byte, aligned
+#pragma unroll
+        for (int d = 0; d < kTcHD / 2; d += 2)
+            *reinterpret_cast<float2*>(rec + half * 64 + d) = make_float2(acc[d], acc[d + 1]);
+        if (half == 0) {
+            rec[kTcHD] = m_run;
+            rec[kTcHD + 1] = red[row] + red[128 + row];
+        }
+    }
+    tmem_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tmem_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256) : "memory");
+    }
 }
 
 // f32 rows [T, K] -> prefill operand (zero rows for padding tokens), through
@@ -687,6 +984,8 @@ cudaError_t pf_prepare() {
         e = cudaFuncSetAttribute(pf_attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem(128));
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(pf_attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem(256));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(pf_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
     return e;
 }
 
@@ -718,10 +1017,10 @@ cudaError_t launch_pf_qkv(const PfQkvArgs& a, cudaStream_t s) {
     return cudaGetLastError();
 }
 
-int pf_attn_cmax(int T, int len0, int win, int kc) {
+int pf_attn_cmax(int T, int len0, int win, int kc, int qb) {
     int worst = 0;
-    for (int t0 = 0; t0 < T; t0 += kPfQB) {
-        const int nq = T - t0 < kPfQB ? T - t0 : kPfQB;
+    for (int t0 = 0; t0 < T; t0 += qb) {
+        const int nq = T - t0 < qb ? T - t0 : qb;
         const int hi0 = len0 + t0, lo = hi0 + 1 - (hi0 + 1 < win ? hi0 + 1 : win);
         const int n = (len0 + t0 + nq - 1 - lo) / kc + 1;
         worst = n > worst ? n : worst;
@@ -729,14 +1028,14 @@ int pf_attn_cmax(int T, int len0, int win, int kc) {
     return worst;
 }
 
-size_t pf_attn_part_floats(int T, int n_kv, int head_dim, int cmax) {
-    return (size_t)((T + kPfQB - 1) / kPfQB) * cmax * n_kv * 4 * kPfQB * (head_dim + 2);
+size_t pf_attn_part_floats(int T, int n_kv, int head_dim, int cmax, int qb) {
+    return (size_t)((T + qb - 1) / qb) * cmax * n_kv * 4 * qb * (head_dim + 2);
 }
 
 cudaError_t launch_pf_attn(const PfAttnArgs& a, cudaStream_t s) {
     const int G = a.n_kv > 0 ? a.n_heads / a.n_kv : 0;
     if (G < 1 || G > 4 || a.n_heads % a.n_kv || a.win < 1 || a.kc < kPfKT || a.kc % kPfKT || a.cmax < 1 ||
-        !a.part)
+        !a.part || a.qb != kPfQB)
         return cudaErrorInvalidValue;
     const int C = a.head_dim / 32;
     if (a.head_dim % 32 || (C != 1 && C != 2 && C != 4 && C != 8)) return cudaErrorInvalidValue;
@@ -751,7 +1050,21 @@ cudaError_t launch_pf_attn(const PfAttnArgs& a, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+bool pf_attn_tc_supported(int n_heads, int n_kv, int head_dim) {
+    return n_kv > 0 && n_heads == 4 * n_kv && head_dim == kTcHD;
+}
+
+cudaError_t launch_pf_attn_tc(const PfAttnArgs& a, cudaStream_t s) {
+    if (!pf_attn_tc_supported(a.n_heads, a.n_kv, a.head_dim) || a.win < 1 || a.kc < kTcKT || a.kc % kTcKT ||
+        a.cmax < 1 || !a.part || a.qb != kTcQB)
+        return cudaErrorInvalidValue;
+    const dim3 grid((unsigned)(((a.T + kTcQB - 1) / kTcQB) * a.cmax), a.n_kv);
+    pf_attn_tc_kernel<<<grid, kTcThreads, kTcSmem, s>>>(a);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_pf_attn_merge(const PfAttnArgs& a, cudaStream_t s) {
+    if (a.qb < 1) return cudaErrorInvalidValue;
     const dim3 grid(a.T, a.n_kv);
     switch (a.head_dim / 32) {
         case 1: pf_attn_merge_kernel<1><<<grid, 128, 0, s>>>(a); break;
