@@ -858,12 +858,17 @@ int prefill_batched(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, siz
                 aa.start0 = (int)hs.start;
                 aa.win = win;
                 // tensor-core blocks of 32 tokens (4 q heads per kv head, head_dim
-                // 128), else CUDA-core blocks of 16; chunks of >= 128 keys, at
-                // most about 8 per block
+                // 128), else CUDA-core blocks of 16; chunks of >= 128 keys.  The
+                // tensor-core kernel takes one chunk per block when the blocks x kv
+                // heads fill 3/4 of the SMs (at 512-token passes 1-5 % faster than
+                // 2, 3, 4 or 6 chunks per block, or fixed 128-192 keys), else enough
+                // chunks to cover the SMs (at most 8); the CUDA-core kernel about 8.
                 const bool tc = pf_attn_tc_supported(aa.n_heads, aa.n_kv, aa.head_dim);
                 aa.qb = tc ? 32 : 16;
                 const int span = std::min((int)hs.len + T, win) + aa.qb - 1, kt = tc ? 64 : 32;
-                aa.kc = std::max(128, ((span + 7) / 8 + kt - 1) / kt * kt);
+                const int units = (T + aa.qb - 1) / aa.qb * aa.n_kv, sms = c->num_sms;
+                const int per = !tc ? 8 : 4 * units >= 3 * sms ? 1 : std::min(8, (sms + units - 1) / units);
+                aa.kc = std::max(128, ((span + per - 1) / per + kt - 1) / kt * kt);
                 aa.cmax = pf_attn_cmax(T, aa.len0, win, aa.kc, aa.qb);
                 aa.err = c->err;
                 TRY(ensure_scratch(c, &f.attn_part, &f.attn_part_floats,
@@ -872,7 +877,8 @@ int prefill_batched(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, siz
                 aa.scale = 1.0f / sqrtf((float)g.head_dim);
                 aa.out = f.attn;
                 CUDA_TRY(record_launch(c, tc ? launch_pf_attn_tc(aa, c->stream) : launch_pf_attn(aa, c->stream)));
-                CUDA_TRY(record_launch(c, launch_pf_attn_merge(aa, c->stream)));
+                // a single chunk per block leaves normalised rows (tensor-core kernel)
+                if (!tc || aa.cmax > 1) CUDA_TRY(record_launch(c, launch_pf_attn_merge(aa, c->stream)));
                 CUDA_TRY(record_launch(c, launch_pf_split(f.attn, T, Tp, qd, f.xop, tn, c->stream)));
             }
             // 3) the pass's keys and values into the ring, state after T appends

@@ -151,6 +151,16 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {  // round to nea
     return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
 }
 
+// v0, v1 as packed bf16 hi parts, hi = bf16(v) rounded to nearest even (the
+// same bits as f32_to_bf16_bits for finite v, in one cvt.rn.bf16x2
+// instruction), and lo parts, lo = bf16(v - hi) (the subtraction is exact);
+// v0 in the low half of each word.
+__device__ __forceinline__ void split_bf16x2(float v0, float v1, uint32_t& hi, uint32_t& lo) {
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(v1), "f"(v0));
+    const float h0 = __uint_as_float(hi << 16), h1 = __uint_as_float(hi & 0xFFFF0000u);
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(__fsub_rn(v1, h1)), "f"(__fsub_rn(v0, h0)));
+}
+
 // Element k of stream b into an X operand in XOP layout (vox_kernels.h):
 // v as bf16 hi = bf16(v) and lo = bf16(v - hi).
 __device__ __forceinline__ void xop_store(unsigned char* xop, int k, int b, float v) {

@@ -228,13 +228,7 @@ __device__ __forceinline__ void pf_store8(unsigned char* xop, int tn, int kbt, i
     unsigned char* base = xop + ((size_t)nb * kbt + kb) * (size_t)n * 128 + (size_t)s * n * 32 + (size_t)k2 * n * 16;
     uint32_t hi[4], lo[4];
 #pragma unroll
-    for (int j = 0; j < 8; j += 2) {
-        const uint16_t h0 = f32_to_bf16_bits(v[j]), h1 = f32_to_bf16_bits(v[j + 1]);
-        const uint16_t l0 = f32_to_bf16_bits(v[j] - bf16_bits_to_f32(h0));
-        const uint16_t l1 = f32_to_bf16_bits(v[j + 1] - bf16_bits_to_f32(h1));
-        hi[j >> 1] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-        lo[j >> 1] = (uint32_t)l0 | ((uint32_t)l1 << 16);
-    }
+    for (int j = 0; j < 8; j += 2) split_bf16x2(v[j], v[j + 1], hi[j >> 1], lo[j >> 1]);
     const int lr = tn + tt;
     *reinterpret_cast<uint4*>(base + (tt >> 3) * 128 + (tt & 7) * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
     *reinterpret_cast<uint4*>(base + (lr >> 3) * 128 + (lr & 7) * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
@@ -616,14 +610,19 @@ __global__ void __launch_bounds__(128) pf_attn_merge_kernel(const __grid_constan
 // incrementally: the row maximum is exchanged through shared memory, each
 // half keeps its own running sum l under the common correction), write P's
 // hi and lo parts for the second product, and add their half of O_tile into
-// registers with the correction.
+// registers with the correction.  With one chunk per block (cmax == 1) the
+// CTA writes the normalised rows itself and no merge runs.
 //
 // Keys and values arrive as f32 rows through cp.async into one padded
 // staging buffer: the next tile's copies are issued as soon as this tile's
-// rows are converted, so they overlap the two products and the softmax.  P
-// reuses the K operand's space (the S product has finished reading K when the
-// softmax writes P).  Operands in shared memory in the UMMA canonical K-major
-// layout without swizzle (vox_tcgen05.cuh).
+// rows are converted, so they overlap the two products and the softmax (one
+// 512-byte bulk copy per row, issued by one warp, measured slower: 74 vs 50
+// us per 512-token pass).  P reuses the K operand's space (the S product has
+// finished reading K when the softmax writes P).  Operands in shared memory
+// in the UMMA canonical K-major layout without swizzle (vox_tcgen05.cuh);
+// the bf16 hi / lo split is one cvt.rn.bf16x2 per pair (split_bf16x2), which
+// took a 512-token pass from 63 to 50 us (the kernel issue-bound on integer
+// rounding before).
 constexpr int kTcQB = 32, kTcKT = 64, kTcThreads = 256, kTcHD = 128;
 constexpr int kTcQBytes = 128 * kTcHD * 2;    // one of Q hi / Q lo (32 KB)
 constexpr int kTcKBytes = kTcKT * kTcHD * 2;  // one of K hi / K lo, later P hi / P lo (16 KB)
@@ -646,13 +645,7 @@ __device__ __forceinline__ void tc_put8(unsigned char* hi_base, unsigned char* l
                                         const float (&v)[8]) {
     uint32_t hi[4], lo[4];
 #pragma unroll
-    for (int j = 0; j < 8; j += 2) {
-        const uint16_t h0 = f32_to_bf16_bits(v[j]), h1 = f32_to_bf16_bits(v[j + 1]);
-        const uint16_t l0 = f32_to_bf16_bits(v[j] - bf16_bits_to_f32(h0));
-        const uint16_t l1 = f32_to_bf16_bits(v[j + 1] - bf16_bits_to_f32(h1));
-        hi[j >> 1] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-        lo[j >> 1] = (uint32_t)l0 | ((uint32_t)l1 << 16);
-    }
+    for (int j = 0; j < 8; j += 2) split_bf16x2(v[j], v[j + 1], hi[j >> 1], lo[j >> 1]);
     *reinterpret_cast<uint4*>(hi_base + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
     *reinterpret_cast<uint4*>(lo_base + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
 }
@@ -880,7 +873,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_attn_tc_kernel(const __grid_
     __syncthreads();
     red[half * 128 + row] = l_run;
     __syncthreads();
-    if (tt < nq) {
+    if (tt < nq && A.cmax == 1) {
+        // one chunk per block: the normalised row itself, as the merge of a
+        // single record computes it (weight e^0 = 1, then times 1 / l)
+        const float L = red[row] + red[128 + row], inv = L > 0.0f ? 1.0f / L : 0.0f;
+        float* out = A.out + (size_t)t * A.n_heads * kTcHD + (size_t)(hk * 4 + g) * kTcHD + half * 64;
+#pragma unroll
+        for (int d = 0; d < kTcHD / 2; d += 4)
+            *reinterpret_cast<float4*>(out + d) =
+                make_float4(acc[d] * inv, acc[d + 1] * inv, acc[d + 2] * inv, acc[d + 3] * inv);
+    } else if (tt < nq) {
         float* rec = pf_attn_rec(A, qblk, chunk, hk, g, tt);
         // records are head_dim + 2 floats: 8-byte, not 16-byte, aligned
 #pragma unroll
