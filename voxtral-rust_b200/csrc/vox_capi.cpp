@@ -114,22 +114,32 @@ struct PrefillBufs {
 // blocks per split, ties to fewer splits.  An item costs its K blocks (48 KB
 // of operands each) plus its epilogue: a 128-row x tn-token f32 tile written
 // and read back once by the consumer, about 3 K blocks' worth at tn = 128.
+//
+// The wide form (full 128-token blocks, rows a multiple of 256; only where the
+// caller allows it) takes a pair of tiles per item: a K block moves 64 KB for
+// twice the products, and the epilogue's 256-row tile costs about 4 of them.
+// Measured at 512 tokens: the w1|w3 GEMM (one split, SwiGLU epilogue) 92 vs
+// 97 us, the prefill 1.5 % faster; the split-K GEMMs slower (q|k|v 42 vs 35,
+// o-proj 31 vs 24, w2 52 vs 45 us: half the items need more splits, and a
+// lane's partial row is stored along one token), so they stay narrow.
 struct PfPlan {
     int rows = 0, K = 0, tiles = 0, kbt = 0, splits = 1, grid = 1;
+    bool wide = false;
 };
-PfPlan make_pfplan(int rows, int K, int nblocks, int tn, int num_sms) {
+PfPlan make_pfplan(int rows, int K, int nblocks, int tn, int num_sms, bool allow_wide = false) {
     PfPlan p;
     p.rows = rows;
     p.K = K;
     p.tiles = (rows + 127) / 128;
     p.kbt = K / 64;
-    const long long base = (long long)p.tiles * nblocks;
+    p.wide = allow_wide && pf_gemm_wide_ok(rows, tn);
+    const long long base = (long long)(p.wide ? p.tiles / 2 : p.tiles) * nblocks;
     long long best = -1;
     for (int s = 1; s <= 16 && s <= p.kbt; ++s) {
         if (s > 1 && p.kbt / s < 4) break;
         const long long items = base * s;
         const long long grid = std::min<long long>(items, num_sms);
-        const long long epi = (3 * tn + 127) / 128;
+        const long long epi = p.wide ? 4 : (3 * tn + 127) / 128;
         const long long cost = ((items + grid - 1) / grid) * ((p.kbt + s - 1) / s + epi);
         if (best < 0 || cost < best) {
             best = cost;
@@ -765,7 +775,7 @@ int enqueue_pf_gemm(vox_ctx* c, const PfPlan& p, const unsigned char* wt, int tn
     a.T = T;
     a.splits = p.splits;
     a.err = c->err;
-    CUDA_TRY(record_launch(c, launch_pf_gemm(a, p.grid, c->stream)));
+    CUDA_TRY(record_launch(c, launch_pf_gemm(a, p.grid, p.wide, c->stream)));
     return VOX_OK;
 }
 
@@ -792,7 +802,7 @@ int prefill_batched(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, siz
         const int nblocks = (T + tn - 1) / tn, Tp = nblocks * tn;
         const PfPlan pq = make_pfplan(rows_qkv, dim, nblocks, tn, c->num_sms);
         const PfPlan po = make_pfplan(dim, qd, nblocks, tn, c->num_sms);
-        const PfPlan p13 = make_pfplan(2 * hid, dim, nblocks, tn, c->num_sms);
+        const PfPlan p13 = make_pfplan(2 * hid, dim, nblocks, tn, c->num_sms, true);
         const PfPlan p2 = make_pfplan(dim, hid, nblocks, tn, c->num_sms);
         size_t part = 0;
         for (const PfPlan* p : {&pq, &po, &p13, &p2}) part = std::max(part, (size_t)p->splits * T * p->rows);

@@ -252,7 +252,7 @@ struct PfGemmArgs {
     const unsigned char* xop;   // prefill operand of the pass
     float* part;                // [splits, T, rows] K-split partial products, or
     float* act;                 // non-null (splits 1, w1|w3 rows interleaved): SiLU(gate) * up [T, rows / 2]
-    int rows, kbt, tiles;       // weight shape: rows, 64-wide K blocks, 128-row tiles
+    int rows, kbt, tiles;       // weight shape: rows, 64-wide K blocks, 128-row tiles (even in the wide form)
     int tn, nblocks, T;         // tokens per block (16..128, multiple of 16), blocks, live tokens
     int splits;                 // K splits (<= kbt)
     unsigned* err;
@@ -321,9 +321,12 @@ struct PfCommitArgs {
     KvState final_state;        // state after T single-token appends
 };
 
-size_t pf_gemm_smem_bytes();
+size_t pf_gemm_smem_bytes(bool wide);
+// The wide form (tokens as the M = 128 rows, two weight tiles as N = 256)
+// takes full 128-token blocks and a multiple of 256 weight rows.
+bool pf_gemm_wide_ok(int rows, int tn);
 cudaError_t pf_prepare();
-cudaError_t launch_pf_gemm(const PfGemmArgs& a, int grid, cudaStream_t s);
+cudaError_t launch_pf_gemm(const PfGemmArgs& a, int grid, bool wide, cudaStream_t s);
 // The hidden rows (embedding + adapter, or residual + split sums) and their
 // sums of squares; then RMSNorm x gain into the operand (Tp = padded tokens,
 // blocks x tn, a multiple of 16).

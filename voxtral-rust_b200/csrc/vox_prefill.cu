@@ -34,6 +34,12 @@ constexpr int kPfStages = 4;
 constexpr int kPfABytes = 128 * 64 * 2;                // one pre-tiled weight block
 constexpr int kPfMaxSlab = 256 * 128;                  // X slab of one K block, N <= 256
 constexpr int kPfStageBytes = kPfABytes + kPfMaxSlab;  // 48 KB
+// Wide form (tn = 128, an even number of tiles): tokens are the M = 128 rows
+// (the slab's hi and lo halves as two A operands into one accumulator) and
+// two weight tiles the N = 2 x 128 columns; a stage is the slab plus two
+// weight blocks, 64 KB for twice the products of a 48 KB stage above.
+constexpr int kPfWideStages = 3;
+constexpr int kPfWideStageBytes = kPfMaxSlab + 2 * kPfABytes;  // 64 KB
 constexpr int kPfThreads = 192;                        // w0 producer, w1 MMA, w2..w5 epilogue
 constexpr uint32_t kPfTmemCols = 512;                  // two accumulators of up to 256 columns
 constexpr unsigned kFull = 0xFFFFFFFFu;
@@ -44,6 +50,7 @@ struct PfItem {
 
 // Item i -> (weight tile, K split, token block), token block fastest: the
 // CTAs that run at the same time share weight blocks, which L2 then serves.
+// In the wide form `tile` is a pair of weight tiles.
 __device__ __forceinline__ PfItem pf_item(const PfGemmArgs& A, int i) {
     PfItem it;
     it.nb = i % A.nblocks;
@@ -55,22 +62,25 @@ __device__ __forceinline__ PfItem pf_item(const PfGemmArgs& A, int i) {
     return it;
 }
 
+template <bool WIDE>
 __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_constant__ PfGemmArgs A) {
+    constexpr int kStages = WIDE ? kPfWideStages : kPfStages;
+    constexpr int kStageBytes = WIDE ? kPfWideStageBytes : kPfStageBytes;
     extern __shared__ __align__(1024) unsigned char smem[];
     unsigned char* ring = smem;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPfStages * kPfStageBytes);
-    uint64_t* empty = full + kPfStages;
-    uint64_t* acc_full = empty + kPfStages;  // [2]
-    uint64_t* acc_empty = acc_full + 2;      // [2]
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+    uint64_t* empty = full + kStages;
+    uint64_t* acc_full = empty + kStages;  // [2]
+    uint64_t* acc_empty = acc_full + 2;    // [2]
     uint32_t* tmem_s = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n = 2 * A.tn;
     const uint32_t slab = (uint32_t)n * 128u;
-    const int n_items = A.tiles * A.splits * A.nblocks;
+    const int n_items = (WIDE ? A.tiles / 2 : A.tiles) * A.splits * A.nblocks;
 
     if (tid == 0) {
-        for (int s = 0; s < kPfStages; ++s) {
+        for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
@@ -99,32 +109,44 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
             for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
                 const PfItem it = pf_item(A, i);
                 for (int kb = it.kb0; kb < it.kb1; ++kb, ++g) {
-                    const int slot = (int)(g % kPfStages);
-                    if (g >= (uint32_t)kPfStages && !mbar_wait(&empty[slot], ((g / kPfStages) - 1) & 1)) {
+                    const int slot = (int)(g % kStages);
+                    if (g >= (uint32_t)kStages && !mbar_wait(&empty[slot], ((g / kStages) - 1) & 1)) {
                         raise_error(A.err, ERR_EMPTY_WAIT);
                         ok = false;
                         break;
                     }
-                    unsigned char* dst = ring + (size_t)slot * kPfStageBytes;
-                    mbar_arrive_expect_tx(&full[slot], (uint32_t)kPfABytes + slab);
-                    bulk_copy_g2s_nohint(dst, A.wt + ((size_t)it.tile * A.kbt + kb) * kPfABytes, kPfABytes,
-                                         &full[slot]);
-                    bulk_copy_g2s_nohint(dst + kPfABytes, A.xop + ((size_t)it.nb * A.kbt + kb) * slab, slab,
-                                         &full[slot]);
+                    unsigned char* dst = ring + (size_t)slot * kStageBytes;
+                    const unsigned char* xsrc = A.xop + ((size_t)it.nb * A.kbt + kb) * slab;
+                    if (WIDE) {  // slab, then the pair's two weight blocks of this K block
+                        mbar_arrive_expect_tx(&full[slot], slab + 2u * kPfABytes);
+                        bulk_copy_g2s_nohint(dst, xsrc, slab, &full[slot]);
+                        for (int w = 0; w < 2; ++w)
+                            bulk_copy_g2s_nohint(dst + slab + w * kPfABytes,
+                                                 A.wt + ((size_t)(2 * it.tile + w) * A.kbt + kb) * kPfABytes,
+                                                 kPfABytes, &full[slot]);
+                    } else {
+                        mbar_arrive_expect_tx(&full[slot], (uint32_t)kPfABytes + slab);
+                        bulk_copy_g2s_nohint(dst, A.wt + ((size_t)it.tile * A.kbt + kb) * kPfABytes, kPfABytes,
+                                             &full[slot]);
+                        bulk_copy_g2s_nohint(dst + kPfABytes, xsrc, slab, &full[slot]);
+                    }
                 }
             }
             // no copy may be in flight when the CTA exits
-            const uint32_t first = g > (uint32_t)kPfStages ? g - kPfStages : 0u;
+            const uint32_t first = g > (uint32_t)kStages ? g - kStages : 0u;
             for (uint32_t s = first; s < g; ++s)
-                if (!mbar_wait(&full[s % kPfStages], (s / kPfStages) & 1)) raise_error(A.err, ERR_DRAIN_WAIT);
+                if (!mbar_wait(&full[s % kStages], (s / kStages) & 1)) raise_error(A.err, ERR_DRAIN_WAIT);
         }
         return;  // the barriers below count warps 1..5 only
     }
 
     if (warp == 1) {
-        // ---- MMA issuer: 4 x (M 128, N n, K 16) per K block ----
+        // ---- MMA issuer: 4 x (M 128, N n, K 16) per K block; wide: 4 x 4 x
+        // (M 128 tokens, N 128 weight rows, K 16): hi and lo token rows into the
+        // same accumulator, the pair's first tile into columns 0..127, the
+        // second into 128..255 ----
         if (lane == 0) {
-            const uint32_t idesc = umma_idesc_bf16(128, n);
+            const uint32_t idesc = WIDE ? umma_idesc_bf16(128, 128) : umma_idesc_bf16(128, n);
             const uint32_t b_kstep = (uint32_t)n * 32u, b_lbo = (uint32_t)n * 16u;
             uint32_t g = 0;
             bool ok = true;
@@ -139,20 +161,39 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                 tmem_fence_after();
                 const uint32_t d = tmem + (uint32_t)(ab * 256);
                 for (int kb = it.kb0; kb < it.kb1 && ok; ++kb, ++g) {
-                    const int slot = (int)(g % kPfStages);
-                    if (!mbar_wait(&full[slot], (g / kPfStages) & 1)) {
+                    const int slot = (int)(g % kStages);
+                    if (!mbar_wait(&full[slot], (g / kStages) & 1)) {
                         raise_error(A.err, ERR_FULL_WAIT);
                         ok = false;
                         break;
                     }
                     tmem_fence_after();
-                    const uint32_t a_addr = smem_addr(ring + (size_t)slot * kPfStageBytes);
-                    const uint32_t b_addr = a_addr + (uint32_t)kPfABytes;
+                    const uint32_t s_addr = smem_addr(ring + (size_t)slot * kStageBytes);
+                    if (WIDE) {
+                        // slab: K step j at j * 8 KB, K halves 4 KB apart, hi token
+                        // rows 0..127 then lo rows from 2 KB; weight blocks after it
+                        const uint32_t w_addr = s_addr + slab;
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const uint64_t ad = umma_desc(a_addr + (uint32_t)j * 4096u, 2048u, 128u);
-                        const uint64_t bd = umma_desc(b_addr + (uint32_t)j * b_kstep, b_lbo, 128u);
-                        umma_f16(d, ad, bd, idesc, (kb > it.kb0 || j > 0) ? 1u : 0u);
+                        for (int j = 0; j < 4; ++j) {
+                            const uint32_t acc = (kb > it.kb0 || j > 0) ? 1u : 0u;
+                            const uint64_t ah = umma_desc(s_addr + (uint32_t)j * b_kstep, b_lbo, 128u);
+                            const uint64_t al = umma_desc(s_addr + (uint32_t)j * b_kstep + 2048u, b_lbo, 128u);
+#pragma unroll
+                            for (int w = 0; w < 2; ++w) {
+                                const uint64_t bd =
+                                    umma_desc(w_addr + (uint32_t)(w * kPfABytes) + (uint32_t)j * 4096u, 2048u, 128u);
+                                umma_f16(d + (uint32_t)(w * 128), ah, bd, idesc, acc);
+                                umma_f16(d + (uint32_t)(w * 128), al, bd, idesc, 1u);
+                            }
+                        }
+                    } else {
+                        const uint32_t b_addr = s_addr + (uint32_t)kPfABytes;
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const uint64_t ad = umma_desc(s_addr + (uint32_t)j * 4096u, 2048u, 128u);
+                            const uint64_t bd = umma_desc(b_addr + (uint32_t)j * b_kstep, b_lbo, 128u);
+                            umma_f16(d, ad, bd, idesc, (kb > it.kb0 || j > 0) ? 1u : 0u);
+                        }
                     }
                     umma_commit(&empty[slot]);  // frees the stage once these MMAs have read it
                 }
@@ -170,10 +211,52 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
             const int ab = local & 1;
             if (!mbar_wait(&acc_full[ab], (local >> 1) & 1)) raise_error(A.err, ERR_FULL_WAIT);
             tmem_fence_after();
+            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * 256);
+            if (WIDE) {
+                // lane = token t of the block, columns = weight rows r0 .. r0 + 255:
+                // 32 rows per round as float4 stores (rows are a multiple of 64)
+                const int t = it.nb * 128 + row, r0 = it.tile * 256;
+                for (int c = 0; c < 256; c += 32) {
+                    uint32_t a[16], b[16];
+                    tmem_ld16x2(taddr + (uint32_t)c, taddr + (uint32_t)(c + 16), a, b);
+                    float y[32];
+#pragma unroll
+                    for (int u = 0; u < 16; ++u) {
+                        y[u] = __uint_as_float(a[u]);
+                        y[16 + u] = __uint_as_float(b[u]);
+                    }
+                    const int r = r0 + c;
+                    if (t < A.T && r < A.rows) {
+                        if (A.act) {
+                            // rows 2j (gate) and 2j + 1 (up) are adjacent columns:
+                            // SiLU(gate) * up (math.rs:4-9, decoder.rs:147-150)
+                            float* out = A.act + (size_t)t * (A.rows >> 1) + (r >> 1);
+#pragma unroll
+                            for (int k = 0; k < 16; k += 4) {
+                                float v[4];
+#pragma unroll
+                                for (int u = 0; u < 4; ++u) {
+                                    const float gt = y[2 * (k + u)], up = y[2 * (k + u) + 1];
+                                    v[u] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), up);
+                                }
+                                *reinterpret_cast<float4*>(out + k) = make_float4(v[0], v[1], v[2], v[3]);
+                            }
+                        } else {
+                            float* out = A.part + ((size_t)it.ks * A.T + t) * A.rows + r;
+#pragma unroll
+                            for (int k = 0; k < 32; k += 4)
+                                *reinterpret_cast<float4*>(out + k) = make_float4(y[k], y[k + 1], y[k + 2], y[k + 3]);
+                        }
+                    }
+                }
+                tmem_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[ab]);
+                continue;
+            }
             const int r = it.tile * 128 + row;
             const bool live = r < A.rows;
             const int t0 = it.nb * A.tn;
-            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * 256);
             if (A.act) {
                 // rows 2j (gate) and 2j + 1 (up) sit in adjacent lanes: SiLU(gate) * up
                 // (math.rs:4-9, decoder.rs:147-150) straight to act[t, j]
@@ -972,11 +1055,19 @@ int grid_for(long long work, int per_block) {
 
 }  // namespace
 
-size_t pf_gemm_smem_bytes() { return (size_t)kPfStages * kPfStageBytes + (2 * kPfStages + 4) * 8 + 16; }
+size_t pf_gemm_smem_bytes(bool wide) {
+    return wide ? (size_t)kPfWideStages * kPfWideStageBytes + (2 * kPfWideStages + 4) * 8 + 16
+                : (size_t)kPfStages * kPfStageBytes + (2 * kPfStages + 4) * 8 + 16;
+}
+
+bool pf_gemm_wide_ok(int rows, int tn) { return tn == 128 && rows % 256 == 0; }
 
 cudaError_t pf_prepare() {
-    cudaError_t e = cudaFuncSetAttribute(pf_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)pf_gemm_smem_bytes());
+    cudaError_t e = cudaFuncSetAttribute(pf_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)pf_gemm_smem_bytes(false));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(pf_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)pf_gemm_smem_bytes(true));
     const auto attn_smem = [](int hd) { return pf_attn_smem_floats(hd) * 4; };
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(pf_attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem(32));
@@ -991,11 +1082,14 @@ cudaError_t pf_prepare() {
     return e;
 }
 
-cudaError_t launch_pf_gemm(const PfGemmArgs& a, int grid, cudaStream_t s) {
+cudaError_t launch_pf_gemm(const PfGemmArgs& a, int grid, bool wide, cudaStream_t s) {
     if (a.tn < 16 || a.tn > 128 || a.tn % 16 || a.splits < 1 || a.splits > a.kbt || grid < 1 ||
-        (a.act && (a.splits != 1 || a.rows % 2)))
+        (a.act && (a.splits != 1 || a.rows % 2)) || (wide && (!pf_gemm_wide_ok(a.rows, a.tn) || a.tiles % 2)))
         return cudaErrorInvalidValue;
-    pf_gemm_kernel<<<grid, kPfThreads, pf_gemm_smem_bytes(), s>>>(a);
+    if (wide)
+        pf_gemm_kernel<true><<<grid, kPfThreads, pf_gemm_smem_bytes(true), s>>>(a);
+    else
+        pf_gemm_kernel<false><<<grid, kPfThreads, pf_gemm_smem_bytes(false), s>>>(a);
     return cudaGetLastError();
 }
 
