@@ -105,6 +105,7 @@ struct PrefillBufs {
     float* attn_part = nullptr;  // attention chunk partials
     size_t attn_part_floats = 0;
     unsigned char* xop = nullptr;
+    unsigned char* xop2 = nullptr;  // second operand buffer: the w2 operand written by the w1|w3 epilogue
     int32_t* tokens = nullptr;    // [kPrefillPass]
     int32_t* h_tokens = nullptr;  // pinned staging
 };
@@ -724,6 +725,7 @@ int ensure_prefill(vox_ctx* c) {
     CUDA_TRY(dalloc(&f.vc, T * kvd));
     CUDA_TRY(dalloc(&f.attn, T * qd));
     CUDA_TRY(cudaMalloc(&f.xop, pf_xop_bytes((int)T, (int)kmax)));
+    CUDA_TRY(cudaMalloc(&f.xop2, pf_xop_bytes((int)T, (int)kmax)));
     CUDA_TRY(dalloc(&f.tokens, T));
     CUDA_TRY(dalloc(&f.ssp, T * ((dim + 511) / 512)));
     CUDA_TRY(cudaMallocHost(&f.h_tokens, T * sizeof(int32_t)));
@@ -761,12 +763,13 @@ int enqueue_pf_norm(vox_ctx* c, PfNormArgs a) {
 }
 
 int enqueue_pf_gemm(vox_ctx* c, const PfPlan& p, const unsigned char* wt, int tn, int nblocks, int T,
-                    float* act = nullptr) {
+                    float* act = nullptr, unsigned char* xop_out = nullptr, const unsigned char* xop = nullptr) {
     PfGemmArgs a{};
     a.wt = wt;
-    a.xop = c->pf.xop;
+    a.xop = xop ? xop : c->pf.xop;
     a.part = c->pf.part;
     a.act = act;
+    a.xop_out = xop_out;
     a.rows = p.rows;
     a.kbt = p.kbt;
     a.tiles = p.tiles;
@@ -886,10 +889,19 @@ int prefill_batched(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, siz
                 aa.part = f.attn_part;
                 aa.scale = 1.0f / sqrtf((float)g.head_dim);
                 aa.out = f.attn;
+                // the tensor-core kernel with a single chunk per block writes the
+                // normalised rows straight into the o-proj's operand (the q|k|v
+                // GEMM that read the operand buffer before has finished)
+                const bool direct = tc && aa.cmax == 1;
+                if (direct) {
+                    aa.xop = f.xop;
+                    aa.xop_tn = tn;
+                }
                 CUDA_TRY(record_launch(c, tc ? launch_pf_attn_tc(aa, c->stream) : launch_pf_attn(aa, c->stream)));
-                // a single chunk per block leaves normalised rows (tensor-core kernel)
-                if (!tc || aa.cmax > 1) CUDA_TRY(record_launch(c, launch_pf_attn_merge(aa, c->stream)));
-                CUDA_TRY(record_launch(c, launch_pf_split(f.attn, T, Tp, qd, f.xop, tn, c->stream)));
+                if (!direct) {
+                    CUDA_TRY(record_launch(c, launch_pf_attn_merge(aa, c->stream)));
+                    CUDA_TRY(record_launch(c, launch_pf_split(f.attn, T, Tp, qd, f.xop, tn, c->stream)));
+                }
             }
             // 3) the pass's keys and values into the ring, state after T appends
             PfCommitArgs ca{};
@@ -919,14 +931,20 @@ int prefill_batched(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, siz
             na.T = T;
             na.Tp = Tp;
             TRY(enqueue_pf_norm(c, na));
-            if (p13.splits == 1) {  // SwiGLU in the GEMM epilogue, then the w2 operand
+            const unsigned char* w2_xop = f.xop;
+            if (p13.splits == 1 && p13.wide) {
+                // SwiGLU in the GEMM epilogue straight into the w2 operand, a second
+                // buffer (other CTAs still read the w1|w3 operand from the first)
+                TRY(enqueue_pf_gemm(c, p13, L.w13_t, tn, nblocks, T, f.part, f.xop2));
+                w2_xop = f.xop2;
+            } else if (p13.splits == 1) {  // SwiGLU in the GEMM epilogue, then the w2 operand
                 TRY(enqueue_pf_gemm(c, p13, L.w13_t, tn, nblocks, T, f.part));
                 CUDA_TRY(record_launch(c, launch_pf_split(f.part, T, Tp, hid, f.xop, tn, c->stream)));
             } else {
                 TRY(enqueue_pf_gemm(c, p13, L.w13_t, tn, nblocks, T));
                 CUDA_TRY(record_launch(c, launch_pf_swiglu(f.part, p13.splits, T, Tp, hid, f.xop, tn, c->stream)));
             }
-            TRY(enqueue_pf_gemm(c, p2, L.w2_t, tn, nblocks, T));
+            TRY(enqueue_pf_gemm(c, p2, L.w2_t, tn, nblocks, T, nullptr, nullptr, w2_xop));
             na.splits = p2.splits;
             na.gain = c->layers[l + 1].attn_norm;
             TRY(enqueue_pf_norm(c, na));
@@ -1299,7 +1317,7 @@ void vox_ctx_destroy(vox_ctx* c) {
     }
     {
         PrefillBufs& f = c->pf;
-        void* fp[] = {f.h, f.q, f.kc, f.vc, f.attn, f.part, f.xop, f.tokens, f.ssp, f.attn_part};
+        void* fp[] = {f.h, f.q, f.kc, f.vc, f.attn, f.part, f.xop, f.xop2, f.tokens, f.ssp, f.attn_part};
         for (void* p : fp)
             if (p) cudaFree(p);
         if (f.h_tokens) cudaFreeHost(f.h_tokens);

@@ -252,6 +252,8 @@ struct PfGemmArgs {
     const unsigned char* xop;   // prefill operand of the pass
     float* part;                // [splits, T, rows] K-split partial products, or
     float* act;                 // non-null (splits 1, w1|w3 rows interleaved): SiLU(gate) * up [T, rows / 2]
+    unsigned char* xop_out;     // wide form with act: SiLU(gate) * up as the next GEMM's prefill operand
+                                //   (a buffer other than xop) instead of act
     int rows, kbt, tiles;       // weight shape: rows, 64-wide K blocks, 128-row tiles (even in the wide form)
     int tn, nblocks, T;         // tokens per block (16..128, multiple of 16), blocks, live tokens
     int splits;                 // K splits (<= kbt)
@@ -308,6 +310,8 @@ struct PfAttnArgs {
     float* part;                // chunk partials, pf_attn_part_floats
     float scale;
     float* out;                 // [T, n_heads * head_dim]
+    unsigned char* xop;         // tensor-core kernel, cmax 1: non-null = write the rows as the next
+    int xop_tn;                 //   GEMM's prefill operand (tokens per block) instead of `out`
 };
 
 struct PfCommitArgs {

@@ -62,6 +62,20 @@ __device__ __forceinline__ PfItem pf_item(const PfGemmArgs& A, int i) {
     return it;
 }
 
+// Eight consecutive elements k .. k + 7 of token t into the prefill operand.
+__device__ __forceinline__ void pf_store8(unsigned char* xop, int tn, int kbt, int t, int k, const float (&v)[8]) {
+    const int nb = t / tn, tt = t - nb * tn, n = 2 * tn;
+    const int kb = k >> 6, kk = k & 63;
+    const int s = kk >> 4, k2 = (kk >> 3) & 1;
+    unsigned char* base = xop + ((size_t)nb * kbt + kb) * (size_t)n * 128 + (size_t)s * n * 32 + (size_t)k2 * n * 16;
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) split_bf16x2(v[j], v[j + 1], hi[j >> 1], lo[j >> 1]);
+    const int lr = tn + tt;
+    *reinterpret_cast<uint4*>(base + (tt >> 3) * 128 + (tt & 7) * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(base + (lr >> 3) * 128 + (lr & 7) * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+}
+
 template <bool WIDE>
 __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_constant__ PfGemmArgs A) {
     constexpr int kStages = WIDE ? kPfWideStages : kPfStages;
@@ -229,17 +243,28 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
                     if (t < A.T && r < A.rows) {
                         if (A.act) {
                             // rows 2j (gate) and 2j + 1 (up) are adjacent columns:
-                            // SiLU(gate) * up (math.rs:4-9, decoder.rs:147-150)
-                            float* out = A.act + (size_t)t * (A.rows >> 1) + (r >> 1);
+                            // SiLU(gate) * up (math.rs:4-9, decoder.rs:147-150), for
+                            // hidden units r / 2 .. r / 2 + 15
+                            float v[16];
 #pragma unroll
-                            for (int k = 0; k < 16; k += 4) {
-                                float v[4];
+                            for (int u = 0; u < 16; ++u) {
+                                const float gt = y[2 * u], up = y[2 * u + 1];
+                                v[u] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), up);
+                            }
+                            if (A.xop_out) {  // straight into the next GEMM's operand
+                                const int kbt_out = A.rows >> 7;  // (rows / 2) / 64 K blocks
 #pragma unroll
-                                for (int u = 0; u < 4; ++u) {
-                                    const float gt = y[2 * (k + u)], up = y[2 * (k + u) + 1];
-                                    v[u] = __fmul_rn(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))), up);
+                                for (int h8 = 0; h8 < 2; ++h8) {
+                                    float w8[8];
+#pragma unroll
+                                    for (int u = 0; u < 8; ++u) w8[u] = v[h8 * 8 + u];
+                                    pf_store8(A.xop_out, 128, kbt_out, t, (r >> 1) + h8 * 8, w8);
                                 }
-                                *reinterpret_cast<float4*>(out + k) = make_float4(v[0], v[1], v[2], v[3]);
+                            } else {
+                                float* out = A.act + (size_t)t * (A.rows >> 1) + (r >> 1);
+#pragma unroll
+                                for (int k = 0; k < 16; k += 4)
+                                    *reinterpret_cast<float4*>(out + k) = make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
                             }
                         } else {
                             float* out = A.part + ((size_t)it.ks * A.T + t) * A.rows + r;
@@ -301,20 +326,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPfTmemCols)
                      : "memory");
     }
-}
-
-// Eight consecutive elements k .. k + 7 of token t into the prefill operand.
-__device__ __forceinline__ void pf_store8(unsigned char* xop, int tn, int kbt, int t, int k, const float (&v)[8]) {
-    const int nb = t / tn, tt = t - nb * tn, n = 2 * tn;
-    const int kb = k >> 6, kk = k & 63;
-    const int s = kk >> 4, k2 = (kk >> 3) & 1;
-    unsigned char* base = xop + ((size_t)nb * kbt + kb) * (size_t)n * 128 + (size_t)s * n * 32 + (size_t)k2 * n * 16;
-    uint32_t hi[4], lo[4];
-#pragma unroll
-    for (int j = 0; j < 8; j += 2) split_bf16x2(v[j], v[j + 1], hi[j >> 1], lo[j >> 1]);
-    const int lr = tn + tt;
-    *reinterpret_cast<uint4*>(base + (tt >> 3) * 128 + (tt & 7) * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    *reinterpret_cast<uint4*>(base + (lr >> 3) * 128 + (lr & 7) * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
 }
 
 // Ordered sum of the K-split partials of element e of token t.
@@ -694,7 +705,8 @@ __global__ void __launch_bounds__(128) pf_attn_merge_kernel(const __grid_constan
 // half keeps its own running sum l under the common correction), write P's
 // hi and lo parts for the second product, and add their half of O_tile into
 // registers with the correction.  With one chunk per block (cmax == 1) the
-// CTA writes the normalised rows itself and no merge runs.
+// CTA writes the normalised rows itself and no merge runs: as f32 rows, or
+// (xop given) straight into the o-proj's prefill operand.
 //
 // Keys and values arrive as f32 rows through cp.async into one padded
 // staging buffer: the next tile's copies are issued as soon as this tile's
@@ -960,11 +972,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_attn_tc_kernel(const __grid_
         // one chunk per block: the normalised row itself, as the merge of a
         // single record computes it (weight e^0 = 1, then times 1 / l)
         const float L = red[row] + red[128 + row], inv = L > 0.0f ? 1.0f / L : 0.0f;
-        float* out = A.out + (size_t)t * A.n_heads * kTcHD + (size_t)(hk * 4 + g) * kTcHD + half * 64;
+        if (A.xop) {  // straight into the o-proj's operand (64 dims = one K block)
+            const int k0 = (hk * 4 + g) * kTcHD + half * 64;
 #pragma unroll
-        for (int d = 0; d < kTcHD / 2; d += 4)
-            *reinterpret_cast<float4*>(out + d) =
-                make_float4(acc[d] * inv, acc[d + 1] * inv, acc[d + 2] * inv, acc[d + 3] * inv);
+            for (int d = 0; d < kTcHD / 2; d += 8) {
+                float v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = acc[d + u] * inv;
+                pf_store8(A.xop, A.xop_tn, qd / 64, t, k0 + d, v);
+            }
+        } else {
+            float* out = A.out + (size_t)t * A.n_heads * kTcHD + (size_t)(hk * 4 + g) * kTcHD + half * 64;
+#pragma unroll
+            for (int d = 0; d < kTcHD / 2; d += 4)
+                *reinterpret_cast<float4*>(out + d) =
+                    make_float4(acc[d] * inv, acc[d + 1] * inv, acc[d + 2] * inv, acc[d + 3] * inv);
+        }
     } else if (tt < nq) {
         float* rec = pf_attn_rec(A, qblk, chunk, hk, g, tt);
         // records are head_dim + 2 floats: 8-byte, not 16-byte, aligned
@@ -1084,7 +1107,8 @@ cudaError_t pf_prepare() {
 
 cudaError_t launch_pf_gemm(const PfGemmArgs& a, int grid, bool wide, cudaStream_t s) {
     if (a.tn < 16 || a.tn > 128 || a.tn % 16 || a.splits < 1 || a.splits > a.kbt || grid < 1 ||
-        (a.act && (a.splits != 1 || a.rows % 2)) || (wide && (!pf_gemm_wide_ok(a.rows, a.tn) || a.tiles % 2)))
+        (a.act && (a.splits != 1 || a.rows % 2)) || (wide && (!pf_gemm_wide_ok(a.rows, a.tn) || a.tiles % 2)) ||
+        (a.xop_out && (!wide || !a.act || a.xop_out == a.xop)))
         return cudaErrorInvalidValue;
     if (wide)
         pf_gemm_kernel<true><<<grid, kPfThreads, pf_gemm_smem_bytes(true), s>>>(a);
@@ -1152,7 +1176,8 @@ bool pf_attn_tc_supported(int n_heads, int n_kv, int head_dim) {
 
 cudaError_t launch_pf_attn_tc(const PfAttnArgs& a, cudaStream_t s) {
     if (!pf_attn_tc_supported(a.n_heads, a.n_kv, a.head_dim) || a.win < 1 || a.kc < kTcKT || a.kc % kTcKT ||
-        a.cmax < 1 || !a.part || a.qb != kTcQB)
+        a.cmax < 1 || !a.part || a.qb != kTcQB ||
+        (a.xop && (a.cmax != 1 || a.xop_tn < 16 || a.xop_tn > 128 || a.xop_tn % 16)))
         return cudaErrorInvalidValue;
     const dim3 grid((unsigned)(((a.T + kTcQB - 1) / kTcQB) * a.cmax), a.n_kv);
     pf_attn_tc_kernel<<<grid, kTcThreads, kTcSmem, s>>>(a);
