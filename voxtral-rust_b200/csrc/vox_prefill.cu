@@ -433,33 +433,49 @@ __global__ void __launch_bounds__(256) pf_norm_xop_kernel(const __grid_constant_
 
 // q|k|v split sums -> RoPE (math.rs:30-65) on q and k at position pos0 + t ->
 // q [T, q_dim], the pass's keys and values [T, kv_dim].  One thread per
-// (token, element pair).
+// (token, 4 consecutive elements) = two RoPE pairs of one head (q_dim and
+// kv_dim are multiples of 64, head_dim of 4); the splits' float4 loads are all
+// issued before the sum, which adds them in split order as pf_sum does.
 __global__ void __launch_bounds__(256) pf_qkv_kernel(const __grid_constant__ PfQkvArgs A) {
-    const int pairs = (A.q_dim + 2 * A.kv_dim) / 2;
-    const long long total = (long long)A.T * pairs;
+    const int rows = A.q_dim + 2 * A.kv_dim, quads = rows / 4;
+    const long long total = (long long)A.T * quads;
     const int half = A.head_dim / 2;
-    const int rows = A.q_dim + 2 * A.kv_dim;
     for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
          e += (long long)gridDim.x * blockDim.x) {
-        const int t = (int)(e / pairs), r = 2 * (int)(e - (long long)t * pairs);
-        const float y0 = pf_sum(A.part, A.splits, A.T, rows, t, r);
-        const float y1 = pf_sum(A.part, A.splits, A.T, rows, t, r + 1);
+        const int t = (int)(e / quads), r = 4 * (int)(e - (long long)t * quads);
+        float4 p[4];
+#pragma unroll
+        for (int sp = 0; sp < 4; ++sp)
+            if (sp < A.splits) p[sp] = *reinterpret_cast<const float4*>(A.part + ((size_t)sp * A.T + t) * rows + r);
+        float4 y = p[0];
+#pragma unroll
+        for (int sp = 1; sp < 4; ++sp)
+            if (sp < A.splits) {
+                y.x += p[sp].x; y.y += p[sp].y; y.z += p[sp].z; y.w += p[sp].w;
+            }
+        for (int sp = 4; sp < A.splits; ++sp) {
+            const float4 q = *reinterpret_cast<const float4*>(A.part + ((size_t)sp * A.T + t) * rows + r);
+            y.x += q.x; y.y += q.y; y.z += q.z; y.w += q.w;
+        }
         if (r < A.q_dim + A.kv_dim) {
             const int rr = r < A.q_dim ? r : r - A.q_dim;
             const int d = rr % A.head_dim;
-            long long p = A.pos0 + t;
-            if (p >= A.max_pos) {
+            long long pos = A.pos0 + t;
+            if (pos >= A.max_pos) {
                 if (r == 0) raise_error(A.err, ERR_POS_RANGE);
-                p = 0;
+                pos = 0;
             }
-            const float c = A.rope_cos[p * half + d / 2], sn = A.rope_sin[p * half + d / 2];
-            const float o0 = __fsub_rn(__fmul_rn(y0, c), __fmul_rn(y1, sn));
-            const float o1 = __fadd_rn(__fmul_rn(y0, sn), __fmul_rn(y1, c));
+            const float2 c = *reinterpret_cast<const float2*>(A.rope_cos + pos * half + d / 2);
+            const float2 sn = *reinterpret_cast<const float2*>(A.rope_sin + pos * half + d / 2);
+            const float o0 = __fsub_rn(__fmul_rn(y.x, c.x), __fmul_rn(y.y, sn.x));
+            const float o1 = __fadd_rn(__fmul_rn(y.x, sn.x), __fmul_rn(y.y, c.x));
+            const float o2 = __fsub_rn(__fmul_rn(y.z, c.y), __fmul_rn(y.w, sn.y));
+            const float o3 = __fadd_rn(__fmul_rn(y.z, sn.y), __fmul_rn(y.w, c.y));
             float* dst = r < A.q_dim ? A.q + (size_t)t * A.q_dim + rr : A.kc + (size_t)t * A.kv_dim + rr;
-            *reinterpret_cast<float2*>(dst) = make_float2(o0, o1);
+            *reinterpret_cast<float4*>(dst) = make_float4(o0, o1, o2, o3);
         } else {
             const int rr = r - A.q_dim - A.kv_dim;
-            *reinterpret_cast<float2*>(A.vc + (size_t)t * A.kv_dim + rr) = make_float2(y0, y1);
+            *reinterpret_cast<float4*>(A.vc + (size_t)t * A.kv_dim + rr) = y;
         }
     }
 }
@@ -1131,8 +1147,8 @@ cudaError_t launch_pf_norm_xop(const PfNormArgs& a, cudaStream_t s) {
 }
 
 cudaError_t launch_pf_qkv(const PfQkvArgs& a, cudaStream_t s) {
-    if (a.head_dim % 2 || a.q_dim % 2 || a.kv_dim % 2) return cudaErrorInvalidValue;
-    const long long work = (long long)a.T * ((a.q_dim + 2 * a.kv_dim) / 2);
+    if (a.head_dim % 4 || a.q_dim % 64 || a.kv_dim % 64 || a.splits < 1) return cudaErrorInvalidValue;
+    const long long work = (long long)a.T * ((a.q_dim + 2 * a.kv_dim) / 4);
     pf_qkv_kernel<<<grid_for(work, 256), 256, 0, s>>>(a);
     return cudaGetLastError();
 }
