@@ -104,6 +104,8 @@ struct PrefillBufs {
     float* ssp = nullptr;        // [kPrefillPass, ceil(dim / 512)] RMSNorm partial sums
     float* attn_part = nullptr;  // attention chunk partials
     size_t attn_part_floats = 0;
+    float* kvop = nullptr;       // K / V operand tiles of the tensor-core attention
+    size_t kvop_floats = 0;
     unsigned char* xop = nullptr;
     unsigned char* xop2 = nullptr;  // second operand buffer: the w2 operand written by the w1|w3 epilogue
     int32_t* tokens = nullptr;    // [kPrefillPass]
@@ -897,6 +899,17 @@ int prefill_batched(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, siz
                     aa.xop = f.xop;
                     aa.xop_tn = tn;
                 }
+                if (tc) {
+                    // the keys and values it reads, once, as 64-key operand tiles
+                    // from the pass's first visible key rounded down to 64
+                    const int first = aa.len0 + 1 - std::min(aa.len0 + 1, win);
+                    aa.kv_base = first / 64 * 64;
+                    aa.kv_tiles = (aa.len0 + T - 1 - aa.kv_base) / 64 + 1;
+                    TRY(ensure_scratch(c, &f.kvop, &f.kvop_floats,
+                                       (size_t)aa.n_kv * aa.kv_tiles * pf_kv_tile_bytes() / sizeof(float)));
+                    aa.kvop = reinterpret_cast<unsigned char*>(f.kvop);
+                    CUDA_TRY(record_launch(c, launch_pf_kv_tiles(aa, c->stream)));
+                }
                 CUDA_TRY(record_launch(c, tc ? launch_pf_attn_tc(aa, c->stream) : launch_pf_attn(aa, c->stream)));
                 if (!direct) {
                     CUDA_TRY(record_launch(c, launch_pf_attn_merge(aa, c->stream)));
@@ -1317,7 +1330,7 @@ void vox_ctx_destroy(vox_ctx* c) {
     }
     {
         PrefillBufs& f = c->pf;
-        void* fp[] = {f.h, f.q, f.kc, f.vc, f.attn, f.part, f.xop, f.xop2, f.tokens, f.ssp, f.attn_part};
+        void* fp[] = {f.h, f.q, f.kc, f.vc, f.attn, f.part, f.xop, f.xop2, f.tokens, f.ssp, f.attn_part, f.kvop};
         for (void* p : fp)
             if (p) cudaFree(p);
         if (f.h_tokens) cudaFreeHost(f.h_tokens);

@@ -312,6 +312,9 @@ struct PfAttnArgs {
     float* out;                 // [T, n_heads * head_dim]
     unsigned char* xop;         // tensor-core kernel, cmax 1: non-null = write the rows as the next
     int xop_tn;                 //   GEMM's prefill operand (tokens per block) instead of `out`
+    unsigned char* kvop;        // tensor-core kernel: K / V operand tiles (pf_kv_tiles_kernel), kv_tiles
+    int kv_base, kv_tiles;      //   of pf_kv_tile_bytes() per kv head from key kv_base (a multiple of 64,
+                                //   at most the pass's first key) through the pass's last key
 };
 
 struct PfCommitArgs {
@@ -342,6 +345,9 @@ size_t pf_attn_part_floats(int T, int n_kv, int head_dim, int cmax, int qb);
 // Tensor-core variant (4 q heads per kv head, head_dim 128; qb 32, kc a multiple of 64).
 bool pf_attn_tc_supported(int n_heads, int n_kv, int head_dim);
 cudaError_t launch_pf_attn_tc(const PfAttnArgs& a, cudaStream_t s);
+// The pass's keys and values as the tensor-core attention's operand tiles.
+cudaError_t launch_pf_kv_tiles(const PfAttnArgs& a, cudaStream_t s);
+size_t pf_kv_tile_bytes();
 cudaError_t launch_pf_attn(const PfAttnArgs& a, cudaStream_t s);
 cudaError_t launch_pf_attn_merge(const PfAttnArgs& a, cudaStream_t s);
 cudaError_t launch_pf_split(const float* src, int T, int Tp, int K, unsigned char* xop, int tn, cudaStream_t s);

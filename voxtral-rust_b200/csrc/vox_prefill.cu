@@ -328,13 +328,6 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(const __grid_con
     }
 }
 
-// Ordered sum of the K-split partials of element e of token t.
-__device__ __forceinline__ float pf_sum(const float* part, int splits, int T, int rows, int t, int e) {
-    float y = part[(size_t)t * rows + e];
-    for (int s = 1; s < splits; ++s) y += part[((size_t)s * T + t) * rows + e];
-    return y;
-}
-
 // Operand tiles: 32 tokens x 64 elements staged in shared memory, read from
 // row-major f32 rows (consecutive threads on consecutive elements of a row)
 // and written to the prefill operand with eight consecutive threads on eight
@@ -724,23 +717,24 @@ __global__ void __launch_bounds__(128) pf_attn_merge_kernel(const __grid_constan
 // CTA writes the normalised rows itself and no merge runs: as f32 rows, or
 // (xop given) straight into the o-proj's prefill operand.
 //
-// Keys and values arrive as f32 rows through cp.async into one padded
-// staging buffer: the next tile's copies are issued as soon as this tile's
-// rows are converted, so they overlap the two products and the softmax (one
-// 512-byte bulk copy per row, issued by one warp, measured slower: 74 vs 50
-// us per 512-token pass).  P reuses the K operand's space (the S product has
-// finished reading K when the softmax writes P).  Operands in shared memory
-// in the UMMA canonical K-major layout without swizzle (vox_tcgen05.cuh);
-// the bf16 hi / lo split is one cvt.rn.bf16x2 per pair (split_bf16x2), which
-// took a 512-token pass from 63 to 50 us (the kernel issue-bound on integer
-// rounding before).
+// The key / value operands are converted once per layer and pass by
+// pf_kv_tiles_kernel into 64 KB tiles on a 64-key grid (kv_base + 64 i), so
+// the attention CTAs, which read overlapping key ranges, only bulk-copy them:
+// one 64 KB copy per tile into a two-stage ring, the next tile landing while
+// this one's products and softmax run.  A CTA's tiles may start before its
+// chunk (the grid is global), so keys outside [j_lo, j_hi] are masked like
+// keys outside the token's window.  P reuses the stage's K space (the S
+// product has finished reading K when the softmax writes P).  Operands in the
+// UMMA canonical K-major layout without swizzle (vox_tcgen05.cuh); the bf16
+// hi / lo split is one cvt.rn.bf16x2 per pair (split_bf16x2).  Measured per
+// 512-token pass: CTAs that each converted their K/V tiles from f32 (staged
+// with cp.async) 49 us; with per-thread global loads 91 us.
 constexpr int kTcQB = 32, kTcKT = 64, kTcThreads = 256, kTcHD = 128;
 constexpr int kTcQBytes = 128 * kTcHD * 2;    // one of Q hi / Q lo (32 KB)
 constexpr int kTcKBytes = kTcKT * kTcHD * 2;  // one of K hi / K lo, later P hi / P lo (16 KB)
 constexpr int kTcVBytes = kTcHD * kTcKT * 2;  // one of V^T hi / lo (16 KB)
-constexpr int kTcFS = kTcHD + 4;              // staging row stride (floats): conflict-free float4 reads
-constexpr int kTcFBytes = 128 * kTcFS * 4;    // 128 Q rows, or 64 K rows + 64 V rows
-constexpr int kTcSmem = 2 * (kTcQBytes + kTcKBytes + kTcVBytes) + kTcFBytes + 2 * 128 * 4 + 64;
+constexpr int kTcTileBytes = 2 * kTcKBytes + 2 * kTcVBytes;  // 64 KB: K hi | K lo | V^T hi | V^T lo
+constexpr int kTcSmem = 2 * kTcQBytes + 2 * kTcTileBytes + 2 * 128 * 4 + 64;
 static_assert(kTcKBytes == 128 * kTcKT * 2, "P (128 rows x 64 keys) fits the K operand's space");
 
 // Byte offset of element (row, k) of an operand with `rows` rows (a multiple
@@ -761,96 +755,129 @@ __device__ __forceinline__ void tc_put8(unsigned char* hi_base, unsigned char* l
     *reinterpret_cast<uint4*>(lo_base + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
 }
 
-__device__ __forceinline__ void ld8_shared(const float* src, float (&v)[8]) {
+__device__ __forceinline__ void ld8(const float* src, float (&v)[8]) {
     const float4 a = *reinterpret_cast<const float4*>(src);
     const float4 b = *reinterpret_cast<const float4*>(src + 4);
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
     v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
+// Row of logical key j (cache before the pass, then the pass) of kv head hk.
+__device__ __forceinline__ const float* pf_key_row(const PfAttnArgs& A, int hk, int j, const float* ring,
+                                                   const float* pass) {
+    if (j < A.len0) {
+        int slot = A.start0 + j;  // start0 < cap and j < len0 <= cap
+        if (slot >= A.cap) slot -= A.cap;
+        return ring + ((size_t)hk * A.cap + slot) * kTcHD;
+    }
+    return pass + (size_t)(j - A.len0) * A.n_kv * kTcHD + (size_t)hk * kTcHD;
+}
+
+// Keys and values the pass's attention reads, converted once as the
+// tensor-core kernel's B operands: for kv head hk and tile i (keys kv_base +
+// 64 i ..), K hi | K lo (64 keys x 128 dims) then V^T hi | V^T lo (128 dims x
+// 64 keys); keys past the pass's last are zero.  Grid (kv_tiles, n_kv, 4):
+// z = 0, 1 the K rows of keys 32 z .., z = 2, 3 the V^T rows of dims 64 (z - 2) ..
+// (64 CTAs per tile-and-head grid took 10.2 us at a 512-token pass).
+__global__ void __launch_bounds__(256) pf_kv_tiles_kernel(const __grid_constant__ PfAttnArgs A) {
+    const int i = blockIdx.x, hk = blockIdx.y, z = blockIdx.z, tid = threadIdx.x;
+    const int j0 = A.kv_base + i * kTcKT, j_last = A.len0 + A.T - 1;
+    unsigned char* base = A.kvop + ((size_t)hk * A.kv_tiles + i) * kTcTileBytes;
+    // K: key kk, dims d0 .. d0 + 7 (consecutive threads take consecutive keys)
+    if (z < 2)
+    for (int e = tid; e < (kTcKT / 2) * (kTcHD / 8); e += 256) {
+        const int kk = z * 32 + (e & 31), d0 = (e >> 5) * 8, j = j0 + kk;
+        float v[8];
+        if (j <= j_last) {
+            ld8(pf_key_row(A, hk, j, A.k_ring, A.kc_in) + d0, v);
+        } else {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = 0.0f;
+        }
+        tc_put8(base, base + kTcKBytes, kmaj_off(kk, d0, kTcKT), v);
+    }
+    // V^T: dim d, keys k0 .. k0 + 7 (consecutive threads take consecutive dims)
+    unsigned char* vb = base + 2 * kTcKBytes;
+    if (z >= 2)
+    for (int e = tid; e < (kTcHD / 2) * (kTcKT / 8); e += 256) {
+        const int d = (z - 2) * 64 + (e & 63), k0 = (e >> 6) * 8;
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int j = j0 + k0 + u;
+            v[u] = j <= j_last ? pf_key_row(A, hk, j, A.v_ring, A.vc_in)[d] : 0.0f;
+        }
+        tc_put8(vb, vb + kTcVBytes, kmaj_off(d, k0, kTcHD), v);
+    }
+}
+
 __global__ void __launch_bounds__(kTcThreads, 1) pf_attn_tc_kernel(const __grid_constant__ PfAttnArgs A) {
     extern __shared__ __align__(1024) unsigned char tsm[];
     unsigned char* Qh = tsm;
     unsigned char* Ql = Qh + kTcQBytes;
-    unsigned char* Kh = Ql + kTcQBytes;  // K hi, then P hi
-    unsigned char* Kl = Kh + kTcKBytes;  // K lo, then P lo
-    unsigned char* Vh = Kl + kTcKBytes;
-    unsigned char* Vl = Vh + kTcVBytes;
-    float* F = reinterpret_cast<float*>(Vl + kTcVBytes);  // staging rows, stride kTcFS
-    float* red = F + 128 * kTcFS;                          // [2][128] half-row maxima, then sums
+    unsigned char* ring = Ql + kTcQBytes;  // 2 stages of kTcTileBytes
+    float* red = reinterpret_cast<float*>(ring + 2 * kTcTileBytes);  // [2][128] half-row maxima, then sums
     uint64_t* bar_s = reinterpret_cast<uint64_t*>(red + 2 * 128);
     uint64_t* bar_o = bar_s + 1;
-    uint32_t* tmem_s = reinterpret_cast<uint32_t*>(bar_o + 1);
+    uint64_t* bar_f = bar_o + 1;  // [2] a stage's tile landed
+    uint32_t* tmem_s = reinterpret_cast<uint32_t*>(bar_f + 2);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int hk = blockIdx.y;
     const int qblk = blockIdx.x / A.cmax, chunk = blockIdx.x % A.cmax;
     const int t0 = qblk * kTcQB, nq = min(kTcQB, A.T - t0);
-    const int qd = A.n_heads * kTcHD, kvd = A.n_kv * kTcHD;
+    const int qd = A.n_heads * kTcHD;
     const int b_lo = pf_first_key(A, t0), b_hi = A.len0 + t0 + nq - 1;
     const int j_lo = b_lo + chunk * A.kc;
     if (j_lo > b_hi) return;  // this block has fewer chunks (uniform across the CTA)
     const int j_hi = min(b_hi, j_lo + A.kc - 1);
-    const int n_tiles = (j_hi - j_lo) / kTcKT + 1;
-    const float* kr = A.k_ring + (size_t)hk * A.cap * kTcHD;
-    const float* vr = A.v_ring + (size_t)hk * A.cap * kTcHD;
+    const int i_first = (j_lo - A.kv_base) / kTcKT, n_tiles = (j_hi - A.kv_base) / kTcKT - i_first + 1;
+    const unsigned char* tiles = A.kvop + ((size_t)hk * A.kv_tiles + i_first) * kTcTileBytes;
 
-    // f32 rows of one tile into F: keys at rows 0..63, values at 64..127
-    // (rows past j_hi zero-filled); 16 bytes per copy, a warp per row pair
-    auto issue_tile = [&](int j0) {
-#pragma unroll 4
-        for (int e = tid; e < kTcKT * (kTcHD / 4); e += kTcThreads) {
-            const int kk = e >> 5, c4 = (e & 31) * 4, j = j0 + kk;
-            const float *ks = A.kc_in, *vs = A.vc_in;  // any valid address when j is past the range
-            if (j <= j_hi) {
-                if (j < A.len0) {
-                    int slot = A.start0 + j;  // start0 < cap and j < len0 <= cap
-                    if (slot >= A.cap) slot -= A.cap;
-                    ks = kr + (size_t)slot * kTcHD + c4;
-                    vs = vr + (size_t)slot * kTcHD + c4;
-                } else {
-                    ks = A.kc_in + (size_t)(j - A.len0) * kvd + (size_t)hk * kTcHD + c4;
-                    vs = A.vc_in + (size_t)(j - A.len0) * kvd + (size_t)hk * kTcHD + c4;
-                }
-            }
-            cp_async16(F + kk * kTcFS + c4, ks, j <= j_hi);
-            cp_async16(F + (kTcKT + kk) * kTcFS + c4, vs, j <= j_hi);
-        }
-        cp_async_commit();
-    };
-
-    // Q rows (token t0 + tt, q head 4 hk + g) through F
-#pragma unroll 4
-    for (int e = tid; e < 128 * (kTcHD / 4); e += kTcThreads) {
-        const int r = e >> 5, c4 = (e & 31) * 4, tt = r & 31, g = r >> 5;
-        const bool ok = tt < nq;
-        const float* src = ok ? A.q + (size_t)(t0 + tt) * qd + (size_t)(hk * 4 + g) * kTcHD + c4 : A.q;
-        cp_async16(F + r * kTcFS + c4, src, ok);
-    }
-    cp_async_commit();
     if (tid == 0) {
         mbar_init(bar_s, 1);
         mbar_init(bar_o, 1);
+        mbar_init(&bar_f[0], 1);
+        mbar_init(&bar_f[1], 1);
         fence_barrier_init();
     }
+    __syncthreads();
+    auto issue = [&](int k) {  // thread 0: tile k into stage k % 2
+        const int st = k & 1;
+        mbar_arrive_expect_tx(&bar_f[st], (uint32_t)kTcTileBytes);
+        bulk_copy_g2s_nohint(ring + (size_t)st * kTcTileBytes, tiles + (size_t)k * kTcTileBytes,
+                             (uint32_t)kTcTileBytes, &bar_f[st]);
+    };
+    if (tid == 0)
+        for (int k = 0; k < min(2, n_tiles); ++k) issue(k);
     if (warp == 0) {
+        __syncwarp();  // the allocation is warp-collective
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_s)),
                      "r"(256)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
-    cp_async_wait<0>();
-    __syncthreads();
-    // consecutive threads take consecutive rows: conflict-free 16-byte reads
-    // (padded stride) and 16-byte operand stores
-    for (int e = tid; e < 128 * (kTcHD / 8); e += kTcThreads) {
-        const int r = e & 127, d0 = (e >> 7) * 8;
-        float v[8];
-        ld8_shared(F + r * kTcFS + d0, v);
-        tc_put8(Qh, Ql, kmaj_off(r, d0, 128), v);
+    // Q rows (token t0 + tt, q head 4 hk + g) as hi / lo, four rows' loads in
+    // flight per thread; consecutive threads take consecutive rows
+    for (int e0 = tid; e0 < 128 * (kTcHD / 8); e0 += 4 * kTcThreads) {
+        float v[4][8];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int e = e0 + u * kTcThreads, r = e & 127, d0 = (e >> 7) * 8, tt = r & 31, g = r >> 5;
+            if (tt < nq) {
+                ld8(A.q + (size_t)(t0 + tt) * qd + (size_t)(hk * 4 + g) * kTcHD + d0, v[u]);
+            } else {
+#pragma unroll
+                for (int w = 0; w < 8; ++w) v[u][w] = 0.0f;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int e = e0 + u * kTcThreads, r = e & 127, d0 = (e >> 7) * 8;
+            tc_put8(Qh, Ql, kmaj_off(r, d0, 128), v[u]);
+        }
     }
-    __syncthreads();  // F free again
-    issue_tile(j_lo);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
     tmem_fence_before();
     __syncthreads();
     tmem_fence_after();
@@ -860,7 +887,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_attn_tc_kernel(const __grid_
     const int q4 = warp & 3, half = warp >> 2;  // TMEM lane quarter, column half
     const int row = q4 * 32 + lane, tt = lane, g = q4;
     const int t = t0 + tt;
-    const int kfirst = pf_first_key(A, t), klast = A.len0 + t;
+    const int kfirst = max(pf_first_key(A, t), j_lo), klast = min(A.len0 + t, j_hi);
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
     float acc[kTcHD / 2];
 #pragma unroll
@@ -869,30 +896,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_attn_tc_kernel(const __grid_
     constexpr uint32_t idS = umma_idesc_bf16(128, kTcKT), idO = umma_idesc_bf16(128, kTcHD);
     uint32_t phase = 0;
 
-    for (int tile = 0; tile < n_tiles; ++tile) {
-        const int j0 = j_lo + tile * kTcKT;
-        cp_async_wait<0>();
-        __syncthreads();  // this tile's rows in F; the previous products read
-        // K rows (B operand, N = 64 keys) and V^T (B operand, N = 128 dims) as hi / lo
-        for (int e = tid; e < kTcKT * (kTcHD / 8); e += kTcThreads) {
-            const int kk = e & 63, d0 = (e >> 6) * 8;
-            float v[8];
-            ld8_shared(F + kk * kTcFS + d0, v);
-            tc_put8(Kh, Kl, kmaj_off(kk, d0, kTcKT), v);
-        }
-        for (int e = tid; e < kTcHD * (kTcKT / 8); e += kTcThreads) {
-            const int d = e & 127, k0 = (e >> 7) * 8;
-            float v[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) v[u] = F[(kTcKT + k0 + u) * kTcFS + d];
-            tc_put8(Vh, Vl, kmaj_off(d, k0, kTcHD), v);
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
-        tmem_fence_before();
-        __syncthreads();  // operands written, F free
-        tmem_fence_after();
-        if (tile + 1 < n_tiles) issue_tile(j0 + kTcKT);
+    for (int k = 0; k < n_tiles; ++k) {
+        const int j0 = A.kv_base + (i_first + k) * kTcKT;
+        unsigned char* Kh = ring + (size_t)(k & 1) * kTcTileBytes;  // K hi, then P hi
+        unsigned char* Kl = Kh + kTcKBytes;                           // K lo, then P lo
+        unsigned char* Vh = Kl + kTcKBytes;
+        unsigned char* Vl = Vh + kTcVBytes;
         if (tid == 0) {
+            if (!mbar_wait(&bar_f[k & 1], (uint32_t)(k >> 1) & 1u)) raise_error(A.err, ERR_FULL_WAIT);
+            tmem_fence_after();
             const uint32_t qh = smem_addr(Qh), ql = smem_addr(Ql), kh = smem_addr(Kh), kl = smem_addr(Kl);
 #pragma unroll
             for (int s = 0; s < kTcHD / 16; ++s) {
@@ -923,7 +935,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_attn_tc_kernel(const __grid_
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
             const int j = j0 + half * 32 + c;
-            const bool ok = tt < nq && j <= j_hi && j >= kfirst && j <= klast;
+            const bool ok = tt < nq && j >= kfirst && j <= klast;
             const float sc = ok ? __uint_as_float(sr[c]) * A.scale : -INFINITY;
             sr[c] = __float_as_uint(sc);
             mt = fmaxf(mt, sc);
@@ -979,9 +991,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) pf_attn_tc_kernel(const __grid_
         }
         phase ^= 1u;
         tmem_fence_before();
+        __syncthreads();  // this stage's products are read and TMEM is free for the next tile
+        tmem_fence_after();
+        if (tid == 0 && k + 2 < n_tiles) issue(k + 2);
     }
     // the two halves' sums under the same corrections add to the row's l
-    __syncthreads();
     red[half * 128 + row] = l_run;
     __syncthreads();
     if (tt < nq && A.cmax == 1) {
@@ -1192,13 +1206,25 @@ bool pf_attn_tc_supported(int n_heads, int n_kv, int head_dim) {
 
 cudaError_t launch_pf_attn_tc(const PfAttnArgs& a, cudaStream_t s) {
     if (!pf_attn_tc_supported(a.n_heads, a.n_kv, a.head_dim) || a.win < 1 || a.kc < kTcKT || a.kc % kTcKT ||
-        a.cmax < 1 || !a.part || a.qb != kTcQB ||
+        a.cmax < 1 || !a.part || a.qb != kTcQB || !a.kvop || a.kv_base % kTcKT ||
+        a.kv_base > a.len0 + 1 - (a.len0 + 1 < a.win ? a.len0 + 1 : a.win) ||
+        a.kv_base + a.kv_tiles * kTcKT < a.len0 + a.T ||
         (a.xop && (a.cmax != 1 || a.xop_tn < 16 || a.xop_tn > 128 || a.xop_tn % 16)))
         return cudaErrorInvalidValue;
     const dim3 grid((unsigned)(((a.T + kTcQB - 1) / kTcQB) * a.cmax), a.n_kv);
     pf_attn_tc_kernel<<<grid, kTcThreads, kTcSmem, s>>>(a);
     return cudaGetLastError();
 }
+
+cudaError_t launch_pf_kv_tiles(const PfAttnArgs& a, cudaStream_t s) {
+    if (!pf_attn_tc_supported(a.n_heads, a.n_kv, a.head_dim) || !a.kvop || a.kv_tiles < 1 || a.kv_base < 0 ||
+        a.kv_base % kTcKT || a.kv_base + a.kv_tiles * kTcKT < a.len0 + a.T)
+        return cudaErrorInvalidValue;
+    pf_kv_tiles_kernel<<<dim3(a.kv_tiles, a.n_kv, 4), 256, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+size_t pf_kv_tile_bytes() { return (size_t)kTcTileBytes; }
 
 cudaError_t launch_pf_attn_merge(const PfAttnArgs& a, cudaStream_t s) {
     if (a.qb < 1) return cudaErrorInvalidValue;
