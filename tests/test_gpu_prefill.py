@@ -164,6 +164,19 @@ def test_prefill_tensor_core_attention(V, oracle, window, cache_window, prompt, 
     run_case(V, oracle, c, 2, 4096, prompt, 6, window=cache_window, calls=calls)
 
 
+@pytest.mark.parametrize("width", ["g4_hd128", "g4_hd32"])
+@pytest.mark.parametrize("window,cache_window,prompt,calls", [
+    (64, None, 237, [100, 100, 37]),  # each later call reads a ring whose live keys wrap past its end
+    (48, 128, 240, [150, 90]),        # wrapped 128-slot ring, attention window 48 inside it
+])
+def test_prefill_reads_a_wrapped_ring(V, oracle, width, window, cache_window, prompt, calls):
+    """Calls after the first read the cache before the pass from a ring whose
+    start is not slot 0 (start0 + j runs past the capacity): the tensor-core
+    attention (4 q heads per kv head, head_dim 128) and the CUDA-core one."""
+    base = NARROW_G4 if width == "g4_hd128" else NARROW
+    run_case(V, oracle, dict(base, sliding_window=window), 2, 4096, prompt, 6, window=cache_window, calls=calls)
+
+
 def test_prefill_matches_token_steps(V):
     """The batched prefill and vox_model_prefill_steps leave the same ring
     state and caches within tolerance (26 layers at full width)."""
