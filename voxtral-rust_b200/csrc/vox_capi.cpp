@@ -875,8 +875,9 @@ int prefill_batched(vox_ctx* c, vox_kv* kv, const int32_t* tokens, size_t n, siz
                 // tensor-core blocks of 32 tokens (4 q heads per kv head, head_dim
                 // 128), else CUDA-core blocks of 16; chunks of >= 128 keys.  The
                 // tensor-core kernel takes one chunk per block when the blocks x kv
-                // heads fill 3/4 of the SMs (at 512-token passes 1-5 % faster than
-                // 2, 3, 4 or 6 chunks per block, or fixed 128-192 keys), else enough
+                // heads fill 3/4 of the SMs (prompts of 512 / 4096 tokens: 6.90 /
+                // 76.7 ms against 7.48-7.73 / 83.7-87.1 ms with 2, 4 or 8 chunks per
+                // block, which also need the merge), else enough
                 // chunks to cover the SMs (at most 8); the CUDA-core kernel about 8.
                 const bool tc = pf_attn_tc_supported(aa.n_heads, aa.n_kv, aa.head_dim);
                 aa.qb = tc ? 32 : 16;
