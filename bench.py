@@ -760,7 +760,7 @@ def run_ours(args):
             "unit": "tokens/s", "ms": pf_max, "prompt_tokens": PROMPT, "gpu_launches": pf_run["launches"],
             "workload": (f"the {PROMPT}-id prompt of the token-loop workload into an empty cache, 26 layers: "
                          f"vox_model_prefill, one pass of dense tcgen05 GEMMs over all {PROMPT} tokens "
-                         f"(activations as bf16 hi + lo parts), causal attention, ring append"),
+                         f"(activations as bf16 hi + lo parts), causal attention on tcgen05, ring append"),
             "e2e": {"value": PROMPT * world / (pf_wall_max / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": 4 * PROMPT, "d2h_bytes_per_step": 4},
             "token_steps_ms": pf_steps_max, "speedup_vs_token_steps": pf_steps_max / pf_max,
